@@ -1,0 +1,267 @@
+#!/usr/bin/env python3
+"""Headline benchmark: evict/restore GB/s per GPU on B200 (aggregate over N GPUs).
+
+Workload (single-B200 eviction sweep point, run on every GPU of the job): a
+bf16 N(0,1) tensor (default 1 GiB, larger than the 126 MB L2 so every step
+streams from HBM) is evicted GPU -> pinned arena with the fused content hash
+(K1) and restored pinned -> GPU (K2), while an 8192x8192 bf16 matmul loop runs
+concurrently on the same GPU. The arena lives on the GPU's NUMA node, slots
+are 64 MiB, data stays pinned between evict and restore.
+
+Timing: W warm-up steps, then K steps bracketed by barrier + synchronize;
+device time from CUDA events on the copy stream, max over ranks. ``value`` is
+the whole-job aggregate: N * K * 2 * nbytes / max_rank_time. ``e2e`` repeats
+the cycle through the public API (destructive ``off.evict`` + ``h.restore()``
++ reading the content hash back) timed on the host.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--size-mb MB] [--matmul 0|1]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+    python bench.py --impl reference
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# Reference numbers (StateSpectre docs/PERFORMANCE.md:33, H20 PCIe Gen5, 1 GiB):
+BASELINE_D2H_GBS = 53.6
+BASELINE_H2D_GBS = 57.5
+BASELINE_ROUNDTRIP_GBS = 2.0 / (1.0 / BASELINE_D2H_GBS + 1.0 / BASELINE_H2D_GBS)
+METRIC = "evict/restore GB/s per GPU at 1/2/4/8 B200; 32B weight-sync latency (ms)"
+REFERENCE_UNAVAILABLE = (
+    "reference cannot be installed offline: /root/reference has neither setup.py nor pyproject.toml "
+    "(pip install fails) and its CMake build requires libnuma and liburing (numa.h, liburing.h), "
+    "which are absent from this image")
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--size-mb", type=int, default=1024)
+    p.add_argument("--matmul", type=int, default=1)
+    p.add_argument("--engine", default="kernel", choices=["kernel", "copy_engine"])
+    p.add_argument("--evict-ctas", type=int, default=0)
+    p.add_argument("--restore-ctas", type=int, default=0)
+    p.add_argument("--hash", type=int, default=1)
+    p.add_argument("--e2e-steps", type=int, default=0, help="default: same as --steps")
+    p.add_argument("--out", default="")
+    return p.parse_args()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        line = {"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    from statespectre_b200 import launch_daemon, offload_context
+    from statespectre_b200._native import native
+    from statespectre_b200.utils.clocks import ClockSampler
+    from statespectre_b200.utils.topology import daemon_yaml, gpu_numa_nodes
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE", file=sys.stderr)
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    nbytes = args.size_mb << 20
+    window_gb = max(4, (3 * nbytes >> 30) + 2)
+    run_dir = os.environ.get("OFLD_BENCH_DIR", "/tmp/ofld_bench")
+    os.makedirs(run_dir, exist_ok=True)
+    sock = os.path.join(run_dir, "offloadd.sock")
+    daemon = None
+    if local_rank == 0:
+        if os.path.exists(sock):
+            os.unlink(sock)
+        cfg = os.path.join(run_dir, "offloadd.yaml")
+        n_local = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+        with open(cfg, "w") as f:
+            f.write(daemon_yaml(sock, gpu_numa_nodes(max(n_local, torch.cuda.device_count())), window_gb))
+        daemon = launch_daemon(sock, config=cfg, log_path=os.path.join(run_dir, "offloadd.log"))
+    barrier()
+    if world > 1 and local_rank != 0:
+        deadline = time.time() + 120
+        while not os.path.exists(sock) and time.time() < deadline:
+            time.sleep(0.05)
+
+    sess = offload_context(daemon_addr=sock, device=device, rank=rank, local_rank=local_rank, world_rank=rank,
+                           eager_register=True, engine=args.engine, evict_ctas=args.evict_ctas,
+                           restore_ctas=args.restore_ctas, hash_on_evict=bool(args.hash), stream_priority=-1)
+    off = sess.off
+    g = torch.Generator(device=device)
+    g.manual_seed(1234 + rank)
+    x = torch.randn(nbytes // 2, dtype=torch.bfloat16, device=device, generator=g)
+    ref_hash = off.hash_tensor(x)
+    copy_stream = torch.cuda.Stream(device=device, priority=-1)
+
+    # ---- concurrent 8192^2 bf16 matmul loop on its own stream ----
+    stop_mm = threading.Event()
+    mm_count = [0]
+    mm_thread = None
+    if args.matmul:
+        mm_stream = torch.cuda.Stream(device=device)
+        a = torch.randn(8192, 8192, dtype=torch.bfloat16, device=device)
+        b = torch.randn(8192, 8192, dtype=torch.bfloat16, device=device)
+        c = torch.empty(8192, 8192, dtype=torch.bfloat16, device=device)
+
+        def mm_loop():
+            torch.cuda.set_device(device)
+            with torch.cuda.stream(mm_stream):
+                while not stop_mm.is_set():
+                    for _ in range(8):
+                        torch.matmul(a, b, out=c)
+                    mm_stream.synchronize()
+                    mm_count[0] += 8
+
+        mm_thread = threading.Thread(target=mm_loop, daemon=True)
+        mm_thread.start()
+
+    tid = ((rank & 0x7FFFFF) << 40) | 0xB0000
+    evict_ms, restore_ms = [], []
+
+    def cycle(version: int, record: bool):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e2 = torch.cuda.Event(enable_timing=True)
+        e0.record(copy_stream)
+        h = off.copy(x, stream=copy_stream, wait=True, tensor_id=tid, version=version)
+        e1.record(copy_stream)
+        h.restore_into(x, stream=copy_stream, wait=True)
+        e2.record(copy_stream)
+        h.discard()
+        if record:
+            e2.synchronize()
+            evict_ms.append(e0.elapsed_time(e1))
+            restore_ms.append(e1.elapsed_time(e2))
+        return h
+
+    for i in range(args.warmup):
+        cycle(i + 1, False)
+    torch.cuda.synchronize(device)
+    assert off.hash_tensor(x) == ref_hash, "round trip corrupted the tensor"
+    launches0 = native().kernel_launch_count()
+    sampler = ClockSampler([local_rank]).start()
+    barrier()
+    torch.cuda.synchronize(device)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(copy_stream)
+    for i in range(args.steps):
+        cycle(1000 + i, False)
+    t_end.record(copy_stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    clocks = sampler.stop()
+    launches = native().kernel_launch_count() - launches0
+    dev_ms = t_start.elapsed_time(t_end)
+    dev_ms_max = max_over_ranks(dev_ms)
+    value = world * args.steps * 2 * nbytes / (dev_ms_max / 1e3) / 1e9
+
+    # per-direction rates (separately timed steps, for the breakdown)
+    for i in range(3):
+        cycle(5000 + i, True)
+    ev = sorted(evict_ms)[len(evict_ms) // 2]
+    rs = sorted(restore_ms)[len(restore_ms) // 2]
+
+    # ---- end to end through the public API ----
+    e2e_steps = args.e2e_steps or args.steps
+    torch.cuda.synchronize(device)
+    barrier()
+    t0 = time.perf_counter()
+    hashes_ok = True
+    for i in range(e2e_steps):
+        h = off.evict(x, wait=True, tensor_id=tid, version=20000 + i)   # D2H, VRAM released
+        x = h.restore()                                                   # H2D from pinned host memory
+        hashes_ok &= h.content_hash == ref_hash                           # 16 B result read back
+        h.discard()
+    torch.cuda.synchronize(device)
+    e2e_s = time.perf_counter() - t0
+    e2e_s_max = max_over_ranks(e2e_s)
+    barrier()
+    e2e_value = world * e2e_steps * 2 * nbytes / e2e_s_max / 1e9
+    stop_mm.set()
+    if mm_thread:
+        mm_thread.join(timeout=30)
+    mm_tflops = None
+    assert hashes_ok, "content hash changed across the e2e round trips"
+
+    sess.close()
+    barrier()
+    if daemon is not None:
+        daemon.stop()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "GB/s (aggregate over all GPUs, evict+restore bytes / device time)",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dev_ms_max / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": round(value / (world * BASELINE_ROUNDTRIP_GBS), 4),
+            "dtype": "bf16",
+            "data": "synthetic: bf16 N(0,1) random tensor, seeded per rank",
+            "config": {
+                "model": "single-B200 eviction sweep point: bf16 tensor evict (K1, fused ssh128 hash) + restore (K2)",
+                "tensor_bytes": nbytes, "global_batch": world, "seq_len": 0, "parallelism": f"dp{world}",
+                "concurrent_matmul": "8192x8192 bf16 loop" if args.matmul else "none",
+                "engine": args.engine, "hash": bool(args.hash), "slot_mb": 64,
+                "l2": "inputs (1 GiB) larger than the 126 MB L2; no flush needed",
+                "baseline": f"StateSpectre H20 PCIe Gen5 1 GiB: D2H {BASELINE_D2H_GBS}, H2D {BASELINE_H2D_GBS} GB/s "
+                            f"(round trip {BASELINE_ROUNDTRIP_GBS:.2f} GB/s per GPU)",
+            },
+            "evict_gbs_per_gpu": round(nbytes / (ev / 1e3) / 1e9, 3),
+            "restore_gbs_per_gpu": round(nbytes / (rs / 1e3) / 1e9, 3),
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s (aggregate, public API, host-timed)",
+                    "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes + 16},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "matmul_iters": mm_count[0],
+        }
+        print(json.dumps(line), flush=True)
+        if args.out:
+            with open(args.out, "w") as f:
+                json.dump(line, f, indent=1)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,1232 @@
+// Rank agent implementation. See agent.h.
+//
+// Transfer protocol per evict (StateSpectre order, reference:
+// src/agent/agent.cpp:753-868): reserve a run (RequestOffload), mark it
+// submitted, launch the copy, record an event, and on completion report
+// D2H-complete (completion ring, else RPC) and run the invalidate callback.
+// With fast_submit the reservation and the submitted mark travel in one
+// round trip (OFLD_FLAG_SUBMIT_ON_GRANT); restore likewise folds
+// MarkH2DSubmitted into the ready prefetch (OFLD_FLAG_SUBMIT_ON_READY).
+#include "agent.h"
+
+#include <cuda_runtime.h>
+#include <sys/mman.h>
+#include <unistd.h>
+
+#include <atomic>
+#include <condition_variable>
+#include <cstring>
+#include <list>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <thread>
+#include <unordered_map>
+
+#include "../kernels/kernels.h"
+#include "ofld/abi/offload_canonical_abi.hpp"
+#include "ofld/chunk_hash.h"
+#include "ofld/log.h"
+#include "ofld/metrics.h"
+#include "ofld/numa.h"
+#include "ofld/shm.h"
+#include "ofld/transport.h"
+
+namespace ofld {
+
+namespace {
+constexpr const char* TAG = "agent";
+
+#define CUDA_OK(expr)                                                                                 \
+    do {                                                                                              \
+        cudaError_t e_ = (expr);                                                                      \
+        if (e_ != cudaSuccess)                                                                        \
+            throw std::runtime_error(std::string("CUDA error at " #expr ": ") + cudaGetErrorString(e_)); \
+    } while (0)
+
+struct TvKey {
+    uint64_t tid, ver;
+    bool operator<(const TvKey& o) const { return tid != o.tid ? tid < o.tid : ver < o.ver; }
+};
+
+// Small host-mapped pinned buffers (chunk digests, mismatch counters) cached
+// by power-of-two size class.
+class PinnedPool {
+ public:
+    struct Buf {
+        void* host = nullptr;
+        void* dev = nullptr;
+        size_t cls = 0;
+    };
+    Buf get(size_t bytes) {
+        size_t cls = 64;
+        while (cls < bytes) cls <<= 1;
+        {
+            std::lock_guard<std::mutex> g(mu_);
+            auto& v = free_[cls];
+            if (!v.empty()) {
+                Buf b = v.back();
+                v.pop_back();
+                return b;
+            }
+        }
+        Buf b;
+        b.cls = cls;
+        CUDA_OK(cudaHostAlloc(&b.host, cls, cudaHostAllocMapped | cudaHostAllocPortable));
+        CUDA_OK(cudaHostGetDevicePointer(&b.dev, b.host, 0));
+        return b;
+    }
+    void put(const Buf& b) {
+        if (!b.host) return;
+        std::lock_guard<std::mutex> g(mu_);
+        free_[b.cls].push_back(b);
+    }
+    void clear() {
+        std::lock_guard<std::mutex> g(mu_);
+        for (auto& kv : free_)
+            for (Buf& b : kv.second) cudaFreeHost(b.host);
+        free_.clear();
+    }
+
+ private:
+    std::mutex mu_;
+    std::map<size_t, std::vector<Buf>> free_;
+};
+
+}  // namespace
+
+struct Agent::Impl {
+    AgentOptions opt;
+    bool gpu = false;
+    int numa = 0;
+    uint64_t epoch = 0;
+    std::unique_ptr<RpcClient> rpc;
+    std::atomic<uint64_t> rpc_count{0};
+
+    struct ArenaMap {
+        uint64_t id = 0;
+        char* base = nullptr;
+        uint64_t size = 0;
+        char* dev = nullptr;  // device alias after registration
+        bool registered = false;
+    };
+    std::vector<ArenaMap> arenas;
+    std::mutex reg_mu;
+    char* control = nullptr;
+    uint64_t control_size = 0;
+    ofld_slot_entry_t* slots = nullptr;
+    uint32_t num_slots = 0;
+    RingHeader* ring = nullptr;
+    std::mutex ring_mu;
+
+    cudaStream_t stream = nullptr;
+    PinnedPool pool;
+
+    struct Pending {
+        bool d2h = true;
+        uint64_t lease = 0, tid = 0, ver = 0, nbytes = 0;
+        uint32_t slot = 0;
+        cudaEvent_t ev = nullptr;
+        DoneCallback cb;
+        bool keep_pinned = false;
+        PinnedPool::Buf dig, mism, exp;  // digests out, mismatch counter, expected digests
+        uint64_t ndig = 0;
+    };
+    std::mutex inflight_mu;
+    std::list<Pending> inflight;
+
+    struct TensorRec {
+        bool offloaded = false, restored = false;
+        uint64_t hash_lo = 0, hash_hi = 0, lease = 0, ring_seq = ~0ull;
+        std::vector<uint64_t> digests;
+    };
+    mutable std::mutex tab_mu;
+    std::condition_variable tab_cv;
+    std::map<TvKey, TensorRec> tensors;
+
+    std::atomic<uint64_t> inflight_d2h{0}, inflight_h2d{0}, evicts{0}, restores{0}, d2h_done{0}, h2d_done{0};
+    std::atomic<uint64_t> d2h_bytes{0}, h2d_bytes{0}, registered_bytes{0}, d2h_ns{0}, h2d_ns{0};
+    std::atomic<bool> stop{false}, hb_paused{false};
+    std::thread progress_thr, heartbeat_thr;
+
+    // ------------------------------------------------------------------
+    explicit Impl(const AgentOptions& o) : opt(o) {
+        gpu = opt.device >= 0;
+        if (gpu) {
+            CUDA_OK(cudaSetDevice(opt.device));
+            if (opt.numa_node < 0) {
+                char bus[32] = {0};
+                if (cudaDeviceGetPCIBusId(bus, sizeof(bus), opt.device) == cudaSuccess) numa = pci_numa_node(bus);
+                if (numa < 0) numa = 0;
+            } else {
+                numa = opt.numa_node;
+            }
+        } else {
+            numa = opt.numa_node < 0 ? 0 : opt.numa_node;
+        }
+        rpc.reset(new RpcClient(uds_connect(opt.socket_path)));
+        RegisterRankRequest rq;
+        rq.rank_id = opt.rank_id;
+        rq.local_rank = opt.local_rank;
+        rq.world_rank = opt.world_rank;
+        rq.gpu_id = gpu ? uint32_t(opt.device) : 0xFFFFu;
+        rq.numa_node = uint32_t(numa);
+        rq.pid = uint64_t(::getpid());
+        std::vector<int> fds;
+        RegisterRankResponse rr = rpc->call<Op::kRegisterRank>(rq, &fds);
+        ++rpc_count;
+        if (!rr.ok) {
+            for (int f : fds) ::close(f);
+            throw std::runtime_error("RegisterRank rejected: " + rr.message);
+        }
+        epoch = rr.rank_epoch;
+        try {
+            for (const ArenaFd& a : rr.arenas) {
+                if (a.fd_index >= fds.size()) throw std::runtime_error("arena fd index out of range");
+                void* p = ::mmap(nullptr, a.size, PROT_READ | PROT_WRITE, MAP_SHARED, fds[a.fd_index], 0);
+                if (p == MAP_FAILED) throw std::runtime_error(std::string("mmap arena: ") + std::strerror(errno));
+                ArenaMap m;
+                m.id = a.arena_id;
+                m.base = static_cast<char*>(p);
+                m.size = a.size;
+                arenas.push_back(m);
+            }
+            if (rr.control_fd_index >= fds.size()) throw std::runtime_error("control fd index out of range");
+            control_size = rr.control_size;
+            void* c = ::mmap(nullptr, control_size, PROT_READ | PROT_WRITE, MAP_SHARED, fds[rr.control_fd_index], 0);
+            if (c == MAP_FAILED) throw std::runtime_error(std::string("mmap control: ") + std::strerror(errno));
+            control = static_cast<char*>(c);
+        } catch (...) {
+            for (int f : fds) ::close(f);
+            unmap_all();
+            throw;
+        }
+        for (int f : fds) ::close(f);
+        auto* h = header_of(control);
+        if (h->magic != OFLD_MAGIC || h->abi_version != OFLD_ABI_VERSION) {
+            unmap_all();
+            throw std::runtime_error("control region magic/ABI mismatch");
+        }
+        slots = slots_of(control);
+        num_slots = h->num_slots;
+        if (opt.use_ring && rr.ring_index != 0xFFFFFFFFu) {
+            RingHeader* r = ring_at(control, rr.ring_index);
+            if (r && r->owner_rank == opt.rank_id && r->rank_epoch == epoch) ring = r;
+        }
+        if (gpu) {
+            int lo = 0, hi = 0;
+            cudaDeviceGetStreamPriorityRange(&lo, &hi);
+            int prio = opt.stream_priority < 0 ? hi : 0;
+            CUDA_OK(cudaStreamCreateWithPriority(&stream, cudaStreamNonBlocking, prio));
+            if (opt.eager_register)
+                for (ArenaMap& m : arenas) register_arena(m);
+        }
+        progress_thr = std::thread([this] { progress_loop(); });
+        heartbeat_thr = std::thread([this] { heartbeat_loop(); });
+        LOG_INFO(TAG, "rank %u epoch %llu %s numa %d, %zu arenas, %u slots, ring %s", opt.rank_id,
+                 (unsigned long long)epoch, gpu ? ("gpu " + std::to_string(opt.device)).c_str() : "host-mode", numa,
+                 arenas.size(), num_slots, ring ? "on" : "off");
+    }
+
+    ~Impl() {
+        stop.store(true);
+        if (progress_thr.joinable()) progress_thr.join();
+        if (heartbeat_thr.joinable()) heartbeat_thr.join();
+        try {
+            drain_all();
+        } catch (...) {
+        }
+        if (stream) cudaStreamDestroy(stream);
+        pool.clear();
+        unmap_all();
+    }
+
+    void unmap_all() {
+        std::lock_guard<std::mutex> g(reg_mu);
+        for (ArenaMap& m : arenas) {
+            if (m.registered) {
+                cudaHostUnregister(m.base);
+                cudaGetLastError();
+            }
+            if (m.base) ::munmap(m.base, m.size);
+        }
+        arenas.clear();
+        if (control) ::munmap(control, control_size);
+        control = nullptr;
+    }
+
+    template <Op O>
+    typename OpTypes<O>::Response call(const typename OpTypes<O>::Request& r) {
+        ++rpc_count;
+        return rpc->call<O>(r);
+    }
+
+    // One cudaHostRegister per arena, whole-range (a copy must not span two
+    // registrations), mapped so kernels address it directly.
+    void register_arena(ArenaMap& m) {
+        std::lock_guard<std::mutex> g(reg_mu);
+        if (m.registered) return;
+        uint64_t t0 = mono_ns();
+        cudaError_t e = cudaHostRegister(m.base, m.size, cudaHostRegisterPortable | cudaHostRegisterMapped);
+        if (e == cudaErrorHostMemoryAlreadyRegistered) {
+            cudaGetLastError();
+        } else if (e != cudaSuccess) {
+            throw std::runtime_error(std::string("cudaHostRegister(arena): ") + cudaGetErrorString(e));
+        }
+        void* dev = nullptr;
+        CUDA_OK(cudaHostGetDevicePointer(&dev, m.base, 0));
+        m.dev = static_cast<char*>(dev);
+        m.registered = true;
+        registered_bytes += m.size;
+        LOG_INFO(TAG, "registered arena %llu: %llu MiB in %.1f ms", (unsigned long long)m.id,
+                 (unsigned long long)(m.size >> 20), double(mono_ns() - t0) / 1e6);
+    }
+
+    ArenaMap& arena(uint64_t id) {
+        for (ArenaMap& m : arenas)
+            if (m.id == id) return m;
+        throw std::runtime_error("unknown arena id " + std::to_string(id));
+    }
+
+    // Host pointer and (GPU mode) device alias of (arena, offset, nbytes).
+    void resolve(uint64_t arena_id, uint64_t off, uint64_t nbytes, char** host, char** dev) {
+        ArenaMap& m = arena(arena_id);
+        if (off + nbytes > m.size) throw std::runtime_error("slot range outside arena");
+        *host = m.base + off;
+        if (gpu) {
+            register_arena(m);
+            *dev = m.dev + off;
+        } else {
+            *dev = nullptr;
+        }
+    }
+
+    cudaStream_t stream_of(StreamHandle s) const {
+        return s == kInternalStream ? stream : reinterpret_cast<cudaStream_t>(s);
+    }
+
+    // ---- completions -----------------------------------------------------
+    bool ring_push_entry(EventType ev, const Pending& p, uint64_t* seq) {
+        if (!ring) return false;
+        std::lock_guard<std::mutex> g(ring_mu);
+        ofld_completion_entry_t e{};
+        e.lease_id = p.lease;
+        e.tensor_id = p.tid;
+        e.version = p.ver;
+        e.slot_id = p.slot;
+        e.event_type = uint32_t(ev);
+        e.timestamp_ns = real_ns();
+        uint64_t t = ring->tail.load(std::memory_order_relaxed);
+        if (!ring_push(ring, e)) return false;
+        if (seq) *seq = t;
+        return true;
+    }
+
+    void wait_ring_consumed(uint64_t seq) {
+        if (!ring || seq == ~0ull) return;
+        uint64_t deadline = mono_ns() + 30ull * 1000000000ull;
+        while (ring->head.load(std::memory_order_acquire) <= seq) {
+            if (mono_ns() > deadline) throw std::runtime_error("daemon did not consume completion ring");
+            sleep_us(10);
+        }
+    }
+
+    void report_d2h(const Pending& p) {
+        uint64_t seq = ~0ull;
+        // keep_pinned cannot travel through the ring; the RPC carries it.
+        if (!ring_push_entry(EventType::kD2HComplete, p, &seq)) {
+            TransferMark m;
+            m.rank_id = opt.rank_id;
+            m.rank_epoch = epoch;
+            m.lease_id = p.lease;
+            m.tensor_id = p.tid;
+            m.version = p.ver;
+            m.slot_id = p.slot;
+            m.timestamp_ns = real_ns();
+            MarkD2HCompleteResponse r = call<Op::kMarkD2HComplete>(m);
+            if (!r.ok) LOG_ERR(TAG, "MarkD2HComplete rejected for tensor %llu", (unsigned long long)p.tid);
+        }
+        std::lock_guard<std::mutex> g(tab_mu);
+        tensors[{p.tid, p.ver}].ring_seq = seq;
+    }
+
+    void report_h2d(const Pending& p) {
+        if (p.keep_pinned || !ring_push_entry(EventType::kH2DComplete, p, nullptr)) {
+            MarkH2DCompleteRequest m;
+            m.rank_id = opt.rank_id;
+            m.rank_epoch = epoch;
+            m.lease_id = p.lease;
+            m.tensor_id = p.tid;
+            m.version = p.ver;
+            m.slot_id = p.slot;
+            m.keep_pinned = p.keep_pinned;
+            m.timestamp_ns = real_ns();
+            StatusResponse r = call<Op::kMarkH2DComplete>(m);
+            if (!r.ok) LOG_ERR(TAG, "MarkH2DComplete rejected for tensor %llu: %s", (unsigned long long)p.tid,
+                               r.message.c_str());
+        }
+    }
+
+    // Retire one completed transfer (copy finished).
+    void finish(Pending& p) {
+        if (p.d2h) {
+            uint64_t lo = 0, hi = 0;
+            std::vector<uint64_t> dig;
+            if (p.dig.host) {
+                const uint64_t* d = static_cast<const uint64_t*>(p.dig.host);
+                ssh::Object o = ssh::fold_digests(d, p.ndig, p.nbytes);
+                lo = o.lo;
+                hi = o.hi;
+                if (opt.keep_digests) dig.assign(d, d + p.ndig);
+                pool.put(p.dig);
+            }
+            report_d2h(p);
+            {
+                std::lock_guard<std::mutex> g(tab_mu);
+                TensorRec& t = tensors[{p.tid, p.ver}];
+                t.offloaded = true;
+                t.restored = false;
+                t.hash_lo = lo;
+                t.hash_hi = hi;
+                t.lease = p.lease;
+                t.digests = std::move(dig);
+            }
+            inflight_d2h -= p.nbytes;
+            ++d2h_done;
+            d2h_bytes += p.nbytes;
+            if (p.cb) p.cb();
+        } else {
+            report_h2d(p);
+            {
+                std::lock_guard<std::mutex> g(tab_mu);
+                tensors[{p.tid, p.ver}].restored = true;
+            }
+            inflight_h2d -= p.nbytes;
+            ++h2d_done;
+            h2d_bytes += p.nbytes;
+            pool.put(p.mism);
+            pool.put(p.exp);
+            if (p.cb) p.cb();
+        }
+        if (p.ev) cudaEventDestroy(p.ev);
+        p.ev = nullptr;
+        tab_cv.notify_all();
+    }
+
+    void progress_loop() {
+        if (gpu) cudaSetDevice(opt.device);
+        pin_thread_to_node(numa);
+        const uint64_t poll = opt.progress_poll_us ? opt.progress_poll_us : 50;
+        while (!stop.load()) {
+            std::list<Pending> done;
+            {
+                std::lock_guard<std::mutex> g(inflight_mu);
+                for (auto it = inflight.begin(); it != inflight.end();) {
+                    cudaError_t st = cudaEventQuery(it->ev);
+                    if (st == cudaErrorNotReady) {
+                        ++it;
+                        continue;
+                    }
+                    if (st != cudaSuccess) LOG_ERR(TAG, "transfer failed: %s", cudaGetErrorString(st));
+                    auto nx = std::next(it);
+                    done.splice(done.end(), inflight, it);
+                    it = nx;
+                }
+            }
+            for (Pending& p : done) {
+                try {
+                    finish(p);
+                } catch (const std::exception& e) {
+                    LOG_ERR(TAG, "completion failed: %s", e.what());
+                }
+            }
+            if (done.empty()) sleep_us(poll);
+        }
+    }
+
+    void drain_all() {
+        std::list<Pending> all;
+        {
+            std::lock_guard<std::mutex> g(inflight_mu);
+            all.swap(inflight);
+        }
+        for (Pending& p : all) {
+            if (p.ev) cudaEventSynchronize(p.ev);
+            finish(p);
+        }
+    }
+
+    void heartbeat_loop() {
+        const uint64_t period = opt.heartbeat_ms ? opt.heartbeat_ms : 1000;
+        uint64_t next = mono_ns() + period * 1000000ull;
+        while (!stop.load()) {
+            sleep_us(10000);
+            if (mono_ns() < next || hb_paused.load()) continue;
+            next = mono_ns() + period * 1000000ull;
+            HeartbeatRequest hb{opt.rank_id, epoch, real_ns()};
+            try {
+                StatusResponse r = call<Op::kHeartbeat>(hb);
+                if (!r.ok) LOG_ERR(TAG, "heartbeat rejected: %s (session invalidated?)", r.message.c_str());
+            } catch (const std::exception& e) {
+                LOG_ERR(TAG, "heartbeat failed: %s", e.what());
+            }
+        }
+    }
+
+    // Launch K1 (or the copy-engine A/B path) for one reserved run.
+    void launch_d2h(Pending& p, uint64_t src, char* dst_host, char* dst_dev, cudaStream_t s, bool hash) {
+        if (!gpu) {
+            std::memcpy(dst_host, reinterpret_cast<const void*>(src), p.nbytes);
+            if (hash) {
+                p.ndig = kern::digest_count(p.nbytes);
+                p.dig.host = std::malloc(std::max<uint64_t>(p.ndig, 1) * 8);  // host mode: plain memory
+                ssh::host_chunk_digests(dst_host, p.nbytes, static_cast<uint64_t*>(p.dig.host));
+            }
+            return;
+        }
+        uint64_t* dig_dev = nullptr;
+        if (hash) {
+            p.ndig = kern::digest_count(p.nbytes);
+            p.dig = pool.get(std::max<uint64_t>(p.ndig, 1) * 8);
+            dig_dev = static_cast<uint64_t*>(p.dig.dev);
+        }
+        if (opt.engine == "copy_engine") {
+            if (hash) CUDA_OK(kern::hash_device(reinterpret_cast<const void*>(src), p.nbytes, dig_dev, s, opt.hash_ctas));
+            CUDA_OK(cudaMemcpyAsync(dst_host, reinterpret_cast<const void*>(src), p.nbytes, cudaMemcpyDeviceToHost, s));
+        } else {
+            CUDA_OK(kern::evict_hash(reinterpret_cast<const void*>(src), dst_dev, p.nbytes, dig_dev, s, opt.evict_ctas));
+        }
+        CUDA_OK(cudaEventCreateWithFlags(&p.ev, cudaEventDisableTiming));
+        CUDA_OK(cudaEventRecord(p.ev, s));
+    }
+
+    void complete_or_queue(Pending&& p, bool wait) {
+        if (!gpu || wait) {
+            if (p.ev) CUDA_OK(cudaEventSynchronize(p.ev));
+            if (!gpu && p.dig.host) {
+                // host-mode digests are malloc'd, not pooled
+                const uint64_t* d = static_cast<const uint64_t*>(p.dig.host);
+                std::vector<uint64_t> keep(d, d + p.ndig);
+                std::free(p.dig.host);
+                p.dig = {};
+                ssh::Object o = ssh::fold_digests(keep.data(), keep.size(), p.nbytes);
+                report_d2h(p);
+                {
+                    std::lock_guard<std::mutex> g(tab_mu);
+                    TensorRec& t = tensors[{p.tid, p.ver}];
+                    t.offloaded = true;
+                    t.restored = false;
+                    t.hash_lo = o.lo;
+                    t.hash_hi = o.hi;
+                    t.lease = p.lease;
+                    if (opt.keep_digests) t.digests = std::move(keep);
+                }
+                inflight_d2h -= p.nbytes;
+                ++d2h_done;
+                d2h_bytes += p.nbytes;
+                if (p.cb) p.cb();
+                tab_cv.notify_all();
+                return;
+            }
+            finish(p);
+            return;
+        }
+        std::lock_guard<std::mutex> g(inflight_mu);
+        inflight.push_back(std::move(p));
+    }
+};
+
+// ============================================================================
+Agent::Agent(const AgentOptions& opt) : d_(new Impl(opt)) {}
+Agent::~Agent() = default;
+
+EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive, uint64_t tensor_id,
+                         uint64_t version, const std::string& name, DoneCallback on_done, bool wait) {
+    Impl& D = *d_;
+    EvictTicket t;
+    t.tensor_id = tensor_id;
+    t.version = version;
+    t.nbytes = nbytes;
+    if (nbytes == 0) {
+        t.message = "nbytes must be > 0";
+        return t;
+    }
+    RequestOffloadRequest rq;
+    rq.rank_id = D.opt.rank_id;
+    rq.rank_epoch = D.epoch;
+    rq.tensor_id = tensor_id;
+    rq.version = version;
+    rq.nbytes = nbytes;
+    rq.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
+    rq.numa_node = uint32_t(D.numa);
+    rq.alignment = 256;
+    rq.flags = OFLD_FLAG_ALLOW_OVERFLOW | (destructive ? OFLD_FLAG_DESTRUCTIVE : 0) |
+               (D.opt.fast_submit ? OFLD_FLAG_SUBMIT_ON_GRANT : 0);
+    rq.debug_name = name;
+    RequestOffloadResponse g = D.call<Op::kRequestOffload>(rq);
+    if (!g.ok || g.blocked) {
+        t.message = g.ok ? "offload blocked (pinned pressure)" : g.message;
+        return t;
+    }
+    ++D.evicts;
+    char *host = nullptr, *dev = nullptr;
+    D.resolve(g.arena_id, g.arena_offset, nbytes, &host, &dev);
+    if (g.state != OFLD_SLOT_D2H_IN_FLIGHT) {
+        TransferMark m{D.opt.rank_id, D.epoch, g.lease_id, tensor_id, version, g.slot_id, 0, real_ns()};
+        StatusResponse sr = D.call<Op::kMarkD2HSubmitted>(m);
+        if (!sr.ok) LOG_WARN(TAG, "MarkD2HSubmitted: %s (continuing)", sr.message.c_str());
+    }
+    Impl::Pending p;
+    p.d2h = true;
+    p.lease = g.lease_id;
+    p.tid = tensor_id;
+    p.ver = version;
+    p.slot = g.slot_id;
+    p.nbytes = nbytes;
+    p.cb = std::move(on_done);
+    D.inflight_d2h += nbytes;
+    {
+        std::lock_guard<std::mutex> lg(D.tab_mu);
+        Impl::TensorRec& r = D.tensors[{tensor_id, version}];
+        r.offloaded = false;
+        r.lease = g.lease_id;
+    }
+    D.launch_d2h(p, ptr, host, dev, D.stream_of(stream), D.opt.hash_on_evict);
+    D.complete_or_queue(std::move(p), wait);
+    t.ok = true;
+    t.message = "ok";
+    t.lease_id = g.lease_id;
+    t.slot_id = g.slot_id;
+    if (wait) tensor_hash(tensor_id, version, &t.hash_lo, &t.hash_hi);
+    return t;
+}
+
+std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait) {
+    Impl& D = *d_;
+    std::vector<EvictTicket> out(items.size());
+    BatchRequestOffloadRequest br;
+    br.rank_id = D.opt.rank_id;
+    br.rank_epoch = D.epoch;
+    for (const BatchItem& it : items) {
+        RequestOffloadRequest rq;
+        rq.tensor_id = it.tensor_id;
+        rq.version = it.version;
+        rq.nbytes = it.nbytes;
+        rq.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
+        rq.numa_node = uint32_t(D.numa);
+        rq.alignment = 256;
+        rq.flags = OFLD_FLAG_ALLOW_OVERFLOW | OFLD_FLAG_SUBMIT_ON_GRANT;
+        br.items.push_back(rq);
+    }
+    BatchRequestOffloadResponse resp = D.call<Op::kBatchRequestOffload>(br);
+    cudaStream_t s = D.stream_of(stream);
+    std::vector<Impl::Pending> launched;
+    for (size_t i = 0; i < items.size() && i < resp.grants.size(); ++i) {
+        const RequestOffloadResponse& g = resp.grants[i];
+        EvictTicket& t = out[i];
+        t.tensor_id = items[i].tensor_id;
+        t.version = items[i].version;
+        t.nbytes = items[i].nbytes;
+        if (!g.ok || g.blocked) {
+            t.message = g.ok ? "offload blocked (pinned pressure)" : g.message;
+            continue;
+        }
+        char *host = nullptr, *dev = nullptr;
+        D.resolve(g.arena_id, g.arena_offset, items[i].nbytes, &host, &dev);
+        Impl::Pending p;
+        p.lease = g.lease_id;
+        p.tid = items[i].tensor_id;
+        p.ver = items[i].version;
+        p.slot = g.slot_id;
+        p.nbytes = items[i].nbytes;
+        D.inflight_d2h += p.nbytes;
+        ++D.evicts;
+        {
+            std::lock_guard<std::mutex> lg(D.tab_mu);
+            D.tensors[{p.tid, p.ver}].offloaded = false;
+        }
+        D.launch_d2h(p, items[i].ptr, host, dev, s, D.opt.hash_on_evict);
+        t.ok = true;
+        t.lease_id = g.lease_id;
+        t.slot_id = g.slot_id;
+        launched.push_back(std::move(p));
+    }
+    // Every launch recorded its own event; the last one covers the batch on
+    // this stream, so a waiting caller synchronizes once.
+    if (wait && D.gpu && !launched.empty()) CUDA_OK(cudaEventSynchronize(launched.back().ev));
+    for (Impl::Pending& p : launched) D.complete_or_queue(std::move(p), wait);
+    return out;
+}
+
+RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr, uint64_t nbytes,
+                              StreamHandle stream, bool wait, const RestoreOptions& ro) {
+    Impl& D = *d_;
+    RestoreOutcome out;
+    uint64_t seq = ~0ull;
+    std::vector<uint64_t> expect;
+    {
+        std::lock_guard<std::mutex> g(D.tab_mu);
+        auto it = D.tensors.find({tensor_id, version});
+        if (it != D.tensors.end()) {
+            seq = it->second.ring_seq;
+            if (ro.verify) expect = it->second.digests;
+            it->second.restored = false;
+        }
+    }
+    D.wait_ring_consumed(seq);
+    RequestPrefetchRequest pr;
+    pr.rank_id = D.opt.rank_id;
+    pr.rank_epoch = D.epoch;
+    pr.tensor_id = tensor_id;
+    pr.version = version;
+    pr.nbytes = nbytes;
+    pr.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
+    pr.numa_node = uint32_t(D.numa);
+    pr.flags = D.opt.fast_submit ? OFLD_FLAG_SUBMIT_ON_READY : 0;
+    RequestPrefetchResponse r = D.call<Op::kRequestPrefetch>(pr);
+    const uint64_t deadline = mono_ns() + 600ull * 1000000000ull;
+    while (r.ok && !r.ready) {
+        if (mono_ns() > deadline) {
+            out.message = "restore: readback timed out";
+            return out;
+        }
+        sleep_us(D.opt.prefetch_poll_us);
+        r = D.call<Op::kRequestPrefetch>(pr);
+    }
+    if (!r.ok) {
+        out.message = r.message;
+        return out;
+    }
+    const uint64_t src_bytes = r.nbytes ? r.nbytes : nbytes;
+    uint32_t st = r.slot_id < D.num_slots ? D.slots[r.slot_id].state.load(std::memory_order_acquire) : 0;
+    bool submitted = r.state == OFLD_SLOT_H2D_IN_FLIGHT;
+    if (!(st == OFLD_SLOT_PINNED_VALID || (submitted && st == OFLD_SLOT_H2D_IN_FLIGHT))) {
+        out.message = "restore: slot not readable at H2D time";
+        return out;
+    }
+    if (ro.cast == 0 && src_bytes != nbytes) {
+        out.message = "restore: destination size " + std::to_string(nbytes) + " != offloaded size " +
+                      std::to_string(src_bytes);
+        return out;
+    }
+    char *host = nullptr, *dev = nullptr;
+    D.resolve(r.arena_id, r.arena_offset, src_bytes, &host, &dev);
+    if (!submitted) {
+        TransferMark m{D.opt.rank_id, D.epoch, r.lease_id, tensor_id, r.version, r.slot_id, 0, real_ns()};
+        StatusResponse sr = D.call<Op::kMarkH2DSubmitted>(m);
+        if (!sr.ok) {
+            out.message = "MarkH2DSubmitted: " + sr.message;
+            return out;
+        }
+    }
+    ++D.restores;
+    Impl::Pending p;
+    p.d2h = false;
+    p.lease = r.lease_id;
+    p.tid = tensor_id;
+    p.ver = r.version ? r.version : version;
+    p.slot = r.slot_id;
+    p.nbytes = src_bytes;
+    p.keep_pinned = ro.keep_pinned;
+    D.inflight_h2d += src_bytes;
+    uint32_t* mism_dev = nullptr;
+    if (!D.gpu) {
+        if (ro.cast != 0) {
+            out.message = "casts need a GPU";
+            return out;
+        }
+        std::memcpy(reinterpret_cast<void*>(ptr), host, src_bytes);
+        if (ro.verify && !expect.empty()) {
+            std::vector<uint64_t> got(kern::digest_count(src_bytes));
+            ssh::host_chunk_digests(host, src_bytes, got.data());
+            for (size_t i = 0; i < got.size() && i < expect.size(); ++i) out.mismatched_chunks += got[i] != expect[i];
+        }
+        D.finish(p);
+        out.ok = out.mismatched_chunks == 0;
+        out.message = out.ok ? "ok" : "content digest mismatch";
+        return out;
+    }
+    cudaStream_t s = D.stream_of(stream);
+    const uint64_t* exp_dev = nullptr;
+    if (ro.verify && !expect.empty()) {
+        p.exp = D.pool.get(expect.size() * 8);  // returned to the pool when the copy retires
+        std::memcpy(p.exp.host, expect.data(), expect.size() * 8);
+        exp_dev = static_cast<const uint64_t*>(p.exp.dev);
+        p.mism = D.pool.get(64);
+        std::memset(p.mism.host, 0, 4);
+        mism_dev = static_cast<uint32_t*>(p.mism.dev);
+    }
+    if (D.opt.engine == "copy_engine" && ro.cast == 0 && !exp_dev) {
+        CUDA_OK(cudaMemcpyAsync(reinterpret_cast<void*>(ptr), host, src_bytes, cudaMemcpyHostToDevice, s));
+    } else {
+        CUDA_OK(kern::restore_cast(dev, reinterpret_cast<void*>(ptr), src_bytes, kern::Cast(ro.cast),
+                                   reinterpret_cast<float*>(ro.scales_ptr), exp_dev, mism_dev, s, D.opt.restore_ctas));
+    }
+    CUDA_OK(cudaEventCreateWithFlags(&p.ev, cudaEventDisableTiming));
+    CUDA_OK(cudaEventRecord(p.ev, s));
+    if (wait) {
+        CUDA_OK(cudaEventSynchronize(p.ev));
+        if (mism_dev) out.mismatched_chunks = *static_cast<volatile uint32_t*>(p.mism.host);
+        D.finish(p);
+        out.ok = out.mismatched_chunks == 0;
+        out.message = out.ok ? "ok" : "content digest mismatch";
+        return out;
+    }
+    D.complete_or_queue(std::move(p), false);
+    out.ok = true;
+    out.message = "ok";
+    return out;
+}
+
+std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait) {
+    Impl& D = *d_;
+    std::vector<RestoreOutcome> out(items.size());
+    uint64_t maxseq = ~0ull;
+    {
+        std::lock_guard<std::mutex> g(D.tab_mu);
+        for (const BatchItem& it : items) {
+            auto f = D.tensors.find({it.tensor_id, it.version});
+            if (f != D.tensors.end() && f->second.ring_seq != ~0ull)
+                maxseq = maxseq == ~0ull ? f->second.ring_seq : std::max(maxseq, f->second.ring_seq);
+        }
+    }
+    D.wait_ring_consumed(maxseq);
+    BatchRequestPrefetchRequest br;
+    br.rank_id = D.opt.rank_id;
+    br.rank_epoch = D.epoch;
+    for (const BatchItem& it : items) {
+        RequestPrefetchRequest pr;
+        pr.tensor_id = it.tensor_id;
+        pr.version = it.version;
+        pr.nbytes = it.nbytes;
+        pr.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
+        pr.numa_node = uint32_t(D.numa);
+        pr.flags = OFLD_FLAG_SUBMIT_ON_READY;
+        br.items.push_back(pr);
+    }
+    std::vector<size_t> pending(items.size());
+    for (size_t i = 0; i < items.size(); ++i) pending[i] = i;
+    cudaStream_t s = D.stream_of(stream);
+    std::vector<Impl::Pending> launched;
+    const uint64_t deadline = mono_ns() + 600ull * 1000000000ull;
+    while (!pending.empty()) {
+        BatchRequestPrefetchRequest q;
+        q.rank_id = br.rank_id;
+        q.rank_epoch = br.rank_epoch;
+        for (size_t i : pending) q.items.push_back(br.items[i]);
+        BatchRequestPrefetchResponse resp = D.call<Op::kBatchRequestPrefetch>(q);
+        std::vector<size_t> again;
+        for (size_t k = 0; k < pending.size() && k < resp.results.size(); ++k) {
+            size_t i = pending[k];
+            const RequestPrefetchResponse& r = resp.results[k];
+            if (!r.ok) {
+                out[i].message = r.message;
+                continue;
+            }
+            if (!r.ready) {
+                again.push_back(i);
+                continue;
+            }
+            char *host = nullptr, *dev = nullptr;
+            D.resolve(r.arena_id, r.arena_offset, r.nbytes, &host, &dev);
+            Impl::Pending p;
+            p.d2h = false;
+            p.lease = r.lease_id;
+            p.tid = items[i].tensor_id;
+            p.ver = r.version;
+            p.slot = r.slot_id;
+            p.nbytes = r.nbytes;
+            D.inflight_h2d += p.nbytes;
+            ++D.restores;
+            if (D.gpu) {
+                CUDA_OK(kern::restore_cast(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes, kern::Cast::kNone,
+                                           nullptr, nullptr, nullptr, s, D.opt.restore_ctas));
+                CUDA_OK(cudaEventCreateWithFlags(&p.ev, cudaEventDisableTiming));
+                CUDA_OK(cudaEventRecord(p.ev, s));
+            } else {
+                std::memcpy(reinterpret_cast<void*>(items[i].ptr), host, r.nbytes);
+            }
+            out[i].ok = true;
+            out[i].message = "ok";
+            launched.push_back(std::move(p));
+        }
+        pending.swap(again);
+        if (!pending.empty()) {
+            if (mono_ns() > deadline) {
+                for (size_t i : pending) out[i].message = "readback timed out";
+                break;
+            }
+            sleep_us(D.opt.prefetch_poll_us);
+        }
+    }
+    if (wait && D.gpu && !launched.empty()) CUDA_OK(cudaEventSynchronize(launched.back().ev));
+    for (Impl::Pending& p : launched) {
+        if (!D.gpu || wait)
+            D.finish(p);
+        else
+            D.complete_or_queue(std::move(p), false);
+    }
+    return out;
+}
+
+bool Agent::is_offloaded(uint64_t tid, uint64_t ver) const {
+    std::lock_guard<std::mutex> g(d_->tab_mu);
+    auto it = d_->tensors.find({tid, ver});
+    return it != d_->tensors.end() && it->second.offloaded;
+}
+
+void Agent::wait_offloaded(uint64_t tid, uint64_t ver) {
+    std::unique_lock<std::mutex> g(d_->tab_mu);
+    d_->tab_cv.wait(g, [&] {
+        auto it = d_->tensors.find({tid, ver});
+        return it == d_->tensors.end() || it->second.offloaded;
+    });
+}
+
+bool Agent::is_restored(uint64_t tid, uint64_t ver) const {
+    std::lock_guard<std::mutex> g(d_->tab_mu);
+    auto it = d_->tensors.find({tid, ver});
+    return it != d_->tensors.end() && it->second.restored;
+}
+
+void Agent::wait_restored(uint64_t tid, uint64_t ver) {
+    std::unique_lock<std::mutex> g(d_->tab_mu);
+    d_->tab_cv.wait(g, [&] {
+        auto it = d_->tensors.find({tid, ver});
+        return it == d_->tensors.end() || it->second.restored;
+    });
+}
+
+bool Agent::tensor_hash(uint64_t tid, uint64_t ver, uint64_t* lo, uint64_t* hi) const {
+    std::lock_guard<std::mutex> g(d_->tab_mu);
+    auto it = d_->tensors.find({tid, ver});
+    if (it == d_->tensors.end() || !it->second.offloaded) return false;
+    *lo = it->second.hash_lo;
+    *hi = it->second.hash_hi;
+    return true;
+}
+
+// Completions published through the ring are applied by the daemon
+// asynchronously; queries about a tensor first wait until its entry is consumed.
+static uint64_t ring_seq_of(Agent::Impl& D, uint64_t tid, uint64_t ver) {
+    std::lock_guard<std::mutex> g(D.tab_mu);
+    auto it = D.tensors.find({tid, ver});
+    return it == D.tensors.end() ? ~0ull : it->second.ring_seq;
+}
+
+std::string Agent::location(uint64_t tid, uint64_t ver) {
+    d_->wait_ring_consumed(ring_seq_of(*d_, tid, ver));
+    LocationQueryResponse r = d_->call<Op::kQueryLocation>(LocationQueryRequest{tid, ver});
+    if (!r.ok) return "none";
+    switch (r.location_kind) {
+        case OFLD_LOC_GPU: return "gpu";
+        case OFLD_LOC_PINNED: return "pinned";
+        case OFLD_LOC_PAGEABLE: return "pageable";
+        case OFLD_LOC_NVME: return "nvme";
+        default: return "none";
+    }
+}
+
+void Agent::discard(uint64_t tid, uint64_t ver) {
+    Impl& D = *d_;
+    D.wait_ring_consumed(ring_seq_of(D, tid, ver));
+    DiscardTensorRequest r{D.opt.rank_id, D.epoch, tid, ver};
+    StatusResponse s = D.call<Op::kDiscardTensor>(r);
+    if (!s.ok) LOG_WARN(TAG, "discard(%llu:%llu): %s", (unsigned long long)tid, (unsigned long long)ver, s.message.c_str());
+    std::lock_guard<std::mutex> g(D.tab_mu);
+    D.tensors.erase({tid, ver});
+    D.tab_cv.notify_all();
+}
+
+void Agent::assert_no_inflight() const {
+    std::lock_guard<std::mutex> g(d_->inflight_mu);
+    if (!d_->inflight.empty())
+        throw std::runtime_error("assert_no_inflight: " + std::to_string(d_->inflight.size()) + " transfers in flight");
+}
+
+void Agent::synchronize() {
+    for (;;) {
+        {
+            std::lock_guard<std::mutex> g(d_->inflight_mu);
+            if (d_->inflight.empty()) return;
+        }
+        sleep_us(50);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Canonical model state
+// ---------------------------------------------------------------------------
+RegisterJobResponse Agent::register_job(const RegisterJobRequest& r) { return d_->call<Op::kRegisterJob>(r); }
+
+CanonicalOutcome Agent::canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
+                                        const RequestCanonicalEvictRequest& in, DoneCallback on_invalidate, bool wait) {
+    Impl& D = *d_;
+    CanonicalOutcome out;
+    RequestCanonicalEvictRequest req = in;
+    req.rank_id = D.opt.rank_id;
+    req.rank_epoch = D.epoch;
+    req.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
+    req.numa_node = uint32_t(D.numa);
+    req.destructive = destructive;
+    req.key.nbytes = nbytes;
+    if (req.key.shard_nbytes == 0) req.key.shard_nbytes = nbytes;
+    RequestCanonicalEvictResponse resp = D.call<Op::kRequestCanonicalEvict>(req);
+    out.action = resp.action;
+    out.object_id = resp.object_id;
+    out.message = resp.message;
+    if (!resp.ok) return out;
+    cudaStream_t s = D.stream_of(stream);
+
+    if (resp.action == offload_v2::ATTACH_ACTION_ATTACHED_EXISTING ||
+        resp.action == offload_v2::ATTACH_ACTION_WAIT_FOR_CREATOR) {
+        out.ok = true;
+        if (resp.action == offload_v2::ATTACH_ACTION_ATTACHED_EXISTING && destructive && on_invalidate) {
+            if (D.gpu) CUDA_OK(cudaStreamSynchronize(s));  // producer kernels done before the storage goes
+            on_invalidate();
+        }
+        return out;
+    }
+    if (resp.action == 6 /* verify-hash-only */) {
+        // Replica verification without a copy: hash the local GPU bytes.
+        hash_buffer(ptr, nbytes, stream, &out.hash_lo, &out.hash_hi);
+        CommitCanonicalObjectRequest cm;
+        cm.rank_id = D.opt.rank_id;
+        cm.rank_epoch = D.epoch;
+        cm.object_id = resp.object_id;
+        cm.lease_id = 0;
+        cm.content_hash_lo = out.hash_lo;
+        cm.content_hash_hi = out.hash_hi;
+        CommitCanonicalObjectResponse cr = D.call<Op::kCommitCanonicalObject>(cm);
+        out.ok = cr.ok;
+        out.message = cr.message;
+        if (cr.ok && destructive && on_invalidate) on_invalidate();
+        return out;
+    }
+    if (resp.action != offload_v2::ATTACH_ACTION_NEED_D2H_CREATE &&
+        resp.action != offload_v2::ATTACH_ACTION_DUPLICATE_CANDIDATE)
+        return out;
+
+    // Create or candidate: copy into the reserved run with the fused hash.
+    char *host = nullptr, *dev = nullptr;
+    D.resolve(resp.arena_id, resp.arena_offset, nbytes, &host, &dev);
+    TransferMark m{D.opt.rank_id, D.epoch, resp.lease_id, resp.synthetic_tid, 1, resp.slot_id, 0, real_ns()};
+    StatusResponse sr = D.call<Op::kMarkD2HSubmitted>(m);
+    if (!sr.ok) LOG_WARN(TAG, "canonical MarkD2HSubmitted: %s", sr.message.c_str());
+    ++D.evicts;
+    Impl::Pending p;
+    p.nbytes = nbytes;
+    D.launch_d2h(p, ptr, host, dev, s, true);
+    if (p.ev) CUDA_OK(cudaEventSynchronize(p.ev));
+    if (p.ev) cudaEventDestroy(p.ev);
+    ssh::Object h{0, 0};
+    if (p.dig.host) {
+        h = ssh::fold_digests(static_cast<const uint64_t*>(p.dig.host), p.ndig, nbytes);
+        if (D.gpu)
+            D.pool.put(p.dig);
+        else
+            std::free(p.dig.host);
+    }
+    D.d2h_bytes += nbytes;
+    ++D.d2h_done;
+    MarkD2HCompleteResponse dr = D.call<Op::kMarkD2HComplete>(m);
+    if (!dr.ok) {
+        out.message = "canonical MarkD2HComplete rejected";
+        return out;
+    }
+    const bool trusted = req.dedup_mode == offload_v2::DEDUP_SEMANTIC_TRUSTED || req.dedup_mode == offload_v2::DEDUP_DISABLED;
+    CommitCanonicalObjectRequest cm;
+    cm.rank_id = D.opt.rank_id;
+    cm.rank_epoch = D.epoch;
+    cm.object_id = resp.object_id;
+    cm.lease_id = resp.lease_id;
+    cm.slot_id = resp.slot_id;
+    if (!(trusted && D.opt.zero_canonical_hash)) {
+        cm.content_hash_lo = h.lo;
+        cm.content_hash_hi = h.hi;
+    }
+    CommitCanonicalObjectResponse cr = D.call<Op::kCommitCanonicalObject>(cm);
+    out.ok = cr.ok;
+    out.did_d2h = true;
+    out.message = cr.message;
+    out.hash_lo = h.lo;
+    out.hash_hi = h.hi;
+    if (cr.ok && destructive && on_invalidate) on_invalidate();
+    return out;
+}
+
+RestoreOutcome Agent::canonical_restore(uint64_t object_id, uint64_t ptr, uint64_t nbytes, StreamHandle stream,
+                                        bool wait, const RestoreOptions& ro) {
+    Impl& D = *d_;
+    RestoreOutcome out;
+    RequestCanonicalRestoreRequest rq{D.opt.rank_id, D.epoch, object_id, D.gpu ? uint32_t(D.opt.device) : 0,
+                                      uint32_t(D.numa)};
+    RequestCanonicalRestoreResponse rr;
+    const uint64_t deadline = mono_ns() + 600ull * 1000000000ull;
+    for (;;) {
+        rr = D.call<Op::kRequestCanonicalRestore>(rq);
+        if (rr.ok || !rr.retriable) break;
+        if (mono_ns() > deadline) {
+            out.message = "canonical_restore: object stuck transitioning";
+            return out;
+        }
+        sleep_us(D.opt.prefetch_poll_us);
+    }
+    if (!rr.ok) {
+        out.message = rr.message;
+        return out;
+    }
+    auto release = [&] {
+        try {
+            D.call<Op::kReleaseCanonicalRestore>(ReleaseCanonicalRestoreRequest{D.opt.rank_id, D.epoch, object_id});
+        } catch (...) {
+        }
+    };
+    if (ro.cast == 0 && nbytes > rr.nbytes) {
+        release();
+        out.message = "canonical_restore: destination larger than object";
+        return out;
+    }
+    try {
+        char *host = nullptr, *dev = nullptr;
+        D.resolve(rr.arena_id, rr.arena_offset, rr.nbytes, &host, &dev);
+        ++D.restores;
+        uint64_t n = ro.cast == 0 ? nbytes : rr.nbytes;
+        if (!D.gpu) {
+            std::memcpy(reinterpret_cast<void*>(ptr), host, n);
+        } else {
+            cudaStream_t s = D.stream_of(stream);
+            CUDA_OK(kern::restore_cast(dev, reinterpret_cast<void*>(ptr), n, kern::Cast(ro.cast),
+                                       reinterpret_cast<float*>(ro.scales_ptr), nullptr, nullptr, s,
+                                       D.opt.restore_ctas));
+            // The hold is released only after the copy finished reading.
+            CUDA_OK(cudaStreamSynchronize(s));
+        }
+        D.h2d_bytes += n;
+        ++D.h2d_done;
+        out.ok = true;
+        out.message = "ok";
+    } catch (const std::exception& e) {
+        out.message = std::string("canonical_restore: ") + e.what();
+    }
+    release();
+    (void)wait;
+    return out;
+}
+
+SealModelVersionResponse Agent::seal(const SealModelVersionRequest& r) { return d_->call<Op::kSealModelVersion>(r); }
+GetLatestSealedVersionResponse Agent::latest(const GetLatestSealedVersionRequest& r) {
+    return d_->call<Op::kGetLatestSealedVersion>(r);
+}
+GetManifestResponse Agent::manifest(const GetManifestRequest& r) { return d_->call<Op::kGetManifest>(r); }
+PullTensorResponse Agent::pull(const PullTensorRequest& r) { return d_->call<Op::kPullTensor>(r); }
+DropCanonicalVersionResponse Agent::drop_version(const DropCanonicalVersionRequest& r) {
+    return d_->call<Op::kDropCanonicalVersion>(r);
+}
+ReleaseCanonicalResponse Agent::release(const ReleaseCanonicalRequest& in) {
+    ReleaseCanonicalRequest r = in;
+    r.rank_id = d_->opt.rank_id;
+    r.rank_epoch = d_->epoch;
+    return d_->call<Op::kReleaseCanonical>(r);
+}
+ExportManifestResponse Agent::export_manifest(const ExportManifestRequest& r) {
+    return d_->call<Op::kExportManifest>(r);
+}
+GetJobStatsResponse Agent::job_stats(const GetJobStatsRequest& r) { return d_->call<Op::kGetJobStats>(r); }
+GetStatsResponse Agent::daemon_stats() { return d_->call<Op::kGetStats>(GetStatsRequest{}); }
+
+StatusResponse Agent::publish_peer_buffer(const PeerBufferDesc& desc, int fd) {
+    PublishPeerBufferRequest r;
+    r.rank_id = d_->opt.rank_id;
+    r.rank_epoch = d_->epoch;
+    r.desc = desc;
+    ++d_->rpc_count;
+    std::vector<int> fds;
+    if (fd >= 0) fds.push_back(fd);
+    return d_->rpc->call<Op::kPublishPeerBuffer>(r, nullptr, fds);
+}
+
+LookupPeerBufferResponse Agent::lookup_peer_buffer(const std::string& key, uint32_t wait_ms, int* fd_out) {
+    ++d_->rpc_count;
+    std::vector<int> fds;
+    LookupPeerBufferResponse r = d_->rpc->call<Op::kLookupPeerBuffer>(LookupPeerBufferRequest{key, wait_ms}, &fds);
+    if (fd_out) *fd_out = fds.empty() ? -1 : fds[0];
+    for (size_t i = fd_out ? 1 : 0; i < fds.size(); ++i) ::close(fds[i]);
+    return r;
+}
+
+void Agent::hash_buffer(uint64_t ptr, uint64_t nbytes, StreamHandle stream, uint64_t* lo, uint64_t* hi) {
+    Impl& D = *d_;
+    if (!D.gpu) {
+        ssh::Object o = ssh::host_hash(reinterpret_cast<const void*>(ptr), nbytes);
+        *lo = o.lo;
+        *hi = o.hi;
+        return;
+    }
+    uint64_t n = kern::digest_count(nbytes);
+    PinnedPool::Buf b = D.pool.get(std::max<uint64_t>(n, 1) * 8);
+    cudaStream_t s = D.stream_of(stream);
+    CUDA_OK(kern::hash_device(reinterpret_cast<const void*>(ptr), nbytes, static_cast<uint64_t*>(b.dev), s,
+                              D.opt.hash_ctas));
+    CUDA_OK(cudaStreamSynchronize(s));
+    ssh::Object o = ssh::fold_digests(static_cast<const uint64_t*>(b.host), n, nbytes);
+    D.pool.put(b);
+    *lo = o.lo;
+    *hi = o.hi;
+}
+
+uint64_t Agent::map_arena(uint64_t arena_id, uint64_t offset) const {
+    for (const Impl::ArenaMap& m : d_->arenas)
+        if (m.id == arena_id) return reinterpret_cast<uint64_t>(m.base + offset);
+    return 0;
+}
+
+AgentStats Agent::stats() const {
+    const Impl& D = *d_;
+    AgentStats s;
+    s.rank_id = D.opt.rank_id;
+    s.gpu_id = D.gpu ? D.opt.device : -1;
+    s.numa_node = D.numa;
+    s.registered_pinned_bytes = D.registered_bytes;
+    s.inflight_d2h_bytes = D.inflight_d2h;
+    s.inflight_h2d_bytes = D.inflight_h2d;
+    s.evict_count = D.evicts;
+    s.restore_count = D.restores;
+    s.d2h_completed = D.d2h_done;
+    s.h2d_completed = D.h2d_done;
+    s.rank_epoch = D.epoch;
+    s.num_slots = D.num_slots;
+    s.d2h_bytes = D.d2h_bytes;
+    s.h2d_bytes = D.h2d_bytes;
+    s.kernel_launches = D.gpu ? kern::launch_count() : 0;
+    s.rpc_count = D.rpc_count;
+    return s;
+}
+
+std::string Agent::summary_string() const {
+    AgentStats s = stats();
+    char buf[768];
+    std::snprintf(buf, sizeof(buf),
+                  "Agent rank=%u gpu=%d numa=%d epoch=%llu\n"
+                  "  registered_pinned_bytes=%llu\n"
+                  "  inflight: d2h=%llu bytes  h2d=%llu bytes\n"
+                  "  counts: evict=%llu restore=%llu d2h_done=%llu h2d_done=%llu\n"
+                  "  bytes: d2h=%llu h2d=%llu  kernel_launches=%llu rpcs=%llu\n"
+                  "  slots=%llu",
+                  s.rank_id, s.gpu_id, s.numa_node, (unsigned long long)s.rank_epoch,
+                  (unsigned long long)s.registered_pinned_bytes, (unsigned long long)s.inflight_d2h_bytes,
+                  (unsigned long long)s.inflight_h2d_bytes, (unsigned long long)s.evict_count,
+                  (unsigned long long)s.restore_count, (unsigned long long)s.d2h_completed,
+                  (unsigned long long)s.h2d_completed, (unsigned long long)s.d2h_bytes,
+                  (unsigned long long)s.h2d_bytes, (unsigned long long)s.kernel_launches,
+                  (unsigned long long)s.rpc_count, (unsigned long long)s.num_slots);
+    return buf;
+}
+
+int Agent::device() const { return d_->gpu ? d_->opt.device : -1; }
+int Agent::numa_node() const { return d_->numa; }
+uint32_t Agent::rank_id() const { return d_->opt.rank_id; }
+uint64_t Agent::rank_epoch() const { return d_->epoch; }
+void Agent::pause_heartbeat(bool paused) { d_->hb_paused.store(paused); }
+
+}  // namespace ofld

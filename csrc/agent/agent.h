@@ -1,0 +1,162 @@
+// Rank agent: the per-process side of the offload runtime.
+//
+// Connects to offloadd, maps the shared arenas and control region, registers
+// the arenas with CUDA once (host-mapped, so kernels address them directly),
+// and moves tensor bytes with the sm_100a kernels (kernels.h): K1 for evict
+// (copy + content hash in one pass), K2 for restore (copy + optional verify
+// and cast). A progress thread retires asynchronous transfers and publishes
+// completions through the shared completion ring; a heartbeat thread keeps
+// the session alive. Host mode (device < 0) serves CPU tensors with memcpy
+// and the host hash, so every control-plane path also runs without a GPU.
+//
+// Public API mirrors StateSpectre's OffloadAgent (reference:
+// src/agent/agent.h:112-217); the header carries no CUDA or torch types.
+#pragma once
+
+#include <cstdint>
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "ofld/protocol.h"
+
+namespace ofld {
+
+using StreamHandle = uintptr_t;
+constexpr StreamHandle kInternalStream = ~StreamHandle(0);
+using DoneCallback = std::function<void()>;
+
+struct AgentOptions {
+    std::string socket_path = "/tmp/state_spectre.sock";
+    int device = 0;  // CUDA device index; -1 = host mode
+    uint32_t rank_id = 0, local_rank = 0, world_rank = 0;
+    int numa_node = -1;  // -1: from the GPU's PCI affinity
+    bool eager_register = false;
+    uint64_t heartbeat_ms = 1000;
+    uint64_t progress_poll_us = 50;
+    uint64_t prefetch_poll_us = 200;
+    std::string engine = "kernel";  // "kernel" (SM copies) | "copy_engine" (cudaMemcpyAsync)
+    int evict_ctas = 0, restore_ctas = 0, hash_ctas = 0;
+    bool hash_on_evict = true;
+    bool use_ring = true;
+    bool fast_submit = true;     // reserve+submit and ready+submit in one round trip
+    bool keep_digests = true;    // remember chunk digests for verify-on-restore
+    bool zero_canonical_hash = false;  // commit hash 0 in trusted mode (manifest parity)
+    int stream_priority = 0;     // internal stream priority (0 = default)
+};
+
+struct EvictTicket {
+    bool ok = false;
+    std::string message;
+    uint64_t tensor_id = 0, version = 0, nbytes = 0, lease_id = 0;
+    uint32_t slot_id = 0;
+    uint64_t hash_lo = 0, hash_hi = 0;  // valid once the copy completed (wait=true)
+};
+
+struct RestoreOptions {
+    int cast = 0;               // kern::Cast
+    uint64_t scales_ptr = 0;    // device fp32 scales for fp8 casts
+    bool verify = false;        // re-hash while copying and compare with the evict-time digests
+    bool keep_pinned = false;   // keep the pinned copy resident after H2D
+};
+
+struct RestoreOutcome {
+    bool ok = false;
+    std::string message;
+    uint32_t mismatched_chunks = 0;
+};
+
+struct CanonicalOutcome {
+    bool ok = false;
+    std::string message;
+    uint32_t action = 0;
+    uint64_t object_id = 0;
+    bool did_d2h = false;
+    uint64_t hash_lo = 0, hash_hi = 0;
+};
+
+struct AgentStats {
+    uint32_t rank_id = 0;
+    int gpu_id = -1, numa_node = 0;
+    uint64_t registered_pinned_bytes = 0, inflight_d2h_bytes = 0, inflight_h2d_bytes = 0;
+    uint64_t evict_count = 0, restore_count = 0, d2h_completed = 0, h2d_completed = 0;
+    uint64_t rank_epoch = 0, num_slots = 0;
+    uint64_t d2h_bytes = 0, h2d_bytes = 0, kernel_launches = 0, rpc_count = 0;
+    uint64_t d2h_ns = 0, h2d_ns = 0;  // summed device time of completed copies (wait paths)
+};
+
+struct BatchItem {
+    uint64_t ptr = 0, nbytes = 0, tensor_id = 0, version = 0;
+};
+
+class Agent {
+ public:
+    explicit Agent(const AgentOptions& opt);
+    ~Agent();
+    Agent(const Agent&) = delete;
+    Agent& operator=(const Agent&) = delete;
+
+    // ---- v1 offload ----
+    // Copy nbytes at `ptr` (device pointer, or host pointer in host mode) into
+    // a pinned slot. `on_done` runs once the copy is complete (from the
+    // progress thread, or inline when wait=true).
+    EvictTicket evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive, uint64_t tensor_id,
+                      uint64_t version, const std::string& name, DoneCallback on_done, bool wait);
+    // Many tensors with one reservation round trip (KV-cache blocks). All or
+    // nothing per item; returns one ticket per item.
+    std::vector<EvictTicket> evict_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait);
+    RestoreOutcome restore(uint64_t tensor_id, uint64_t version, uint64_t ptr, uint64_t nbytes, StreamHandle stream,
+                           bool wait, const RestoreOptions& ro);
+    std::vector<RestoreOutcome> restore_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait);
+    bool is_offloaded(uint64_t tensor_id, uint64_t version) const;
+    void wait_offloaded(uint64_t tensor_id, uint64_t version);
+    bool is_restored(uint64_t tensor_id, uint64_t version) const;
+    void wait_restored(uint64_t tensor_id, uint64_t version);
+    // Object hash recorded at evict time (0,0 when not hashed).
+    bool tensor_hash(uint64_t tensor_id, uint64_t version, uint64_t* lo, uint64_t* hi) const;
+    std::string location(uint64_t tensor_id, uint64_t version);
+    void discard(uint64_t tensor_id, uint64_t version);
+    void assert_no_inflight() const;
+    void synchronize();
+
+    // ---- canonical model state ----
+    RegisterJobResponse register_job(const RegisterJobRequest& r);
+    CanonicalOutcome canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
+                                     const RequestCanonicalEvictRequest& req, DoneCallback on_invalidate, bool wait);
+    RestoreOutcome canonical_restore(uint64_t object_id, uint64_t ptr, uint64_t nbytes, StreamHandle stream,
+                                     bool wait, const RestoreOptions& ro);
+    SealModelVersionResponse seal(const SealModelVersionRequest& r);
+    GetLatestSealedVersionResponse latest(const GetLatestSealedVersionRequest& r);
+    GetManifestResponse manifest(const GetManifestRequest& r);
+    PullTensorResponse pull(const PullTensorRequest& r);
+    DropCanonicalVersionResponse drop_version(const DropCanonicalVersionRequest& r);
+    ReleaseCanonicalResponse release(const ReleaseCanonicalRequest& r);
+    ExportManifestResponse export_manifest(const ExportManifestRequest& r);
+    GetJobStatsResponse job_stats(const GetJobStatsRequest& r);
+    GetStatsResponse daemon_stats();
+    StatusResponse publish_peer_buffer(const PeerBufferDesc& d, int fd);
+    LookupPeerBufferResponse lookup_peer_buffer(const std::string& key, uint32_t wait_ms, int* fd_out);
+
+    // ---- device utilities (GPU mode) ----
+    // ssh128 of a device (or host, in host mode) buffer.
+    void hash_buffer(uint64_t ptr, uint64_t nbytes, StreamHandle stream, uint64_t* lo, uint64_t* hi);
+    uint64_t map_arena(uint64_t arena_id, uint64_t offset) const;  // host pointer of (arena, offset)
+
+    AgentStats stats() const;
+    std::string summary_string() const;
+    int device() const;
+    int numa_node() const;
+    uint32_t rank_id() const;
+    uint64_t rank_epoch() const;
+
+    // Test hook: stop heartbeating (simulates a hung rank without killing it).
+    void pause_heartbeat(bool paused);
+
+    struct Impl;
+
+ private:
+    std::unique_ptr<Impl> d_;
+};
+
+}  // namespace ofld

@@ -1,0 +1,73 @@
+// Host-side launchers of the sm_100a data-path kernels.
+//
+//   evict_hash      K1: device -> host-mapped pinned copy, ssh128 chunk digests
+//                       computed from the same registers in the same pass.
+//   restore_cast    K2: host-mapped pinned -> device copy with optional digest
+//                       re-verification and an optional cast (bf16 -> fp8 e4m3
+//                       with one fp32 scale per 128 elements, fp32 -> bf16,
+//                       bf16 -> fp32).
+//   hash_device         ssh128 chunk digests of a device buffer at HBM rate.
+//   verify_peer     K3: digests of a local buffer plus an exact byte compare
+//                       against a peer GPU's replica read over NVLink.
+//   quant_fp8_block     standalone 1x128 block quantization (used by the
+//                       weight-sync push and tests).
+//
+// Every launcher takes explicit (pointer, nbytes) and validates alignment and
+// bounds on the host before launching; nothing is launched on bad arguments.
+// All launches go on the caller's stream; none allocate memory.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace ofld {
+namespace kern {
+
+enum class Cast : int {
+    kNone = 0,
+    kBf16ToFp8Block128 = 1,  // out: fp8 e4m3 bytes (n elems) + fp32 scales (n/128)
+    kFp32ToBf16 = 2,
+    kBf16ToFp32 = 3,
+};
+
+struct LaunchCfg {
+    int ctas = 0;        // 0 = launcher default
+    int priority = 0;    // informational
+};
+
+// Launch counter for every kernel of this library (what bench.py reports as
+// gpu_launches). Monotonic per process.
+uint64_t launch_count();
+
+// K1. `digests` (may be null) receives ceil(nbytes/64KiB) chunk digests and
+// must be device-accessible (device or host-mapped memory).
+cudaError_t evict_hash(const void* src_dev, void* dst_mapped, uint64_t nbytes, uint64_t* digests,
+                       cudaStream_t stream, int ctas);
+
+// K2. `expect` (may be null): chunk digests to verify against; mismatches are
+// counted into *mismatch_dev (device-accessible u32, may be null).
+cudaError_t restore_cast(const void* src_mapped, void* dst_dev, uint64_t src_nbytes, Cast cast,
+                         float* scales_dev, const uint64_t* expect, uint32_t* mismatch_dev,
+                         cudaStream_t stream, int ctas);
+
+cudaError_t hash_device(const void* src_dev, uint64_t nbytes, uint64_t* digests, cudaStream_t stream, int ctas);
+
+// Fold chunk digests into the 128-bit object hash on the device (single CTA);
+// `out` receives {lo, hi}.
+cudaError_t fold_digests(const uint64_t* digests, uint64_t nchunks, uint64_t nbytes, uint64_t* out,
+                         cudaStream_t stream);
+
+// K3. Compares local and peer bytes; *mismatch_dev counts differing 16-byte
+// vectors. Digests of the local buffer are produced in the same pass.
+cudaError_t verify_peer(const void* local_dev, const void* peer_dev, uint64_t nbytes, uint64_t* digests,
+                        uint32_t* mismatch_dev, cudaStream_t stream, int ctas);
+
+cudaError_t quant_fp8_block(const void* bf16_src, void* fp8_dst, float* scales, uint64_t nelem,
+                            cudaStream_t stream, int ctas);
+
+// Number of chunk digests for nbytes.
+inline uint64_t digest_count(uint64_t nbytes) { return (nbytes + 65535) / 65536; }
+
+}  // namespace kern
+}  // namespace ofld

@@ -1,0 +1,424 @@
+// sm_100a data-path kernels of the offload runtime.
+//
+// StateSpectre moves every byte with cudaMemcpyAsync on the copy engines and
+// hashes on the host, byte-serially (reference: src/agent/agent.cpp:57-68,
+// 825-829, 992-996). Here the SMs move the bytes so the content hash, digest
+// verification and dtype casts happen in the same pass over the data:
+//
+//   * One CTA of 256 threads owns one 64 KiB chunk at a time; thread t is hash
+//     lane t and touches 16-byte vectors t, t+256, ... (16 per chunk). Each
+//     thread issues all 16 of its loads before consuming any, so a CTA keeps
+//     64 KiB in flight: enough memory-level parallelism to cover PCIe read
+//     latency for host-mapped sources with a few dozen CTAs.
+//   * Loads use the non-coherent read-only path without L1 allocation; stores
+//     to host memory are streaming (.cs): every byte is touched once.
+//   * The 256 lane digests reduce with warp shuffles and one shared-memory
+//     step into the chunk digest (the ssh128 tree, ofld/chunk_hash.h).
+//   * Grids are persistent and sized by the caller (a few dozen CTAs) so a
+//     concurrent GEMM keeps most SMs.
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include <atomic>
+
+#include "kernels.h"
+#include "ofld/chunk_hash.h"
+
+namespace ofld {
+namespace kern {
+
+namespace {
+
+std::atomic<uint64_t> g_launches{0};
+
+constexpr int kThreads = 256;  // == ssh::kLanes
+constexpr uint32_t kChunk = ssh::kChunkBytes;
+constexpr int kVecs = ssh::kVecsPerLane;  // 16
+static_assert(kThreads == int(ssh::kLanes), "one thread per hash lane");
+
+__host__ __device__ __forceinline__ uint64_t round_up_dev(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+__device__ __forceinline__ uint4 ld_once(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_stream(void* p, uint4 v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_bytes(const uint8_t* p, uint32_t n) {
+    uint32_t w[4] = {0, 0, 0, 0};
+    for (uint32_t i = 0; i < n; ++i) w[i >> 2] |= uint32_t(p[i]) << (8 * (i & 3));
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ void st_bytes(uint8_t* p, uint4 v, uint32_t n) {
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (uint32_t i = 0; i < n; ++i) p[i] = uint8_t(w[i >> 2] >> (8 * (i & 3)));
+}
+
+template <bool ALIGNED>
+__device__ __forceinline__ uint4 load_vec(const uint8_t* p, uint32_t n) {
+    if (ALIGNED && n == 16) return ld_once(p);
+    return ld_bytes(p, n);
+}
+
+template <bool ALIGNED>
+__device__ __forceinline__ void store_vec(uint8_t* p, uint4 v, uint32_t n) {
+    if (ALIGNED && n == 16)
+        st_stream(p, v);
+    else
+        st_bytes(p, v, n);
+}
+
+// Reduce lane digests to the chunk digest (valid in thread 0). Implements the
+// ssh128 tree: at distance s, entry i (multiple of 2s) = fold(x[i], x[i+s]).
+__device__ __forceinline__ uint64_t tree_fold(uint64_t d, uint64_t* red) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int s = 1; s < 32; s <<= 1) {
+        uint64_t other = __shfl_down_sync(0xffffffffu, d, s);
+        if (((lane & (2 * s - 1)) == 0)) d = ssh::fold(d, other);
+    }
+    if (lane == 0) red[warp] = d;
+    __syncthreads();
+    uint64_t root = 0;
+    if (threadIdx.x == 0) {
+        uint64_t x[kThreads / 32];
+#pragma unroll
+        for (int i = 0; i < kThreads / 32; ++i) x[i] = red[i];
+#pragma unroll
+        for (int s = 1; s < kThreads / 32; s <<= 1)
+#pragma unroll
+            for (int i = 0; i < kThreads / 32; i += 2 * s) x[i] = ssh::fold(x[i], x[i + s]);
+        root = x[0];
+    }
+    __syncthreads();
+    return root;
+}
+
+// K1 and the device hash. STORE=false hashes without copying.
+template <bool ALIGNED, bool HASH, bool STORE>
+__global__ void __launch_bounds__(kThreads, 2)
+    k_evict(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
+            uint64_t* __restrict__ digests) {
+    __shared__ uint64_t red[kThreads / 32];
+    const uint32_t t = threadIdx.x;
+    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+        const uint64_t base = c * kChunk;
+        const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+        const uint32_t nvec = (len + 15) / 16;
+        uint4 v[kVecs];
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            const uint32_t n = vi < nvec ? min(16u, len - vi * 16) : 0u;
+            v[k] = n ? load_vec<ALIGNED>(src + base + uint64_t(vi) * 16, n) : make_uint4(0, 0, 0, 0);
+        }
+        ssh::Lane L = ssh::lane_init(t);
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            if (vi < nvec) {
+                if (HASH) ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
+                if (STORE) store_vec<ALIGNED>(dst + base + uint64_t(vi) * 16, v[k], min(16u, len - vi * 16));
+            }
+        }
+        if (HASH) {
+            uint64_t root = tree_fold(ssh::lane_digest(L, t), red);
+            if (t == 0) digests[c] = ssh::chunk_finish(root, len);
+        }
+    }
+}
+
+// ---- K2: restore with optional verify and cast -----------------------------
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t fp8x4(float a, float b, float c, float d) {
+    uint32_t r = 0;
+    r |= uint32_t(__nv_cvt_float_to_fp8(a, __NV_SATFINITE, __NV_E4M3));
+    r |= uint32_t(__nv_cvt_float_to_fp8(b, __NV_SATFINITE, __NV_E4M3)) << 8;
+    r |= uint32_t(__nv_cvt_float_to_fp8(c, __NV_SATFINITE, __NV_E4M3)) << 16;
+    r |= uint32_t(__nv_cvt_float_to_fp8(d, __NV_SATFINITE, __NV_E4M3)) << 24;
+    return r;
+}
+
+// Quantize 8 bf16 values (one 16-byte vector) of a 128-element block whose 16
+// vectors sit in 16 consecutive lanes. Returns the 8 fp8 bytes; lane 0 of the
+// group stores the block scale.
+__device__ __forceinline__ uint2 quant8(uint4 v, bool valid, float* scale_out) {
+    float f[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
+                  bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, valid ? fabsf(f[i]) : 0.f);
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.f ? 448.f / amax : 1.f;
+    *scale_out = amax > 0.f ? amax / 448.f : 1.f;
+    return make_uint2(fp8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv),
+                      fp8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv));
+}
+
+template <bool ALIGNED, bool VERIFY, int CAST>
+__global__ void __launch_bounds__(kThreads, 2)
+    k_restore(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
+              float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch) {
+    __shared__ uint64_t red[kThreads / 32];
+    const uint32_t t = threadIdx.x;
+    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+        const uint64_t base = c * kChunk;
+        const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+        const uint32_t nvec = (len + 15) / 16;
+        uint4 v[kVecs];
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            const uint32_t n = vi < nvec ? min(16u, len - vi * 16) : 0u;
+            v[k] = n ? load_vec<ALIGNED>(src + base + uint64_t(vi) * 16, n) : make_uint4(0, 0, 0, 0);
+        }
+        ssh::Lane L = ssh::lane_init(t);
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            const bool valid = vi < nvec;
+            if (VERIFY && valid) ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
+            const uint64_t gv = base / 16 + vi;  // global vector index
+            if (CAST == int(Cast::kNone)) {
+                if (valid) store_vec<ALIGNED>(dst + gv * 16, v[k], min(16u, len - vi * 16));
+            } else if (CAST == int(Cast::kBf16ToFp8Block128)) {
+                float s;
+                uint2 q = quant8(v[k], valid, &s);  // all lanes take part in the shuffle
+                if (valid) {
+                    *reinterpret_cast<uint2*>(dst + gv * 8) = q;
+                    if ((t & 15) == 0) scales[gv / 16] = s;
+                }
+            } else if (CAST == int(Cast::kFp32ToBf16)) {
+                if (valid) {
+                    uint2 o = make_uint2(pack_bf16x2(__uint_as_float(v[k].x), __uint_as_float(v[k].y)),
+                                         pack_bf16x2(__uint_as_float(v[k].z), __uint_as_float(v[k].w)));
+                    *reinterpret_cast<uint2*>(dst + gv * 8) = o;
+                }
+            } else if (CAST == int(Cast::kBf16ToFp32)) {
+                if (valid) {
+                    uint4 a = make_uint4(__float_as_uint(bf16_lo(v[k].x)), __float_as_uint(bf16_hi(v[k].x)),
+                                         __float_as_uint(bf16_lo(v[k].y)), __float_as_uint(bf16_hi(v[k].y)));
+                    uint4 b = make_uint4(__float_as_uint(bf16_lo(v[k].z)), __float_as_uint(bf16_hi(v[k].z)),
+                                         __float_as_uint(bf16_lo(v[k].w)), __float_as_uint(bf16_hi(v[k].w)));
+                    *reinterpret_cast<uint4*>(dst + gv * 32) = a;
+                    *reinterpret_cast<uint4*>(dst + gv * 32 + 16) = b;
+                }
+            }
+        }
+        if (VERIFY) {
+            uint64_t root = tree_fold(ssh::lane_digest(L, t), red);
+            if (t == 0 && ssh::chunk_finish(root, len) != expect[c]) atomicAdd(mismatch, 1u);
+        }
+    }
+}
+
+// ---- K3: local hash + exact compare against a peer replica ----------------
+__global__ void __launch_bounds__(kThreads, 2)
+    k_verify_peer(const uint8_t* __restrict__ local, const uint8_t* __restrict__ peer, uint64_t nbytes,
+                  uint64_t* __restrict__ digests, uint32_t* mismatch) {
+    __shared__ uint64_t red[kThreads / 32];
+    const uint32_t t = threadIdx.x;
+    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+        const uint64_t base = c * kChunk;
+        const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+        const uint32_t nvec = (len + 15) / 16;
+        uint4 a[kVecs / 2], b[kVecs / 2];
+        ssh::Lane L = ssh::lane_init(t);
+        uint32_t bad = 0;
+        // Two halves of 8 vectors each keep 16 loads (8 local + 8 peer) in flight.
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int k = 0; k < kVecs / 2; ++k) {
+                const uint32_t vi = uint32_t(h * (kVecs / 2) + k) * kThreads + t;
+                const uint32_t n = vi < nvec ? min(16u, len - vi * 16) : 0u;
+                a[k] = n ? load_vec<true>(local + base + uint64_t(vi) * 16, n) : make_uint4(0, 0, 0, 0);
+                b[k] = n ? load_vec<true>(peer + base + uint64_t(vi) * 16, n) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int k = 0; k < kVecs / 2; ++k) {
+                const uint32_t vi = uint32_t(h * (kVecs / 2) + k) * kThreads + t;
+                if (vi < nvec) {
+                    ssh::lane_update(L, a[k].x, a[k].y, a[k].z, a[k].w);
+                    bad += (a[k].x != b[k].x) | (a[k].y != b[k].y) | (a[k].z != b[k].z) | (a[k].w != b[k].w);
+                }
+            }
+        }
+        uint64_t root = tree_fold(ssh::lane_digest(L, t), red);
+        if (t == 0 && digests) digests[c] = ssh::chunk_finish(root, len);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) bad += __shfl_xor_sync(0xffffffffu, bad, o);
+        if ((t & 31) == 0 && bad) atomicAdd(mismatch, bad);
+    }
+}
+
+__global__ void k_fold(const uint64_t* __restrict__ d, uint64_t n, uint64_t nbytes, uint64_t* out) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    uint64_t lo, hi;
+    ssh::object_init(lo, hi);
+    for (uint64_t i = 0; i < n; ++i) ssh::object_absorb(lo, hi, d[i]);
+    ssh::Object o = ssh::object_finish(lo, hi, nbytes);
+    out[0] = o.lo;
+    out[1] = o.hi;
+}
+
+// Standalone 1x128 quantization: one half-warp per 128-element block.
+__global__ void __launch_bounds__(kThreads) k_quant_fp8(const uint4* __restrict__ src, uint2* __restrict__ dst,
+                                                          float* __restrict__ scales, uint64_t nelem) {
+    const uint64_t nvec = (nelem + 7) / 8;
+    const uint64_t nblocks = (nelem + 127) / 128;
+    const uint64_t stride = uint64_t(gridDim.x) * kThreads;
+    // Iterate whole blocks so every half-warp stays converged for its shuffle.
+    for (uint64_t vi = uint64_t(blockIdx.x) * kThreads + threadIdx.x; vi < round_up_dev(nblocks * 16, 32);
+         vi += stride) {
+        const bool valid = vi < nvec;
+        uint4 v = valid ? ld_once(src + vi) : make_uint4(0, 0, 0, 0);
+        if (valid && (vi + 1) * 8 > nelem) {  // zero elements past the end
+            uint32_t keep = uint32_t(nelem - vi * 8);
+            uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            for (uint32_t e = keep; e < 8; ++e) w[e / 2] &= (e & 1) ? 0x0000ffffu : 0xffff0000u;
+            v = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        float s;
+        uint2 q = quant8(v, valid, &s);
+        if (valid) {
+            dst[vi] = q;
+            if ((threadIdx.x & 15) == 0) scales[vi / 16] = s;
+        }
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int grid_for(uint64_t nbytes, int ctas, int dflt) {
+    uint64_t chunks = (nbytes + kChunk - 1) / kChunk;
+    int g = ctas > 0 ? ctas : dflt;
+    if (uint64_t(g) > chunks) g = int(chunks);
+    return g < 1 ? 1 : g;
+}
+
+}  // namespace
+
+
+
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+cudaError_t evict_hash(const void* src, void* dst, uint64_t nbytes, uint64_t* digests, cudaStream_t s, int ctas) {
+    if (nbytes == 0) return cudaSuccess;
+    if (!src || !dst) return cudaErrorInvalidValue;
+    const int g = grid_for(nbytes, ctas, 48);
+    const bool al = aligned16(src) && aligned16(dst);
+    auto S = static_cast<const uint8_t*>(src);
+    auto D = static_cast<uint8_t*>(dst);
+    if (digests) {
+        if (al) k_evict<true, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests);
+        else k_evict<false, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests);
+    } else {
+        if (al) k_evict<true, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr);
+        else k_evict<false, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr);
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t hash_device(const void* src, uint64_t nbytes, uint64_t* digests, cudaStream_t s, int ctas) {
+    if (nbytes == 0) return cudaSuccess;
+    if (!src || !digests) return cudaErrorInvalidValue;
+    const int g = grid_for(nbytes, ctas, 148 * 4);
+    auto S = static_cast<const uint8_t*>(src);
+    if (aligned16(src)) k_evict<true, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests);
+    else k_evict<false, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t restore_cast(const void* src, void* dst, uint64_t nbytes, Cast cast, float* scales,
+                         const uint64_t* expect, uint32_t* mismatch, cudaStream_t s, int ctas) {
+    if (nbytes == 0) return cudaSuccess;
+    if (!src || !dst) return cudaErrorInvalidValue;
+    if (expect && !mismatch) return cudaErrorInvalidValue;
+    const int g = grid_for(nbytes, ctas, 96);
+    auto S = static_cast<const uint8_t*>(src);
+    auto D = static_cast<uint8_t*>(dst);
+    const bool verify = expect != nullptr;
+    if (cast == Cast::kNone) {
+        const bool al = aligned16(src) && aligned16(dst);
+        if (al && verify) k_restore<true, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch);
+        else if (al) k_restore<true, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr);
+        else if (verify) k_restore<false, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch);
+        else k_restore<false, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr);
+    } else {
+        // Casts need element-aligned whole vectors.
+        if (!aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7) || nbytes % 16) return cudaErrorInvalidValue;
+        if (cast == Cast::kBf16ToFp8Block128) {
+            if (!scales) return cudaErrorInvalidValue;
+            if (verify) k_restore<true, true, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, expect, mismatch);
+            else k_restore<true, false, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, nullptr, nullptr);
+        } else if (cast == Cast::kFp32ToBf16) {
+            if (verify) k_restore<true, true, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch);
+            else k_restore<true, false, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr);
+        } else if (cast == Cast::kBf16ToFp32) {
+            if (reinterpret_cast<uintptr_t>(dst) & 15) return cudaErrorInvalidValue;
+            if (verify) k_restore<true, true, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch);
+            else k_restore<true, false, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr);
+        } else {
+            return cudaErrorInvalidValue;
+        }
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t fold_digests(const uint64_t* digests, uint64_t n, uint64_t nbytes, uint64_t* out, cudaStream_t s) {
+    if (!out || (n && !digests)) return cudaErrorInvalidValue;
+    k_fold<<<1, 32, 0, s>>>(digests, n, nbytes, out);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t verify_peer(const void* local, const void* peer, uint64_t nbytes, uint64_t* digests, uint32_t* mismatch,
+                        cudaStream_t s, int ctas) {
+    if (nbytes == 0) return cudaSuccess;
+    if (!local || !peer || !mismatch) return cudaErrorInvalidValue;
+    if (!aligned16(local) || !aligned16(peer) || nbytes % 16) return cudaErrorInvalidValue;
+    const int g = grid_for(nbytes, ctas, 148 * 2);
+    k_verify_peer<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(local), static_cast<const uint8_t*>(peer),
+                                         nbytes, digests, mismatch);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t quant_fp8_block(const void* src, void* dst, float* scales, uint64_t nelem, cudaStream_t s, int ctas) {
+    if (nelem == 0) return cudaSuccess;
+    if (!src || !dst || !scales || !aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7))
+        return cudaErrorInvalidValue;
+    uint64_t nvec = (nelem + 7) / 8;
+    int g = ctas > 0 ? ctas : int(std::min<uint64_t>((nvec + kThreads - 1) / kThreads, 148 * 8));
+    k_quant_fp8<<<g < 1 ? 1 : g, kThreads, 0, s>>>(static_cast<const uint4*>(src), static_cast<uint2*>(dst), scales,
+                                                    nelem);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+}  // namespace kern
+}  // namespace ofld

@@ -1,0 +1,129 @@
+// offload-stat: query a running offloadd and print its counters.
+//
+// Flags follow StateSpectre's tool (reference: src/tools/offload_stat.cpp:12-97):
+//   offload-stat [--socket PATH | --tcp HOST:PORT] [--prometheus] [--watch N]
+//                [--jobs] [--shutdown]
+// --jobs prints the per-job accounting table (an addition of this runtime).
+#include <unistd.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "ofld/codec.h"
+#include "ofld/transport.h"
+
+using namespace ofld;
+
+namespace {
+void usage() {
+    std::fprintf(stderr,
+                 "usage: offload-stat [--socket PATH | --tcp HOST:PORT] [--prometheus] [--watch SECONDS]\n"
+                 "                    [--jobs] [--shutdown]\n");
+}
+
+std::string human(uint64_t v) {
+    const char* u[] = {"B", "KiB", "MiB", "GiB", "TiB"};
+    double d = double(v);
+    int i = 0;
+    while (d >= 1024 && i < 4) {
+        d /= 1024;
+        ++i;
+    }
+    char b[64];
+    std::snprintf(b, sizeof(b), "%.2f %s", d, u[i]);
+    return b;
+}
+
+bool is_bytes(const std::string& k) { return k.find("bytes") != std::string::npos; }
+
+void print_table(const GetStatsResponse& r) {
+    std::printf("%-44s %20s\n", "metric", "value");
+    for (const StatEntry& e : r.stats) {
+        if (is_bytes(e.key))
+            std::printf("%-44s %20s\n", e.key.c_str(), human(e.value).c_str());
+        else
+            std::printf("%-44s %20llu\n", e.key.c_str(), (unsigned long long)e.value);
+    }
+}
+
+void print_prometheus(const GetStatsResponse& r) {
+    for (const StatEntry& e : r.stats) {
+        std::string name = "offloadd_" + e.key;
+        bool counter = e.key.size() > 6 && e.key.compare(e.key.size() - 6, 6, "_total") == 0;
+        std::printf("# TYPE %s %s\n%s %llu\n", name.c_str(), counter ? "counter" : "gauge", name.c_str(),
+                    (unsigned long long)e.value);
+    }
+}
+
+void print_jobs(const GetJobStatsResponse& r) {
+    std::printf("%-24s %20s %6s %12s %12s %12s %8s %14s\n", "job", "job_id", "epoch", "pinned", "pageable", "nvme",
+                "objects", "dedup_saved");
+    for (const JobStatsEntry& j : r.jobs)
+        std::printf("%-24s %20llu %6llu %12s %12s %12s %8llu %14s\n", j.job.job_name.c_str(),
+                    (unsigned long long)j.job.job_id, (unsigned long long)j.job.launch_epoch,
+                    human(j.pinned_bytes).c_str(), human(j.pageable_bytes).c_str(), human(j.nvme_bytes).c_str(),
+                    (unsigned long long)j.canonical_object_count, human(j.dedup_bytes_saved).c_str());
+}
+}  // namespace
+
+int main(int argc, char** argv) {
+    std::string sock = "/tmp/state_spectre.sock", tcp;
+    bool prom = false, shutdown = false, jobs = false;
+    int watch = 0;
+    for (int i = 1; i < argc; ++i) {
+        std::string a = argv[i];
+        if (a == "--socket" && i + 1 < argc) sock = argv[++i];
+        else if (a == "--tcp" && i + 1 < argc) tcp = argv[++i];
+        else if (a == "--prometheus") prom = true;
+        else if (a == "--watch" && i + 1 < argc) watch = std::atoi(argv[++i]);
+        else if (a == "--shutdown") shutdown = true;
+        else if (a == "--jobs") jobs = true;
+        else if (a == "-h" || a == "--help") {
+            usage();
+            return 0;
+        } else {
+            usage();
+            return 2;
+        }
+    }
+    try {
+        int fd;
+        if (!tcp.empty()) {
+            std::string host;
+            uint16_t port;
+            if (!split_host_port(tcp, &host, &port)) throw std::runtime_error("bad --tcp HOST:PORT");
+            fd = tcp_connect(host, port, 3000);
+        } else {
+            fd = uds_connect(sock, 3000);
+        }
+        RpcClient c(fd);
+        if (shutdown) {
+            StatusResponse r = c.call<Op::kShutdown>(ShutdownRequest{});
+            std::printf("%s\n", r.message.c_str());
+            return r.ok ? 0 : 1;
+        }
+        do {
+            if (jobs) {
+                print_jobs(c.call<Op::kGetJobStats>(GetJobStatsRequest{}));
+            } else {
+                GetStatsResponse r = c.call<Op::kGetStats>(GetStatsRequest{});
+                if (prom)
+                    print_prometheus(r);
+                else
+                    print_table(r);
+            }
+            std::fflush(stdout);
+            if (watch > 0) {
+                sleep(unsigned(watch));
+                if (!prom) std::printf("\n");
+            }
+        } while (watch > 0);
+    } catch (const std::exception& e) {
+        std::fprintf(stderr, "offload-stat: %s\n", e.what());
+        return 1;
+    }
+    return 0;
+}

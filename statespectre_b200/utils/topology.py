@@ -1,0 +1,57 @@
+"""Node topology: GPU -> NUMA node affinity and daemon config generation."""
+
+from __future__ import annotations
+
+import os
+from typing import Dict, List
+
+
+def gpu_numa_nodes(num_gpus: int) -> List[int]:
+    """NUMA node of each visible GPU (0 when unknown)."""
+    out = []
+    try:
+        import torch
+    except ImportError:  # pragma: no cover
+        return [0] * num_gpus
+    for i in range(num_gpus):
+        node = 0
+        try:
+            bus = torch.cuda.get_device_properties(i).pci_bus_id.lower()
+            if bus.count(":") == 1:
+                bus = "0000:" + bus
+            parts = bus.split(":")
+            parts[0] = parts[0][-4:].rjust(4, "0")
+            path = f"/sys/bus/pci/devices/{':'.join(parts)}/numa_node"
+            with open(path) as f:
+                node = max(int(f.read().strip()), 0)
+        except Exception:  # noqa: BLE001
+            node = 0
+        out.append(node)
+    return out
+
+
+def daemon_yaml(socket_path: str, gpu_nodes: List[int], window_gb_per_gpu: int, slot_mb: int = 64,
+                overflow_gb: int = 1, drain_on_complete: bool = False, extra: str = "") -> str:
+    """A daemon config with one arena per NUMA node holding a window per GPU."""
+    by_node: Dict[int, List[int]] = {}
+    for g, n in enumerate(gpu_nodes):
+        by_node.setdefault(n, []).append(g)
+    lines = ["daemon:", f"  socket_path: {socket_path}", "  heartbeat_timeout_ms: 30000",
+             "arenas:", f"  allocation_granularity_mb: {slot_mb}", "  per_numa:"]
+    for node, gpus in sorted(by_node.items()):
+        size = window_gb_per_gpu * len(gpus) + overflow_gb
+        lines += [f"    - numa_node: {node}", f"      size_gb: {size}", f"      overflow_gb: {overflow_gb}",
+                  "      gpu_windows:"]
+        for g in gpus:
+            lines += [f"        - gpu: {g}", f"          size_gb: {window_gb_per_gpu}"]
+    lines += ["drain_policy:", "  target_tier: pageable", f"  drain_on_d2h_complete: {str(drain_on_complete).lower()}",
+              "nvme:", "  enabled: false"]
+    return "\n".join(lines) + "\n" + extra
+
+
+def host_numa_nodes() -> List[int]:
+    base = "/sys/devices/system/node"
+    try:
+        return sorted(int(d[4:]) for d in os.listdir(base) if d.startswith("node") and d[4:].isdigit())
+    except OSError:
+        return [0]

@@ -1,0 +1,105 @@
+"""End-to-end GPU round trips through the public API and an in-process daemon."""
+
+import pytest
+import torch
+
+from statespectre_b200 import DedupPolicy, ModelRole, in_process_daemon, offload_context
+from statespectre_b200._native import native
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def gpu_off(sock_path):
+    d = in_process_daemon(socket=sock_path, arena_mb=1024, drain_on_complete=False)
+    s = offload_context(daemon_addr=sock_path, device="cuda:0", rank=0, job_name="gpu-test")
+    yield s.off
+    s.close()
+    d.stop()
+
+
+def test_evict_restore_releases_vram_and_roundtrips(gpu_off):
+    off = gpu_off
+    x = torch.randn(64 << 20, dtype=torch.bfloat16, device="cuda")  # 128 MiB
+    ref = x.clone()
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated()
+    h = off.evict(x, wait=True)
+    torch.cuda.synchronize()
+    assert x.numel() == 0
+    assert torch.cuda.memory_allocated() <= before - (128 << 20)
+    assert h.location() == "pinned"
+    y = h.restore()
+    assert torch.equal(y, ref)
+    assert h.content_hash == native().ssh_hash(ref.cpu().view(torch.uint8).numpy())
+    h.discard()
+
+
+def test_async_evict_prefetch_restore_into_and_verify(gpu_off):
+    off = gpu_off
+    x = torch.randn(3 << 20, device="cuda")
+    ref = x.clone()
+    h = off.copy(x)  # async, non-destructive
+    h.wait_offloaded()
+    assert h.ready()
+    p = h.prefetch()
+    y = p.wait()
+    assert torch.equal(y, ref)
+    z = torch.empty_like(ref)
+    h.restore_into(z, verify=True)
+    assert torch.equal(z, ref)
+    w = h.restore(cast="bf16")
+    assert torch.equal(w, ref.to(torch.bfloat16))
+
+
+def test_odd_sizes_and_views(gpu_off):
+    off = gpu_off
+    for n in (1, 17, 333, 65537):
+        x = torch.randint(0, 255, (n,), dtype=torch.uint8, device="cuda")
+        h = off.copy(x, wait=True)
+        assert torch.equal(h.restore(), x)
+    base = torch.randn(1000, 64, device="cuda")
+    view = base[:, 3:40]
+    h = off.evict(view, compact=True, wait=True)
+    assert torch.equal(h.restore(), view.contiguous())
+    with pytest.raises(RuntimeError):
+        off.evict(view)  # destructive eviction of a view is refused
+
+
+def test_fp8_restore_cast(gpu_off):
+    off = gpu_off
+    x = torch.randn(1 << 20, dtype=torch.bfloat16, device="cuda")
+    h = off.copy(x, wait=True)
+    q, scales = h.restore(cast="fp8_block128")
+    deq = (q.float().reshape(-1, 128) * scales[:, None]).reshape(-1)
+    torch.testing.assert_close(deq, x.float(), rtol=0.07, atol=1e-2)
+
+
+def test_batch_evict_restore(gpu_off):
+    off = gpu_off
+    blocks = [torch.randn(16, 8, 128, dtype=torch.bfloat16, device="cuda") for _ in range(64)]
+    refs = [b.clone() for b in blocks]
+    hs = off.evict_batch(blocks)
+    outs = off.restore_batch(hs)
+    for o, r in zip(outs, refs):
+        assert torch.equal(o, r)
+
+
+def test_canonical_evict_seal_restore(gpu_off):
+    off = gpu_off
+    w = torch.randn(4096, 512, dtype=torch.bfloat16, device="cuda")
+    ref = w.clone()
+    key = off.canonical_key(model_role=ModelRole.POLICY_ROLLOUT, model_version=1, param_name="layer0.w", tensor=w)
+    ch = off.canonical_evict(w, key)
+    assert ch.action_name == "NEED_D2H_CREATE" and ch.did_d2h
+    assert ch.content_hash == off.hash_tensor(ref)
+    sealed = off.promote_rollout_version(1)
+    assert sealed["tensor_count"] == 1
+    out = torch.empty_like(ref)
+    ch.restore_into(out)
+    assert torch.equal(out, ref)
+    # a second replica verifies by device hash without any copy
+    key2 = off.canonical_key(model_role=ModelRole.POLICY_ROLLOUT, model_version=2, param_name="layer0.w", tensor=ref)
+    c1 = off.canonical_evict(ref.clone(), key2)
+    c2 = off.canonical_evict(ref.clone(), key2, dedup_policy=DedupPolicy("device_hash_verified"))
+    assert c1.did_d2h and not c2.did_d2h and c2.action_name == "VERIFIED_BY_DEVICE_HASH"
