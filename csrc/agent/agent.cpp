@@ -172,6 +172,7 @@ struct Agent::Impl {
         rq.gpu_id = gpu ? uint32_t(opt.device) : 0xFFFFu;
         rq.numa_node = uint32_t(numa);
         rq.pid = uint64_t(::getpid());
+        rq.capabilities = kCapMultiSession;
         std::vector<int> fds;
         RegisterRankResponse rr = rpc->call<Op::kRegisterRank>(rq, &fds);
         ++rpc_count;
@@ -351,7 +352,13 @@ struct Agent::Impl {
     }
 
     void report_h2d(const Pending& p) {
-        if (p.keep_pinned || !ring_push_entry(EventType::kH2DComplete, p, nullptr)) {
+        uint64_t seq = ~0ull;
+        if (!p.keep_pinned && ring_push_entry(EventType::kH2DComplete, p, &seq)) {
+            std::lock_guard<std::mutex> g(tab_mu);
+            tensors[{p.tid, p.ver}].ring_seq = seq;  // later queries wait for this entry
+            return;
+        }
+        {
             MarkH2DCompleteRequest m;
             m.rank_id = opt.rank_id;
             m.rank_epoch = epoch;

@@ -483,9 +483,12 @@ RegisterRankResponse Daemon::on_register(const RegisterRankRequest& r, std::vect
     RegisterRankResponse resp;
     auto it = sessions_.find(r.rank_id);
     if (it != sessions_.end()) recover_session(it->second, "re-registered");
-    for (auto& kv : sessions_)
-        if (kv.first != r.rank_id && kv.second.alive && kv.second.pid == r.pid)
-            recover_session(kv.second, "pid re-registered under a new rank id");
+    // A process re-registering under a new rank id replaces its old session,
+    // unless it declares that it holds several sessions at once.
+    if (!(r.capabilities & kCapMultiSession))
+        for (auto& kv : sessions_)
+            if (kv.first != r.rank_id && kv.second.alive && kv.second.pid == r.pid)
+                recover_session(kv.second, "pid re-registered under a new rank id");
 
     Session s;
     s.rank_id = r.rank_id;

@@ -434,8 +434,14 @@ RequestPrefetchResponse Daemon::do_request_prefetch(const RequestPrefetchRequest
         return resp;
     }
     if (loc.kind == OFLD_LOC_PINNED) {
-        resp.message = "pinned copy transitioning; retry";
-        resp.ok = false;
+        // Drain or another transfer in flight on the run: not ready yet, the
+        // caller polls again (a finished drain turns this into a readback).
+        resp.ok = true;
+        resp.ready = false;
+        resp.state = state_of(loc.slot);
+        resp.version = want;
+        resp.nbytes = loc.nbytes;
+        resp.message = "pinned copy transitioning";
         return resp;
     }
     // Cold: allocate a pinned run and read it back in the background.

@@ -89,6 +89,9 @@ template <class V> void fields(V& v, ArenaFd& m) {
       m.fd_index, m.registration_granularity, m.allocation_granularity);
 }
 
+// RegisterRankRequest.capabilities bits.
+constexpr uint64_t kCapMultiSession = 1ull << 0;  // process may hold several rank sessions
+
 struct RegisterRankRequest {
     uint32_t rank_id = 0, local_rank = 0, world_rank = 0, gpu_id = 0, numa_node = 0;
     uint64_t pid = 0, capabilities = 0;

@@ -756,6 +756,30 @@ class Off:
                 json.dump({"traceEvents": ev, "displayTimeUnit": "ms"}, f)
 
 
+_LIVE_SESSIONS: "weakref.WeakSet" = None  # type: ignore[assignment]
+
+
+def _close_live_sessions() -> None:
+    """atexit: stop agent threads before the interpreter finalizes, so no
+    native thread tries to take the GIL of a dying interpreter."""
+    for s in list(_LIVE_SESSIONS or ()):
+        try:
+            s.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def _track(session) -> None:
+    global _LIVE_SESSIONS
+    if _LIVE_SESSIONS is None:
+        import atexit
+        import weakref
+
+        _LIVE_SESSIONS = weakref.WeakSet()
+        atexit.register(_close_live_sessions)
+    _LIVE_SESSIONS.add(session)
+
+
 class _OffloadSession:
     """Context manager returned by :func:`offload_context` (a plain object, so a
     session used without ``with`` is closed only explicitly)."""
@@ -781,6 +805,7 @@ class _OffloadSession:
                               job_labels)
         self._off = off
         self._closed = False
+        _track(self)
 
     def __enter__(self) -> Off:
         return self._off

@@ -116,7 +116,13 @@ def in_process_daemon(**kw):
     """
     if "socket" not in kw:
         kw["socket"] = os.path.join(tempfile.mkdtemp(prefix="offloadd-"), "offloadd.sock")
-    return native().DaemonThread(**kw)
+    d = native().DaemonThread(**kw)
+    import atexit
+    import weakref
+
+    ref = weakref.ref(d)
+    atexit.register(lambda: ref() is not None and ref().stop())
+    return d
 
 
 class DaemonClient(_wire.Connection):

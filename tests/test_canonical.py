@@ -1,0 +1,249 @@
+"""Canonical model-state store through the public API (host-mode ranks).
+
+Mirrors StateSpectre's canonical suite (job namespaces, DP attach vs TP /
+expert distinct, creating race, hash mismatch, duplicate candidate, seal +
+pull, seal failure, canonical restore, drop, multi-consumer refcount, pull of
+an unsealed version, quota; reference: tests/cpp/test_canonical.cpp:226-727).
+"""
+
+import os
+import struct
+
+import pytest
+import torch
+
+from statespectre_b200 import (DedupPolicy, ModelRole, RolloutWeightClient, in_process_daemon, offload_context)
+from statespectre_b200._wire import Op
+
+from rawclient import RawRank
+
+ROLL = ModelRole.POLICY_ROLLOUT
+
+
+@pytest.fixture
+def cdaemon(sock_path):
+    d = in_process_daemon(socket=sock_path, arena_mb=128, drain_on_complete=False)
+    yield sock_path
+    d.stop()
+
+
+def session(sock, rank, job="train", **kw):
+    return offload_context(daemon_addr=sock, device="cpu", rank=rank, job_name=job, **kw)
+
+
+def test_dp_replicas_attach_and_tp_shards_stay_distinct(cdaemon):
+    w = torch.randn(256, 64)
+    with session(cdaemon, 0) as r0, session(cdaemon, 1) as r1, session(cdaemon, 2) as r2:
+        assert r0.job_id == r1.job_id and r0.launch_epoch == r1.launch_epoch  # one namespace per job
+        k0 = r0.canonical_key(model_role=ROLL, model_version=1, param_name="w", tensor=w, tp_rank=0)
+        h0 = r0.canonical_evict(w.clone(), k0)
+        assert h0.action_name == "NEED_D2H_CREATE" and h0.did_d2h
+        k1 = r1.canonical_key(model_role=ROLL, model_version=1, param_name="w", tensor=w, tp_rank=0)
+        h1 = r1.canonical_evict(w.clone(), k1)  # DP replica: same identity, no copy
+        assert h1.action_name == "ATTACHED_EXISTING" and not h1.did_d2h and h1.object_id == h0.object_id
+        k2 = r2.canonical_key(model_role=ROLL, model_version=1, param_name="w", tensor=w, tp_rank=1)
+        h2 = r2.canonical_evict(w.clone(), k2)  # different TP shard: distinct object
+        assert h2.did_d2h and h2.object_id != h0.object_id
+        ke = r2.canonical_key(model_role=ROLL, model_version=1, param_name="w", tensor=w, tp_rank=0, expert_id=3)
+        he = r2.canonical_evict(w.clone(), ke)
+        assert he.object_id not in (h0.object_id, h2.object_id)
+        s = r0.daemon_stats()
+        assert s["canonical_attach_existing_total"] == 1
+        assert s["canonical_d2h_bytes_avoided"] == w.numel() * 4
+
+
+def test_relaunch_gets_fresh_epoch_and_jobs_are_isolated(cdaemon):
+    with session(cdaemon, 0, job="a") as a, session(cdaemon, 1, job="b") as b:
+        assert a.job_id != b.job_id
+        w = torch.ones(128)
+        ka = a.canonical_key(model_role=ROLL, model_version=1, param_name="x", tensor=w)
+        kb = b.canonical_key(model_role=ROLL, model_version=1, param_name="x", tensor=w)
+        assert a.canonical_evict(w.clone(), ka).did_d2h
+        assert b.canonical_evict(w.clone(), kb).did_d2h  # other job: no cross-job dedup
+
+
+def test_hash_verified_detects_corrupt_replica(cdaemon):
+    w = torch.randn(1024)
+    with session(cdaemon, 0) as r0, session(cdaemon, 1) as r1:
+        pol = DedupPolicy("hash_verified")
+        k = r0.canonical_key(model_role=ROLL, model_version=3, param_name="w", tensor=w)
+        r0.canonical_evict(w.clone(), k, dedup_policy=pol)
+        ok = r1.canonical_evict(w.clone(), k, dedup_policy=pol)
+        assert ok.action_name == "DUPLICATE_CANDIDATE" and ok.did_d2h
+        bad = w.clone()
+        bad[17] += 1.0
+        with pytest.raises(RuntimeError, match="mismatch"):
+            r1.canonical_evict(bad, k, dedup_policy=pol)
+        assert r0.daemon_stats()["canonical_hash_mismatch_total"] == 1
+
+
+def test_device_hash_verified_needs_no_copy(cdaemon):
+    w = torch.randn(4096)
+    with session(cdaemon, 0) as r0, session(cdaemon, 1) as r1:
+        pol = DedupPolicy("device_hash_verified")
+        k = r0.canonical_key(model_role=ROLL, model_version=4, param_name="w", tensor=w)
+        c = r0.canonical_evict(w.clone(), k, dedup_policy=pol)
+        assert c.did_d2h
+        used = r0.daemon_stats()["used_slots"]
+        v = r1.canonical_evict(w.clone(), k, dedup_policy=pol)
+        assert v.action_name == "VERIFIED_BY_DEVICE_HASH" and not v.did_d2h
+        assert r0.daemon_stats()["used_slots"] == used  # no candidate slot reserved
+        bad = w.clone()
+        bad[0] = 7
+        with pytest.raises(RuntimeError, match="mismatch"):
+            r1.canonical_evict(bad, k, dedup_policy=pol)
+
+
+def test_creating_race_waits_then_attaches(cdaemon):
+    """A second rank arriving while the creator has not committed gets WAIT."""
+    r0 = RawRank(cdaemon, 0)
+    job = r0.call(Op.REGISTER_JOB, tenant_id=0, job_name="race")["job"]
+    key = {"job": job, "model_role": ROLL, "model_version": 1, "param_id": 5, "nbytes": 4096, "shard_nbytes": 4096,
+           "expert_id": -1}
+    req = dict(rank_id=0, rank_epoch=r0.epoch, key=key, destructive=True, attach_if_exists=True,
+               create_if_missing=True, dedup_mode=1)
+    c = r0.call(Op.REQUEST_CANONICAL_EVICT, **req)
+    assert c["action"] == 1
+    r1 = RawRank(cdaemon, 1)
+    w = r1.call(Op.REQUEST_CANONICAL_EVICT, **dict(req, rank_id=1, rank_epoch=r1.epoch))
+    assert w["action"] == 2 and w["object_id"] == c["object_id"]
+    dup = r1.call(Op.REQUEST_CANONICAL_EVICT, **dict(req, rank_id=1, rank_epoch=r1.epoch,
+                                                     allow_duplicate_candidate=True))
+    assert dup["action"] == 3 and dup["synthetic_tid"] >> 62 == 3
+    # creator finishes: D2H complete + commit
+    assert r0.mark(Op.MARK_D2H_SUBMITTED, c["lease_id"], c["synthetic_tid"], 1, c["slot_id"])["ok"]
+    assert r0.mark(Op.MARK_D2H_COMPLETE, c["lease_id"], c["synthetic_tid"], 1, c["slot_id"])["ok"]
+    cm = r0.call(Op.COMMIT_CANONICAL_OBJECT, rank_id=0, rank_epoch=r0.epoch, object_id=c["object_id"],
+                 lease_id=c["lease_id"], slot_id=c["slot_id"])
+    assert cm["ok"] and cm["won"]
+    # the candidate loser commits and attaches; its slot is freed
+    lose = r1.call(Op.COMMIT_CANONICAL_OBJECT, rank_id=1, rank_epoch=r1.epoch, object_id=c["object_id"],
+                   lease_id=dup["lease_id"], slot_id=dup["slot_id"])
+    assert lose["ok"] and not lose["won"]
+    again = r1.call(Op.REQUEST_CANONICAL_EVICT, **dict(req, rank_id=1, rank_epoch=r1.epoch))
+    assert again["action"] == 0
+
+
+def test_seal_pull_tcp_and_file_restore_drop(cdaemon, tmp_path):
+    tensors = {f"layer{i}.w": torch.randn(100 + i, 33) for i in range(3)}
+    with session(cdaemon, 0) as off:
+        handles = {}
+        for name, t in tensors.items():
+            k = off.canonical_key(model_role=ROLL, model_version=5, param_name=name, tensor=t)
+            handles[name] = off.canonical_evict(t.clone(), k)
+        # pulling an unsealed version is refused
+        c = RolloutWeightClient(cdaemon, off.job_id, off.launch_epoch, job_name=off.job_name)
+        man_req_failed = False
+        try:
+            c.get_manifest(5)
+        except IOError:
+            man_req_failed = True
+        assert man_req_failed
+        info = off.promote_rollout_version(5)
+        assert info["tensor_count"] == 3
+        for transport in ("tcp", "file"):
+            c2 = RolloutWeightClient(cdaemon, off.job_id, off.launch_epoch, job_name=off.job_name)
+            res = c2.sync_latest(transport=transport, workers=2)
+            assert len(res["pulled"]) == 3
+            man = c2.get_manifest(5)
+            for e in man["tensors"]:
+                name = e["key"]["param_fqn_debug"]
+                assert res["data"][e["object_id"]] == tensors[name].numpy().tobytes()
+                assert e["location_hint"] == "pinned"
+            c2.close()
+        # canonical restore by object id
+        for name, h in handles.items():
+            out = torch.empty_like(tensors[name])
+            h.restore_into(out)
+            assert torch.equal(out, tensors[name])
+        # manifest export in fixed record format
+        path = str(tmp_path / "m.bin")
+        r = off.export_manifest(ROLL, 5, path)
+        assert r["tensor_count"] == 3 and os.path.getsize(path) == 192 + 3 * 384
+        with open(path, "rb") as f:
+            hdr = f.read(192)
+        tenant, job_id, epoch, role, state, ver, ntens = struct.unpack("<QQQIIQQ", hdr[:48])
+        assert (job_id, role, state, ver, ntens) == (off.job_id, ROLL, 2, 5, 3)
+        # writes into a sealed version are rejected
+        t = torch.randn(8)
+        k = off.canonical_key(model_role=ROLL, model_version=5, param_name="late", tensor=t)
+        with pytest.raises(RuntimeError, match="REJECTED_STALE_VERSION"):
+            off.canonical_evict(t, k)
+        d = off.drop_canonical_version(ROLL, 5)
+        assert d["dropped"] == 3 and d["skipped_inflight"] == 0
+        assert off.daemon_stats()["canonical_objects"] == 0
+
+
+def test_seal_fails_when_expected_params_missing(cdaemon):
+    with session(cdaemon, 0) as off:
+        t = torch.randn(64)
+        k = off.canonical_key(model_role=ROLL, model_version=2, param_name="a", tensor=t)
+        off.canonical_evict(t, k)
+        with pytest.raises(RuntimeError, match="missing"):
+            off.seal_model_version(ROLL, 2, expected_param_ids=[k.param_id, 12345])
+        assert off.seal_model_version(ROLL, 2, expected_param_ids=[k.param_id])["tensor_count"] == 1
+
+
+def test_multi_consumer_refcount_release(cdaemon):
+    w = torch.randn(512)
+    with session(cdaemon, 0) as a, session(cdaemon, 1) as b:
+        k = a.canonical_key(model_role=ROLL, model_version=9, param_name="w", tensor=w)
+        ha = a.canonical_evict(w.clone(), k)
+        hb = b.canonical_evict(w.clone(), k)
+        assert hb.attached
+        r1 = ha.release()
+        assert r1 == {"released": 1, "freed": 0, "bytes_freed": 0, "message": "ok"}
+        out = torch.empty_like(w)
+        hb.restore_into(out)  # still alive for the other holder
+        assert torch.equal(out, w)
+        r2 = b.release_canonical_version(ROLL, 9)
+        assert r2["freed"] == 1 and r2["bytes_freed"] == w.numel() * 4
+
+
+def test_pinned_quota_rejects(sock_path):
+    d = in_process_daemon(socket=sock_path, arena_mb=128, drain_on_complete=False, quota_max_pinned_bytes=1 << 20)
+    try:
+        with session(sock_path, 0) as off:
+            t = torch.randn(1 << 18)  # exactly 1 MiB
+            off.canonical_evict(t, off.canonical_key(model_role=ROLL, model_version=1, param_name="a", tensor=t))
+            t2 = torch.randn(16)
+            with pytest.raises(RuntimeError, match="QUOTA"):
+                off.canonical_evict(t2, off.canonical_key(model_role=ROLL, model_version=1, param_name="b",
+                                                          tensor=t2))
+            jobs = off.job_stats()
+            assert jobs[0]["pinned_bytes"] == 1 << 20
+    finally:
+        d.stop()
+
+
+def test_sealed_retention_drops_old_versions(sock_path):
+    d = in_process_daemon(socket=sock_path, arena_mb=128, drain_on_complete=False, retain_sealed_versions=2)
+    try:
+        with session(sock_path, 0) as off:
+            for v in range(1, 5):
+                t = torch.full((256,), float(v))
+                off.canonical_evict(t, off.canonical_key(model_role=ROLL, model_version=v, param_name="w", tensor=t))
+                off.promote_rollout_version(v)
+            c = RolloutWeightClient(sock_path, off.job_id, off.launch_epoch)
+            assert c.get_latest_sealed_version() == 4
+            with pytest.raises(IOError):
+                c.get_manifest(1)
+            assert len(c.get_manifest(3)["tensors"]) == 1
+            c.close()
+    finally:
+        d.stop()
+
+
+def test_diff_skips_unchanged_tensors_across_versions(cdaemon):
+    """A tensor whose bytes did not change between versions is not re-pulled."""
+    a, b = torch.randn(300), torch.randn(300)
+    with session(cdaemon, 0) as off:
+        c = RolloutWeightClient(cdaemon, off.job_id, off.launch_epoch)
+        for v, tensors in ((1, (a, b)), (2, (a, b + 1))):
+            for name, t in zip(("a", "b"), tensors):
+                off.canonical_evict(t.clone(), off.canonical_key(model_role=ROLL, model_version=v, param_name=name,
+                                                                 tensor=t))
+            off.promote_rollout_version(v)
+            res = c.sync_latest()
+            assert len(res["pulled"]) == (2 if v == 1 else 1)
+        c.close()

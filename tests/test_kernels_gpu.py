@@ -145,7 +145,13 @@ def test_quant_fp8_standalone():
     torch.cuda.synchronize()
     q_ref, s_ref = _fp8_reference(x.cpu())
     torch.testing.assert_close(scales.cpu(), s_ref, rtol=0, atol=0)
-    assert (out.cpu().float() != q_ref.float()).float().mean().item() < 1e-3
+    got, ref = out.cpu(), q_ref
+    diff = got.float() != ref.float()
+    assert diff.float().mean().item() < 5e-3
+    # every difference is a one-step rounding difference of the e4m3 code
+    codes_g = got.view(torch.uint8)[diff].int() & 0x7F
+    codes_r = ref.view(torch.uint8)[diff].int() & 0x7F
+    assert (codes_g - codes_r).abs().max().item() <= 1 if diff.any() else True
 
 
 def test_verify_peer_same_device_counts_mismatches():
