@@ -312,7 +312,10 @@ const std::map<std::string, Binder>& binders() {
         {"manager.enable_manifests", [](DaemonConfig& c, const Node& n, const std::string& k) { c.v2_enable_manifests = as_bool(n, k); }},
         {"manager.enable_rollout_export", [](DaemonConfig& c, const Node& n, const std::string& k) { c.v2_enable_rollout_export = as_bool(n, k); }},
         {"manager.control_tcp_port", [](DaemonConfig& c, const Node& n, const std::string& k) { c.v2_control_tcp_port = uint32_t(as_u64(n, k)); }},
-        {"manager.daemon_socket", [](DaemonConfig& c, const Node& n, const std::string& k) { c.socket_path = need_scalar(n, k); }},
+        {"manager.daemon_socket", [](DaemonConfig& c, const Node& n, const std::string& k) {
+             std::string s = need_scalar(n, k);
+             c.socket_path = s.rfind("unix://", 0) == 0 ? s.substr(7) : s;
+         }},
         // namespace
         {"namespace.default_tenant_id", [](DaemonConfig& c, const Node& n, const std::string& k) { c.v2_default_tenant_id = as_u64(n, k); }},
         {"namespace.require_job_registration", [](DaemonConfig& c, const Node& n, const std::string& k) { c.v2_require_job_registration = as_bool(n, k); }},

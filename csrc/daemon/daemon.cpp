@@ -42,6 +42,7 @@ char* map_shared(int fd, uint64_t size) {
 
 Daemon::Daemon(const DaemonConfig& cfg) : cfg_(cfg) {
     validate(cfg_);
+    Metrics::get().reset();  // counters describe this daemon instance
     daemon_epoch_ = real_ns();
     stripes_ = cfg_.nvme_stripe ? std::max<uint32_t>(1, cfg_.nvme_stripe_count) : 1;
     stripe_cursor_ = std::vector<std::atomic<uint64_t>>(stripes_);

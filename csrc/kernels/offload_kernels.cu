@@ -46,9 +46,43 @@ __device__ __forceinline__ uint4 ld_once(const void* p) {
     return v;
 }
 
+// Memory-access policy (uniform kernel argument): low nibble selects the
+// load form, high nibble the store form. Host-mapped traffic crosses PCIe,
+// where request sizes matter more than cache behaviour.
+//   load 0: ld.global.nc.L1::no_allocate      load 1: ... + .L2::256B prefetch
+//   load 2: ld.global.L2::128B (coherent path)
+//   store 0: st.global.cs   store 1: st.global (write-back)   store 2: st.global.wt
+__device__ __forceinline__ uint4 ld_policy(const void* p, int pol) {
+    uint4 v;
+    if ((pol & 15) == 1) {
+        asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(p));
+    } else if ((pol & 15) == 2) {
+        asm volatile("ld.global.L2::128B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(p));
+    } else {
+        v = ld_once(p);
+    }
+    return v;
+}
+
 __device__ __forceinline__ void st_stream(void* p, uint4 v) {
     asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
+}
+
+__device__ __forceinline__ void st_policy(void* p, uint4 v, int pol) {
+    int s = (pol >> 4) & 15;
+    if (s == 1)
+        asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                     : "memory");
+    else if (s == 2)
+        asm volatile("st.global.wt.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                     : "memory");
+    else
+        st_stream(p, v);
 }
 
 __device__ __forceinline__ uint4 ld_bytes(const uint8_t* p, uint32_t n) {
@@ -63,15 +97,15 @@ __device__ __forceinline__ void st_bytes(uint8_t* p, uint4 v, uint32_t n) {
 }
 
 template <bool ALIGNED>
-__device__ __forceinline__ uint4 load_vec(const uint8_t* p, uint32_t n) {
-    if (ALIGNED && n == 16) return ld_once(p);
+__device__ __forceinline__ uint4 load_vec(const uint8_t* p, uint32_t n, int pol = 0) {
+    if (ALIGNED && n == 16) return ld_policy(p, pol);
     return ld_bytes(p, n);
 }
 
 template <bool ALIGNED>
-__device__ __forceinline__ void store_vec(uint8_t* p, uint4 v, uint32_t n) {
+__device__ __forceinline__ void store_vec(uint8_t* p, uint4 v, uint32_t n, int pol = 0) {
     if (ALIGNED && n == 16)
-        st_stream(p, v);
+        st_policy(p, v, pol);
     else
         st_bytes(p, v, n);
 }
@@ -106,7 +140,7 @@ __device__ __forceinline__ uint64_t tree_fold(uint64_t d, uint64_t* red) {
 template <bool ALIGNED, bool HASH, bool STORE>
 __global__ void __launch_bounds__(kThreads, 2)
     k_evict(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
-            uint64_t* __restrict__ digests) {
+            uint64_t* __restrict__ digests, int pol) {
     __shared__ uint64_t red[kThreads / 32];
     const uint32_t t = threadIdx.x;
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
@@ -127,7 +161,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint32_t vi = uint32_t(k) * kThreads + t;
             if (vi < nvec) {
                 if (HASH) ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
-                if (STORE) store_vec<ALIGNED>(dst + base + uint64_t(vi) * 16, v[k], min(16u, len - vi * 16));
+                if (STORE) store_vec<ALIGNED>(dst + base + uint64_t(vi) * 16, v[k], min(16u, len - vi * 16), pol);
             }
         }
         if (HASH) {
@@ -176,7 +210,7 @@ __device__ __forceinline__ uint2 quant8(uint4 v, bool valid, float* scale_out) {
 template <bool ALIGNED, bool VERIFY, int CAST>
 __global__ void __launch_bounds__(kThreads, 2)
     k_restore(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
-              float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch) {
+              float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, int pol) {
     __shared__ uint64_t red[kThreads / 32];
     const uint32_t t = threadIdx.x;
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
@@ -189,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int k = 0; k < kVecs; ++k) {
             const uint32_t vi = uint32_t(k) * kThreads + t;
             const uint32_t n = vi < nvec ? min(16u, len - vi * 16) : 0u;
-            v[k] = n ? load_vec<ALIGNED>(src + base + uint64_t(vi) * 16, n) : make_uint4(0, 0, 0, 0);
+            v[k] = n ? load_vec<ALIGNED>(src + base + uint64_t(vi) * 16, n, pol) : make_uint4(0, 0, 0, 0);
         }
         ssh::Lane L = ssh::lane_init(t);
 #pragma unroll
@@ -323,19 +357,28 @@ int grid_for(uint64_t nbytes, int ctas, int dflt) {
 
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
+namespace {
+// Process-wide access policy for host-mapped traffic (see ld_policy/st_policy).
+std::atomic<int> g_policy{0};
+}  // namespace
+
+void set_access_policy(int load_form, int store_form) { g_policy.store((load_form & 15) | ((store_form & 15) << 4)); }
+int access_policy() { return g_policy.load(); }
+
 cudaError_t evict_hash(const void* src, void* dst, uint64_t nbytes, uint64_t* digests, cudaStream_t s, int ctas) {
     if (nbytes == 0) return cudaSuccess;
     if (!src || !dst) return cudaErrorInvalidValue;
     const int g = grid_for(nbytes, ctas, 48);
     const bool al = aligned16(src) && aligned16(dst);
+    const int pol = g_policy.load(std::memory_order_relaxed);
     auto S = static_cast<const uint8_t*>(src);
     auto D = static_cast<uint8_t*>(dst);
     if (digests) {
-        if (al) k_evict<true, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests);
-        else k_evict<false, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests);
+        if (al) k_evict<true, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests, pol);
+        else k_evict<false, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests, pol);
     } else {
-        if (al) k_evict<true, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr);
-        else k_evict<false, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr);
+        if (al) k_evict<true, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, pol);
+        else k_evict<false, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, pol);
     }
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
@@ -346,8 +389,8 @@ cudaError_t hash_device(const void* src, uint64_t nbytes, uint64_t* digests, cud
     if (!src || !digests) return cudaErrorInvalidValue;
     const int g = grid_for(nbytes, ctas, 148 * 4);
     auto S = static_cast<const uint8_t*>(src);
-    if (aligned16(src)) k_evict<true, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests);
-    else k_evict<false, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests);
+    if (aligned16(src)) k_evict<true, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests, 0);
+    else k_evict<false, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests, 0);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -358,29 +401,30 @@ cudaError_t restore_cast(const void* src, void* dst, uint64_t nbytes, Cast cast,
     if (!src || !dst) return cudaErrorInvalidValue;
     if (expect && !mismatch) return cudaErrorInvalidValue;
     const int g = grid_for(nbytes, ctas, 96);
+    const int p = g_policy.load(std::memory_order_relaxed);
     auto S = static_cast<const uint8_t*>(src);
     auto D = static_cast<uint8_t*>(dst);
     const bool verify = expect != nullptr;
     if (cast == Cast::kNone) {
         const bool al = aligned16(src) && aligned16(dst);
-        if (al && verify) k_restore<true, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch);
-        else if (al) k_restore<true, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr);
-        else if (verify) k_restore<false, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch);
-        else k_restore<false, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr);
+        if (al && verify) k_restore<true, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
+        else if (al) k_restore<true, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+        else if (verify) k_restore<false, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
+        else k_restore<false, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
     } else {
         // Casts need element-aligned whole vectors.
         if (!aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7) || nbytes % 16) return cudaErrorInvalidValue;
         if (cast == Cast::kBf16ToFp8Block128) {
             if (!scales) return cudaErrorInvalidValue;
-            if (verify) k_restore<true, true, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, expect, mismatch);
-            else k_restore<true, false, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, nullptr, nullptr);
+            if (verify) k_restore<true, true, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, expect, mismatch, p);
+            else k_restore<true, false, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, nullptr, nullptr, p);
         } else if (cast == Cast::kFp32ToBf16) {
-            if (verify) k_restore<true, true, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch);
-            else k_restore<true, false, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr);
+            if (verify) k_restore<true, true, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
+            else k_restore<true, false, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
         } else if (cast == Cast::kBf16ToFp32) {
             if (reinterpret_cast<uintptr_t>(dst) & 15) return cudaErrorInvalidValue;
-            if (verify) k_restore<true, true, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch);
-            else k_restore<true, false, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr);
+            if (verify) k_restore<true, true, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
+            else k_restore<true, false, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
         } else {
             return cudaErrorInvalidValue;
         }

@@ -541,6 +541,8 @@ PYBIND11_MODULE(_C, m) {
 
     // ---- raw kernel launchers (tests, benchmarks, fabric layer) ----
     m.def("kernel_launch_count", &kern::launch_count);
+    m.def("set_access_policy", &kern::set_access_policy, py::arg("load_form"), py::arg("store_form"));
+    m.def("access_policy", &kern::access_policy);
     m.def("cuda_available", [] {
         int n = 0;
         return cudaGetDeviceCount(&n) == cudaSuccess && n > 0;
