@@ -29,7 +29,7 @@ COMMON = ["common/codec.cpp", "common/transport.cpp", "common/metrics.cpp", "com
 DAEMON = ["daemon/config.cpp", "daemon/daemon.cpp", "daemon/slots.cpp", "daemon/tiers.cpp",
           "daemon/nvme.cpp", "daemon/canonical.cpp", "daemon/rollout.cpp"]
 AGENT = ["agent/agent.cpp"]
-KERNELS = ["kernels/offload_kernels.cu", "kernels/weight_sync.cu"]
+KERNELS = ["kernels/offload_kernels.cu", "kernels/weight_sync.cu", "kernels/hash_noalloc.cu"]
 FABRIC = ["fabric/fabric.cpp"]
 MODULE = ["python/module.cpp", "python/fabric_bind.cpp"]
 
