@@ -1136,6 +1136,12 @@ ReleaseCanonicalResponse Agent::release(const ReleaseCanonicalRequest& in) {
     r.rank_epoch = d_->epoch;
     return d_->call<Op::kReleaseCanonical>(r);
 }
+CarryForwardResponse Agent::carry_forward(const CarryForwardRequest& in) {
+    CarryForwardRequest r = in;
+    r.rank_id = d_->opt.rank_id;
+    r.rank_epoch = d_->epoch;
+    return d_->call<Op::kCarryForward>(r);
+}
 ExportManifestResponse Agent::export_manifest(const ExportManifestRequest& r) {
     return d_->call<Op::kExportManifest>(r);
 }

@@ -131,6 +131,9 @@ class Agent {
     GetManifestResponse manifest(const GetManifestRequest& r);
     PullTensorResponse pull(const PullTensorRequest& r);
     DropCanonicalVersionResponse drop_version(const DropCanonicalVersionRequest& r);
+    // Objects of a new version that share the storage of an older version's
+    // unchanged objects (rank id / epoch are filled in).
+    CarryForwardResponse carry_forward(const CarryForwardRequest& r);
     ReleaseCanonicalResponse release(const ReleaseCanonicalRequest& r);
     ExportManifestResponse export_manifest(const ExportManifestRequest& r);
     GetJobStatsResponse job_stats(const GetJobStatsRequest& r);

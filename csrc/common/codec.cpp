@@ -40,6 +40,7 @@ const char* op_name(Op op) {
         case Op::kGetJobStats: return "GetJobStats";
         case Op::kExportManifest: return "ExportManifest";
         case Op::kDiscardTensor: return "DiscardTensor";
+        case Op::kCarryForward: return "CarryForward";
     }
     return "Unknown";
 }
@@ -87,6 +88,7 @@ std::vector<uint8_t> reencode_body(Op op, bool response, const std::vector<uint8
         CASE(kReleaseCanonicalRestore) CASE(kDropCanonicalVersion) CASE(kReleaseCanonical)
         CASE(kBatchRequestOffload) CASE(kBatchRequestPrefetch) CASE(kPublishPeerBuffer)
         CASE(kLookupPeerBuffer) CASE(kGetJobStats) CASE(kExportManifest) CASE(kDiscardTensor)
+        CASE(kCarryForward)
 #undef CASE
         default: break;
     }

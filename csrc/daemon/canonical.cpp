@@ -325,6 +325,7 @@ RequestCanonicalEvictResponse Daemon::on_canonical_evict(const RequestCanonicalE
     o.slot_count = slots_for(r.key.nbytes);
     o.created_ns = o.last_access_ns = real_ns();
     objects_[oid] = o;
+    storage_[syn].objects = 1;
     object_by_key_[ks] = oid;
     jobs_[juid].object_count++;
     resp.ok = true;
@@ -427,9 +428,34 @@ CommitCanonicalObjectResponse Daemon::on_commit_canonical(const CommitCanonicalO
 
 // Free an object's backing and table entry unless a transfer is in flight.
 // Ignores holders (callers decide). mu_ held.
+void Daemon::storage_io(uint64_t tid, int delta) {
+    auto it = storage_.find(tid);
+    if (it == storage_.end()) return;
+    if (delta > 0) it->second.io += uint32_t(delta);
+    else it->second.io -= std::min(it->second.io, uint32_t(-delta));
+}
+
+bool Daemon::storage_busy(uint64_t tid) const {
+    auto it = storage_.find(tid);
+    return it != storage_.end() && it->second.io > 0;
+}
+
 bool Daemon::release_object(CanonicalObject& o) {
     if (o.export_refs || o.restore_refs) return false;
     const uint64_t oid = o.object_id, nbytes = o.nbytes;
+    // Storage shared with carried-forward objects stays until its last user goes.
+    auto sit = storage_.find(o.synthetic_tid);
+    if (sit != storage_.end() && sit->second.objects > 1) {
+        sit->second.objects--;
+        auto kit = object_by_key_.find(o.key_str);
+        if (kit != object_by_key_.end() && kit->second == oid) object_by_key_.erase(kit);
+        if (Job* j = find_job(o.key.job))
+            if (j->object_count) j->object_count--;
+        Metrics::get().inc(M::kCanonicalObjectsDropped);
+        objects_.erase(oid);
+        return true;
+    }
+    if (sit != storage_.end()) storage_.erase(sit);
     auto lit = locations_.find(o.synthetic_tid);
     if (lit != locations_.end()) {
         if (lit->second.kind == OFLD_LOC_PINNED) {
@@ -472,6 +498,83 @@ void Daemon::purge_rank_holds(uint32_t rank) {
         if (kv.second.holders.erase(rank)) touched.push_back(kv.first);
     for (uint64_t oid : touched)
         if (CanonicalObject* o = find_object(oid)) maybe_free_object(*o);
+}
+
+CarryForwardResponse Daemon::on_carry_forward(const CarryForwardRequest& r) {
+    std::lock_guard<std::mutex> g(mu_);
+    CarryForwardResponse resp;
+    if (!cfg_.v2_enable_canonical_store) {
+        resp.message = "canonical store disabled";
+        return resp;
+    }
+    if (!epoch_ok(r.rank_id, r.rank_epoch)) {
+        Metrics::get().inc(M::kEpochMismatchRejected);
+        resp.message = "epoch invalid";
+        return resp;
+    }
+    Job* job = find_job(r.job);
+    if (!job) {
+        resp.message = "job not registered";
+        return resp;
+    }
+    if (r.to_version == r.from_version) {
+        resp.message = "from_version == to_version";
+        return resp;
+    }
+    auto mit = manifests_.find(VersionKey{job->uid, r.model_role, r.to_version});
+    if (mit != manifests_.end() && mit->second.state == MANIFEST_SEALED) {
+        resp.message = "target version already sealed";
+        return resp;
+    }
+    std::unordered_map<uint64_t, uint64_t> by_param;  // param_id -> object id at from_version
+    for (uint64_t oid : objects_of_version(job->uid, r.model_role, r.from_version)) {
+        const CanonicalObject& o = objects_[oid];
+        if (readable(o.state)) by_param[o.key.param_id] = oid;
+    }
+    std::vector<uint64_t> want = r.param_ids;
+    if (want.empty())
+        for (auto& kv : by_param) want.push_back(kv.first);
+    for (uint64_t pid : want) {
+        auto bit = by_param.find(pid);
+        if (bit == by_param.end()) {
+            resp.missing_count++;
+            continue;
+        }
+        const CanonicalObject src = objects_[bit->second];
+        CanonicalTensorKeyWire key = src.key;
+        key.model_version = r.to_version;
+        const std::string ks = key_string(key, cfg_.v2_cross_job_dedup);
+        if (object_by_key_.count(ks)) {
+            resp.existing_count++;
+            continue;
+        }
+        CanonicalObject o;
+        o.object_id = next_object_++;
+        o.key = key;
+        o.key_str = ks;
+        o.nbytes = src.nbytes;
+        // The new object is a committed member of its version; where its bytes
+        // live is read from the shared storage's location entry.
+        o.state = src.state == OBJ_SEALED || src.state == OBJ_EXPORT_IN_FLIGHT ? OBJ_VALID_MULTI_TIER : src.state;
+        o.holders.insert(r.rank_id);
+        o.producer_rank = src.producer_rank;
+        o.hash_lo = src.hash_lo;
+        o.hash_hi = src.hash_hi;
+        o.synthetic_tid = src.synthetic_tid;
+        o.slot_count = src.slot_count;
+        o.created_ns = o.last_access_ns = real_ns();
+        storage_[src.synthetic_tid].objects++;
+        object_by_key_[ks] = o.object_id;
+        objects_[o.object_id] = o;
+        job->object_count++;
+        job->dedup_bytes_saved += src.nbytes;
+        resp.carried_count++;
+        resp.bytes_shared += src.nbytes;
+    }
+    Metrics::get().add(M::kCanonicalDedupBytesSaved, resp.bytes_shared);
+    resp.ok = true;
+    resp.message = "ok";
+    return resp;
 }
 
 ReleaseCanonicalResponse Daemon::on_release_canonical(const ReleaseCanonicalRequest& r) {

@@ -391,6 +391,7 @@ void Daemon::dispatch(int fd, Op op, const std::vector<uint8_t>& b, std::vector<
         ROUTE(kGetJobStats, on_get_job_stats(req))
         ROUTE(kExportManifest, on_export_manifest(req))
         ROUTE(kDiscardTensor, on_discard_tensor(req))
+        ROUTE(kCarryForward, on_carry_forward(req))
         default:
             LOG_WARN(TAG, "unknown opcode %u", unsigned(op));
             throw std::runtime_error("unknown opcode");

@@ -271,6 +271,7 @@ class Daemon {
 
     // rollout.cpp
     SealModelVersionResponse on_seal(const SealModelVersionRequest& r);
+    CarryForwardResponse on_carry_forward(const CarryForwardRequest& r);
     GetLatestSealedVersionResponse on_get_latest(const GetLatestSealedVersionRequest& r);
     GetManifestResponse on_get_manifest(const GetManifestRequest& r);
     PullTensorResponse on_pull_tensor(const PullTensorRequest& r);
@@ -349,6 +350,16 @@ class Daemon {
 
     std::map<JobUID, Job> jobs_;
     std::unordered_map<uint64_t, CanonicalObject> objects_;
+    // Canonical storage (keyed by synthetic tensor id) shared by the objects
+    // of carried-forward versions: `objects` counts the objects that reference
+    // it, `io` the exports / restores reading it across all of them.
+    struct StorageRef {
+        uint32_t objects = 0;
+        uint32_t io = 0;
+    };
+    std::unordered_map<uint64_t, StorageRef> storage_;
+    void storage_io(uint64_t tid, int delta);
+    bool storage_busy(uint64_t tid) const;
     std::unordered_map<std::string, uint64_t> object_by_key_;
     std::map<VersionKey, Manifest> manifests_;
     std::map<std::pair<JobUID, uint32_t>, uint64_t> latest_sealed_;

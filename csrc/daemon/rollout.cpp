@@ -344,6 +344,7 @@ PullTensorResponse Daemon::on_pull_tensor(const PullTensorRequest& r) {
         return resp;
     }
     if (o->export_refs++ == 0) o->state_before_export = o->state;
+    storage_io(o->synthetic_tid, +1);
     o->state = OBJ_EXPORT_IN_FLIGHT;
     job->inflight_export_bytes += nbytes;
     job->exports_in_flight++;
@@ -395,7 +396,10 @@ PullTensorResponse Daemon::on_pull_tensor(const PullTensorRequest& r) {
     }
     Metrics::get().sub(M::kExportInflightBytes, nbytes);
     if (CanonicalObject* o2 = find_object(r.object_id)) {
-        if (o2->export_refs) o2->export_refs--;
+        if (o2->export_refs) {
+            o2->export_refs--;
+            storage_io(o2->synthetic_tid, -1);
+        }
         if (o2->export_refs == 0) o2->state = o2->state_before_export;
         maybe_free_object(*o2);
     }
@@ -505,6 +509,7 @@ RequestCanonicalRestoreResponse Daemon::on_canonical_restore(const RequestCanoni
         return resp;
     }
     o->restore_refs++;
+    storage_io(o->synthetic_tid, +1);
     o->last_access_ns = real_ns();
     Metrics::get().inc(M::kCanonicalRestoreServed);
     resp.ok = true;
@@ -522,7 +527,10 @@ StatusResponse Daemon::on_release_canonical_restore(const ReleaseCanonicalRestor
         return {false, "epoch invalid"};
     }
     if (CanonicalObject* o = find_object(r.object_id)) {
-        if (o->restore_refs) o->restore_refs--;
+        if (o->restore_refs) {
+            o->restore_refs--;
+            storage_io(o->synthetic_tid, -1);
+        }
         maybe_free_object(*o);
     }
     return {true, "ok"};

@@ -210,7 +210,7 @@ void Daemon::finish_drain(uint32_t base, uint32_t count, uint64_t tid, uint64_t 
     for (uint32_t k = 0; k < count; ++k) slots_[base + k].cold_ref = ref;
     CanonicalObject* o = nullptr;
     if (is_canonical_tid(tid) && !is_candidate_tid(tid)) o = find_object(tid & ~kCanonicalTidBit);
-    if (o && (o->export_refs || o->restore_refs)) {
+    if (storage_busy(tid) || (o && (o->export_refs || o->restore_refs))) {
         set_run_state(base, count, OFLD_SLOT_PINNED_VALID);
         set_location(tid, ver, OFLD_LOC_PINNED, base, ref, nbytes);
         if (o->state == OBJ_VALID_PINNED) o->state = OBJ_VALID_MULTI_TIER;

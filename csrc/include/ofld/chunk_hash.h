@@ -121,6 +121,7 @@ SSH_HD Object object_finish(uint64_t lo, uint64_t hi, uint64_t nbytes) {
 }
 
 inline uint64_t num_chunks(uint64_t nbytes) { return (nbytes + kChunkBytes - 1) / kChunkBytes; }
+SSH_HD uint64_t num_chunks_dev(uint64_t nbytes) { return (nbytes + kChunkBytes - 1) / kChunkBytes; }
 
 // ---- host reference implementation -------------------------------------
 

@@ -56,6 +56,7 @@ enum class Op : uint16_t {
     kGetJobStats = 44,           // per-job accounting export
     kExportManifest = 45,        // write a sealed manifest in ABI record format
     kDiscardTensor = 46,         // drop a tensor's pinned and cold copies by identity
+    kCarryForward = 47,          // new-version objects that share an older version's storage
 };
 
 const char* op_name(Op op);
@@ -658,6 +659,32 @@ struct LookupPeerBufferResponse {
 };
 template <class V> void fields(V& v, LookupPeerBufferResponse& m) {
     v(m.ok, m.message, m.found, m.desc);
+}
+
+// Carry-forward: for every object of `from_version` whose param_id is listed
+// (all objects when the list is empty), create the same key at `to_version`
+// sharing the old object's storage and content hash. No bytes move; the
+// storage is freed when the last object that shares it is released.
+struct CarryForwardRequest {
+    uint32_t rank_id = 0;
+    uint64_t rank_epoch = 0;
+    JobKeyWire job;
+    uint32_t model_role = 0;
+    uint64_t from_version = 0, to_version = 0;
+    std::vector<uint64_t> param_ids;
+};
+template <class V> void fields(V& v, CarryForwardRequest& m) {
+    v(m.rank_id, m.rank_epoch, m.job, m.model_role, m.from_version, m.to_version, m.param_ids);
+}
+
+struct CarryForwardResponse {
+    bool ok = false;
+    std::string message;
+    uint32_t carried_count = 0, existing_count = 0, missing_count = 0;
+    uint64_t bytes_shared = 0;
+};
+template <class V> void fields(V& v, CarryForwardResponse& m) {
+    v(m.ok, m.message, m.carried_count, m.existing_count, m.missing_count, m.bytes_shared);
 }
 
 struct JobStatsEntry {

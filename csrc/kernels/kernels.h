@@ -76,5 +76,49 @@ cudaError_t quant_fp8_block(const void* bf16_src, void* fp8_dst, float* scales, 
 // Number of chunk digests for nbytes.
 inline uint64_t digest_count(uint64_t nbytes) { return (nbytes + 65535) / 65536; }
 
+// K4 work item (64 bytes, laid out for a host-packed table). `chunk_begin` is
+// the global index of the item's first 64 KiB chunk; items are sorted by it
+// and item i owns chunks [chunk_begin_i, chunk_begin_i + ceil(nbytes/64KiB)).
+// nbytes is a multiple of 16 (a multiple of 256 for kPushFp8).
+//   mode kPushRaw   copy the bytes to `dst`
+//        kPushFp8   bf16 source; write fp8 e4m3 bytes to `dst` and one fp32
+//                   scale (amax/448) per 128 elements to `dst_scales`
+//        kPushHash  digests only, nothing is stored
+//   flags kPushDelta  skip the stores of a chunk whose new digest equals the
+//                     digest already in the launch's `digests` table (the
+//                     table describes what the destination holds)
+// `dst` / `dst_scales` are typically peer-GPU pointers (CUDA IPC mappings).
+enum : uint32_t { kPushRaw = 0, kPushFp8 = 1, kPushHash = 2 };
+enum : uint32_t { kPushDelta = 1u << 0 };
+struct PushItem {
+    const void* src;
+    void* dst;
+    float* dst_scales;
+    uint64_t nbytes;
+    uint64_t chunk_begin;
+    uint32_t mode;
+    uint32_t flags;
+    uint64_t pad1, pad2;
+};
+static_assert(sizeof(PushItem) == 64, "PushItem is a 64-byte record");
+
+// Per-launch device state of K4 (all device-accessible memory).
+//   digests     [total_chunks] u64, in/out: one ssh128 chunk digest per chunk
+//   item_hash   [2*nitems] u64 out (may be null): 128-bit object hash per item
+//   item_done   [nitems] u32, must be zero before the first launch; the
+//               kernel returns every entry to zero
+//   stats       [2] u64 accumulated (may be null): chunks stored, bytes stored
+struct PushState {
+    uint64_t* digests;
+    uint64_t* item_hash;
+    uint32_t* item_done;
+    unsigned long long* stats;
+};
+
+// K4. Launches one persistent grid over every chunk of every item.
+cudaError_t push(const PushItem* items_dev, int nitems, uint64_t total_chunks, PushState st, cudaStream_t s,
+                 int ctas);
+uint64_t push_launch_count();
+
 }  // namespace kern
 }  // namespace ofld

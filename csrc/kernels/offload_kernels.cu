@@ -355,7 +355,7 @@ int grid_for(uint64_t nbytes, int ctas, int dflt) {
 
 
 
-uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed) + push_launch_count(); }
 
 namespace {
 // Process-wide access policy for host-mapped traffic (see ld_policy/st_policy).

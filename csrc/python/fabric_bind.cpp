@@ -1,0 +1,52 @@
+// Python bindings of the intra-node fabric (CUDA IPC export / open of device
+// buffers) and of the K4 weight-sync push kernel. Pointers cross as integers,
+// IPC handles as 64-byte `bytes`.
+#include <cuda_runtime.h>
+#include <pybind11/pybind11.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "../fabric/fabric.h"
+#include "../kernels/kernels.h"
+
+namespace py = pybind11;
+using namespace ofld;
+
+void bind_fabric(py::module_& m) {
+    m.def("ipc_export", [](uint64_t ptr) {
+        fabric::Export e = fabric::export_ptr(ptr);
+        py::dict d;
+        d["handle"] = py::bytes(e.handle);
+        d["base"] = e.base;
+        d["offset"] = e.offset;
+        d["alloc_size"] = e.alloc_size;
+        d["device"] = e.device;
+        return d;
+    });
+    m.def(
+        "ipc_open",
+        [](py::bytes handle, uint64_t offset) {
+            py::gil_scoped_release r;
+            return fabric::open_handle(std::string(handle), offset);
+        },
+        py::arg("handle"), py::arg("offset") = 0);
+    m.def("ipc_close", [](uint64_t ptr) { fabric::close_ptr(ptr); });
+    m.def("ipc_open_count", &fabric::open_count);
+    m.def("can_access_peer", &fabric::can_access_peer);
+    m.def("enable_peer", &fabric::enable_peer);
+    m.def("push_item_bytes", [] { return int(sizeof(kern::PushItem)); });
+    m.def(
+        "k_push",
+        [](uint64_t items, int nitems, uint64_t total_chunks, uint64_t digests, uint64_t item_hash,
+           uint64_t item_done, uint64_t stats, uint64_t stream, int ctas) {
+            kern::PushState st{reinterpret_cast<uint64_t*>(digests), reinterpret_cast<uint64_t*>(item_hash),
+                               reinterpret_cast<uint32_t*>(item_done),
+                               reinterpret_cast<unsigned long long*>(stats)};
+            cudaError_t e = kern::push(reinterpret_cast<const kern::PushItem*>(items), nitems, total_chunks, st,
+                                       reinterpret_cast<cudaStream_t>(stream), ctas);
+            if (e != cudaSuccess) throw std::runtime_error(std::string("push: ") + cudaGetErrorString(e));
+        },
+        py::arg("items"), py::arg("nitems"), py::arg("total_chunks"), py::arg("digests"), py::arg("item_hash"),
+        py::arg("item_done"), py::arg("stats"), py::arg("stream"), py::arg("ctas") = 0);
+}

@@ -25,6 +25,8 @@
 namespace py = pybind11;
 using namespace ofld;
 
+void bind_fabric(py::module_& m);  // fabric_bind.cpp
+
 namespace {
 
 bool py_alive() { return Py_IsInitialized() && !_Py_IsFinalizing(); }
@@ -389,6 +391,7 @@ PYBIND11_MODULE(_C, m) {
                          RAW(kReleaseCanonical, release)
                          RAW(kExportManifest, export_manifest)
                          RAW(kGetJobStats, job_stats)
+                         RAW(kCarryForward, carry_forward)
 #undef RAW
                          case Op::kGetStats: out = encode(a.daemon_stats()); break;
                          default: throw std::invalid_argument("call_raw: opcode not routed through the agent");
@@ -590,4 +593,5 @@ PYBIND11_MODULE(_C, m) {
         return reinterpret_cast<uint64_t>(dev);
     });
     m.def("host_unregister", [](uint64_t ptr) { check(cudaHostUnregister(reinterpret_cast<void*>(ptr)), "cudaHostUnregister"); });
+    bind_fabric(m);
 }

@@ -58,6 +58,7 @@ class Op:
     GET_JOB_STATS = 44
     EXPORT_MANIFEST = 45
     DISCARD_TENSOR = 46
+    CARRY_FORWARD = 47
 
 
 # Backward-compatible names used by rollout engines.
@@ -189,6 +190,10 @@ SCHEMA: Dict[str, List[Tuple[str, Any]]] = {
     "ExportManifestRequest": [("job", "JobKey"), ("model_role", "u32"), ("model_version", "u64"), ("path", S)],
     "ExportManifestResponse": STATUS + [("bytes_written", "u64"), ("tensor_count", "u64")],
     "DiscardTensorRequest": [("rank_id", "u32"), ("rank_epoch", "u64"), ("tensor_id", "u64"), ("version", "u64")],
+    "CarryForwardRequest": [("rank_id", "u32"), ("rank_epoch", "u64"), ("job", "JobKey"), ("model_role", "u32"),
+                            ("from_version", "u64"), ("to_version", "u64"), ("param_ids", ["u64"])],
+    "CarryForwardResponse": STATUS + [("carried_count", "u32"), ("existing_count", "u32"), ("missing_count", "u32"),
+                                      ("bytes_shared", "u64")],
 }
 
 # opcode -> (request message, response message)
@@ -224,6 +229,7 @@ OPS: Dict[int, Tuple[str, str]] = {
     Op.GET_JOB_STATS: ("GetJobStatsRequest", "GetJobStatsResponse"),
     Op.EXPORT_MANIFEST: ("ExportManifestRequest", "ExportManifestResponse"),
     Op.DISCARD_TENSOR: ("DiscardTensorRequest", "Status"),
+    Op.CARRY_FORWARD: ("CarryForwardRequest", "CarryForwardResponse"),
 }
 
 _PRIM = {"u8": struct.Struct("<B"), "u16": struct.Struct("<H"), "u32": struct.Struct("<I"),

@@ -537,6 +537,23 @@ class Off:
         return {"dropped": r["dropped_count"], "skipped_inflight": r["skipped_inflight"],
                 "bytes_freed": r["bytes_freed"], "message": r["message"]}
 
+    def carry_forward_version(self, model_role, from_version: int, to_version: int,
+                              param_ids: Optional[Sequence[int]] = None) -> dict:
+        """Make `to_version` objects for unchanged params that share the
+        storage (and content hash) of `from_version`'s objects; nothing is
+        copied. `param_ids=None` carries every object of `from_version`.
+        Keys already present at `to_version` are left alone (`existing`).
+        (No reference counterpart: the reference re-evicts every object of
+        each version, python_api/state_spectre/__init__.py:575.)"""
+        r = self._raw(_wire.Op.CARRY_FORWARD, {
+            "rank_id": 0, "rank_epoch": 0, "job": self._job(), "model_role": ModelRole.parse(model_role),
+            "from_version": int(from_version), "to_version": int(to_version),
+            "param_ids": [int(p) for p in (param_ids or [])]})
+        if not r["ok"]:
+            raise RuntimeError(f"carry_forward failed: {r['message']}")
+        return {"carried": r["carried_count"], "existing": r["existing_count"], "missing": r["missing_count"],
+                "bytes_shared": r["bytes_shared"]}
+
     def _release(self, role: int, version: int, object_id: int) -> dict:
         r = self._raw(_wire.Op.RELEASE_CANONICAL, {
             "rank_id": self._agent.rank_id(), "rank_epoch": self._agent.rank_epoch(), "job": self._job(),

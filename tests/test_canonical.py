@@ -247,3 +247,57 @@ def test_diff_skips_unchanged_tensors_across_versions(cdaemon):
             res = c.sync_latest()
             assert len(res["pulled"]) == (2 if v == 1 else 1)
         c.close()
+
+
+def test_carry_forward_shares_storage_and_survives_retention(sock_path):
+    """Unchanged params of a new version share the old version's storage; the
+    storage outlives the version that created it and is pulled byte-exact."""
+    d = in_process_daemon(socket=sock_path, arena_mb=128, drain_on_complete=False, retain_sealed_versions=2)
+    try:
+        a, b = torch.randn(4096), torch.randn(4096)
+        with session(sock_path, 0) as off:
+            keys = {}
+            for name, t in (("a", a), ("b", b)):
+                k = off.canonical_key(model_role=ROLL, model_version=1, param_name=name, tensor=t)
+                keys[name] = k
+                off.canonical_evict(t.clone(), k)
+            off.promote_rollout_version(1)
+            used1 = off.daemon_stats()["used_slots"]
+            cur_b = b
+            for v in range(2, 6):
+                cur_b = cur_b + 1
+                k = off.canonical_key(model_role=ROLL, model_version=v, param_name="b", tensor=cur_b)
+                off.canonical_evict(cur_b.clone(), k)
+                r = off.carry_forward_version(ROLL, v - 1, v, [keys["a"].param_id])
+                assert r["carried"] == 1 and r["missing"] == 0 and r["bytes_shared"] == a.numel() * 4
+                again = off.carry_forward_version(ROLL, v - 1, v, [keys["a"].param_id])
+                assert again["existing"] == 1 and again["carried"] == 0
+                off.promote_rollout_version(v)
+            # v1 and v2.. v3 dropped by retention; "a" still lives in v4/v5 without a copy
+            stats = off.daemon_stats()
+            assert stats["used_slots"] <= used1 + 2  # one slot run for a, and b of v4 + v5 (64 MiB slots)
+            c = RolloutWeightClient(sock_path, off.job_id, off.launch_epoch)
+            man = c.get_manifest(5)
+            names = {e["object_id"]: e["key"]["param_fqn_debug"] for e in man["tensors"]}
+            assert set(names.values()) == {"a", "b"}
+            res = c.sync_latest()
+            want = {"a": a, "b": cur_b}
+            for oid, data in res["data"].items():
+                assert data == want[names[oid]].numpy().tobytes()
+            c.close()
+            off.drop_canonical_version(ROLL, 4)
+            off.drop_canonical_version(ROLL, 5)
+            assert off.daemon_stats()["used_slots"] == 0
+    finally:
+        d.stop()
+
+
+def test_carry_forward_rejects_sealed_target_and_unknown_job(cdaemon):
+    with session(cdaemon, 0) as off:
+        t = torch.ones(64)
+        off.canonical_evict(t, off.canonical_key(model_role=ROLL, model_version=1, param_name="w", tensor=t))
+        off.promote_rollout_version(1)
+        with pytest.raises(RuntimeError, match="already sealed"):
+            off.carry_forward_version(ROLL, 2, 1)
+        r = off.carry_forward_version(ROLL, 1, 2, [12345])
+        assert r["missing"] == 1 and r["carried"] == 0
