@@ -104,16 +104,32 @@ static_assert(sizeof(PushItem) == 64, "PushItem is a 64-byte record");
 
 // Per-launch device state of K4 (all device-accessible memory).
 //   digests     [total_chunks] u64, in/out: one ssh128 chunk digest per chunk
-//   item_hash   [2*nitems] u64 out (may be null): 128-bit object hash per item
-//   item_done   [nitems] u32, must be zero before the first launch; the
-//               kernel returns every entry to zero
+//   item_hash   [2*nitems] u64 out (may be null): 128-bit object hash per
+//               item, folded by a second small launch on the same stream
 //   stats       [2] u64 accumulated (may be null): chunks stored, bytes stored
+//   error       u32 (may be null): 0, or the first bounded wait that expired
+//               (1 chunk never arrived in shared memory, 2 stage never freed)
 struct PushState {
     uint64_t* digests;
     uint64_t* item_hash;
-    uint32_t* item_done;
     unsigned long long* stats;
+    uint32_t* error;
 };
+
+// K4. One persistent grid over every chunk of every item (+ the item-hash
+// fold when `item_hash` is set). `launch_flags` & kPushDelta must be set when
+// any item carries kPushDelta (it selects the block shape that holds stages
+// across the store decision).
+cudaError_t push(const PushItem* items_dev, int nitems, uint64_t total_chunks, PushState st, cudaStream_t s,
+                 int ctas, uint32_t launch_flags);
+
+// Chunk digests of a device buffer through the K4 pipeline (bulk copies into
+// shared memory, one CTA per SM). src 16-byte aligned, nbytes % 16 == 0.
+cudaError_t hash_stream(const void* src_dev, uint64_t nbytes, uint64_t* digests, uint32_t* error, cudaStream_t s,
+                        int ctas);
+
+// Dynamic shared memory of one K4 CTA (three 64 KiB stages + barriers).
+size_t push_smem_bytes();
 
 // K4. Launches one persistent grid over every chunk of every item.
 cudaError_t push(const PushItem* items_dev, int nitems, uint64_t total_chunks, PushState st, cudaStream_t s,

@@ -38,15 +38,24 @@ void bind_fabric(py::module_& m) {
     m.def("push_item_bytes", [] { return int(sizeof(kern::PushItem)); });
     m.def(
         "k_push",
-        [](uint64_t items, int nitems, uint64_t total_chunks, uint64_t digests, uint64_t item_hash,
-           uint64_t item_done, uint64_t stats, uint64_t stream, int ctas) {
+        [](uint64_t items, int nitems, uint64_t total_chunks, uint64_t digests, uint64_t item_hash, uint64_t stats,
+           uint64_t error, uint64_t stream, int ctas, uint32_t launch_flags) {
             kern::PushState st{reinterpret_cast<uint64_t*>(digests), reinterpret_cast<uint64_t*>(item_hash),
-                               reinterpret_cast<uint32_t*>(item_done),
-                               reinterpret_cast<unsigned long long*>(stats)};
+                               reinterpret_cast<unsigned long long*>(stats), reinterpret_cast<uint32_t*>(error)};
             cudaError_t e = kern::push(reinterpret_cast<const kern::PushItem*>(items), nitems, total_chunks, st,
-                                       reinterpret_cast<cudaStream_t>(stream), ctas);
+                                       reinterpret_cast<cudaStream_t>(stream), ctas, launch_flags);
             if (e != cudaSuccess) throw std::runtime_error(std::string("push: ") + cudaGetErrorString(e));
         },
         py::arg("items"), py::arg("nitems"), py::arg("total_chunks"), py::arg("digests"), py::arg("item_hash"),
-        py::arg("item_done"), py::arg("stats"), py::arg("stream"), py::arg("ctas") = 0);
+        py::arg("stats"), py::arg("error"), py::arg("stream"), py::arg("ctas") = 0, py::arg("launch_flags") = 0);
+    m.def("push_smem_bytes", &kern::push_smem_bytes);
+    m.def(
+        "k_hash_stream",
+        [](uint64_t src, uint64_t n, uint64_t digests, uint64_t error, uint64_t stream, int ctas) {
+            cudaError_t e = kern::hash_stream(reinterpret_cast<const void*>(src), n, reinterpret_cast<uint64_t*>(digests),
+                                              reinterpret_cast<uint32_t*>(error), reinterpret_cast<cudaStream_t>(stream),
+                                              ctas);
+            if (e != cudaSuccess) throw std::runtime_error(std::string("hash_stream: ") + cudaGetErrorString(e));
+        },
+        py::arg("src"), py::arg("nbytes"), py::arg("digests"), py::arg("error"), py::arg("stream"), py::arg("ctas") = 0);
 }

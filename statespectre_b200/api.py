@@ -412,6 +412,10 @@ class Off:
     def device(self) -> torch.device:
         return self._device
 
+    @property
+    def rank(self) -> int:
+        return self._rank
+
     def _next_tensor_id(self) -> int:
         # rank in the top 24 bits, a per-process counter in the low 40 (bit 63 stays clear)
         return ((self._rank & 0x7FFFFF) << 40) | (next(self._ids) & 0xFFFFFFFFFF)

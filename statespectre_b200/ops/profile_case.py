@@ -4,9 +4,11 @@
 
 Kernels: evict (K1, device -> pinned + ssh128), restore (K2, pinned ->
 device), restore_fp8 (K2 with the bf16 -> fp8 1x128 cast), hash (device
-ssh128), verify (K3 local vs second buffer). The case is larger than the
-126 MB L2 so DRAM counters are meaningful; it holds about 2x --mb of device
-memory and --mb of pinned host memory.
+ssh128), hash_stream (ssh128 through the K4 bulk-copy pipeline), verify (K3
+local vs second buffer), push / push_fp8 (K4 into a second buffer, raw or
+quantized; --peer 1 puts that buffer on cuda:1 so the stores cross NVLink).
+The case is larger than the 126 MB L2 so DRAM counters are meaningful; it
+holds about 2x --mb of device memory and --mb of pinned host memory.
 """
 
 from __future__ import annotations
@@ -20,10 +22,16 @@ from .._native import native
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", required=True, choices=["evict", "restore", "restore_fp8", "hash", "verify"])
+    ap.add_argument("--kernel", required=True, choices=["evict", "restore", "restore_fp8", "hash", "hash_stream",
+                                                          "verify", "push", "push_fp8"])
     ap.add_argument("--mb", type=int, default=512)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--ctas", type=int, default=0)
+    ap.add_argument("--peer", type=int, default=-1, help="device of the push destination (default: same GPU)")
+    ap.add_argument("--items", type=int, default=64, help="push: split the buffer into this many tensors")
+    ap.add_argument("--delta", type=int, default=0,
+                    help="push: 1 = delta mode with the destination table cleared before each launch "
+                         "(every chunk stored after its digest), 2 = delta mode with nothing changed")
     a = ap.parse_args()
     C = native()
     n = a.mb << 20
@@ -36,6 +44,20 @@ def main():
     mism = torch.zeros(1, dtype=torch.int32, device=dev)
     scales = torch.empty(n // 256, dtype=torch.float32, device=dev)
     C.k_evict_hash(x.data_ptr(), host.data_ptr(), n, dig.data_ptr(), s, a.ctas)  # fill the host copy
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    pusher = None
+    if a.kernel.startswith("push"):
+        from ..parallel.weight_sync import WeightLayout, WeightPusher
+        params = {f"x{i}": v for i, v in enumerate(x.view(a.items, -1))}
+        layout = WeightLayout.from_params(params, "fp8" if a.kernel == "push_fp8" else "bf16")
+        if a.peer >= 0:
+            C.enable_peer(a.peer)
+            dst = torch.empty(layout.total_bytes, dtype=torch.uint8, device=torch.device("cuda", a.peer))
+        else:
+            dst = torch.empty(layout.total_bytes, dtype=torch.uint8, device=dev)
+        pusher = WeightPusher(params, layout, dst.data_ptr(), dev, delta=a.delta > 0, ctas=a.ctas)
+        if a.delta == 2:
+            pusher.push()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
@@ -48,11 +70,26 @@ def main():
             C.k_restore_cast(host.data_ptr(), out.data_ptr(), n, 1, scales.data_ptr(), 0, 0, s, a.ctas)
         elif a.kernel == "hash":
             C.k_hash_device(x.data_ptr(), n, dig.data_ptr(), s, a.ctas)
+        elif a.kernel == "hash_stream":
+            C.k_hash_stream(x.data_ptr(), n, dig.data_ptr(), err.data_ptr(), s, a.ctas)
+        elif pusher is not None:
+            if a.delta == 1:
+                pusher.invalidate()
+            pusher.push()
         else:
             C.k_verify_peer(x.data_ptr(), out.data_ptr(), n, dig.data_ptr(), mism.data_ptr(), s, a.ctas)
     ev1.record()
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / a.iters
+    if int(err.item()) != 0 or (pusher is not None and pusher.result()["error"]):
+        code = int(err.item()) if pusher is None else pusher.result()["error"]
+        raise SystemExit(f"{a.kernel}: device status {code}")
+    if a.kernel == "hash_stream":  # the digests must equal the one-pass hash kernel's
+        ref = torch.zeros_like(dig)
+        C.k_hash_device(x.data_ptr(), n, ref.data_ptr(), s, 0)
+        torch.cuda.synchronize()
+        if not torch.equal(ref, dig):
+            raise SystemExit("hash_stream: digests differ from hash_device")
     print(f"{a.kernel}: {n / (ms / 1e3) / 1e9:.2f} GB/s ({ms:.3f} ms per launch, {n} bytes)")
 
 

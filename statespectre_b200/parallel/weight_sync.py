@@ -1,0 +1,324 @@
+"""In-box RL weight sync: trainer GPUs push sealed versions into rollout GPUs.
+
+StateSpectre syncs a rollout engine by sealing a version in offloadd (every
+object copied device -> pinned host first), after which the rollout pulls each
+changed object over TCP and copies it host -> device (reference:
+python_api/state_spectre/_rollout.py:101-175, src/daemon/canonical_rollout.cpp:240-411).
+On one B200 node the rollout GPUs are NVLink peers of the trainer GPUs, so the
+bytes take one hop instead:
+
+* the rollout allocates ONE receive buffer for all its parameters, laid out by
+  :class:`WeightLayout` (bf16 as trained, or fp8 e4m3 + fp32 1x128 block
+  scales for 2-D weights), and publishes it under a key through the daemon's
+  peer-buffer broker (:mod:`.fabric`);
+* the trainer maps it and runs the K4 push kernel: every parameter is read
+  from HBM once, hashed per 64 KiB chunk (ssh128), and only chunks whose digest
+  differs from what the rollout already holds cross NVLink, quantized on the
+  fly in fp8 mode; the same pass yields every parameter's 128-bit content hash;
+* the version is then made durable in offloadd without re-copying unchanged
+  parameters: changed ones go through ``canonical_evict`` (K1, D2H + hash),
+  unchanged ones are carried forward (objects that share the previous
+  version's storage), then the version is sealed and promoted. Manifests are
+  the same as StateSpectre's, so cross-node rollouts pull as before.
+"""
+
+from __future__ import annotations
+
+import math
+import struct
+import time
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from .._native import native
+from . import fabric
+
+ALIGN = 256
+CHUNK = 64 * 1024
+_ITEM = struct.Struct("<QQQQQIIQQ")  # PushItem: src, dst, dst_scales, nbytes, chunk_begin, mode, flags, pad x2
+PUSH_RAW, PUSH_FP8, PUSH_HASH = 0, 1, 2
+PUSH_DELTA = 1
+
+
+def _align(n: int) -> int:
+    return (n + ALIGN - 1) // ALIGN * ALIGN
+
+
+@dataclass
+class LayoutEntry:
+    name: str
+    shape: Tuple[int, ...]
+    dtype: torch.dtype
+    nbytes: int          # source (trainer) bytes
+    quant: bool          # stored as fp8 e4m3 + scales on the rollout
+    dst_offset: int
+    dst_nbytes: int
+    scale_offset: int = 0
+    nscales: int = 0
+
+
+class WeightLayout:
+    """Deterministic placement of a parameter list in one rollout buffer.
+
+    Trainer and rollout build it from the same (name, shape, dtype) list, so
+    no offsets travel; ``fingerprint`` lets both sides check they agree."""
+
+    def __init__(self, specs: Sequence[Tuple[str, Sequence[int], torch.dtype]], mode: str = "bf16"):
+        if mode not in ("bf16", "fp8"):
+            raise ValueError("mode must be 'bf16' or 'fp8'")
+        self.mode = mode
+        self.entries: List[LayoutEntry] = []
+        off = 0
+        for name, shape, dtype in specs:
+            shape = tuple(int(s) for s in shape)
+            nel = math.prod(shape)
+            esz = torch.empty((), dtype=dtype).element_size()
+            nbytes = nel * esz
+            if nbytes % 16:
+                raise ValueError(f"{name}: {nbytes} bytes is not a multiple of 16")
+            quant = mode == "fp8" and dtype == torch.bfloat16 and len(shape) >= 2 and nel % 128 == 0
+            e = LayoutEntry(name, shape, dtype, nbytes, quant, off, nel if quant else nbytes)
+            off = _align(off + e.dst_nbytes)
+            if quant:
+                e.scale_offset, e.nscales = off, nel // 128
+                off = _align(off + 4 * e.nscales)
+            self.entries.append(e)
+        self.total_bytes = max(off, ALIGN)
+        self.by_name = {e.name: e for e in self.entries}
+        h = 1469598103934665603
+        for e in self.entries:
+            for b in f"{e.name}|{e.shape}|{e.dtype}|{int(e.quant)};".encode():
+                h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+        self.fingerprint = h
+
+    @classmethod
+    def from_params(cls, params: Dict[str, torch.Tensor], mode: str = "bf16") -> "WeightLayout":
+        return cls([(n, tuple(t.shape), t.dtype) for n, t in params.items()], mode)
+
+    @property
+    def total_chunks(self) -> int:
+        return sum((e.nbytes + CHUNK - 1) // CHUNK for e in self.entries)
+
+
+class RolloutWeights:
+    """Rollout-side receive buffer holding every parameter of a layout."""
+
+    def __init__(self, layout: WeightLayout, device=None):
+        self.layout = layout
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.buf = torch.zeros(layout.total_bytes, dtype=torch.uint8, device=self.device)
+        self.key: Optional[str] = None
+
+    def publish(self, off, key: str) -> dict:
+        """Make the buffer reachable by trainer ranks as ``key``."""
+        self.key = key
+        return fabric.publish(off, key, self.buf, kind=fabric.KIND_WEIGHTS)
+
+    def get(self, name: str):
+        """bf16 view of a parameter, or (fp8 e4m3 view, fp32 scales) when quantized."""
+        e = self.layout.by_name[name]
+        raw = self.buf[e.dst_offset:e.dst_offset + e.dst_nbytes]
+        if not e.quant:
+            return raw.view(e.dtype).view(e.shape)
+        q = raw.view(torch.float8_e4m3fn).view(e.shape)
+        sc = self.buf[e.scale_offset:e.scale_offset + 4 * e.nscales].view(torch.float32)
+        return q, sc
+
+    def dequantized(self, name: str) -> torch.Tensor:
+        """A parameter as bf16 (fp8 entries rescaled block by block)."""
+        v = self.get(name)
+        if not isinstance(v, tuple):
+            return v
+        q, sc = v
+        return (q.float().view(-1, 128) * sc.view(-1, 1)).view(q.shape).to(torch.bfloat16)
+
+    def content_hashes(self, names: Optional[Sequence[str]] = None, stream=None) -> Dict[str, Tuple[int, int]]:
+        """ssh128 of the received bytes of bf16 entries (equal to the trainer's
+        manifest content hash when the push was byte-exact)."""
+        C = native()
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        out = {}
+        for e in self.layout.entries:
+            if e.quant or (names is not None and e.name not in names):
+                continue
+            dig = torch.empty((e.nbytes + CHUNK - 1) // CHUNK, dtype=torch.int64, device=self.device)
+            err = torch.zeros(1, dtype=torch.int32, device=self.device)
+            C.k_hash_stream(self.buf.data_ptr() + e.dst_offset, e.nbytes, dig.data_ptr(), err.data_ptr(), s, 0)
+            h = torch.empty(2, dtype=torch.int64, device=self.device)
+            C.k_fold_digests(dig.data_ptr(), dig.numel(), e.nbytes, h.data_ptr(), s)
+            out[e.name] = h
+        torch.cuda.current_stream(self.device).synchronize() if stream is None else stream.synchronize()
+        return {n: (int(h[0]) & (2**64 - 1), int(h[1]) & (2**64 - 1)) for n, h in out.items()}
+
+
+class WeightPusher:
+    """Trainer-side K4 launcher for one destination buffer.
+
+    ``digests`` records, per 64 KiB chunk, the digest of what the destination
+    holds, so each push (``delta=True``) only moves chunks that changed since
+    the previous push to the same destination. A 64-bit chunk digest decides
+    the skip; ``invalidate()`` forces the next push to send everything."""
+
+    def __init__(self, params: Dict[str, torch.Tensor], layout: WeightLayout, dst_ptr: int, device=None,
+                 delta: bool = True, ctas: int = 0):
+        self.params = params
+        self.layout = layout
+        self.dst_ptr = int(dst_ptr)
+        self.delta = delta
+        self.ctas = ctas
+        first = next(iter(params.values()))
+        self.device = torch.device(device) if device is not None else first.device
+        n = len(layout.entries)
+        if [e.name for e in layout.entries] != list(params):
+            raise ValueError("params and layout disagree on names / order")
+        if self.dst_ptr % 16:
+            raise ValueError("destination buffer must be 16-byte aligned")
+        self.total_chunks = layout.total_chunks
+        self.digests = torch.zeros(max(1, self.total_chunks), dtype=torch.int64, device=self.device)
+        self.item_hash = torch.zeros(2 * n, dtype=torch.int64, device=self.device)
+        self.stats = torch.zeros(2, dtype=torch.int64, device=self.device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._ptrs: List[int] = []
+        self.items = None
+        self._build_items()
+
+    def _build_items(self) -> None:
+        buf = bytearray()
+        chunk = 0
+        ptrs = []
+        for e in self.layout.entries:
+            t = self.params[e.name]
+            if not t.is_contiguous() or t.device != self.device:
+                raise ValueError(f"{e.name}: push sources must be contiguous tensors on {self.device}")
+            if t.numel() * t.element_size() != e.nbytes:
+                raise ValueError(f"{e.name}: size differs from the layout")
+            p = t.data_ptr()
+            if p % 16:
+                raise ValueError(f"{e.name}: source must be 16-byte aligned")
+            ptrs.append(p)
+            mode = PUSH_FP8 if e.quant else PUSH_RAW
+            scales = self.dst_ptr + e.scale_offset if e.quant else 0
+            buf += _ITEM.pack(p, self.dst_ptr + e.dst_offset, scales, e.nbytes, chunk, mode,
+                              PUSH_DELTA if self.delta else 0, 0, 0)
+            chunk += (e.nbytes + CHUNK - 1) // CHUNK
+        self._ptrs = ptrs
+        host = torch.frombuffer(buf, dtype=torch.uint8) if buf else torch.zeros(64, dtype=torch.uint8)
+        self.items = host.to(self.device)
+
+    def refresh(self) -> None:
+        """Rebuild the work list if any parameter was reallocated."""
+        if [self.params[e.name].data_ptr() for e in self.layout.entries] != self._ptrs:
+            self._build_items()
+
+    def invalidate(self) -> None:
+        self.digests.zero_()
+
+    def push(self, stream=None) -> None:
+        """Enqueue the push on ``stream`` (default: current stream)."""
+        s = stream or torch.cuda.current_stream(self.device)
+        native().k_push(self.items.data_ptr(), len(self.layout.entries), self.total_chunks, self.digests.data_ptr(),
+                        self.item_hash.data_ptr(), self.stats.data_ptr(), self.err.data_ptr(), s.cuda_stream,
+                        self.ctas, PUSH_DELTA if self.delta else 0)
+
+    def result(self) -> dict:
+        """Totals since construction (synchronizes the device)."""
+        st = self.stats.tolist()
+        return {"chunks_stored": st[0], "bytes_stored": st[1], "error": int(self.err.item())}
+
+    def hashes(self) -> Dict[str, Tuple[int, int]]:
+        h = self.item_hash.view(-1, 2).tolist()
+        m = 2**64 - 1
+        return {e.name: (h[i][0] & m, h[i][1] & m) for i, e in enumerate(self.layout.entries)}
+
+
+class TrainerWeightSync:
+    """Trainer side of in-box weight sync for one TP/PP shard.
+
+    ``publish_version(v)`` pushes the changed chunks of ``params`` into every
+    rollout buffer in ``rollout_keys`` (K4, one launch per destination), then,
+    with ``persist=True``, records version ``v`` in offloadd: changed
+    parameters are copied (K1) as new canonical objects, unchanged ones are
+    carried forward from ``v - 1``, and the version is sealed and promoted.
+    """
+
+    def __init__(self, off, params: Dict[str, torch.Tensor], rollout_keys: Sequence[str], mode: str = "bf16",
+                 model_role="policy_rollout", persist: bool = True, tp_rank: int = 0, pp_rank: int = 0,
+                 lookup_wait_ms: int = 60000, ctas: int = 0):
+        from ..api import ModelRole
+        self.off = off
+        self.params = dict(params)
+        self.layout = WeightLayout.from_params(self.params, mode)
+        self.role = ModelRole.parse(model_role)
+        self.persist = persist
+        self.tp_rank, self.pp_rank = tp_rank, pp_rank
+        first = next(iter(self.params.values()))
+        self.device = first.device
+        self.peers = [fabric.lookup(off, k, lookup_wait_ms) for k in rollout_keys]
+        for p in self.peers:
+            if p.nbytes < self.layout.total_bytes:
+                raise ValueError(f"rollout buffer {p.key!r} holds {p.nbytes} bytes, layout needs "
+                                 f"{self.layout.total_bytes}")
+        self.pushers = [WeightPusher(self.params, self.layout, p.ptr, self.device, ctas=ctas) for p in self.peers]
+        self.stream = torch.cuda.Stream(self.device)
+        self.last_hash: Dict[str, Tuple[int, int]] = {}
+        self.last_version: Optional[int] = None
+        self._pids: Dict[str, int] = {}
+
+    def _key(self, name: str, version: int):
+        k = self.off.canonical_key(model_role=self.role, model_version=version, param_name=name,
+                                   tensor=self.params[name], tp_rank=self.tp_rank, pp_rank=self.pp_rank)
+        self._pids[name] = k.param_id
+        return k
+
+    def push(self) -> Tuple[torch.cuda.Event, torch.cuda.Event]:
+        """Enqueue the pushes after the work already on the current stream."""
+        cur = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(cur)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        for p in self.pushers:
+            p.refresh()
+            p.push(self.stream)
+        e1.record(self.stream)
+        return e0, e1
+
+    def publish_version(self, version: int) -> dict:
+        t0 = time.perf_counter()
+        e0, e1 = self.push()
+        e1.synchronize()
+        push_ms = e0.elapsed_time(e1)
+        res = self.pushers[0].result() if self.pushers else {"error": 0}
+        if res["error"]:
+            raise RuntimeError(f"weight push failed with device status {res['error']}")
+        hashes = self.pushers[0].hashes() if self.pushers else {}
+        changed = [n for n in self.params if self.last_hash.get(n) != hashes.get(n)]
+        t_push = time.perf_counter()
+        out = {"version": version, "changed": len(changed), "push_ms": push_ms,
+               "push_wall_ms": (t_push - t0) * 1e3}
+        if self.persist:
+            handles = []
+            carry = self.last_version is not None
+            for n in (changed if carry else self.params):
+                handles.append(self.off.canonical_evict(self.params[n], self._key(n, version), destructive=False,
+                                                        wait=False, stream=self.stream))
+            if carry:
+                unchanged = [self._pids[n] if n in self._pids else self._key(n, version).param_id
+                             for n in self.params if n not in changed]
+                if unchanged:
+                    self.off.carry_forward_version(self.role, self.last_version, version, unchanged)
+            self.stream.synchronize()
+            self.off._agent.synchronize()
+            self.off.promote_rollout_version(version) if self.role == 2 else \
+                self.off.seal_model_version(self.role, version)
+            out["seal_wall_ms"] = (time.perf_counter() - t_push) * 1e3
+        self.last_hash = hashes
+        self.last_version = version
+        return out
+
+    def close(self) -> None:
+        for p in self.peers:
+            p.close()
+        self.peers = []

@@ -1,0 +1,112 @@
+"""Two processes on two GPUs: peer-buffer broker, K4 push over NVLink, K3
+P2P byte verification, and a sealed version the rollout can check.
+
+The trainer (this process, cuda:0) hosts the daemon; the rollout is a spawned
+child on cuda:1 that publishes its receive buffer and checks what arrives.
+Every wait between the processes has a timeout.
+"""
+
+import multiprocessing as mp
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+TIMEOUT = 120
+
+
+def _specs():
+    return [("w0", (1024, 1024), "bfloat16"), ("w1", (4096, 256), "bfloat16"), ("b", (256,), "bfloat16"),
+            ("w2", (3000, 512), "bfloat16")]
+
+
+def _rollout(sock, mode, q_in, q_out):
+    import torch
+
+    from statespectre_b200 import offload_context
+    from statespectre_b200.parallel.weight_sync import RolloutWeights, WeightLayout
+
+    torch.cuda.set_device(1)
+    try:
+        with offload_context(daemon_addr=sock, device="cuda:1", rank=1, job_name="fabric2") as off:
+            layout = WeightLayout([(n, s, getattr(torch, d)) for n, s, d in _specs()], mode)
+            rw = RolloutWeights(layout, "cuda:1")
+            rw.publish(off, f"rollout/{mode}")
+            q_out.put(("published", layout.fingerprint))
+            while True:
+                msg = q_in.get(timeout=TIMEOUT)
+                if msg[0] == "done":
+                    break
+                _, version, hashes, host = msg
+                torch.cuda.synchronize()
+                ok = True
+                if mode == "bf16":
+                    ok = rw.content_hashes() == hashes
+                    for n, t in host.items():
+                        ok &= torch.equal(rw.get(n).cpu(), t)
+                else:
+                    for n, t in host.items():
+                        ok &= torch.allclose(rw.dequantized(n).float().cpu(), t.float(), rtol=0.07, atol=1e-6)
+                q_out.put(("checked", version, bool(ok)))
+    except Exception as e:  # noqa: BLE001
+        q_out.put(("error", repr(e)))
+
+
+@pytest.fixture
+def two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+
+
+@pytest.mark.parametrize("mode", ["bf16", "fp8"])
+def test_push_across_gpus_and_verify_peer(two_gpus, sock_path, mode):
+    from statespectre_b200 import in_process_daemon, offload_context
+    from statespectre_b200._native import native
+    from statespectre_b200.parallel.weight_sync import TrainerWeightSync
+
+    d = in_process_daemon(socket=sock_path, arena_mb=1024, drain_on_complete=False)
+    ctx = mp.get_context("spawn")
+    q_in, q_out = ctx.Queue(), ctx.Queue()
+    child = ctx.Process(target=_rollout, args=(sock_path, mode, q_in, q_out))
+    child.start()
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", rank=0, job_name="fabric2") as off:
+            torch.manual_seed(0)
+            params = {n: (torch.randn(s, device="cuda:0") * 0.02).to(getattr(torch, dt)) for n, s, dt in _specs()}
+            tag, fp = q_out.get(timeout=TIMEOUT)
+            assert tag == "published"
+            tr = TrainerWeightSync(off, params, [f"rollout/{mode}"], mode=mode)
+            assert tr.layout.fingerprint == fp
+            for version in (1, 2):
+                if version == 2:
+                    params["w1"].add_(0.5)
+                r = tr.publish_version(version)
+                assert r["changed"] == (len(params) if version == 1 else 1)
+                q_in.put(("check", version, tr.pushers[0].hashes(), {n: t.cpu() for n, t in params.items()}))
+                msg = q_out.get(timeout=TIMEOUT)
+                assert msg == ("checked", version, True), msg
+            if mode == "bf16":
+                # K3: compare the local parameter with the rollout's copy by P2P loads
+                C = native()
+                peer = tr.peers[0]
+                e = tr.layout.by_name["w2"]
+                n = e.nbytes
+                dig = torch.zeros((n + 65535) // 65536, dtype=torch.int64, device="cuda:0")
+                mism = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+                s = torch.cuda.current_stream().cuda_stream
+                C.k_verify_peer(params["w2"].data_ptr(), peer.ptr + e.dst_offset, n, dig.data_ptr(),
+                                mism.data_ptr(), s, 0)
+                torch.cuda.synchronize()
+                assert mism.item() == 0
+            man = off.get_manifest("policy_rollout", 2)
+            assert len(man["tensors"]) == len(params)
+            tr.close()
+        q_in.put(("done",))
+        child.join(TIMEOUT)
+        assert child.exitcode == 0
+    finally:
+        if child.is_alive():
+            child.kill()
+            child.join(10)
+        d.stop()
