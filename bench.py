@@ -57,6 +57,17 @@ def parse():
     p.add_argument("--hash", type=int, default=1)
     p.add_argument("--e2e-steps", type=int, default=0, help="default: same as --steps")
     p.add_argument("--out", default="")
+    # --workload weight_sync: in-box RL weight sync (trainer half -> rollout half of the GPUs)
+    p.add_argument("--workload", default="evict_restore", choices=["evict_restore", "weight_sync"])
+    p.add_argument("--model", default="qwen2.5-32b")
+    p.add_argument("--layers", type=int, default=0, help="weight_sync: layer count override (0 = the model's)")
+    p.add_argument("--push-mode", default="bf16", choices=["bf16", "fp8"])
+    p.add_argument("--persist", type=int, default=1, help="weight_sync: seal every version in offloadd")
+    p.add_argument("--verify", type=int, default=1, help="weight_sync: rollout re-hashes what it received")
+    p.add_argument("--change-fraction", type=float, default=0.1)
+    p.add_argument("--delta-std", type=float, default=1e-3)
+    p.add_argument("--hint", type=int, default=0,
+                   help="weight_sync: pass the changed-tensor list instead of hashing every tensor")
     return p.parse_args()
 
 
@@ -65,6 +76,18 @@ def main():
     if args.impl == "reference":
         line = {"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}
         print(json.dumps(line), flush=True)
+        return 0
+
+    if args.workload == "weight_sync":
+        from statespectre_b200.parallel.weight_sync_bench import run
+
+        out = run(args, METRIC)
+        if out is not None:
+            line = json.dumps(out)
+            print(line, flush=True)
+            if args.out:
+                with open(args.out, "w") as f:
+                    f.write(line + "\n")
         return 0
 
     import torch
@@ -174,9 +197,10 @@ def main():
     torch.cuda.synchronize(device)
     assert off.hash_tensor(x) == ref_hash, "round trip corrupted the tensor"
     launches0 = native().kernel_launch_count()
-    sampler = ClockSampler([local_rank]).start()
+    sampler = ClockSampler([local_rank]).start().wait_first()
     barrier()
     torch.cuda.synchronize(device)
+    sampler.mark_start()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(copy_stream)
@@ -184,6 +208,7 @@ def main():
         cycle(1000 + i, False)
     t_end.record(copy_stream)
     torch.cuda.synchronize(device)
+    sampler.mark_end()
     barrier()
     clocks = sampler.stop()
     launches = native().kernel_launch_count() - launches0

@@ -90,6 +90,9 @@ inline uint64_t digest_count(uint64_t nbytes) { return (nbytes + 65535) / 65536;
 // `dst` / `dst_scales` are typically peer-GPU pointers (CUDA IPC mappings).
 enum : uint32_t { kPushRaw = 0, kPushFp8 = 1, kPushHash = 2 };
 enum : uint32_t { kPushDelta = 1u << 0 };
+// `digest_base` is the index of the item's first chunk in the launch's digest
+// table (equal to chunk_begin for a full table; a subset launch keeps the
+// full table's indices so the record of what the destination holds stays put).
 struct PushItem {
     const void* src;
     void* dst;
@@ -98,7 +101,8 @@ struct PushItem {
     uint64_t chunk_begin;
     uint32_t mode;
     uint32_t flags;
-    uint64_t pad1, pad2;
+    uint64_t digest_base;
+    uint64_t reserved;
 };
 static_assert(sizeof(PushItem) == 64, "PushItem is a 64-byte record");
 
@@ -124,16 +128,13 @@ cudaError_t push(const PushItem* items_dev, int nitems, uint64_t total_chunks, P
                  int ctas, uint32_t launch_flags);
 
 // Chunk digests of a device buffer through the K4 pipeline (bulk copies into
-// shared memory, one CTA per SM). src 16-byte aligned, nbytes % 16 == 0.
+// shared memory, three CTAs per SM). src 16-byte aligned, nbytes % 16 == 0.
 cudaError_t hash_stream(const void* src_dev, uint64_t nbytes, uint64_t* digests, uint32_t* error, cudaStream_t s,
                         int ctas);
 
-// Dynamic shared memory of one K4 CTA (three 64 KiB stages + barriers).
+// Dynamic shared memory of one delta-mode K4 CTA (three 32 KiB half-chunk
+// stages + barriers).
 size_t push_smem_bytes();
-
-// K4. Launches one persistent grid over every chunk of every item.
-cudaError_t push(const PushItem* items_dev, int nitems, uint64_t total_chunks, PushState st, cudaStream_t s,
-                 int ctas);
 uint64_t push_launch_count();
 
 }  // namespace kern

@@ -8,18 +8,18 @@
 // pushes the changed tensors of a sealed version directly into the rollout's
 // weight buffers:
 //
-//   * one persistent launch (one CTA per SM) walks a work list of (src, dst)
-//     items 64 KiB chunk by chunk, so a version with hundreds of changed
-//     tensors is one launch;
-//   * a producer warp streams chunks HBM -> shared memory with 1-D bulk
-//     copies (cp.async.bulk, completion on an mbarrier) three stages ahead,
-//     so loads stay in flight while the consumer warps hash;
-//   * the consumers compute the chunk's ssh128 digest from shared memory,
-//     compare it with what the destination already holds (delta mode) and
-//     store the chunk to the peer from registers: raw bytes, or bf16 quantized
-//     to fp8 e4m3 with one fp32 scale per 128 elements;
-//   * the CTA that finishes an item's last chunk folds the item's 128-bit
-//     object hash (manifest content hash) from the chunk digests.
+//   * one persistent launch (two or three CTAs per SM) walks a work list of
+//     (src, dst) items 64 KiB chunk by chunk, so a version with hundreds of
+//     changed tensors is one launch;
+//   * in each CTA a producer warp streams 32 KiB half-chunks HBM -> shared
+//     memory with 1-D bulk copies (cp.async.bulk, completion on an mbarrier)
+//     ahead of the consumers, so loads stay in flight while they hash;
+//   * the 256 consumer threads compute the chunk's ssh128 digest from shared
+//     memory, compare it with what the destination already holds (delta mode)
+//     and store the chunk to the peer: raw bytes, or bf16 quantized to fp8
+//     e4m3 with one fp32 scale per 128 elements;
+//   * a second small launch folds every item's 128-bit object hash (manifest
+//     content hash) from the chunk digests.
 //
 // Peer memory is only ever the target of plain st.global from registers; the
 // bulk copies read this GPU's own memory and carry no multicast.
@@ -217,7 +217,7 @@ __device__ __forceinline__ uint64_t chunk_tree(uint64_t d, uint64_t* red, int g,
 __device__ __forceinline__ void fold_item_warp(const PushItem& it, int idx, const PushState& st) {
     const uint32_t lane = threadIdx.x & 31;
     const uint64_t n = ssh::num_chunks_dev(it.nbytes);
-    const uint64_t* d = st.digests + it.chunk_begin;
+    const uint64_t* d = st.digests + it.digest_base;
     uint64_t lo, hi;
     ssh::object_init(lo, hi);
     uint64_t cur = lane < n ? __ldcg(d + lane) : 0;
@@ -316,7 +316,8 @@ __global__ void __launch_bounds__(kThreads, (S == 2 ? 3 : 2))
         const bool store_now = !delta && it.mode != kPushHash;  // stores need no digest: issue from the same registers
         const bool hold = delta && it.mode != kPushHash;        // stages kept until the store decision
         // the destination's digest of this chunk, loaded now and used after the hash
-        const uint64_t old_dg = (delta && lt == 0) ? st.digests[c] : 0;
+        const uint64_t dgi = it.digest_base + (c - it.chunk_begin);
+        const uint64_t old_dg = (delta && lt == 0) ? st.digests[dgi] : 0;
         ssh::Lane L = ssh::lane_init(lt);
         for (uint32_t h = 0; h < 2; ++h) {
             const uint32_t q = 2 * i + h;
@@ -360,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, (S == 2 ? 3 : 2))
         if (lt == 0) {
             const uint64_t dg = ssh::chunk_finish(root, len);
             const bool same = delta && old_dg == dg;
-            st.digests[c] = dg;
+            st.digests[dgi] = dg;
             const bool stored = it.mode != kPushHash && !same;
             flags[0] = hold && stored;
             if (stored && st.stats) {

@@ -37,7 +37,7 @@ from . import fabric
 
 ALIGN = 256
 CHUNK = 64 * 1024
-_ITEM = struct.Struct("<QQQQQIIQQ")  # PushItem: src, dst, dst_scales, nbytes, chunk_begin, mode, flags, pad x2
+_ITEM = struct.Struct("<QQQQQIIQQ")  # PushItem: src, dst, dst_scales, nbytes, chunk_begin, mode, flags, digest_base, -
 PUSH_RAW, PUSH_FP8, PUSH_HASH = 0, 1, 2
 PUSH_DELTA = 1
 
@@ -136,21 +136,33 @@ class RolloutWeights:
 
     def content_hashes(self, names: Optional[Sequence[str]] = None, stream=None) -> Dict[str, Tuple[int, int]]:
         """ssh128 of the received bytes of bf16 entries (equal to the trainer's
-        manifest content hash when the push was byte-exact)."""
-        C = native()
-        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
-        out = {}
-        for e in self.layout.entries:
-            if e.quant or (names is not None and e.name not in names):
-                continue
-            dig = torch.empty((e.nbytes + CHUNK - 1) // CHUNK, dtype=torch.int64, device=self.device)
-            err = torch.zeros(1, dtype=torch.int32, device=self.device)
-            C.k_hash_stream(self.buf.data_ptr() + e.dst_offset, e.nbytes, dig.data_ptr(), err.data_ptr(), s, 0)
-            h = torch.empty(2, dtype=torch.int64, device=self.device)
-            C.k_fold_digests(dig.data_ptr(), dig.numel(), e.nbytes, h.data_ptr(), s)
-            out[e.name] = h
-        torch.cuda.current_stream(self.device).synchronize() if stream is None else stream.synchronize()
-        return {n: (int(h[0]) & (2**64 - 1), int(h[1]) & (2**64 - 1)) for n, h in out.items()}
+        manifest content hash when the push was byte-exact). One hash-only K4
+        launch over every selected entry plus the item-hash fold."""
+        ents = [e for e in self.layout.entries if not e.quant and (names is None or e.name in names)]
+        if not ents:
+            return {}
+        key = tuple(e.name for e in ents)
+        if getattr(self, "_hash_key", None) != key:
+            buf = bytearray()
+            chunk = 0
+            for e in ents:
+                buf += _ITEM.pack(self.buf.data_ptr() + e.dst_offset, 0, 0, e.nbytes, chunk, PUSH_HASH, 0, chunk, 0)
+                chunk += (e.nbytes + CHUNK - 1) // CHUNK
+            self._hash_items = torch.frombuffer(buf, dtype=torch.uint8).to(self.device)
+            self._hash_dig = torch.empty(chunk, dtype=torch.int64, device=self.device)
+            self._hash_out = torch.empty(2 * len(ents), dtype=torch.int64, device=self.device)
+            self._hash_err = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self._hash_chunks = chunk
+            self._hash_key = key
+        s = stream or torch.cuda.current_stream(self.device)
+        native().k_push(self._hash_items.data_ptr(), len(ents), self._hash_chunks, self._hash_dig.data_ptr(),
+                        self._hash_out.data_ptr(), 0, self._hash_err.data_ptr(), s.cuda_stream, 0, 0)
+        s.synchronize()
+        if int(self._hash_err.item()):
+            raise RuntimeError(f"hash pass failed with device status {int(self._hash_err.item())}")
+        h = self._hash_out.view(-1, 2).tolist()
+        m = 2**64 - 1
+        return {e.name: (h[i][0] & m, h[i][1] & m) for i, e in enumerate(ents)}
 
 
 class WeightPusher:
@@ -184,11 +196,13 @@ class WeightPusher:
         self.items = None
         self._build_items()
 
-    def _build_items(self) -> None:
+    def _table(self, entries) -> Tuple[torch.Tensor, int, List[int]]:
+        """Work table for `entries` (layout order): compact work-chunk
+        indices, digest-table indices of the full layout."""
         buf = bytearray()
-        chunk = 0
+        work = 0
         ptrs = []
-        for e in self.layout.entries:
+        for e in entries:
             t = self.params[e.name]
             if not t.is_contiguous() or t.device != self.device:
                 raise ValueError(f"{e.name}: push sources must be contiguous tensors on {self.device}")
@@ -200,12 +214,21 @@ class WeightPusher:
             ptrs.append(p)
             mode = PUSH_FP8 if e.quant else PUSH_RAW
             scales = self.dst_ptr + e.scale_offset if e.quant else 0
-            buf += _ITEM.pack(p, self.dst_ptr + e.dst_offset, scales, e.nbytes, chunk, mode,
-                              PUSH_DELTA if self.delta else 0, 0, 0)
-            chunk += (e.nbytes + CHUNK - 1) // CHUNK
-        self._ptrs = ptrs
+            buf += _ITEM.pack(p, self.dst_ptr + e.dst_offset, scales, e.nbytes, work, mode,
+                              PUSH_DELTA if self.delta else 0, self._digest_base[e.name], 0)
+            work += (e.nbytes + CHUNK - 1) // CHUNK
         host = torch.frombuffer(buf, dtype=torch.uint8) if buf else torch.zeros(64, dtype=torch.uint8)
-        self.items = host.to(self.device)
+        return host.to(self.device), work, ptrs
+
+    def _build_items(self) -> None:
+        self._digest_base = {}
+        chunk = 0
+        for e in self.layout.entries:
+            self._digest_base[e.name] = chunk
+            chunk += (e.nbytes + CHUNK - 1) // CHUNK
+        self.items, _, self._ptrs = self._table(self.layout.entries)
+        self._subsets: Dict[tuple, tuple] = {}
+        self._row = {e.name: i for i, e in enumerate(self.layout.entries)}
 
     def refresh(self) -> None:
         """Rebuild the work list if any parameter was reallocated."""
@@ -215,12 +238,38 @@ class WeightPusher:
     def invalidate(self) -> None:
         self.digests.zero_()
 
-    def push(self, stream=None) -> None:
-        """Enqueue the push on ``stream`` (default: current stream)."""
+    def push(self, stream=None, names: Optional[Sequence[str]] = None) -> None:
+        """Enqueue the push on ``stream`` (default: current stream).
+
+        ``names`` restricts the launch to those parameters (the caller knows
+        the others did not change); their hashes land in the rows of
+        ``item_hash`` that the full layout gives them."""
         s = stream or torch.cuda.current_stream(self.device)
-        native().k_push(self.items.data_ptr(), len(self.layout.entries), self.total_chunks, self.digests.data_ptr(),
-                        self.item_hash.data_ptr(), self.stats.data_ptr(), self.err.data_ptr(), s.cuda_stream,
-                        self.ctas, PUSH_DELTA if self.delta else 0)
+        C = native()
+        flags = PUSH_DELTA if self.delta else 0
+        if names is None:
+            C.k_push(self.items.data_ptr(), len(self.layout.entries), self.total_chunks, self.digests.data_ptr(),
+                     self.item_hash.data_ptr(), self.stats.data_ptr(), self.err.data_ptr(), s.cuda_stream,
+                     self.ctas, flags)
+            return
+        want = set(names)
+        ents = [e for e in self.layout.entries if e.name in want]
+        if not ents:
+            return
+        key = tuple(e.name for e in ents)
+        sub = self._subsets.get(key)
+        if sub is None or sub[3] != [self.params[n].data_ptr() for n in key]:
+            items, work, ptrs = self._table(ents)
+            rows = torch.tensor([self._row[n] for n in key], dtype=torch.int64, device=self.device)
+            out = torch.zeros(2 * len(ents), dtype=torch.int64, device=self.device)
+            if len(self._subsets) > 64:
+                self._subsets.clear()
+            sub = self._subsets[key] = (items, work, out, ptrs, rows)
+        items, work, out, _, rows = sub
+        C.k_push(items.data_ptr(), len(ents), work, self.digests.data_ptr(), out.data_ptr(), self.stats.data_ptr(),
+                 self.err.data_ptr(), s.cuda_stream, self.ctas, flags)
+        with torch.cuda.stream(s):
+            self.item_hash.view(-1, 2).index_copy_(0, rows, out.view(-1, 2))
 
     def result(self) -> dict:
         """Totals since construction (synchronizes the device)."""
@@ -272,7 +321,7 @@ class TrainerWeightSync:
         self._pids[name] = k.param_id
         return k
 
-    def push(self) -> Tuple[torch.cuda.Event, torch.cuda.Event]:
+    def push(self, names: Optional[Sequence[str]] = None) -> Tuple[torch.cuda.Event, torch.cuda.Event]:
         """Enqueue the pushes after the work already on the current stream."""
         cur = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(cur)
@@ -281,13 +330,21 @@ class TrainerWeightSync:
         e0.record(self.stream)
         for p in self.pushers:
             p.refresh()
-            p.push(self.stream)
+            p.push(self.stream, names)
         e1.record(self.stream)
         return e0, e1
 
-    def publish_version(self, version: int) -> dict:
+    def publish_version(self, version: int, changed: Optional[Sequence[str]] = None) -> dict:
+        """Push and (with ``persist``) seal version ``version``.
+
+        Without ``changed`` every parameter is hashed on the device and the
+        changed set is found by comparing content hashes with the previous
+        version (the manifest diff). With ``changed`` (names the caller
+        updated) only those parameters are hashed and pushed; the others keep
+        their previous hashes. The first version always covers everything."""
         t0 = time.perf_counter()
-        e0, e1 = self.push()
+        hint = None if (changed is None or self.last_version is None) else list(changed)
+        e0, e1 = self.push(hint)
         e1.synchronize()
         push_ms = e0.elapsed_time(e1)
         res = self.pushers[0].result() if self.pushers else {"error": 0}

@@ -11,6 +11,7 @@ import shutil
 import statistics
 import subprocess
 import threading
+import time
 from typing import List, Optional
 
 FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -20,12 +21,13 @@ REASON_COLS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_
 
 
 class ClockSampler:
-    def __init__(self, gpu_indices: Optional[List[int]] = None, period_ms: int = 200):
+    def __init__(self, gpu_indices: Optional[List[int]] = None, period_ms: int = 100):
         self.gpus = gpu_indices
         self.period_ms = period_ms
-        self.rows: List[list] = []
+        self.rows: List[list] = []  # [monotonic time, *csv fields]
         self._proc = None
         self._thread = None
+        self._window = None
 
     def start(self) -> "ClockSampler":
         exe = shutil.which("nvidia-smi")
@@ -40,11 +42,25 @@ class ClockSampler:
             for line in self._proc.stdout:
                 parts = [p.strip() for p in line.split(",")]
                 if len(parts) >= 9:
-                    self.rows.append(parts)
+                    self.rows.append([time.monotonic()] + parts)
 
         self._thread = threading.Thread(target=reader, daemon=True)
         self._thread.start()
         return self
+
+    def wait_first(self, timeout_s: float = 5.0) -> "ClockSampler":
+        """Block until nvidia-smi delivered its first sample (it starts slowly)."""
+        end = time.monotonic() + timeout_s
+        while self._proc is not None and not self.rows and time.monotonic() < end:
+            time.sleep(0.02)
+        return self
+
+    def mark_start(self) -> None:
+        self._window = [time.monotonic(), None]
+
+    def mark_end(self) -> None:
+        if self._window:
+            self._window[1] = time.monotonic()
 
     def stop(self) -> dict:
         if self._proc is not None:
@@ -58,10 +74,19 @@ class ClockSampler:
         return self.summary()
 
     def summary(self) -> dict:
-        if not self.rows:
+        rows = self.rows
+        if self._window and self._window[1] is not None and rows:
+            # samples inside the marked window, plus the nearest one on each side
+            t0, t1 = self._window
+            inside = [i for i, r in enumerate(rows) if t0 <= r[0] <= t1]
+            before = [i for i, r in enumerate(rows) if r[0] < t0][-1:]
+            after = [i for i, r in enumerate(rows) if r[0] > t1][:1]
+            rows = [rows[i] for i in before + inside + after]
+        rows = [r[1:] for r in rows]
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         sm, mx, reasons = [], [], set()
-        for r in self.rows:
+        for r in rows:
             try:
                 sm.append(float(r[1]))
                 mx.append(float(r[2]))

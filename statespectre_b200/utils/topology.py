@@ -30,20 +30,27 @@ def gpu_numa_nodes(num_gpus: int) -> List[int]:
     return out
 
 
-def daemon_yaml(socket_path: str, gpu_nodes: List[int], window_gb_per_gpu: int, slot_mb: int = 64,
+def daemon_yaml(socket_path: str, gpu_nodes: List[int], window_gb_per_gpu, slot_mb: int = 64,
                 overflow_gb: int = 1, drain_on_complete: bool = False, extra: str = "") -> str:
-    """A daemon config with one arena per NUMA node holding a window per GPU."""
+    """A daemon config with one arena per NUMA node holding a window per GPU.
+
+    ``window_gb_per_gpu`` is one size for every GPU or a list (one per GPU;
+    GPUs with 0 get no window and allocate from the overflow pool)."""
+    sizes = list(window_gb_per_gpu) if isinstance(window_gb_per_gpu, (list, tuple)) else \
+        [window_gb_per_gpu] * len(gpu_nodes)
+    sizes += [0] * (len(gpu_nodes) - len(sizes))
     by_node: Dict[int, List[int]] = {}
     for g, n in enumerate(gpu_nodes):
-        by_node.setdefault(n, []).append(g)
+        if sizes[g] > 0:
+            by_node.setdefault(n, []).append(g)
     lines = ["daemon:", f"  socket_path: {socket_path}", "  heartbeat_timeout_ms: 30000",
              "arenas:", f"  allocation_granularity_mb: {slot_mb}", "  per_numa:"]
     for node, gpus in sorted(by_node.items()):
-        size = window_gb_per_gpu * len(gpus) + overflow_gb
+        size = sum(sizes[g] for g in gpus) + overflow_gb
         lines += [f"    - numa_node: {node}", f"      size_gb: {size}", f"      overflow_gb: {overflow_gb}",
                   "      gpu_windows:"]
         for g in gpus:
-            lines += [f"        - gpu: {g}", f"          size_gb: {window_gb_per_gpu}"]
+            lines += [f"        - gpu: {g}", f"          size_gb: {sizes[g]}"]
     lines += ["drain_policy:", "  target_tier: pageable", f"  drain_on_d2h_complete: {str(drain_on_complete).lower()}",
               "nvme:", "  enabled: false"]
     return "\n".join(lines) + "\n" + extra

@@ -144,3 +144,24 @@ def test_trainer_weight_sync_seals_versions_with_carry_forward(sock_path):
             tr.close()
     finally:
         d.stop()
+
+
+def test_subset_push_updates_hash_rows_and_digest_table():
+    params = _params(4)
+    layout = WeightLayout.from_params(params, "bf16")
+    rw = RolloutWeights(layout)
+    p = WeightPusher(params, layout, rw.buf.data_ptr())
+    p.push()
+    full = p.result()["bytes_stored"]
+    params["q"].mul_(2)
+    params["norm"].add_(1)
+    p.push(names=["q", "norm"])
+    sub = p.result()["bytes_stored"] - full
+    assert sub == params["q"].numel() * 2 + params["norm"].numel() * 2
+    torch.cuda.synchronize()
+    for n, t in params.items():
+        assert torch.equal(rw.get(n), t), n
+        assert p.hashes()[n] == _host_hash(t), n
+    # the digest table now describes the destination: a full delta push moves nothing
+    p.push()
+    assert p.result()["bytes_stored"] == full + sub
