@@ -46,6 +46,31 @@ int64_t find_free_run(const std::vector<uint64_t>& bm, uint32_t nbits, uint32_t 
     }
     return -1;
 }
+
+// Highest run of `count` free bits (scanning down from the top of the window).
+int64_t find_free_run_top(const std::vector<uint64_t>& bm, uint32_t nbits, uint32_t count) {
+    uint64_t run = 0;
+    for (int64_t i = int64_t(nbits) - 1; i >= 0; --i) {
+        const uint64_t x = bm[size_t(i) / 64];
+        if ((i % 64) == 63 && x == ~0ull && i - 63 >= 0) {  // a whole free word
+            run += 64;
+            i -= 63;
+            if (run >= count) return i + int64_t(run - count);
+            continue;
+        }
+        if ((i % 64) == 63 && x == 0) {  // a whole used word
+            run = 0;
+            i -= 63;
+            continue;
+        }
+        if ((x >> (i % 64)) & 1ull) {
+            if (++run >= count) return i;
+        } else {
+            run = 0;
+        }
+    }
+    return -1;
+}
 }  // namespace
 
 void Daemon::set_state(uint32_t s, ofld_slot_state_t st) {
@@ -68,9 +93,15 @@ Daemon::Window* Daemon::window_of_slot(uint32_t s) {
     return s < slot_window_.size() && slot_window_[s] != 0xFFFFFFFFu ? &windows_[slot_window_[s]] : nullptr;
 }
 
+// Size-segregated placement: runs of kLargeRun slots or more are placed from
+// the top of the window, smaller ones first-fit from the bottom, so freeing
+// many small objects (norms, biases, KV blocks) does not splinter the space
+// that multi-GB tensors need as one contiguous run.
 bool Daemon::alloc_in_window(Window& w, uint32_t count, uint32_t* base) {
+    constexpr uint32_t kLargeRun = 8;
     if (count > w.nslots) return false;
-    int64_t rel = find_free_run(w.free_bits, w.nslots, count);
+    int64_t rel = count >= kLargeRun ? find_free_run_top(w.free_bits, w.nslots, count)
+                                     : find_free_run(w.free_bits, w.nslots, count);
     if (rel < 0) return false;
     for (uint32_t k = 0; k < count; ++k) {
         uint64_t i = uint64_t(rel) + k;

@@ -58,9 +58,11 @@ def run(args, metric: str) -> dict:
     mode = args.push_mode
 
     # persistence needs pinned room for one full shard per trainer plus the
-    # changed tensors of the retained versions
+    # changed tensors of the retained versions: until a seal drops the oldest
+    # one, two older diffs and the version being written are live (x6 margin
+    # for the contiguous runs that multi-GB tensors need)
     n_local = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
-    per_trainer_gb = int(shard_bytes * 1.35 / GiB) + 4
+    per_trainer_gb = int(shard_bytes * (1.0 + 6 * args.change_fraction) / GiB) + 4
     need = per_trainer_gb * GiB * min(tp, n_local)
     persist = bool(args.persist)
     avail = host_mem_available_bytes()
