@@ -372,6 +372,10 @@ class Daemon {
     std::deque<ReadbackJob> readback_q_;
     std::mutex q_mu_;
     std::condition_variable drain_cv_, readback_cv_;
+    // Queued drains not yet finished (mu_), and the signal a blocked
+    // reservation waits on for one of them to free its pinned run.
+    uint32_t drains_pending_ = 0;
+    std::condition_variable_any drained_cv_;
 
     std::vector<std::thread> workers_;
     struct Conn {

@@ -9,6 +9,7 @@
 // (tensor, version) or an invalid state transition, and each rejection is
 // counted.
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 
 #include "daemon.h"
@@ -47,29 +48,40 @@ int64_t find_free_run(const std::vector<uint64_t>& bm, uint32_t nbits, uint32_t 
     return -1;
 }
 
-// Highest run of `count` free bits (scanning down from the top of the window).
-int64_t find_free_run_top(const std::vector<uint64_t>& bm, uint32_t nbits, uint32_t count) {
-    uint64_t run = 0;
-    for (int64_t i = int64_t(nbits) - 1; i >= 0; --i) {
-        const uint64_t x = bm[size_t(i) / 64];
-        if ((i % 64) == 63 && x == ~0ull && i - 63 >= 0) {  // a whole free word
+// Best fit: the smallest free run that holds `count` bits (ties: the higher
+// one), placed at the top of that run.
+int64_t find_free_run_best(const std::vector<uint64_t>& bm, uint32_t nbits, uint32_t count) {
+    int64_t best = -1;
+    uint64_t best_len = ~0ull;
+    uint64_t run = 0, start = 0;
+    auto close = [&](uint64_t end) {  // run occupies [start, end)
+        if (run >= count && run <= best_len) {
+            best_len = run;
+            best = int64_t(end - count);
+        }
+        run = 0;
+    };
+    for (uint32_t w = 0; w < bm.size(); ++w) {
+        const uint64_t x = bm[w];
+        const uint64_t base = uint64_t(w) * 64;
+        if (x == ~0ull && base + 64 <= nbits) {
+            if (run == 0) start = base;
             run += 64;
-            i -= 63;
-            if (run >= count) return i + int64_t(run - count);
             continue;
         }
-        if ((i % 64) == 63 && x == 0) {  // a whole used word
-            run = 0;
-            i -= 63;
-            continue;
-        }
-        if ((x >> (i % 64)) & 1ull) {
-            if (++run >= count) return i;
-        } else {
-            run = 0;
+        for (uint32_t b = 0; b < 64; ++b) {
+            const uint64_t i = base + b;
+            if (i >= nbits) break;
+            if ((x >> b) & 1ull) {
+                if (run == 0) start = i;
+                ++run;
+            } else if (run) {
+                close(i);
+            }
         }
     }
-    return -1;
+    if (run) close(start + run);
+    return best;
 }
 }  // namespace
 
@@ -93,14 +105,15 @@ Daemon::Window* Daemon::window_of_slot(uint32_t s) {
     return s < slot_window_.size() && slot_window_[s] != 0xFFFFFFFFu ? &windows_[slot_window_[s]] : nullptr;
 }
 
-// Size-segregated placement: runs of kLargeRun slots or more are placed from
-// the top of the window, smaller ones first-fit from the bottom, so freeing
-// many small objects (norms, biases, KV blocks) does not splinter the space
-// that multi-GB tensors need as one contiguous run.
+// Size-segregated placement: runs of kLargeRun slots or more go best-fit
+// (smallest hole that holds them, placed at its top; model tensors repeat in
+// size, so a freed hole is usually refilled exactly), smaller ones first-fit
+// from the bottom, so freeing many small objects (norms, biases, KV blocks)
+// does not splinter the space that multi-GB tensors need as one run.
 bool Daemon::alloc_in_window(Window& w, uint32_t count, uint32_t* base) {
     constexpr uint32_t kLargeRun = 8;
     if (count > w.nslots) return false;
-    int64_t rel = count >= kLargeRun ? find_free_run_top(w.free_bits, w.nslots, count)
+    int64_t rel = count >= kLargeRun ? find_free_run_best(w.free_bits, w.nslots, count)
                                      : find_free_run(w.free_bits, w.nslots, count);
     if (rel < 0) return false;
     for (uint32_t k = 0; k < count; ++k) {
@@ -137,6 +150,7 @@ void Daemon::free_run(uint32_t base, uint32_t count) {
 bool Daemon::allocate(uint32_t gpu, uint32_t numa, uint64_t nbytes, uint64_t flags, uint32_t* base,
                       uint32_t* count, std::unique_lock<std::mutex>& lk) {
     *count = slots_for(nbytes);
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(30);
     for (int attempt = 0; attempt <= 64; ++attempt) {
         auto pick = [&](auto pred) {
             for (Window& w : windows_)
@@ -151,7 +165,15 @@ bool Daemon::allocate(uint32_t gpu, uint32_t numa, uint64_t nbytes, uint64_t fla
             Metrics::get().inc(M::kRemoteNumaAllocs);
             return true;
         }
-        if (!force_drain_one(lk)) break;
+        if (force_drain_one(lk)) continue;
+        // Nothing left to drain synchronously: wait (bounded) for queued
+        // background drains to give their pinned runs back, then retry.
+        if (drains_pending_ == 0 || std::chrono::steady_clock::now() > deadline) break;
+        const uint32_t before = drains_pending_;
+        while (drains_pending_ == before && drains_pending_ > 0 && running_.load())
+            if (drained_cv_.wait_until(lk, deadline) == std::cv_status::timeout) break;
+        if (drains_pending_ == before) break;  // no progress within the bound
+        --attempt;                            // a finished drain is not a forced-drain attempt
     }
     return false;
 }

@@ -143,6 +143,7 @@ uint64_t Daemon::commit_cold(ColdEntry&& c) {
 
 void Daemon::enqueue_drain(const Lease& L) {
     set_run_state(L.base, L.count, OFLD_SLOT_DRAIN_IN_FLIGHT);
+    ++drains_pending_;
     {
         std::lock_guard<std::mutex> q(q_mu_);
         drain_q_.push_back(DrainJob{L.base, L.count});
@@ -198,6 +199,13 @@ void Daemon::finish_drain(uint32_t base, uint32_t count, uint64_t tid, uint64_t 
                           uint32_t owner, uint64_t nbytes, uint64_t ref) {
     if (state_of(base) != OFLD_SLOT_DRAIN_IN_FLIGHT || slots_[base].lease_id != lid) {
         if (ref && ref != reusable_cold(tid, ver)) free_cold(ref);  // raced with recovery
+        return;
+    }
+    if (!lease(lid)) {
+        // The owner released the object while its bytes were being drained
+        // (release leaves a draining run alone): drop both copies here.
+        if (ref && ref != reusable_cold(tid, ver)) free_cold(ref);
+        free_run(base, count);
         return;
     }
     if (!ref) {
@@ -299,6 +307,8 @@ void Daemon::drain_loop() {
             std::lock_guard<std::mutex> g(mu_);
             if (state_of(job.base) != OFLD_SLOT_DRAIN_IN_FLIGHT) {
                 Metrics::get().sub(M::kDrainingBytes, slots_[job.base].nbytes);
+                if (drains_pending_) --drains_pending_;
+                drained_cv_.notify_all();
                 continue;
             }
             const ofld_slot_entry_t& e = slots_[job.base];
@@ -317,6 +327,8 @@ void Daemon::drain_loop() {
         Metrics::get().sub(M::kDrainingBytes, nbytes);
         if (!ref && ok) ref = commit_cold(std::move(cold));
         finish_drain(job.base, job.count, tid, ver, lid, owner, nbytes, ref);
+        if (drains_pending_) --drains_pending_;
+        drained_cv_.notify_all();
     }
 }
 
