@@ -219,11 +219,14 @@ struct Agent::Impl {
             cudaDeviceGetStreamPriorityRange(&lo, &hi);
             int prio = opt.stream_priority < 0 ? hi : 0;
             CUDA_OK(cudaStreamCreateWithPriority(&stream, cudaStreamNonBlocking, prio));
-            if (opt.eager_register)
-                for (ArenaMap& m : arenas) register_arena(m);
         }
+        // Heartbeats start before the eager pinning below: registering a
+        // 100+ GB arena while other ranks pin theirs can outlast the daemon's
+        // heartbeat timeout, which would expire this session.
         progress_thr = std::thread([this] { progress_loop(); });
         heartbeat_thr = std::thread([this] { heartbeat_loop(); });
+        if (gpu && opt.eager_register)
+            for (ArenaMap& m : arenas) register_arena(m);
         LOG_INFO(TAG, "rank %u epoch %llu %s numa %d, %zu arenas, %u slots, ring %s", opt.rank_id,
                  (unsigned long long)epoch, gpu ? ("gpu " + std::to_string(opt.device)).c_str() : "host-mode", numa,
                  arenas.size(), num_slots, ring ? "on" : "off");

@@ -272,6 +272,7 @@ const std::map<std::string, Binder>& binders() {
         {"arenas.registration_chunk_mb", [](DaemonConfig& c, const Node& n, const std::string& k) { c.registration_chunk_bytes = as_u64(n, k) << 20; }},
         {"arenas.allocation_granularity_mb", [](DaemonConfig& c, const Node& n, const std::string& k) { c.allocation_granularity_bytes = as_u64(n, k) << 20; }},
         {"arenas.first_touch", [](DaemonConfig& c, const Node& n, const std::string& k) { c.numa_first_touch = as_bool(n, k); }},
+        {"arenas.huge_pages", [](DaemonConfig& c, const Node& n, const std::string& k) { c.arena_huge_pages = as_bool(n, k); }},
         // drain_policy
         {"drain_policy.target_tier", [](DaemonConfig& c, const Node& n, const std::string& k) {
              std::string s = need_scalar(n, k);

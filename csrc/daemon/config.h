@@ -45,6 +45,9 @@ struct DaemonConfig {
     uint64_t allocation_granularity_bytes = 16ull << 20;
     std::vector<NumaArena> per_numa;
     bool numa_first_touch = true;
+    // Ask for transparent huge pages on the arena mappings (madvise): 2 MiB
+    // pages cut IOMMU translation misses of GPU DMA into host memory.
+    bool arena_huge_pages = true;
 
     // drain_policy
     DrainTarget drain_target = DrainTarget::kPageableThenNvme;

@@ -83,11 +83,30 @@ void Daemon::build_arenas() {
         char* base = A.base;
         uint64_t sz = A.size;
         bool touch = cfg_.numa_first_touch;
-        std::thread t([node, base, sz, touch] {
+        bool huge = cfg_.arena_huge_pages;
+        std::thread t([node, base, sz, touch, huge] {
             pin_thread_to_node(node);
             int rc = bind_range_to_node(base, sz, node, false);
             if (rc != 0) LOG_WARN(TAG, "mbind(node=%d) failed rc=%d (continuing)", node, rc);
-            if (touch) first_touch(base, sz);
+            if (huge && ::madvise(base, sz, MADV_HUGEPAGE) != 0)
+                LOG_WARN(TAG, "madvise(MADV_HUGEPAGE) failed: %s (continuing with base pages)", std::strerror(errno));
+            if (touch) {
+                // fault the pages in from several threads on the node (a
+                // 100 GB arena is millions of page faults)
+                const uint64_t n = std::max<uint64_t>(1, std::min<uint64_t>(8, sz >> 30));
+                const uint64_t step = (sz / n + (2u << 20) - 1) & ~uint64_t((2u << 20) - 1);
+                std::vector<std::thread> ts;
+                for (uint64_t k = 0; k < n; ++k) {
+                    const uint64_t off = k * step;
+                    if (off >= sz) break;
+                    const uint64_t len = std::min(step, sz - off);
+                    ts.emplace_back([node, base, off, len] {
+                        pin_thread_to_node(node);
+                        first_touch(base + off, len);
+                    });
+                }
+                for (auto& th : ts) th.join();
+            }
         });
         t.join();
         LOG_INFO(TAG, "arena %zu: node=%u size=%llu MiB", i, A.numa_node,
