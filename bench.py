@@ -55,6 +55,7 @@ def parse():
     p.add_argument("--evict-ctas", type=int, default=0)
     p.add_argument("--restore-ctas", type=int, default=0)
     p.add_argument("--hash", type=int, default=1)
+    p.add_argument("--compress", type=int, default=1, help="zbf16 lossless coding of the bf16 payload over PCIe")
     p.add_argument("--e2e-steps", type=int, default=0, help="default: same as --steps")
     p.add_argument("--out", default="")
     # --workload weight_sync: in-box RL weight sync (trainer half -> rollout half of the GPUs)
@@ -143,12 +144,20 @@ def main():
 
     sess = offload_context(daemon_addr=sock, device=device, rank=rank, local_rank=local_rank, world_rank=rank,
                            eager_register=True, engine=args.engine, evict_ctas=args.evict_ctas,
-                           restore_ctas=args.restore_ctas, hash_on_evict=bool(args.hash), stream_priority=-1)
+                           restore_ctas=args.restore_ctas, hash_on_evict=bool(args.hash), stream_priority=-1,
+                           compress=bool(args.compress))
     off = sess.off
     g = torch.Generator(device=device)
     g.manual_seed(1234 + rank)
     x = torch.randn(nbytes // 2, dtype=torch.bfloat16, device=device, generator=g)
     ref_hash = off.hash_tensor(x)
+    # what crosses PCIe: zbf16 coding of the bf16 payload (host codec on a 64 MiB sample)
+    coding = "none"
+    if args.compress and args.engine == "kernel":
+        sample = x.view(torch.uint8)[: min(nbytes, 64 << 20)].cpu().numpy()
+        coded = native().zbf16_encode(sample)
+        if coded is not None:
+            coding = f"zbf16 lossless, {native().zbf16_coded_bytes(coded) / len(sample):.4f} of the bytes"
     copy_stream = torch.cuda.Stream(device=device, priority=-1)
 
     # ---- concurrent 8192^2 bf16 matmul loop on its own stream ----
@@ -269,6 +278,7 @@ def main():
                 "tensor_bytes": nbytes, "global_batch": world, "seq_len": 0, "parallelism": f"dp{world}",
                 "concurrent_matmul": "8192x8192 bf16 loop" if args.matmul else "none",
                 "engine": args.engine, "hash": bool(args.hash), "slot_mb": 64,
+                "transfer_coding": coding,
                 "l2": "inputs (1 GiB) larger than the 126 MB L2; no flush needed",
                 "baseline": f"StateSpectre H20 PCIe Gen5 1 GiB: D2H {BASELINE_D2H_GBS}, H2D {BASELINE_H2D_GBS} GB/s "
                             f"(round trip {BASELINE_ROUNDTRIP_GBS:.2f} GB/s per GPU)",

@@ -26,6 +26,7 @@
 #include "../kernels/kernels.h"
 #include "ofld/abi/offload_canonical_abi.hpp"
 #include "ofld/chunk_hash.h"
+#include "ofld/zbf16.h"
 #include "ofld/log.h"
 #include "ofld/metrics.h"
 #include "ofld/numa.h"
@@ -131,6 +132,8 @@ struct Agent::Impl {
         bool keep_pinned = false;
         PinnedPool::Buf dig, mism, exp;  // digests out, mismatch counter, expected digests
         uint64_t ndig = 0;
+        PinnedPool::Buf zb;              // zbf16 window bases (one byte per chunk) + pre-pass flag
+        bool z = false;
     };
     std::mutex inflight_mu;
     std::list<Pending> inflight;
@@ -390,6 +393,8 @@ struct Agent::Impl {
                 if (opt.keep_digests) dig.assign(d, d + p.ndig);
                 pool.put(p.dig);
             }
+            pool.put(p.zb);
+            p.zb = PinnedPool::Buf{};
             report_d2h(p);
             {
                 std::lock_guard<std::mutex> g(tab_mu);
@@ -484,6 +489,39 @@ struct Agent::Impl {
     }
 
     // Launch K1 (or the copy-engine A/B path) for one reserved run.
+    // zbf16 pre-pass: per-chunk window bases into a mapped buffer; true when
+    // every chunk fits coded. Waits for the stream (the decision precedes the
+    // reservation, whose flags record the format).
+    bool zscan(uint64_t src, uint64_t nbytes, cudaStream_t s, PinnedPool::Buf* out) {
+        const uint64_t nch = kern::digest_count(nbytes);
+        const uint64_t flag_off = (nch + 15) / 16 * 16;
+        *out = pool.get(flag_off + 16);
+        auto* fail_host = reinterpret_cast<volatile uint32_t*>(static_cast<char*>(out->host) + flag_off);
+        *fail_host = 0;
+        CUDA_OK(kern::zscan(reinterpret_cast<const void*>(src), nbytes, static_cast<uint8_t*>(out->dev),
+                            reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off), s, 0));
+        cudaEvent_t ev;
+        CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        CUDA_OK(cudaEventRecord(ev, s));
+        CUDA_OK(cudaEventSynchronize(ev));
+        cudaEventDestroy(ev);
+        if (*fail_host == 0) return true;
+        pool.put(*out);
+        *out = PinnedPool::Buf{};
+        return false;
+    }
+
+    bool want_z(uint64_t ptr, uint64_t nbytes, uint32_t fmt_hint) const {
+        return gpu && fmt_hint == kFmtBf16 && opt.compress && opt.engine != "copy_engine" &&
+               nbytes >= opt.compress_min_bytes && zbf16::eligible(nbytes) && (ptr & 15) == 0;
+    }
+
+    // Format of the bytes in a granted run (slot entries of the shared table).
+    bool run_is_z(uint32_t slot) const {
+        return slots && slot < num_slots &&
+               (reinterpret_cast<const volatile uint64_t&>(slots[slot].flags) & OFLD_FLAG_FORMAT_ZBF16) != 0;
+    }
+
     void launch_d2h(Pending& p, uint64_t src, char* dst_host, char* dst_dev, cudaStream_t s, bool hash) {
         if (!gpu) {
             std::memcpy(dst_host, reinterpret_cast<const void*>(src), p.nbytes);
@@ -500,7 +538,10 @@ struct Agent::Impl {
             p.dig = pool.get(std::max<uint64_t>(p.ndig, 1) * 8);
             dig_dev = static_cast<uint64_t*>(p.dig.dev);
         }
-        if (opt.engine == "copy_engine") {
+        if (p.z) {
+            CUDA_OK(kern::evict_z(reinterpret_cast<const void*>(src), dst_dev, p.nbytes,
+                                  static_cast<const uint8_t*>(p.zb.dev), dig_dev, s, opt.evict_ctas));
+        } else if (opt.engine == "copy_engine") {
             if (hash) CUDA_OK(kern::hash_device(reinterpret_cast<const void*>(src), p.nbytes, dig_dev, s, opt.hash_ctas));
             CUDA_OK(cudaMemcpyAsync(dst_host, reinterpret_cast<const void*>(src), p.nbytes, cudaMemcpyDeviceToHost, s));
         } else {
@@ -551,7 +592,8 @@ Agent::Agent(const AgentOptions& opt) : d_(new Impl(opt)) {}
 Agent::~Agent() = default;
 
 EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive, uint64_t tensor_id,
-                         uint64_t version, const std::string& name, DoneCallback on_done, bool wait) {
+                         uint64_t version, const std::string& name, DoneCallback on_done, bool wait,
+                         uint32_t fmt_hint) {
     Impl& D = *d_;
     EvictTicket t;
     t.tensor_id = tensor_id;
@@ -573,8 +615,12 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
     rq.flags = OFLD_FLAG_ALLOW_OVERFLOW | (destructive ? OFLD_FLAG_DESTRUCTIVE : 0) |
                (D.opt.fast_submit ? OFLD_FLAG_SUBMIT_ON_GRANT : 0);
     rq.debug_name = name;
+    PinnedPool::Buf zb;
+    const bool z = D.want_z(ptr, nbytes, fmt_hint) && D.zscan(ptr, nbytes, D.stream_of(stream), &zb);
+    if (z) rq.flags |= OFLD_FLAG_FORMAT_ZBF16;
     RequestOffloadResponse g = D.call<Op::kRequestOffload>(rq);
     if (!g.ok || g.blocked) {
+        D.pool.put(zb);
         t.message = g.ok ? "offload blocked (pinned pressure)" : g.message;
         return t;
     }
@@ -594,6 +640,9 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
     p.slot = g.slot_id;
     p.nbytes = nbytes;
     p.cb = std::move(on_done);
+    p.z = z;
+    p.zb = zb;
+    t.coded = z;
     D.inflight_d2h += nbytes;
     {
         std::lock_guard<std::mutex> lg(D.tab_mu);
@@ -740,12 +789,22 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
     p.keep_pinned = ro.keep_pinned;
     D.inflight_h2d += src_bytes;
     uint32_t* mism_dev = nullptr;
+    const bool z = D.run_is_z(r.slot_id);
     if (!D.gpu) {
         if (ro.cast != 0) {
             out.message = "casts need a GPU";
             return out;
         }
-        std::memcpy(reinterpret_cast<void*>(ptr), host, src_bytes);
+        if (z) {
+            if (!zbf16::decode_object(reinterpret_cast<const uint8_t*>(host), src_bytes,
+                                      reinterpret_cast<uint8_t*>(ptr))) {
+                out.message = "malformed zbf16 object";
+                D.finish(p);
+                return out;
+            }
+        } else {
+            std::memcpy(reinterpret_cast<void*>(ptr), host, src_bytes);
+        }
         if (ro.verify && !expect.empty()) {
             std::vector<uint64_t> got(kern::digest_count(src_bytes));
             ssh::host_chunk_digests(host, src_bytes, got.data());
@@ -766,7 +825,10 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
         std::memset(p.mism.host, 0, 4);
         mism_dev = static_cast<uint32_t*>(p.mism.dev);
     }
-    if (D.opt.engine == "copy_engine" && ro.cast == 0 && !exp_dev) {
+    if (z) {
+        CUDA_OK(kern::restore_z(dev, reinterpret_cast<void*>(ptr), src_bytes, kern::Cast(ro.cast),
+                                reinterpret_cast<float*>(ro.scales_ptr), exp_dev, mism_dev, s, D.opt.restore_ctas));
+    } else if (D.opt.engine == "copy_engine" && ro.cast == 0 && !exp_dev) {
         CUDA_OK(cudaMemcpyAsync(reinterpret_cast<void*>(ptr), host, src_bytes, cudaMemcpyHostToDevice, s));
     } else {
         CUDA_OK(kern::restore_cast(dev, reinterpret_cast<void*>(ptr), src_bytes, kern::Cast(ro.cast),
@@ -848,11 +910,23 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
             p.nbytes = r.nbytes;
             D.inflight_h2d += p.nbytes;
             ++D.restores;
+            const bool z = D.run_is_z(r.slot_id);
             if (D.gpu) {
-                CUDA_OK(kern::restore_cast(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes, kern::Cast::kNone,
-                                           nullptr, nullptr, nullptr, s, D.opt.restore_ctas));
+                if (z)
+                    CUDA_OK(kern::restore_z(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes, kern::Cast::kNone,
+                                            nullptr, nullptr, nullptr, s, D.opt.restore_ctas));
+                else
+                    CUDA_OK(kern::restore_cast(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes,
+                                               kern::Cast::kNone, nullptr, nullptr, nullptr, s, D.opt.restore_ctas));
                 CUDA_OK(cudaEventCreateWithFlags(&p.ev, cudaEventDisableTiming));
                 CUDA_OK(cudaEventRecord(p.ev, s));
+            } else if (z) {
+                if (!zbf16::decode_object(reinterpret_cast<const uint8_t*>(host), r.nbytes,
+                                          reinterpret_cast<uint8_t*>(items[i].ptr))) {
+                    out[i].message = "malformed zbf16 object";
+                    D.finish(p);
+                    continue;
+                }
             } else {
                 std::memcpy(reinterpret_cast<void*>(items[i].ptr), host, r.nbytes);
             }

@@ -44,7 +44,16 @@ struct AgentOptions {
     bool keep_digests = true;    // remember chunk digests for verify-on-restore
     bool zero_canonical_hash = false;  // commit hash 0 in trusted mode (manifest parity)
     int stream_priority = 0;     // internal stream priority (0 = default)
+    // zbf16 coding of bf16 evictions (ofld/zbf16.h): fewer bytes over PCIe
+    // and host memory. Applies to evict() calls that pass fmt_hint = kFmtBf16,
+    // on objects of at least compress_min_bytes, in kernel-engine mode.
+    bool compress = true;
+    uint64_t compress_min_bytes = 4ull << 20;
 };
+
+// evict() data hints.
+constexpr uint32_t kFmtUnknown = 0;
+constexpr uint32_t kFmtBf16 = 1;
 
 struct EvictTicket {
     bool ok = false;
@@ -52,6 +61,7 @@ struct EvictTicket {
     uint64_t tensor_id = 0, version = 0, nbytes = 0, lease_id = 0;
     uint32_t slot_id = 0;
     uint64_t hash_lo = 0, hash_hi = 0;  // valid once the copy completed (wait=true)
+    bool coded = false;                  // moved in zbf16 coding
 };
 
 struct RestoreOptions {
@@ -102,7 +112,8 @@ class Agent {
     // a pinned slot. `on_done` runs once the copy is complete (from the
     // progress thread, or inline when wait=true).
     EvictTicket evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive, uint64_t tensor_id,
-                      uint64_t version, const std::string& name, DoneCallback on_done, bool wait);
+                      uint64_t version, const std::string& name, DoneCallback on_done, bool wait,
+                      uint32_t fmt_hint = kFmtUnknown);
     // Many tensors with one reservation round trip (KV-cache blocks). All or
     // nothing per item; returns one ticket per item.
     std::vector<EvictTicket> evict_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait);

@@ -180,6 +180,7 @@ class Daemon {
         ofld_location_kind_t kind = OFLD_LOC_NONE;
         uint32_t slot = 0;
         uint64_t cold_ref = 0, nbytes = 0;
+        uint64_t fmt = 0;  // OFLD_FLAG_FORMAT_* of the stored bytes
     };
     struct Extent {
         std::string path;

@@ -246,7 +246,12 @@ bool Daemon::set_location(uint64_t tid, uint64_t ver, ofld_location_kind_t kind,
         Metrics::get().inc(M::kStaleVersionRejected);
         return false;
     }
+    // The byte format follows the data: read it off a pinned run, keep it
+    // while the same version moves between tiers.
+    const uint64_t prev_fmt = it != locations_.end() && it->second.version == ver ? it->second.fmt : 0;
     Location& L = locations_[tid];
+    L.fmt = kind == OFLD_LOC_PINNED && slot < layout_.num_slots ? (slots_[slot].flags & OFLD_FLAG_FORMAT_MASK)
+                                                                 : prev_fmt;
     L.version = ver;
     L.kind = kind;
     L.slot = slot;
@@ -514,7 +519,7 @@ RequestPrefetchResponse Daemon::do_request_prefetch(const RequestPrefetchRequest
     }
     uint64_t lid = new_lease(base, count, r.tensor_id, want, r.rank_id, r.rank_epoch, loc.nbytes, true);
     stamp_run(base, count, r.tensor_id, want, lid, r.rank_id, leases_[lid].owner_pid, r.rank_epoch,
-              loc.nbytes, r.flags, OFLD_SLOT_READBACK_IN_FLIGHT);
+              loc.nbytes, (r.flags & ~OFLD_FLAG_FORMAT_MASK) | loc.fmt, OFLD_SLOT_READBACK_IN_FLIGHT);
     for (uint32_t k = 0; k < count; ++k) slots_[base + k].cold_ref = loc.cold_ref;
     {
         std::lock_guard<std::mutex> q(q_mu_);

@@ -91,6 +91,11 @@ typedef enum ofld_arena_kind_e {
 #define OFLD_FLAG_SUBMIT_ON_GRANT (1ull << 16)
 /* Extension: a ready prefetch moves the run straight to H2D_IN_FLIGHT. */
 #define OFLD_FLAG_SUBMIT_ON_READY (1ull << 17)
+/* Extension: the run holds the object in zbf16 chunk coding (ofld/zbf16.h).
+ * Set by the rank at reservation, stamped on the run's slot entries, kept
+ * across drains and readbacks; readers decode. */
+#define OFLD_FLAG_FORMAT_ZBF16 (1ull << 18)
+#define OFLD_FLAG_FORMAT_MASK (OFLD_FLAG_FORMAT_ZBF16)
 
 typedef struct ofld_arena_desc_s {
     ofld_arena_id_t arena_id;

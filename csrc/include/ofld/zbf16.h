@@ -1,0 +1,220 @@
+// zbf16: lossless chunk coding of bf16 tensors for host transfers.
+//
+// PCIe (and the host memory behind it) is the bottleneck of evict/restore, so
+// bf16 data crosses it coded: a bf16 value is sign(1) exponent(8) mantissa(7);
+// sign and mantissa are near-random, but the exponents of weights,
+// activations and KV caches cluster in a few binades. Per 64 KiB chunk
+// (the same chunking as the ssh128 hash):
+//
+//   offset 0           header (16 bytes, below)
+//   16                 low plane: one byte per element, (sign << 7) | mantissa
+//   16 + n             code plane: one 4-bit code per element (element 2j in
+//                      the low nibble of byte j): code = exponent - ebase when
+//                      that is 0..14, else 15 (escape)
+//   16 + n + n/2       escape bytes: the raw exponent of every escaped
+//                      element, ordered by hash lane t = 0..255, then by the
+//                      lane's vectors k*256 + t (k = 0..15), then by element
+//                      within the 16-byte vector
+//
+// with n = len / 2 elements. ebase is chosen per chunk as the start of the
+// 15-binade window that holds the most elements. A coded chunk must fit in
+// its own raw length (so every byte of an object stays inside [0, nbytes)
+// of its pinned run and tiers that copy nbytes keep it intact). A final
+// chunk shorter than kRawTail bytes is stored raw (decided from nbytes
+// alone). An object is coded only when every other chunk fits; the format is
+// a property of the pinned run (OFLD_FLAG_FORMAT_ZBF16 on its slot entries).
+//
+// Typical ratio for N(0, s) bf16 data: 0.75 + escapes (a few per chunk).
+#pragma once
+
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "ofld/chunk_hash.h"  // SSH_HD
+
+namespace ofld {
+namespace zbf16 {
+
+constexpr uint32_t kChunk = 65536;
+constexpr uint32_t kHeader = 16;
+constexpr uint32_t kWindow = 15;
+constexpr uint32_t kEscape = 15;
+constexpr uint32_t kRawTail = 4096;  // a final chunk shorter than this is stored raw
+constexpr uint32_t kLanes = 256;
+constexpr uint32_t kVecsPerLane = 16;
+constexpr uint16_t kTag = 0x425A;  // "ZB"
+
+struct Header {
+    uint16_t tag;
+    uint8_t mode;  // 1 = coded
+    uint8_t ebase;
+    uint32_t n_esc;
+    uint32_t src_len;
+    uint32_t comp_len;
+};
+static_assert(sizeof(Header) == kHeader, "16-byte chunk header");
+
+SSH_HD uint32_t exponent(uint16_t h) { return (h >> 7) & 0xFFu; }
+SSH_HD uint8_t low_byte(uint16_t h) { return uint8_t(((h >> 8) & 0x80u) | (h & 0x7Fu)); }
+SSH_HD uint32_t code_of(uint32_t e, uint32_t ebase) {
+    const uint32_t d = e - ebase;  // wraps below ebase
+    return d < kWindow ? d : kEscape;
+}
+SSH_HD uint16_t rebuild(uint8_t low, uint32_t e) {
+    return uint16_t((uint32_t(low & 0x80u) << 8) | ((e & 0xFFu) << 7) | (low & 0x7Fu));
+}
+SSH_HD uint32_t coded_len(uint32_t len, uint32_t n_esc) {
+    const uint32_t n = len / 2;
+    return kHeader + n + n / 2 + n_esc;
+}
+// Whether chunk c (of `nchunks`, raw length len) is stored raw by rule.
+SSH_HD bool raw_by_rule(uint64_t c, uint64_t nchunks, uint32_t len) { return c + 1 == nchunks && len < kRawTail; }
+// Objects that can be coded at all: 16-byte multiple, at least one chunk.
+SSH_HD bool eligible(uint64_t nbytes) { return nbytes >= kRawTail && nbytes % 16 == 0; }
+
+// ---- host reference implementation (tests, tools) -------------------------
+
+// Best window start and the escape count it leaves, from a 256-bin histogram.
+inline void best_window(const uint32_t* hist, uint32_t total, uint32_t* ebase, uint32_t* n_esc) {
+    uint32_t best = 0, best_w = 0, s = 0;
+    for (uint32_t e = 0; e < kWindow; ++e) s += hist[e];
+    best = s;
+    for (uint32_t w = 1; w + kWindow <= 256; ++w) {
+        s += hist[w + kWindow - 1];
+        s -= hist[w - 1];
+        if (s > best) {
+            best = s;
+            best_w = w;
+        }
+    }
+    *ebase = best_w;
+    *n_esc = total - best;
+}
+
+// Elements of a chunk in escape order: lane t, vector k*256+t, element j.
+template <class F>
+inline void for_each_in_lane_order(uint32_t len, F&& f) {
+    const uint32_t nvec = len / 16;
+    for (uint32_t t = 0; t < kLanes; ++t)
+        for (uint32_t k = 0; k < kVecsPerLane; ++k) {
+            const uint32_t vi = k * kLanes + t;
+            if (vi >= nvec) continue;
+            for (uint32_t j = 0; j < 8; ++j) f(vi * 8 + j);
+        }
+}
+
+// Code one chunk (len % 16 == 0). Returns the coded length, or 0 when the
+// chunk does not fit in `len` bytes.
+inline uint32_t encode_chunk(const uint8_t* src, uint32_t len, uint8_t* out) {
+    const uint32_t n = len / 2;
+    std::vector<uint16_t> h(n);
+    std::memcpy(h.data(), src, len);
+    uint32_t hist[256] = {0};
+    for (uint32_t i = 0; i < n; ++i) hist[exponent(h[i])]++;
+    uint32_t ebase, n_esc;
+    best_window(hist, n, &ebase, &n_esc);
+    const uint32_t total = coded_len(len, n_esc);
+    if (total > len) return 0;
+    Header hd{kTag, 1, uint8_t(ebase), n_esc, len, total};
+    std::memcpy(out, &hd, kHeader);
+    uint8_t* low = out + kHeader;
+    uint8_t* codes = low + n;
+    uint8_t* esc = codes + n / 2;
+    std::memset(codes, 0, n / 2);
+    for (uint32_t i = 0; i < n; ++i) {
+        low[i] = low_byte(h[i]);
+        codes[i / 2] |= uint8_t(code_of(exponent(h[i]), ebase) << (4 * (i & 1)));
+    }
+    uint32_t k = 0;
+    for_each_in_lane_order(len, [&](uint32_t i) {
+        if (code_of(exponent(h[i]), ebase) == kEscape) esc[k++] = uint8_t(exponent(h[i]));
+    });
+    return total;
+}
+
+// Decode one coded chunk into `len` bytes; false on a malformed chunk.
+inline bool decode_chunk(const uint8_t* in, uint32_t len, uint8_t* out) {
+    Header hd;
+    std::memcpy(&hd, in, kHeader);
+    if (hd.tag != kTag || hd.mode != 1 || hd.src_len != len || hd.comp_len != coded_len(len, hd.n_esc) ||
+        hd.comp_len > len)
+        return false;
+    const uint32_t n = len / 2;
+    const uint8_t* low = in + kHeader;
+    const uint8_t* codes = low + n;
+    const uint8_t* esc = codes + n / 2;
+    std::vector<uint16_t> h(n);
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t c = (codes[i / 2] >> (4 * (i & 1))) & 15u;
+        h[i] = rebuild(low[i], hd.ebase + c);  // escapes patched below
+    }
+    uint32_t k = 0;
+    bool ok = true;
+    for_each_in_lane_order(len, [&](uint32_t i) {
+        const uint32_t c = (codes[i / 2] >> (4 * (i & 1))) & 15u;
+        if (c == kEscape) {
+            if (k >= hd.n_esc) {
+                ok = false;
+                return;
+            }
+            h[i] = rebuild(low[i], esc[k++]);
+        }
+    });
+    if (!ok || k != hd.n_esc) return false;
+    std::memcpy(out, h.data(), len);
+    return true;
+}
+
+// Whole objects at the 64 KiB stride. encode_object returns false (and
+// leaves `out` unspecified) when the object is not codable.
+inline bool encode_object(const uint8_t* src, uint64_t nbytes, uint8_t* out) {
+    if (!eligible(nbytes)) return false;
+    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    for (uint64_t c = 0; c < nchunks; ++c) {
+        const uint64_t base = c * kChunk;
+        const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+        if (raw_by_rule(c, nchunks, len)) {
+            std::memcpy(out + base, src + base, len);
+            continue;
+        }
+        if (!encode_chunk(src + base, len, out + base)) return false;
+    }
+    return true;
+}
+
+inline bool decode_object(const uint8_t* in, uint64_t nbytes, uint8_t* out) {
+    if (!eligible(nbytes)) return false;
+    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    for (uint64_t c = 0; c < nchunks; ++c) {
+        const uint64_t base = c * kChunk;
+        const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+        if (raw_by_rule(c, nchunks, len)) {
+            std::memcpy(out + base, in + base, len);
+            continue;
+        }
+        if (!decode_chunk(in + base, len, out + base)) return false;
+    }
+    return true;
+}
+
+// Bytes that actually carry data (what crosses PCIe), for statistics.
+inline uint64_t coded_bytes(const uint8_t* in, uint64_t nbytes) {
+    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    uint64_t total = 0;
+    for (uint64_t c = 0; c < nchunks; ++c) {
+        const uint64_t base = c * kChunk;
+        const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+        if (raw_by_rule(c, nchunks, len)) {
+            total += len;
+        } else {
+            Header hd;
+            std::memcpy(&hd, in + base, kHeader);
+            total += hd.comp_len;
+        }
+    }
+    return total;
+}
+
+}  // namespace zbf16
+}  // namespace ofld

@@ -73,6 +73,19 @@ cudaError_t verify_peer(const void* local_dev, const void* peer_dev, uint64_t nb
 cudaError_t quant_fp8_block(const void* bf16_src, void* fp8_dst, float* scales, uint64_t nelem,
                             cudaStream_t stream, int ctas);
 
+// zbf16 coding of bf16 objects for host transfers (format: ofld/zbf16.h).
+// zscan: per-chunk window base into `ebase` (device-accessible, one byte per
+// 64 KiB chunk) and *fail |= 1 when some chunk does not fit coded (then the
+// object must move uncoded). evict_z / restore_z: K1 / K2 over a coded run;
+// all require zbf16::eligible(nbytes) and 16-byte aligned pointers. restore_z
+// supports Cast::kNone, kBf16ToFp8Block128 and kBf16ToFp32.
+cudaError_t zscan(const void* src_dev, uint64_t nbytes, uint8_t* ebase, uint32_t* fail, cudaStream_t stream,
+                  int ctas);
+cudaError_t evict_z(const void* src_dev, void* dst_mapped, uint64_t nbytes, const uint8_t* ebase,
+                    uint64_t* digests, cudaStream_t stream, int ctas);
+cudaError_t restore_z(const void* src_mapped, void* dst_dev, uint64_t nbytes, Cast cast, float* scales_dev,
+                      const uint64_t* expect, uint32_t* mismatch_dev, cudaStream_t stream, int ctas);
+
 // Number of chunk digests for nbytes.
 inline uint64_t digest_count(uint64_t nbytes) { return (nbytes + 65535) / 65536; }
 

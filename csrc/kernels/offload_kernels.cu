@@ -23,6 +23,7 @@
 
 #include "kernels.h"
 #include "ofld/chunk_hash.h"
+#include "ofld/zbf16.h"
 
 namespace ofld {
 namespace kern {
@@ -265,6 +266,278 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 }
 
+// ---- zbf16 coding (pre-pass, K1 with coding, K2 with decoding) -----------
+
+// Exclusive prefix sum over the 256 threads of the block; *total = the sum.
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t x, uint32_t* sm, uint32_t* total) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t inc = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= uint32_t(o)) inc += y;
+    }
+    if (lane == 31) sm[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = lane < kThreads / 32 ? sm[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < kThreads / 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= uint32_t(o)) w += y;
+        }
+        if (lane < kThreads / 32) sm[lane] = w;
+    }
+    __syncthreads();
+    const uint32_t warp_off = warp ? sm[warp - 1] : 0;
+    *total = sm[kThreads / 32 - 1];
+    __syncthreads();  // sm is reused by the next call
+    return warp_off + inc - x;
+}
+
+__device__ __forceinline__ uint32_t half_of(const uint4& v, int j) {
+    const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
+    return (j & 1) ? (w >> 16) : (w & 0xFFFFu);
+}
+
+// Pre-pass: per chunk, the exponent histogram, the best 15-binade window
+// (ebase) and whether the coded chunk fits in its raw length. Any chunk that
+// does not fit sets *fail: the object is then moved uncoded.
+__global__ void __launch_bounds__(kThreads, 3)
+    k_zscan(const uint8_t* __restrict__ src, uint64_t nbytes, uint8_t* __restrict__ ebase_out, uint32_t* fail) {
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t best[kThreads / 32];
+    const uint32_t t = threadIdx.x, lane = t & 31;
+    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+        const uint64_t base = c * kChunk;
+        const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+        if (zbf16::raw_by_rule(c, nchunks, len)) {
+            if (t == 0) ebase_out[c] = 0;
+            continue;  // uniform per chunk
+        }
+        const uint32_t nvec = len / 16;
+        hist[t] = 0;
+        __syncthreads();
+#pragma unroll 4
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            const bool valid = vi < nvec;
+            const uint4 v = valid ? ld_once(src + base + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t e = valid ? zbf16::exponent(uint16_t(half_of(v, j))) : 256u;
+                const uint32_t peers = __match_any_sync(0xffffffffu, e);
+                if (e < 256u && lane == uint32_t(__ffs(peers) - 1)) atomicAdd(&hist[e], uint32_t(__popc(peers)));
+            }
+        }
+        __syncthreads();
+        // window sums; argmax with ties to the lowest start: (sum << 8) | (255 - w)
+        uint32_t key = 0;
+        if (t + zbf16::kWindow <= 256) {
+            uint32_t sum = 0;
+#pragma unroll
+            for (uint32_t e = 0; e < zbf16::kWindow; ++e) sum += hist[t + e];
+            key = (sum << 8) | (255u - t);
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+        if (lane == 0) best[t >> 5] = key;
+        __syncthreads();
+        if (t == 0) {
+            uint32_t m = 0;
+#pragma unroll
+            for (int w = 0; w < kThreads / 32; ++w) m = max(m, best[w]);
+            const uint32_t n = len / 2, covered = m >> 8, eb = 255u - (m & 0xFFu);
+            ebase_out[c] = uint8_t(eb);
+            if (zbf16::coded_len(len, n - covered) > len) atomicOr(fail, 1u);
+        }
+        __syncthreads();  // hist / best are reused by the next chunk
+    }
+}
+
+// K1 with coding: hash the raw bytes and write each chunk coded (or raw by
+// rule) to the host-mapped run. Requires 16-byte aligned src/dst and
+// nbytes % 16 == 0 (zbf16::eligible).
+__global__ void __launch_bounds__(kThreads, 2)
+    k_evict_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
+              const uint8_t* __restrict__ ebase, uint64_t* __restrict__ digests, int pol) {
+    __shared__ uint64_t red[kThreads / 32];
+    __shared__ uint32_t sc[kThreads / 32];
+    const uint32_t t = threadIdx.x;
+    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+        const uint64_t base = c * kChunk;
+        const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+        const uint32_t nvec = len / 16;
+        const bool raw = zbf16::raw_by_rule(c, nchunks, len);
+        const uint32_t eb = raw ? 0u : uint32_t(ebase[c]);
+        uint4 v[kVecs];
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            v[k] = vi < nvec ? ld_policy(src + base + uint64_t(vi) * 16, 0) : make_uint4(0, 0, 0, 0);
+        }
+        ssh::Lane L = ssh::lane_init(t);
+        uint32_t cnt = 0;
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            if (vi < nvec) {
+                ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
+                if (raw) {
+                    st_policy(dst + base + uint64_t(vi) * 16, v[k], pol);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        cnt += zbf16::code_of(zbf16::exponent(uint16_t(half_of(v[k], j))), eb) == zbf16::kEscape;
+                }
+            }
+        }
+        if (!raw) {  // uniform per chunk
+            uint32_t total;
+            uint32_t off = block_excl_scan(cnt, sc, &total);
+            const uint32_t n = len / 2;
+            uint8_t* out = dst + base;
+            if (t == 0) {
+                const uint4 hd = make_uint4(uint32_t(zbf16::kTag) | (1u << 16) | (eb << 24), total, len,
+                                            zbf16::coded_len(len, total));
+                st_policy(out, hd, pol);
+            }
+            uint8_t* esc = out + zbf16::kHeader + n + n / 2;
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k) {
+                const uint32_t vi = uint32_t(k) * kThreads + t;
+                if (vi >= nvec) continue;
+                uint32_t lo0 = 0, lo1 = 0, codes = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint16_t h = uint16_t(half_of(v[k], j));
+                    const uint32_t e = zbf16::exponent(h);
+                    const uint32_t cd = zbf16::code_of(e, eb);
+                    const uint32_t lb = zbf16::low_byte(h);
+                    if (j < 4) lo0 |= lb << (8 * j);
+                    else lo1 |= lb << (8 * (j - 4));
+                    codes |= cd << (4 * j);
+                    if (cd == zbf16::kEscape) esc[off++] = uint8_t(e);
+                }
+                asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(out + zbf16::kHeader + uint64_t(vi) * 8),
+                             "r"(lo0), "r"(lo1)
+                             : "memory");
+                asm volatile("st.global.cs.u32 [%0], %1;" ::"l"(out + zbf16::kHeader + n + uint64_t(vi) * 4), "r"(codes)
+                             : "memory");
+            }
+        }
+        uint64_t root = tree_fold(ssh::lane_digest(L, t), red);
+        if (t == 0 && digests) digests[c] = ssh::chunk_finish(root, len);
+    }
+}
+
+// K2 with decoding: read each coded chunk from the host-mapped run (16 bytes
+// of header, 12 bytes per 8 elements, the chunk's escapes), rebuild the bf16
+// vectors in registers and continue as K2 (verify, cast, store).
+template <bool VERIFY, int CAST>
+__global__ void __launch_bounds__(kThreads, 2)
+    k_restore_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
+                float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, int pol) {
+    __shared__ uint64_t red[kThreads / 32];
+    __shared__ uint32_t sc[kThreads / 32];
+    const uint32_t t = threadIdx.x;
+    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+        const uint64_t base = c * kChunk;
+        const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+        const uint32_t nvec = len / 16;
+        const uint8_t* in = src + base;
+        uint4 v[kVecs];
+        if (zbf16::raw_by_rule(c, nchunks, len)) {
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k) {
+                const uint32_t vi = uint32_t(k) * kThreads + t;
+                v[k] = vi < nvec ? ld_policy(in + uint64_t(vi) * 16, pol) : make_uint4(0, 0, 0, 0);
+            }
+        } else {
+            const uint32_t n = len / 2;
+            const uint4 hd = ld_policy(in, pol);  // every thread: one broadcast request per warp
+            uint2 lo[kVecs];
+            uint32_t cd[kVecs];
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k) {
+                const uint32_t vi = uint32_t(k) * kThreads + t;
+                if (vi < nvec) {
+                    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                                 : "=r"(lo[k].x), "=r"(lo[k].y)
+                                 : "l"(in + zbf16::kHeader + uint64_t(vi) * 8));
+                    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];"
+                                 : "=r"(cd[k])
+                                 : "l"(in + zbf16::kHeader + n + uint64_t(vi) * 4));
+                } else {
+                    lo[k] = make_uint2(0, 0);
+                    cd[k] = 0;
+                }
+            }
+            const uint32_t eb = hd.x >> 24;
+            uint32_t cnt = 0;
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k) {
+                const uint32_t vi = uint32_t(k) * kThreads + t;
+                if (vi < nvec)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) cnt += ((cd[k] >> (4 * j)) & 15u) == zbf16::kEscape;
+            }
+            uint32_t total;
+            uint32_t off = block_excl_scan(cnt, sc, &total);
+            const uint8_t* esc = in + zbf16::kHeader + n + n / 2;
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k) {
+                uint32_t w[4];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t code = (cd[k] >> (4 * j)) & 15u;
+                    const uint32_t lb = ((j < 4 ? lo[k].x : lo[k].y) >> (8 * (j & 3))) & 0xFFu;
+                    uint32_t e = eb + code;
+                    if (code == zbf16::kEscape) e = esc[off++];  // only valid vectors carry escapes
+                    const uint32_t h = zbf16::rebuild(uint8_t(lb), e);
+                    if (j & 1) w[j >> 1] |= h << 16;
+                    else w[j >> 1] = h;
+                }
+                v[k] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+        ssh::Lane L = ssh::lane_init(t);
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            const bool valid = vi < nvec;
+            if (VERIFY && valid) ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
+            const uint64_t gv = base / 16 + vi;
+            if (CAST == int(Cast::kNone)) {
+                if (valid) store_vec<true>(dst + gv * 16, v[k], 16u);
+            } else if (CAST == int(Cast::kBf16ToFp8Block128)) {
+                float s;
+                uint2 q = quant8(v[k], valid, &s);
+                if (valid) {
+                    *reinterpret_cast<uint2*>(dst + gv * 8) = q;
+                    if ((t & 15) == 0) scales[gv / 16] = s;
+                }
+            } else if (CAST == int(Cast::kBf16ToFp32)) {
+                if (valid) {
+                    uint4 a = make_uint4(__float_as_uint(bf16_lo(v[k].x)), __float_as_uint(bf16_hi(v[k].x)),
+                                         __float_as_uint(bf16_lo(v[k].y)), __float_as_uint(bf16_hi(v[k].y)));
+                    uint4 b = make_uint4(__float_as_uint(bf16_lo(v[k].z)), __float_as_uint(bf16_hi(v[k].z)),
+                                         __float_as_uint(bf16_lo(v[k].w)), __float_as_uint(bf16_hi(v[k].w)));
+                    *reinterpret_cast<uint4*>(dst + gv * 32) = a;
+                    *reinterpret_cast<uint4*>(dst + gv * 32 + 16) = b;
+                }
+            }
+        }
+        if (VERIFY) {
+            uint64_t root = tree_fold(ssh::lane_digest(L, t), red);
+            if (t == 0 && ssh::chunk_finish(root, len) != expect[c]) atomicAdd(mismatch, 1u);
+        }
+    }
+}
+
 // ---- K3: local hash + exact compare against a peer replica ----------------
 __global__ void __launch_bounds__(kThreads, 2)
     k_verify_peer(const uint8_t* __restrict__ local, const uint8_t* __restrict__ peer, uint64_t nbytes,
@@ -428,6 +701,60 @@ cudaError_t restore_cast(const void* src, void* dst, uint64_t nbytes, Cast cast,
         } else {
             return cudaErrorInvalidValue;
         }
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t zscan(const void* src, uint64_t nbytes, uint8_t* ebase, uint32_t* fail, cudaStream_t s, int ctas) {
+    if (!zbf16::eligible(nbytes) || !aligned16(src) || !ebase || !fail) return cudaErrorInvalidValue;
+    int sms = 148;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    int g = ctas > 0 ? ctas : sms * 3;
+    if (uint64_t(g) > nchunks) g = int(nchunks);
+    k_zscan<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), nbytes, ebase, fail);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t evict_z(const void* src, void* dst, uint64_t nbytes, const uint8_t* ebase, uint64_t* digests,
+                    cudaStream_t s, int ctas) {
+    if (!zbf16::eligible(nbytes) || !aligned16(src) || !aligned16(dst) || !ebase) return cudaErrorInvalidValue;
+    const int g = grid_for(nbytes, ctas, 48);
+    k_evict_z<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nbytes, ebase,
+                                     digests, g_policy.load(std::memory_order_relaxed));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t restore_z(const void* src, void* dst, uint64_t nbytes, Cast cast, float* scales, const uint64_t* expect,
+                      uint32_t* mismatch, cudaStream_t s, int ctas) {
+    if (!zbf16::eligible(nbytes) || !aligned16(src) || !aligned16(dst)) return cudaErrorInvalidValue;
+    if (expect && !mismatch) return cudaErrorInvalidValue;
+    const int g = grid_for(nbytes, ctas, 96);
+    const int p = g_policy.load(std::memory_order_relaxed);
+    auto S = static_cast<const uint8_t*>(src);
+    auto D = static_cast<uint8_t*>(dst);
+    const bool v = expect != nullptr;
+    switch (cast) {
+        case Cast::kNone:
+            if (v) k_restore_z<true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
+            else k_restore_z<false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+            break;
+        case Cast::kBf16ToFp8Block128:
+            if (!scales) return cudaErrorInvalidValue;
+            if (v) k_restore_z<true, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, expect, mismatch, p);
+            else k_restore_z<false, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, nullptr, nullptr, p);
+            break;
+        case Cast::kBf16ToFp32:
+            if (v) k_restore_z<true, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
+            else k_restore_z<false, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+            break;
+        default:
+            return cudaErrorInvalidValue;  // coded objects are bf16
     }
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();

@@ -17,6 +17,7 @@
 #include "../daemon/daemon.h"
 #include "../kernels/kernels.h"
 #include "ofld/chunk_hash.h"
+#include "ofld/zbf16.h"
 #include "ofld/codec.h"
 #include "ofld/log.h"
 #include "ofld/metrics.h"
@@ -219,6 +220,8 @@ class PyAgent {
             else if (k == "keep_digests") o.keep_digests = v.cast<bool>();
             else if (k == "zero_canonical_hash") o.zero_canonical_hash = v.cast<bool>();
             else if (k == "stream_priority") o.stream_priority = v.cast<int>();
+            else if (k == "compress") o.compress = v.cast<bool>();
+            else if (k == "compress_min_bytes") o.compress_min_bytes = v.cast<uint64_t>();
             else throw std::invalid_argument("unknown agent option '" + k + "'");
         }
         py::gil_scoped_release nogil;
@@ -249,17 +252,18 @@ PYBIND11_MODULE(_C, m) {
         .def(
             "evict",
             [](PyAgent& self, uint64_t ptr, uint64_t nbytes, uint64_t stream, bool destructive, uint64_t tid,
-               uint64_t ver, std::string name, py::object cb, bool wait) {
+               uint64_t ver, std::string name, py::object cb, bool wait, uint32_t fmt_hint) {
                 DoneCallback f = wrap_cb(std::move(cb));
                 EvictTicket t;
                 {
                     py::gil_scoped_release nogil;
-                    t = self.ag().evict(ptr, nbytes, stream, destructive, tid, ver, name, std::move(f), wait);
+                    t = self.ag().evict(ptr, nbytes, stream, destructive, tid, ver, name, std::move(f), wait,
+                                        fmt_hint);
                 }
-                return py::make_tuple(t.ok, t.message, t.lease_id, t.slot_id, t.hash_lo, t.hash_hi);
+                return py::make_tuple(t.ok, t.message, t.lease_id, t.slot_id, t.hash_lo, t.hash_hi, t.coded);
             },
             py::arg("ptr"), py::arg("nbytes"), py::arg("stream"), py::arg("destructive"), py::arg("tensor_id"),
-            py::arg("version"), py::arg("name"), py::arg("callback"), py::arg("wait"))
+            py::arg("version"), py::arg("name"), py::arg("callback"), py::arg("wait"), py::arg("fmt_hint") = 0)
         .def(
             "evict_batch",
             [](PyAgent& self, std::vector<std::tuple<uint64_t, uint64_t, uint64_t, uint64_t>> items, uint64_t stream,
@@ -591,6 +595,50 @@ PYBIND11_MODULE(_C, m) {
         void* dev = nullptr;
         check(cudaHostGetDevicePointer(&dev, reinterpret_cast<void*>(ptr), 0), "cudaHostGetDevicePointer");
         return reinterpret_cast<uint64_t>(dev);
+    });
+    // zbf16 host reference codec (tests, tools)
+    m.def("zbf16_encode", [](py::buffer b) -> py::object {
+        py::buffer_info i = b.request();
+        const uint64_t n = uint64_t(i.size) * uint64_t(i.itemsize);
+        std::string out(n, '\0');
+        bool ok;
+        {
+            py::gil_scoped_release nogil;
+            ok = zbf16::encode_object(static_cast<const uint8_t*>(i.ptr), n, reinterpret_cast<uint8_t*>(&out[0]));
+        }
+        if (!ok) return py::none();
+        return py::bytes(out);
+    });
+    m.def("zbf16_decode", [](py::bytes coded) {
+        std::string in = coded;
+        std::string out(in.size(), '\0');
+        if (!zbf16::decode_object(reinterpret_cast<const uint8_t*>(in.data()), in.size(),
+                                  reinterpret_cast<uint8_t*>(&out[0])))
+            throw std::runtime_error("malformed zbf16 object");
+        return py::bytes(out);
+    });
+    m.def("zbf16_coded_bytes", [](py::bytes coded) {
+        std::string in = coded;
+        return zbf16::coded_bytes(reinterpret_cast<const uint8_t*>(in.data()), in.size());
+    });
+    m.def("k_zscan", [](uint64_t src, uint64_t n, uint64_t ebase, uint64_t fail, uint64_t stream, int ctas) {
+        check(kern::zscan(reinterpret_cast<const void*>(src), n, reinterpret_cast<uint8_t*>(ebase),
+                          reinterpret_cast<uint32_t*>(fail), reinterpret_cast<cudaStream_t>(stream), ctas),
+              "zscan");
+    });
+    m.def("k_evict_z", [](uint64_t src, uint64_t dst, uint64_t n, uint64_t ebase, uint64_t dig, uint64_t stream,
+                          int ctas) {
+        check(kern::evict_z(reinterpret_cast<const void*>(src), reinterpret_cast<void*>(dst), n,
+                            reinterpret_cast<const uint8_t*>(ebase), reinterpret_cast<uint64_t*>(dig),
+                            reinterpret_cast<cudaStream_t>(stream), ctas),
+              "evict_z");
+    });
+    m.def("k_restore_z", [](uint64_t src, uint64_t dst, uint64_t n, int cast, uint64_t scales, uint64_t expect,
+                            uint64_t mismatch, uint64_t stream, int ctas) {
+        check(kern::restore_z(reinterpret_cast<const void*>(src), reinterpret_cast<void*>(dst), n, kern::Cast(cast),
+                              reinterpret_cast<float*>(scales), reinterpret_cast<const uint64_t*>(expect),
+                              reinterpret_cast<uint32_t*>(mismatch), reinterpret_cast<cudaStream_t>(stream), ctas),
+              "restore_z");
     });
     m.def("host_unregister", [](uint64_t ptr) { check(cudaHostUnregister(reinterpret_cast<void*>(ptr)), "cudaHostUnregister"); });
     bind_fabric(m);

@@ -17,7 +17,10 @@ Differences that are additions, not changes:
   * ``evict_batch`` / ``restore_batch`` move many small tensors (KV-cache
     blocks) with one reservation round trip;
   * ``PrefetchHandle.wait`` waits for the restore copy itself (StateSpectre
-    waited on the evict flag, reference: __init__.py:272-274).
+    waited on the evict flag, reference: __init__.py:272-274);
+  * bf16 tensors of 4 MiB and more cross PCIe in zbf16 coding (lossless
+    exponent coding, about 0.75 of the bytes; ``OffloadHandle.coded``);
+    ``offload_context(..., compress=False)`` moves them uncoded.
 """
 
 from __future__ import annotations
@@ -139,7 +142,7 @@ class OffloadHandle:
     """Handle to an offloaded tensor; carries what restore needs."""
 
     __slots__ = ("tensor_id", "version", "name", "shape", "stride", "dtype", "device_origin", "nbytes", "_off",
-                 "_prefetched", "_discarded")
+                 "_prefetched", "_discarded", "coded")
 
     def __init__(self, off, tensor_id, version, name, shape, stride, dtype, device_origin, nbytes):
         self._off = off
@@ -153,6 +156,7 @@ class OffloadHandle:
         self.nbytes = int(nbytes)
         self._prefetched = None
         self._discarded = False
+        self.coded = False  # moved zbf16-coded (lossless) when True
 
     def ready(self) -> bool:
         """True once the copy into the pinned slot has completed."""
@@ -639,12 +643,16 @@ class Off:
         nbytes = src.numel() * src.element_size()
         tid = int(tensor_id) or self._next_tensor_id()
         ver = int(version) or 1
-        ok, msg, _lease, _slot, _lo, _hi = self._agent.evict(
+        # bf16 payloads may travel zbf16-coded (lossless; the agent decides per object)
+        hint = 1 if src.dtype == torch.bfloat16 else 0
+        ok, msg, _lease, _slot, _lo, _hi, coded = self._agent.evict(
             src.data_ptr(), nbytes, _stream_handle(stream, src.device), bool(destructive), tid, ver, name or "",
-            cb, bool(wait))
+            cb, bool(wait), hint)
         if not ok:
             raise RuntimeError(f"evict failed: {msg}")
-        return OffloadHandle(self, tid, ver, name, shape, stride, dtype, tensor.device, nbytes)
+        h = OffloadHandle(self, tid, ver, name, shape, stride, dtype, tensor.device, nbytes)
+        h.coded = bool(coded)
+        return h
 
     def evict(self, tensor, name=None, stream=None, invalidate="set_empty", wait=False, allow_views=False,
               unsafe_autograd=False, compact=False, tensor_id: int = 0, version: int = 0) -> OffloadHandle:
