@@ -16,9 +16,10 @@
 //                      lane's vectors k*256 + t (k = 0..15), then by element
 //                      within the 16-byte vector
 //
-// with n = len / 2 elements. ebase is chosen per chunk as the start of the
-// 15-binade window that holds the most elements. A coded chunk must fit in
-// its own raw length (so every byte of an object stays inside [0, nbytes)
+// with n = len / 2 elements. The window is anchored at the top: ebase =
+// max(emax - 14, 0) for the chunk's largest exponent emax, so only values
+// more than 14 binades below the chunk's largest escape (for N(0, s) data a
+// few per chunk). A coded chunk must fit in its own raw length (so every byte of an object stays inside [0, nbytes)
 // of its pinned run and tiers that copy nbytes keep it intact). A final
 // chunk shorter than kRawTail bytes is stored raw (decided from nbytes
 // alone). An object is coded only when every other chunk fits; the format is
@@ -75,22 +76,7 @@ SSH_HD bool eligible(uint64_t nbytes) { return nbytes >= kRawTail && nbytes % 16
 
 // ---- host reference implementation (tests, tools) -------------------------
 
-// Best window start and the escape count it leaves, from a 256-bin histogram.
-inline void best_window(const uint32_t* hist, uint32_t total, uint32_t* ebase, uint32_t* n_esc) {
-    uint32_t best = 0, best_w = 0, s = 0;
-    for (uint32_t e = 0; e < kWindow; ++e) s += hist[e];
-    best = s;
-    for (uint32_t w = 1; w + kWindow <= 256; ++w) {
-        s += hist[w + kWindow - 1];
-        s -= hist[w - 1];
-        if (s > best) {
-            best = s;
-            best_w = w;
-        }
-    }
-    *ebase = best_w;
-    *n_esc = total - best;
-}
+SSH_HD uint32_t window_base(uint32_t emax) { return emax >= kWindow - 1 ? emax - (kWindow - 1) : 0; }
 
 // Elements of a chunk in escape order: lane t, vector k*256+t, element j.
 template <class F>
@@ -110,10 +96,11 @@ inline uint32_t encode_chunk(const uint8_t* src, uint32_t len, uint8_t* out) {
     const uint32_t n = len / 2;
     std::vector<uint16_t> h(n);
     std::memcpy(h.data(), src, len);
-    uint32_t hist[256] = {0};
-    for (uint32_t i = 0; i < n; ++i) hist[exponent(h[i])]++;
-    uint32_t ebase, n_esc;
-    best_window(hist, n, &ebase, &n_esc);
+    uint32_t emax = 0;
+    for (uint32_t i = 0; i < n; ++i) emax = exponent(h[i]) > emax ? exponent(h[i]) : emax;
+    const uint32_t ebase = window_base(emax);
+    uint32_t n_esc = 0;
+    for (uint32_t i = 0; i < n; ++i) n_esc += code_of(exponent(h[i]), ebase) == kEscape;
     const uint32_t total = coded_len(len, n_esc);
     if (total > len) return 0;
     Header hd{kTag, 1, uint8_t(ebase), n_esc, len, total};

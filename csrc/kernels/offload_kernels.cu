@@ -20,6 +20,8 @@
 #include <cuda_fp8.h>
 
 #include <atomic>
+#include <mutex>
+#include <set>
 
 #include "kernels.h"
 #include "ofld/chunk_hash.h"
@@ -300,14 +302,14 @@ __device__ __forceinline__ uint32_t half_of(const uint4& v, int j) {
     return (j & 1) ? (w >> 16) : (w & 0xFFFFu);
 }
 
-// Pre-pass: per chunk, the exponent histogram, the best 15-binade window
-// (ebase) and whether the coded chunk fits in its raw length. Any chunk that
-// does not fit sets *fail: the object is then moved uncoded.
+// Pre-pass: per chunk, the largest exponent (window base = emax - 14) and
+// whether the coded chunk fits in its raw length. Any chunk that does not fit
+// sets *fail: the object is then moved uncoded. Two register passes per
+// chunk, so the pass runs at HBM rate.
 __global__ void __launch_bounds__(kThreads, 3)
     k_zscan(const uint8_t* __restrict__ src, uint64_t nbytes, uint8_t* __restrict__ ebase_out, uint32_t* fail) {
-    __shared__ uint32_t hist[256];
-    __shared__ uint32_t best[kThreads / 32];
-    const uint32_t t = threadIdx.x, lane = t & 31;
+    __shared__ uint32_t red[kThreads / 32];
+    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
     for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
         const uint64_t base = c * kChunk;
@@ -317,51 +319,63 @@ __global__ void __launch_bounds__(kThreads, 3)
             continue;  // uniform per chunk
         }
         const uint32_t nvec = len / 16;
-        hist[t] = 0;
-        __syncthreads();
-#pragma unroll 4
+        uint4 v[kVecs];
+#pragma unroll
         for (int k = 0; k < kVecs; ++k) {
             const uint32_t vi = uint32_t(k) * kThreads + t;
-            const bool valid = vi < nvec;
-            const uint4 v = valid ? ld_once(src + base + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const uint32_t e = valid ? zbf16::exponent(uint16_t(half_of(v, j))) : 256u;
-                const uint32_t peers = __match_any_sync(0xffffffffu, e);
-                if (e < 256u && lane == uint32_t(__ffs(peers) - 1)) atomicAdd(&hist[e], uint32_t(__popc(peers)));
-            }
+            v[k] = vi < nvec ? ld_once(src + base + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
         }
+        // bf16 bit patterns with the sign cleared order like their magnitudes
+        uint32_t m = 0;
+        auto hmax = [](uint32_t w) { return max(w & 0x7FFFu, (w >> 16) & 0x7FFFu); };
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k)
+            m = max(m, max(max(hmax(v[k].x), hmax(v[k].y)), max(hmax(v[k].z), hmax(v[k].w))));
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) red[warp] = m;
         __syncthreads();
-        // window sums; argmax with ties to the lowest start: (sum << 8) | (255 - w)
-        uint32_t key = 0;
-        if (t + zbf16::kWindow <= 256) {
-            uint32_t sum = 0;
+        uint32_t mm = 0;
 #pragma unroll
-            for (uint32_t e = 0; e < zbf16::kWindow; ++e) sum += hist[t + e];
-            key = (sum << 8) | (255u - t);
+        for (int w = 0; w < kThreads / 32; ++w) mm = max(mm, red[w]);
+        const uint32_t eb = zbf16::window_base(zbf16::exponent(uint16_t(mm)));
+        uint32_t cnt = 0;
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            if (vi < nvec)
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    cnt += zbf16::code_of(zbf16::exponent(uint16_t(half_of(v[k], j))), eb) == zbf16::kEscape;
         }
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
-        if (lane == 0) best[t >> 5] = key;
+        for (int o = 16; o >= 1; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+        __syncthreads();  // everyone has read red[] (the max)
+        if (lane == 0) red[warp] = cnt;
         __syncthreads();
         if (t == 0) {
-            uint32_t m = 0;
+            uint32_t esc = 0;
 #pragma unroll
-            for (int w = 0; w < kThreads / 32; ++w) m = max(m, best[w]);
-            const uint32_t n = len / 2, covered = m >> 8, eb = 255u - (m & 0xFFu);
+            for (int w = 0; w < kThreads / 32; ++w) esc += red[w];
             ebase_out[c] = uint8_t(eb);
-            if (zbf16::coded_len(len, n - covered) > len) atomicOr(fail, 1u);
+            if (zbf16::coded_len(len, esc) > len) atomicOr(fail, 1u);
         }
-        __syncthreads();  // hist / best are reused by the next chunk
+        __syncthreads();  // red[] is reused by the next chunk
     }
 }
 
-// K1 with coding: hash the raw bytes and write each chunk coded (or raw by
-// rule) to the host-mapped run. Requires 16-byte aligned src/dst and
-// nbytes % 16 == 0 (zbf16::eligible).
+// Shared-memory stage of one coded chunk: PCIe moves it with full 16-byte
+// vector accesses (512 bytes per warp instruction), like the uncoded path;
+// the planes' 8- and 4-byte pieces are only ever touched in shared memory.
+constexpr uint32_t kZStage = zbf16::kChunk;
+
+// K1 with coding: hash the raw bytes, code each chunk into shared memory
+// (or keep it raw by rule) and stream it to the host-mapped run. Requires
+// 16-byte aligned src/dst and nbytes % 16 == 0 (zbf16::eligible).
 __global__ void __launch_bounds__(kThreads, 2)
     k_evict_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
               const uint8_t* __restrict__ ebase, uint64_t* __restrict__ digests, int pol) {
+    extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint64_t red[kThreads / 32];
     __shared__ uint32_t sc[kThreads / 32];
     const uint32_t t = threadIdx.x;
@@ -398,13 +412,11 @@ __global__ void __launch_bounds__(kThreads, 2)
             uint32_t total;
             uint32_t off = block_excl_scan(cnt, sc, &total);
             const uint32_t n = len / 2;
-            uint8_t* out = dst + base;
-            if (t == 0) {
-                const uint4 hd = make_uint4(uint32_t(zbf16::kTag) | (1u << 16) | (eb << 24), total, len,
-                                            zbf16::coded_len(len, total));
-                st_policy(out, hd, pol);
-            }
-            uint8_t* esc = out + zbf16::kHeader + n + n / 2;
+            const uint32_t comp = zbf16::coded_len(len, total);
+            if (t == 0)
+                *reinterpret_cast<uint4*>(zbuf) =
+                    make_uint4(uint32_t(zbf16::kTag) | (1u << 16) | (eb << 24), total, len, comp);
+            uint8_t* esc = zbuf + zbf16::kHeader + n + n / 2;
 #pragma unroll
             for (int k = 0; k < kVecs; ++k) {
                 const uint32_t vi = uint32_t(k) * kThreads + t;
@@ -421,25 +433,50 @@ __global__ void __launch_bounds__(kThreads, 2)
                     codes |= cd << (4 * j);
                     if (cd == zbf16::kEscape) esc[off++] = uint8_t(e);
                 }
-                asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(out + zbf16::kHeader + uint64_t(vi) * 8),
-                             "r"(lo0), "r"(lo1)
-                             : "memory");
-                asm volatile("st.global.cs.u32 [%0], %1;" ::"l"(out + zbf16::kHeader + n + uint64_t(vi) * 4), "r"(codes)
-                             : "memory");
+                *reinterpret_cast<uint2*>(zbuf + zbf16::kHeader + vi * 8) = make_uint2(lo0, lo1);
+                *reinterpret_cast<uint32_t*>(zbuf + zbf16::kHeader + n + vi * 4) = codes;
             }
+            __syncthreads();
+            uint8_t* out = dst + base;
+            const uint32_t nout = (comp + 15) / 16;  // <= len / 16: coded chunks fit their raw length
+            for (uint32_t i = t; i < nout; i += kThreads)
+                st_policy(out + uint64_t(i) * 16, *reinterpret_cast<const uint4*>(zbuf + i * 16), pol);
         }
-        uint64_t root = tree_fold(ssh::lane_digest(L, t), red);
+        uint64_t root = tree_fold(ssh::lane_digest(L, t), red);  // also orders zbuf reuse
         if (t == 0 && digests) digests[c] = ssh::chunk_finish(root, len);
     }
 }
 
-// K2 with decoding: read each coded chunk from the host-mapped run (16 bytes
-// of header, 12 bytes per 8 elements, the chunk's escapes), rebuild the bf16
-// vectors in registers and continue as K2 (verify, cast, store).
+// Loads [lo, hi) of a host-mapped chunk into the stage with 16-byte vectors,
+// up to 13 in flight per thread (one full coded chunk plus 1 KiB of escapes).
+__device__ __forceinline__ void stage_in(const uint8_t* in, uint8_t* zbuf, uint32_t lo, uint32_t hi, int pol) {
+    constexpr int kPer = 13;
+    const uint32_t t = threadIdx.x;
+    const uint32_t v0 = lo / 16, v1 = (hi + 15) / 16;
+    for (uint32_t b = v0; b < v1; b += kPer * kThreads) {
+        uint4 r[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const uint32_t i = b + uint32_t(k) * kThreads + t;
+            r[k] = i < v1 ? ld_policy(in + uint64_t(i) * 16, pol) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const uint32_t i = b + uint32_t(k) * kThreads + t;
+            if (i < v1) *reinterpret_cast<uint4*>(zbuf + i * 16) = r[k];
+        }
+    }
+}
+
+// K2 with decoding: bring each coded chunk into shared memory with 16-byte
+// loads (header, planes and, speculatively, 1 KiB of escapes in one round
+// trip; the rest of the escapes in a second one when present), rebuild the
+// bf16 vectors and continue as K2 (verify, cast, store).
 template <bool VERIFY, int CAST>
 __global__ void __launch_bounds__(kThreads, 2)
     k_restore_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
                 float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, int pol) {
+    extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint64_t red[kThreads / 32];
     __shared__ uint32_t sc[kThreads / 32];
     const uint32_t t = threadIdx.x;
@@ -458,36 +495,36 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
         } else {
             const uint32_t n = len / 2;
-            const uint4 hd = ld_policy(in, pol);  // every thread: one broadcast request per warp
-            uint2 lo[kVecs];
-            uint32_t cd[kVecs];
-#pragma unroll
-            for (int k = 0; k < kVecs; ++k) {
-                const uint32_t vi = uint32_t(k) * kThreads + t;
-                if (vi < nvec) {
-                    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
-                                 : "=r"(lo[k].x), "=r"(lo[k].y)
-                                 : "l"(in + zbf16::kHeader + uint64_t(vi) * 8));
-                    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];"
-                                 : "=r"(cd[k])
-                                 : "l"(in + zbf16::kHeader + n + uint64_t(vi) * 4));
-                } else {
-                    lo[k] = make_uint2(0, 0);
-                    cd[k] = 0;
-                }
+            const uint32_t fixed = zbf16::kHeader + n + n / 2;
+            const uint32_t spec = min(len, fixed + 1024u);
+            stage_in(in, zbuf, 0, spec, pol);
+            __syncthreads();
+            const uint4 hd = *reinterpret_cast<const uint4*>(zbuf);
+            const uint32_t comp = min(hd.w, len);
+            if (comp > spec) {  // uniform: every thread read the same header
+                stage_in(in, zbuf, spec / 16 * 16, comp, pol);
+                __syncthreads();
             }
             const uint32_t eb = hd.x >> 24;
+            uint2 lo[kVecs];
+            uint32_t cd[kVecs];
             uint32_t cnt = 0;
 #pragma unroll
             for (int k = 0; k < kVecs; ++k) {
                 const uint32_t vi = uint32_t(k) * kThreads + t;
-                if (vi < nvec)
+                if (vi < nvec) {
+                    lo[k] = *reinterpret_cast<const uint2*>(zbuf + zbf16::kHeader + vi * 8);
+                    cd[k] = *reinterpret_cast<const uint32_t*>(zbuf + zbf16::kHeader + n + vi * 4);
+                } else {
+                    lo[k] = make_uint2(0, 0);
+                    cd[k] = 0;
+                }
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) cnt += ((cd[k] >> (4 * j)) & 15u) == zbf16::kEscape;
+                for (int j = 0; j < 8; ++j) cnt += ((cd[k] >> (4 * j)) & 15u) == zbf16::kEscape;
             }
             uint32_t total;
             uint32_t off = block_excl_scan(cnt, sc, &total);
-            const uint8_t* esc = in + zbf16::kHeader + n + n / 2;
+            const uint8_t* esc = zbuf + fixed;
 #pragma unroll
             for (int k = 0; k < kVecs; ++k) {
                 uint32_t w[4];
@@ -503,6 +540,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 }
                 v[k] = make_uint4(w[0], w[1], w[2], w[3]);
             }
+            __syncthreads();  // the stage is refilled by the next chunk
         }
         ssh::Lane L = ssh::lane_init(t);
 #pragma unroll
@@ -617,6 +655,21 @@ __global__ void __launch_bounds__(kThreads) k_quant_fp8(const uint4* __restrict_
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Opt a coded-path kernel into the 64 KiB dynamic shared-memory stage, once
+// per (kernel, device) per process.
+cudaError_t allow_stage(const void* fn, int id) {
+    static std::mutex mu;
+    static std::set<std::pair<int, int>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> g(mu);
+    if (done.count({id, dev})) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kZStage));
+    if (e == cudaSuccess) done.insert({id, dev});
+    return e;
+}
+
 int grid_for(uint64_t nbytes, int ctas, int dflt) {
     uint64_t chunks = (nbytes + kChunk - 1) / kChunk;
     int g = ctas > 0 ? ctas : dflt;
@@ -723,9 +776,11 @@ cudaError_t zscan(const void* src, uint64_t nbytes, uint8_t* ebase, uint32_t* fa
 cudaError_t evict_z(const void* src, void* dst, uint64_t nbytes, const uint8_t* ebase, uint64_t* digests,
                     cudaStream_t s, int ctas) {
     if (!zbf16::eligible(nbytes) || !aligned16(src) || !aligned16(dst) || !ebase) return cudaErrorInvalidValue;
+    cudaError_t e = allow_stage(reinterpret_cast<const void*>(&k_evict_z), 0);
+    if (e != cudaSuccess) return e;
     const int g = grid_for(nbytes, ctas, 48);
-    k_evict_z<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nbytes, ebase,
-                                     digests, g_policy.load(std::memory_order_relaxed));
+    k_evict_z<<<g, kThreads, kZStage, s>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nbytes,
+                                           ebase, digests, g_policy.load(std::memory_order_relaxed));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -739,22 +794,33 @@ cudaError_t restore_z(const void* src, void* dst, uint64_t nbytes, Cast cast, fl
     auto S = static_cast<const uint8_t*>(src);
     auto D = static_cast<uint8_t*>(dst);
     const bool v = expect != nullptr;
+    const void* fn = nullptr;
+    int id = 0;
     switch (cast) {
-        case Cast::kNone:
-            if (v) k_restore_z<true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
-            else k_restore_z<false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
-            break;
+        case Cast::kNone: fn = v ? (const void*)&k_restore_z<true, 0> : (const void*)&k_restore_z<false, 0>; id = v ? 1 : 2; break;
         case Cast::kBf16ToFp8Block128:
             if (!scales) return cudaErrorInvalidValue;
-            if (v) k_restore_z<true, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, expect, mismatch, p);
-            else k_restore_z<false, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, nullptr, nullptr, p);
+            fn = v ? (const void*)&k_restore_z<true, 1> : (const void*)&k_restore_z<false, 1>;
+            id = v ? 3 : 4;
             break;
-        case Cast::kBf16ToFp32:
-            if (v) k_restore_z<true, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
-            else k_restore_z<false, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+        case Cast::kBf16ToFp32: fn = v ? (const void*)&k_restore_z<true, 3> : (const void*)&k_restore_z<false, 3>; id = v ? 5 : 6; break;
+        default: return cudaErrorInvalidValue;  // coded objects are bf16
+    }
+    cudaError_t e = allow_stage(fn, id);
+    if (e != cudaSuccess) return e;
+    switch (cast) {
+        case Cast::kNone:
+            if (v) k_restore_z<true, 0><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
+            else k_restore_z<false, 0><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+            break;
+        case Cast::kBf16ToFp8Block128:
+            if (v) k_restore_z<true, 1><<<g, kThreads, kZStage, s>>>(S, D, nbytes, scales, expect, mismatch, p);
+            else k_restore_z<false, 1><<<g, kThreads, kZStage, s>>>(S, D, nbytes, scales, nullptr, nullptr, p);
             break;
         default:
-            return cudaErrorInvalidValue;  // coded objects are bf16
+            if (v) k_restore_z<true, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
+            else k_restore_z<false, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+            break;
     }
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();

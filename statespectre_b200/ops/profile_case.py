@@ -23,7 +23,8 @@ from .._native import native
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True, choices=["evict", "restore", "restore_fp8", "hash", "hash_stream",
-                                                          "verify", "push", "push_fp8"])
+                                                          "verify", "push", "push_fp8", "zscan", "evict_z",
+                                                          "restore_z"])
     ap.add_argument("--mb", type=int, default=512)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--ctas", type=int, default=0)
@@ -45,6 +46,10 @@ def main():
     scales = torch.empty(n // 256, dtype=torch.float32, device=dev)
     C.k_evict_hash(x.data_ptr(), host.data_ptr(), n, dig.data_ptr(), s, a.ctas)  # fill the host copy
     err = torch.zeros(1, dtype=torch.int32, device=dev)
+    zeb = torch.zeros((n + 65535) // 65536, dtype=torch.uint8, device=dev)
+    if a.kernel in ("zscan", "evict_z", "restore_z"):  # zbf16: window bases, then the coded host copy
+        C.k_zscan(x.data_ptr(), n, zeb.data_ptr(), err.data_ptr(), s, 0)
+        C.k_evict_z(x.data_ptr(), host.data_ptr(), n, zeb.data_ptr(), dig.data_ptr(), s, a.ctas)
     pusher = None
     if a.kernel.startswith("push"):
         from ..parallel.weight_sync import WeightLayout, WeightPusher
@@ -70,6 +75,12 @@ def main():
             C.k_restore_cast(host.data_ptr(), out.data_ptr(), n, 1, scales.data_ptr(), 0, 0, s, a.ctas)
         elif a.kernel == "hash":
             C.k_hash_device(x.data_ptr(), n, dig.data_ptr(), s, a.ctas)
+        elif a.kernel == "zscan":
+            C.k_zscan(x.data_ptr(), n, zeb.data_ptr(), err.data_ptr(), s, 0)
+        elif a.kernel == "evict_z":
+            C.k_evict_z(x.data_ptr(), host.data_ptr(), n, zeb.data_ptr(), dig.data_ptr(), s, a.ctas)
+        elif a.kernel == "restore_z":
+            C.k_restore_z(host.data_ptr(), out.data_ptr(), n, 0, 0, 0, 0, s, a.ctas)
         elif a.kernel == "hash_stream":
             C.k_hash_stream(x.data_ptr(), n, dig.data_ptr(), err.data_ptr(), s, a.ctas)
         elif pusher is not None:
