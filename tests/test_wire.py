@@ -111,3 +111,10 @@ def test_op_names_cover_all_opcodes():
     C = native()
     for op in _wire.OPS:
         assert C.op_name(op) != "Unknown"
+
+
+def test_proto_schema_docs_are_current():
+    """rpc/*.proto are generated from the wire schema and must match it."""
+    from statespectre_b200 import _proto
+
+    assert _proto.main(["--check"]) == 0, "run: python -m statespectre_b200._proto"
