@@ -59,8 +59,9 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=0, help="default: same as --steps")
     p.add_argument("--out", default="")
     # --workload weight_sync: in-box RL weight sync (trainer half -> rollout half of the GPUs)
-    p.add_argument("--workload", default="evict_restore", choices=["evict_restore", "weight_sync"])
-    p.add_argument("--model", default="qwen2.5-32b")
+    p.add_argument("--workload", default="evict_restore",
+                   choices=["evict_restore", "weight_sync", "sweep", "kv_cache", "dp_dedup"])
+    p.add_argument("--model", default="", help="weight_sync: qwen2.5-32b (default); dp_dedup: llama-3-8b (default)")
     p.add_argument("--layers", type=int, default=0, help="weight_sync: layer count override (0 = the model's)")
     p.add_argument("--push-mode", default="bf16", choices=["bf16", "fp8"])
     p.add_argument("--persist", type=int, default=1, help="weight_sync: seal every version in offloadd")
@@ -69,6 +70,13 @@ def parse():
     p.add_argument("--delta-std", type=float, default=1e-3)
     p.add_argument("--hint", type=int, default=0,
                    help="weight_sync: pass the changed-tensor list instead of hashing every tensor")
+    p.add_argument("--max-size-mb", type=int, default=8192, help="sweep: largest tensor")
+    p.add_argument("--kv-gb", type=float, default=40.0, help="kv_cache: KV cache bytes per GPU")
+    p.add_argument("--evict-fraction", type=float, default=0.5, help="kv_cache: blocks moved per iteration")
+    p.add_argument("--kv-batch", type=int, default=256, help="kv_cache: blocks per reservation round trip")
+    p.add_argument("--pinned-gb", type=int, default=0, help="kv_cache: pinned window per GPU (0 = fits the set)")
+    p.add_argument("--nvme-dir", default="", help="dp_dedup: NVMe spill directory")
+    p.add_argument("--spill-timeout", type=float, default=600.0, help="dp_dedup: seconds to wait for the spill")
     return p.parse_args()
 
 
@@ -79,8 +87,15 @@ def main():
         print(json.dumps(line), flush=True)
         return 0
 
-    if args.workload == "weight_sync":
-        from statespectre_b200.parallel.weight_sync_bench import run
+    if args.workload != "evict_restore":
+        if args.workload == "weight_sync":
+            from statespectre_b200.parallel.weight_sync_bench import run
+        elif args.workload == "sweep":
+            from statespectre_b200.benchmarks.sweep import run
+        elif args.workload == "kv_cache":
+            from statespectre_b200.benchmarks.kv_cache import run
+        else:
+            from statespectre_b200.benchmarks.dp_dedup import run
 
         out = run(args, METRIC)
         if out is not None:

@@ -52,7 +52,7 @@ def run(args, metric: str) -> dict:
     tp = world // 2
     trainer = rank < tp
     tp_rank = rank % tp
-    spec = MODELS.get(args.model, QWEN2_5_32B)
+    spec = MODELS.get(args.model or "qwen2.5-32b", QWEN2_5_32B)
     shapes = param_shapes(spec, tp_rank, tp, layers=args.layers or None)
     shard_bytes = num_params(shapes) * 2
     mode = args.push_mode

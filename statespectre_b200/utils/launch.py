@@ -15,7 +15,8 @@ from .topology import daemon_yaml, gpu_numa_nodes
 
 
 def start_node_daemon(local_rank: int, n_local: int, window_gb, run_dir: str, barrier=None,
-                      n_devices: Optional[int] = None, extra_yaml: str = "", slot_mb: int = 64) -> Tuple[str, object]:
+                      n_devices: Optional[int] = None, extra_yaml: str = "", slot_mb: int = 64,
+                      **yaml_kw) -> Tuple[str, object]:
     """Returns (socket path, daemon handle or None on non-zero local ranks).
 
     ``window_gb`` is one size for every GPU or a list with one size per GPU."""
@@ -30,7 +31,7 @@ def start_node_daemon(local_rank: int, n_local: int, window_gb, run_dir: str, ba
         cfg = os.path.join(run_dir, "offloadd.yaml")
         with open(cfg, "w") as f:
             f.write(daemon_yaml(sock, gpu_numa_nodes(max(n_local, n_devices or n_local)), window_gb,
-                                slot_mb=slot_mb, extra=extra_yaml))
+                                slot_mb=slot_mb, extra=extra_yaml, **yaml_kw))
         daemon = launch_daemon(sock, config=cfg, log_path=os.path.join(run_dir, "offloadd.log"))
     if barrier is not None:
         barrier()

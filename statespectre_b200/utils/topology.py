@@ -31,7 +31,8 @@ def gpu_numa_nodes(num_gpus: int) -> List[int]:
 
 
 def daemon_yaml(socket_path: str, gpu_nodes: List[int], window_gb_per_gpu, slot_mb: int = 64,
-                overflow_gb: int = 1, drain_on_complete: bool = False, extra: str = "") -> str:
+                overflow_gb: int = 1, drain_on_complete: bool = False, extra: str = "",
+                drain_target: str = "pageable", nvme_dir: str = "") -> str:
     """A daemon config with one arena per NUMA node holding a window per GPU.
 
     ``window_gb_per_gpu`` is one size for every GPU or a list (one per GPU;
@@ -51,8 +52,12 @@ def daemon_yaml(socket_path: str, gpu_nodes: List[int], window_gb_per_gpu, slot_
                   "      gpu_windows:"]
         for g in gpus:
             lines += [f"        - gpu: {g}", f"          size_gb: {sizes[g]}"]
-    lines += ["drain_policy:", "  target_tier: pageable", f"  drain_on_d2h_complete: {str(drain_on_complete).lower()}",
-              "nvme:", "  enabled: false"]
+    lines += ["drain_policy:", f"  target_tier: {drain_target}",
+              f"  drain_on_d2h_complete: {str(drain_on_complete).lower()}", "nvme:"]
+    if nvme_dir:
+        lines += ["  enabled: true", f"  path: {nvme_dir}", "  io_engine: io_uring", "  direct_io: true"]
+    else:
+        lines += ["  enabled: false"]
     return "\n".join(lines) + "\n" + extra
 
 
