@@ -493,22 +493,33 @@ struct Agent::Impl {
     // every chunk fits coded. Waits for the stream (the decision precedes the
     // reservation, whose flags record the format).
     bool zscan(uint64_t src, uint64_t nbytes, cudaStream_t s, PinnedPool::Buf* out) {
+        zscan_launch(src, nbytes, s, out);
+        stream_wait(s);
+        return zscan_result(nbytes, out);
+    }
+    // The pre-pass in two halves, so a batch launches every item's scan and
+    // waits once.
+    void zscan_launch(uint64_t src, uint64_t nbytes, cudaStream_t s, PinnedPool::Buf* out) {
         const uint64_t nch = kern::digest_count(nbytes);
         const uint64_t flag_off = (nch + 15) / 16 * 16;
         *out = pool.get(flag_off + 16);
-        auto* fail_host = reinterpret_cast<volatile uint32_t*>(static_cast<char*>(out->host) + flag_off);
-        *fail_host = 0;
+        *reinterpret_cast<volatile uint32_t*>(static_cast<char*>(out->host) + flag_off) = 0;
         CUDA_OK(kern::zscan(reinterpret_cast<const void*>(src), nbytes, static_cast<uint8_t*>(out->dev),
                             reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off), s, 0));
+    }
+    bool zscan_result(uint64_t nbytes, PinnedPool::Buf* out) {
+        const uint64_t flag_off = (kern::digest_count(nbytes) + 15) / 16 * 16;
+        if (*reinterpret_cast<volatile uint32_t*>(static_cast<char*>(out->host) + flag_off) == 0) return true;
+        pool.put(*out);
+        *out = PinnedPool::Buf{};
+        return false;
+    }
+    void stream_wait(cudaStream_t s) {
         cudaEvent_t ev;
         CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
         CUDA_OK(cudaEventRecord(ev, s));
         CUDA_OK(cudaEventSynchronize(ev));
         cudaEventDestroy(ev);
-        if (*fail_host == 0) return true;
-        pool.put(*out);
-        *out = PinnedPool::Buf{};
-        return false;
     }
 
     bool want_z(uint64_t ptr, uint64_t nbytes, uint32_t fmt_hint) const {
@@ -666,7 +677,23 @@ std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items,
     BatchRequestOffloadRequest br;
     br.rank_id = D.opt.rank_id;
     br.rank_epoch = D.epoch;
-    for (const BatchItem& it : items) {
+    cudaStream_t s = D.stream_of(stream);
+    // zbf16 pre-pass of every eligible item, one wait for the batch
+    std::vector<PinnedPool::Buf> zb(items.size());
+    std::vector<char> z(items.size(), 0);
+    bool any_z = false;
+    for (size_t i = 0; i < items.size(); ++i)
+        if (D.want_z(items[i].ptr, items[i].nbytes, items[i].fmt_hint)) {
+            D.zscan_launch(items[i].ptr, items[i].nbytes, s, &zb[i]);
+            z[i] = any_z = true;
+        }
+    if (any_z) {
+        D.stream_wait(s);
+        for (size_t i = 0; i < items.size(); ++i)
+            if (z[i]) z[i] = D.zscan_result(items[i].nbytes, &zb[i]);
+    }
+    for (size_t i = 0; i < items.size(); ++i) {
+        const BatchItem& it = items[i];
         RequestOffloadRequest rq;
         rq.tensor_id = it.tensor_id;
         rq.version = it.version;
@@ -674,11 +701,10 @@ std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items,
         rq.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
         rq.numa_node = uint32_t(D.numa);
         rq.alignment = 256;
-        rq.flags = OFLD_FLAG_ALLOW_OVERFLOW | OFLD_FLAG_SUBMIT_ON_GRANT;
+        rq.flags = OFLD_FLAG_ALLOW_OVERFLOW | OFLD_FLAG_SUBMIT_ON_GRANT | (z[i] ? OFLD_FLAG_FORMAT_ZBF16 : 0);
         br.items.push_back(rq);
     }
     BatchRequestOffloadResponse resp = D.call<Op::kBatchRequestOffload>(br);
-    cudaStream_t s = D.stream_of(stream);
     std::vector<Impl::Pending> launched;
     for (size_t i = 0; i < items.size() && i < resp.grants.size(); ++i) {
         const RequestOffloadResponse& g = resp.grants[i];
@@ -688,11 +714,17 @@ std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items,
         t.nbytes = items[i].nbytes;
         if (!g.ok || g.blocked) {
             t.message = g.ok ? "offload blocked (pinned pressure)" : g.message;
+            D.pool.put(zb[i]);
+            zb[i] = PinnedPool::Buf{};
             continue;
         }
         char *host = nullptr, *dev = nullptr;
         D.resolve(g.arena_id, g.arena_offset, items[i].nbytes, &host, &dev);
         Impl::Pending p;
+        p.z = z[i] != 0;
+        p.zb = zb[i];
+        zb[i] = PinnedPool::Buf{};
+        t.coded = p.z;
         p.lease = g.lease_id;
         p.tid = items[i].tensor_id;
         p.ver = items[i].version;
@@ -710,6 +742,7 @@ std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items,
         t.slot_id = g.slot_id;
         launched.push_back(std::move(p));
     }
+    for (PinnedPool::Buf& b : zb) D.pool.put(b);  // items without a grant
     // Every launch recorded its own event; the last one covers the batch on
     // this stream, so a waiting caller synchronizes once.
     if (wait && D.gpu && !launched.empty()) CUDA_OK(cudaEventSynchronize(launched.back().ev));

@@ -98,6 +98,7 @@ struct AgentStats {
 
 struct BatchItem {
     uint64_t ptr = 0, nbytes = 0, tensor_id = 0, version = 0;
+    uint32_t fmt_hint = 0;  // evict_batch: kFmtBf16 allows zbf16 coding
 };
 
 class Agent {

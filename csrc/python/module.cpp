@@ -266,17 +266,20 @@ PYBIND11_MODULE(_C, m) {
             py::arg("version"), py::arg("name"), py::arg("callback"), py::arg("wait"), py::arg("fmt_hint") = 0)
         .def(
             "evict_batch",
-            [](PyAgent& self, std::vector<std::tuple<uint64_t, uint64_t, uint64_t, uint64_t>> items, uint64_t stream,
-               bool wait) {
+            [](PyAgent& self, std::vector<std::vector<uint64_t>> items, uint64_t stream, bool wait) {
+                // items: (ptr, nbytes, tensor_id, version[, fmt_hint])
                 std::vector<BatchItem> b;
-                for (auto& t : items) b.push_back(BatchItem{std::get<0>(t), std::get<1>(t), std::get<2>(t), std::get<3>(t)});
+                for (auto& t : items) {
+                    if (t.size() < 4) throw std::invalid_argument("evict_batch item needs 4 or 5 fields");
+                    b.push_back(BatchItem{t[0], t[1], t[2], t[3], t.size() > 4 ? uint32_t(t[4]) : 0u});
+                }
                 std::vector<EvictTicket> r;
                 {
                     py::gil_scoped_release nogil;
                     r = self.ag().evict_batch(b, stream, wait);
                 }
                 py::list out;
-                for (auto& t : r) out.append(py::make_tuple(t.ok, t.message));
+                for (auto& t : r) out.append(py::make_tuple(t.ok, t.message, t.coded));
                 return out;
             })
         .def(

@@ -690,14 +690,17 @@ class Off:
                 raise RuntimeError("evict_batch: tensors must be contiguous")
         ids = [self._next_tensor_id() for _ in tensors]
         vers = list(versions) if versions is not None else [1] * len(tensors)
-        items = [(t.data_ptr(), t.numel() * t.element_size(), i, v) for t, i, v in zip(tensors, ids, vers)]
+        items = [(t.data_ptr(), t.numel() * t.element_size(), i, v, 1 if t.dtype == torch.bfloat16 else 0)
+                 for t, i, v in zip(tensors, ids, vers)]
         res = self._agent.evict_batch(items, _stream_handle(stream, tensors[0].device), bool(wait))
         out = []
-        for t, (ok, msg), i, v in zip(tensors, res, ids, vers):
+        for t, (ok, msg, coded), i, v in zip(tensors, res, ids, vers):
             if not ok:
                 raise RuntimeError(f"evict_batch failed for tensor {i}: {msg}")
-            out.append(OffloadHandle(self, i, v, None, tuple(t.shape), tuple(t.stride()), t.dtype, t.device,
-                                     t.numel() * t.element_size()))
+            h = OffloadHandle(self, i, v, None, tuple(t.shape), tuple(t.stride()), t.dtype, t.device,
+                              t.numel() * t.element_size())
+            h.coded = bool(coded)
+            out.append(h)
         return out
 
     def restore_batch(self, handles: Sequence[OffloadHandle], dsts: Optional[Sequence[torch.Tensor]] = None,

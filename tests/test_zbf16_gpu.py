@@ -170,3 +170,19 @@ def test_compress_off_moves_uncoded(sock_path):
             assert not h.coded and torch.equal(h.restore(), x)
     finally:
         d.stop()
+
+
+def test_batch_evict_codes_kv_blocks(zsession):
+    off = zsession
+    cache = _case(16 * (4 << 20), "normal", seed=21).view(16, -1)  # 16 KV blocks of 4 MiB
+    ref = cache.clone()
+    blocks = [cache[i] for i in range(0, 16, 2)]
+    hs = off.evict_batch(blocks)
+    assert all(h.coded for h in hs)
+    for b in blocks:
+        b.zero_()
+    off.restore_batch(hs, blocks)
+    torch.cuda.synchronize()
+    assert torch.equal(cache, ref)
+    for h in hs:
+        h.discard()
