@@ -134,6 +134,9 @@ struct Agent::Impl {
         uint64_t ndig = 0;
         PinnedPool::Buf zb;              // zbf16 window bases (one byte per chunk) + pre-pass flag
         bool z = false;
+        // Batched launches: every item of the batch shares one event and the
+        // job table; the last item to finish releases both.
+        std::shared_ptr<void> batch_keep;
     };
     std::mutex inflight_mu;
     std::list<Pending> inflight;
@@ -423,9 +426,28 @@ struct Agent::Impl {
             pool.put(p.exp);
             if (p.cb) p.cb();
         }
-        if (p.ev) cudaEventDestroy(p.ev);
+        if (p.batch_keep) p.batch_keep.reset();  // shared event: the keep owns it
+        else if (p.ev) cudaEventDestroy(p.ev);
         p.ev = nullptr;
         tab_cv.notify_all();
+    }
+
+    // One event and one job table for a batched launch, shared by its items.
+    std::shared_ptr<void> make_batch_keep(cudaEvent_t ev, PinnedPool::Buf jobs) {
+        struct Keep {
+            cudaEvent_t ev;
+            PinnedPool::Buf jobs;
+            PinnedPool* pool;
+            ~Keep() {
+                cudaEventDestroy(ev);
+                pool->put(jobs);
+            }
+        };
+        return std::shared_ptr<void>(new Keep{ev, jobs, &pool}, [](void* k) { delete static_cast<Keep*>(k); });
+    }
+
+    bool batch_kernel_ok(uint64_t ptr, uint64_t nbytes) const {
+        return gpu && opt.engine != "copy_engine" && (ptr & 15) == 0 && nbytes % 16 == 0 && nbytes > 0;
     }
 
     void progress_loop() {
@@ -706,6 +728,11 @@ std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items,
     }
     BatchRequestOffloadResponse resp = D.call<Op::kBatchRequestOffload>(br);
     std::vector<Impl::Pending> launched;
+    // One K1 launch for the whole batch when every item suits the job kernel.
+    bool jobs_ok = D.gpu && !items.empty();
+    for (const BatchItem& it : items) jobs_ok = jobs_ok && D.batch_kernel_ok(it.ptr, it.nbytes);
+    std::vector<kern::XferJob> jobs;
+    uint64_t total_chunks = 0;
     for (size_t i = 0; i < items.size() && i < resp.grants.size(); ++i) {
         const RequestOffloadResponse& g = resp.grants[i];
         EvictTicket& t = out[i];
@@ -736,13 +763,43 @@ std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items,
             std::lock_guard<std::mutex> lg(D.tab_mu);
             D.tensors[{p.tid, p.ver}].offloaded = false;
         }
-        D.launch_d2h(p, items[i].ptr, host, dev, s, D.opt.hash_on_evict);
+        if (jobs_ok) {
+            kern::XferJob j{};
+            j.src = reinterpret_cast<const void*>(items[i].ptr);
+            j.dst = dev;
+            j.nbytes = p.nbytes;
+            j.chunk_begin = total_chunks;
+            j.ebase = p.z ? static_cast<const uint8_t*>(p.zb.dev) : nullptr;
+            if (D.opt.hash_on_evict) {
+                p.ndig = kern::digest_count(p.nbytes);
+                p.dig = D.pool.get(std::max<uint64_t>(p.ndig, 1) * 8);
+                j.digests = static_cast<uint64_t*>(p.dig.dev);
+            }
+            total_chunks += kern::digest_count(p.nbytes);
+            jobs.push_back(j);
+        } else {
+            D.launch_d2h(p, items[i].ptr, host, dev, s, D.opt.hash_on_evict);
+        }
         t.ok = true;
         t.lease_id = g.lease_id;
         t.slot_id = g.slot_id;
         launched.push_back(std::move(p));
     }
     for (PinnedPool::Buf& b : zb) D.pool.put(b);  // items without a grant
+    if (!jobs.empty()) {
+        PinnedPool::Buf tab = D.pool.get(jobs.size() * sizeof(kern::XferJob));
+        std::memcpy(tab.host, jobs.data(), jobs.size() * sizeof(kern::XferJob));
+        CUDA_OK(kern::evict_jobs(static_cast<const kern::XferJob*>(tab.dev), int(jobs.size()), total_chunks, s,
+                                 D.opt.evict_ctas));
+        cudaEvent_t ev;
+        CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        CUDA_OK(cudaEventRecord(ev, s));
+        auto keep = D.make_batch_keep(ev, tab);
+        for (Impl::Pending& p : launched) {
+            p.ev = ev;
+            p.batch_keep = keep;
+        }
+    }
     // Every launch recorded its own event; the last one covers the batch on
     // this stream, so a waiting caller synchronizes once.
     if (wait && D.gpu && !launched.empty()) CUDA_OK(cudaEventSynchronize(launched.back().ev));
@@ -914,6 +971,8 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
     cudaStream_t s = D.stream_of(stream);
     std::vector<Impl::Pending> launched;
     const uint64_t deadline = mono_ns() + 600ull * 1000000000ull;
+    bool jobs_ok = D.gpu && !items.empty();
+    for (const BatchItem& it : items) jobs_ok = jobs_ok && D.batch_kernel_ok(it.ptr, it.nbytes);
     while (!pending.empty()) {
         BatchRequestPrefetchRequest q;
         q.rank_id = br.rank_id;
@@ -921,6 +980,9 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
         for (size_t i : pending) q.items.push_back(br.items[i]);
         BatchRequestPrefetchResponse resp = D.call<Op::kBatchRequestPrefetch>(q);
         std::vector<size_t> again;
+        std::vector<kern::XferJob> jobs;  // this round's ready items, one K2 launch
+        const size_t first = launched.size();
+        uint64_t total_chunks = 0;
         for (size_t k = 0; k < pending.size() && k < resp.results.size(); ++k) {
             size_t i = pending[k];
             const RequestPrefetchResponse& r = resp.results[k];
@@ -944,7 +1006,16 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
             D.inflight_h2d += p.nbytes;
             ++D.restores;
             const bool z = D.run_is_z(r.slot_id);
-            if (D.gpu) {
+            if (jobs_ok) {
+                kern::XferJob j{};
+                j.src = dev;
+                j.dst = reinterpret_cast<void*>(items[i].ptr);
+                j.nbytes = r.nbytes;
+                j.chunk_begin = total_chunks;
+                j.coded = z ? 1u : 0u;
+                total_chunks += kern::digest_count(r.nbytes);
+                jobs.push_back(j);
+            } else if (D.gpu) {
                 if (z)
                     CUDA_OK(kern::restore_z(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes, kern::Cast::kNone,
                                             nullptr, nullptr, nullptr, s, D.opt.restore_ctas));
@@ -966,6 +1037,20 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
             out[i].ok = true;
             out[i].message = "ok";
             launched.push_back(std::move(p));
+        }
+        if (!jobs.empty()) {
+            PinnedPool::Buf tab = D.pool.get(jobs.size() * sizeof(kern::XferJob));
+            std::memcpy(tab.host, jobs.data(), jobs.size() * sizeof(kern::XferJob));
+            CUDA_OK(kern::restore_jobs(static_cast<const kern::XferJob*>(tab.dev), int(jobs.size()), total_chunks, s,
+                                       D.opt.restore_ctas));
+            cudaEvent_t ev;
+            CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+            CUDA_OK(cudaEventRecord(ev, s));
+            auto keep = D.make_batch_keep(ev, tab);
+            for (size_t k = first; k < launched.size(); ++k) {
+                launched[k].ev = ev;
+                launched[k].batch_keep = keep;
+            }
         }
         pending.swap(again);
         if (!pending.empty()) {

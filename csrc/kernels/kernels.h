@@ -86,6 +86,28 @@ cudaError_t evict_z(const void* src_dev, void* dst_mapped, uint64_t nbytes, cons
 cudaError_t restore_z(const void* src_mapped, void* dst_dev, uint64_t nbytes, Cast cast, float* scales_dev,
                       const uint64_t* expect, uint32_t* mismatch_dev, cudaStream_t stream, int ctas);
 
+// Batched K1/K2: one launch moves every item of a batch (KV-cache blocks).
+// Jobs are 64-byte records sorted by chunk_begin (the global index of the
+// job's first 64 KiB chunk; total_chunks covers them all), in
+// device-accessible memory. src/dst 16-byte aligned, nbytes % 16 == 0.
+//   evict:   src = device, dst = host-mapped run; ebase non-null = code the
+//            job in zbf16 with those window bases; digests (may be null)
+//   restore: src = host-mapped run, dst = device; coded != 0 = zbf16 run
+struct XferJob {
+    const void* src;
+    void* dst;
+    uint64_t nbytes;
+    uint64_t chunk_begin;
+    const uint8_t* ebase;
+    uint64_t* digests;
+    uint32_t coded;
+    uint32_t pad0;
+    uint64_t pad1;
+};
+static_assert(sizeof(XferJob) == 64, "XferJob is a 64-byte record");
+cudaError_t evict_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cudaStream_t stream, int ctas);
+cudaError_t restore_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cudaStream_t stream, int ctas);
+
 // Number of chunk digests for nbytes.
 inline uint64_t digest_count(uint64_t nbytes) { return (nbytes + 65535) / 65536; }
 

@@ -369,81 +369,116 @@ __global__ void __launch_bounds__(kThreads, 3)
 // the planes' 8- and 4-byte pieces are only ever touched in shared memory.
 constexpr uint32_t kZStage = zbf16::kChunk;
 
-// K1 with coding: hash the raw bytes, code each chunk into shared memory
-// (or keep it raw by rule) and stream it to the host-mapped run. Requires
-// 16-byte aligned src/dst and nbytes % 16 == 0 (zbf16::eligible).
+// One chunk of K1 with coding: hash the raw bytes, code the chunk into shared
+// memory (or keep it raw) and stream it to the host-mapped destination with
+// 16-byte vector stores. `src`/`dst` point at the chunk; 16-byte aligned,
+// len % 16 == 0. Every thread of the block calls this.
+__device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                              uint32_t len, bool raw, uint32_t eb, uint64_t* digest_out, int pol,
+                                              uint64_t* red, uint32_t* sc, uint8_t* zbuf) {
+    const uint32_t t = threadIdx.x;
+    const uint32_t nvec = len / 16;
+    uint4 v[kVecs];
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+        const uint32_t vi = uint32_t(k) * kThreads + t;
+        v[k] = vi < nvec ? ld_policy(src + uint64_t(vi) * 16, 0) : make_uint4(0, 0, 0, 0);
+    }
+    ssh::Lane L = ssh::lane_init(t);
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+        const uint32_t vi = uint32_t(k) * kThreads + t;
+        if (vi < nvec) {
+            ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
+            if (raw) {
+                st_policy(dst + uint64_t(vi) * 16, v[k], pol);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    cnt += zbf16::code_of(zbf16::exponent(uint16_t(half_of(v[k], j))), eb) == zbf16::kEscape;
+            }
+        }
+    }
+    if (!raw) {  // uniform per chunk
+        uint32_t total;
+        uint32_t off = block_excl_scan(cnt, sc, &total);
+        const uint32_t n = len / 2;
+        const uint32_t comp = zbf16::coded_len(len, total);
+        if (t == 0)
+            *reinterpret_cast<uint4*>(zbuf) =
+                make_uint4(uint32_t(zbf16::kTag) | (1u << 16) | (eb << 24), total, len, comp);
+        uint8_t* esc = zbuf + zbf16::kHeader + n + n / 2;
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            if (vi >= nvec) continue;
+            uint32_t lo0 = 0, lo1 = 0, codes = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint16_t h = uint16_t(half_of(v[k], j));
+                const uint32_t e = zbf16::exponent(h);
+                const uint32_t cd = zbf16::code_of(e, eb);
+                const uint32_t lb = zbf16::low_byte(h);
+                if (j < 4) lo0 |= lb << (8 * j);
+                else lo1 |= lb << (8 * (j - 4));
+                codes |= cd << (4 * j);
+                if (cd == zbf16::kEscape) esc[off++] = uint8_t(e);
+            }
+            *reinterpret_cast<uint2*>(zbuf + zbf16::kHeader + vi * 8) = make_uint2(lo0, lo1);
+            *reinterpret_cast<uint32_t*>(zbuf + zbf16::kHeader + n + vi * 4) = codes;
+        }
+        __syncthreads();
+        const uint32_t nout = (comp + 15) / 16;  // <= len / 16: coded chunks fit their raw length
+        for (uint32_t i = t; i < nout; i += kThreads)
+            st_policy(dst + uint64_t(i) * 16, *reinterpret_cast<const uint4*>(zbuf + i * 16), pol);
+    }
+    uint64_t root = tree_fold(ssh::lane_digest(L, t), red);  // also orders zbuf reuse
+    if (t == 0 && digest_out) *digest_out = ssh::chunk_finish(root, len);
+}
+
+// K1 with coding over one object. Requires 16-byte aligned src/dst and
+// nbytes % 16 == 0 (zbf16::eligible).
 __global__ void __launch_bounds__(kThreads, 2)
     k_evict_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
               const uint8_t* __restrict__ ebase, uint64_t* __restrict__ digests, int pol) {
     extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint64_t red[kThreads / 32];
     __shared__ uint32_t sc[kThreads / 32];
-    const uint32_t t = threadIdx.x;
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
     for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
         const uint64_t base = c * kChunk;
         const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
-        const uint32_t nvec = len / 16;
         const bool raw = zbf16::raw_by_rule(c, nchunks, len);
         const uint32_t eb = raw ? 0u : uint32_t(ebase[c]);
-        uint4 v[kVecs];
-#pragma unroll
-        for (int k = 0; k < kVecs; ++k) {
-            const uint32_t vi = uint32_t(k) * kThreads + t;
-            v[k] = vi < nvec ? ld_policy(src + base + uint64_t(vi) * 16, 0) : make_uint4(0, 0, 0, 0);
-        }
-        ssh::Lane L = ssh::lane_init(t);
-        uint32_t cnt = 0;
-#pragma unroll
-        for (int k = 0; k < kVecs; ++k) {
-            const uint32_t vi = uint32_t(k) * kThreads + t;
-            if (vi < nvec) {
-                ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
-                if (raw) {
-                    st_policy(dst + base + uint64_t(vi) * 16, v[k], pol);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        cnt += zbf16::code_of(zbf16::exponent(uint16_t(half_of(v[k], j))), eb) == zbf16::kEscape;
-                }
-            }
-        }
-        if (!raw) {  // uniform per chunk
-            uint32_t total;
-            uint32_t off = block_excl_scan(cnt, sc, &total);
-            const uint32_t n = len / 2;
-            const uint32_t comp = zbf16::coded_len(len, total);
-            if (t == 0)
-                *reinterpret_cast<uint4*>(zbuf) =
-                    make_uint4(uint32_t(zbf16::kTag) | (1u << 16) | (eb << 24), total, len, comp);
-            uint8_t* esc = zbuf + zbf16::kHeader + n + n / 2;
-#pragma unroll
-            for (int k = 0; k < kVecs; ++k) {
-                const uint32_t vi = uint32_t(k) * kThreads + t;
-                if (vi >= nvec) continue;
-                uint32_t lo0 = 0, lo1 = 0, codes = 0;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint16_t h = uint16_t(half_of(v[k], j));
-                    const uint32_t e = zbf16::exponent(h);
-                    const uint32_t cd = zbf16::code_of(e, eb);
-                    const uint32_t lb = zbf16::low_byte(h);
-                    if (j < 4) lo0 |= lb << (8 * j);
-                    else lo1 |= lb << (8 * (j - 4));
-                    codes |= cd << (4 * j);
-                    if (cd == zbf16::kEscape) esc[off++] = uint8_t(e);
-                }
-                *reinterpret_cast<uint2*>(zbuf + zbf16::kHeader + vi * 8) = make_uint2(lo0, lo1);
-                *reinterpret_cast<uint32_t*>(zbuf + zbf16::kHeader + n + vi * 4) = codes;
-            }
-            __syncthreads();
-            uint8_t* out = dst + base;
-            const uint32_t nout = (comp + 15) / 16;  // <= len / 16: coded chunks fit their raw length
-            for (uint32_t i = t; i < nout; i += kThreads)
-                st_policy(out + uint64_t(i) * 16, *reinterpret_cast<const uint4*>(zbuf + i * 16), pol);
-        }
-        uint64_t root = tree_fold(ssh::lane_digest(L, t), red);  // also orders zbuf reuse
-        if (t == 0 && digests) digests[c] = ssh::chunk_finish(root, len);
+        evict_chunk_z(src + base, dst + base, len, raw, eb, digests ? digests + c : nullptr, pol, red, sc, zbuf);
+    }
+}
+
+// Items of a batch are sorted by first chunk and every CTA visits its chunks
+// in increasing order, so the owning job only ever advances.
+__device__ __forceinline__ void advance_job(const XferJob* jobs, int n, uint64_t c, int& idx) {
+    while (idx + 1 < n && jobs[idx + 1].chunk_begin <= c) ++idx;
+}
+
+// K1 over a batch: one grid walks every chunk of every job (raw or coded per
+// job), so many small tensors (KV-cache blocks) cost one launch.
+__global__ void __launch_bounds__(kThreads, 2)
+    k_evict_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, int pol) {
+    extern __shared__ __align__(16) uint8_t zbuf[];
+    __shared__ uint64_t red[kThreads / 32];
+    __shared__ uint32_t sc[kThreads / 32];
+    int idx = 0;
+    for (uint64_t c = blockIdx.x; c < total_chunks; c += gridDim.x) {
+        advance_job(jobs, njobs, c, idx);
+        const XferJob j = jobs[idx];
+        const uint64_t lc = c - j.chunk_begin, nch = (j.nbytes + kChunk - 1) / kChunk;
+        const uint64_t base = lc * kChunk;
+        const uint32_t len = uint32_t(j.nbytes - base < kChunk ? j.nbytes - base : kChunk);
+        const bool raw = !j.ebase || zbf16::raw_by_rule(lc, nch, len);
+        const uint32_t eb = raw ? 0u : uint32_t(j.ebase[lc]);
+        evict_chunk_z(static_cast<const uint8_t*>(j.src) + base, static_cast<uint8_t*>(j.dst) + base, len, raw, eb,
+                      j.digests ? j.digests + lc : nullptr, pol, red, sc, zbuf);
     }
 }
 
@@ -468,10 +503,74 @@ __device__ __forceinline__ void stage_in(const uint8_t* in, uint8_t* zbuf, uint3
     }
 }
 
-// K2 with decoding: bring each coded chunk into shared memory with 16-byte
-// loads (header, planes and, speculatively, 1 KiB of escapes in one round
-// trip; the rest of the escapes in a second one when present), rebuild the
-// bf16 vectors and continue as K2 (verify, cast, store).
+// One chunk of K2 with decoding, into registers: thread t receives vectors
+// k*256 + t (zeros past the end). Coded chunks come into shared memory with
+// 16-byte loads (header, planes and, speculatively, 1 KiB of escapes in one
+// round trip; the rest of the escapes in a second one when present); raw
+// chunks load straight into registers. Every thread of the block calls this.
+__device__ __forceinline__ void load_chunk_z(const uint8_t* __restrict__ in, uint32_t len, bool raw, int pol,
+                                             uint32_t* sc, uint8_t* zbuf, uint4 (&v)[kVecs]) {
+    const uint32_t t = threadIdx.x;
+    const uint32_t nvec = len / 16;
+    if (raw) {
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            v[k] = vi < nvec ? ld_policy(in + uint64_t(vi) * 16, pol) : make_uint4(0, 0, 0, 0);
+        }
+        return;
+    }
+    const uint32_t n = len / 2;
+    const uint32_t fixed = zbf16::kHeader + n + n / 2;
+    const uint32_t spec = min(len, fixed + 1024u);
+    stage_in(in, zbuf, 0, spec, pol);
+    __syncthreads();
+    const uint4 hd = *reinterpret_cast<const uint4*>(zbuf);
+    const uint32_t comp = min(hd.w, len);
+    if (comp > spec) {  // uniform: every thread read the same header
+        stage_in(in, zbuf, spec / 16 * 16, comp, pol);
+        __syncthreads();
+    }
+    const uint32_t eb = hd.x >> 24;
+    uint2 lo[kVecs];
+    uint32_t cd[kVecs];
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+        const uint32_t vi = uint32_t(k) * kThreads + t;
+        if (vi < nvec) {
+            lo[k] = *reinterpret_cast<const uint2*>(zbuf + zbf16::kHeader + vi * 8);
+            cd[k] = *reinterpret_cast<const uint32_t*>(zbuf + zbf16::kHeader + n + vi * 4);
+        } else {
+            lo[k] = make_uint2(0, 0);
+            cd[k] = 0;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cnt += ((cd[k] >> (4 * j)) & 15u) == zbf16::kEscape;
+    }
+    uint32_t total;
+    uint32_t off = block_excl_scan(cnt, sc, &total);
+    const uint8_t* esc = zbuf + fixed;
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t code = (cd[k] >> (4 * j)) & 15u;
+            const uint32_t lb = ((j < 4 ? lo[k].x : lo[k].y) >> (8 * (j & 3))) & 0xFFu;
+            uint32_t e = eb + code;
+            if (code == zbf16::kEscape) e = esc[off++];  // only valid vectors carry escapes
+            const uint32_t h = zbf16::rebuild(uint8_t(lb), e);
+            if (j & 1) w[j >> 1] |= h << 16;
+            else w[j >> 1] = h;
+        }
+        v[k] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    __syncthreads();  // the stage is refilled by the next chunk
+}
+
+// K2 with decoding over one object: decode into registers, then continue as
+// K2 (verify, cast, store).
 template <bool VERIFY, int CAST>
 __global__ void __launch_bounds__(kThreads, 2)
     k_restore_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
@@ -485,63 +584,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint64_t base = c * kChunk;
         const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
         const uint32_t nvec = len / 16;
-        const uint8_t* in = src + base;
         uint4 v[kVecs];
-        if (zbf16::raw_by_rule(c, nchunks, len)) {
-#pragma unroll
-            for (int k = 0; k < kVecs; ++k) {
-                const uint32_t vi = uint32_t(k) * kThreads + t;
-                v[k] = vi < nvec ? ld_policy(in + uint64_t(vi) * 16, pol) : make_uint4(0, 0, 0, 0);
-            }
-        } else {
-            const uint32_t n = len / 2;
-            const uint32_t fixed = zbf16::kHeader + n + n / 2;
-            const uint32_t spec = min(len, fixed + 1024u);
-            stage_in(in, zbuf, 0, spec, pol);
-            __syncthreads();
-            const uint4 hd = *reinterpret_cast<const uint4*>(zbuf);
-            const uint32_t comp = min(hd.w, len);
-            if (comp > spec) {  // uniform: every thread read the same header
-                stage_in(in, zbuf, spec / 16 * 16, comp, pol);
-                __syncthreads();
-            }
-            const uint32_t eb = hd.x >> 24;
-            uint2 lo[kVecs];
-            uint32_t cd[kVecs];
-            uint32_t cnt = 0;
-#pragma unroll
-            for (int k = 0; k < kVecs; ++k) {
-                const uint32_t vi = uint32_t(k) * kThreads + t;
-                if (vi < nvec) {
-                    lo[k] = *reinterpret_cast<const uint2*>(zbuf + zbf16::kHeader + vi * 8);
-                    cd[k] = *reinterpret_cast<const uint32_t*>(zbuf + zbf16::kHeader + n + vi * 4);
-                } else {
-                    lo[k] = make_uint2(0, 0);
-                    cd[k] = 0;
-                }
-#pragma unroll
-                for (int j = 0; j < 8; ++j) cnt += ((cd[k] >> (4 * j)) & 15u) == zbf16::kEscape;
-            }
-            uint32_t total;
-            uint32_t off = block_excl_scan(cnt, sc, &total);
-            const uint8_t* esc = zbuf + fixed;
-#pragma unroll
-            for (int k = 0; k < kVecs; ++k) {
-                uint32_t w[4];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t code = (cd[k] >> (4 * j)) & 15u;
-                    const uint32_t lb = ((j < 4 ? lo[k].x : lo[k].y) >> (8 * (j & 3))) & 0xFFu;
-                    uint32_t e = eb + code;
-                    if (code == zbf16::kEscape) e = esc[off++];  // only valid vectors carry escapes
-                    const uint32_t h = zbf16::rebuild(uint8_t(lb), e);
-                    if (j & 1) w[j >> 1] |= h << 16;
-                    else w[j >> 1] = h;
-                }
-                v[k] = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-            __syncthreads();  // the stage is refilled by the next chunk
-        }
+        load_chunk_z(src + base, len, zbf16::raw_by_rule(c, nchunks, len), pol, sc, zbuf, v);
         ssh::Lane L = ssh::lane_init(t);
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) {
@@ -572,6 +616,32 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (VERIFY) {
             uint64_t root = tree_fold(ssh::lane_digest(L, t), red);
             if (t == 0 && ssh::chunk_finish(root, len) != expect[c]) atomicAdd(mismatch, 1u);
+        }
+    }
+}
+
+// K2 over a batch (no cast, no verification): one grid for every chunk of
+// every job, raw or coded per job.
+__global__ void __launch_bounds__(kThreads, 2)
+    k_restore_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, int pol) {
+    extern __shared__ __align__(16) uint8_t zbuf[];
+    __shared__ uint32_t sc[kThreads / 32];
+    const uint32_t t = threadIdx.x;
+    int idx = 0;
+    for (uint64_t c = blockIdx.x; c < total_chunks; c += gridDim.x) {
+        advance_job(jobs, njobs, c, idx);
+        const XferJob j = jobs[idx];
+        const uint64_t lc = c - j.chunk_begin, nch = (j.nbytes + kChunk - 1) / kChunk;
+        const uint64_t base = lc * kChunk;
+        const uint32_t len = uint32_t(j.nbytes - base < kChunk ? j.nbytes - base : kChunk);
+        const bool raw = !j.coded || zbf16::raw_by_rule(lc, nch, len);
+        uint4 v[kVecs];
+        load_chunk_z(static_cast<const uint8_t*>(j.src) + base, len, raw, pol, sc, zbuf, v);
+        uint8_t* out = static_cast<uint8_t*>(j.dst) + base;
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            if (vi < len / 16) store_vec<true>(out + uint64_t(vi) * 16, v[k], 16u);
         }
     }
 }
@@ -822,6 +892,30 @@ cudaError_t restore_z(const void* src, void* dst, uint64_t nbytes, Cast cast, fl
             else k_restore_z<false, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
             break;
     }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t evict_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cudaStream_t s, int ctas) {
+    if (njobs <= 0 || total_chunks == 0) return cudaSuccess;
+    if (!jobs) return cudaErrorInvalidValue;
+    cudaError_t e = allow_stage(reinterpret_cast<const void*>(&k_evict_jobs), 10);
+    if (e != cudaSuccess) return e;
+    int g = ctas > 0 ? ctas : 48;
+    if (uint64_t(g) > total_chunks) g = int(total_chunks);
+    k_evict_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, g_policy.load(std::memory_order_relaxed));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t restore_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cudaStream_t s, int ctas) {
+    if (njobs <= 0 || total_chunks == 0) return cudaSuccess;
+    if (!jobs) return cudaErrorInvalidValue;
+    cudaError_t e = allow_stage(reinterpret_cast<const void*>(&k_restore_jobs), 11);
+    if (e != cudaSuccess) return e;
+    int g = ctas > 0 ? ctas : 96;
+    if (uint64_t(g) > total_chunks) g = int(total_chunks);
+    k_restore_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, g_policy.load(std::memory_order_relaxed));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
