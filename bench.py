@@ -73,7 +73,8 @@ def parse():
     p.add_argument("--max-size-mb", type=int, default=8192, help="sweep: largest tensor")
     p.add_argument("--kv-gb", type=float, default=40.0, help="kv_cache: KV cache bytes per GPU")
     p.add_argument("--evict-fraction", type=float, default=0.5, help="kv_cache: blocks moved per iteration")
-    p.add_argument("--kv-batch", type=int, default=256, help="kv_cache: blocks per reservation round trip")
+    p.add_argument("--kv-batch", type=int, default=0,
+                   help="kv_cache: blocks per evict_batch/restore_batch call (0: the whole iteration in one call)")
     p.add_argument("--pinned-gb", type=int, default=0, help="kv_cache: pinned window per GPU (0 = fits the set)")
     p.add_argument("--nvme-dir", default="", help="dp_dedup: NVMe spill directory")
     p.add_argument("--spill-timeout", type=float, default=600.0, help="dp_dedup: seconds to wait for the spill")

@@ -143,7 +143,7 @@ struct Agent::Impl {
 
     struct TensorRec {
         bool offloaded = false, restored = false;
-        uint64_t hash_lo = 0, hash_hi = 0, lease = 0, ring_seq = ~0ull;
+        uint64_t hash_lo = 0, hash_hi = 0, lease = 0;
         std::vector<uint64_t> digests;
     };
     mutable std::mutex tab_mu;
@@ -316,7 +316,7 @@ struct Agent::Impl {
     }
 
     // ---- completions -----------------------------------------------------
-    bool ring_push_entry(EventType ev, const Pending& p, uint64_t* seq) {
+    bool ring_push_entry(EventType ev, const Pending& p) {
         if (!ring) return false;
         std::lock_guard<std::mutex> g(ring_mu);
         ofld_completion_entry_t e{};
@@ -326,25 +326,14 @@ struct Agent::Impl {
         e.slot_id = p.slot;
         e.event_type = uint32_t(ev);
         e.timestamp_ns = real_ns();
-        uint64_t t = ring->tail.load(std::memory_order_relaxed);
-        if (!ring_push(ring, e)) return false;
-        if (seq) *seq = t;
-        return true;
+        return ring_push(ring, e);
     }
 
-    void wait_ring_consumed(uint64_t seq) {
-        if (!ring || seq == ~0ull) return;
-        uint64_t deadline = mono_ns() + 30ull * 1000000000ull;
-        while (ring->head.load(std::memory_order_acquire) <= seq) {
-            if (mono_ns() > deadline) throw std::runtime_error("daemon did not consume completion ring");
-            sleep_us(10);
-        }
-    }
-
+    // A completion goes through the shared ring when it has room; the daemon
+    // applies pending ring entries before answering any request that depends
+    // on them, so the next request of this rank sees it.
     void report_d2h(const Pending& p) {
-        uint64_t seq = ~0ull;
-        // keep_pinned cannot travel through the ring; the RPC carries it.
-        if (!ring_push_entry(EventType::kD2HComplete, p, &seq)) {
+        if (!ring_push_entry(EventType::kD2HComplete, p)) {
             TransferMark m;
             m.rank_id = opt.rank_id;
             m.rank_epoch = epoch;
@@ -356,17 +345,11 @@ struct Agent::Impl {
             MarkD2HCompleteResponse r = call<Op::kMarkD2HComplete>(m);
             if (!r.ok) LOG_ERR(TAG, "MarkD2HComplete rejected for tensor %llu", (unsigned long long)p.tid);
         }
-        std::lock_guard<std::mutex> g(tab_mu);
-        tensors[{p.tid, p.ver}].ring_seq = seq;
     }
 
     void report_h2d(const Pending& p) {
-        uint64_t seq = ~0ull;
-        if (!p.keep_pinned && ring_push_entry(EventType::kH2DComplete, p, &seq)) {
-            std::lock_guard<std::mutex> g(tab_mu);
-            tensors[{p.tid, p.ver}].ring_seq = seq;  // later queries wait for this entry
-            return;
-        }
+        // keep_pinned cannot travel through the ring; the RPC carries it.
+        if (!p.keep_pinned && ring_push_entry(EventType::kH2DComplete, p)) return;
         {
             MarkH2DCompleteRequest m;
             m.rank_id = opt.rank_id;
@@ -693,116 +676,148 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
     return t;
 }
 
+// Batched eviction. One zbf16 pre-pass launch covers every eligible item
+// and the stream is waited on once; then the batch is reserved and launched
+// in groups of about batch_group_bytes, each group one K1 launch, so the
+// daemon round trip of group g+1 overlaps the PCIe copy of group g.
 std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait) {
     Impl& D = *d_;
     std::vector<EvictTicket> out(items.size());
-    BatchRequestOffloadRequest br;
-    br.rank_id = D.opt.rank_id;
-    br.rank_epoch = D.epoch;
     cudaStream_t s = D.stream_of(stream);
-    // zbf16 pre-pass of every eligible item, one wait for the batch
     std::vector<PinnedPool::Buf> zb(items.size());
     std::vector<char> z(items.size(), 0);
-    bool any_z = false;
-    for (size_t i = 0; i < items.size(); ++i)
-        if (D.want_z(items[i].ptr, items[i].nbytes, items[i].fmt_hint)) {
-            D.zscan_launch(items[i].ptr, items[i].nbytes, s, &zb[i]);
-            z[i] = any_z = true;
-        }
-    if (any_z) {
-        D.stream_wait(s);
-        for (size_t i = 0; i < items.size(); ++i)
-            if (z[i]) z[i] = D.zscan_result(items[i].nbytes, &zb[i]);
-    }
-    for (size_t i = 0; i < items.size(); ++i) {
-        const BatchItem& it = items[i];
-        RequestOffloadRequest rq;
-        rq.tensor_id = it.tensor_id;
-        rq.version = it.version;
-        rq.nbytes = it.nbytes;
-        rq.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
-        rq.numa_node = uint32_t(D.numa);
-        rq.alignment = 256;
-        rq.flags = OFLD_FLAG_ALLOW_OVERFLOW | OFLD_FLAG_SUBMIT_ON_GRANT | (z[i] ? OFLD_FLAG_FORMAT_ZBF16 : 0);
-        br.items.push_back(rq);
-    }
-    BatchRequestOffloadResponse resp = D.call<Op::kBatchRequestOffload>(br);
-    std::vector<Impl::Pending> launched;
-    // One K1 launch for the whole batch when every item suits the job kernel.
-    bool jobs_ok = D.gpu && !items.empty();
-    for (const BatchItem& it : items) jobs_ok = jobs_ok && D.batch_kernel_ok(it.ptr, it.nbytes);
-    std::vector<kern::XferJob> jobs;
-    uint64_t total_chunks = 0;
-    for (size_t i = 0; i < items.size() && i < resp.grants.size(); ++i) {
-        const RequestOffloadResponse& g = resp.grants[i];
-        EvictTicket& t = out[i];
-        t.tensor_id = items[i].tensor_id;
-        t.version = items[i].version;
-        t.nbytes = items[i].nbytes;
-        if (!g.ok || g.blocked) {
-            t.message = g.ok ? "offload blocked (pinned pressure)" : g.message;
-            D.pool.put(zb[i]);
-            zb[i] = PinnedPool::Buf{};
-            continue;
-        }
-        char *host = nullptr, *dev = nullptr;
-        D.resolve(g.arena_id, g.arena_offset, items[i].nbytes, &host, &dev);
-        Impl::Pending p;
-        p.z = z[i] != 0;
-        p.zb = zb[i];
-        zb[i] = PinnedPool::Buf{};
-        t.coded = p.z;
-        p.lease = g.lease_id;
-        p.tid = items[i].tensor_id;
-        p.ver = items[i].version;
-        p.slot = g.slot_id;
-        p.nbytes = items[i].nbytes;
-        D.inflight_d2h += p.nbytes;
-        ++D.evicts;
-        {
-            std::lock_guard<std::mutex> lg(D.tab_mu);
-            D.tensors[{p.tid, p.ver}].offloaded = false;
-        }
-        if (jobs_ok) {
+    {
+        std::vector<kern::XferJob> scan;
+        uint64_t scan_chunks = 0;
+        for (size_t i = 0; i < items.size(); ++i) {
+            if (!D.want_z(items[i].ptr, items[i].nbytes, items[i].fmt_hint)) continue;
+            const uint64_t nch = kern::digest_count(items[i].nbytes);
+            const uint64_t flag_off = (nch + 15) / 16 * 16;
+            zb[i] = D.pool.get(flag_off + 16);
+            *reinterpret_cast<volatile uint32_t*>(static_cast<char*>(zb[i].host) + flag_off) = 0;
             kern::XferJob j{};
             j.src = reinterpret_cast<const void*>(items[i].ptr);
-            j.dst = dev;
-            j.nbytes = p.nbytes;
-            j.chunk_begin = total_chunks;
-            j.ebase = p.z ? static_cast<const uint8_t*>(p.zb.dev) : nullptr;
-            if (D.opt.hash_on_evict) {
-                p.ndig = kern::digest_count(p.nbytes);
-                p.dig = D.pool.get(std::max<uint64_t>(p.ndig, 1) * 8);
-                j.digests = static_cast<uint64_t*>(p.dig.dev);
-            }
-            total_chunks += kern::digest_count(p.nbytes);
-            jobs.push_back(j);
-        } else {
-            D.launch_d2h(p, items[i].ptr, host, dev, s, D.opt.hash_on_evict);
+            j.dst = zb[i].dev;
+            j.nbytes = items[i].nbytes;
+            j.chunk_begin = scan_chunks;
+            scan_chunks += nch;
+            scan.push_back(j);
+            z[i] = 1;
         }
-        t.ok = true;
-        t.lease_id = g.lease_id;
-        t.slot_id = g.slot_id;
-        launched.push_back(std::move(p));
+        if (!scan.empty()) {
+            PinnedPool::Buf tab = D.pool.get(scan.size() * sizeof(kern::XferJob));
+            std::memcpy(tab.host, scan.data(), scan.size() * sizeof(kern::XferJob));
+            CUDA_OK(kern::zscan_jobs(static_cast<const kern::XferJob*>(tab.dev), int(scan.size()), scan_chunks, s,
+                                     D.opt.hash_ctas));
+            D.stream_wait(s);
+            D.pool.put(tab);
+            for (size_t i = 0; i < items.size(); ++i)
+                if (z[i]) z[i] = D.zscan_result(items[i].nbytes, &zb[i]);
+        }
+    }
+    std::vector<Impl::Pending> launched;
+    cudaEvent_t last_ev = nullptr;
+    const uint64_t group_bytes = std::max<uint64_t>(D.opt.batch_group_bytes, 1);
+    for (size_t g0 = 0; g0 < items.size();) {
+        size_t g1 = g0;
+        uint64_t bytes = 0;
+        while (g1 < items.size() && (g1 == g0 || bytes < group_bytes)) bytes += items[g1++].nbytes;
+        BatchRequestOffloadRequest br;
+        br.rank_id = D.opt.rank_id;
+        br.rank_epoch = D.epoch;
+        for (size_t i = g0; i < g1; ++i) {
+            const BatchItem& it = items[i];
+            RequestOffloadRequest rq;
+            rq.tensor_id = it.tensor_id;
+            rq.version = it.version;
+            rq.nbytes = it.nbytes;
+            rq.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
+            rq.numa_node = uint32_t(D.numa);
+            rq.alignment = 256;
+            rq.flags = OFLD_FLAG_ALLOW_OVERFLOW | OFLD_FLAG_SUBMIT_ON_GRANT | (z[i] ? OFLD_FLAG_FORMAT_ZBF16 : 0);
+            br.items.push_back(rq);
+        }
+        BatchRequestOffloadResponse resp = D.call<Op::kBatchRequestOffload>(br);
+        std::vector<kern::XferJob> jobs;  // this group's items on the job kernel, one K1 launch
+        const size_t first = launched.size();
+        uint64_t total_chunks = 0;
+        for (size_t i = g0; i < g1; ++i) {
+            EvictTicket& t = out[i];
+            t.tensor_id = items[i].tensor_id;
+            t.version = items[i].version;
+            t.nbytes = items[i].nbytes;
+            if (i - g0 >= resp.grants.size()) {
+                t.message = resp.message.empty() ? "no grant" : resp.message;
+                continue;
+            }
+            const RequestOffloadResponse& g = resp.grants[i - g0];
+            if (!g.ok || g.blocked) {
+                t.message = g.ok ? "offload blocked (pinned pressure)" : g.message;
+                continue;
+            }
+            char *host = nullptr, *dev = nullptr;
+            D.resolve(g.arena_id, g.arena_offset, items[i].nbytes, &host, &dev);
+            Impl::Pending p;
+            p.z = z[i] != 0;
+            p.zb = zb[i];
+            zb[i] = PinnedPool::Buf{};
+            t.coded = p.z;
+            p.lease = g.lease_id;
+            p.tid = items[i].tensor_id;
+            p.ver = items[i].version;
+            p.slot = g.slot_id;
+            p.nbytes = items[i].nbytes;
+            D.inflight_d2h += p.nbytes;
+            ++D.evicts;
+            {
+                std::lock_guard<std::mutex> lg(D.tab_mu);
+                D.tensors[{p.tid, p.ver}].offloaded = false;
+            }
+            if (D.batch_kernel_ok(items[i].ptr, p.nbytes)) {
+                kern::XferJob j{};
+                j.src = reinterpret_cast<const void*>(items[i].ptr);
+                j.dst = dev;
+                j.nbytes = p.nbytes;
+                j.chunk_begin = total_chunks;
+                j.ebase = p.z ? static_cast<const uint8_t*>(p.zb.dev) : nullptr;
+                if (D.opt.hash_on_evict) {
+                    p.ndig = kern::digest_count(p.nbytes);
+                    p.dig = D.pool.get(std::max<uint64_t>(p.ndig, 1) * 8);
+                    j.digests = static_cast<uint64_t*>(p.dig.dev);
+                }
+                total_chunks += kern::digest_count(p.nbytes);
+                jobs.push_back(j);
+            } else {
+                D.launch_d2h(p, items[i].ptr, host, dev, s, D.opt.hash_on_evict);
+                if (p.ev) last_ev = p.ev;
+            }
+            t.ok = true;
+            t.lease_id = g.lease_id;
+            t.slot_id = g.slot_id;
+            launched.push_back(std::move(p));
+        }
+        if (!jobs.empty()) {
+            PinnedPool::Buf tab = D.pool.get(jobs.size() * sizeof(kern::XferJob));
+            std::memcpy(tab.host, jobs.data(), jobs.size() * sizeof(kern::XferJob));
+            CUDA_OK(kern::evict_jobs(static_cast<const kern::XferJob*>(tab.dev), int(jobs.size()), total_chunks, s,
+                                     D.opt.evict_ctas));
+            cudaEvent_t ev;
+            CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+            CUDA_OK(cudaEventRecord(ev, s));
+            auto keep = D.make_batch_keep(ev, tab);
+            for (size_t k = first; k < launched.size(); ++k)
+                if (!launched[k].ev) {
+                    launched[k].ev = ev;
+                    launched[k].batch_keep = keep;
+                }
+            last_ev = ev;
+        }
+        g0 = g1;
     }
     for (PinnedPool::Buf& b : zb) D.pool.put(b);  // items without a grant
-    if (!jobs.empty()) {
-        PinnedPool::Buf tab = D.pool.get(jobs.size() * sizeof(kern::XferJob));
-        std::memcpy(tab.host, jobs.data(), jobs.size() * sizeof(kern::XferJob));
-        CUDA_OK(kern::evict_jobs(static_cast<const kern::XferJob*>(tab.dev), int(jobs.size()), total_chunks, s,
-                                 D.opt.evict_ctas));
-        cudaEvent_t ev;
-        CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-        CUDA_OK(cudaEventRecord(ev, s));
-        auto keep = D.make_batch_keep(ev, tab);
-        for (Impl::Pending& p : launched) {
-            p.ev = ev;
-            p.batch_keep = keep;
-        }
-    }
-    // Every launch recorded its own event; the last one covers the batch on
-    // this stream, so a waiting caller synchronizes once.
-    if (wait && D.gpu && !launched.empty()) CUDA_OK(cudaEventSynchronize(launched.back().ev));
+    // The last event recorded covers the whole batch on this stream, so a
+    // waiting caller synchronizes once.
+    if (wait && D.gpu && last_ev) CUDA_OK(cudaEventSynchronize(last_ev));
     for (Impl::Pending& p : launched) D.complete_or_queue(std::move(p), wait);
     return out;
 }
@@ -811,18 +826,15 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
                               StreamHandle stream, bool wait, const RestoreOptions& ro) {
     Impl& D = *d_;
     RestoreOutcome out;
-    uint64_t seq = ~0ull;
     std::vector<uint64_t> expect;
     {
         std::lock_guard<std::mutex> g(D.tab_mu);
         auto it = D.tensors.find({tensor_id, version});
         if (it != D.tensors.end()) {
-            seq = it->second.ring_seq;
             if (ro.verify) expect = it->second.digests;
             it->second.restored = false;
         }
     }
-    D.wait_ring_consumed(seq);
     RequestPrefetchRequest pr;
     pr.rank_id = D.opt.rank_id;
     pr.rank_epoch = D.epoch;
@@ -940,22 +952,14 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
     return out;
 }
 
+// Batched restore: prefetch requests and K2 launches go in groups of about
+// batch_group_bytes (one round trip and one launch per group, the next
+// group's round trip overlapping this group's copy). Items the daemon still
+// has to read back from a cold tier are asked for again after the rest.
 std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait) {
     Impl& D = *d_;
     std::vector<RestoreOutcome> out(items.size());
-    uint64_t maxseq = ~0ull;
-    {
-        std::lock_guard<std::mutex> g(D.tab_mu);
-        for (const BatchItem& it : items) {
-            auto f = D.tensors.find({it.tensor_id, it.version});
-            if (f != D.tensors.end() && f->second.ring_seq != ~0ull)
-                maxseq = maxseq == ~0ull ? f->second.ring_seq : std::max(maxseq, f->second.ring_seq);
-        }
-    }
-    D.wait_ring_consumed(maxseq);
-    BatchRequestPrefetchRequest br;
-    br.rank_id = D.opt.rank_id;
-    br.rank_epoch = D.epoch;
+    std::vector<RequestPrefetchRequest> reqs;
     for (const BatchItem& it : items) {
         RequestPrefetchRequest pr;
         pr.tensor_id = it.tensor_id;
@@ -964,93 +968,110 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
         pr.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
         pr.numa_node = uint32_t(D.numa);
         pr.flags = OFLD_FLAG_SUBMIT_ON_READY;
-        br.items.push_back(pr);
+        reqs.push_back(pr);
     }
     std::vector<size_t> pending(items.size());
     for (size_t i = 0; i < items.size(); ++i) pending[i] = i;
     cudaStream_t s = D.stream_of(stream);
     std::vector<Impl::Pending> launched;
+    cudaEvent_t last_ev = nullptr;
     const uint64_t deadline = mono_ns() + 600ull * 1000000000ull;
-    bool jobs_ok = D.gpu && !items.empty();
-    for (const BatchItem& it : items) jobs_ok = jobs_ok && D.batch_kernel_ok(it.ptr, it.nbytes);
+    const uint64_t group_bytes = std::max<uint64_t>(D.opt.batch_group_bytes, 1);
     while (!pending.empty()) {
-        BatchRequestPrefetchRequest q;
-        q.rank_id = br.rank_id;
-        q.rank_epoch = br.rank_epoch;
-        for (size_t i : pending) q.items.push_back(br.items[i]);
-        BatchRequestPrefetchResponse resp = D.call<Op::kBatchRequestPrefetch>(q);
         std::vector<size_t> again;
-        std::vector<kern::XferJob> jobs;  // this round's ready items, one K2 launch
-        const size_t first = launched.size();
-        uint64_t total_chunks = 0;
-        for (size_t k = 0; k < pending.size() && k < resp.results.size(); ++k) {
-            size_t i = pending[k];
-            const RequestPrefetchResponse& r = resp.results[k];
-            if (!r.ok) {
-                out[i].message = r.message;
-                continue;
-            }
-            if (!r.ready) {
-                again.push_back(i);
-                continue;
-            }
-            char *host = nullptr, *dev = nullptr;
-            D.resolve(r.arena_id, r.arena_offset, r.nbytes, &host, &dev);
-            Impl::Pending p;
-            p.d2h = false;
-            p.lease = r.lease_id;
-            p.tid = items[i].tensor_id;
-            p.ver = r.version;
-            p.slot = r.slot_id;
-            p.nbytes = r.nbytes;
-            D.inflight_h2d += p.nbytes;
-            ++D.restores;
-            const bool z = D.run_is_z(r.slot_id);
-            if (jobs_ok) {
-                kern::XferJob j{};
-                j.src = dev;
-                j.dst = reinterpret_cast<void*>(items[i].ptr);
-                j.nbytes = r.nbytes;
-                j.chunk_begin = total_chunks;
-                j.coded = z ? 1u : 0u;
-                total_chunks += kern::digest_count(r.nbytes);
-                jobs.push_back(j);
-            } else if (D.gpu) {
-                if (z)
-                    CUDA_OK(kern::restore_z(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes, kern::Cast::kNone,
-                                            nullptr, nullptr, nullptr, s, D.opt.restore_ctas));
-                else
-                    CUDA_OK(kern::restore_cast(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes,
-                                               kern::Cast::kNone, nullptr, nullptr, nullptr, s, D.opt.restore_ctas));
-                CUDA_OK(cudaEventCreateWithFlags(&p.ev, cudaEventDisableTiming));
-                CUDA_OK(cudaEventRecord(p.ev, s));
-            } else if (z) {
-                if (!zbf16::decode_object(reinterpret_cast<const uint8_t*>(host), r.nbytes,
-                                          reinterpret_cast<uint8_t*>(items[i].ptr))) {
-                    out[i].message = "malformed zbf16 object";
-                    D.finish(p);
+        for (size_t g0 = 0; g0 < pending.size();) {
+            size_t g1 = g0;
+            uint64_t bytes = 0;
+            while (g1 < pending.size() && (g1 == g0 || bytes < group_bytes)) bytes += items[pending[g1++]].nbytes;
+            BatchRequestPrefetchRequest q;
+            q.rank_id = D.opt.rank_id;
+            q.rank_epoch = D.epoch;
+            for (size_t k = g0; k < g1; ++k) q.items.push_back(reqs[pending[k]]);
+            BatchRequestPrefetchResponse resp = D.call<Op::kBatchRequestPrefetch>(q);
+            std::vector<kern::XferJob> jobs;  // this group's ready items, one K2 launch
+            const size_t first = launched.size();
+            uint64_t total_chunks = 0;
+            for (size_t k = g0; k < g1; ++k) {
+                const size_t i = pending[k];
+                if (k - g0 >= resp.results.size()) {
+                    out[i].message = resp.message.empty() ? "no prefetch result" : resp.message;
                     continue;
                 }
-            } else {
-                std::memcpy(reinterpret_cast<void*>(items[i].ptr), host, r.nbytes);
+                const RequestPrefetchResponse& r = resp.results[k - g0];
+                if (!r.ok) {
+                    out[i].message = r.message;
+                    continue;
+                }
+                if (!r.ready) {
+                    again.push_back(i);
+                    continue;
+                }
+                char *host = nullptr, *dev = nullptr;
+                D.resolve(r.arena_id, r.arena_offset, r.nbytes, &host, &dev);
+                Impl::Pending p;
+                p.d2h = false;
+                p.lease = r.lease_id;
+                p.tid = items[i].tensor_id;
+                p.ver = r.version;
+                p.slot = r.slot_id;
+                p.nbytes = r.nbytes;
+                D.inflight_h2d += p.nbytes;
+                ++D.restores;
+                const bool z = D.run_is_z(r.slot_id);
+                if (D.batch_kernel_ok(items[i].ptr, r.nbytes)) {
+                    kern::XferJob j{};
+                    j.src = dev;
+                    j.dst = reinterpret_cast<void*>(items[i].ptr);
+                    j.nbytes = r.nbytes;
+                    j.chunk_begin = total_chunks;
+                    j.coded = z ? 1u : 0u;
+                    total_chunks += kern::digest_count(r.nbytes);
+                    jobs.push_back(j);
+                } else if (D.gpu) {
+                    if (z)
+                        CUDA_OK(kern::restore_z(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes,
+                                                kern::Cast::kNone, nullptr, nullptr, nullptr, s, D.opt.restore_ctas));
+                    else if (D.opt.engine == "copy_engine")
+                        CUDA_OK(cudaMemcpyAsync(reinterpret_cast<void*>(items[i].ptr), host, r.nbytes,
+                                                cudaMemcpyHostToDevice, s));
+                    else
+                        CUDA_OK(kern::restore_cast(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes,
+                                                   kern::Cast::kNone, nullptr, nullptr, nullptr, s,
+                                                   D.opt.restore_ctas));
+                    CUDA_OK(cudaEventCreateWithFlags(&p.ev, cudaEventDisableTiming));
+                    CUDA_OK(cudaEventRecord(p.ev, s));
+                    last_ev = p.ev;
+                } else if (z) {
+                    if (!zbf16::decode_object(reinterpret_cast<const uint8_t*>(host), r.nbytes,
+                                              reinterpret_cast<uint8_t*>(items[i].ptr))) {
+                        out[i].message = "malformed zbf16 object";
+                        D.finish(p);
+                        continue;
+                    }
+                } else {
+                    std::memcpy(reinterpret_cast<void*>(items[i].ptr), host, r.nbytes);
+                }
+                out[i].ok = true;
+                out[i].message = "ok";
+                launched.push_back(std::move(p));
             }
-            out[i].ok = true;
-            out[i].message = "ok";
-            launched.push_back(std::move(p));
-        }
-        if (!jobs.empty()) {
-            PinnedPool::Buf tab = D.pool.get(jobs.size() * sizeof(kern::XferJob));
-            std::memcpy(tab.host, jobs.data(), jobs.size() * sizeof(kern::XferJob));
-            CUDA_OK(kern::restore_jobs(static_cast<const kern::XferJob*>(tab.dev), int(jobs.size()), total_chunks, s,
-                                       D.opt.restore_ctas));
-            cudaEvent_t ev;
-            CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-            CUDA_OK(cudaEventRecord(ev, s));
-            auto keep = D.make_batch_keep(ev, tab);
-            for (size_t k = first; k < launched.size(); ++k) {
-                launched[k].ev = ev;
-                launched[k].batch_keep = keep;
+            if (!jobs.empty()) {
+                PinnedPool::Buf tab = D.pool.get(jobs.size() * sizeof(kern::XferJob));
+                std::memcpy(tab.host, jobs.data(), jobs.size() * sizeof(kern::XferJob));
+                CUDA_OK(kern::restore_jobs(static_cast<const kern::XferJob*>(tab.dev), int(jobs.size()), total_chunks,
+                                           s, D.opt.restore_ctas));
+                cudaEvent_t ev;
+                CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+                CUDA_OK(cudaEventRecord(ev, s));
+                auto keep = D.make_batch_keep(ev, tab);
+                for (size_t k = first; k < launched.size(); ++k)
+                    if (!launched[k].ev) {
+                        launched[k].ev = ev;
+                        launched[k].batch_keep = keep;
+                    }
+                last_ev = ev;
             }
+            g0 = g1;
         }
         pending.swap(again);
         if (!pending.empty()) {
@@ -1061,7 +1082,7 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
             sleep_us(D.opt.prefetch_poll_us);
         }
     }
-    if (wait && D.gpu && !launched.empty()) CUDA_OK(cudaEventSynchronize(launched.back().ev));
+    if (wait && D.gpu && last_ev) CUDA_OK(cudaEventSynchronize(last_ev));
     for (Impl::Pending& p : launched) {
         if (!D.gpu || wait)
             D.finish(p);
@@ -1108,16 +1129,7 @@ bool Agent::tensor_hash(uint64_t tid, uint64_t ver, uint64_t* lo, uint64_t* hi) 
     return true;
 }
 
-// Completions published through the ring are applied by the daemon
-// asynchronously; queries about a tensor first wait until its entry is consumed.
-static uint64_t ring_seq_of(Agent::Impl& D, uint64_t tid, uint64_t ver) {
-    std::lock_guard<std::mutex> g(D.tab_mu);
-    auto it = D.tensors.find({tid, ver});
-    return it == D.tensors.end() ? ~0ull : it->second.ring_seq;
-}
-
 std::string Agent::location(uint64_t tid, uint64_t ver) {
-    d_->wait_ring_consumed(ring_seq_of(*d_, tid, ver));
     LocationQueryResponse r = d_->call<Op::kQueryLocation>(LocationQueryRequest{tid, ver});
     if (!r.ok) return "none";
     switch (r.location_kind) {
@@ -1131,7 +1143,6 @@ std::string Agent::location(uint64_t tid, uint64_t ver) {
 
 void Agent::discard(uint64_t tid, uint64_t ver) {
     Impl& D = *d_;
-    D.wait_ring_consumed(ring_seq_of(D, tid, ver));
     DiscardTensorRequest r{D.opt.rank_id, D.epoch, tid, ver};
     StatusResponse s = D.call<Op::kDiscardTensor>(r);
     if (!s.ok) LOG_WARN(TAG, "discard(%llu:%llu): %s", (unsigned long long)tid, (unsigned long long)ver, s.message.c_str());

@@ -49,6 +49,10 @@ struct AgentOptions {
     // on objects of at least compress_min_bytes, in kernel-engine mode.
     bool compress = true;
     uint64_t compress_min_bytes = 4ull << 20;
+    // evict_batch/restore_batch reserve and launch in groups of about this
+    // many bytes: one daemon round trip and one kernel launch per group, the
+    // round trip of the next group overlapping the copy of this one.
+    uint64_t batch_group_bytes = 256ull << 20;
 };
 
 // evict() data hints.

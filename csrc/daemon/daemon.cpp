@@ -600,6 +600,20 @@ void Daemon::apply_ring_entry(uint32_t rank, uint64_t epoch, const ofld_completi
     }
 }
 
+// Handlers whose answer depends on completions (prefetch, location, discard)
+// call this first: an agent publishes a completion before it sends the next
+// request, so the request sees its own earlier transfers without waiting for
+// the poller.
+void Daemon::drain_rings() {
+    for (uint32_t i = 0; i < ring_max_; ++i) {
+        if (ring_owner_[i] == 0xFFFFFFFFu) continue;
+        RingHeader* r = ring_at(control_, i);
+        if (r->rank_epoch == 0) continue;
+        ofld_completion_entry_t e;
+        while (ring_pop(r, &e)) apply_ring_entry(r->owner_rank, r->rank_epoch, e);
+    }
+}
+
 void Daemon::ring_loop() {
     const uint64_t idle_us = cfg_.ring_poll_us ? cfg_.ring_poll_us : 50;
     while (workers_on_.load()) {
@@ -632,8 +646,11 @@ GetStatsResponse Daemon::on_get_stats(const GetStatsRequest&) {
     GetStatsResponse resp;
     resp.ok = true;
     resp.message = "ok";
+    std::unique_lock<std::mutex> g(mu_);
+    drain_rings();
+    g.unlock();
     for (auto& kv : Metrics::get().snapshot()) resp.stats.push_back(StatEntry{kv.first, kv.second});
-    std::lock_guard<std::mutex> g(mu_);
+    g.lock();
     uint64_t live = 0;
     for (auto& kv : sessions_) live += kv.second.alive ? 1 : 0;
     resp.stats.push_back({"live_rank_sessions", live});
@@ -707,6 +724,7 @@ LookupPeerBufferResponse Daemon::on_lookup_peer_buffer(const LookupPeerBufferReq
 
 GetJobStatsResponse Daemon::on_get_job_stats(const GetJobStatsRequest& r) {
     std::lock_guard<std::mutex> g(mu_);
+    drain_rings();
     GetJobStatsResponse resp;
     resp.ok = true;
     resp.message = "ok";

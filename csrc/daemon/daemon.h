@@ -302,6 +302,8 @@ class Daemon {
     void readback_loop();
     void heartbeat_loop();
     void ring_loop();
+    // Applies every completion already published in the rings. mu_ held.
+    void drain_rings();
     void apply_ring_entry(uint32_t rank, uint64_t epoch, const ofld_completion_entry_t& e);
     void enqueue_drain(const Lease& L);
     bool force_drain_one(std::unique_lock<std::mutex>& lk);

@@ -535,11 +535,13 @@ RequestPrefetchResponse Daemon::do_request_prefetch(const RequestPrefetchRequest
 
 RequestPrefetchResponse Daemon::on_request_prefetch(const RequestPrefetchRequest& r) {
     std::unique_lock<std::mutex> lk(mu_);
+    drain_rings();
     return do_request_prefetch(r, lk);
 }
 
 BatchRequestPrefetchResponse Daemon::on_batch_request_prefetch(const BatchRequestPrefetchRequest& r) {
     std::unique_lock<std::mutex> lk(mu_);
+    drain_rings();
     BatchRequestPrefetchResponse resp;
     resp.ok = true;
     resp.message = "ok";
@@ -629,6 +631,7 @@ StatusResponse Daemon::on_h2d_complete(const MarkH2DCompleteRequest& r) {
 
 StatusResponse Daemon::on_release_lease(const ReleaseLeaseRequest& r) {
     std::lock_guard<std::mutex> g(mu_);
+    drain_rings();
     if (!epoch_ok(r.rank_id, r.rank_epoch)) {
         Metrics::get().inc(M::kEpochMismatchRejected);
         return {false, "epoch invalid"};
@@ -687,6 +690,7 @@ StatusResponse Daemon::on_release_lease(const ReleaseLeaseRequest& r) {
 // was never freed (reference: src/agent/agent.cpp:1100-1131).
 StatusResponse Daemon::on_discard_tensor(const DiscardTensorRequest& r) {
     std::lock_guard<std::mutex> g(mu_);
+    drain_rings();
     if (!epoch_ok(r.rank_id, r.rank_epoch)) {
         Metrics::get().inc(M::kEpochMismatchRejected);
         return {false, "epoch invalid"};
@@ -716,6 +720,7 @@ StatusResponse Daemon::on_discard_tensor(const DiscardTensorRequest& r) {
 
 LocationQueryResponse Daemon::on_query_location(const LocationQueryRequest& r) {
     std::lock_guard<std::mutex> g(mu_);
+    drain_rings();
     LocationQueryResponse resp;
     auto it = locations_.find(r.tensor_id);
     if (it == locations_.end()) {

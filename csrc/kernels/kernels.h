@@ -105,6 +105,11 @@ struct XferJob {
     uint64_t pad1;
 };
 static_assert(sizeof(XferJob) == 64, "XferJob is a 64-byte record");
+// zbf16 pre-pass over a batch: per job, `dst` receives one window base per
+// chunk followed, at the next 16-byte boundary, by a u32 fail word (set to 1
+// when a chunk does not fit coded; the caller zeroes it). Every src 16-byte
+// aligned and zbf16-eligible in size.
+cudaError_t zscan_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cudaStream_t stream, int ctas);
 cudaError_t evict_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cudaStream_t stream, int ctas);
 cudaError_t restore_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cudaStream_t stream, int ctas);
 

@@ -302,65 +302,71 @@ __device__ __forceinline__ uint32_t half_of(const uint4& v, int j) {
     return (j & 1) ? (w >> 16) : (w & 0xFFFFu);
 }
 
-// Pre-pass: per chunk, the largest exponent (window base = emax - 14) and
-// whether the coded chunk fits in its raw length. Any chunk that does not fit
-// sets *fail: the object is then moved uncoded. Two register passes per
-// chunk, so the pass runs at HBM rate.
+// Pre-pass over one chunk: the largest exponent (window base = emax - 14)
+// and whether the coded chunk fits in its raw length; a chunk that does not
+// fit sets *fail and the object is then moved uncoded. Two register passes
+// per chunk, so the pass runs at HBM rate. Every thread of the block calls
+// this; `red` is reused on return.
+__device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uint32_t len, uint8_t* eb_out,
+                                            uint32_t* fail, uint32_t* red) {
+    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const uint32_t nvec = len / 16;
+    uint4 v[kVecs];
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+        const uint32_t vi = uint32_t(k) * kThreads + t;
+        v[k] = vi < nvec ? ld_once(src + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
+    }
+    // bf16 bit patterns with the sign cleared order like their magnitudes
+    uint32_t m = 0;
+    auto hmax = [](uint32_t w) { return max(w & 0x7FFFu, (w >> 16) & 0x7FFFu); };
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k)
+        m = max(m, max(max(hmax(v[k].x), hmax(v[k].y)), max(hmax(v[k].z), hmax(v[k].w))));
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    uint32_t mm = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) mm = max(mm, red[w]);
+    const uint32_t eb = zbf16::window_base(zbf16::exponent(uint16_t(mm)));
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+        const uint32_t vi = uint32_t(k) * kThreads + t;
+        if (vi < nvec)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                cnt += zbf16::code_of(zbf16::exponent(uint16_t(half_of(v[k], j))), eb) == zbf16::kEscape;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    __syncthreads();  // everyone has read red[] (the max)
+    if (lane == 0) red[warp] = cnt;
+    __syncthreads();
+    if (t == 0) {
+        uint32_t esc = 0;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) esc += red[w];
+        *eb_out = uint8_t(eb);
+        if (zbf16::coded_len(len, esc) > len) atomicOr(fail, 1u);
+    }
+    __syncthreads();  // red[] is reused by the next chunk
+}
+
 __global__ void __launch_bounds__(kThreads, 3)
     k_zscan(const uint8_t* __restrict__ src, uint64_t nbytes, uint8_t* __restrict__ ebase_out, uint32_t* fail) {
     __shared__ uint32_t red[kThreads / 32];
-    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
     for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
         const uint64_t base = c * kChunk;
         const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
         if (zbf16::raw_by_rule(c, nchunks, len)) {
-            if (t == 0) ebase_out[c] = 0;
+            if (threadIdx.x == 0) ebase_out[c] = 0;
             continue;  // uniform per chunk
         }
-        const uint32_t nvec = len / 16;
-        uint4 v[kVecs];
-#pragma unroll
-        for (int k = 0; k < kVecs; ++k) {
-            const uint32_t vi = uint32_t(k) * kThreads + t;
-            v[k] = vi < nvec ? ld_once(src + base + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
-        }
-        // bf16 bit patterns with the sign cleared order like their magnitudes
-        uint32_t m = 0;
-        auto hmax = [](uint32_t w) { return max(w & 0x7FFFu, (w >> 16) & 0x7FFFu); };
-#pragma unroll
-        for (int k = 0; k < kVecs; ++k)
-            m = max(m, max(max(hmax(v[k].x), hmax(v[k].y)), max(hmax(v[k].z), hmax(v[k].w))));
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) red[warp] = m;
-        __syncthreads();
-        uint32_t mm = 0;
-#pragma unroll
-        for (int w = 0; w < kThreads / 32; ++w) mm = max(mm, red[w]);
-        const uint32_t eb = zbf16::window_base(zbf16::exponent(uint16_t(mm)));
-        uint32_t cnt = 0;
-#pragma unroll
-        for (int k = 0; k < kVecs; ++k) {
-            const uint32_t vi = uint32_t(k) * kThreads + t;
-            if (vi < nvec)
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    cnt += zbf16::code_of(zbf16::exponent(uint16_t(half_of(v[k], j))), eb) == zbf16::kEscape;
-        }
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-        __syncthreads();  // everyone has read red[] (the max)
-        if (lane == 0) red[warp] = cnt;
-        __syncthreads();
-        if (t == 0) {
-            uint32_t esc = 0;
-#pragma unroll
-            for (int w = 0; w < kThreads / 32; ++w) esc += red[w];
-            ebase_out[c] = uint8_t(eb);
-            if (zbf16::coded_len(len, esc) > len) atomicOr(fail, 1u);
-        }
-        __syncthreads();  // red[] is reused by the next chunk
+        zscan_chunk(src + base, len, ebase_out + c, fail, red);
     }
 }
 
@@ -459,6 +465,29 @@ __global__ void __launch_bounds__(kThreads, 2)
 // in increasing order, so the owning job only ever advances.
 __device__ __forceinline__ void advance_job(const XferJob* jobs, int n, uint64_t c, int& idx) {
     while (idx + 1 < n && jobs[idx + 1].chunk_begin <= c) ++idx;
+}
+
+// The pre-pass over a batch: job `src`/`nbytes`/`chunk_begin` as for K1;
+// `dst` is the job's scan buffer (one window base per chunk, then the fail
+// word at the next 16-byte boundary).
+__global__ void __launch_bounds__(kThreads, 3)
+    k_zscan_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks) {
+    __shared__ uint32_t red[kThreads / 32];
+    int idx = 0;
+    for (uint64_t c = blockIdx.x; c < total_chunks; c += gridDim.x) {
+        advance_job(jobs, njobs, c, idx);
+        const XferJob j = jobs[idx];
+        const uint64_t lc = c - j.chunk_begin, nch = (j.nbytes + kChunk - 1) / kChunk;
+        const uint64_t base = lc * kChunk;
+        const uint32_t len = uint32_t(j.nbytes - base < kChunk ? j.nbytes - base : kChunk);
+        uint8_t* eb = static_cast<uint8_t*>(j.dst);
+        if (zbf16::raw_by_rule(lc, nch, len)) {
+            if (threadIdx.x == 0) eb[lc] = 0;
+            continue;  // uniform per chunk
+        }
+        zscan_chunk(static_cast<const uint8_t*>(j.src) + base, len, eb + lc,
+                    reinterpret_cast<uint32_t*>(eb + (nch + 15) / 16 * 16), red);
+    }
 }
 
 // K1 over a batch: one grid walks every chunk of every job (raw or coded per
@@ -839,6 +868,20 @@ cudaError_t zscan(const void* src, uint64_t nbytes, uint8_t* ebase, uint32_t* fa
     int g = ctas > 0 ? ctas : sms * 3;
     if (uint64_t(g) > nchunks) g = int(nchunks);
     k_zscan<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), nbytes, ebase, fail);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t zscan_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cudaStream_t s, int ctas) {
+    if (!jobs || njobs <= 0) return cudaErrorInvalidValue;
+    if (total_chunks == 0) return cudaSuccess;
+    int sms = 148;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int g = ctas > 0 ? ctas : sms * 3;
+    if (uint64_t(g) > total_chunks) g = int(total_chunks);
+    k_zscan_jobs<<<g, kThreads, 0, s>>>(jobs, njobs, total_chunks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }

@@ -222,6 +222,7 @@ class PyAgent {
             else if (k == "stream_priority") o.stream_priority = v.cast<int>();
             else if (k == "compress") o.compress = v.cast<bool>();
             else if (k == "compress_min_bytes") o.compress_min_bytes = v.cast<uint64_t>();
+            else if (k == "batch_group_bytes") o.batch_group_bytes = v.cast<uint64_t>();
             else throw std::invalid_argument("unknown agent option '" + k + "'");
         }
         py::gil_scoped_release nogil;

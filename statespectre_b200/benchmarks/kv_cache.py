@@ -3,8 +3,10 @@
 Workload: a paged KV cache of 16-token blocks x 64 layers x 8 KV heads x
 head_dim 128, bf16 N(0,1) (4 MiB per block), ``--kv-gb`` per GPU (default
 40 GB). Every iteration a seeded random ``--evict-fraction`` of the blocks is
-evicted (batched reservations, one round trip per batch) and restored into
-place while a bf16 GEMM loop stands in for the training step. The pinned
+evicted and restored into place with one ``evict_batch``/``restore_batch``
+call each (``--kv-batch`` splits it; the agent reserves and launches in
+groups of 256 MiB, one round trip and one kernel launch per group) while a
+bf16 GEMM loop stands in for the training step. The pinned
 window per GPU is ``--pinned-gb``: when it is smaller than the evicted set,
 the daemon drains to pageable DRAM (and NVMe when enabled) and restores read
 back, exercising the tiers. Device time per iteration is the max over ranks.
@@ -34,7 +36,7 @@ def run(args, metric: str) -> dict:
     kv_bytes = int(args.kv_gb * GiB)
     nblocks = spec.blocks_for(kv_bytes)
     per_iter = max(1, int(round(args.evict_fraction * nblocks)))
-    batch = max(1, args.kv_batch)
+    batch = args.kv_batch if args.kv_batch > 0 else per_iter
     pinned_gb = args.pinned_gb or int(per_iter * spec.block_bytes * 1.2 / GiB) + 2
     sock, daemon = node_daemon(env, pinned_gb, "/tmp/ofld_kv", slot_mb=4)
     sess = offload_context(daemon_addr=sock, device=env.device, rank=env.rank, local_rank=env.local_rank,

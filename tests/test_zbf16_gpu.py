@@ -186,3 +186,28 @@ def test_batch_evict_codes_kv_blocks(zsession):
     assert torch.equal(cache, ref)
     for h in hs:
         h.discard()
+
+
+def test_batch_groups_mixed_items(sock_path):
+    """Several reservation groups, coded and uncoded items side by side."""
+    d = in_process_daemon(socket=sock_path, arena_mb=512, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", rank=0, batch_group_bytes=8 << 20) as off:
+            xs = [_case(4 << 20, "weights", seed=40 + i) for i in range(6)]
+            xs.append(torch.randn(1 << 20, device="cuda"))          # fp32: uncoded
+            xs.append(_case(1 << 20, "normal", seed=50))            # below the coding floor
+            rb = torch.randint(0, 256, (4 << 20,), dtype=torch.uint8, device="cuda")
+            xs.append(rb.view(torch.bfloat16))                      # random bits: scan fails
+            refs = [x.clone() for x in xs]
+            hs = off.evict_batch(xs)
+            assert [h.coded for h in hs] == [True] * 6 + [False, False, False]
+            for x in xs:
+                x.zero_()
+            off.restore_batch(hs, xs)
+            torch.cuda.synchronize()
+            for x, r in zip(xs, refs):  # bytes: the random-bits item holds NaNs
+                assert torch.equal(x.view(torch.uint8), r.view(torch.uint8))
+            for h in hs:
+                h.discard()
+    finally:
+        d.stop()
