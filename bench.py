@@ -64,6 +64,10 @@ def parse():
     p.add_argument("--model", default="", help="weight_sync: qwen2.5-32b (default); dp_dedup: llama-3-8b (default)")
     p.add_argument("--layers", type=int, default=0, help="weight_sync: layer count override (0 = the model's)")
     p.add_argument("--push-mode", default="bf16", choices=["bf16", "fp8"])
+    p.add_argument("--rollout-replicas", type=int, default=1,
+                   help="weight_sync: rollout engines fed by each trainer shard (GPUs split 1 + R ways)")
+    p.add_argument("--transport", default="auto", choices=["auto", "p2p", "multicast"],
+                   help="weight_sync: NVLS multicast team or one point-to-point push per replica")
     p.add_argument("--persist", type=int, default=1, help="weight_sync: seal every version in offloadd")
     p.add_argument("--verify", type=int, default=1, help="weight_sync: rollout re-hashes what it received")
     p.add_argument("--change-fraction", type=float, default=0.1)

@@ -127,9 +127,13 @@ inline uint64_t digest_count(uint64_t nbytes) { return (nbytes + 65535) / 65536;
 //   flags kPushDelta  skip the stores of a chunk whose new digest equals the
 //                     digest already in the launch's `digests` table (the
 //                     table describes what the destination holds)
-// `dst` / `dst_scales` are typically peer-GPU pointers (CUDA IPC mappings).
+//         kPushMulticast  `dst` / `dst_scales` are addresses in a multicast
+//                     team mapping: stores are `multimem.st`, so the NVSwitch
+//                     writes every member's buffer
+// Without kPushMulticast, `dst` / `dst_scales` are typically peer-GPU
+// pointers (CUDA IPC or VMM mappings).
 enum : uint32_t { kPushRaw = 0, kPushFp8 = 1, kPushHash = 2 };
-enum : uint32_t { kPushDelta = 1u << 0 };
+enum : uint32_t { kPushDelta = 1u << 0, kPushMulticast = 1u << 1 };
 // `digest_base` is the index of the item's first chunk in the launch's digest
 // table (equal to chunk_begin for a full table; a subset launch keeps the
 // full table's indices so the record of what the destination holds stays put).

@@ -21,8 +21,9 @@
 //   * a second small launch folds every item's 128-bit object hash (manifest
 //     content hash) from the chunk digests.
 //
-// Peer memory is only ever the target of plain st.global from registers; the
-// bulk copies read this GPU's own memory and carry no multicast.
+// Peer memory is only ever the target of plain st.global (or, through a
+// multicast team mapping, multimem.st) from registers; the bulk copies read
+// this GPU's own memory and carry no multicast qualifier.
 // Every mbarrier wait is bounded (about two seconds of SM clock); on expiry the
 // kernel records an error code in PushState::error and returns.
 #include <cuda_bf16.h>
@@ -134,6 +135,22 @@ __device__ __forceinline__ void st_peer8(void* p, uint2 v) {
     asm volatile("st.global.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
 }
 
+// Stores through a multicast team mapping: one instruction, the NVSwitch
+// writes the bytes to every member GPU. The .f32 type only names the 32-bit
+// lanes; a store does no arithmetic, so every bit pattern arrives unchanged.
+__device__ __forceinline__ void st_multi(void* p, uint4 v) {
+    asm volatile("multimem.st.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void st_multi8(void* p, uint2 v) {
+    asm volatile("multimem.st.global.v2.f32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+
+__device__ __forceinline__ void st_multi4(void* p, float v) {
+    asm volatile("multimem.st.global.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
 __device__ __forceinline__ void group_sync(int g) {
     asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "n"(kGroupThreads) : "memory");
 }
@@ -164,8 +181,15 @@ __device__ __forceinline__ uint32_t chunk_len(const PushItem& it, uint64_t c) {
 // byte `base` of the item. Every lane of the warp calls this together (the
 // fp8 block amax is a half-warp reduction); `valid` masks the ragged tail.
 __device__ __forceinline__ void store_vec(const PushItem& it, uint64_t base, uint32_t vi, uint4 v, bool valid) {
+    const bool multi = (it.flags & kPushMulticast) != 0;
     if (it.mode == kPushRaw) {
-        if (valid) st_peer(static_cast<uint8_t*>(it.dst) + base + size_t(vi) * 16, v);
+        uint8_t* p = static_cast<uint8_t*>(it.dst) + base + size_t(vi) * 16;
+        if (valid) {
+            if (multi)
+                st_multi(p, v);
+            else
+                st_peer(p, v);
+        }
         return;
     }
     // 16 consecutive lanes hold one 128-element block (chunk bases are block aligned)
@@ -180,8 +204,14 @@ __device__ __forceinline__ void store_vec(const PushItem& it, uint64_t base, uin
         const uint64_t elem = base / 2 + uint64_t(vi) * 8;
         const uint2 q = make_uint2(pack_fp8(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv),
                                    pack_fp8(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv));
-        st_peer8(static_cast<uint8_t*>(it.dst) + elem, q);
-        if ((threadIdx.x & 15) == 0) it.dst_scales[elem / 128] = amax > 0.f ? amax / 448.f : 1.f;
+        const float scale = amax > 0.f ? amax / 448.f : 1.f;
+        if (multi) {
+            st_multi8(static_cast<uint8_t*>(it.dst) + elem, q);
+            if ((threadIdx.x & 15) == 0) st_multi4(it.dst_scales + elem / 128, scale);
+        } else {
+            st_peer8(static_cast<uint8_t*>(it.dst) + elem, q);
+            if ((threadIdx.x & 15) == 0) it.dst_scales[elem / 128] = scale;
+        }
     }
 }
 

@@ -1,6 +1,7 @@
 // Python bindings of the intra-node fabric (CUDA IPC export / open of device
-// buffers) and of the K4 weight-sync push kernel. Pointers cross as integers,
-// IPC handles as 64-byte `bytes`.
+// buffers; VMM buffers and multicast teams shared as fds) and of the K4
+// weight-sync push kernel. Pointers cross as integers, IPC handles as 64-byte
+// `bytes`.
 #include <cuda_runtime.h>
 #include <pybind11/pybind11.h>
 
@@ -8,6 +9,7 @@
 #include <string>
 
 #include "../fabric/fabric.h"
+#include "../fabric/vmm.h"
 #include "../kernels/kernels.h"
 
 namespace py = pybind11;
@@ -35,6 +37,40 @@ void bind_fabric(py::module_& m) {
     m.def("ipc_open_count", &fabric::open_count);
     m.def("can_access_peer", &fabric::can_access_peer);
     m.def("enable_peer", &fabric::enable_peer);
+    py::class_<fabric::Vmm>(m, "Vmm")
+        .def_readonly("ptr", &fabric::Vmm::ptr)
+        .def_readonly("size", &fabric::Vmm::size)
+        .def_readonly("device", &fabric::Vmm::device)
+        .def_readonly("imported", &fabric::Vmm::imported);
+    py::class_<fabric::Team>(m, "Team")
+        .def_readonly("size", &fabric::Team::size)
+        .def_readonly("mc_ptr", &fabric::Team::mc_ptr)
+        .def_readonly("ndevices", &fabric::Team::ndevices);
+    m.def("multicast_supported", &fabric::multicast_supported);
+    m.def("vmm_granularity", &fabric::granularity, py::arg("device"), py::arg("multicast") = false,
+          py::arg("ndevices") = 1);
+    m.def("vmm_alloc", &fabric::vmm_alloc, py::arg("device"), py::arg("nbytes"), py::arg("align_to") = 0);
+    m.def("vmm_free", [](fabric::Vmm& v) { fabric::vmm_free(v); });
+    m.def("vmm_export", &fabric::vmm_export);
+    m.def("vmm_import", &fabric::vmm_import, py::arg("fd"), py::arg("size"), py::arg("owner_device"),
+          py::arg("access_device"));
+    m.def("team_create", &fabric::team_create);
+    m.def("team_export", &fabric::team_export);
+    m.def("team_import", &fabric::team_import);
+    m.def("team_add_device", [](const fabric::Team& t, int device) {
+        py::gil_scoped_release r;
+        fabric::team_add_device(t, device);
+    });
+    m.def("team_bind", [](const fabric::Team& t, const fabric::Vmm& mem) {
+        py::gil_scoped_release r;
+        fabric::team_bind(t, mem);
+    });
+    m.def("team_map", [](fabric::Team& t, int device) {
+        py::gil_scoped_release r;
+        return fabric::team_map(t, device);
+    });
+    m.def("team_unbind", &fabric::team_unbind);
+    m.def("team_release", [](fabric::Team& t) { fabric::team_release(t); });
     m.def("push_item_bytes", [] { return int(sizeof(kern::PushItem)); });
     m.def(
         "k_push",

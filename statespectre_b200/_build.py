@@ -30,7 +30,7 @@ DAEMON = ["daemon/config.cpp", "daemon/daemon.cpp", "daemon/slots.cpp", "daemon/
           "daemon/nvme.cpp", "daemon/canonical.cpp", "daemon/rollout.cpp"]
 AGENT = ["agent/agent.cpp"]
 KERNELS = ["kernels/offload_kernels.cu", "kernels/weight_sync.cu", "kernels/hash_noalloc.cu"]
-FABRIC = ["fabric/fabric.cpp"]
+FABRIC = ["fabric/fabric.cpp", "fabric/vmm.cpp"]
 MODULE = ["python/module.cpp", "python/fabric_bind.cpp"]
 
 ARCH = "-gencode arch=compute_100a,code=sm_100a"

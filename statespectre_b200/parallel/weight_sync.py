@@ -25,6 +25,7 @@ bytes take one hop instead:
 from __future__ import annotations
 
 import math
+import os
 import struct
 import time
 from dataclasses import dataclass
@@ -39,7 +40,8 @@ ALIGN = 256
 CHUNK = 64 * 1024
 _ITEM = struct.Struct("<QQQQQIIQQ")  # PushItem: src, dst, dst_scales, nbytes, chunk_begin, mode, flags, digest_base, -
 PUSH_RAW, PUSH_FP8, PUSH_HASH = 0, 1, 2
-PUSH_DELTA = 1
+PUSH_DELTA, PUSH_MULTICAST = 1, 2
+TRANSPORTS = ("auto", "p2p", "multicast")
 
 
 def _align(n: int) -> int:
@@ -103,18 +105,62 @@ class WeightLayout:
 
 
 class RolloutWeights:
-    """Rollout-side receive buffer holding every parameter of a layout."""
+    """Rollout-side receive buffer holding every parameter of a layout.
 
-    def __init__(self, layout: WeightLayout, device=None):
+    The buffer comes from the CUDA virtual memory API when the driver offers
+    it (shareable as an fd, sized to join a multicast team), else from
+    torch's allocator (shared through CUDA IPC, point-to-point only)."""
+
+    def __init__(self, layout: WeightLayout, device=None, vmm: Optional[bool] = None):
         self.layout = layout
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-        self.buf = torch.zeros(layout.total_bytes, dtype=torch.uint8, device=self.device)
         self.key: Optional[str] = None
+        self.dbuf: Optional[fabric.DeviceBuffer] = None
+        self.membership = None
+        self.transport: Optional[str] = None
+        if vmm is None:
+            vmm = fabric.vmm_available(self.device.index)
+        if vmm:
+            align = fabric.team_granularity(self.device.index) if fabric.multicast_supported(self.device.index) else 0
+            self.dbuf = fabric.DeviceBuffer(layout.total_bytes, self.device, align)
+            self.buf = self.dbuf.tensor
+            self.buf.zero_()
+        else:
+            self.buf = torch.zeros(layout.total_bytes, dtype=torch.uint8, device=self.device)
 
     def publish(self, off, key: str) -> dict:
         """Make the buffer reachable by trainer ranks as ``key``."""
         self.key = key
+        if self.dbuf is not None:
+            return fabric.publish_vmm(off, key, self.dbuf, kind=fabric.KIND_WEIGHTS)
         return fabric.publish(off, key, self.buf, kind=fabric.KIND_WEIGHTS)
+
+    def connect(self, off, wait_ms: int = 60000) -> str:
+        """Wait for the trainer that feeds this buffer (in another process)
+        and join its multicast team when it builds one. Returns the
+        transport, "multicast" or "p2p"."""
+        if self.key is None:
+            raise RuntimeError("publish() the buffer first")
+        if self.dbuf is None:
+            fabric.wait_signal(off, f"wsync/invite/{self.key}", wait_ms)
+            self.transport = "p2p"
+        else:
+            self.membership = fabric.join(off, self.key, self.dbuf, wait_ms)
+            self.transport = "multicast" if self.membership is not None else "p2p"
+        return self.transport
+
+    def close(self, wait_ms: int = 60000) -> None:
+        """Leave the multicast team (after its trainer closed it) and free
+        the buffer; views returned by ``get`` must not be used afterwards."""
+        if self.membership is not None:
+            self.membership.close(wait_ms)
+            self.membership = None
+        if self.dbuf is not None:
+            if self.key is not None:
+                fabric._LOCAL_VMM.pop(self.key, None)
+            self.buf = None
+            self.dbuf.close()
+            self.dbuf = None
 
     def get(self, name: str):
         """bf16 view of a parameter, or (fp8 e4m3 view, fp32 scales) when quantized."""
@@ -155,8 +201,9 @@ class RolloutWeights:
             self._hash_chunks = chunk
             self._hash_key = key
         s = stream or torch.cuda.current_stream(self.device)
-        native().k_push(self._hash_items.data_ptr(), len(ents), self._hash_chunks, self._hash_dig.data_ptr(),
-                        self._hash_out.data_ptr(), 0, self._hash_err.data_ptr(), s.cuda_stream, 0, 0)
+        with torch.cuda.device(self.device):
+            native().k_push(self._hash_items.data_ptr(), len(ents), self._hash_chunks, self._hash_dig.data_ptr(),
+                            self._hash_out.data_ptr(), 0, self._hash_err.data_ptr(), s.cuda_stream, 0, 0)
         s.synchronize()
         if int(self._hash_err.item()):
             raise RuntimeError(f"hash pass failed with device status {int(self._hash_err.item())}")
@@ -174,12 +221,13 @@ class WeightPusher:
     the skip; ``invalidate()`` forces the next push to send everything."""
 
     def __init__(self, params: Dict[str, torch.Tensor], layout: WeightLayout, dst_ptr: int, device=None,
-                 delta: bool = True, ctas: int = 0):
+                 delta: bool = True, ctas: int = 0, multicast: bool = False):
         self.params = params
         self.layout = layout
         self.dst_ptr = int(dst_ptr)
         self.delta = delta
         self.ctas = ctas
+        self.multicast = multicast  # dst_ptr is a multicast team mapping
         first = next(iter(params.values()))
         self.device = torch.device(device) if device is not None else first.device
         n = len(layout.entries)
@@ -214,8 +262,9 @@ class WeightPusher:
             ptrs.append(p)
             mode = PUSH_FP8 if e.quant else PUSH_RAW
             scales = self.dst_ptr + e.scale_offset if e.quant else 0
-            buf += _ITEM.pack(p, self.dst_ptr + e.dst_offset, scales, e.nbytes, work, mode,
-                              PUSH_DELTA if self.delta else 0, self._digest_base[e.name], 0)
+            flags = (PUSH_DELTA if self.delta else 0) | (PUSH_MULTICAST if self.multicast else 0)
+            buf += _ITEM.pack(p, self.dst_ptr + e.dst_offset, scales, e.nbytes, work, mode, flags,
+                              self._digest_base[e.name], 0)
             work += (e.nbytes + CHUNK - 1) // CHUNK
         host = torch.frombuffer(buf, dtype=torch.uint8) if buf else torch.zeros(64, dtype=torch.uint8)
         return host.to(self.device), work, ptrs
@@ -286,16 +335,26 @@ class TrainerWeightSync:
     """Trainer side of in-box weight sync for one TP/PP shard.
 
     ``publish_version(v)`` pushes the changed chunks of ``params`` into every
-    rollout buffer in ``rollout_keys`` (K4, one launch per destination), then,
+    rollout buffer in ``rollout_keys`` (the replicas of this shard), then,
     with ``persist=True``, records version ``v`` in offloadd: changed
     parameters are copied (K1) as new canonical objects, unchanged ones are
     carried forward from ``v - 1``, and the version is sealed and promoted.
+
+    ``transport``: "multicast" builds an NVLS multicast team over this GPU
+    and every rollout buffer, so one K4 launch with ``multimem.st`` stores
+    feeds all replicas through the NVSwitch; "p2p" maps each buffer and runs
+    one K4 launch per replica with plain stores over NVLink; "auto" takes
+    multicast for two or more replicas when every buffer is VMM-shared on its
+    own GPU and the GPUs support it, else p2p. Rollout ranks in other
+    processes call ``RolloutWeights.connect`` to take part.
     """
 
     def __init__(self, off, params: Dict[str, torch.Tensor], rollout_keys: Sequence[str], mode: str = "bf16",
                  model_role="policy_rollout", persist: bool = True, tp_rank: int = 0, pp_rank: int = 0,
-                 lookup_wait_ms: int = 60000, ctas: int = 0):
+                 lookup_wait_ms: int = 60000, ctas: int = 0, transport: str = "auto"):
         from ..api import ModelRole
+        if transport not in TRANSPORTS:
+            raise ValueError(f"transport must be one of {TRANSPORTS}")
         self.off = off
         self.params = dict(params)
         self.layout = WeightLayout.from_params(self.params, mode)
@@ -304,16 +363,51 @@ class TrainerWeightSync:
         self.tp_rank, self.pp_rank = tp_rank, pp_rank
         first = next(iter(self.params.values()))
         self.device = first.device
-        self.peers = [fabric.lookup(off, k, lookup_wait_ms) for k in rollout_keys]
-        for p in self.peers:
-            if p.nbytes < self.layout.total_bytes:
-                raise ValueError(f"rollout buffer {p.key!r} holds {p.nbytes} bytes, layout needs "
-                                 f"{self.layout.total_bytes}")
-        self.pushers = [WeightPusher(self.params, self.layout, p.ptr, self.device, ctas=ctas) for p in self.peers]
+        self.team: Optional[fabric.MulticastTeam] = None
+        self.peers = []
+        found = [fabric.lookup_desc(off, k, lookup_wait_ms) for k in rollout_keys]
+        try:
+            for desc, _ in found:
+                if desc["nbytes"] < self.layout.total_bytes:
+                    raise ValueError(f"rollout buffer {desc['key']!r} holds {desc['nbytes']} bytes, layout needs "
+                                     f"{self.layout.total_bytes}")
+            self.transport = self._choose(transport, [d for d, _ in found])
+            if self.transport == "multicast":
+                members = [fabric.member_of(d) for d, _ in found]
+                self.team = fabric.MulticastTeam(off, f"{rollout_keys[0]}#{off.rank}", members, self.device.index,
+                                                 self.layout.total_bytes, lookup_wait_ms)
+                self.pushers = [WeightPusher(self.params, self.layout, self.team.ptr, self.device, ctas=ctas,
+                                             multicast=True)]
+            else:
+                self.peers = [fabric.open_desc(d, fd) for d, fd in found]
+                for d, _ in found:
+                    if d["key"] not in fabric._LOCAL_VMM:
+                        fabric.signal(off, f"wsync/invite/{d['key']}", b"p2p")
+                self.pushers = [WeightPusher(self.params, self.layout, p.ptr, self.device, ctas=ctas)
+                                for p in self.peers]
+        finally:
+            for _, fd in found:
+                if fd >= 0:
+                    os.close(fd)
         self.stream = torch.cuda.Stream(self.device)
         self.last_hash: Dict[str, Tuple[int, int]] = {}
         self.last_version: Optional[int] = None
         self._pids: Dict[str, int] = {}
+
+    def _choose(self, transport: str, descs) -> str:
+        if transport == "p2p":
+            return "p2p"
+        dev = self.device.index
+        devices = [int(d["device"]) for d in descs]
+        ok = (all(fabric.is_vmm_desc(d) for d in descs) and len(set(devices)) == len(devices)
+              and len(set(devices) | {dev}) >= 2
+              and all(fabric.multicast_supported(x) for x in set(devices) | {dev}))
+        if transport == "multicast":
+            if not ok:
+                raise RuntimeError("multicast transport needs VMM-shared rollout buffers on distinct GPUs "
+                                   "(two or more GPUs in all) with switch multicast support")
+            return "multicast"
+        return "multicast" if ok and len(descs) >= 2 else "p2p"
 
     def _key(self, name: str, version: int):
         k = self.off.canonical_key(model_role=self.role, model_version=version, param_name=name,
@@ -376,6 +470,12 @@ class TrainerWeightSync:
         return out
 
     def close(self) -> None:
+        """Release the mappings (and the multicast team: its members may
+        leave after this)."""
+        torch.cuda.synchronize(self.device)
+        if self.team is not None:
+            self.team.close()
+            self.team = None
         for p in self.peers:
             p.close()
         self.peers = []

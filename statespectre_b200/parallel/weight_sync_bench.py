@@ -1,9 +1,12 @@
-"""In-box RL weight-sync benchmark (trainer TP=N/2 GPUs -> rollout TP=N/2 GPUs).
+"""In-box RL weight-sync benchmark (trainer TP=N/(1+R) GPUs -> R rollout
+engines of the same TP).
 
 Workload: the trainer holds a Qwen2.5-32B-shaped bf16 model, random-init
-N(0, 0.02), tensor-parallel over the first N/2 GPUs; the rollout engine holds
-the same shards on the last N/2 GPUs (trainer tp rank r pushes to rollout tp
-rank r). Every version, a seeded 10 % of the tensors get +N(0, 1e-3); the
+N(0, 0.02), tensor-parallel over the first N/(1+R) GPUs; each of the R
+rollout engines (``--rollout-replicas``, default 1) holds the same shards on
+the next N/(1+R) GPUs (trainer tp rank r feeds tp rank r of every engine:
+one NVLS multicast push for all of them, or one point-to-point push each,
+``--transport``). Every version, a seeded 10 % of the tensors get +N(0, 1e-3); the
 update arrives from pinned host memory (H2D) and is applied on the trainer.
 The trainer then pushes the version (K4: hash every chunk, move only chunks
 whose digest changed, quantize in fp8 mode) into the rollout's receive buffer
@@ -42,16 +45,18 @@ def run(args, metric: str) -> dict:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if world < 2 or world % 2:
-        raise SystemExit("weight_sync needs an even number of GPUs >= 2 (trainer half, rollout half)")
+    replicas = max(1, int(getattr(args, "rollout_replicas", 1)))
+    if world < 2 or world % (1 + replicas):
+        raise SystemExit(f"weight_sync needs a multiple of {1 + replicas} GPUs (trainer + {replicas} rollout engines)")
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     # trainer/rollout pairs exchange hashes with plain send/recv on the default group
     os.environ.setdefault("TORCH_NCCL_SHOW_EAGER_INIT_P2P_SERIALIZATION_WARNING", "false")
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
-    tp = world // 2
+    tp = world // (1 + replicas)
     trainer = rank < tp
     tp_rank = rank % tp
+    engine = rank // tp - 1  # rollout engine index (-1 on trainer ranks)
     spec = MODELS.get(args.model or "qwen2.5-32b", QWEN2_5_32B)
     shapes = param_shapes(spec, tp_rank, tp, layers=args.layers or None)
     shard_bytes = num_params(shapes) * 2
@@ -90,11 +95,17 @@ def run(args, metric: str) -> dict:
     names = [n for n, _ in shapes]
     if not trainer:
         rw = RolloutWeights(layout, device)
-        rw.publish(off, f"rollout/{tp_rank}")
+        rw.publish(off, f"rollout/{engine}/{tp_rank}")
     dist.barrier()
     if trainer:
         params = random_init(shapes, device, seed=1000 + tp_rank)
-        tr = TrainerWeightSync(off, params, [f"rollout/{tp_rank}"], mode=mode, persist=persist, tp_rank=tp_rank)
+        tr = TrainerWeightSync(off, params, [f"rollout/{j}/{tp_rank}" for j in range(replicas)], mode=mode,
+                               persist=persist, tp_rank=tp_rank, transport=args.transport)
+    else:
+        rw.connect(off)
+    dist.barrier()
+    transport = tr.transport if trainer else rw.transport
+    if trainer:
         # pinned host pool of update deltas: as large as the largest tensor,
         # sliced cyclically (N(0, delta_std) drawn on the GPU, copied once)
         biggest = max(t.numel() for t in params.values())
@@ -103,7 +114,7 @@ def run(args, metric: str) -> dict:
         pool = torch.empty(biggest, dtype=torch.bfloat16, pin_memory=True)
         pool.copy_(scratch)
     nitems = len(shapes)
-    peer = rank + tp if trainer else rank - tp
+    peers = [tp_rank + tp * (1 + j) for j in range(replicas)] if trainer else [tp_rank]
     hbuf = torch.zeros(2 * nitems, dtype=torch.int64, device=device)
     ack = torch.zeros(2, dtype=torch.int64, device=device)
     ack_host = torch.zeros(2, dtype=torch.int64, pin_memory=True)
@@ -135,11 +146,16 @@ def run(args, metric: str) -> dict:
             res = tr.publish_version(v, changed=hint)
             pushed = tr.pushers[0].result()["bytes_stored"] - before
             hbuf.copy_(tr.pushers[0].item_hash)
-            dist.send(hbuf, peer)
-            dist.recv(ack, peer)
-            ack_host.copy_(ack)  # D2H of the rollout's answer
+            for q in peers:
+                dist.send(hbuf, q)
+            acks = 0
+            for q in peers:
+                dist.recv(ack, q)
+                acks += int(ack[0].item())
+            ack.fill_(acks)
+            ack_host.copy_(ack)  # D2H of the rollouts' answers
         else:
-            dist.recv(hbuf, peer)
+            dist.recv(hbuf, peers[0])
             ok = 1
             if args.verify and mode == "bf16":
                 got = rw.content_hashes()
@@ -149,7 +165,7 @@ def run(args, metric: str) -> dict:
                     if got[e.name] != (want[i][0] & m, want[i][1] & m):
                         ok = 0
             ack.fill_(ok)
-            dist.send(ack, peer)
+            dist.send(ack, peers[0])
         t2 = time.perf_counter()
         if stats is not None:
             vals = torch.tensor([res.get("push_ms", 0.0), res.get("seal_wall_ms", 0.0), (t2 - t0) * 1e3,
@@ -193,9 +209,12 @@ def run(args, metric: str) -> dict:
                     "+N(0,1e-3) per version, update fed from pinned host memory",
             "config": {"model": f"{spec.name}-shaped" + (f" ({args.layers} layers)" if args.layers else ""),
                        "params": num_params(full), "model_bytes": num_params(full) * 2,
-                       "trainer": f"TP={tp} on GPUs 0-{tp - 1}", "rollout": f"TP={tp} on GPUs {tp}-{world - 1}",
-                       "push_mode": mode, "change_fraction": args.change_fraction, "global_batch": 1, "seq_len": 0,
-                       "parallelism": f"tp{tp}->tp{tp}", "persist": persist, "slot_mb": 2,
+                       "trainer": f"TP={tp} on GPUs 0-{tp - 1}",
+                       "rollout": f"{replicas} x TP={tp} on GPUs {tp}-{world - 1}",
+                       "transport": transport, "push_mode": mode, "change_fraction": args.change_fraction,
+                       "global_batch": 1, "seq_len": 0,
+                       "parallelism": f"tp{tp}->tp{tp}" + (f" x{replicas}" if replicas > 1 else ""),
+                       "persist": persist, "slot_mb": 2,
                        "change_detection": "caller hint" if args.hint else "device hash of every tensor",
                        "l2": "every push reads the whole shard (GBs) from HBM; no flush needed"},
             "push_ms_p90": round(push[min(len(push) - 1, int(0.9 * len(push)))], 4),
@@ -209,11 +228,14 @@ def run(args, metric: str) -> dict:
                     "unit": "ms (host wall: H2D update + push + seal + rollout verify + D2H answer, max over ranks)",
                     "h2d_bytes_per_step": int(statistics.median(stats["h2d"])),
                     "d2h_bytes_per_step": 16 * tp},
+            "delivered_bytes_per_version": int(statistics.median(stats["bytes"])) * replicas,
             "gpu_launches": int(launches.item()),
             "clocks": clocks,
         }
     if tr:
         tr.close()
+    if rw:
+        rw.close()
     sess.close()
     dist.barrier()
     dist.destroy_process_group()

@@ -21,7 +21,7 @@ def _specs():
             ("w2", (3000, 512), "bfloat16")]
 
 
-def _rollout(sock, mode, q_in, q_out):
+def _rollout(sock, mode, transport, q_in, q_out):
     import torch
 
     from statespectre_b200 import offload_context
@@ -32,8 +32,9 @@ def _rollout(sock, mode, q_in, q_out):
         with offload_context(daemon_addr=sock, device="cuda:1", rank=1, job_name="fabric2") as off:
             layout = WeightLayout([(n, s, getattr(torch, d)) for n, s, d in _specs()], mode)
             rw = RolloutWeights(layout, "cuda:1")
-            rw.publish(off, f"rollout/{mode}")
+            rw.publish(off, f"rollout/{mode}/{transport}")
             q_out.put(("published", layout.fingerprint))
+            q_out.put(("connected", rw.connect(off, TIMEOUT * 1000)))
             while True:
                 msg = q_in.get(timeout=TIMEOUT)
                 if msg[0] == "done":
@@ -49,6 +50,7 @@ def _rollout(sock, mode, q_in, q_out):
                     for n, t in host.items():
                         ok &= torch.allclose(rw.dequantized(n).float().cpu(), t.float(), rtol=0.07, atol=1e-6)
                 q_out.put(("checked", version, bool(ok)))
+            rw.close(TIMEOUT * 1000)
     except Exception as e:  # noqa: BLE001
         q_out.put(("error", repr(e)))
 
@@ -59,16 +61,20 @@ def two_gpus():
         pytest.skip("needs 2 GPUs")
 
 
+@pytest.mark.parametrize("transport", ["p2p", "multicast"])
 @pytest.mark.parametrize("mode", ["bf16", "fp8"])
-def test_push_across_gpus_and_verify_peer(two_gpus, sock_path, mode):
+def test_push_across_gpus_and_verify_peer(two_gpus, sock_path, mode, transport):
     from statespectre_b200 import in_process_daemon, offload_context
     from statespectre_b200._native import native
+    from statespectre_b200.parallel import fabric
     from statespectre_b200.parallel.weight_sync import TrainerWeightSync
 
+    if transport == "multicast" and not (fabric.multicast_supported(0) and fabric.multicast_supported(1)):
+        pytest.skip("no switch multicast on these GPUs")
     d = in_process_daemon(socket=sock_path, arena_mb=1024, drain_on_complete=False)
     ctx = mp.get_context("spawn")
     q_in, q_out = ctx.Queue(), ctx.Queue()
-    child = ctx.Process(target=_rollout, args=(sock_path, mode, q_in, q_out))
+    child = ctx.Process(target=_rollout, args=(sock_path, mode, transport, q_in, q_out))
     child.start()
     try:
         with offload_context(daemon_addr=sock_path, device="cuda:0", rank=0, job_name="fabric2") as off:
@@ -76,8 +82,10 @@ def test_push_across_gpus_and_verify_peer(two_gpus, sock_path, mode):
             params = {n: (torch.randn(s, device="cuda:0") * 0.02).to(getattr(torch, dt)) for n, s, dt in _specs()}
             tag, fp = q_out.get(timeout=TIMEOUT)
             assert tag == "published"
-            tr = TrainerWeightSync(off, params, [f"rollout/{mode}"], mode=mode)
+            tr = TrainerWeightSync(off, params, [f"rollout/{mode}/{transport}"], mode=mode, transport=transport)
             assert tr.layout.fingerprint == fp
+            assert tr.transport == transport
+            assert q_out.get(timeout=TIMEOUT) == ("connected", transport)
             for version in (1, 2):
                 if version == 2:
                     params["w1"].add_(0.5)
@@ -86,7 +94,7 @@ def test_push_across_gpus_and_verify_peer(two_gpus, sock_path, mode):
                 q_in.put(("check", version, tr.pushers[0].hashes(), {n: t.cpu() for n, t in params.items()}))
                 msg = q_out.get(timeout=TIMEOUT)
                 assert msg == ("checked", version, True), msg
-            if mode == "bf16":
+            if mode == "bf16" and transport == "p2p":
                 # K3: compare the local parameter with the rollout's copy by P2P loads
                 C = native()
                 peer = tr.peers[0]
@@ -109,4 +117,52 @@ def test_push_across_gpus_and_verify_peer(two_gpus, sock_path, mode):
         if child.is_alive():
             child.kill()
             child.join(10)
+        d.stop()
+
+
+@pytest.mark.parametrize("mode", ["bf16", "fp8"])
+def test_multicast_team_in_one_process(two_gpus, sock_path, mode):
+    """Trainer on cuda:0 and two rollout buffers (cuda:1 and a second one on
+    cuda:0) in one process: a two-GPU team, one K4 launch with multimem.st
+    stores fills both."""
+    from statespectre_b200 import in_process_daemon, offload_context
+    from statespectre_b200.parallel import fabric
+    from statespectre_b200.parallel.weight_sync import RolloutWeights, TrainerWeightSync, WeightLayout
+
+    if not (fabric.multicast_supported(0) and fabric.multicast_supported(1)):
+        pytest.skip("no switch multicast on these GPUs")
+    d = in_process_daemon(socket=sock_path, arena_mb=256, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", rank=0, job_name="wsync-mc2") as off:
+            torch.manual_seed(1)
+            params = {n: (torch.randn(s, device="cuda:0") * 0.02).to(getattr(torch, dt)) for n, s, dt in _specs()}
+            layout = WeightLayout.from_params(params, mode)
+            rws = [RolloutWeights(layout, "cuda:1"), RolloutWeights(layout, "cuda:0")]
+            keys = [f"rollout/mc2/{mode}/{i}" for i in range(2)]
+            for rw, k in zip(rws, keys):
+                rw.publish(off, k)
+            tr = TrainerWeightSync(off, params, keys, mode=mode, persist=False)  # auto: 2 replicas -> multicast
+            assert tr.transport == "multicast" and tr.team.ndevices == 2 and tr.team.scratch is None
+            assert len(tr.pushers) == 1
+            tr.publish_version(1)
+            full = tr.pushers[0].result()["bytes_stored"]
+            params["w1"].add_(0.5)
+            r2 = tr.publish_version(2)
+            assert r2["changed"] == 1
+            assert tr.pushers[0].result()["bytes_stored"] - full == params["w1"].numel() * 2
+            torch.cuda.synchronize(0)
+            torch.cuda.synchronize(1)
+            for rw in rws:
+                for n, t in params.items():
+                    if mode == "bf16" or not layout.by_name[n].quant:
+                        assert torch.equal(rw.get(n).to("cuda:0"), t), n
+                    else:
+                        got = rw.dequantized(n).float().to("cuda:0")
+                        assert torch.allclose(got, t.float(), rtol=0.07, atol=1e-6), n
+                if mode == "bf16":
+                    assert rw.content_hashes() == tr.pushers[0].hashes()
+            tr.close()
+            for rw in rws:
+                rw.close()
+    finally:
         d.stop()

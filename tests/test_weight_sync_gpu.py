@@ -165,3 +165,52 @@ def test_subset_push_updates_hash_rows_and_digest_table():
     # the digest table now describes the destination: a full delta push moves nothing
     p.push()
     assert p.result()["bytes_stored"] == full + sub
+
+
+def test_multicast_needs_two_gpus(sock_path):
+    from statespectre_b200.parallel import fabric
+
+    if not fabric.vmm_available(0):
+        pytest.skip("no CUDA virtual memory management")
+    d = in_process_daemon(socket=sock_path, arena_mb=256, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", rank=0, job_name="wsync-mc1") as off:
+            params = _params(5)
+            rw = RolloutWeights(WeightLayout.from_params(params, "bf16"))
+            rw.publish(off, "rollout/mc1")
+            with pytest.raises(RuntimeError, match="two or more GPUs"):
+                TrainerWeightSync(off, params, ["rollout/mc1"], persist=False, transport="multicast")
+            tr = TrainerWeightSync(off, params, ["rollout/mc1"], persist=False)  # auto: one GPU -> p2p
+            assert tr.transport == "p2p"
+            tr.close()
+            rw.close()
+    finally:
+        d.stop()
+
+
+def test_vmm_buffer_tensor_view_and_p2p_push(sock_path):
+    from statespectre_b200.parallel import fabric
+
+    if not fabric.vmm_available(0):
+        pytest.skip("no CUDA virtual memory management")
+    buf = fabric.DeviceBuffer(3 << 20, "cuda:0")
+    assert buf.size >= 3 << 20 and buf.tensor.numel() == 3 << 20 and buf.tensor.data_ptr() == buf.ptr
+    buf.tensor.fill_(7)
+    assert int(buf.tensor.sum().item()) == 7 * (3 << 20)
+    buf.close()
+    d = in_process_daemon(socket=sock_path, arena_mb=256, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", rank=0, job_name="wsync-vmm") as off:
+            params = _params(6)
+            layout = WeightLayout.from_params(params, "bf16")
+            rw = RolloutWeights(layout)
+            rw.publish(off, "rollout/vmm")
+            tr = TrainerWeightSync(off, params, ["rollout/vmm"], persist=False, transport="p2p")
+            tr.publish_version(1)
+            torch.cuda.synchronize()
+            for n, t in params.items():
+                assert torch.equal(rw.get(n), t), n
+            tr.close()
+            rw.close()
+    finally:
+        d.stop()
