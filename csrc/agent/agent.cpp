@@ -24,6 +24,7 @@
 #include <unordered_map>
 
 #include "../kernels/kernels.h"
+#include "../kernels/timing.h"
 #include "ofld/abi/offload_canonical_abi.hpp"
 #include "ofld/chunk_hash.h"
 #include "ofld/zbf16.h"
@@ -160,6 +161,7 @@ struct Agent::Impl {
         gpu = opt.device >= 0;
         if (gpu) {
             CUDA_OK(cudaSetDevice(opt.device));
+            if (opt.kernel_timing) CUDA_OK(kern::timing_enable(opt.device, 4096));
             if (opt.numa_node < 0) {
                 char bus[32] = {0};
                 if (cudaDeviceGetPCIBusId(bus, sizeof(bus), opt.device) == cudaSuccess) numa = pci_numa_node(bus);

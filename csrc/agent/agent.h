@@ -53,6 +53,9 @@ struct AgentOptions {
     // many bytes: one daemon round trip and one kernel launch per group, the
     // round trip of the next group overlapping the copy of this one.
     uint64_t batch_group_bytes = 256ull << 20;
+    // Device-side kernel timing (%globaltimer stamps into a host-mapped ring,
+    // read with Agent::kernel_timings / statespectre_b200.Off.kernel_timings).
+    bool kernel_timing = false;
 };
 
 // evict() data hints.

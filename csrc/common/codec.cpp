@@ -41,6 +41,7 @@ const char* op_name(Op op) {
         case Op::kExportManifest: return "ExportManifest";
         case Op::kDiscardTensor: return "DiscardTensor";
         case Op::kCarryForward: return "CarryForward";
+        case Op::kGetAgentOptions: return "GetAgentOptions";
     }
     return "Unknown";
 }
@@ -89,6 +90,7 @@ std::vector<uint8_t> reencode_body(Op op, bool response, const std::vector<uint8
         CASE(kBatchRequestOffload) CASE(kBatchRequestPrefetch) CASE(kPublishPeerBuffer)
         CASE(kLookupPeerBuffer) CASE(kGetJobStats) CASE(kExportManifest) CASE(kDiscardTensor)
         CASE(kCarryForward)
+        CASE(kGetAgentOptions)
 #undef CASE
         default: break;
     }

@@ -411,6 +411,7 @@ void Daemon::dispatch(int fd, Op op, const std::vector<uint8_t>& b, std::vector<
         ROUTE(kExportManifest, on_export_manifest(req))
         ROUTE(kDiscardTensor, on_discard_tensor(req))
         ROUTE(kCarryForward, on_carry_forward(req))
+        ROUTE(kGetAgentOptions, on_get_agent_options(req))
         default:
             LOG_WARN(TAG, "unknown opcode %u", unsigned(op));
             throw std::runtime_error("unknown opcode");
@@ -720,6 +721,16 @@ LookupPeerBufferResponse Daemon::on_lookup_peer_buffer(const LookupPeerBufferReq
             }
         }
     }
+}
+
+// The `kernels:` and `nvlink:` sections of the config, flattened to dotted
+// keys; sessions apply them before they start (explicit options win).
+GetAgentOptionsResponse Daemon::on_get_agent_options(const GetAgentOptionsRequest&) {
+    GetAgentOptionsResponse resp;
+    resp.ok = true;
+    resp.message = "ok";
+    for (const auto& kv : cfg_.agent_options) resp.options.push_back(OptionEntry{kv.first, kv.second});
+    return resp;
 }
 
 GetJobStatsResponse Daemon::on_get_job_stats(const GetJobStatsRequest& r) {

@@ -255,6 +255,7 @@ class Daemon {
     StatusResponse on_publish_peer_buffer(const PublishPeerBufferRequest& r, std::vector<int>* fds_in);
     LookupPeerBufferResponse on_lookup_peer_buffer(const LookupPeerBufferRequest& r, std::vector<int>* fds_out);
     GetJobStatsResponse on_get_job_stats(const GetJobStatsRequest& r);
+    GetAgentOptionsResponse on_get_agent_options(const GetAgentOptionsRequest& r);
     StatusResponse on_discard_tensor(const DiscardTensorRequest& r);
 
     // canonical.cpp

@@ -57,6 +57,7 @@ enum class Op : uint16_t {
     kExportManifest = 45,        // write a sealed manifest in ABI record format
     kDiscardTensor = 46,         // drop a tensor's pinned and cold copies by identity
     kCarryForward = 47,          // new-version objects that share an older version's storage
+    kGetAgentOptions = 48,       // tuning the daemon config forwards to rank agents (kernels:, nvlink:)
 };
 
 const char* op_name(Op op);
@@ -709,6 +710,24 @@ struct GetJobStatsResponse {
     std::vector<JobStatsEntry> jobs;
 };
 template <class V> void fields(V& v, GetJobStatsResponse& m) { v(m.ok, m.message, m.jobs); }
+
+struct OptionEntry {
+    std::string key, value;
+};
+template <class V> void fields(V& v, OptionEntry& m) { v(m.key, m.value); }
+
+struct GetAgentOptionsRequest {
+    uint32_t rank_id = 0;
+    uint32_t gpu_id = 0;
+};
+template <class V> void fields(V& v, GetAgentOptionsRequest& m) { v(m.rank_id, m.gpu_id); }
+
+struct GetAgentOptionsResponse {
+    bool ok = false;
+    std::string message;
+    std::vector<OptionEntry> options;
+};
+template <class V> void fields(V& v, GetAgentOptionsResponse& m) { v(m.ok, m.message, m.options); }
 
 struct ExportManifestRequest {
     JobKeyWire job;

@@ -24,6 +24,7 @@
 #include <set>
 
 #include "kernels.h"
+#include "timing.h"
 #include "ofld/chunk_hash.h"
 #include "ofld/zbf16.h"
 
@@ -143,7 +144,8 @@ __device__ __forceinline__ uint64_t tree_fold(uint64_t d, uint64_t* red) {
 template <bool ALIGNED, bool HASH, bool STORE>
 __global__ void __launch_bounds__(kThreads, 2)
     k_evict(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
-            uint64_t* __restrict__ digests, int pol) {
+            uint64_t* __restrict__ digests, int pol, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
     __shared__ uint64_t red[kThreads / 32];
     const uint32_t t = threadIdx.x;
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
@@ -213,7 +215,8 @@ __device__ __forceinline__ uint2 quant8(uint4 v, bool valid, float* scale_out) {
 template <bool ALIGNED, bool VERIFY, int CAST>
 __global__ void __launch_bounds__(kThreads, 2)
     k_restore(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
-              float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, int pol) {
+              float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, int pol, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
     __shared__ uint64_t red[kThreads / 32];
     const uint32_t t = threadIdx.x;
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
@@ -356,7 +359,8 @@ __device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uin
 }
 
 __global__ void __launch_bounds__(kThreads, 3)
-    k_zscan(const uint8_t* __restrict__ src, uint64_t nbytes, uint8_t* __restrict__ ebase_out, uint32_t* fail) {
+    k_zscan(const uint8_t* __restrict__ src, uint64_t nbytes, uint8_t* __restrict__ ebase_out, uint32_t* fail, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
     __shared__ uint32_t red[kThreads / 32];
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
     for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
@@ -447,7 +451,8 @@ __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, u
 // nbytes % 16 == 0 (zbf16::eligible).
 __global__ void __launch_bounds__(kThreads, 2)
     k_evict_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
-              const uint8_t* __restrict__ ebase, uint64_t* __restrict__ digests, int pol) {
+              const uint8_t* __restrict__ ebase, uint64_t* __restrict__ digests, int pol, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
     extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint64_t red[kThreads / 32];
     __shared__ uint32_t sc[kThreads / 32];
@@ -471,7 +476,8 @@ __device__ __forceinline__ void advance_job(const XferJob* jobs, int n, uint64_t
 // `dst` is the job's scan buffer (one window base per chunk, then the fail
 // word at the next 16-byte boundary).
 __global__ void __launch_bounds__(kThreads, 3)
-    k_zscan_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks) {
+    k_zscan_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
     __shared__ uint32_t red[kThreads / 32];
     int idx = 0;
     for (uint64_t c = blockIdx.x; c < total_chunks; c += gridDim.x) {
@@ -493,7 +499,8 @@ __global__ void __launch_bounds__(kThreads, 3)
 // K1 over a batch: one grid walks every chunk of every job (raw or coded per
 // job), so many small tensors (KV-cache blocks) cost one launch.
 __global__ void __launch_bounds__(kThreads, 2)
-    k_evict_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, int pol) {
+    k_evict_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, int pol, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
     extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint64_t red[kThreads / 32];
     __shared__ uint32_t sc[kThreads / 32];
@@ -603,7 +610,8 @@ __device__ __forceinline__ void load_chunk_z(const uint8_t* __restrict__ in, uin
 template <bool VERIFY, int CAST>
 __global__ void __launch_bounds__(kThreads, 2)
     k_restore_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
-                float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, int pol) {
+                float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, int pol, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
     extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint64_t red[kThreads / 32];
     __shared__ uint32_t sc[kThreads / 32];
@@ -652,7 +660,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 // K2 over a batch (no cast, no verification): one grid for every chunk of
 // every job, raw or coded per job.
 __global__ void __launch_bounds__(kThreads, 2)
-    k_restore_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, int pol) {
+    k_restore_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, int pol, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
     extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint32_t sc[kThreads / 32];
     const uint32_t t = threadIdx.x;
@@ -678,7 +687,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ---- K3: local hash + exact compare against a peer replica ----------------
 __global__ void __launch_bounds__(kThreads, 2)
     k_verify_peer(const uint8_t* __restrict__ local, const uint8_t* __restrict__ peer, uint64_t nbytes,
-                  uint64_t* __restrict__ digests, uint32_t* mismatch) {
+                  uint64_t* __restrict__ digests, uint32_t* mismatch, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
     __shared__ uint64_t red[kThreads / 32];
     const uint32_t t = threadIdx.x;
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
@@ -796,14 +806,15 @@ cudaError_t evict_hash(const void* src, void* dst, uint64_t nbytes, uint64_t* di
     const int g = grid_for(nbytes, ctas, 48);
     const bool al = aligned16(src) && aligned16(dst);
     const int pol = g_policy.load(std::memory_order_relaxed);
+    KernelStamp* ks = timing_take(kIdEvict, nbytes);
     auto S = static_cast<const uint8_t*>(src);
     auto D = static_cast<uint8_t*>(dst);
     if (digests) {
-        if (al) k_evict<true, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests, pol);
-        else k_evict<false, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests, pol);
+        if (al) k_evict<true, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests, pol, ks);
+        else k_evict<false, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests, pol, ks);
     } else {
-        if (al) k_evict<true, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, pol);
-        else k_evict<false, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, pol);
+        if (al) k_evict<true, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, pol, ks);
+        else k_evict<false, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, pol, ks);
     }
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
@@ -814,8 +825,9 @@ cudaError_t hash_device(const void* src, uint64_t nbytes, uint64_t* digests, cud
     if (!src || !digests) return cudaErrorInvalidValue;
     const int g = grid_for(nbytes, ctas, 148 * 4);
     auto S = static_cast<const uint8_t*>(src);
-    if (aligned16(src)) k_evict<true, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests, 0);
-    else k_evict<false, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests, 0);
+    KernelStamp* ks = timing_take(kIdHash, nbytes);
+    if (aligned16(src)) k_evict<true, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests, 0, ks);
+    else k_evict<false, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests, 0, ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -830,26 +842,27 @@ cudaError_t restore_cast(const void* src, void* dst, uint64_t nbytes, Cast cast,
     auto S = static_cast<const uint8_t*>(src);
     auto D = static_cast<uint8_t*>(dst);
     const bool verify = expect != nullptr;
+    KernelStamp* ks = timing_take(kIdRestore, nbytes);
     if (cast == Cast::kNone) {
         const bool al = aligned16(src) && aligned16(dst);
-        if (al && verify) k_restore<true, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
-        else if (al) k_restore<true, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
-        else if (verify) k_restore<false, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
-        else k_restore<false, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+        if (al && verify) k_restore<true, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
+        else if (al) k_restore<true, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
+        else if (verify) k_restore<false, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
+        else k_restore<false, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
     } else {
         // Casts need element-aligned whole vectors.
         if (!aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7) || nbytes % 16) return cudaErrorInvalidValue;
         if (cast == Cast::kBf16ToFp8Block128) {
             if (!scales) return cudaErrorInvalidValue;
-            if (verify) k_restore<true, true, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, expect, mismatch, p);
-            else k_restore<true, false, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, nullptr, nullptr, p);
+            if (verify) k_restore<true, true, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, expect, mismatch, p, ks);
+            else k_restore<true, false, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, nullptr, nullptr, p, ks);
         } else if (cast == Cast::kFp32ToBf16) {
-            if (verify) k_restore<true, true, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
-            else k_restore<true, false, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+            if (verify) k_restore<true, true, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
+            else k_restore<true, false, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
         } else if (cast == Cast::kBf16ToFp32) {
             if (reinterpret_cast<uintptr_t>(dst) & 15) return cudaErrorInvalidValue;
-            if (verify) k_restore<true, true, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
-            else k_restore<true, false, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+            if (verify) k_restore<true, true, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
+            else k_restore<true, false, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
         } else {
             return cudaErrorInvalidValue;
         }
@@ -867,7 +880,8 @@ cudaError_t zscan(const void* src, uint64_t nbytes, uint8_t* ebase, uint32_t* fa
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
     int g = ctas > 0 ? ctas : sms * 3;
     if (uint64_t(g) > nchunks) g = int(nchunks);
-    k_zscan<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), nbytes, ebase, fail);
+    KernelStamp* ks = timing_take(kIdZScan, nbytes);
+    k_zscan<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), nbytes, ebase, fail, ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -881,7 +895,8 @@ cudaError_t zscan_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cu
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int g = ctas > 0 ? ctas : sms * 3;
     if (uint64_t(g) > total_chunks) g = int(total_chunks);
-    k_zscan_jobs<<<g, kThreads, 0, s>>>(jobs, njobs, total_chunks);
+    KernelStamp* ks = timing_take(kIdZScanJobs, total_chunks * kChunk);
+    k_zscan_jobs<<<g, kThreads, 0, s>>>(jobs, njobs, total_chunks, ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -892,8 +907,9 @@ cudaError_t evict_z(const void* src, void* dst, uint64_t nbytes, const uint8_t* 
     cudaError_t e = allow_stage(reinterpret_cast<const void*>(&k_evict_z), 0);
     if (e != cudaSuccess) return e;
     const int g = grid_for(nbytes, ctas, 48);
+    KernelStamp* ks = timing_take(kIdEvictZ, nbytes);
     k_evict_z<<<g, kThreads, kZStage, s>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nbytes,
-                                           ebase, digests, g_policy.load(std::memory_order_relaxed));
+                                           ebase, digests, g_policy.load(std::memory_order_relaxed), ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -921,18 +937,19 @@ cudaError_t restore_z(const void* src, void* dst, uint64_t nbytes, Cast cast, fl
     }
     cudaError_t e = allow_stage(fn, id);
     if (e != cudaSuccess) return e;
+    KernelStamp* ks = timing_take(kIdRestoreZ, nbytes);
     switch (cast) {
         case Cast::kNone:
-            if (v) k_restore_z<true, 0><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
-            else k_restore_z<false, 0><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+            if (v) k_restore_z<true, 0><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
+            else k_restore_z<false, 0><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
             break;
         case Cast::kBf16ToFp8Block128:
-            if (v) k_restore_z<true, 1><<<g, kThreads, kZStage, s>>>(S, D, nbytes, scales, expect, mismatch, p);
-            else k_restore_z<false, 1><<<g, kThreads, kZStage, s>>>(S, D, nbytes, scales, nullptr, nullptr, p);
+            if (v) k_restore_z<true, 1><<<g, kThreads, kZStage, s>>>(S, D, nbytes, scales, expect, mismatch, p, ks);
+            else k_restore_z<false, 1><<<g, kThreads, kZStage, s>>>(S, D, nbytes, scales, nullptr, nullptr, p, ks);
             break;
         default:
-            if (v) k_restore_z<true, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, expect, mismatch, p);
-            else k_restore_z<false, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p);
+            if (v) k_restore_z<true, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
+            else k_restore_z<false, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
             break;
     }
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -946,7 +963,8 @@ cudaError_t evict_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cu
     if (e != cudaSuccess) return e;
     int g = ctas > 0 ? ctas : 48;
     if (uint64_t(g) > total_chunks) g = int(total_chunks);
-    k_evict_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, g_policy.load(std::memory_order_relaxed));
+    KernelStamp* ks = timing_take(kIdEvictJobs, total_chunks * kChunk);
+    k_evict_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, g_policy.load(std::memory_order_relaxed), ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -958,7 +976,8 @@ cudaError_t restore_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, 
     if (e != cudaSuccess) return e;
     int g = ctas > 0 ? ctas : 96;
     if (uint64_t(g) > total_chunks) g = int(total_chunks);
-    k_restore_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, g_policy.load(std::memory_order_relaxed));
+    KernelStamp* ks = timing_take(kIdRestoreJobs, total_chunks * kChunk);
+    k_restore_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, g_policy.load(std::memory_order_relaxed), ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -976,8 +995,9 @@ cudaError_t verify_peer(const void* local, const void* peer, uint64_t nbytes, ui
     if (!local || !peer || !mismatch) return cudaErrorInvalidValue;
     if (!aligned16(local) || !aligned16(peer) || nbytes % 16) return cudaErrorInvalidValue;
     const int g = grid_for(nbytes, ctas, 148 * 2);
+    KernelStamp* ks = timing_take(kIdVerifyPeer, nbytes);
     k_verify_peer<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(local), static_cast<const uint8_t*>(peer),
-                                         nbytes, digests, mismatch);
+                                         nbytes, digests, mismatch, ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }

@@ -32,6 +32,7 @@
 #include <atomic>
 
 #include "kernels.h"
+#include "timing.h"
 #include "ofld/chunk_hash.h"
 
 namespace ofld {
@@ -271,7 +272,8 @@ __device__ __forceinline__ void set_error(const PushState& st, uint32_t code) {
 
 template <int S>
 __global__ void __launch_bounds__(kThreads, (S == 2 ? 3 : 2))
-    k_push(const PushItem* __restrict__ items, int nitems, uint64_t total_chunks, PushState st, PushItem one) {
+    k_push(const PushItem* __restrict__ items, int nitems, uint64_t total_chunks, PushState st, PushItem one, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
     // `items == nullptr`: a single item passed by value (no device table)
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(S) * kHalf);
@@ -471,7 +473,8 @@ cudaError_t launch_stages(const PushItem* items_dev, int nitems, uint64_t total_
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int g = ctas > 0 ? ctas : sms * (S == 2 ? 3 : 2);  // persistent: every resident slot
     if (uint64_t(g) > total_chunks) g = int(total_chunks);
-    k_push<S><<<g, kThreads, smem_bytes<S>(), s>>>(items_dev, nitems, total_chunks, st, one);
+    KernelStamp* ks = timing_take(kIdPush, total_chunks * kChunk);  // source bytes read (chunk-rounded)
+    k_push<S><<<g, kThreads, smem_bytes<S>(), s>>>(items_dev, nitems, total_chunks, st, one, ks);
     g_push_launches.fetch_add(1, std::memory_order_relaxed);
     e = cudaGetLastError();
     if (e != cudaSuccess || !st.item_hash) return e;

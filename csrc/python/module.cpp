@@ -16,6 +16,7 @@
 #include "../daemon/config.h"
 #include "../daemon/daemon.h"
 #include "../kernels/kernels.h"
+#include "../kernels/timing.h"
 #include "ofld/chunk_hash.h"
 #include "ofld/zbf16.h"
 #include "ofld/codec.h"
@@ -223,6 +224,7 @@ class PyAgent {
             else if (k == "compress") o.compress = v.cast<bool>();
             else if (k == "compress_min_bytes") o.compress_min_bytes = v.cast<uint64_t>();
             else if (k == "batch_group_bytes") o.batch_group_bytes = v.cast<uint64_t>();
+            else if (k == "kernel_timing") o.kernel_timing = v.cast<bool>();
             else throw std::invalid_argument("unknown agent option '" + k + "'");
         }
         py::gil_scoped_release nogil;
@@ -552,6 +554,32 @@ PYBIND11_MODULE(_C, m) {
 
     // ---- raw kernel launchers (tests, benchmarks, fabric layer) ----
     m.def("kernel_launch_count", &kern::launch_count);
+    m.def(
+        "kernel_timing_enable",
+        [](int device, uint32_t capacity) {
+            cudaError_t e = kern::timing_enable(device, capacity);
+            if (e != cudaSuccess) throw std::runtime_error(std::string("timing_enable: ") + cudaGetErrorString(e));
+        },
+        py::arg("device"), py::arg("capacity") = 4096);
+    m.def("kernel_timing_disable", &kern::timing_disable);
+    m.def(
+        "kernel_timings",
+        [](int device, uint64_t since) {
+            uint64_t next = 0;
+            std::vector<kern::StampRecord> recs = kern::timing_read(device, since, &next);
+            py::list out;
+            for (const kern::StampRecord& r : recs) {
+                py::dict d;
+                d["seq"] = r.seq;
+                d["kernel"] = kern::kernel_name(r.kernel);
+                d["bytes"] = r.bytes;
+                d["ns"] = r.t1 - r.t0;
+                d["t0"] = r.t0;
+                out.append(d);
+            }
+            return py::make_tuple(out, next);
+        },
+        py::arg("device"), py::arg("since") = 0);
     m.def("set_access_policy", &kern::set_access_policy, py::arg("load_form"), py::arg("store_form"));
     m.def("access_policy", &kern::access_policy);
     m.def("cuda_available", [] {

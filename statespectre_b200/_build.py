@@ -30,6 +30,7 @@ DAEMON = ["daemon/config.cpp", "daemon/daemon.cpp", "daemon/slots.cpp", "daemon/
           "daemon/nvme.cpp", "daemon/canonical.cpp", "daemon/rollout.cpp"]
 AGENT = ["agent/agent.cpp"]
 KERNELS = ["kernels/offload_kernels.cu", "kernels/weight_sync.cu", "kernels/hash_noalloc.cu"]
+KERNEL_HOST = ["kernels/timing.cpp"]
 FABRIC = ["fabric/fabric.cpp", "fabric/vmm.cpp"]
 MODULE = ["python/module.cpp", "python/fabric_bind.cpp"]
 
@@ -88,7 +89,7 @@ def write_ninja() -> str:
         "  description = DLINK $out",
     ]
     objs = {}
-    for rel in COMMON + DAEMON + AGENT + FABRIC + ["daemon/main.cpp", "tools/offload_stat.cpp", "tests/selftest.cpp"]:
+    for rel in COMMON + DAEMON + AGENT + FABRIC + KERNEL_HOST + ["daemon/main.cpp", "tools/offload_stat.cpp", "tests/selftest.cpp"]:
         if not _exists(rel):
             continue
         o = _obj(rel)
@@ -126,7 +127,7 @@ def write_ninja() -> str:
     lines.append(f"build {dlink}: nvlink_dev {kern}")
     ext = os.path.join(PKG, "_C" + _ext_suffix())
     lines.append(f"build {ext}: link_so {pick(MODULE)} {pick(AGENT)} {pick(FABRIC)} {pick(DAEMON)} "
-                 f"{pick(COMMON)} {kern} {dlink}")
+                 f"{pick(COMMON)} {pick(KERNEL_HOST)} {kern} {dlink}")
     lines.append("  libs = $cudalib")
     os.makedirs(BUILD, exist_ok=True)
     path = os.path.join(BUILD, "build.ninja")

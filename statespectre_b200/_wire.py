@@ -59,6 +59,7 @@ class Op:
     EXPORT_MANIFEST = 45
     DISCARD_TENSOR = 46
     CARRY_FORWARD = 47
+    GET_AGENT_OPTIONS = 48
 
 
 # Backward-compatible names used by rollout engines.
@@ -194,6 +195,9 @@ SCHEMA: Dict[str, List[Tuple[str, Any]]] = {
                             ("from_version", "u64"), ("to_version", "u64"), ("param_ids", ["u64"])],
     "CarryForwardResponse": STATUS + [("carried_count", "u32"), ("existing_count", "u32"), ("missing_count", "u32"),
                                       ("bytes_shared", "u64")],
+    "OptionEntry": [("key", S), ("value", S)],
+    "GetAgentOptionsRequest": [("rank_id", "u32"), ("gpu_id", "u32")],
+    "GetAgentOptionsResponse": STATUS + [("options", ["OptionEntry"])],
 }
 
 # opcode -> (request message, response message)
@@ -230,6 +234,7 @@ OPS: Dict[int, Tuple[str, str]] = {
     Op.EXPORT_MANIFEST: ("ExportManifestRequest", "ExportManifestResponse"),
     Op.DISCARD_TENSOR: ("DiscardTensorRequest", "Status"),
     Op.CARRY_FORWARD: ("CarryForwardRequest", "CarryForwardResponse"),
+    Op.GET_AGENT_OPTIONS: ("GetAgentOptionsRequest", "GetAgentOptionsResponse"),
 }
 
 _PRIM = {"u8": struct.Struct("<B"), "u16": struct.Struct("<H"), "u32": struct.Struct("<I"),

@@ -410,6 +410,7 @@ class Off:
         self.launch_epoch = None
         self.job_name = None
         self._dedup_policy = DedupPolicy()
+        self.nvlink_options: dict = {}  # the daemon config's `nvlink:` section
 
     # ---- identity ----
     @property
@@ -603,6 +604,39 @@ class Off:
     def daemon_stats(self) -> dict:
         r = self._raw(_wire.Op.GET_STATS, {"rank_id": 0xFFFFFFFF})
         return {e["key"]: e["value"] for e in r["stats"]}
+
+    # ---- kernel timing (device-side %globaltimer stamps) ----
+    def enable_kernel_timing(self, capacity: int = 4096) -> None:
+        """Stamp every transfer/hash/push kernel launched on this session's GPU
+        (also ``offload_context(kernel_timing=True)`` or ``kernels.timing`` in
+        the daemon config)."""
+        if self._device.type == "cuda":
+            native().kernel_timing_enable(self._device.index, int(capacity))
+
+    def kernel_timings(self, since: int = 0):
+        """(records, next): finished launches with sequence >= ``since``; each
+        record has ``kernel``, ``bytes``, ``ns`` (first CTA start to last CTA
+        end, measured on the device) and ``seq``."""
+        if self._device.type != "cuda":
+            return [], 0
+        return native().kernel_timings(self._device.index, int(since))
+
+    def kernel_profile(self, since: int = 0) -> dict:
+        """Per kernel: launches, total device ms, bytes and median GB/s."""
+        recs, _ = self.kernel_timings(since)
+        out: dict = {}
+        for r in recs:
+            e = out.setdefault(r["kernel"], {"launches": 0, "ms": 0.0, "bytes": 0, "_gbs": []})
+            e["launches"] += 1
+            e["ms"] += r["ns"] / 1e6
+            e["bytes"] += r["bytes"]
+            if r["ns"] > 0:
+                e["_gbs"].append(r["bytes"] / r["ns"])
+        for e in out.values():
+            g = sorted(e.pop("_gbs"))
+            e["median_gbs"] = round(g[len(g) // 2], 3) if g else None
+            e["ms"] = round(e["ms"], 4)
+        return out
 
     # ---- v1 offload ----
     @staticmethod
@@ -812,6 +846,47 @@ def _track(session) -> None:
     _LIVE_SESSIONS.add(session)
 
 
+def _as_bool(v: str) -> bool:
+    t = str(v).strip().lower()
+    if t in ("1", "true", "yes", "on"):
+        return True
+    if t in ("0", "false", "no", "off"):
+        return False
+    raise ValueError(v)
+
+
+# `kernels:` keys of the daemon config -> agent option (name, parser)
+_AGENT_OPTION_KEYS = {
+    "kernels.evict_ctas": ("evict_ctas", int),
+    "kernels.restore_ctas": ("restore_ctas", int),
+    "kernels.hash_ctas": ("hash_ctas", int),
+    "kernels.engine": ("engine", str),
+    "kernels.compress": ("compress", _as_bool),
+    "kernels.compress_min_mb": ("compress_min_bytes", lambda v: int(float(v) * (1 << 20))),
+    "kernels.batch_group_mb": ("batch_group_bytes", lambda v: int(float(v) * (1 << 20))),
+    "kernels.timing": ("kernel_timing", _as_bool),
+    "kernels.stream_priority": ("stream_priority", int),
+}
+
+
+def _daemon_agent_options(path: str, rank: int, gpu: int) -> dict:
+    """The daemon's forwarded ``kernels:`` / ``nvlink:`` settings (empty when
+    the daemon does not offer them)."""
+    try:
+        conn = native().RawConn(path, 5000)
+    except Exception:  # noqa: BLE001 - the agent reports connection errors itself
+        return {}
+    try:
+        _, body, _ = conn.call(_wire.Op.GET_AGENT_OPTIONS,
+                               _wire.encode("GetAgentOptionsRequest", {"rank_id": rank, "gpu_id": gpu}))
+        r = _wire.decode("GetAgentOptionsResponse", body)
+        return {e["key"]: e["value"] for e in r["options"]} if r["ok"] else {}
+    except Exception:  # noqa: BLE001
+        return {}
+    finally:
+        conn.close()
+
+
 class _OffloadSession:
     """Context manager returned by :func:`offload_context` (a plain object, so a
     session used without ``with`` is closed only explicitly)."""
@@ -827,9 +902,18 @@ class _OffloadSession:
         opts = {"socket_path": path, "device": dev.index if dev.type == "cuda" else -1, "rank_id": int(rank),
                 "local_rank": int(local_rank), "world_rank": int(world_rank), "numa_node": int(numa_node),
                 "eager_register": bool(eager_register or register_policy in ("eager", "eager_all"))}
+        daemon_opts = _daemon_agent_options(path, int(rank), dev.index if dev.type == "cuda" else 0)
+        for k, v in daemon_opts.items():
+            if k in _AGENT_OPTION_KEYS and _AGENT_OPTION_KEYS[k][0] not in agent_opts:
+                name, conv = _AGENT_OPTION_KEYS[k]
+                try:
+                    opts[name] = conv(v)
+                except ValueError:
+                    pass
         opts.update(agent_opts)
         self._agent = native().Agent(opts)
         off = Off(self._agent, dev, rank)
+        off.nvlink_options = {k[len("nvlink."):]: v for k, v in daemon_opts.items() if k.startswith("nvlink.")}
         if dedup_policy is not None:
             off.set_dedup_policy(dedup_policy)
         if job_name is not None:

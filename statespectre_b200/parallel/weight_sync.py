@@ -351,8 +351,10 @@ class TrainerWeightSync:
 
     def __init__(self, off, params: Dict[str, torch.Tensor], rollout_keys: Sequence[str], mode: str = "bf16",
                  model_role="policy_rollout", persist: bool = True, tp_rank: int = 0, pp_rank: int = 0,
-                 lookup_wait_ms: int = 60000, ctas: int = 0, transport: str = "auto"):
+                 lookup_wait_ms: int = 60000, ctas: int = 0, transport: Optional[str] = None):
         from ..api import ModelRole
+        if transport is None:  # the daemon config's nvlink.weight_sync, else auto
+            transport = getattr(off, "nvlink_options", {}).get("weight_sync", "auto")
         if transport not in TRANSPORTS:
             raise ValueError(f"transport must be one of {TRANSPORTS}")
         self.off = off

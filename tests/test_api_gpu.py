@@ -103,3 +103,29 @@ def test_canonical_evict_seal_restore(gpu_off):
     c1 = off.canonical_evict(ref.clone(), key2)
     c2 = off.canonical_evict(ref.clone(), key2, dedup_policy=DedupPolicy("device_hash_verified"))
     assert c1.did_d2h and not c2.did_d2h and c2.action_name == "VERIFIED_BY_DEVICE_HASH"
+
+
+def test_kernel_timing_stamps_transfers(gpu_off):
+    """Device-side %globaltimer stamps: one record per instrumented launch,
+    with the launch's bytes and a plausible duration."""
+    off = gpu_off
+    off.enable_kernel_timing()
+    _, start = off.kernel_timings()
+    x = torch.randn(32 << 20, dtype=torch.bfloat16, device="cuda")  # 64 MiB: zbf16-coded
+    f = torch.randn(8 << 20, device="cuda")                         # 32 MiB fp32: uncoded
+    hx, hf = off.copy(x, wait=True), off.copy(f, wait=True)
+    hx.restore_into(x, wait=True)
+    hf.restore_into(f, wait=True)
+    torch.cuda.synchronize()
+    recs, nxt = off.kernel_timings(start)
+    assert nxt >= start + 5
+    kinds = {r["kernel"] for r in recs}
+    assert {"zbf16_scan", "k1_evict_zbf16", "k1_evict", "k2_restore_zbf16", "k2_restore"} <= kinds, kinds
+    for r in recs:
+        assert r["ns"] > 0 and r["bytes"] > 0
+        gbs = r["bytes"] / r["ns"]
+        assert 1.0 < gbs < 20000.0, r  # PCIe kernels tens of GB/s, the scan HBM-rate
+    prof = off.kernel_profile(start)
+    assert prof["k1_evict"]["bytes"] == 32 << 20
+    hx.discard()
+    hf.discard()

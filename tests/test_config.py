@@ -179,3 +179,38 @@ def test_offload_stat_cli(tmp_path):
         sd = subprocess.run([bin_path("offload-stat"), "--socket", sock, "--shutdown"], capture_output=True,
                             text=True)
         assert sd.returncode == 0 and "shutting down" in sd.stdout
+
+
+def test_daemon_forwards_kernels_and_nvlink_sections(tmp_path):
+    """`kernels:` and `nvlink:` reach every session (GetAgentOptions, op 48);
+    explicit session options win."""
+    from statespectre_b200 import in_process_daemon, offload_context
+    from statespectre_b200.api import _daemon_agent_options
+
+    sock = str(tmp_path / "d.sock")
+    text = f"""
+daemon:
+  socket_path: {sock}
+arenas:
+  allocation_granularity_mb: 1
+  per_numa:
+    - numa_node: 0
+      size_mb: 128
+nvlink:
+  weight_sync: multicast
+kernels:
+  evict_ctas: 40
+  timing: true
+"""
+    d = in_process_daemon(yaml=text, socket=sock)
+    try:
+        opts = _daemon_agent_options(sock, 0, 0)
+        assert opts == {"kernels.evict_ctas": "40", "kernels.timing": "true", "nvlink.weight_sync": "multicast"}
+        with offload_context(daemon_addr=sock, device="cpu", rank=0, evict_ctas=8) as off:
+            assert off.nvlink_options == {"weight_sync": "multicast"}
+            t = __import__("torch").randn(1000)
+            h = off.copy(t, wait=True)
+            assert __import__("torch").equal(h.restore(), t)
+    finally:
+        d.stop()
+    assert _daemon_agent_options(sock + ".missing", 0, 0) == {}
