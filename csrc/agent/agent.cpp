@@ -25,6 +25,8 @@
 
 #include "../kernels/kernels.h"
 #include "../kernels/timing.h"
+
+#include <nvtx3/nvToolsExt.h>
 #include "ofld/abi/offload_canonical_abi.hpp"
 #include "ofld/chunk_hash.h"
 #include "ofld/zbf16.h"
@@ -35,6 +37,14 @@
 #include "ofld/transport.h"
 
 namespace ofld {
+
+namespace {
+// NVTX range over an agent call (nsys/ncu timelines); no cost without a tool.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+};
+}  // namespace
 
 namespace {
 constexpr const char* TAG = "agent";
@@ -612,6 +622,7 @@ Agent::~Agent() = default;
 EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive, uint64_t tensor_id,
                          uint64_t version, const std::string& name, DoneCallback on_done, bool wait,
                          uint32_t fmt_hint) {
+    NvtxRange nvtx_("ofld.evict");
     Impl& D = *d_;
     EvictTicket t;
     t.tensor_id = tensor_id;
@@ -683,6 +694,7 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
 // in groups of about batch_group_bytes, each group one K1 launch, so the
 // daemon round trip of group g+1 overlaps the PCIe copy of group g.
 std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait) {
+    NvtxRange nvtx_("ofld.evict_batch");
     Impl& D = *d_;
     std::vector<EvictTicket> out(items.size());
     cudaStream_t s = D.stream_of(stream);
@@ -826,6 +838,7 @@ std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items,
 
 RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr, uint64_t nbytes,
                               StreamHandle stream, bool wait, const RestoreOptions& ro) {
+    NvtxRange nvtx_("ofld.restore");
     Impl& D = *d_;
     RestoreOutcome out;
     std::vector<uint64_t> expect;
@@ -959,6 +972,7 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
 // group's round trip overlapping this group's copy). Items the daemon still
 // has to read back from a cold tier are asked for again after the rest.
 std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait) {
+    NvtxRange nvtx_("ofld.restore_batch");
     Impl& D = *d_;
     std::vector<RestoreOutcome> out(items.size());
     std::vector<RequestPrefetchRequest> reqs;
@@ -1176,6 +1190,7 @@ RegisterJobResponse Agent::register_job(const RegisterJobRequest& r) { return d_
 
 CanonicalOutcome Agent::canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
                                         const RequestCanonicalEvictRequest& in, DoneCallback on_invalidate, bool wait) {
+    NvtxRange nvtx_("ofld.canonical_evict");
     Impl& D = *d_;
     CanonicalOutcome out;
     RequestCanonicalEvictRequest req = in;

@@ -7,6 +7,12 @@ Produces, next to the sources so they travel with the repository:
   statespectre_b200/bin/offload-stat  metrics CLI
   statespectre_b200/bin/ofld_selftest C++ unit tests (codec, config, layout, allocator)
 
+and, on request (``build(sanitizers=True)`` or ``--sanitizers``), host-code
+sanitizer builds of the daemon and the self-test: ``offloadd_asan`` /
+``ofld_selftest_asan`` (AddressSanitizer + UndefinedBehaviorSanitizer) and
+``offloadd_tsan`` (ThreadSanitizer). The daemon is CUDA-free, so these cover
+its whole control plane.
+
 CUDA sources compile with ``-gencode arch=compute_100a,code=sm_100a -lineinfo``.
 Run ``python -m statespectre_b200._build`` (or ``__graft_entry__.build()``).
 """
@@ -35,6 +41,10 @@ FABRIC = ["fabric/fabric.cpp", "fabric/vmm.cpp"]
 MODULE = ["python/module.cpp", "python/fabric_bind.cpp"]
 
 ARCH = "-gencode arch=compute_100a,code=sm_100a"
+SANITIZERS = {
+    "asan": "-fsanitize=address,undefined -fno-sanitize-recover=undefined -fno-omit-frame-pointer -g -O1",
+    "tsan": "-fsanitize=thread -g -O1",
+}
 
 
 def _ext_suffix() -> str:
@@ -122,6 +132,29 @@ def write_ninja() -> str:
     if "tests/selftest.cpp" in objs:
         lines.append(f"build {bindir}/ofld_selftest: link_exe {objs['tests/selftest.cpp']} {pick(DAEMON)} {pick(COMMON)}")
         lines.append("  libs = ")
+    defaults = [f"{bindir}/offloadd"] + [f"{bindir}/{t}" for t in ("offload-stat", "ofld_selftest")
+                                           if f"build {bindir}/{t}:" in "\n".join(lines)]
+    # sanitizer variants of the CUDA-free host programs (built only when named)
+    for tag, flags in SANITIZERS.items():
+        lines.append(f"rule cxx_{tag}")
+        lines.append(f"  command = g++ $cxxflags {flags} -MMD -MF $out.d -c $in -o $out")
+        lines.append("  depfile = $out.d")
+        lines.append("  deps = gcc")
+        lines.append(f"  description = CXX[{tag}] $out")
+        lines.append(f"rule link_{tag}")
+        lines.append(f"  command = g++ {flags} -o $out $in -pthread")
+        lines.append(f"  description = LINK[{tag}] $out")
+        sobj = {}
+        for rel in COMMON + DAEMON + ["daemon/main.cpp", "tests/selftest.cpp"]:
+            if not _exists(rel):
+                continue
+            o = os.path.join(BUILD, tag, rel.replace("/", "_").rsplit(".", 1)[0] + ".o")
+            sobj[rel] = o
+            lines.append(f"build {o}: cxx_{tag} {os.path.join(CSRC, rel)}")
+        core = " ".join(sobj[r] for r in COMMON + DAEMON if r in sobj)
+        lines.append(f"build {bindir}/offloadd_{tag}: link_{tag} {sobj['daemon/main.cpp']} {core}")
+        if tag == "asan" and "tests/selftest.cpp" in sobj:
+            lines.append(f"build {bindir}/ofld_selftest_{tag}: link_{tag} {sobj['tests/selftest.cpp']} {core}")
     kern = pick(KERNELS)
     dlink = os.path.join(BUILD, "kernels_dlink.o")
     lines.append(f"build {dlink}: nvlink_dev {kern}")
@@ -129,6 +162,7 @@ def write_ninja() -> str:
     lines.append(f"build {ext}: link_so {pick(MODULE)} {pick(AGENT)} {pick(FABRIC)} {pick(DAEMON)} "
                  f"{pick(COMMON)} {pick(KERNEL_HOST)} {kern} {dlink}")
     lines.append("  libs = $cudalib")
+    lines.append("default " + " ".join(defaults + [ext]))
     os.makedirs(BUILD, exist_ok=True)
     path = os.path.join(BUILD, "build.ninja")
     with open(path, "w") as f:
@@ -136,8 +170,14 @@ def write_ninja() -> str:
     return path
 
 
-def build(verbose: bool = False, jobs: int | None = None) -> None:
-    """Compile every native target in-tree. Raises CalledProcessError on failure."""
+def sanitizer_targets() -> list:
+    bindir = os.path.join(PKG, "bin")
+    return [os.path.join(bindir, t) for t in ("offloadd_asan", "ofld_selftest_asan", "offloadd_tsan")]
+
+
+def build(verbose: bool = False, jobs: int | None = None, sanitizers: bool = False) -> None:
+    """Compile every native target in-tree (plus the sanitizer builds with
+    ``sanitizers``). Raises CalledProcessError on failure."""
     if shutil.which("nvcc") is None and os.path.exists(os.path.join(CUDA_HOME, "bin", "nvcc")):
         os.environ["PATH"] = os.path.join(CUDA_HOME, "bin") + os.pathsep + os.environ.get("PATH", "")
     path = write_ninja()
@@ -147,6 +187,8 @@ def build(verbose: bool = False, jobs: int | None = None) -> None:
     if verbose:
         cmd.append("-v")
     subprocess.run(cmd, check=True, cwd=ROOT)
+    if sanitizers:
+        subprocess.run(cmd + sanitizer_targets(), check=True, cwd=ROOT)
 
 
 def built() -> bool:
@@ -155,4 +197,4 @@ def built() -> bool:
 
 
 if __name__ == "__main__":
-    build(verbose="-v" in sys.argv)
+    build(verbose="-v" in sys.argv, sanitizers="--sanitizers" in sys.argv)

@@ -82,11 +82,12 @@ def launch_daemon(socket_path: Optional[str] = None, *, config: Optional[str] = 
                   slot_mb: Optional[int] = None, numa: int = 0, gpu: int = 0, tcp_port: int = 0,
                   trace: Optional[str] = None, nvme_dir: Optional[str] = None,
                   drain_on_complete: Optional[bool] = None, log_path: Optional[str] = None,
-                  extra_args=(), wait: bool = True, env=None) -> DaemonProcess:
-    """Start ``offloadd``; returns once it answers on its socket."""
+                  extra_args=(), wait: bool = True, env=None, binary: str = "offloadd") -> DaemonProcess:
+    """Start ``offloadd`` (or a sanitizer build of it, ``binary="offloadd_asan"``
+    / ``"offloadd_tsan"``); returns once it answers on its socket."""
     if socket_path is None:
         socket_path = os.path.join(tempfile.mkdtemp(prefix="offloadd-"), "offloadd.sock")
-    args = [bin_path("offloadd"), "--socket", socket_path]
+    args = [bin_path(binary), "--socket", socket_path]
     if config:
         args += ["--config", config]
     else:
