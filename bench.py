@@ -57,6 +57,8 @@ def parse():
     p.add_argument("--hash", type=int, default=1)
     p.add_argument("--compress", type=int, default=1, help="zbf16 lossless coding of the bf16 payload over PCIe")
     p.add_argument("--e2e-steps", type=int, default=0, help="default: same as --steps")
+    p.add_argument("--kernel-timing", type=int, default=0,
+                   help="stamp kernels on the device (%%globaltimer) and report per-kernel time and GB/s")
     p.add_argument("--out", default="")
     # --workload weight_sync: in-box RL weight sync (trainer half -> rollout half of the GPUs)
     p.add_argument("--workload", default="evict_restore",
@@ -165,7 +167,7 @@ def main():
     sess = offload_context(daemon_addr=sock, device=device, rank=rank, local_rank=local_rank, world_rank=rank,
                            eager_register=True, engine=args.engine, evict_ctas=args.evict_ctas,
                            restore_ctas=args.restore_ctas, hash_on_evict=bool(args.hash), stream_priority=-1,
-                           compress=bool(args.compress))
+                           compress=bool(args.compress), kernel_timing=bool(args.kernel_timing))
     off = sess.off
     g = torch.Generator(device=device)
     g.manual_seed(1234 + rank)
@@ -226,6 +228,7 @@ def main():
     torch.cuda.synchronize(device)
     assert off.hash_tensor(x) == ref_hash, "round trip corrupted the tensor"
     launches0 = native().kernel_launch_count()
+    _, stamp0 = off.kernel_timings()
     sampler = ClockSampler([local_rank]).start().wait_first()
     barrier()
     torch.cuda.synchronize(device)
@@ -241,6 +244,7 @@ def main():
     barrier()
     clocks = sampler.stop()
     launches = native().kernel_launch_count() - launches0
+    kernels = off.kernel_profile(stamp0) if args.kernel_timing else None
     dev_ms = t_start.elapsed_time(t_end)
     dev_ms_max = max_over_ranks(dev_ms)
     value = world * args.steps * 2 * nbytes / (dev_ms_max / 1e3) / 1e9
@@ -311,6 +315,8 @@ def main():
             "clocks": clocks,
             "matmul_iters": mm_count[0],
         }
+        if kernels is not None:
+            line["kernels"] = kernels  # device-stamped, timed region, rank 0
         print(json.dumps(line), flush=True)
         if args.out:
             with open(args.out, "w") as f:

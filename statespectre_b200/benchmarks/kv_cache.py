@@ -40,7 +40,8 @@ def run(args, metric: str) -> dict:
     pinned_gb = args.pinned_gb or int(per_iter * spec.block_bytes * 1.2 / GiB) + 2
     sock, daemon = node_daemon(env, pinned_gb, "/tmp/ofld_kv", slot_mb=4)
     sess = offload_context(daemon_addr=sock, device=env.device, rank=env.rank, local_rank=env.local_rank,
-                           world_rank=env.rank, eager_register=True, stream_priority=-1)
+                           world_rank=env.rank, eager_register=True, stream_priority=-1,
+                           kernel_timing=bool(getattr(args, "kernel_timing", 0)))
     off = sess.off
     stream = torch.cuda.Stream(device=env.device, priority=-1)
     g = torch.Generator(device=env.device).manual_seed(99 + env.rank)
@@ -68,6 +69,7 @@ def run(args, metric: str) -> dict:
     env.barrier()
     ev, rs = [], []
     launches0 = native().kernel_launch_count()
+    _, stamp0 = off.kernel_timings()
     sampler = ClockSampler([env.local_rank]).start().wait_first()
     sampler.mark_start()
     for _ in range(args.steps):
@@ -81,6 +83,7 @@ def run(args, metric: str) -> dict:
     byte_exact = off.hash_tensor(cache) == ref
     ok_all = env.sum(0 if byte_exact else 1) == 0
     stats = off.daemon_stats()
+    kernels = off.kernel_profile(stamp0) if getattr(args, "kernel_timing", 0) else None
     launches = env.sum(native().kernel_launch_count() - launches0)
     mm = load.stop() if load else 0
     sess.close()
@@ -112,4 +115,5 @@ def run(args, metric: str) -> dict:
         "tiers": {k: stats.get(k) for k in ("pinned_to_pageable_bytes", "pageable_to_pinned_bytes",
                                             "drains_completed", "readbacks_completed")},
         "gpu_launches": int(launches), "clocks": clocks, "matmul_iters": mm,
+        **({"kernels": kernels} if kernels is not None else {}),
     }
