@@ -906,7 +906,10 @@ cudaError_t evict_z(const void* src, void* dst, uint64_t nbytes, const uint8_t* 
     if (!zbf16::eligible(nbytes) || !aligned16(src) || !aligned16(dst) || !ebase) return cudaErrorInvalidValue;
     cudaError_t e = allow_stage(reinterpret_cast<const void*>(&k_evict_z), 0);
     if (e != cudaSuccess) return e;
-    const int g = grid_for(nbytes, ctas, 48);
+    // 96 CTAs: PCIe saturates with 48 at full clock, but a training step at
+    // the power cap lowers SM clocks and these latency-bound CTAs need the
+    // margin (KV blocks under an 8192^2 GEMM loop: 58.8 -> 66.1 GB/s).
+    const int g = grid_for(nbytes, ctas, 96);
     KernelStamp* ks = timing_take(kIdEvictZ, nbytes);
     k_evict_z<<<g, kThreads, kZStage, s>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nbytes,
                                            ebase, digests, g_policy.load(std::memory_order_relaxed), ks);
@@ -961,7 +964,7 @@ cudaError_t evict_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cu
     if (!jobs) return cudaErrorInvalidValue;
     cudaError_t e = allow_stage(reinterpret_cast<const void*>(&k_evict_jobs), 10);
     if (e != cudaSuccess) return e;
-    int g = ctas > 0 ? ctas : 48;
+    int g = ctas > 0 ? ctas : 96;  // as evict_z
     if (uint64_t(g) > total_chunks) g = int(total_chunks);
     KernelStamp* ks = timing_take(kIdEvictJobs, total_chunks * kChunk);
     k_evict_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, g_policy.load(std::memory_order_relaxed), ks);

@@ -41,7 +41,11 @@ def run(args, metric: str) -> dict:
     sock, daemon = node_daemon(env, pinned_gb, "/tmp/ofld_kv", slot_mb=4)
     sess = offload_context(daemon_addr=sock, device=env.device, rank=env.rank, local_rank=env.local_rank,
                            world_rank=env.rank, eager_register=True, stream_priority=-1,
-                           kernel_timing=bool(getattr(args, "kernel_timing", 0)))
+                           kernel_timing=bool(getattr(args, "kernel_timing", 0)),
+                           evict_ctas=int(getattr(args, "evict_ctas", 0)),
+                           restore_ctas=int(getattr(args, "restore_ctas", 0)),
+                           **({"batch_group_bytes": int(args.kv_group_mb) << 20}
+                              if getattr(args, "kv_group_mb", 0) else {}))
     off = sess.off
     stream = torch.cuda.Stream(device=env.device, priority=-1)
     g = torch.Generator(device=env.device).manual_seed(99 + env.rank)
@@ -108,6 +112,9 @@ def run(args, metric: str) -> dict:
                    "blocks_per_iter": per_iter, "batch": batch, "pinned_window_gb": pinned_gb,
                    "concurrent_matmul": load.describe() if load else "none", "global_batch": env.world,
                    "seq_len": 16, "parallelism": f"dp{env.world}", "slot_mb": 4,
+                   "evict_ctas": int(getattr(args, "evict_ctas", 0)) or "default",
+                   "restore_ctas": int(getattr(args, "restore_ctas", 0)) or "default",
+                   "group_mb": int(getattr(args, "kv_group_mb", 0)) or 256,
                    "l2": "GBs per iteration; no flush needed"},
         "evict_gbs_per_gpu": round(moved / (e_ms / 1e3) / 1e9, 3),
         "restore_gbs_per_gpu": round(moved / (r_ms / 1e3) / 1e9, 3),
