@@ -62,7 +62,7 @@ def parse():
     p.add_argument("--out", default="")
     # --workload weight_sync: in-box RL weight sync (trainer half -> rollout half of the GPUs)
     p.add_argument("--workload", default="evict_restore",
-                   choices=["evict_restore", "weight_sync", "sweep", "kv_cache", "dp_dedup"])
+                   choices=["evict_restore", "weight_sync", "sweep", "kv_cache", "dp_dedup", "sections"])
     p.add_argument("--model", default="", help="weight_sync: qwen2.5-32b (default); dp_dedup: llama-3-8b (default)")
     p.add_argument("--layers", type=int, default=0, help="weight_sync: layer count override (0 = the model's)")
     p.add_argument("--push-mode", default="bf16", choices=["bf16", "fp8"])
@@ -102,6 +102,8 @@ def main():
             from statespectre_b200.benchmarks.sweep import run
         elif args.workload == "kv_cache":
             from statespectre_b200.benchmarks.kv_cache import run
+        elif args.workload == "sections":
+            from statespectre_b200.benchmarks.sections import run
         else:
             from statespectre_b200.benchmarks.dp_dedup import run
 

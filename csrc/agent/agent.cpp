@@ -121,6 +121,7 @@ struct Agent::Impl {
         uint64_t size = 0;
         char* dev = nullptr;  // device alias after registration
         bool registered = false;
+        std::vector<std::pair<char*, uint64_t>> pieces;  // registered ranges
     };
     std::vector<ArenaMap> arenas;
     std::mutex reg_mu;
@@ -162,7 +163,7 @@ struct Agent::Impl {
     std::map<TvKey, TensorRec> tensors;
 
     std::atomic<uint64_t> inflight_d2h{0}, inflight_h2d{0}, evicts{0}, restores{0}, d2h_done{0}, h2d_done{0};
-    std::atomic<uint64_t> d2h_bytes{0}, h2d_bytes{0}, registered_bytes{0}, d2h_ns{0}, h2d_ns{0};
+    std::atomic<uint64_t> d2h_bytes{0}, h2d_bytes{0}, registered_bytes{0}, d2h_ns{0}, h2d_ns{0}, reg_ns{0};
     std::atomic<bool> stop{false}, hb_paused{false};
     std::thread progress_thr, heartbeat_thr;
 
@@ -266,10 +267,11 @@ struct Agent::Impl {
     void unmap_all() {
         std::lock_guard<std::mutex> g(reg_mu);
         for (ArenaMap& m : arenas) {
-            if (m.registered) {
-                cudaHostUnregister(m.base);
+            for (auto& pc : m.pieces) {
+                cudaHostUnregister(pc.first);
                 cudaGetLastError();
             }
+            m.pieces.clear();
             if (m.base) ::munmap(m.base, m.size);
         }
         arenas.clear();
@@ -283,25 +285,65 @@ struct Agent::Impl {
         return rpc->call<O>(r);
     }
 
-    // One cudaHostRegister per arena, whole-range (a copy must not span two
-    // registrations), mapped so kernels address it directly.
+    // Arena registration, mapped so kernels address it directly. Pinning is
+    // page by page (4 KiB pages: memfd shmem gets no huge pages here), so a
+    // large arena takes seconds; when the GPU addresses registered memory by
+    // its host pointer, the arena is registered as `registration_threads`
+    // pieces concurrently: the device sees one contiguous range either way.
+    // Otherwise one whole-range registration (a copy must not span two
+    // separately mapped registrations).
     void register_arena(ArenaMap& m) {
         std::lock_guard<std::mutex> g(reg_mu);
         if (m.registered) return;
         uint64_t t0 = mono_ns();
-        cudaError_t e = cudaHostRegister(m.base, m.size, cudaHostRegisterPortable | cudaHostRegisterMapped);
-        if (e == cudaErrorHostMemoryAlreadyRegistered) {
-            cudaGetLastError();
-        } else if (e != cudaSuccess) {
-            throw std::runtime_error(std::string("cudaHostRegister(arena): ") + cudaGetErrorString(e));
+        const unsigned flags = cudaHostRegisterPortable | cudaHostRegisterMapped;
+        int same_ptr = 0;
+        cudaDeviceGetAttribute(&same_ptr, cudaDevAttrCanUseHostPointerForRegisteredMem, opt.device);
+        const uint64_t min_piece = 1ull << 30;
+        int nthreads = std::max(1, opt.registration_threads);
+        if (!same_ptr || m.size < 2 * min_piece) nthreads = 1;
+        nthreads = int(std::min<uint64_t>(uint64_t(nthreads), m.size / min_piece ? m.size / min_piece : 1));
+        std::vector<std::pair<char*, uint64_t>> pieces;
+        const uint64_t step = (m.size / uint64_t(nthreads) + 0xFFFFF) & ~uint64_t(0xFFFFF);  // 1 MiB aligned
+        for (uint64_t off = 0; off < m.size; off += step) pieces.push_back({m.base + off, std::min(step, m.size - off)});
+        std::vector<cudaError_t> errs(pieces.size(), cudaSuccess);
+        auto reg = [&](size_t i) {
+            cudaSetDevice(opt.device);
+            errs[i] = cudaHostRegister(pieces[i].first, pieces[i].second, flags);
+            if (errs[i] == cudaErrorHostMemoryAlreadyRegistered) {
+                cudaGetLastError();
+                errs[i] = cudaSuccess;
+            }
+        };
+        if (pieces.size() == 1) {
+            reg(0);
+        } else {
+            std::vector<std::thread> ts;
+            for (size_t i = 0; i < pieces.size(); ++i) ts.emplace_back(reg, i);
+            for (auto& t : ts) t.join();
+        }
+        for (size_t i = 0; i < pieces.size(); ++i) {
+            if (errs[i] != cudaSuccess) {
+                for (size_t j = 0; j < pieces.size(); ++j)
+                    if (errs[j] == cudaSuccess) cudaHostUnregister(pieces[j].first);
+                cudaGetLastError();
+                throw std::runtime_error(std::string("cudaHostRegister(arena): ") + cudaGetErrorString(errs[i]));
+            }
         }
         void* dev = nullptr;
         CUDA_OK(cudaHostGetDevicePointer(&dev, m.base, 0));
+        if (pieces.size() > 1 && dev != m.base) {  // cannot happen when same_ptr; keep the invariant explicit
+            for (auto& pc : pieces) cudaHostUnregister(pc.first);
+            throw std::runtime_error("pieced registration without host-pointer addressing");
+        }
         m.dev = static_cast<char*>(dev);
+        m.pieces = std::move(pieces);
         m.registered = true;
         registered_bytes += m.size;
-        LOG_INFO(TAG, "registered arena %llu: %llu MiB in %.1f ms", (unsigned long long)m.id,
-                 (unsigned long long)(m.size >> 20), double(mono_ns() - t0) / 1e6);
+        const double ms = double(mono_ns() - t0) / 1e6;
+        reg_ns += uint64_t(ms * 1e6);
+        LOG_INFO(TAG, "registered arena %llu: %llu MiB in %.1f ms (%zu piece%s)", (unsigned long long)m.id,
+                 (unsigned long long)(m.size >> 20), ms, m.pieces.size(), m.pieces.size() == 1 ? "" : "s");
     }
 
     ArenaMap& arena(uint64_t id) {
@@ -1436,6 +1478,9 @@ AgentStats Agent::stats() const {
     s.h2d_bytes = D.h2d_bytes;
     s.kernel_launches = D.gpu ? kern::launch_count() : 0;
     s.rpc_count = D.rpc_count;
+    s.d2h_ns = D.d2h_ns;
+    s.h2d_ns = D.h2d_ns;
+    s.registration_ns = D.reg_ns;
     return s;
 }
 

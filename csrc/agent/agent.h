@@ -56,6 +56,9 @@ struct AgentOptions {
     // Device-side kernel timing (%globaltimer stamps into a host-mapped ring,
     // read with Agent::kernel_timings / statespectre_b200.Off.kernel_timings).
     bool kernel_timing = false;
+    // Threads that register an arena with CUDA concurrently (pieces of at
+    // least 1 GiB), when the GPU addresses registered memory by host pointer.
+    int registration_threads = 8;
 };
 
 // evict() data hints.
@@ -101,6 +104,7 @@ struct AgentStats {
     uint64_t rank_epoch = 0, num_slots = 0;
     uint64_t d2h_bytes = 0, h2d_bytes = 0, kernel_launches = 0, rpc_count = 0;
     uint64_t d2h_ns = 0, h2d_ns = 0;  // summed device time of completed copies (wait paths)
+    uint64_t registration_ns = 0;     // host time spent registering arenas with CUDA
 };
 
 struct BatchItem {

@@ -190,6 +190,9 @@ py::dict stats_dict(const AgentStats& s) {
     d["h2d_bytes"] = s.h2d_bytes;
     d["kernel_launches"] = s.kernel_launches;
     d["rpc_count"] = s.rpc_count;
+    d["d2h_ns"] = s.d2h_ns;
+    d["h2d_ns"] = s.h2d_ns;
+    d["registration_ns"] = s.registration_ns;
     return d;
 }
 
@@ -225,6 +228,7 @@ class PyAgent {
             else if (k == "compress_min_bytes") o.compress_min_bytes = v.cast<uint64_t>();
             else if (k == "batch_group_bytes") o.batch_group_bytes = v.cast<uint64_t>();
             else if (k == "kernel_timing") o.kernel_timing = v.cast<bool>();
+            else if (k == "registration_threads") o.registration_threads = v.cast<int>();
             else throw std::invalid_argument("unknown agent option '" + k + "'");
         }
         py::gil_scoped_release nogil;
