@@ -60,3 +60,12 @@ def host_session(daemon, sock_path):
     s = offload_context(daemon_addr=sock_path, device="cpu", rank=0)
     yield s.off
     s.close()
+
+
+@pytest.fixture(autouse=True)
+def _seeded():
+    """Every test starts from the same torch RNG state (reproducible data)."""
+    import torch
+
+    torch.manual_seed(0)
+    yield

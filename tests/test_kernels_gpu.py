@@ -98,7 +98,7 @@ def _fp8_reference(x: torch.Tensor):
 @pytest.mark.parametrize("nelem", [128, 4096, 65536 * 3, (1 << 20) + 256])
 def test_restore_cast_bf16_to_fp8(nelem):
     C = native()
-    x = (torch.randn(nelem) * 3).to(torch.bfloat16)
+    x = (torch.randn(nelem, generator=torch.Generator().manual_seed(nelem)) * 3).to(torch.bfloat16)
     host = x.view(torch.uint8).pin_memory()
     out = torch.empty(nelem, dtype=torch.float8_e4m3fn, device="cuda")
     scales = torch.empty((nelem + 127) // 128, dtype=torch.float32, device="cuda")
@@ -108,10 +108,11 @@ def test_restore_cast_bf16_to_fp8(nelem):
     q_ref, s_ref = _fp8_reference(x)
     torch.testing.assert_close(scales.cpu(), s_ref, rtol=0, atol=0)
     got = out.cpu().float()
-    ref = q_ref.float()
-    # identical except for rare one-ulp rounding differences of the scaled input
-    diff = (got != ref).float().mean().item()
-    assert diff < 1e-3
+    # codes equal the fp32 reference's except for rare one-step rounding
+    # differences (subnormal and tie cases of the scaled input)
+    step = (out.cpu().view(torch.uint8).int() - q_ref.view(torch.uint8).int()).abs()
+    assert step.max().item() <= 1
+    assert (step != 0).float().mean().item() < 5e-3
     deq = (got.reshape(-1, 128) * scales.cpu()[:, None]).reshape(-1)
     torch.testing.assert_close(deq, x.float(), rtol=0.07, atol=1e-2)
 
