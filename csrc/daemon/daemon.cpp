@@ -13,6 +13,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <map>
 #include <cerrno>
 #include <cstring>
 #include <stdexcept>
@@ -662,6 +663,21 @@ GetStatsResponse Daemon::on_get_stats(const GetStatsRequest&) {
     resp.stats.push_back({"canonical_objects", objects_.size()});
     resp.stats.push_back({"sealed_manifests", manifests_.size()});
     resp.stats.push_back({"jobs", jobs_.size()});
+    // Per-GPU window (and per-NUMA overflow pool) occupancy: "<scope>.<name>",
+    // rendered as labelled series by offload-stat --prometheus.
+    const uint64_t gran = cfg_.allocation_granularity_bytes;
+    for (const Window& w : windows_) {
+        uint64_t free_slots = 0;
+        for (uint64_t word : w.free_bits) free_slots += uint64_t(__builtin_popcountll(word));
+        const std::string scope =
+            w.overflow ? "numa" + std::to_string(w.numa_node) + "_overflow" : "gpu" + std::to_string(w.gpu);
+        resp.stats.push_back({scope + ".window_bytes", uint64_t(w.nslots) * gran});
+        resp.stats.push_back({scope + ".window_used_bytes", (uint64_t(w.nslots) - free_slots) * gran});
+    }
+    std::map<uint32_t, uint64_t> per_gpu;
+    for (auto& kv : sessions_)
+        if (kv.second.alive) per_gpu[kv.second.gpu]++;
+    for (auto& kv : per_gpu) resp.stats.push_back({"gpu" + std::to_string(kv.first) + ".live_sessions", kv.second});
     resp.stats.push_back({"daemon_epoch", daemon_epoch_});
     return resp;
 }

@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <string>
 #include <vector>
 
@@ -49,12 +50,62 @@ void print_table(const GetStatsResponse& r) {
     }
 }
 
-void print_prometheus(const GetStatsResponse& r) {
+// "gpu3.window_used_bytes" -> ("window_used_bytes", gpu="3");
+// "numa1_overflow.window_bytes" -> ("window_bytes", numa="1",pool="overflow").
+std::pair<std::string, std::string> split_scope(const std::string& key) {
+    const size_t dot = key.find('.');
+    if (dot == std::string::npos) return {key, ""};
+    const std::string scope = key.substr(0, dot), name = key.substr(dot + 1);
+    std::string labels;
+    if (scope.rfind("gpu", 0) == 0) {
+        labels = "gpu=\"" + scope.substr(3) + "\"";
+    } else if (scope.rfind("numa", 0) == 0) {
+        const size_t us = scope.find('_');
+        labels = "numa=\"" + scope.substr(4, us == std::string::npos ? std::string::npos : us - 4) + "\"";
+        if (us != std::string::npos) labels += ",pool=\"" + scope.substr(us + 1) + "\"";
+    } else {
+        labels = "scope=\"" + scope + "\"";
+    }
+    return {name, labels};
+}
+
+// One TYPE line per metric family; scoped keys become labelled samples.
+void print_prometheus(const GetStatsResponse& r, const GetJobStatsResponse* jobs) {
+    std::map<std::string, std::vector<std::pair<std::string, uint64_t>>> fams;
+    std::vector<std::string> order;
     for (const StatEntry& e : r.stats) {
-        std::string name = "offloadd_" + e.key;
-        bool counter = e.key.size() > 6 && e.key.compare(e.key.size() - 6, 6, "_total") == 0;
-        std::printf("# TYPE %s %s\n%s %llu\n", name.c_str(), counter ? "counter" : "gauge", name.c_str(),
-                    (unsigned long long)e.value);
+        auto nl = split_scope(e.key);
+        const std::string name = "offloadd_" + nl.first;
+        if (!fams.count(name)) order.push_back(name);
+        fams[name].push_back({nl.second, e.value});
+    }
+    if (jobs) {
+        for (const JobStatsEntry& j : jobs->jobs) {
+            const std::string l = "job=\"" + j.job.job_name + "\",job_id=\"" + std::to_string(j.job.job_id) +
+                                  "\",tenant=\"" + std::to_string(j.job.tenant_id) + "\"";
+            const std::pair<const char*, uint64_t> vals[] = {
+                {"offloadd_job_pinned_bytes", j.pinned_bytes},
+                {"offloadd_job_pageable_bytes", j.pageable_bytes},
+                {"offloadd_job_nvme_bytes", j.nvme_bytes},
+                {"offloadd_job_inflight_d2h_bytes", j.inflight_d2h_bytes},
+                {"offloadd_job_inflight_export_bytes", j.inflight_export_bytes},
+                {"offloadd_job_canonical_objects", j.canonical_object_count},
+                {"offloadd_job_dedup_bytes_saved", j.dedup_bytes_saved}};
+            for (const auto& v : vals) {
+                if (!fams.count(v.first)) order.push_back(v.first);
+                fams[v.first].push_back({l, v.second});
+            }
+        }
+    }
+    for (const std::string& name : order) {
+        const bool counter = name.size() > 6 && name.compare(name.size() - 6, 6, "_total") == 0;
+        std::printf("# TYPE %s %s\n", name.c_str(), counter ? "counter" : "gauge");
+        for (const auto& sample : fams[name]) {
+            if (sample.first.empty())
+                std::printf("%s %llu\n", name.c_str(), (unsigned long long)sample.second);
+            else
+                std::printf("%s{%s} %llu\n", name.c_str(), sample.first.c_str(), (unsigned long long)sample.second);
+        }
     }
 }
 
@@ -110,10 +161,12 @@ int main(int argc, char** argv) {
                 print_jobs(c.call<Op::kGetJobStats>(GetJobStatsRequest{}));
             } else {
                 GetStatsResponse r = c.call<Op::kGetStats>(GetStatsRequest{});
-                if (prom)
-                    print_prometheus(r);
-                else
+                if (prom) {
+                    GetJobStatsResponse js = c.call<Op::kGetJobStats>(GetJobStatsRequest{});
+                    print_prometheus(r, js.ok ? &js : nullptr);
+                } else {
                     print_table(r);
+                }
             }
             std::fflush(stdout);
             if (watch > 0) {

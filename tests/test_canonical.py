@@ -301,3 +301,51 @@ def test_carry_forward_rejects_sealed_target_and_unknown_job(cdaemon):
             off.carry_forward_version(ROLL, 2, 1)
         r = off.carry_forward_version(ROLL, 1, 2, [12345])
         assert r["missing"] == 1 and r["carried"] == 0
+
+
+def test_export_cancelled_when_receiver_disconnects(cdaemon):
+    """A rollout receiver that hangs up mid-stream: the daemon's export fails
+    cleanly (error counted, in-flight bytes released, object unpinned), the
+    object stays pullable and the version can be dropped."""
+    import socket
+    import threading
+
+    from statespectre_b200 import _wire
+
+    big = torch.randn(8 << 20)  # 32 MiB: far more than the socket buffers hold
+    with session(cdaemon, 0) as off:
+        k = off.canonical_key(model_role=ROLL, model_version=1, param_name="big", tensor=big)
+        off.canonical_evict(big.clone(), k)
+        off.promote_rollout_version(1)
+        c = RolloutWeightClient(cdaemon, off.job_id, off.launch_epoch, job_name=off.job_name)
+        entry = c.get_manifest(1)["tensors"][0]
+        lsock = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
+        lsock.bind(("127.0.0.1", 0))
+        lsock.listen(1)
+        lsock.settimeout(30)
+        result = {}
+        base = {"job": c._job(), "model_role": int(ROLL), "model_version": 1, "object_id": int(entry["object_id"])}
+
+        def rpc():
+            result["resp"] = c._conn_for_pull().call(Op.PULL_TENSOR, base, transport=_wire.TK_TCP,
+                                                      target_descriptor=f"127.0.0.1:{lsock.getsockname()[1]}")
+
+        th = threading.Thread(target=rpc)
+        th.start()
+        conn, _ = lsock.accept()
+        conn.recv(1 << 20)
+        conn.setsockopt(socket.SOL_SOCKET, socket.SO_LINGER, struct.pack("ii", 1, 0))  # reset, not FIN
+        conn.close()
+        lsock.close()
+        th.join(60)
+        assert not th.is_alive()
+        assert result["resp"]["ok"] is False and "transport failed" in result["resp"]["message"]
+        st = off.daemon_stats()
+        assert st["export_transport_errors_total"] >= 1
+        assert st["export_inflight_bytes"] == 0
+        # the object is intact and exports again
+        res = c.sync_latest(transport="tcp")
+        assert res["data"][entry["object_id"]] == big.numpy().tobytes()
+        c.close()
+        d = off.drop_canonical_version(ROLL, 1)
+        assert d["dropped"] == 1 and d["skipped_inflight"] == 0
