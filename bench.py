@@ -38,7 +38,7 @@ BASELINE_H2D_GBS = 57.5
 BASELINE_ROUNDTRIP_GBS = 2.0 / (1.0 / BASELINE_D2H_GBS + 1.0 / BASELINE_H2D_GBS)
 METRIC = "evict/restore GB/s per GPU at 1/2/4/8 B200; 32B weight-sync latency (ms)"
 REFERENCE_UNAVAILABLE = (
-    "reference cannot be installed offline: /root/reference has neither setup.py nor pyproject.toml "
+    "reference cannot be installed offline: its source tree has neither setup.py nor pyproject.toml "
     "(pip install fails) and its CMake build requires libnuma and liburing (numa.h, liburing.h), "
     "which are absent from this image")
 

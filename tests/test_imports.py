@@ -1,5 +1,5 @@
-"""Every module of the package imports on a CPU-only host (syntax and
-import-time errors surface here, not on a GPU box)."""
+"""Every module of the package imports on a CPU-only host, so syntax and
+import-time errors show up without a GPU."""
 
 import importlib
 import pkgutil
