@@ -1199,10 +1199,20 @@ std::string Agent::location(uint64_t tid, uint64_t ver) {
     }
 }
 
+// A copy that a drain, readback or restore is moving cannot be dropped yet;
+// the daemon answers "retry" and the call waits (bounded) for the transfer to
+// settle, so a discard never leaves the tensor's pinned or cold copy behind.
 void Agent::discard(uint64_t tid, uint64_t ver) {
     Impl& D = *d_;
     DiscardTensorRequest r{D.opt.rank_id, D.epoch, tid, ver};
     StatusResponse s = D.call<Op::kDiscardTensor>(r);
+    const uint64_t deadline = mono_ns() + 30ull * 1000000000ull;
+    uint64_t backoff_us = 100;
+    while (!s.ok && s.message.find("retry") != std::string::npos && mono_ns() < deadline) {
+        sleep_us(backoff_us);
+        backoff_us = std::min<uint64_t>(backoff_us * 2, 5000);
+        s = D.call<Op::kDiscardTensor>(r);
+    }
     if (!s.ok) LOG_WARN(TAG, "discard(%llu:%llu): %s", (unsigned long long)tid, (unsigned long long)ver, s.message.c_str());
     std::lock_guard<std::mutex> g(D.tab_mu);
     D.tensors.erase({tid, ver});
