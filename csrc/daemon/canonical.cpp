@@ -456,6 +456,7 @@ bool Daemon::release_object(CanonicalObject& o) {
         return true;
     }
     if (sit != storage_.end()) storage_.erase(sit);
+    forget_persisted_storage(o.synthetic_tid);  // the last object of a durable storage
     auto lit = locations_.find(o.synthetic_tid);
     if (lit != locations_.end()) {
         if (lit->second.kind == OFLD_LOC_PINNED) {

@@ -333,6 +333,7 @@ const std::map<std::string, Binder>& binders() {
         // manifest
         {"manifest.seal_requires_all_objects_valid", [](DaemonConfig& c, const Node& n, const std::string& k) { c.v2_seal_requires_all_objects_valid = as_bool(n, k); }},
         {"manifest.retain_sealed_versions", [](DaemonConfig& c, const Node& n, const std::string& k) { c.v2_retain_sealed_versions = uint32_t(as_u64(n, k)); }},
+        {"manifest.persist_dir", [](DaemonConfig& c, const Node& n, const std::string&) { c.v2_persist_dir = n.scalar; }},
         {"manifest.allow_sealed_version_mutation", [](DaemonConfig&, const Node&, const std::string&) {}},
         {"manifest.latest_pointer_update", [](DaemonConfig&, const Node&, const std::string&) {}},
         // export

@@ -92,6 +92,9 @@ struct DaemonConfig {
     uint64_t v2_sampled_hash_bytes_per_gib = 1ull << 20;
     bool v2_seal_requires_all_objects_valid = true;
     uint32_t v2_retain_sealed_versions = 4;
+    // Directory where sealed versions are made durable (empty: off). A daemon
+    // started on the same directory serves them again after a restart.
+    std::string v2_persist_dir;
     uint32_t v2_default_transport = 3;
     uint32_t v2_fallback_transport = 1;
     bool v2_use_dedicated_export_buffers = true;

@@ -52,6 +52,7 @@ Daemon::Daemon(const DaemonConfig& cfg) : cfg_(cfg) {
         build_arenas();
         build_control();
         build_windows();
+        if (!cfg_.v2_persist_dir.empty()) recover_persisted();
     } catch (...) {
         teardown();
         throw;
@@ -256,6 +257,7 @@ void Daemon::run() {
         workers_.emplace_back([this] { readback_loop(); });
     workers_.emplace_back([this] { heartbeat_loop(); });
     if (ring_max_) workers_.emplace_back([this] { ring_loop(); });
+    if (!cfg_.v2_persist_dir.empty()) workers_.emplace_back([this] { persist_loop(); });
     LOG_INFO(TAG, "serving on %s (pid %d, tcp port %u)", cfg_.socket_path.c_str(), int(::getpid()),
              cfg_.v2_control_tcp_port);
     ready_.store(true);
@@ -267,6 +269,7 @@ void Daemon::run() {
     drain_cv_.notify_all();
     readback_cv_.notify_all();
     peer_cv_.notify_all();
+    persist_cv_.notify_all();
     reap_connections(true);
     for (auto& t : workers_)
         if (t.joinable()) t.join();

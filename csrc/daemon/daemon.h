@@ -191,8 +191,17 @@ class Daemon {
         uint64_t nbytes = 0;
         char* pageable = nullptr;
         std::vector<Extent> extents;
-        uint32_t readers = 0;  // unlocked readers in flight (readback/export)
-        bool doomed = false;   // free once the last reader is done
+        uint32_t readers = 0;     // unlocked readers in flight (readback/export)
+        bool doomed = false;      // free once the last reader is done
+        bool persisted = false;   // extents are a durable version file: unlink, do not punch
+    };
+    // A read hold on a canonical object's bytes (export, persistence): the
+    // source is pinned against drains and frees until end_read.
+    struct ReadSrc {
+        const char* pinned = nullptr;
+        ColdEntry cold;
+        uint64_t cold_ref = 0, nbytes = 0;
+        ofld_location_kind_t kind = OFLD_LOC_NONE;
     };
     struct PeerBuffer {
         PeerBufferDesc desc;
@@ -303,6 +312,25 @@ class Daemon {
     void readback_loop();
     void heartbeat_loop();
     void ring_loop();
+
+    // ---------------- read holds and durable versions (persist.cpp) ----------------
+    bool begin_read(CanonicalObject& o, ReadSrc* src, std::string* why);  // mu_ held
+    void end_read(uint64_t oid, const ReadSrc& src);                      // mu_ held
+    bool copy_out(const ReadSrc& src, char* dst, uint64_t off, uint64_t n);  // no lock
+    // Sealed versions are written under manifest.persist_dir by a worker and
+    // reloaded when a daemon starts on the same directory.
+    static constexpr uint32_t kPersistHolder = 0xFFFFFFFEu;  // holder id that keeps persisted objects
+    void enqueue_persist(const VersionKey& vk);               // mu_ held
+    void persist_loop();
+    int persist_version(const VersionKey& vk);                // 1 done, 0 retry later, -1 failed
+    void recover_persisted();
+    std::string persist_job_dir(const JobUID& uid) const;
+    void unlink_persisted_manifest(const VersionKey& vk);    // mu_ held
+    void forget_persisted_storage(uint64_t tid);             // mu_ held
+    std::mutex persist_mu_;
+    std::condition_variable persist_cv_;
+    std::deque<VersionKey> persist_queue_;
+    std::unordered_map<uint64_t, std::string> persisted_files_;  // storage tid -> file (mu_)
     // Applies every completion already published in the rings. mu_ held.
     void drain_rings();
     void apply_ring_entry(uint32_t rank, uint64_t epoch, const ofld_completion_entry_t& e);

@@ -194,6 +194,7 @@ SealModelVersionResponse Daemon::on_seal(const SealModelVersionRequest& r) {
         latest_sealed_[{job->uid, r.model_role}] = r.model_version;
         enforce_retention(job->uid, r.model_role);
     }
+    enqueue_persist(vk);
     resp.ok = true;
     resp.state = MANIFEST_SEALED;
     resp.tensor_count = man.object_ids.size();
@@ -316,41 +317,18 @@ PullTensorResponse Daemon::on_pull_tensor(const PullTensorRequest& r) {
         resp.message = "too many concurrent exports for job";
         return resp;
     }
-    // Resolve the source and take the export hold before dropping the lock.
-    auto lit = locations_.find(o->synthetic_tid);
-    if (lit == locations_.end()) {
-        resp.message = "object not resident";
+    // Resolve the source and take the read hold before dropping the lock.
+    ReadSrc src;
+    std::string why;
+    if (!begin_read(*o, &src, &why)) {
+        resp.message = why;
         return resp;
     }
-    const char* pinned_src = nullptr;
-    ColdEntry cold;
-    uint64_t cold_ref = 0;
-    ofld_location_kind_t src_kind = lit->second.kind;
-    if (src_kind == OFLD_LOC_PINNED) {
-        uint32_t st = state_of(lit->second.slot);
-        if (st != OFLD_SLOT_PINNED_VALID && st != OFLD_SLOT_DRAIN_IN_FLIGHT) {
-            resp.message = "object transitioning; retry";
-            return resp;
-        }
-        pinned_src = slot_ptr(lit->second.slot);
-    } else if (src_kind == OFLD_LOC_PAGEABLE || src_kind == OFLD_LOC_NVME) {
-        cold_ref = lit->second.cold_ref;
-        if (!pin_cold(cold_ref, &cold)) {
-            resp.message = "cold copy unavailable";
-            return resp;
-        }
-    } else {
-        resp.message = "object not resident";
-        return resp;
-    }
-    if (o->export_refs++ == 0) o->state_before_export = o->state;
-    storage_io(o->synthetic_tid, +1);
-    o->state = OBJ_EXPORT_IN_FLIGHT;
     job->inflight_export_bytes += nbytes;
     job->exports_in_flight++;
     Metrics::get().add(M::kExportInflightBytes, nbytes);
-    Metrics::get().inc(src_kind == OFLD_LOC_PINNED     ? M::kExportFromPinned
-                       : src_kind == OFLD_LOC_PAGEABLE ? M::kExportFromPageable
+    Metrics::get().inc(src.kind == OFLD_LOC_PINNED     ? M::kExportFromPinned
+                       : src.kind == OFLD_LOC_PAGEABLE ? M::kExportFromPageable
                                                        : M::kExportFromNvme);
     const uint64_t hlo = o->hash_lo, hhi = o->hash_hi;
     const uint64_t chunk = std::max<uint64_t>(cfg_.v2_export_chunk_bytes, 1 << 20);
@@ -374,13 +352,13 @@ PullTensorResponse Daemon::on_pull_tensor(const PullTensorRequest& r) {
         std::vector<char> bounce;
         for (uint64_t off = 0; ok && off < nbytes; off += chunk) {
             uint64_t n = std::min(chunk, nbytes - off);
-            if (pinned_src) {
-                ok = sink->write(pinned_src + off, n);
-            } else if (cold.kind == OFLD_LOC_PAGEABLE) {
-                ok = sink->write(cold.pageable + off, n);
+            if (src.pinned) {
+                ok = sink->write(src.pinned + off, n);
+            } else if (src.kind == OFLD_LOC_PAGEABLE) {
+                ok = sink->write(src.cold.pageable + off, n);
             } else {
                 bounce.resize(n);
-                ok = read_cold(cold, bounce.data(), off, n) && sink->write(bounce.data(), n);
+                ok = read_cold(src.cold, bounce.data(), off, n) && sink->write(bounce.data(), n);
                 if (!ok) err = "cold read or transport write failed";
             }
             if (!ok && err.empty()) err = "transport write failed";
@@ -389,20 +367,12 @@ PullTensorResponse Daemon::on_pull_tensor(const PullTensorRequest& r) {
     }
 
     lk.lock();
-    if (cold_ref) unpin_cold(cold_ref);
     if (Job* j2 = find_job(r.job)) {
         j2->inflight_export_bytes -= std::min(j2->inflight_export_bytes, nbytes);
         if (j2->exports_in_flight) j2->exports_in_flight--;
     }
     Metrics::get().sub(M::kExportInflightBytes, nbytes);
-    if (CanonicalObject* o2 = find_object(r.object_id)) {
-        if (o2->export_refs) {
-            o2->export_refs--;
-            storage_io(o2->synthetic_tid, -1);
-        }
-        if (o2->export_refs == 0) o2->state = o2->state_before_export;
-        maybe_free_object(*o2);
-    }
+    end_read(r.object_id, src);
     if (!ok) {
         Metrics::get().inc(M::kExportTransportErrors);
         resp.message = "transport failed: " + err;
@@ -561,6 +531,7 @@ DropCanonicalVersionResponse Daemon::on_drop_version(const DropCanonicalVersionR
         }
     }
     manifests_.erase(VersionKey{uid, r.model_role, r.model_version});
+    unlink_persisted_manifest(VersionKey{uid, r.model_role, r.model_version});
     auto lit = latest_sealed_.find({uid, r.model_role});
     if (lit != latest_sealed_.end() && lit->second == r.model_version) latest_sealed_.erase(lit);
     resp.ok = true;
@@ -587,7 +558,10 @@ void Daemon::enforce_retention(const JobUID& uid, uint32_t role) {
             CanonicalObject* o = find_object(oid);
             if (o && !release_object(*o)) all = false;
         }
-        if (all) manifests_.erase(VersionKey{uid, role, sealed[i]});
+        if (all) {
+            manifests_.erase(VersionKey{uid, role, sealed[i]});
+            unlink_persisted_manifest(VersionKey{uid, role, sealed[i]});
+        }
     }
 }
 

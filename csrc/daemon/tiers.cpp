@@ -9,6 +9,7 @@
 //                          drain_policy.pageable_limit_gb, NVMe beyond it
 // (StateSpectre's pageable_then_nvme never reaches NVMe, reference:
 // src/daemon/daemon.cpp:1772; this runtime spills once the budget is hit.)
+#include <unistd.h>
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
@@ -96,6 +97,9 @@ void Daemon::discard_storage(ColdEntry& c) {
         std::free(c.pageable);
         c.pageable = nullptr;
         Metrics::get().sub(M::kPageableResidentBytes, c.nbytes);
+    } else if (c.kind == OFLD_LOC_NVME && c.persisted) {
+        for (const Extent& e : c.extents) ::unlink(e.path.c_str());  // a durable version file
+        c.extents.clear();
     } else if (c.kind == OFLD_LOC_NVME) {
         nvme_release(c.extents);
         c.extents.clear();

@@ -78,7 +78,10 @@ namespace ofld {
     X(kBatchOffloadItems, "batch_offload_items_total")                         \
     X(kBatchPrefetchItems, "batch_prefetch_items_total")                       \
     X(kPeerBuffersPublished, "peer_buffers_published_total")                   \
-    X(kRingCompletionsApplied, "ring_completions_applied_total")
+    X(kRingCompletionsApplied, "ring_completions_applied_total")                 \
+    X(kVersionsPersisted, "versions_persisted_total")                          \
+    X(kPersistedBytes, "persisted_bytes_total")                                \
+    X(kVersionsRecovered, "versions_recovered_total")
 
 enum class M : int {
 #define OFLD_ENUM(id, name) id,

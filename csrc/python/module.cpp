@@ -158,6 +158,7 @@ DaemonConfig config_from(py::dict kw) {
     }
     if (kw.contains("pageable_limit_mb")) c.pageable_limit_bytes = kw["pageable_limit_mb"].cast<uint64_t>() << 20;
     if (kw.contains("io_engine")) c.nvme_io_engine = kw["io_engine"].cast<std::string>();
+    if (kw.contains("persist_dir")) c.v2_persist_dir = kw["persist_dir"].cast<std::string>();
     if (kw.contains("retain_sealed_versions"))
         c.v2_retain_sealed_versions = kw["retain_sealed_versions"].cast<uint32_t>();
     if (kw.contains("thresholds")) {
@@ -540,6 +541,7 @@ PYBIND11_MODULE(_C, m) {
         d["dedup_default_mode"] = c.v2_dedup_default_mode;
         d["creating_policy"] = c.v2_creating_policy;
         d["retain_sealed_versions"] = c.v2_retain_sealed_versions;
+        d["persist_dir"] = c.v2_persist_dir;
         d["default_transport"] = c.v2_default_transport;
         d["fallback_transport"] = c.v2_fallback_transport;
         d["control_tcp_port"] = c.v2_control_tcp_port;

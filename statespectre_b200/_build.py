@@ -33,7 +33,7 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 
 COMMON = ["common/codec.cpp", "common/transport.cpp", "common/metrics.cpp", "common/numa.cpp"]
 DAEMON = ["daemon/config.cpp", "daemon/daemon.cpp", "daemon/slots.cpp", "daemon/tiers.cpp",
-          "daemon/nvme.cpp", "daemon/canonical.cpp", "daemon/rollout.cpp"]
+          "daemon/nvme.cpp", "daemon/canonical.cpp", "daemon/rollout.cpp", "daemon/persist.cpp"]
 AGENT = ["agent/agent.cpp"]
 KERNELS = ["kernels/offload_kernels.cu", "kernels/weight_sync.cu", "kernels/hash_noalloc.cu"]
 KERNEL_HOST = ["kernels/timing.cpp"]

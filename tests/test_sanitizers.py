@@ -91,6 +91,8 @@ arenas:
       size_mb: 64
 drain_policy:
   drain_on_d2h_complete: true
+manifest:
+  persist_dir: {tmp_path / "versions"}
 """)
     d = launch_daemon(sock, config=str(cfg), log_path=log, env=env, binary=f"offloadd_{variant}")
     try:
@@ -108,6 +110,10 @@ drain_policy:
         for t in ths:
             t.join(240)
         assert not errs, errs
+        deadline = time.time() + 30  # the persist worker wrote every sealed version
+        while time.time() < deadline and d.stats()["versions_persisted_total"] < 3:
+            time.sleep(0.05)
+        assert d.stats()["versions_persisted_total"] == 3
         # a session that stops heartbeating: the daemon reclaims it by timeout
         s = offload_context(daemon_addr=sock, device="cpu", rank=9)
         s.off.copy(torch.randn(5000), wait=True)
