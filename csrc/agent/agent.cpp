@@ -690,6 +690,16 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
     const bool z = D.want_z(ptr, nbytes, fmt_hint) && D.zscan(ptr, nbytes, D.stream_of(stream), &zb);
     if (z) rq.flags |= OFLD_FLAG_FORMAT_ZBF16;
     RequestOffloadResponse g = D.call<Op::kRequestOffload>(rq);
+    // Backpressure: every pinned run can be briefly held by transfers in
+    // flight (readbacks, restores) with nothing drainable; they release runs
+    // shortly, so a blocked reservation is retried for up to blocked_wait_ms.
+    const uint64_t blocked_deadline = mono_ns() + D.opt.blocked_wait_ms * 1000000ull;
+    uint64_t backoff_us = 200;
+    while (g.blocked && mono_ns() < blocked_deadline) {
+        sleep_us(backoff_us);
+        backoff_us = std::min<uint64_t>(backoff_us * 2, 20000);
+        g = D.call<Op::kRequestOffload>(rq);
+    }
     if (!g.ok || g.blocked) {
         D.pool.put(zb);
         t.message = g.ok ? "offload blocked (pinned pressure)" : g.message;

@@ -230,6 +230,7 @@ class PyAgent {
             else if (k == "batch_group_bytes") o.batch_group_bytes = v.cast<uint64_t>();
             else if (k == "kernel_timing") o.kernel_timing = v.cast<bool>();
             else if (k == "registration_threads") o.registration_threads = v.cast<int>();
+            else if (k == "blocked_wait_ms") o.blocked_wait_ms = v.cast<uint64_t>();
             else throw std::invalid_argument("unknown agent option '" + k + "'");
         }
         py::gil_scoped_release nogil;

@@ -872,6 +872,8 @@ _AGENT_OPTION_KEYS = {
 def _daemon_agent_options(path: str, rank: int, gpu: int) -> dict:
     """The daemon's forwarded ``kernels:`` / ``nvlink:`` settings (empty when
     the daemon does not offer them)."""
+    if not path.startswith("tcp://") and not os.path.exists(path):
+        return {}  # no daemon there; the session's own connect reports it
     try:
         conn = native().RawConn(path, 5000)
     except Exception:  # noqa: BLE001 - the agent reports connection errors itself
