@@ -1229,6 +1229,41 @@ void Agent::discard(uint64_t tid, uint64_t ver) {
     D.tab_cv.notify_all();
 }
 
+void Agent::discard_batch(const std::vector<std::pair<uint64_t, uint64_t>>& items) {
+    Impl& D = *d_;
+    std::vector<std::pair<uint64_t, uint64_t>> todo = items;
+    const uint64_t deadline = mono_ns() + 30ull * 1000000000ull;
+    uint64_t backoff_us = 100;
+    while (!todo.empty()) {
+        BatchDiscardTensorRequest r;
+        r.rank_id = D.opt.rank_id;
+        r.rank_epoch = D.epoch;
+        for (auto& tv : todo) r.items.push_back(TensorVersion{tv.first, tv.second});
+        BatchDiscardTensorResponse resp = D.call<Op::kBatchDiscardTensor>(r);
+        if (!resp.ok) {
+            LOG_WARN(TAG, "discard_batch: %s", resp.message.c_str());
+            break;
+        }
+        std::vector<std::pair<uint64_t, uint64_t>> again;
+        for (size_t i = 0; i < todo.size() && i < resp.results.size(); ++i) {
+            const StatusResponse& st = resp.results[i];
+            if (!st.ok && st.message.find("retry") != std::string::npos && mono_ns() < deadline)
+                again.push_back(todo[i]);
+            else if (!st.ok)
+                LOG_WARN(TAG, "discard(%llu:%llu): %s", (unsigned long long)todo[i].first,
+                         (unsigned long long)todo[i].second, st.message.c_str());
+        }
+        todo.swap(again);
+        if (!todo.empty()) {
+            sleep_us(backoff_us);
+            backoff_us = std::min<uint64_t>(backoff_us * 2, 5000);
+        }
+    }
+    std::lock_guard<std::mutex> g(D.tab_mu);
+    for (auto& tv : items) D.tensors.erase({tv.first, tv.second});
+    D.tab_cv.notify_all();
+}
+
 void Agent::assert_no_inflight() const {
     std::lock_guard<std::mutex> g(d_->inflight_mu);
     if (!d_->inflight.empty())

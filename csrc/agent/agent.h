@@ -145,6 +145,9 @@ class Agent {
     bool tensor_hash(uint64_t tensor_id, uint64_t version, uint64_t* lo, uint64_t* hi) const;
     std::string location(uint64_t tensor_id, uint64_t version);
     void discard(uint64_t tensor_id, uint64_t version);
+    // One round trip for many tensors; items still in a transfer are retried
+    // together (bounded), like discard().
+    void discard_batch(const std::vector<std::pair<uint64_t, uint64_t>>& items);
     void assert_no_inflight() const;
     void synchronize();
 

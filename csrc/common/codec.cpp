@@ -42,6 +42,7 @@ const char* op_name(Op op) {
         case Op::kDiscardTensor: return "DiscardTensor";
         case Op::kCarryForward: return "CarryForward";
         case Op::kGetAgentOptions: return "GetAgentOptions";
+        case Op::kBatchDiscardTensor: return "BatchDiscardTensor";
     }
     return "Unknown";
 }
@@ -91,6 +92,7 @@ std::vector<uint8_t> reencode_body(Op op, bool response, const std::vector<uint8
         CASE(kLookupPeerBuffer) CASE(kGetJobStats) CASE(kExportManifest) CASE(kDiscardTensor)
         CASE(kCarryForward)
         CASE(kGetAgentOptions)
+        CASE(kBatchDiscardTensor)
 #undef CASE
         default: break;
     }

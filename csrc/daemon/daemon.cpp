@@ -416,6 +416,7 @@ void Daemon::dispatch(int fd, Op op, const std::vector<uint8_t>& b, std::vector<
         ROUTE(kDiscardTensor, on_discard_tensor(req))
         ROUTE(kCarryForward, on_carry_forward(req))
         ROUTE(kGetAgentOptions, on_get_agent_options(req))
+        ROUTE(kBatchDiscardTensor, on_batch_discard(req))
         default:
             LOG_WARN(TAG, "unknown opcode %u", unsigned(op));
             throw std::runtime_error("unknown opcode");

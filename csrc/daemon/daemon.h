@@ -266,6 +266,8 @@ class Daemon {
     GetJobStatsResponse on_get_job_stats(const GetJobStatsRequest& r);
     GetAgentOptionsResponse on_get_agent_options(const GetAgentOptionsRequest& r);
     StatusResponse on_discard_tensor(const DiscardTensorRequest& r);
+    BatchDiscardTensorResponse on_batch_discard(const BatchDiscardTensorRequest& r);
+    StatusResponse do_discard(uint32_t rank, uint64_t tid, uint64_t ver);  // mu_ held, epoch checked
 
     // canonical.cpp
     RegisterJobResponse on_register_job(const RegisterJobRequest& r);

@@ -695,6 +695,26 @@ StatusResponse Daemon::on_discard_tensor(const DiscardTensorRequest& r) {
         Metrics::get().inc(M::kEpochMismatchRejected);
         return {false, "epoch invalid"};
     }
+    return do_discard(r.rank_id, r.tensor_id, r.version);
+}
+
+BatchDiscardTensorResponse Daemon::on_batch_discard(const BatchDiscardTensorRequest& r) {
+    std::lock_guard<std::mutex> g(mu_);
+    drain_rings();
+    BatchDiscardTensorResponse resp;
+    if (!epoch_ok(r.rank_id, r.rank_epoch)) {
+        Metrics::get().inc(M::kEpochMismatchRejected);
+        resp.message = "epoch invalid";
+        return resp;
+    }
+    resp.ok = true;
+    resp.message = "ok";
+    for (const TensorVersion& it : r.items) resp.results.push_back(do_discard(r.rank_id, it.tensor_id, it.version));
+    return resp;
+}
+
+StatusResponse Daemon::do_discard(uint32_t rank, uint64_t tid, uint64_t ver) {
+    const DiscardTensorRequest r{rank, 0, tid, ver};
     if (is_canonical_tid(r.tensor_id)) return {false, "canonical objects are released, not discarded"};
     auto it = locations_.find(r.tensor_id);
     if (it == locations_.end()) return {true, "unknown tensor (already discarded)"};

@@ -200,6 +200,7 @@ OFLD_OP(kExportManifest, ExportManifestRequest, ExportManifestResponse)
 OFLD_OP(kDiscardTensor, DiscardTensorRequest, StatusResponse)
 OFLD_OP(kCarryForward, CarryForwardRequest, CarryForwardResponse)
 OFLD_OP(kGetAgentOptions, GetAgentOptionsRequest, GetAgentOptionsResponse)
+OFLD_OP(kBatchDiscardTensor, BatchDiscardTensorRequest, BatchDiscardTensorResponse)
 #undef OFLD_OP
 
 // Re-encode a body through the C++ schema (decode then encode). Used by the

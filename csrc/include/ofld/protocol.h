@@ -58,6 +58,7 @@ enum class Op : uint16_t {
     kDiscardTensor = 46,         // drop a tensor's pinned and cold copies by identity
     kCarryForward = 47,          // new-version objects that share an older version's storage
     kGetAgentOptions = 48,       // tuning the daemon config forwards to rank agents (kernels:, nvlink:)
+    kBatchDiscardTensor = 49,    // DiscardTensor for many (tensor, version) pairs in one round trip
 };
 
 const char* op_name(Op op);
@@ -746,6 +747,25 @@ struct DiscardTensorRequest {
 template <class V> void fields(V& v, DiscardTensorRequest& m) {
     v(m.rank_id, m.rank_epoch, m.tensor_id, m.version);
 }
+
+struct TensorVersion {
+    uint64_t tensor_id = 0, version = 0;
+};
+template <class V> void fields(V& v, TensorVersion& m) { v(m.tensor_id, m.version); }
+
+struct BatchDiscardTensorRequest {
+    uint32_t rank_id = 0;
+    uint64_t rank_epoch = 0;
+    std::vector<TensorVersion> items;
+};
+template <class V> void fields(V& v, BatchDiscardTensorRequest& m) { v(m.rank_id, m.rank_epoch, m.items); }
+
+struct BatchDiscardTensorResponse {
+    bool ok = false;
+    std::string message;
+    std::vector<StatusResponse> results;
+};
+template <class V> void fields(V& v, BatchDiscardTensorResponse& m) { v(m.ok, m.message, m.results); }
 
 struct ExportManifestResponse {
     bool ok = false;

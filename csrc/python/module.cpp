@@ -348,6 +348,11 @@ PYBIND11_MODULE(_C, m) {
                  py::gil_scoped_release nogil;
                  s.ag().discard(t, v);
              })
+        .def("discard_batch",
+             [](PyAgent& s, std::vector<std::pair<uint64_t, uint64_t>> items) {
+                 py::gil_scoped_release nogil;
+                 s.ag().discard_batch(items);
+             })
         .def("assert_no_inflight", [](PyAgent& s) { s.ag().assert_no_inflight(); })
         .def("synchronize",
              [](PyAgent& s) {

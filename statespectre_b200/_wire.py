@@ -60,6 +60,7 @@ class Op:
     DISCARD_TENSOR = 46
     CARRY_FORWARD = 47
     GET_AGENT_OPTIONS = 48
+    BATCH_DISCARD_TENSOR = 49
 
 
 # Backward-compatible names used by rollout engines.
@@ -198,6 +199,9 @@ SCHEMA: Dict[str, List[Tuple[str, Any]]] = {
     "OptionEntry": [("key", S), ("value", S)],
     "GetAgentOptionsRequest": [("rank_id", "u32"), ("gpu_id", "u32")],
     "GetAgentOptionsResponse": STATUS + [("options", ["OptionEntry"])],
+    "TensorVersion": [("tensor_id", "u64"), ("version", "u64")],
+    "BatchDiscardTensorRequest": [("rank_id", "u32"), ("rank_epoch", "u64"), ("items", ["TensorVersion"])],
+    "BatchDiscardTensorResponse": STATUS + [("results", ["Status"])],
 }
 
 # opcode -> (request message, response message)
@@ -235,6 +239,7 @@ OPS: Dict[int, Tuple[str, str]] = {
     Op.DISCARD_TENSOR: ("DiscardTensorRequest", "Status"),
     Op.CARRY_FORWARD: ("CarryForwardRequest", "CarryForwardResponse"),
     Op.GET_AGENT_OPTIONS: ("GetAgentOptionsRequest", "GetAgentOptionsResponse"),
+    Op.BATCH_DISCARD_TENSOR: ("BatchDiscardTensorRequest", "BatchDiscardTensorResponse"),
 }
 
 _PRIM = {"u8": struct.Struct("<B"), "u16": struct.Struct("<H"), "u32": struct.Struct("<I"),

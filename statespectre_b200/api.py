@@ -712,6 +712,16 @@ class Off:
         return [self._evict_impl(t, n, stream, destructive, not require_own_storage, unsafe_autograd,
                                  not require_own_storage, False) for t, n in zip(tensors, names)]
 
+    def discard_batch(self, handles: Sequence["OffloadHandle"]) -> None:
+        """``h.discard()`` for many handles with one daemon round trip."""
+        todo = [h for h in handles if not h._discarded]
+        if not todo:
+            return
+        self._agent.discard_batch([(h.tensor_id, h.version) for h in todo])
+        for h in todo:
+            h._prefetched = None
+            h._discarded = True
+
     def evict_batch(self, tensors: Sequence[torch.Tensor], stream=None, wait: bool = True,
                     versions: Optional[Sequence[int]] = None) -> List[OffloadHandle]:
         """Non-destructive copy of many contiguous tensors with one reservation round trip."""

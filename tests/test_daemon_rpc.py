@@ -172,3 +172,31 @@ def test_stats_cover_every_metric_name(d64):
     for k in ("bandwidth_mbps_p50", "bandwidth_mbps_p90", "bandwidth_mbps_p99", "total_slots"):
         assert k in s
     assert s["total_slots"] == 32
+
+
+def test_control_plane_benchmark_runs():
+    from statespectre_b200.benchmarks import control
+
+    res = control.run(seconds=0.3, rank_counts=(2,))
+    assert res["single"]["round_trips_per_s"] > 100
+    assert res["batch"]["items_per_s"] > 1000
+    assert res["ranks"]["2"]["round_trips_per_s"] > 100
+
+
+def test_discard_batch_frees_everything(sock_path):
+    import torch
+
+    from statespectre_b200 import in_process_daemon, offload_context
+
+    d = in_process_daemon(socket=sock_path, arena_mb=64, slot_mb=1, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cpu", rank=0) as off:
+            ts = [torch.randn(n) for n in (10, 1000, 300000, 17)]
+            hs = off.evict_batch(ts) + [off.copy(torch.randn(5000), wait=True)]
+            assert off.daemon_stats()["used_slots"] > 0
+            off.discard_batch(hs)
+            off.discard_batch(hs)  # idempotent
+            st = off.daemon_stats()
+            assert st["used_slots"] == 0 and st["pageable_resident_bytes"] == 0
+    finally:
+        d.stop()
