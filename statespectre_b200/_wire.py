@@ -16,7 +16,7 @@ from __future__ import annotations
 
 import socket
 import struct
-from typing import Any, Dict, List, Tuple
+from typing import Any, Dict, List, Optional, Tuple
 
 RPC_MAGIC = 0x4F465250
 FRAME_HEADER = struct.Struct("<IHHI")
@@ -385,6 +385,62 @@ def parse_export_header(data: bytes) -> dict:
     if magic != EXPORT_MAGIC:
         raise WireError("bad export header magic")
     return {"version": ver, "object_id": oid, "nbytes": nbytes, "content_hash_lo": hlo, "content_hash_hi": hhi}
+
+
+# ---------------------------------------------------------------------------
+# Message helpers under StateSpectre's names (reference:
+# python_api/state_spectre/_wire.py), thin wrappers of the schema codec above
+# for tools written against them.
+# ---------------------------------------------------------------------------
+OFLD_RPC_MAGIC = RPC_MAGIC
+EXPORT_HEADER_FMT = EXPORT_HEADER.format
+
+
+def _job(tenant_id, job_id, launch_epoch, job_name) -> dict:
+    return {"tenant_id": int(tenant_id), "job_id": int(job_id), "launch_epoch": int(launch_epoch),
+            "job_name": job_name or ""}
+
+
+def encode_get_latest(tenant_id, job_id, launch_epoch, job_name, model_role) -> bytes:
+    return encode("GetLatestSealedVersionRequest", job=_job(tenant_id, job_id, launch_epoch, job_name),
+                  model_role=int(model_role))
+
+
+def decode_get_latest_resp(payload: bytes) -> dict:
+    return decode("GetLatestSealedVersionResponse", payload)
+
+
+def manifest_filter(flt: Optional[dict] = None) -> dict:
+    """Filter dict (keys ``pp``, ``tp``, ``ep``, ``etp``, ``expert``) as the
+    ManifestFilter message; absent keys match everything."""
+    flt = flt or {}
+    out = {}
+    for axis in ("pp", "tp", "ep", "etp"):
+        out[f"{axis}_present"] = axis in flt
+        out[f"{axis}_rank"] = int(flt.get(axis, 0))
+    out["expert_present"] = "expert" in flt
+    out["expert_id"] = int(flt.get("expert", 0))
+    return out
+
+
+def encode_get_manifest(tenant_id, job_id, launch_epoch, job_name, model_role, model_version, flt=None) -> bytes:
+    return encode("GetManifestRequest", job=_job(tenant_id, job_id, launch_epoch, job_name),
+                  model_role=int(model_role), model_version=int(model_version), filter=manifest_filter(flt))
+
+
+def decode_get_manifest_resp(payload: bytes) -> dict:
+    return decode("GetManifestResponse", payload)
+
+
+def encode_pull(tenant_id, job_id, launch_epoch, job_name, model_role, model_version, object_id, transport,
+                target_descriptor) -> bytes:
+    return encode("PullTensorRequest", job=_job(tenant_id, job_id, launch_epoch, job_name),
+                  model_role=int(model_role), model_version=int(model_version), object_id=int(object_id),
+                  transport=int(transport), target_descriptor=target_descriptor or "")
+
+
+def decode_pull_resp(payload: bytes) -> dict:
+    return decode("PullTensorResponse", payload)
 
 
 class Connection:

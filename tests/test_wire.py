@@ -118,3 +118,25 @@ def test_proto_schema_docs_are_current():
     from statespectre_b200 import _proto
 
     assert _proto.main(["--check"]) == 0, "run: python -m statespectre_b200._proto"
+
+
+def test_reference_named_helpers_and_compat_modules():
+    """StateSpectre's message helpers keep their names and byte layout
+    (job key, then the message's fields in order)."""
+    import struct
+
+    import state_spectre._rollout as R
+    import state_spectre._wire as W
+
+    assert R.RolloutWeightClient is not None
+    job = struct.pack("<QQQI", 1, 42, 3, 2) + b"j0"
+    assert W.encode_get_latest(1, 42, 3, "j0", 2) == job + struct.pack("<I", 2)
+    filt = b"".join(struct.pack("<?I", k == "tp", 5 if k == "tp" else 0) for k in ("pp", "tp", "ep", "etp"))
+    filt += struct.pack("<?i", False, 0)
+    assert W.encode_get_manifest(1, 42, 3, "j0", 2, 7, {"tp": 5}) == job + struct.pack("<IQ", 2, 7) + filt
+    pull = W.encode_pull(1, 42, 3, "j0", 2, 7, 99, 1, "127.0.0.1:5")
+    assert pull == job + struct.pack("<IQQI", 2, 7, 99, 1) + struct.pack("<I", 11) + b"127.0.0.1:5"
+    resp = W.encode("PullTensorResponse", ok=True, message="", object_id=99, nbytes=8, transport=1,
+                    content_hash_lo=1, content_hash_hi=2, transport_metadata="")
+    assert W.decode_pull_resp(resp)["nbytes"] == 8
+    assert W.OFLD_RPC_MAGIC == 0x4F465250 and struct.calcsize(W.EXPORT_HEADER_FMT) == 40
