@@ -99,7 +99,8 @@ def write_ninja() -> str:
         "  description = DLINK $out",
     ]
     objs = {}
-    for rel in COMMON + DAEMON + AGENT + FABRIC + KERNEL_HOST + ["daemon/main.cpp", "tools/offload_stat.cpp", "tests/selftest.cpp"]:
+    for rel in COMMON + DAEMON + AGENT + FABRIC + KERNEL_HOST + ["daemon/main.cpp", "tools/offload_stat.cpp", "tests/selftest.cpp",
+                                                                "tests/compat_agent.cpp"]:
         if not _exists(rel):
             continue
         o = _obj(rel)
@@ -162,6 +163,12 @@ def write_ninja() -> str:
     lines.append(f"build {ext}: link_so {pick(MODULE)} {pick(AGENT)} {pick(FABRIC)} {pick(DAEMON)} "
                  f"{pick(COMMON)} {pick(KERNEL_HOST)} {kern} {dlink}")
     lines.append("  libs = $cudalib")
+    if "tests/compat_agent.cpp" in objs:  # StateSpectre's C++ agent interface, built against this agent
+        compat = f"{bindir}/ofld_compat_agent"
+        lines.append(f"build {compat}: link_exe {objs['tests/compat_agent.cpp']} {pick(AGENT)} {pick(FABRIC)} "
+                     f"{pick(COMMON)} {pick(KERNEL_HOST)} {kern} {dlink}")
+        lines.append("  libs = $cudalib")
+        defaults.append(compat)
     lines.append("default " + " ".join(defaults + [ext]))
     os.makedirs(BUILD, exist_ok=True)
     path = os.path.join(BUILD, "build.ninja")
