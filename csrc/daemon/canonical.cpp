@@ -83,6 +83,24 @@ bool Daemon::quota_allows_pinned(const Job& j, uint64_t nbytes) const {
     return j.max_pinned == 0 || j.pinned_bytes + nbytes <= j.max_pinned;
 }
 
+// quotas.default, then the job name's quotas.per_job_overrides entry.
+void Daemon::init_job_quotas(Job& j) const {
+    j.max_pinned = cfg_.v2_quota_max_pinned_bytes;
+    j.max_pageable = cfg_.v2_quota_max_pageable_bytes;
+    j.max_nvme = cfg_.v2_quota_max_nvme_bytes;
+    j.max_inflight_d2h = cfg_.v2_quota_max_inflight_d2h_bytes;
+    j.max_inflight_export = cfg_.v2_quota_max_inflight_export_bytes;
+    auto ov = cfg_.v2_job_quota_overrides.find(j.name);
+    if (ov == cfg_.v2_job_quota_overrides.end()) return;
+    for (const auto& q : ov->second) {
+        if (q.first == "max_pinned_bytes") j.max_pinned = q.second;
+        else if (q.first == "max_pageable_bytes") j.max_pageable = q.second;
+        else if (q.first == "max_nvme_bytes") j.max_nvme = q.second;
+        else if (q.first == "max_inflight_d2h_bytes") j.max_inflight_d2h = q.second;
+        else if (q.first == "max_inflight_export_bytes") j.max_inflight_export = q.second;
+    }
+}
+
 RegisterJobResponse Daemon::on_register_job(const RegisterJobRequest& r) {
     std::lock_guard<std::mutex> g(mu_);
     RegisterJobResponse resp;
@@ -114,11 +132,7 @@ RegisterJobResponse Daemon::on_register_job(const RegisterJobRequest& r) {
     j.uid = JobUID{r.tenant_id, job_id, cfg_.v2_include_launch_epoch ? next_launch_epoch_++ : 1};
     j.name = r.job_name;
     j.created_ns = real_ns();
-    j.max_pinned = cfg_.v2_quota_max_pinned_bytes;
-    j.max_pageable = cfg_.v2_quota_max_pageable_bytes;
-    j.max_nvme = cfg_.v2_quota_max_nvme_bytes;
-    j.max_inflight_d2h = cfg_.v2_quota_max_inflight_d2h_bytes;
-    j.max_inflight_export = cfg_.v2_quota_max_inflight_export_bytes;
+    init_job_quotas(j);
     for (size_t i = 0; i < r.label_keys.size() && i < r.label_values.size(); ++i)
         j.labels.emplace_back(r.label_keys[i], r.label_values[i]);
     jobs_[j.uid] = j;

@@ -407,6 +407,37 @@ void walk(DaemonConfig& c, const Node& n, const std::string& path) {
             else if (v.kind == Node::kMap) walk(c, v, p);
             continue;
         }
+        if (p == "quotas.per_job_overrides") {
+            for (auto& job : v.map) {
+                for (auto& q : job.second->map) {
+                    static const char* kKeys[] = {"max_pinned_bytes", "max_pageable_bytes", "max_nvme_bytes",
+                                                  "max_inflight_d2h_bytes", "max_inflight_export_bytes"};
+                    bool ok = false;
+                    for (const char* k : kKeys) ok |= q.first == k;
+                    if (!ok) {
+                        LOG_WARN("config", "unknown key %s.%s.%s (ignored)", p.c_str(), job.first.c_str(),
+                                 q.first.c_str());
+                        continue;
+                    }
+                    c.v2_job_quota_overrides[job.first][q.first] =
+                        as_size(*q.second, p + "." + job.first + "." + q.first);
+                }
+            }
+            continue;  // `{}` (no overrides) parses as an empty map or scalar
+        }
+        if (p.rfind("roles.", 0) == 0 || p.rfind("libfabric.", 0) == 0 || p.rfind("cleanup.", 0) == 0 ||
+            p == "metrics.labels" || p.rfind("metrics.labels.", 0) == 0) {
+            if (v.kind == Node::kMap) {
+                walk(c, v, p);
+            } else if (v.kind == Node::kSeq) {
+                std::string joined;
+                for (auto& e : v.seq) joined += (joined.empty() ? "" : ",") + e->scalar;
+                c.accepted_settings[p] = joined;
+            } else {
+                c.accepted_settings[p] = v.scalar;
+            }
+            continue;
+        }
         auto it = binders().find(p);
         if (it != binders().end()) {
             it->second(c, v, p);

@@ -106,6 +106,13 @@ struct DaemonConfig {
     uint64_t v2_quota_max_nvme_bytes = 0;
     uint64_t v2_quota_max_inflight_d2h_bytes = 0;
     uint64_t v2_quota_max_inflight_export_bytes = 0;
+    // quotas.per_job_overrides: job name -> {max_pinned_bytes, max_pageable_bytes,
+    // max_nvme_bytes, max_inflight_d2h_bytes, max_inflight_export_bytes}
+    std::map<std::string, std::map<std::string, uint64_t>> v2_job_quota_overrides;
+    // Sections StateSpectre's config files carry that this daemon accepts and
+    // keeps without acting on them (roles:, libfabric:, cleanup:,
+    // metrics.labels), flattened to dotted keys; sequences joined with ','.
+    std::map<std::string, std::string> accepted_settings;
 
     // Sections forwarded verbatim to rank agents (nvlink.*, kernels.*).
     std::map<std::string, std::string> agent_options;

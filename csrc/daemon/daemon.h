@@ -271,6 +271,7 @@ class Daemon {
 
     // canonical.cpp
     RegisterJobResponse on_register_job(const RegisterJobRequest& r);
+    void init_job_quotas(Job& j) const;
     RequestCanonicalEvictResponse on_canonical_evict(const RequestCanonicalEvictRequest& r);
     CommitCanonicalObjectResponse on_commit_canonical(const CommitCanonicalObjectRequest& r);
     ReleaseCanonicalResponse on_release_canonical(const ReleaseCanonicalRequest& r);

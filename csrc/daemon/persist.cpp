@@ -404,6 +404,7 @@ void Daemon::recover_persisted() {
             j.uid = uid;
             j.name = jk.job_name;
             j.created_ns = real_ns();
+            init_job_quotas(j);
             jobs_[uid] = j;
         }
         next_launch_epoch_ = std::max(next_launch_epoch_, jk.launch_epoch + 1);

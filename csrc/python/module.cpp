@@ -548,6 +548,8 @@ PYBIND11_MODULE(_C, m) {
         d["creating_policy"] = c.v2_creating_policy;
         d["retain_sealed_versions"] = c.v2_retain_sealed_versions;
         d["persist_dir"] = c.v2_persist_dir;
+        d["accepted_settings"] = c.accepted_settings;
+        d["job_quota_overrides"] = c.v2_job_quota_overrides;
         d["default_transport"] = c.v2_default_transport;
         d["fallback_transport"] = c.v2_fallback_transport;
         d["control_tcp_port"] = c.v2_control_tcp_port;

@@ -227,3 +227,59 @@ kernels:
     finally:
         d.stop()
     assert _daemon_agent_options(sock + ".missing", 0, 0) == {}
+
+
+def test_per_job_quota_overrides_and_accepted_sections(tmp_path):
+    """quotas.per_job_overrides applies to the named job only; roles:,
+    libfabric:, cleanup: and metrics.labels are accepted and kept."""
+    import torch
+
+    from statespectre_b200 import ModelRole, in_process_daemon, offload_context
+
+    sock = str(tmp_path / "d.sock")
+    text = f"""
+daemon:
+  socket_path: {sock}
+arenas:
+  allocation_granularity_mb: 1
+  per_numa:
+    - numa_node: 0
+      size_mb: 64
+roles:
+  rollout_visible_roles:
+    - POLICY_ROLLOUT
+  immutable_roles:
+    - POLICY_REFERENCE
+    - REWARD_MODEL
+quotas:
+  default:
+    max_pinned_bytes: 1GiB
+  per_job_overrides:
+    small:
+      max_pinned_bytes: 1MiB
+libfabric:
+  provider: auto
+cleanup:
+  on_job_terminate: release
+metrics:
+  labels:
+    cluster: b200
+"""
+    c = native().parse_config(text)
+    assert c["job_quota_overrides"] == {"small": {"max_pinned_bytes": 1 << 20}}
+    assert c["accepted_settings"]["roles.immutable_roles"] == "POLICY_REFERENCE,REWARD_MODEL"
+    assert c["accepted_settings"]["libfabric.provider"] == "auto"
+    assert c["accepted_settings"]["metrics.labels.cluster"] == "b200"
+    d = in_process_daemon(yaml=text, socket=sock)
+    try:
+        t = torch.randn(1 << 20)  # 4 MiB
+        for job, ok in (("small", False), ("big", True)):
+            with offload_context(daemon_addr=sock, device="cpu", rank=0, job_name=job) as off:
+                k = off.canonical_key(model_role=ModelRole.POLICY_ROLLOUT, model_version=1, param_name="w", tensor=t)
+                if ok:
+                    assert off.canonical_evict(t.clone(), k).did_d2h
+                else:
+                    with pytest.raises(RuntimeError, match="quota"):
+                        off.canonical_evict(t.clone(), k)
+    finally:
+        d.stop()
