@@ -80,3 +80,34 @@ def test_host_hash_oracle_properties():
     assert C.ssh_hash(a[:0]) != (0, 0)
     # digests fold to the object hash
     assert C.ssh_fold(C.ssh_digests(a), a.nbytes) == C.ssh_hash(a)
+
+
+def test_aliased_flat_buffer_restore_into(sock_path):
+    """Parameters that are views of one flat buffer: the buffer is offloaded
+    and restored in place, and every view sees the restored bytes (views keep
+    aliasing); a destructive evict of a single view is refused."""
+    import pytest
+
+    d = in_process_daemon(socket=sock_path, arena_mb=64, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cpu", rank=0) as off:
+            flat = torch.randn(10000, generator=torch.Generator().manual_seed(1))
+            views = {"a": flat[:1000].view(10, 100), "b": flat[1000:5000], "c": flat[5000:].view(50, 100)}
+            ref = flat.clone()
+            h = off.copy(flat, wait=True)
+            flat.zero_()
+            assert float(views["a"].abs().sum()) == 0.0
+            h.restore_into(flat)
+            assert torch.equal(flat, ref)
+            assert torch.equal(views["a"].reshape(-1), ref[:1000])
+            assert torch.equal(views["c"].reshape(-1), ref[5000:])
+            views["b"][0] = 123.0
+            assert float(flat[1000]) == 123.0
+            with pytest.raises(RuntimeError):
+                off.evict(views["b"])  # does not own its storage
+            hv = off.evict(views["b"], allow_views=True, compact=True, wait=True)
+            assert torch.equal(hv.restore(), flat[1000:5000])
+            h.discard()
+            hv.discard()
+    finally:
+        d.stop()
