@@ -811,9 +811,12 @@ class Off:
 
     @contextlib.contextmanager
     def trace(self, path: str):
-        """Write a Chrome-trace JSON of session counters around a block."""
+        """Write a Chrome-trace JSON of session counters around a block; with
+        kernel timing on (``enable_kernel_timing``), every stamped kernel of
+        the block is a complete event on a GPU track (device timestamps)."""
         t0 = time.time_ns()
         before = self._agent.stats()
+        _, stamp0 = self.kernel_timings()
         ev = [{"name": "offload_session", "ph": "B", "ts": t0 / 1000.0, "pid": before["rank_id"],
                "tid": max(before["gpu_id"], 0), "args": before}]
         try:
@@ -828,6 +831,12 @@ class Off:
                        "args": {k: after[k] - before[k] for k in ("d2h_completed", "h2d_completed", "evict_count",
                                                                   "restore_count", "d2h_bytes", "h2d_bytes",
                                                                   "kernel_launches", "rpc_count")}})
+            recs, _ = self.kernel_timings(stamp0)
+            for r in recs:
+                ev.append({"name": r["kernel"], "ph": "X", "ts": r["t0"] / 1000.0, "dur": r["ns"] / 1000.0,
+                           "pid": f"gpu{max(after['gpu_id'], 0)}", "tid": "kernels",
+                           "args": {"bytes": r["bytes"], "GB/s": round(r["bytes"] / max(r["ns"], 1), 3),
+                                    "seq": r["seq"]}})
             with open(path, "w") as f:
                 json.dump({"traceEvents": ev, "displayTimeUnit": "ms"}, f)
 

@@ -127,5 +127,16 @@ def test_kernel_timing_stamps_transfers(gpu_off):
         assert 1.0 < gbs < 20000.0, r  # PCIe kernels tens of GB/s, the scan HBM-rate
     prof = off.kernel_profile(start)
     assert prof["k1_evict"]["bytes"] == 32 << 20
+    # the session trace carries the stamped kernels as device-time events
+    import json
+    import os
+    import tempfile
+
+    tp = os.path.join(tempfile.mkdtemp(), "trace.json")
+    with off.trace(tp):
+        off.copy(x, wait=True).discard()
+    evs = json.load(open(tp))["traceEvents"]
+    kev = [e for e in evs if e.get("ph") == "X"]
+    assert {"zbf16_scan", "k1_evict_zbf16"} <= {e["name"] for e in kev} and all(e["dur"] > 0 for e in kev)
     hx.discard()
     hf.discard()

@@ -111,3 +111,23 @@ def test_aliased_flat_buffer_restore_into(sock_path):
             hv.discard()
     finally:
         d.stop()
+
+
+def test_session_trace_writes_chrome_json(sock_path, tmp_path):
+    import json
+
+    d = in_process_daemon(socket=sock_path, arena_mb=64, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cpu", rank=3) as off:
+            path = str(tmp_path / "t.json")
+            with off.trace(path):
+                h = off.copy(torch.randn(1000), wait=True)
+                h.restore()
+                h.discard()
+            evs = json.load(open(path))["traceEvents"]
+            assert [e["ph"] for e in evs] == ["B", "E", "i"]
+            delta = evs[2]["args"]
+            assert delta["d2h_completed"] == 1 and delta["h2d_completed"] == 1 and delta["rpc_count"] > 0
+            assert evs[0]["pid"] == 3
+    finally:
+        d.stop()
