@@ -288,6 +288,8 @@ const std::map<std::string, Binder>& binders() {
         {"drain_policy.pageable_limit_gb", [](DaemonConfig& c, const Node& n, const std::string& k) { c.pageable_limit_bytes = as_u64(n, k) << 30; }},
         {"drain_policy.drain_workers", [](DaemonConfig& c, const Node& n, const std::string& k) { c.drain_workers = uint32_t(as_u64(n, k)); }},
         {"drain_policy.readback_workers", [](DaemonConfig& c, const Node& n, const std::string& k) { c.readback_workers = uint32_t(as_u64(n, k)); }},
+        {"drain_policy.pageable_pool_mb", [](DaemonConfig& c, const Node& n, const std::string& k) { c.pageable_pool_bytes = as_u64(n, k) << 20; }},
+        {"drain_policy.copy_threads", [](DaemonConfig& c, const Node& n, const std::string& k) { c.copy_threads = uint32_t(as_u64(n, k)); }},
         // nvme
         {"nvme.enabled", [](DaemonConfig& c, const Node& n, const std::string& k) { c.nvme_enabled = as_bool(n, k); }},
         {"nvme.path", [](DaemonConfig& c, const Node& n, const std::string& k) { c.nvme_path = need_scalar(n, k); }},

@@ -58,6 +58,11 @@ struct DaemonConfig {
     uint64_t pageable_limit_bytes = 0;  // 0 = unlimited
     uint32_t drain_workers = 2;
     uint32_t readback_workers = 2;
+    // Freed pageable buffers kept for reuse (bytes), so tensors that cycle
+    // through the pageable tier copy into memory that is already faulted in.
+    uint64_t pageable_pool_bytes = 4ull << 30;
+    // Threads that share one large pinned <-> pageable copy (64 MiB pieces).
+    uint32_t copy_threads = 4;
 
     // nvme
     bool nvme_enabled = true;

@@ -236,7 +236,7 @@ void Daemon::teardown() {
         a.fd = -1;
     }
     for (auto& kv : cold_)
-        if (kv.second.pageable) std::free(kv.second.pageable);
+        if (kv.second.pageable) pageable_pool_.put(kv.second.pageable, kv.second.pageable_size, 0);
     cold_.clear();
     for (auto& kv : peer_buffers_) close_fd(kv.second.fd);
     peer_buffers_.clear();
@@ -667,6 +667,7 @@ GetStatsResponse Daemon::on_get_stats(const GetStatsRequest&) {
     resp.stats.push_back({"canonical_objects", objects_.size()});
     resp.stats.push_back({"sealed_manifests", manifests_.size()});
     resp.stats.push_back({"jobs", jobs_.size()});
+    resp.stats.push_back({"pageable_pool_bytes", pageable_pool_.pooled()});
     // Per-GPU window (and per-NUMA overflow pool) occupancy: "<scope>.<name>",
     // rendered as labelled series by offload-stat --prometheus.
     const uint64_t gran = cfg_.allocation_granularity_bytes;

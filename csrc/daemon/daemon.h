@@ -194,6 +194,7 @@ class Daemon {
         uint32_t readers = 0;     // unlocked readers in flight (readback/export)
         bool doomed = false;      // free once the last reader is done
         bool persisted = false;   // extents are a durable version file: unlink, do not punch
+        uint64_t pageable_size = 0;  // mapping size of `pageable` (pool size class)
     };
     // A read hold on a canonical object's bytes (export, persistence): the
     // source is pinned against drains and frees until end_read.
@@ -315,6 +316,23 @@ class Daemon {
     void readback_loop();
     void heartbeat_loop();
     void ring_loop();
+
+    // ---------------- pageable tier memory (tiers.cpp) ----------------
+    // Anonymous mappings in 2 MiB size classes; freed ones are kept up to
+    // drain_policy.pageable_pool_mb for reuse. Thread-safe.
+    class PageablePool {
+     public:
+        char* get(uint64_t nbytes, uint64_t* size_out);
+        void put(char* p, uint64_t size, uint64_t cap);
+        ~PageablePool();
+        uint64_t pooled() const { return pooled_.load(); }
+     private:
+        std::mutex mu_;
+        std::multimap<uint64_t, char*> free_;
+        std::atomic<uint64_t> pooled_{0};
+    };
+    PageablePool pageable_pool_;
+    void copy_bytes(char* dst, const char* src, uint64_t n) const;  // threaded for large copies
 
     // ---------------- read holds and durable versions (persist.cpp) ----------------
     bool begin_read(CanonicalObject& o, ReadSrc* src, std::string* why);  // mu_ held

@@ -9,10 +9,14 @@
 //                          drain_policy.pageable_limit_gb, NVMe beyond it
 // (StateSpectre's pageable_then_nvme never reaches NVMe, reference:
 // src/daemon/daemon.cpp:1772; this runtime spills once the budget is hit.)
+#include <sys/mman.h>
 #include <unistd.h>
+
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
+#include <thread>
+#include <vector>
 
 #include "daemon.h"
 #include "ofld/log.h"
@@ -28,6 +32,64 @@ void record_bw(uint64_t nbytes, uint64_t t0) {
     if (dt) Metrics::get().record_mbps(double(nbytes) / 1048576.0 / (double(dt) / 1e9));
 }
 }  // namespace
+
+// ---------------------------------------------------------------------------
+// Pageable memory
+// ---------------------------------------------------------------------------
+char* Daemon::PageablePool::get(uint64_t nbytes, uint64_t* size_out) {
+    const uint64_t cls = 2ull << 20;
+    const uint64_t need = (std::max<uint64_t>(nbytes, 1) + cls - 1) / cls * cls;
+    {
+        std::lock_guard<std::mutex> g(mu_);
+        auto it = free_.lower_bound(need);
+        if (it != free_.end() && it->first <= need + need / 8) {  // reuse up to 12.5 % slack
+            char* p = it->second;
+            *size_out = it->first;
+            pooled_ -= it->first;
+            free_.erase(it);
+            return p;
+        }
+    }
+    void* p = ::mmap(nullptr, need, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
+    if (p == MAP_FAILED) return nullptr;
+    *size_out = need;
+    return static_cast<char*>(p);
+}
+
+void Daemon::PageablePool::put(char* p, uint64_t size, uint64_t cap) {
+    if (!p) return;
+    {
+        std::lock_guard<std::mutex> g(mu_);
+        if (pooled_.load() + size <= cap) {
+            free_.emplace(size, p);
+            pooled_ += size;
+            return;
+        }
+    }
+    ::munmap(p, size);
+}
+
+Daemon::PageablePool::~PageablePool() {
+    for (auto& kv : free_) ::munmap(kv.second, kv.first);
+}
+
+void Daemon::copy_bytes(char* dst, const char* src, uint64_t n) const {
+    const uint64_t piece = 64ull << 20;
+    const uint64_t parts = std::min<uint64_t>(std::max<uint32_t>(cfg_.copy_threads, 1), n / piece);
+    if (parts <= 1) {
+        std::memcpy(dst, src, n);
+        return;
+    }
+    const uint64_t step = (n / parts + 4095) & ~uint64_t(4095);
+    std::vector<std::thread> ts;
+    for (uint64_t k = 1; k < parts; ++k) {
+        const uint64_t off = k * step;
+        if (off >= n) break;
+        ts.emplace_back([=] { std::memcpy(dst + off, src + off, std::min(step, n - off)); });
+    }
+    std::memcpy(dst, src, std::min(step, n));
+    for (auto& t : ts) t.join();
+}
 
 bool Daemon::write_cold(const char* src, uint64_t nbytes, ColdEntry* out, bool allow_pageable) {
     out->nbytes = nbytes;
@@ -49,17 +111,19 @@ bool Daemon::write_cold(const char* src, uint64_t nbytes, ColdEntry* out, bool a
     pageable = pageable && allow_pageable;
     uint64_t t0 = mono_ns();
     if (pageable) {
-        char* buf = static_cast<char*>(std::malloc(nbytes ? nbytes : 1));
+        uint64_t size = 0;
+        char* buf = pageable_pool_.get(nbytes, &size);
         if (buf) {
-            std::memcpy(buf, src, nbytes);
+            copy_bytes(buf, src, nbytes);
             out->kind = OFLD_LOC_PAGEABLE;
             out->pageable = buf;
+            out->pageable_size = size;
             Metrics::get().add(M::kPinnedToPageableBytes, nbytes);
             Metrics::get().add(M::kPageableResidentBytes, nbytes);
             record_bw(nbytes, t0);
             return true;
         }
-        LOG_WARN(TAG, "pageable malloc(%llu) failed", (unsigned long long)nbytes);
+        LOG_WARN(TAG, "pageable allocation of %llu bytes failed", (unsigned long long)nbytes);
         if (!cfg_.nvme_enabled) return false;
     }
     if (!cfg_.nvme_enabled) return false;
@@ -80,7 +144,7 @@ bool Daemon::read_cold(const ColdEntry& c, char* dst, uint64_t off, uint64_t nby
     uint64_t t0 = mono_ns();
     if (c.kind == OFLD_LOC_PAGEABLE) {
         if (!c.pageable) return false;
-        std::memcpy(dst, c.pageable + off, nbytes);
+        copy_bytes(dst, c.pageable + off, nbytes);
         Metrics::get().add(M::kPageableToPinnedBytes, nbytes);
     } else if (c.kind == OFLD_LOC_NVME) {
         if (!nvme_read(c.extents, dst, off, nbytes)) return false;
@@ -94,7 +158,7 @@ bool Daemon::read_cold(const ColdEntry& c, char* dst, uint64_t off, uint64_t nby
 
 void Daemon::discard_storage(ColdEntry& c) {
     if (c.kind == OFLD_LOC_PAGEABLE && c.pageable) {
-        std::free(c.pageable);
+        pageable_pool_.put(c.pageable, c.pageable_size, cfg_.pageable_pool_bytes);
         c.pageable = nullptr;
         Metrics::get().sub(M::kPageableResidentBytes, c.nbytes);
     } else if (c.kind == OFLD_LOC_NVME && c.persisted) {

@@ -111,3 +111,33 @@ def test_pressure_threshold_queues_background_drains(sock_path):
                 h.restore()
     finally:
         d.stop()
+
+
+def test_pageable_pool_reuses_drained_buffers(sock_path):
+    """Buffers of drained tensors go back to a bounded pool and the next drains
+    of the same sizes reuse them (already faulted-in memory)."""
+    import time
+
+    import torch
+
+    from statespectre_b200 import in_process_daemon, offload_context
+
+    d = in_process_daemon(socket=sock_path, arena_mb=256, slot_mb=4, drain_on_complete=True)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cpu", rank=0) as off:
+            xs = [torch.randn(n) for n in (3 << 20, 5 << 20, 1000)]
+            for cycle in range(2):
+                hs = [off.copy(x, wait=True) for x in xs]
+                deadline = time.time() + 30
+                while time.time() < deadline and not all(h.location() == "pageable" for h in hs):
+                    time.sleep(0.005)
+                assert all(h.location() == "pageable" for h in hs)
+                for h, x in zip(hs, xs):
+                    assert torch.equal(h.restore(), x)
+                off.discard_batch(hs)
+                st = off.daemon_stats()
+                assert st["pageable_resident_bytes"] == 0
+                # 12 MiB + 20 MiB + one 2 MiB class are pooled, and stay pooled across cycles
+                assert st["pageable_pool_bytes"] == (12 + 20 + 2) << 20, (cycle, st["pageable_pool_bytes"])
+    finally:
+        d.stop()
