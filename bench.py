@@ -25,7 +25,6 @@ import argparse
 import json
 import os
 import sys
-import tempfile
 import threading
 import time
 

@@ -21,9 +21,9 @@ from __future__ import annotations
 
 import argparse
 import json
+import multiprocessing as mp
 import os
 import statistics
-import multiprocessing as mp
 import tempfile
 import time
 
