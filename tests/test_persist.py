@@ -152,3 +152,46 @@ def test_sealed_versions_survive_daemon_kill(tmp_path):
         assert data["w"] == v2["w"].numpy().tobytes()
     finally:
         d.stop()
+
+
+def test_persisted_version_outlives_trainer_and_damaged_files_are_skipped(tmp_path):
+    sock = str(tmp_path / "d.sock")
+    persist = str(tmp_path / "versions")
+    cfg = _config(tmp_path, sock, persist)
+    t1, t2 = torch.randn(5000), torch.randn(7000)
+    d = launch_daemon(sock, config=cfg, log_path=str(tmp_path / "d1.log"))
+    try:
+        with offload_context(daemon_addr=sock, device="cpu", rank=0, job_name="trainer") as off:
+            for v, t in ((1, t1), (2, t2)):
+                off.canonical_evict(t.clone(), off.canonical_key(model_role=ROLL, model_version=v, param_name="w",
+                                                                 tensor=t))
+                off.promote_rollout_version(v)
+            job = {"job_id": off.job_id, "launch_epoch": off.launch_epoch, "job_name": off.job_name}
+            assert _wait_stat(d, "versions_persisted_total", 2)
+        # the trainer's session is gone; the persisted versions stay pullable
+        _, data, latest = _pull_all(sock, job, 1)
+        assert latest == 2 and data["w"] == t1.numpy().tobytes()
+    finally:
+        d.stop()
+    # damage version 1's storage file: only version 1 is skipped at recovery
+    jd = os.path.join(persist, os.listdir(persist)[0])
+    import struct
+
+    # the storage of version 1 is the file whose header records t1's size
+    for f in [f for f in os.listdir(jd) if f.endswith(".obj")]:
+        with open(os.path.join(jd, f), "r+b") as fh:
+            _magic, _fmt, _sid, nbytes = struct.unpack("<IIQQ", fh.read(24))
+            if nbytes == t1.numel() * 4:
+                fh.seek(0)
+                fh.write(b"XXXX")  # bad magic
+    d = launch_daemon(sock, config=cfg, log_path=str(tmp_path / "d2.log"))
+    try:
+        assert d.stats()["versions_recovered_total"] == 1
+        _, data, latest = _pull_all(sock, job, 2)
+        assert latest == 2 and data["w"] == t2.numpy().tobytes()
+        c = RolloutWeightClient(sock, job["job_id"], job["launch_epoch"], job_name=job["job_name"])
+        with pytest.raises(IOError):
+            c.get_manifest(1)
+        c.close()
+    finally:
+        d.stop()
