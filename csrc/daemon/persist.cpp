@@ -230,7 +230,10 @@ void Daemon::enqueue_persist(const VersionKey& vk) {
     persist_cv_.notify_one();
 }
 
+// A version whose objects are moving between tiers is retried after the
+// others (every 10 ms, for up to about a minute) instead of being dropped.
 void Daemon::persist_loop() {
+    std::map<VersionKey, int> attempts;
     while (workers_on_.load()) {
         VersionKey vk;
         {
@@ -241,12 +244,16 @@ void Daemon::persist_loop() {
             vk = persist_queue_.front();
             persist_queue_.pop_front();
         }
-        int rc = 0;
-        for (int attempt = 0; attempt < 200 && workers_on_.load(); ++attempt) {
-            rc = persist_version(vk);
-            if (rc != 0) break;
-            sleep_us(10000);  // an object is moving between tiers; try again shortly
+        const int rc = persist_version(vk);
+        if (rc == 0 && ++attempts[vk] < 6000) {
+            {
+                std::lock_guard<std::mutex> g(persist_mu_);
+                persist_queue_.push_back(vk);
+            }
+            sleep_us(10000);
+            continue;
         }
+        attempts.erase(vk);
         if (rc <= 0)
             LOG_WARN(TAG, "version job=%llu role=%u v=%llu not persisted", (unsigned long long)vk.job.job_id,
                      vk.role, (unsigned long long)vk.version);
