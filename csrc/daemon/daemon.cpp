@@ -611,6 +611,7 @@ void Daemon::apply_ring_entry(uint32_t rank, uint64_t epoch, const ofld_completi
 // request, so the request sees its own earlier transfers without waiting for
 // the poller.
 void Daemon::drain_rings() {
+    if (rings_paused_.load()) return;
     for (uint32_t i = 0; i < ring_max_; ++i) {
         if (ring_owner_[i] == 0xFFFFFFFFu) continue;
         RingHeader* r = ring_at(control_, i);
@@ -624,6 +625,10 @@ void Daemon::ring_loop() {
     const uint64_t idle_us = cfg_.ring_poll_us ? cfg_.ring_poll_us : 50;
     while (workers_on_.load()) {
         bool any = false;
+        if (rings_paused_.load()) {
+            sleep_us(idle_us);
+            continue;
+        }
         {
             std::lock_guard<std::mutex> g(mu_);
             for (uint32_t i = 0; i < ring_max_; ++i) {

@@ -141,6 +141,9 @@ class Daemon {
         fail_writes_.store(writes);
         fail_reads_.store(reads);
     }
+    // Test hook: stop (and resume) consuming the ranks' completion rings, so
+    // a test can fill a ring and watch the agents fall back to RPCs.
+    void pause_rings(bool paused) { rings_paused_.store(paused); }
 
  private:
     // ---------------- memory ----------------
@@ -348,6 +351,7 @@ class Daemon {
     std::string persist_job_dir(const JobUID& uid) const;
     void unlink_persisted_manifest(const VersionKey& vk);    // mu_ held
     void forget_persisted_storage(uint64_t tid);             // mu_ held
+    std::atomic<bool> rings_paused_{false};
     std::mutex persist_mu_;
     std::condition_variable persist_cv_;
     std::deque<VersionKey> persist_queue_;

@@ -124,6 +124,9 @@ class DaemonThread {
     void inject_io_failures(int w, int r) {
         if (d_) d_->inject_io_failures(w, r);
     }
+    void pause_rings(bool p) {
+        if (d_) d_->pause_rings(p);
+    }
     std::string socket() const { return d_ ? d_->config().socket_path : ""; }
 
  private:
@@ -461,6 +464,7 @@ PYBIND11_MODULE(_C, m) {
         .def(py::init([](py::kwargs kw) { return new DaemonThread(config_from(kw)); }))
         .def("stop", &DaemonThread::stop)
         .def("inject_io_failures", &DaemonThread::inject_io_failures)
+        .def("pause_rings", &DaemonThread::pause_rings)
         .def_property_readonly("socket", &DaemonThread::socket);
 
     py::class_<RawConn>(m, "RawConn")

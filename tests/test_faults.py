@@ -182,3 +182,48 @@ def test_exhaustion_blocks_instead_of_overlapping(sock_path):
         assert len(granted) == len(set(granted)) == r.num_slots
     finally:
         d.stop()
+
+
+def test_full_completion_ring_falls_back_to_rpc(tmp_path):
+    """With the daemon not consuming a 4-entry completion ring, completions
+    that do not fit go by RPC: no completion is lost, the RPC-completed
+    tensors are usable at once, the ring-held ones as soon as it drains."""
+    import time
+
+    sock = str(tmp_path / "d.sock")
+    text = f"""
+daemon:
+  socket_path: {sock}
+  completion_ring_capacity: 4
+arenas:
+  allocation_granularity_mb: 1
+  per_numa:
+    - numa_node: 0
+      size_mb: 64
+drain_policy:
+  drain_on_d2h_complete: false
+"""
+    d = in_process_daemon(yaml=text, socket=sock)
+    try:
+        with offload_context(daemon_addr=sock, device="cpu", rank=0) as off:
+            d.pause_rings(True)
+            ts = [torch.full((1024,), float(i)) for i in range(8)]
+            hs = [off.copy(t, wait=True) for t in ts]
+            st = off.daemon_stats()
+            assert st["ring_completions_applied_total"] == 0
+            locs = [h.location() for h in hs]
+            assert locs[4:] == ["pinned"] * 4, locs     # completed over RPC (ring full)
+            assert all(loc != "pinned" for loc in locs[:4]), locs  # still in the paused ring
+            for h, t in zip(hs[4:], ts[4:]):
+                assert torch.equal(h.restore(), t)
+            d.pause_rings(False)
+            deadline = time.time() + 10
+            while time.time() < deadline and off.daemon_stats()["ring_completions_applied_total"] < 4:
+                time.sleep(0.01)
+            assert all(h.location() == "pinned" for h in hs)
+            for h, t in zip(hs, ts):
+                assert torch.equal(h.restore(), t)
+            off.discard_batch(hs)
+            assert off.daemon_stats()["used_slots"] == 0
+    finally:
+        d.stop()
