@@ -300,6 +300,15 @@ RequestCanonicalEvictResponse Daemon::on_canonical_evict(const RequestCanonicalE
         resp.message = "missing and create disabled";
         return resp;
     }
+    {
+        const Job& j = jobs_[juid];
+        if (j.max_inflight_d2h && j.inflight_d2h_bytes + r.key.nbytes > j.max_inflight_d2h) {
+            Metrics::get().inc(M::kQuotaRejections);
+            resp.action = ATTACH_ACTION_QUOTA_EXCEEDED;
+            resp.message = "inflight D2H quota exceeded";
+            return resp;
+        }
+    }
     uint64_t oid = next_object_++;
     uint64_t syn = canonical_tid(oid);
     uint64_t lid;
@@ -338,10 +347,12 @@ RequestCanonicalEvictResponse Daemon::on_canonical_evict(const RequestCanonicalE
     o.base_slot = base;
     o.slot_count = slots_for(r.key.nbytes);
     o.created_ns = o.last_access_ns = real_ns();
+    o.d2h_counted = true;
     objects_[oid] = o;
     storage_[syn].objects = 1;
     object_by_key_[ks] = oid;
     jobs_[juid].object_count++;
+    jobs_[juid].inflight_d2h_bytes += o.nbytes;
     resp.ok = true;
     resp.action = ATTACH_ACTION_NEED_D2H_CREATE;
     resp.object_id = oid;
@@ -382,6 +393,7 @@ CommitCanonicalObjectResponse Daemon::on_commit_canonical(const CommitCanonicalO
         }
         o->hash_lo = r.content_hash_lo;
         o->hash_hi = r.content_hash_hi;
+        settle_d2h(*o);
         o->state = lit->second.kind == OFLD_LOC_PAGEABLE ? OBJ_VALID_PAGEABLE
                    : lit->second.kind == OFLD_LOC_NVME   ? OBJ_VALID_NVME
                                                          : OBJ_VALID_PINNED;
@@ -454,8 +466,15 @@ bool Daemon::storage_busy(uint64_t tid) const {
     return it != storage_.end() && it->second.io > 0;
 }
 
+void Daemon::settle_d2h(CanonicalObject& o) {
+    if (!o.d2h_counted) return;
+    o.d2h_counted = false;
+    if (Job* j = find_job(o.key.job)) j->inflight_d2h_bytes -= std::min(j->inflight_d2h_bytes, o.nbytes);
+}
+
 bool Daemon::release_object(CanonicalObject& o) {
     if (o.export_refs || o.restore_refs) return false;
+    settle_d2h(o);
     const uint64_t oid = o.object_id, nbytes = o.nbytes;
     // Storage shared with carried-forward objects stays until its last user goes.
     auto sit = storage_.find(o.synthetic_tid);
@@ -472,7 +491,16 @@ bool Daemon::release_object(CanonicalObject& o) {
     if (sit != storage_.end()) storage_.erase(sit);
     forget_persisted_storage(o.synthetic_tid);  // the last object of a durable storage
     auto lit = locations_.find(o.synthetic_tid);
+    // pinned bytes were counted at reservation and leave the count at a drain
+    const bool counted_pinned = lit != locations_.end() ? lit->second.kind == OFLD_LOC_PINNED
+                                                         : (o.state == OBJ_CREATING || o.state == OBJ_ERROR);
     if (lit != locations_.end()) {
+        if (Job* j = find_job(o.key.job)) {  // the job's tier accounting follows the bytes out
+            auto cit = lit->second.cold_ref ? cold_.find(lit->second.cold_ref) : cold_.end();
+            if (cit != cold_.end() && !cit->second.persisted)
+                (cit->second.kind == OFLD_LOC_NVME ? j->nvme_bytes : j->pageable_bytes) -=
+                    std::min(cit->second.kind == OFLD_LOC_NVME ? j->nvme_bytes : j->pageable_bytes, nbytes);
+        }
         if (lit->second.kind == OFLD_LOC_PINNED) {
             uint32_t s = lit->second.slot;
             uint32_t st = state_of(s);
@@ -494,7 +522,7 @@ bool Daemon::release_object(CanonicalObject& o) {
     auto kit = object_by_key_.find(o.key_str);
     if (kit != object_by_key_.end() && kit->second == oid) object_by_key_.erase(kit);
     if (Job* j = find_job(o.key.job)) {
-        j->pinned_bytes -= std::min(j->pinned_bytes, nbytes);
+        if (counted_pinned) j->pinned_bytes -= std::min(j->pinned_bytes, nbytes);
         if (j->object_count) j->object_count--;
     }
     Metrics::get().inc(M::kCanonicalObjectsDropped);

@@ -470,6 +470,7 @@ void Daemon::recover_session(Session& s, const char* why) {
             if (is_canonical_tid(L.tensor_id) && !is_candidate_tid(L.tensor_id)) {
                 CanonicalObject* o = find_object(L.tensor_id & ~kCanonicalTidBit);
                 if (o && o->state == OBJ_CREATING) {
+                    settle_d2h(*o);
                     object_by_key_.erase(o->key_str);
                     o->state = OBJ_ERROR;
                 }

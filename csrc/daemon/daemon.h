@@ -98,6 +98,7 @@ struct CanonicalObject {
     uint64_t lease_id = 0;
     uint32_t base_slot = 0xFFFFFFFFu, slot_count = 0;
     CanonicalObjectState state_before_export = OBJ_SEALED;
+    bool d2h_counted = false;  // counted in the job's inflight_d2h_bytes until its copy settles
     uint64_t created_ns = 0, sealed_ns = 0, last_access_ns = 0;
 };
 
@@ -276,6 +277,7 @@ class Daemon {
     // canonical.cpp
     RegisterJobResponse on_register_job(const RegisterJobRequest& r);
     void init_job_quotas(Job& j) const;
+    void settle_d2h(CanonicalObject& o);  // mu_ held: the creating copy is no longer in flight
     RequestCanonicalEvictResponse on_canonical_evict(const RequestCanonicalEvictRequest& r);
     CommitCanonicalObjectResponse on_commit_canonical(const CommitCanonicalObjectRequest& r);
     ReleaseCanonicalResponse on_release_canonical(const ReleaseCanonicalRequest& r);
@@ -362,7 +364,10 @@ class Daemon {
     void enqueue_drain(const Lease& L);
     bool force_drain_one(std::unique_lock<std::mutex>& lk);
     void pressure_drain();
-    bool write_cold(const char* src, uint64_t nbytes, ColdEntry* out, bool allow_pageable);
+    bool write_cold(const char* src, uint64_t nbytes, ColdEntry* out, bool allow_pageable, bool allow_nvme = true);
+    // Cold tiers a drain of `tid` may use under its job's pageable / NVMe
+    // quotas (both true for non-canonical tensors). mu_ held.
+    void cold_quota(uint64_t tid, uint64_t nbytes, bool* allow_pageable, bool* allow_nvme);
     bool read_cold(const ColdEntry& c, char* dst, uint64_t off, uint64_t nbytes);
     void free_cold(uint64_t cold_ref);
     uint64_t commit_cold(ColdEntry&& c);

@@ -91,7 +91,17 @@ void Daemon::copy_bytes(char* dst, const char* src, uint64_t n) const {
     for (auto& t : ts) t.join();
 }
 
-bool Daemon::write_cold(const char* src, uint64_t nbytes, ColdEntry* out, bool allow_pageable) {
+void Daemon::cold_quota(uint64_t tid, uint64_t nbytes, bool* allow_pageable, bool* allow_nvme) {
+    *allow_pageable = *allow_nvme = true;
+    if (!is_canonical_tid(tid) || is_candidate_tid(tid)) return;
+    CanonicalObject* o = find_object(tid & ~kCanonicalTidBit);
+    Job* j = o ? find_job(o->key.job) : nullptr;
+    if (!j) return;
+    *allow_pageable = !j->max_pageable || j->pageable_bytes + nbytes <= j->max_pageable;
+    *allow_nvme = !j->max_nvme || j->nvme_bytes + nbytes <= j->max_nvme;
+}
+
+bool Daemon::write_cold(const char* src, uint64_t nbytes, ColdEntry* out, bool allow_pageable, bool allow_nvme) {
     out->nbytes = nbytes;
     if (fail_writes_.load() > 0 && fail_writes_.fetch_sub(1) > 0) {
         LOG_WARN(TAG, "injected cold write failure");
@@ -126,7 +136,7 @@ bool Daemon::write_cold(const char* src, uint64_t nbytes, ColdEntry* out, bool a
         LOG_WARN(TAG, "pageable allocation of %llu bytes failed", (unsigned long long)nbytes);
         if (!cfg_.nvme_enabled) return false;
     }
-    if (!cfg_.nvme_enabled) return false;
+    if (!cfg_.nvme_enabled || !allow_nvme) return false;
     if (!nvme_write(src, nbytes, &out->extents)) return false;
     out->kind = OFLD_LOC_NVME;
     Metrics::get().add(M::kNvmeWriteBytes, nbytes);
@@ -289,7 +299,9 @@ void Daemon::finish_drain(uint32_t base, uint32_t count, uint64_t tid, uint64_t 
     if (storage_busy(tid) || (o && (o->export_refs || o->restore_refs))) {
         set_run_state(base, count, OFLD_SLOT_PINNED_VALID);
         set_location(tid, ver, OFLD_LOC_PINNED, base, ref, nbytes);
-        if (o->state == OBJ_VALID_PINNED) o->state = OBJ_VALID_MULTI_TIER;
+        // `o` is null when the storage outlived the object that created it
+        // (carried-forward objects still read it)
+        if (o && o->state == OBJ_VALID_PINNED) o->state = OBJ_VALID_MULTI_TIER;
         note_drainable(lid);
         return;
     }
@@ -325,8 +337,11 @@ bool Daemon::force_drain_one(std::unique_lock<std::mutex>& lk) {
         }
         if (is_canonical_tid(L->tensor_id)) {
             CanonicalObject* o = find_object(L->tensor_id & ~kCanonicalTidBit);
+            bool cp = true, cn = true;
+            cold_quota(L->tensor_id, L->nbytes, &cp, &cn);
             if (is_candidate_tid(L->tensor_id) ||
-                (o && (o->restore_refs || o->export_refs || o->state == OBJ_CREATING))) {
+                (o && (o->restore_refs || o->export_refs || o->state == OBJ_CREATING)) ||
+                (!cp && !(cn && cfg_.nvme_enabled))) {
                 ++it;
                 continue;
             }
@@ -345,9 +360,11 @@ bool Daemon::force_drain_one(std::unique_lock<std::mutex>& lk) {
     if (!ref) {
         Metrics::get().add(M::kDrainingBytes, victim.nbytes);
         char* src = slot_ptr(victim.base);
+        bool allow_p = true, allow_n = true;
+        cold_quota(victim.tensor_id, victim.nbytes, &allow_p, &allow_n);
         lk.unlock();
         ColdEntry cold;
-        bool ok = write_cold(src, victim.nbytes, &cold, true);
+        bool ok = write_cold(src, victim.nbytes, &cold, allow_p, allow_n);
         lk.lock();
         Metrics::get().sub(M::kDrainingBytes, victim.nbytes);
         ref = ok ? commit_cold(std::move(cold)) : 0;
@@ -371,6 +388,7 @@ void Daemon::drain_loop() {
         uint64_t nbytes, tid, ver, lid, ref;
         uint32_t owner;
         char* src;
+        bool allow_p = true, allow_n = true;
         {
             std::lock_guard<std::mutex> g(mu_);
             if (state_of(job.base) != OFLD_SLOT_DRAIN_IN_FLIGHT) {
@@ -387,10 +405,20 @@ void Daemon::drain_loop() {
             owner = uint32_t(e.owner_rank);
             src = slot_ptr(job.base);
             ref = reusable_cold(tid, ver);
+            cold_quota(tid, nbytes, &allow_p, &allow_n);
+            if (!ref && !allow_p && !(allow_n && cfg_.nvme_enabled)) {
+                // the job is at its cold-tier quotas: the run stays pinned
+                set_run_state(job.base, job.count, OFLD_SLOT_PINNED_VALID);
+                Metrics::get().inc(M::kQuotaRejections);
+                Metrics::get().sub(M::kDrainingBytes, nbytes);
+                if (drains_pending_) --drains_pending_;
+                drained_cv_.notify_all();
+                continue;
+            }
         }
         Trace::get().event("DRAIN_STARTED", owner, 0, tid, ver, lid, job.base, nbytes);
         ColdEntry cold;
-        bool ok = ref != 0 || write_cold(src, nbytes, &cold, true);
+        bool ok = ref != 0 || write_cold(src, nbytes, &cold, allow_p, allow_n);
         std::lock_guard<std::mutex> g(mu_);
         Metrics::get().sub(M::kDrainingBytes, nbytes);
         if (!ref && ok) ref = commit_cold(std::move(cold));

@@ -349,3 +349,62 @@ def test_export_cancelled_when_receiver_disconnects(cdaemon):
         c.close()
         d = off.drop_canonical_version(ROLL, 1)
         assert d["dropped"] == 1 and d["skipped_inflight"] == 0
+
+
+def test_cold_tier_and_inflight_quotas(tmp_path):
+    """max_pageable_bytes sends a job's drains to NVMe once its pageable share
+    is used up; max_inflight_d2h_bytes caps what a job may copy at once; job
+    accounting follows the bytes out when objects are dropped."""
+    import time
+
+    sock = str(tmp_path / "q.sock")
+    text = f"""
+daemon:
+  socket_path: {sock}
+arenas:
+  allocation_granularity_mb: 1
+  per_numa:
+    - numa_node: 0
+      size_mb: 64
+drain_policy:
+  drain_on_d2h_complete: true
+nvme:
+  enabled: true
+  path: {tmp_path / "nvme"}
+  direct_io: false
+quotas:
+  per_job_overrides:
+    capped:
+      max_pageable_bytes: 6MiB
+    narrow:
+      max_inflight_d2h_bytes: 1MiB
+"""
+    d = in_process_daemon(yaml=text, socket=sock)
+    try:
+        with session(sock, 0, job="capped") as off:
+            hs = []
+            for i in range(3):  # 4 MiB each: the first fits the 6 MiB pageable quota, the others spill
+                t = torch.randn(1 << 20)
+                hs.append(off.canonical_evict(t, off.canonical_key(model_role=ROLL, model_version=1,
+                                                                   param_name=f"w{i}", tensor=t)))
+            deadline = time.time() + 10
+            while time.time() < deadline and off.job_stats()[0]["pageable_bytes"] < (4 << 20):
+                time.sleep(0.01)
+            time.sleep(0.2)
+            js = [j for j in off.job_stats() if j["job"]["job_name"] == "capped"][0]
+            assert js["pageable_bytes"] == 4 << 20 and js["nvme_bytes"] == 8 << 20, js
+            off.drop_canonical_version(ROLL, 1)
+            js = [j for j in off.job_stats() if j["job"]["job_name"] == "capped"][0]
+            assert js["pageable_bytes"] == 0 and js["nvme_bytes"] == 0 and js["pinned_bytes"] == 0, js
+        with session(sock, 1, job="narrow") as off:
+            t = torch.randn(1 << 20)  # 4 MiB > 1 MiB in flight
+            with pytest.raises(RuntimeError, match="QUOTA"):
+                off.canonical_evict(t, off.canonical_key(model_role=ROLL, model_version=1, param_name="w", tensor=t))
+            small = torch.randn(1000)
+            h = off.canonical_evict(small, off.canonical_key(model_role=ROLL, model_version=1, param_name="s",
+                                                             tensor=small))
+            assert h.did_d2h
+            js = [j for j in off.job_stats() if j["job"]["job_name"] == "narrow"][0]
+            assert js["inflight_d2h_bytes"] == 0  # settled at commit
+    finally:
+        d.stop()

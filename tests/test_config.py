@@ -214,6 +214,8 @@ nvlink:
 kernels:
   evict_ctas: 40
   timing: true
+nvme:
+  enabled: false
 """
     d = in_process_daemon(yaml=text, socket=sock)
     try:
@@ -264,6 +266,8 @@ cleanup:
 metrics:
   labels:
     cluster: b200
+nvme:
+  enabled: false
 """
     c = native().parse_config(text)
     assert c["job_quota_overrides"] == {"small": {"max_pinned_bytes": 1 << 20}}

@@ -202,6 +202,8 @@ arenas:
       size_mb: 64
 drain_policy:
   drain_on_d2h_complete: false
+nvme:
+  enabled: false
 """
     d = in_process_daemon(yaml=text, socket=sock)
     try:

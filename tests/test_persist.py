@@ -33,6 +33,8 @@ arenas:
 manifest:
   retain_sealed_versions: 0
   persist_dir: {persist}
+nvme:
+  enabled: false
 """)
     return str(cfg)
 

@@ -93,6 +93,8 @@ drain_policy:
   drain_on_d2h_complete: true
 manifest:
   persist_dir: {tmp_path / "versions"}
+nvme:
+  enabled: false
 """)
     d = launch_daemon(sock, config=str(cfg), log_path=log, env=env, binary=f"offloadd_{variant}")
     try:
