@@ -745,6 +745,10 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
 // and the stream is waited on once; then the batch is reserved and launched
 // in groups of about batch_group_bytes, each group one K1 launch, so the
 // daemon round trip of group g+1 overlaps the PCIe copy of group g.
+// Items the daemon answers as blocked (pinned window full) are retried for
+// up to blocked_wait_ms, after the groups already launched have had their
+// completions handed on: a pinned run becomes drainable only once its copy
+// is published, so the retry never waits on the batch's own reservations.
 std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait) {
     NvtxRange nvtx_("ofld.evict_batch");
     Impl& D = *d_;
@@ -784,107 +788,123 @@ std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items,
     std::vector<Impl::Pending> launched;
     cudaEvent_t last_ev = nullptr;
     const uint64_t group_bytes = std::max<uint64_t>(D.opt.batch_group_bytes, 1);
-    for (size_t g0 = 0; g0 < items.size();) {
-        size_t g1 = g0;
-        uint64_t bytes = 0;
-        while (g1 < items.size() && (g1 == g0 || bytes < group_bytes)) bytes += items[g1++].nbytes;
-        BatchRequestOffloadRequest br;
-        br.rank_id = D.opt.rank_id;
-        br.rank_epoch = D.epoch;
-        for (size_t i = g0; i < g1; ++i) {
-            const BatchItem& it = items[i];
-            RequestOffloadRequest rq;
-            rq.tensor_id = it.tensor_id;
-            rq.version = it.version;
-            rq.nbytes = it.nbytes;
-            rq.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
-            rq.numa_node = uint32_t(D.numa);
-            rq.alignment = 256;
-            rq.flags = OFLD_FLAG_ALLOW_OVERFLOW | OFLD_FLAG_SUBMIT_ON_GRANT | (z[i] ? OFLD_FLAG_FORMAT_ZBF16 : 0);
-            br.items.push_back(rq);
-        }
-        BatchRequestOffloadResponse resp = D.call<Op::kBatchRequestOffload>(br);
-        std::vector<kern::XferJob> jobs;  // this group's items on the job kernel, one K1 launch
-        const size_t first = launched.size();
-        uint64_t total_chunks = 0;
-        for (size_t i = g0; i < g1; ++i) {
-            EvictTicket& t = out[i];
-            t.tensor_id = items[i].tensor_id;
-            t.version = items[i].version;
-            t.nbytes = items[i].nbytes;
-            if (i - g0 >= resp.grants.size()) {
-                t.message = resp.message.empty() ? "no grant" : resp.message;
-                continue;
+    std::vector<size_t> todo(items.size()), blocked;
+    for (size_t i = 0; i < items.size(); ++i) todo[i] = i;
+    const uint64_t blocked_deadline = mono_ns() + D.opt.blocked_wait_ms * 1000000ull;
+    uint64_t backoff_us = 200;
+    for (;;) {
+        blocked.clear();
+        for (size_t g0 = 0; g0 < todo.size();) {
+            size_t g1 = g0;
+            uint64_t bytes = 0;
+            while (g1 < todo.size() && (g1 == g0 || bytes < group_bytes)) bytes += items[todo[g1++]].nbytes;
+            BatchRequestOffloadRequest br;
+            br.rank_id = D.opt.rank_id;
+            br.rank_epoch = D.epoch;
+            for (size_t k = g0; k < g1; ++k) {
+                const size_t i = todo[k];
+                const BatchItem& it = items[i];
+                RequestOffloadRequest rq;
+                rq.tensor_id = it.tensor_id;
+                rq.version = it.version;
+                rq.nbytes = it.nbytes;
+                rq.gpu_id = D.gpu ? uint32_t(D.opt.device) : 0;
+                rq.numa_node = uint32_t(D.numa);
+                rq.alignment = 256;
+                rq.flags = OFLD_FLAG_ALLOW_OVERFLOW | OFLD_FLAG_SUBMIT_ON_GRANT | (z[i] ? OFLD_FLAG_FORMAT_ZBF16 : 0);
+                br.items.push_back(rq);
             }
-            const RequestOffloadResponse& g = resp.grants[i - g0];
-            if (!g.ok || g.blocked) {
-                t.message = g.ok ? "offload blocked (pinned pressure)" : g.message;
-                continue;
-            }
-            char *host = nullptr, *dev = nullptr;
-            D.resolve(g.arena_id, g.arena_offset, items[i].nbytes, &host, &dev);
-            Impl::Pending p;
-            p.z = z[i] != 0;
-            p.zb = zb[i];
-            zb[i] = PinnedPool::Buf{};
-            t.coded = p.z;
-            p.lease = g.lease_id;
-            p.tid = items[i].tensor_id;
-            p.ver = items[i].version;
-            p.slot = g.slot_id;
-            p.nbytes = items[i].nbytes;
-            D.inflight_d2h += p.nbytes;
-            ++D.evicts;
-            {
-                std::lock_guard<std::mutex> lg(D.tab_mu);
-                D.tensors[{p.tid, p.ver}].offloaded = false;
-            }
-            if (D.batch_kernel_ok(items[i].ptr, p.nbytes)) {
-                kern::XferJob j{};
-                j.src = reinterpret_cast<const void*>(items[i].ptr);
-                j.dst = dev;
-                j.nbytes = p.nbytes;
-                j.chunk_begin = total_chunks;
-                j.ebase = p.z ? static_cast<const uint8_t*>(p.zb.dev) : nullptr;
-                if (D.opt.hash_on_evict) {
-                    p.ndig = kern::digest_count(p.nbytes);
-                    p.dig = D.pool.get(std::max<uint64_t>(p.ndig, 1) * 8);
-                    j.digests = static_cast<uint64_t*>(p.dig.dev);
+            BatchRequestOffloadResponse resp = D.call<Op::kBatchRequestOffload>(br);
+            std::vector<kern::XferJob> jobs;  // this group's items on the job kernel, one K1 launch
+            const size_t first = launched.size();
+            uint64_t total_chunks = 0;
+            for (size_t k = g0; k < g1; ++k) {
+                const size_t i = todo[k];
+                EvictTicket& t = out[i];
+                t.tensor_id = items[i].tensor_id;
+                t.version = items[i].version;
+                t.nbytes = items[i].nbytes;
+                if (k - g0 >= resp.grants.size()) {
+                    t.message = resp.message.empty() ? "no grant" : resp.message;
+                    continue;
                 }
-                total_chunks += kern::digest_count(p.nbytes);
-                jobs.push_back(j);
-            } else {
-                D.launch_d2h(p, items[i].ptr, host, dev, s, D.opt.hash_on_evict);
-                if (p.ev) last_ev = p.ev;
-            }
-            t.ok = true;
-            t.lease_id = g.lease_id;
-            t.slot_id = g.slot_id;
-            launched.push_back(std::move(p));
-        }
-        if (!jobs.empty()) {
-            PinnedPool::Buf tab = D.pool.get(jobs.size() * sizeof(kern::XferJob));
-            std::memcpy(tab.host, jobs.data(), jobs.size() * sizeof(kern::XferJob));
-            CUDA_OK(kern::evict_jobs(static_cast<const kern::XferJob*>(tab.dev), int(jobs.size()), total_chunks, s,
-                                     D.opt.evict_ctas));
-            cudaEvent_t ev;
-            CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-            CUDA_OK(cudaEventRecord(ev, s));
-            auto keep = D.make_batch_keep(ev, tab);
-            for (size_t k = first; k < launched.size(); ++k)
-                if (!launched[k].ev) {
-                    launched[k].ev = ev;
-                    launched[k].batch_keep = keep;
+                const RequestOffloadResponse& g = resp.grants[k - g0];
+                if (!g.ok || g.blocked) {
+                    t.message = g.ok ? "offload blocked (pinned pressure)" : g.message;
+                    if (g.blocked) blocked.push_back(i);
+                    continue;
                 }
-            last_ev = ev;
+                char *host = nullptr, *dev = nullptr;
+                D.resolve(g.arena_id, g.arena_offset, items[i].nbytes, &host, &dev);
+                Impl::Pending p;
+                p.z = z[i] != 0;
+                p.zb = zb[i];
+                zb[i] = PinnedPool::Buf{};
+                t.coded = p.z;
+                p.lease = g.lease_id;
+                p.tid = items[i].tensor_id;
+                p.ver = items[i].version;
+                p.slot = g.slot_id;
+                p.nbytes = items[i].nbytes;
+                D.inflight_d2h += p.nbytes;
+                ++D.evicts;
+                {
+                    std::lock_guard<std::mutex> lg(D.tab_mu);
+                    D.tensors[{p.tid, p.ver}].offloaded = false;
+                }
+                if (D.batch_kernel_ok(items[i].ptr, p.nbytes)) {
+                    kern::XferJob j{};
+                    j.src = reinterpret_cast<const void*>(items[i].ptr);
+                    j.dst = dev;
+                    j.nbytes = p.nbytes;
+                    j.chunk_begin = total_chunks;
+                    j.ebase = p.z ? static_cast<const uint8_t*>(p.zb.dev) : nullptr;
+                    if (D.opt.hash_on_evict) {
+                        p.ndig = kern::digest_count(p.nbytes);
+                        p.dig = D.pool.get(std::max<uint64_t>(p.ndig, 1) * 8);
+                        j.digests = static_cast<uint64_t*>(p.dig.dev);
+                    }
+                    total_chunks += kern::digest_count(p.nbytes);
+                    jobs.push_back(j);
+                } else {
+                    D.launch_d2h(p, items[i].ptr, host, dev, s, D.opt.hash_on_evict);
+                    if (p.ev) last_ev = p.ev;
+                }
+                t.ok = true;
+                t.lease_id = g.lease_id;
+                t.slot_id = g.slot_id;
+                launched.push_back(std::move(p));
+            }
+            if (!jobs.empty()) {
+                PinnedPool::Buf tab = D.pool.get(jobs.size() * sizeof(kern::XferJob));
+                std::memcpy(tab.host, jobs.data(), jobs.size() * sizeof(kern::XferJob));
+                CUDA_OK(kern::evict_jobs(static_cast<const kern::XferJob*>(tab.dev), int(jobs.size()), total_chunks, s,
+                                         D.opt.evict_ctas));
+                cudaEvent_t ev;
+                CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+                CUDA_OK(cudaEventRecord(ev, s));
+                auto keep = D.make_batch_keep(ev, tab);
+                for (size_t k = first; k < launched.size(); ++k)
+                    if (!launched[k].ev) {
+                        launched[k].ev = ev;
+                        launched[k].batch_keep = keep;
+                    }
+                last_ev = ev;
+            }
+            g0 = g1;
         }
-        g0 = g1;
+        // The last event recorded covers every launch so far on this stream, so a
+        // waiting caller synchronizes once per pass.
+        if (wait && D.gpu && last_ev) CUDA_OK(cudaEventSynchronize(last_ev));
+        for (Impl::Pending& p : launched) D.complete_or_queue(std::move(p), wait);
+        launched.clear();
+        last_ev = nullptr;
+        if (blocked.empty() || mono_ns() >= blocked_deadline) break;
+        sleep_us(backoff_us);
+        backoff_us = std::min<uint64_t>(backoff_us * 2, 20000);
+        todo.swap(blocked);
     }
     for (PinnedPool::Buf& b : zb) D.pool.put(b);  // items without a grant
-    // The last event recorded covers the whole batch on this stream, so a
-    // waiting caller synchronizes once.
-    if (wait && D.gpu && last_ev) CUDA_OK(cudaEventSynchronize(last_ev));
-    for (Impl::Pending& p : launched) D.complete_or_queue(std::move(p), wait);
     return out;
 }
 

@@ -61,8 +61,9 @@ struct AgentOptions {
     // One by default: on B200 hosts measured 140 ms/GiB with one thread and
     // 159 ms/GiB with eight (the driver serializes the pinning).
     int registration_threads = 1;
-    // How long evict() keeps retrying a reservation the daemon answers as
-    // blocked (pinned window full, nothing drainable yet) before failing.
+    // How long evict() and evict_batch() keep retrying a reservation the
+    // daemon answers as blocked (pinned window full, nothing drainable yet)
+    // before failing.
     uint64_t blocked_wait_ms = 10000;
 };
 

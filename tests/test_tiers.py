@@ -141,3 +141,24 @@ def test_pageable_pool_reuses_drained_buffers(sock_path):
                 assert st["pageable_pool_bytes"] == (12 + 20 + 2) << 20, (cycle, st["pageable_pool_bytes"])
     finally:
         d.stop()
+
+
+@pytest.mark.parametrize("drain_on_complete", [True, False])
+@pytest.mark.parametrize("wait", [True, False])
+def test_evict_batch_larger_than_pinned_window_waits_out_backpressure(sock_path, drain_on_complete, wait):
+    # 8 MiB window, 1 MiB slots, one batch of 24 x 1 MiB: the items past the
+    # window are answered blocked until the batch's own earlier copies are
+    # published and drained (in the background, or forced by the reservation).
+    d = in_process_daemon(socket=sock_path, arena_mb=8, slot_mb=1, drain_on_complete=drain_on_complete,
+                          thresholds=(0.99, 0.995, 0.999))
+    try:
+        with offload_context(daemon_addr=sock_path, device="cpu", rank=0) as off:
+            xs = [torch.randn(1 << 18) for _ in range(24)]
+            hs = off.evict_batch(xs, wait=wait)
+            s = off.daemon_stats()
+            assert s["blocked_reservation_count"] > 0 and s["drains_completed"] >= 16
+            for h, x in zip(hs, xs):
+                assert torch.equal(h.restore(), x)
+            off.discard_batch(hs)
+    finally:
+        d.stop()
