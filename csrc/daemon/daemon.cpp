@@ -165,7 +165,8 @@ void Daemon::build_control() {
     g->stride = ring_stride_;
     g->capacity = ring_cap_;
     for (uint32_t i = 0; i < ring_max_; ++i) {
-        RingHeader* r = ring_at(control_, i);
+        RingHeader* r = ring(i);
+        if (!r) break;
         r->capacity = ring_cap_;
         r->owner_rank = 0xFFFFFFFFu;
         r->rank_epoch = 0;
@@ -447,11 +448,11 @@ void Daemon::recover_session(Session& s, const char* why) {
     Metrics::get().inc(M::kRankSessionsInvalidated);
     LOG_WARN(TAG, "rank %u epoch %llu ended (%s)", s.rank_id, (unsigned long long)s.epoch, why);
     if (s.ring < ring_max_) {
-        RingHeader* r = ring_at(control_, s.ring);
+        RingHeader* r = ring(s.ring);
         ofld_completion_entry_t e;
         // Completions the rank published before dying are still valid.
         s.alive = true;
-        while (ring_pop(r, &e)) apply_ring_entry(s.rank_id, s.epoch, e);
+        while (r && ring_pop(r, ring_cap_, &e)) apply_ring_entry(s.rank_id, s.epoch, e);
         s.alive = false;
         r->owner_rank = 0xFFFFFFFFu;
         r->rank_epoch = 0;
@@ -527,7 +528,8 @@ RegisterRankResponse Daemon::on_register(const RegisterRankRequest& r, std::vect
     s.last_hb_ns = real_ns();
     for (uint32_t i = 0; i < ring_max_; ++i) {
         if (ring_owner_[i] != 0xFFFFFFFFu) continue;
-        RingHeader* rh = ring_at(control_, i);
+        RingHeader* rh = ring(i);
+        if (!rh) break;
         rh->head.store(0, std::memory_order_relaxed);
         rh->tail.store(0, std::memory_order_relaxed);
         rh->owner_rank = r.rank_id;
@@ -615,10 +617,10 @@ void Daemon::drain_rings() {
     if (rings_paused_.load()) return;
     for (uint32_t i = 0; i < ring_max_; ++i) {
         if (ring_owner_[i] == 0xFFFFFFFFu) continue;
-        RingHeader* r = ring_at(control_, i);
-        if (r->rank_epoch == 0) continue;
+        RingHeader* r = ring(i);
+        if (!r || r->rank_epoch == 0) continue;
         ofld_completion_entry_t e;
-        while (ring_pop(r, &e)) apply_ring_entry(r->owner_rank, r->rank_epoch, e);
+        while (ring_pop(r, ring_cap_, &e)) apply_ring_entry(r->owner_rank, r->rank_epoch, e);
     }
 }
 
@@ -634,10 +636,10 @@ void Daemon::ring_loop() {
             std::lock_guard<std::mutex> g(mu_);
             for (uint32_t i = 0; i < ring_max_; ++i) {
                 if (ring_owner_[i] == 0xFFFFFFFFu) continue;
-                RingHeader* r = ring_at(control_, i);
-                if (r->rank_epoch == 0) continue;
+                RingHeader* r = ring(i);
+                if (!r || r->rank_epoch == 0) continue;
                 ofld_completion_entry_t e;
-                for (int budget = 256; budget > 0 && ring_pop(r, &e); --budget) {
+                for (int budget = 256; budget > 0 && ring_pop(r, ring_cap_, &e); --budget) {
                     apply_ring_entry(r->owner_rank, r->rank_epoch, e);
                     any = true;
                 }
@@ -648,9 +650,9 @@ void Daemon::ring_loop() {
     std::lock_guard<std::mutex> g(mu_);
     for (uint32_t i = 0; i < ring_max_; ++i) {
         if (ring_owner_[i] == 0xFFFFFFFFu) continue;
-        RingHeader* r = ring_at(control_, i);
+        RingHeader* r = ring(i);
         ofld_completion_entry_t e;
-        while (r->rank_epoch && ring_pop(r, &e)) apply_ring_entry(r->owner_rank, r->rank_epoch, e);
+        while (r && r->rank_epoch && ring_pop(r, ring_cap_, &e)) apply_ring_entry(r->owner_rank, r->rank_epoch, e);
     }
 }
 

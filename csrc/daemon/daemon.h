@@ -360,6 +360,13 @@ class Daemon {
     std::unordered_map<uint64_t, std::string> persisted_files_;  // storage tid -> file (mu_)
     // Applies every completion already published in the rings. mu_ held.
     void drain_rings();
+    // Ring i of the control region, addressed from the daemon's own layout
+    // (the copy of the geometry in the shared header is writable by ranks).
+    RingHeader* ring(uint32_t i) const {
+        return i < ring_max_ ? reinterpret_cast<RingHeader*>(static_cast<char*>(control_) + layout_.ring_offset +
+                                                             uint64_t(i) * ring_stride_)
+                             : nullptr;
+    }
     void apply_ring_entry(uint32_t rank, uint64_t epoch, const ofld_completion_entry_t& e);
     void enqueue_drain(const Lease& L);
     bool force_drain_one(std::unique_lock<std::mutex>& lk);

@@ -105,13 +105,23 @@ inline bool ring_push(RingHeader* r, const ofld_completion_entry_t& e) {
     r->tail.store(t + 1, std::memory_order_release);
     return true;
 }
-// Consumer side (daemon). False when empty.
-inline bool ring_pop(RingHeader* r, ofld_completion_entry_t* out) {
+// Consumer side (daemon). False when empty. The header sits in memory the
+// producing rank maps writable, so the consumer indexes with the capacity it
+// laid the ring out with, and a tail more than a ring ahead of the head
+// (never written by a correct producer) discards the ring's contents rather
+// than reading entries that were never published.
+inline bool ring_pop(RingHeader* r, uint64_t capacity, ofld_completion_entry_t* out) {
     uint64_t h = r->head.load(std::memory_order_relaxed);
-    if (h == r->tail.load(std::memory_order_acquire)) return false;
-    *out = ring_entries(r)[h & (r->capacity - 1)];
+    const uint64_t t = r->tail.load(std::memory_order_acquire);
+    if (h == t) return false;
+    if (t - h > capacity) {
+        r->head.store(t, std::memory_order_release);
+        return false;
+    }
+    *out = ring_entries(r)[h & (capacity - 1)];
     r->head.store(h + 1, std::memory_order_release);
     return true;
 }
+inline bool ring_pop(RingHeader* r, ofld_completion_entry_t* out) { return ring_pop(r, r->capacity, out); }
 
 }  // namespace ofld

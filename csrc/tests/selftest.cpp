@@ -141,6 +141,14 @@ void layout_and_ring() {
     ofld_completion_entry_t o{};
     for (int i = 0; i < 8; ++i) CHECK(ring_pop(r, &o) && o.tensor_id == uint64_t(i));
     CHECK(!ring_pop(r, &o));
+    // A producer that scribbles over its header (capacity, a tail more than a
+    // ring ahead) cannot make the consumer read outside the ring or loop over
+    // entries that were never published.
+    CHECK(ring_push(r, e));
+    r->capacity = 1u << 30;
+    CHECK(ring_pop(r, 8, &o) && o.tensor_id == e.tensor_id);
+    r->tail.store(r->head.load() + 1000);
+    CHECK(!ring_pop(r, 8, &o) && r->head.load() == r->tail.load());
 }
 
 void hash_properties() {
