@@ -452,7 +452,7 @@ void Daemon::recover_session(Session& s, const char* why) {
         ofld_completion_entry_t e;
         // Completions the rank published before dying are still valid.
         s.alive = true;
-        while (r && ring_pop(r, ring_cap_, &e)) apply_ring_entry(s.rank_id, s.epoch, e);
+        while (ring_pop(r, ring_cap_, &e)) apply_ring_entry(s.rank_id, s.epoch, e);
         s.alive = false;
         r->owner_rank = 0xFFFFFFFFu;
         r->rank_epoch = 0;
@@ -616,12 +616,21 @@ void Daemon::apply_ring_entry(uint32_t rank, uint64_t epoch, const ofld_completi
 void Daemon::drain_rings() {
     if (rings_paused_.load()) return;
     for (uint32_t i = 0; i < ring_max_; ++i) {
-        if (ring_owner_[i] == 0xFFFFFFFFu) continue;
+        const Session* s = ring_session(i);
+        if (!s) continue;
+        const uint32_t rank = s->rank_id;
+        const uint64_t epoch = s->epoch;
         RingHeader* r = ring(i);
-        if (!r || r->rank_epoch == 0) continue;
         ofld_completion_entry_t e;
-        while (ring_pop(r, ring_cap_, &e)) apply_ring_entry(r->owner_rank, r->rank_epoch, e);
+        while (ring_pop(r, ring_cap_, &e)) apply_ring_entry(rank, epoch, e);
     }
+}
+
+const Daemon::Session* Daemon::ring_session(uint32_t i) const {
+    if (i >= ring_max_ || ring_owner_[i] == 0xFFFFFFFFu) return nullptr;
+    auto it = sessions_.find(ring_owner_[i]);
+    if (it == sessions_.end() || !it->second.alive || it->second.ring != i) return nullptr;
+    return &it->second;
 }
 
 void Daemon::ring_loop() {
@@ -635,12 +644,14 @@ void Daemon::ring_loop() {
         {
             std::lock_guard<std::mutex> g(mu_);
             for (uint32_t i = 0; i < ring_max_; ++i) {
-                if (ring_owner_[i] == 0xFFFFFFFFu) continue;
+                const Session* s = ring_session(i);
+                if (!s) continue;
+                const uint32_t rank = s->rank_id;
+                const uint64_t epoch = s->epoch;
                 RingHeader* r = ring(i);
-                if (!r || r->rank_epoch == 0) continue;
                 ofld_completion_entry_t e;
                 for (int budget = 256; budget > 0 && ring_pop(r, ring_cap_, &e); --budget) {
-                    apply_ring_entry(r->owner_rank, r->rank_epoch, e);
+                    apply_ring_entry(rank, epoch, e);
                     any = true;
                 }
             }
@@ -649,10 +660,13 @@ void Daemon::ring_loop() {
     }
     std::lock_guard<std::mutex> g(mu_);
     for (uint32_t i = 0; i < ring_max_; ++i) {
-        if (ring_owner_[i] == 0xFFFFFFFFu) continue;
+        const Session* s = ring_session(i);
+        if (!s) continue;
+        const uint32_t rank = s->rank_id;
+        const uint64_t epoch = s->epoch;
         RingHeader* r = ring(i);
         ofld_completion_entry_t e;
-        while (r && r->rank_epoch && ring_pop(r, ring_cap_, &e)) apply_ring_entry(r->owner_rank, r->rank_epoch, e);
+        while (ring_pop(r, ring_cap_, &e)) apply_ring_entry(rank, epoch, e);
     }
 }
 

@@ -367,6 +367,9 @@ class Daemon {
                                                              uint64_t(i) * ring_stride_)
                              : nullptr;
     }
+    // The live session the daemon assigned ring i to (never the owner and
+    // epoch copies in the ring header, which its rank can write), or null.
+    const Session* ring_session(uint32_t i) const;
     void apply_ring_entry(uint32_t rank, uint64_t epoch, const ofld_completion_entry_t& e);
     void enqueue_drain(const Lease& L);
     bool force_drain_one(std::unique_lock<std::mutex>& lk);

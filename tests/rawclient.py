@@ -4,24 +4,86 @@ It drives the slot state machine (reserve, mark submitted/complete, prefetch,
 release) without copying bytes, so daemon behaviour is testable on any host.
 """
 
+import mmap
 import os
+import socket
+import struct
 
 from statespectre_b200 import _wire
 from statespectre_b200._wire import Op
 
+# Control-region offsets of the v1 ABI: ofld_slot_table_header_t keeps
+# control_ring_offset at byte 72 and the ring geometry (max_ranks, stride,
+# capacity) in its reserved bytes from 80; a ring header holds capacity,
+# owner_rank and rank_epoch at 0/4/8, head at 64, tail at 128, and its 40-byte
+# completion entries (lease, tensor, version, slot, event, timestamp) from 192.
+_RING_OFFSET_AT = 72
+_GEOMETRY_AT = 80
+_ENTRY = struct.Struct("<QQQIIQ")
+
 
 class RawRank:
-    def __init__(self, sock_path: str, rank_id: int, pid: int | None = None, gpu: int = 0, numa: int = 0):
+    def __init__(self, sock_path: str, rank_id: int, pid: int | None = None, gpu: int = 0, numa: int = 0,
+                 map_control: bool = False):
         self.conn = _wire.Connection(sock_path)
         self.rank_id = rank_id
         self.gpu = gpu
         self.numa = numa
-        r = self.conn.call(Op.REGISTER_RANK, rank_id=rank_id, local_rank=rank_id, world_rank=rank_id, gpu_id=gpu,
-                           numa_node=numa, pid=pid if pid is not None else os.getpid() * 1000 + rank_id)
+        req = dict(rank_id=rank_id, local_rank=rank_id, world_rank=rank_id, gpu_id=gpu, numa_node=numa,
+                   pid=pid if pid is not None else os.getpid() * 1000 + rank_id)
+        self.control = None
+        if map_control:
+            r = self._register_with_fds(req)
+        else:
+            r = self.conn.call(Op.REGISTER_RANK, **req)
         assert r["ok"], r["message"]
         self.epoch = r["rank_epoch"]
         self.ring_index = r["ring_index"]
         self.num_slots = r["num_slots"]
+
+    def _register_with_fds(self, req: dict) -> dict:
+        """RegisterRank, keeping the descriptors that ride on the reply's frame
+        header, and map the control region read-write as an agent does."""
+        sock = self.conn.sock
+        sock.sendall(_wire.make_frame(Op.REGISTER_RANK, _wire.encode("RegisterRankRequest", req)))
+        head, fds, _, _ = socket.recv_fds(sock, _wire.FRAME_HEADER.size, 64)
+        if len(head) < _wire.FRAME_HEADER.size:
+            head += _wire.recv_exact(sock, _wire.FRAME_HEADER.size - len(head))
+        _op, _flags, n = _wire.parse_frame_header(head)
+        r = _wire.decode("RegisterRankResponse", _wire.recv_exact(sock, n))
+        try:
+            if r["ok"]:
+                self.control = mmap.mmap(fds[r["control_fd_index"]], r["control_size"])
+        finally:
+            for fd in fds:
+                os.close(fd)
+        return r
+
+    # ---- direct writes into this rank's completion ring (needs map_control) ----
+    def _ring(self) -> int:
+        base = struct.unpack_from("<Q", self.control, _RING_OFFSET_AT)[0]
+        _max_ranks, stride, _cap = struct.unpack_from("<III", self.control, _GEOMETRY_AT)
+        return base + self.ring_index * stride
+
+    def ring_capacity(self) -> int:
+        return struct.unpack_from("<III", self.control, _GEOMETRY_AT)[2]
+
+    def write_ring_header(self, owner_rank: int, rank_epoch: int, capacity: int) -> None:
+        struct.pack_into("<IIQ", self.control, self._ring(), capacity, owner_rank, rank_epoch)
+
+    def ring_head_tail(self) -> tuple:
+        r = self._ring()
+        return struct.unpack_from("<Q", self.control, r + 64)[0], struct.unpack_from("<Q", self.control, r + 128)[0]
+
+    def ring_push(self, lease, tid, ver, slot, event=1) -> None:
+        r = self._ring()
+        _head, tail = self.ring_head_tail()
+        at = r + 192 + (tail & (self.ring_capacity() - 1)) * _ENTRY.size
+        _ENTRY.pack_into(self.control, at, lease, tid, ver, slot, event, 1)
+        struct.pack_into("<Q", self.control, r + 128, tail + 1)
+
+    def set_ring_tail(self, tail: int) -> None:
+        struct.pack_into("<Q", self.control, self._ring() + 128, tail)
 
     def call(self, op, **kw):
         return self.conn.call(op, **kw)
@@ -68,4 +130,6 @@ class RawRank:
         return {e["key"]: e["value"] for e in r["stats"]}
 
     def close(self):
+        if self.control is not None:
+            self.control.close()
         self.conn.close()

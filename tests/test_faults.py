@@ -229,3 +229,41 @@ nvme:
             assert off.daemon_stats()["used_slots"] == 0
     finally:
         d.stop()
+
+
+def test_ring_header_written_by_a_rank_cannot_complete_another_ranks_transfer(sock_path):
+    """A rank maps the control region writable, its ring header included. One
+    that writes another rank's id and epoch there and publishes a completion
+    for that rank's lease is not believed: the daemon takes the ring's owner
+    from its own session table. A scribbled capacity or a tail far ahead of the
+    head costs that ring its entries, never a read outside it."""
+    d = in_process_daemon(socket=sock_path, arena_mb=16, slot_mb=1, drain_on_complete=False)
+    try:
+        victim = RawRank(sock_path, 1)
+        g = victim.reserve(77, 1, 4096)
+        assert g["ok"] and victim.mark(Op.MARK_D2H_SUBMITTED, g["lease_id"], 77, 1, g["slot_id"])["ok"]
+        atk = RawRank(sock_path, 2, map_control=True)
+        before = victim.stats()
+        atk.write_ring_header(owner_rank=1, rank_epoch=victim.epoch, capacity=1 << 30)
+        atk.ring_push(g["lease_id"], 77, 1, g["slot_id"])
+        deadline = time.time() + 10
+        while time.time() < deadline and atk.ring_head_tail()[0] != atk.ring_head_tail()[1]:
+            time.sleep(0.01)
+        assert atk.ring_head_tail()[0] == atk.ring_head_tail()[1]  # consumed
+        after = victim.stats()
+        assert after["lease_owner_mismatch_rejected"] == before["lease_owner_mismatch_rejected"] + 1
+        assert victim.location(77, 1)["location_kind"] != 2  # not completed by the impostor
+        assert victim.mark(Op.MARK_D2H_COMPLETE, g["lease_id"], 77, 1, g["slot_id"])["ok"]
+        assert victim.location(77, 1)["location_kind"] == 2
+        head, _ = atk.ring_head_tail()
+        atk.set_ring_tail(head + 10 ** 9)
+        deadline = time.time() + 10
+        while time.time() < deadline and atk.ring_head_tail()[0] != head + 10 ** 9:
+            time.sleep(0.01)
+        assert atk.ring_head_tail()[0] == head + 10 ** 9  # skipped in one step
+        assert victim.heartbeat()["ok"] and victim.stats()["ring_completions_applied_total"] == \
+            after["ring_completions_applied_total"]
+        atk.close()
+        victim.close()
+    finally:
+        d.stop()
