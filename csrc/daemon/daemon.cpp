@@ -158,7 +158,9 @@ void Daemon::build_control() {
         d[i].registration_granularity = arenas_[i].reg_gran;
         d[i].allocation_granularity = arenas_[i].alloc_gran;
     }
-    slots_ = slots_of(control_);
+    pub_slots_ = slots_of(control_);
+    slot_store_.reset(new ofld_slot_entry_t[std::max<uint32_t>(layout_.num_slots, 1)]());
+    slots_ = slot_store_.get();
 
     RingGeometry* g = ring_geometry(header_);
     g->max_ranks = ring_max_;
@@ -220,6 +222,7 @@ void Daemon::build_windows() {
         uint64_t rest = arena_slots - cursor / gran;
         if (rest) carve(kOverflowGpu, true, rest);
     }
+    for (uint32_t i = 0; i < layout_.num_slots; ++i) publish_slot(i);
     LOG_INFO(TAG, "slot plan: %zu windows, %u slots", windows_.size(), next);
 }
 

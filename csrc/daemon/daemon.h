@@ -223,6 +223,8 @@ class Daemon {
     void set_state(uint32_t slot, ofld_slot_state_t st);
     void set_run_state(uint32_t base, uint32_t count, ofld_slot_state_t st);
     uint32_t state_of(uint32_t slot) const;
+    void publish_slot(uint32_t slot);
+    void set_cold_ref(uint32_t base, uint32_t count, uint64_t ref);
     char* slot_ptr(uint32_t slot);
     uint32_t slots_for(uint64_t nbytes) const;
     double pinned_pressure() const;
@@ -404,7 +406,13 @@ class Daemon {
     char* control_ = nullptr;
     ControlLayout layout_{};
     ofld_slot_table_header_t* header_ = nullptr;
+    // The slot table. slots_ is the daemon's own copy, the one every decision
+    // and every copy address is taken from; pub_slots_ is the table in the
+    // shared control region, which ranks map writable and read (state,
+    // flags). Each state change publishes the whole entry, its state last.
+    std::unique_ptr<ofld_slot_entry_t[]> slot_store_;
     ofld_slot_entry_t* slots_ = nullptr;
+    ofld_slot_entry_t* pub_slots_ = nullptr;
     uint32_t ring_max_ = 0, ring_cap_ = 0, ring_stride_ = 0;
     std::vector<Window> windows_;
     std::vector<uint32_t> slot_window_;  // slot -> window index

@@ -462,7 +462,7 @@ RequestCanonicalRestoreResponse Daemon::on_canonical_restore(const RequestCanoni
             return resp;
         }
         set_run_state(base, count, OFLD_SLOT_PINNED_VALID);
-        for (uint32_t k = 0; k < count; ++k) slots_[base + k].cold_ref = cref;
+        set_cold_ref(base, count, cref);
         Location& loc = locations_[syn];
         loc.kind = OFLD_LOC_PINNED;
         loc.slot = base;

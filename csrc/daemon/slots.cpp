@@ -10,6 +10,7 @@
 // counted.
 #include <algorithm>
 #include <chrono>
+#include <cstddef>
 #include <cstring>
 
 #include "daemon.h"
@@ -87,12 +88,25 @@ int64_t find_free_run_best(const std::vector<uint64_t>& bm, uint32_t nbits, uint
 
 void Daemon::set_state(uint32_t s, ofld_slot_state_t st) {
     slots_[s].last_touch_ns = real_ns();
-    slots_[s].state.store(uint32_t(st), std::memory_order_release);
+    slots_[s].state.store(uint32_t(st), std::memory_order_relaxed);
+    publish_slot(s);
+}
+void Daemon::publish_slot(uint32_t s) {
+    constexpr size_t kBody = offsetof(ofld_slot_entry_t, slot_id);  // everything after the atomic state
+    std::memcpy(reinterpret_cast<char*>(&pub_slots_[s]) + kBody, reinterpret_cast<const char*>(&slots_[s]) + kBody,
+                sizeof(ofld_slot_entry_t) - kBody);
+    pub_slots_[s].state.store(slots_[s].state.load(std::memory_order_relaxed), std::memory_order_release);
+}
+void Daemon::set_cold_ref(uint32_t base, uint32_t count, uint64_t ref) {
+    for (uint32_t k = 0; k < count; ++k) {
+        slots_[base + k].cold_ref = ref;
+        publish_slot(base + k);
+    }
 }
 void Daemon::set_run_state(uint32_t base, uint32_t count, ofld_slot_state_t st) {
     for (uint32_t k = 0; k < count; ++k) set_state(base + k, st);
 }
-uint32_t Daemon::state_of(uint32_t s) const { return slots_[s].state.load(std::memory_order_acquire); }
+uint32_t Daemon::state_of(uint32_t s) const { return slots_[s].state.load(std::memory_order_relaxed); }
 char* Daemon::slot_ptr(uint32_t s) { return arenas_[slots_[s].arena_id].base + slots_[s].arena_offset; }
 uint32_t Daemon::slots_for(uint64_t nbytes) const {
     uint64_t n = (nbytes + cfg_.allocation_granularity_bytes - 1) / cfg_.allocation_granularity_bytes;
@@ -520,7 +534,7 @@ RequestPrefetchResponse Daemon::do_request_prefetch(const RequestPrefetchRequest
     uint64_t lid = new_lease(base, count, r.tensor_id, want, r.rank_id, r.rank_epoch, loc.nbytes, true);
     stamp_run(base, count, r.tensor_id, want, lid, r.rank_id, leases_[lid].owner_pid, r.rank_epoch,
               loc.nbytes, (r.flags & ~OFLD_FLAG_FORMAT_MASK) | loc.fmt, OFLD_SLOT_READBACK_IN_FLIGHT);
-    for (uint32_t k = 0; k < count; ++k) slots_[base + k].cold_ref = loc.cold_ref;
+    set_cold_ref(base, count, loc.cold_ref);
     {
         std::lock_guard<std::mutex> q(q_mu_);
         readback_q_.push_back(ReadbackJob{base, count, loc.cold_ref, loc.nbytes});

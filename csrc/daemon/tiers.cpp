@@ -293,7 +293,7 @@ void Daemon::finish_drain(uint32_t base, uint32_t count, uint64_t tid, uint64_t 
         return;
     }
     ofld_location_kind_t kind = cold_[ref].kind;
-    for (uint32_t k = 0; k < count; ++k) slots_[base + k].cold_ref = ref;
+    set_cold_ref(base, count, ref);
     CanonicalObject* o = nullptr;
     if (is_canonical_tid(tid) && !is_candidate_tid(tid)) o = find_object(tid & ~kCanonicalTidBit);
     if (storage_busy(tid) || (o && (o->export_refs || o->restore_refs))) {

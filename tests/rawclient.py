@@ -17,9 +17,13 @@ from statespectre_b200._wire import Op
 # capacity) in its reserved bytes from 80; a ring header holds capacity,
 # owner_rank and rank_epoch at 0/4/8, head at 64, tail at 128, and its 40-byte
 # completion entries (lease, tensor, version, slot, event, timestamp) from 192.
+_SLOTS_OFFSET_AT = 64
 _RING_OFFSET_AT = 72
 _GEOMETRY_AT = 80
 _ENTRY = struct.Struct("<QQQIIQ")
+# ofld_slot_entry_t: 256 bytes; arena_id at 16, arena_offset 24, nbytes 40,
+# tensor_id 48, lease_id 64.
+_SLOT_SIZE = 256
 
 
 class RawRank:
@@ -81,6 +85,20 @@ class RawRank:
         at = r + 192 + (tail & (self.ring_capacity() - 1)) * _ENTRY.size
         _ENTRY.pack_into(self.control, at, lease, tid, ver, slot, event, 1)
         struct.pack_into("<Q", self.control, r + 128, tail + 1)
+
+    def scribble_slot(self, slot: int, arena_id: int, arena_offset: int, nbytes: int) -> None:
+        """Overwrite where a slot entry says its bytes are, as a faulty rank could."""
+        at = struct.unpack_from("<Q", self.control, _SLOTS_OFFSET_AT)[0] + slot * _SLOT_SIZE
+        struct.pack_into("<QQ", self.control, at + 16, arena_id, arena_offset)
+        struct.pack_into("<Q", self.control, at + 40, nbytes)
+
+    def slot_fields(self, slot: int) -> tuple:
+        """(state, arena_id, arena_offset, nbytes, tensor_id) of a slot entry."""
+        at = struct.unpack_from("<Q", self.control, _SLOTS_OFFSET_AT)[0] + slot * _SLOT_SIZE
+        state = struct.unpack_from("<I", self.control, at)[0]
+        arena_id, off = struct.unpack_from("<QQ", self.control, at + 16)
+        return state, arena_id, off, struct.unpack_from("<Q", self.control, at + 40)[0], \
+            struct.unpack_from("<Q", self.control, at + 48)[0]
 
     def set_ring_tail(self, tail: int) -> None:
         struct.pack_into("<Q", self.control, self._ring() + 128, tail)

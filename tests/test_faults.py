@@ -267,3 +267,46 @@ def test_ring_header_written_by_a_rank_cannot_complete_another_ranks_transfer(so
         victim.close()
     finally:
         d.stop()
+
+
+def test_slot_entries_written_by_a_rank_do_not_steer_the_daemons_copies(tmp_path):
+    """The shared slot table is the daemon's published copy: it takes a run's
+    address and size from its own table, so a rank that rewrites another
+    tensor's entry (arena, offset, size) neither crashes the daemon's drain
+    nor changes the bytes that drain moves; the next state change republishes
+    the entry."""
+    sock = str(tmp_path / "d.sock")
+    cfg = tmp_path / "d.yaml"
+    cfg.write_text(f"""
+daemon:
+  socket_path: {sock}
+arenas:
+  allocation_granularity_mb: 1
+  per_numa:
+    - numa_node: 0
+      size_mb: 8
+drain_policy:
+  drain_on_d2h_complete: false
+nvme:
+  enabled: false
+""")
+    d = launch_daemon(sock, config=str(cfg), log_path=str(tmp_path / "d.log"))
+    try:
+        with offload_context(daemon_addr=sock, device="cpu", rank=0) as off:
+            x = torch.randn(1 << 18)  # 1 MiB: one slot
+            h = off.copy(x, wait=True)
+            atk = RawRank(sock, 5, map_control=True)
+            loc = atk.location(h.tensor_id, h.version)
+            assert loc["location_kind"] == 2
+            slot = loc["slot_id"]
+            atk.scribble_slot(slot, arena_id=999, arena_offset=1 << 50, nbytes=1 << 40)
+            # fill the 8 MiB window: the oldest run (x) is drained under pressure
+            hs = [off.copy(torch.randn(1 << 18), wait=True) for _ in range(10)]
+            assert off.daemon_stats()["drains_completed"] >= 3 and h.location() != "pinned"
+            assert torch.equal(h.restore(), x)
+            assert atk.slot_fields(slot)[1:4] != (999, 1 << 50, 1 << 40)  # republished
+            off.discard_batch(hs + [h])
+            atk.close()
+        assert d.proc.poll() is None  # the daemon is still serving
+    finally:
+        d.stop()
