@@ -724,7 +724,11 @@ class Off:
 
     def evict_batch(self, tensors: Sequence[torch.Tensor], stream=None, wait: bool = True,
                     versions: Optional[Sequence[int]] = None) -> List[OffloadHandle]:
-        """Non-destructive copy of many contiguous tensors with one reservation round trip."""
+        """Non-destructive copy of many contiguous tensors with one reservation round trip.
+
+        Items the daemon answers as blocked (pinned window full) are retried,
+        after the batch's earlier copies are published so they can drain, for
+        up to the session's ``blocked_wait_ms``."""
         tensors = list(tensors)
         if not tensors:
             return []
