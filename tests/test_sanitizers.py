@@ -131,3 +131,61 @@ nvme:
     text = open(log, errors="replace").read()
     assert _clean(text), text[-6000:]
     assert rc == 0, text[-3000:]
+
+
+def test_daemon_under_asan_with_a_rank_that_corrupts_shared_memory(sanitizer_builds, tmp_path):
+    """The ASan daemon serves a rank that rewrites its ring header (another
+    rank's identity, a huge capacity, a tail a billion entries ahead) and
+    another tensor's slot entry (arena, offset, size) while that tensor is
+    drained and read back: no sanitizer report, the bytes come back intact."""
+    from rawclient import RawRank
+
+    from statespectre_b200._wire import Op
+
+    sock = str(tmp_path / "d.sock")
+    log = str(tmp_path / "offloadd_asan.log")
+    env = dict(os.environ, ASAN_OPTIONS="detect_leaks=1:abort_on_error=0", UBSAN_OPTIONS="print_stacktrace=1")
+    cfg = tmp_path / "offloadd.yaml"
+    cfg.write_text(f"""
+daemon:
+  socket_path: {sock}
+arenas:
+  allocation_granularity_mb: 1
+  per_numa:
+    - numa_node: 0
+      size_mb: 8
+drain_policy:
+  drain_on_d2h_complete: false
+nvme:
+  enabled: false
+""")
+    d = launch_daemon(sock, config=str(cfg), log_path=log, env=env, binary="offloadd_asan")
+    try:
+        victim = RawRank(sock, 1)
+        g = victim.reserve(77, 1, 4096)
+        assert g["ok"] and victim.mark(Op.MARK_D2H_SUBMITTED, g["lease_id"], 77, 1, g["slot_id"])["ok"]
+        atk = RawRank(sock, 2, map_control=True)
+        atk.write_ring_header(owner_rank=1, rank_epoch=victim.epoch, capacity=1 << 30)
+        atk.ring_push(g["lease_id"], 77, 1, g["slot_id"])
+        head, _ = atk.ring_head_tail()
+        atk.set_ring_tail(head + 10 ** 9)
+        deadline = time.time() + 20
+        while time.time() < deadline and atk.ring_head_tail()[0] != head + 10 ** 9:
+            time.sleep(0.01)
+        assert atk.ring_head_tail()[0] == head + 10 ** 9
+        assert victim.mark(Op.MARK_D2H_COMPLETE, g["lease_id"], 77, 1, g["slot_id"])["ok"]
+        with offload_context(daemon_addr=sock, device="cpu", rank=0) as off:
+            x = torch.randn(1 << 18)
+            h = off.copy(x, wait=True)
+            slot = atk.location(h.tensor_id, h.version)["slot_id"]
+            atk.scribble_slot(slot, arena_id=999, arena_offset=1 << 50, nbytes=1 << 40)
+            hs = [off.copy(torch.randn(1 << 18), wait=True) for _ in range(10)]
+            assert torch.equal(h.restore(), x)
+            off.discard_batch(hs + [h])
+        atk.close()
+        victim.close()
+    finally:
+        rc = d.stop()
+    text = open(log, errors="replace").read()
+    assert _clean(text), text[-6000:]
+    assert rc == 0, text[-3000:]
