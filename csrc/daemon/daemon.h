@@ -455,6 +455,7 @@ class Daemon {
     // Queued drains not yet finished (mu_), and the signal a blocked
     // reservation waits on for one of them to free its pinned run.
     uint32_t drains_pending_ = 0;
+    uint64_t draining_slots_ = 0;  // slots of runs queued for or in a drain (still counted in used_slots_)
     std::condition_variable_any drained_cv_;
 
     std::vector<std::thread> workers_;

@@ -222,6 +222,7 @@ uint64_t Daemon::commit_cold(ColdEntry&& c) {
 void Daemon::enqueue_drain(const Lease& L) {
     set_run_state(L.base, L.count, OFLD_SLOT_DRAIN_IN_FLIGHT);
     ++drains_pending_;
+    draining_slots_ += L.count;
     {
         std::lock_guard<std::mutex> q(q_mu_);
         drain_q_.push_back(DrainJob{L.base, L.count});
@@ -233,7 +234,10 @@ void Daemon::enqueue_drain(const Lease& L) {
 
 // Under the normal/priority/aggressive thresholds, queue background drains of
 // the least recently touched pinned runs until pressure falls back under the
-// normal threshold. mu_ held.
+// normal threshold. Runs already queued for a drain count as gone: this runs
+// on every D2H completion, and a batch completes many runs before the first
+// drain frees its slots, so counting them again would drain the whole batch.
+// mu_ held.
 void Daemon::pressure_drain() {
     double p = pinned_pressure();
     if (p < cfg_.normal_threshold || layout_.num_slots == 0) return;
@@ -241,7 +245,8 @@ void Daemon::pressure_drain() {
                : p >= cfg_.priority_threshold ? M::kPressureDrainsPriority
                                               : M::kPressureDrainsNormal;
     uint64_t target = uint64_t(cfg_.normal_threshold * double(layout_.num_slots));
-    uint64_t projected = used_slots_;
+    uint64_t projected = used_slots_ > draining_slots_ ? used_slots_ - draining_slots_ : 0;
+    if (projected <= target) return;
     for (auto it = lru_.begin(); it != lru_.end() && projected > target;) {
         uint64_t lid = it->second;
         ++it;
@@ -394,6 +399,7 @@ void Daemon::drain_loop() {
             if (state_of(job.base) != OFLD_SLOT_DRAIN_IN_FLIGHT) {
                 Metrics::get().sub(M::kDrainingBytes, slots_[job.base].nbytes);
                 if (drains_pending_) --drains_pending_;
+                draining_slots_ -= std::min<uint64_t>(draining_slots_, job.count);
                 drained_cv_.notify_all();
                 continue;
             }
@@ -412,6 +418,7 @@ void Daemon::drain_loop() {
                 Metrics::get().inc(M::kQuotaRejections);
                 Metrics::get().sub(M::kDrainingBytes, nbytes);
                 if (drains_pending_) --drains_pending_;
+                draining_slots_ -= std::min<uint64_t>(draining_slots_, job.count);
                 drained_cv_.notify_all();
                 continue;
             }
@@ -424,6 +431,7 @@ void Daemon::drain_loop() {
         if (!ref && ok) ref = commit_cold(std::move(cold));
         finish_drain(job.base, job.count, tid, ver, lid, owner, nbytes, ref);
         if (drains_pending_) --drains_pending_;
+        draining_slots_ -= std::min<uint64_t>(draining_slots_, job.count);
         drained_cv_.notify_all();
     }
 }

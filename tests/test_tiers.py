@@ -162,3 +162,25 @@ def test_evict_batch_larger_than_pinned_window_waits_out_backpressure(sock_path,
             off.discard_batch(hs)
     finally:
         d.stop()
+
+
+def test_pressure_drains_stop_at_the_normal_threshold_during_a_batch(sock_path):
+    # 11 slots of 4 MiB, 8 blocks per batch: 73 % full after the batch, so
+    # pressure drains take it back to the 60 % normal threshold (2 runs), not
+    # every run that completes while earlier drains are still queued.
+    d = in_process_daemon(socket=sock_path, arena_mb=44, slot_mb=4, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cpu", rank=0) as off:
+            blocks = [torch.randn(1 << 20) for _ in range(16)]
+            for it in range(6):
+                sel = blocks[it % 2 * 8: it % 2 * 8 + 8]
+                hs = off.evict_batch(sel, wait=True)
+                outs = [torch.empty_like(b) for b in sel]
+                off.restore_batch(hs, outs)
+                assert all(torch.equal(o, b) for o, b in zip(outs, sel))
+                off.discard_batch(hs)
+            s = off.daemon_stats()
+            assert 1 <= s["drains_completed"] <= 3 * 6, s["drains_completed"]
+            assert s["readbacks_completed"] <= 3 * 6
+    finally:
+        d.stop()
