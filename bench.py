@@ -16,7 +16,7 @@ the cycle through the public API (destructive ``off.evict`` + ``h.restore()``
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--size-mb MB] [--matmul 0|1]
     torchrun --nproc-per-node N bench.py --gpus N ...
-    python bench.py --impl reference
+    python bench.py --impl reference      # the unmodified reference build, same workload
 """
 
 from __future__ import annotations
@@ -36,10 +36,21 @@ BASELINE_D2H_GBS = 53.6
 BASELINE_H2D_GBS = 57.5
 BASELINE_ROUNDTRIP_GBS = 2.0 / (1.0 / BASELINE_D2H_GBS + 1.0 / BASELINE_H2D_GBS)
 METRIC = "evict/restore GB/s per GPU at 1/2/4/8 B200; 32B weight-sync latency (ms)"
-REFERENCE_UNAVAILABLE = (
-    "reference cannot be installed offline: its source tree has neither setup.py nor pyproject.toml "
-    "(pip install fails) and its CMake build requires libnuma and liburing (numa.h, liburing.h), "
-    "which are absent from this image")
+
+
+def _reference_arm(args) -> int:
+    """The unmodified StateSpectre build (baseline/_ref) through its own API;
+    loaded by file path so nothing of this package is imported on that path."""
+    import importlib.util
+
+    path = os.path.join(ROOT, "baseline", "reference_bench.py")
+    spec = importlib.util.spec_from_file_location("reference_bench", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    if args.workload not in ("evict_restore",):
+        print(json.dumps(mod.unavailable(f"no reference arm for workload {args.workload}")), flush=True)
+        return 0
+    return mod.main(args, METRIC, BASELINE_ROUNDTRIP_GBS)
 
 
 def parse():
@@ -90,9 +101,7 @@ def parse():
 def main():
     args = parse()
     if args.impl == "reference":
-        line = {"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}
-        print(json.dumps(line), flush=True)
-        return 0
+        return _reference_arm(args)
 
     if args.workload != "evict_restore":
         if args.workload == "weight_sync":

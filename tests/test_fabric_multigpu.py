@@ -76,48 +76,60 @@ def test_push_across_gpus_and_verify_peer(two_gpus, sock_path, mode, transport):
     q_in, q_out = ctx.Queue(), ctx.Queue()
     child = ctx.Process(target=_rollout, args=(sock_path, mode, transport, q_in, q_out))
     child.start()
+    tr = None
     try:
         with offload_context(daemon_addr=sock_path, device="cuda:0", rank=0, job_name="fabric2") as off:
-            torch.manual_seed(0)
-            params = {n: (torch.randn(s, device="cuda:0") * 0.02).to(getattr(torch, dt)) for n, s, dt in _specs()}
-            tag, fp = q_out.get(timeout=TIMEOUT)
-            assert tag == "published"
-            tr = TrainerWeightSync(off, params, [f"rollout/{mode}/{transport}"], mode=mode, transport=transport)
-            assert tr.layout.fingerprint == fp
-            assert tr.transport == transport
-            assert q_out.get(timeout=TIMEOUT) == ("connected", transport)
-            for version in (1, 2):
-                if version == 2:
-                    params["w1"].add_(0.5)
-                r = tr.publish_version(version)
-                assert r["changed"] == (len(params) if version == 1 else 1)
-                q_in.put(("check", version, tr.pushers[0].hashes(), {n: t.cpu() for n, t in params.items()}))
-                msg = q_out.get(timeout=TIMEOUT)
-                assert msg == ("checked", version, True), msg
-            if mode == "bf16" and transport == "p2p":
-                # K3: compare the local parameter with the rollout's copy by P2P loads
-                C = native()
-                peer = tr.peers[0]
-                e = tr.layout.by_name["w2"]
-                n = e.nbytes
-                dig = torch.zeros((n + 65535) // 65536, dtype=torch.int64, device="cuda:0")
-                mism = torch.zeros(1, dtype=torch.int32, device="cuda:0")
-                s = torch.cuda.current_stream().cuda_stream
-                C.k_verify_peer(params["w2"].data_ptr(), peer.ptr + e.dst_offset, n, dig.data_ptr(),
-                                mism.data_ptr(), s, 0)
-                torch.cuda.synchronize()
-                assert mism.item() == 0
-            man = off.get_manifest("policy_rollout", 2)
-            assert len(man["tensors"]) == len(params)
-            tr.close()
-        q_in.put(("done",))
+            try:
+                torch.manual_seed(0)
+                params = {n: (torch.randn(s, device="cuda:0") * 0.02).to(getattr(torch, dt))
+                          for n, s, dt in _specs()}
+                tag, fp = q_out.get(timeout=TIMEOUT)
+                assert tag == "published"
+                tr = TrainerWeightSync(off, params, [f"rollout/{mode}/{transport}"], mode=mode, transport=transport)
+                assert tr.layout.fingerprint == fp
+                assert tr.transport == transport
+                assert q_out.get(timeout=TIMEOUT) == ("connected", transport)
+                for version in (1, 2):
+                    if version == 2:
+                        params["w1"].add_(0.5)
+                    r = tr.publish_version(version)
+                    assert r["changed"] == (len(params) if version == 1 else 1)
+                    q_in.put(("check", version, tr.pushers[0].hashes(), {n: t.cpu() for n, t in params.items()}))
+                    msg = q_out.get(timeout=TIMEOUT)
+                    assert msg == ("checked", version, True), msg
+                if mode == "bf16" and transport == "p2p":
+                    # K3: compare the local parameter with the rollout's copy by P2P loads
+                    C = native()
+                    peer = tr.peers[0]
+                    e = tr.layout.by_name["w2"]
+                    n = e.nbytes
+                    dig = torch.zeros((n + 65535) // 65536, dtype=torch.int64, device="cuda:0")
+                    mism = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+                    s = torch.cuda.current_stream().cuda_stream
+                    C.k_verify_peer(params["w2"].data_ptr(), peer.ptr + e.dst_offset, n, dig.data_ptr(),
+                                    mism.data_ptr(), s, 0)
+                    torch.cuda.synchronize()
+                    assert mism.item() == 0
+                man = off.get_manifest("policy_rollout", 2)
+                assert len(man["tensors"]) == len(params)
+            finally:
+                # Team teardown and the 'closed' signal come first, on every path: the
+                # rollout leaves the team only after that, never while bound to it.
+                if tr is not None:
+                    tr.close()
+                q_in.put(("done",))
         child.join(TIMEOUT)
         assert child.exitcode == 0
     finally:
         if child.is_alive():
+            child.join(TIMEOUT)
+        if child.is_alive() and transport == "p2p":
+            # Only a point-to-point child may be killed; a child that may still be bound
+            # to a multicast object is left to exit on its own queue timeout.
             child.kill()
             child.join(10)
         d.stop()
+        assert not child.is_alive(), "rollout child did not exit"
 
 
 @pytest.mark.parametrize("mode", ["bf16", "fp8"])
