@@ -145,6 +145,7 @@ struct Agent::Impl {
         PinnedPool::Buf dig, mism, exp;  // digests out, mismatch counter, expected digests
         uint64_t ndig = 0;
         PinnedPool::Buf zb;              // zbf16 window bases (one byte per chunk) + pre-pass flag
+        PinnedPool::Buf err;             // bulk forms: device status word (0 = the copy completed)
         bool z = false;
         // Batched launches: every item of the batch shares one event and the
         // job table; the last item to finish releases both.
@@ -155,6 +156,7 @@ struct Agent::Impl {
 
     struct TensorRec {
         bool offloaded = false, restored = false;
+        bool failed = false;  // the device reported an incomplete copy (bounded wait expired)
         uint64_t hash_lo = 0, hash_hi = 0, lease = 0;
         std::vector<uint64_t> digests;
     };
@@ -163,6 +165,7 @@ struct Agent::Impl {
     std::map<TvKey, TensorRec> tensors;
 
     std::atomic<uint64_t> inflight_d2h{0}, inflight_h2d{0}, evicts{0}, restores{0}, d2h_done{0}, h2d_done{0};
+    std::atomic<uint64_t> xfer_errors{0};  // copies a kernel reported incomplete
     std::atomic<uint64_t> d2h_bytes{0}, h2d_bytes{0}, registered_bytes{0}, d2h_ns{0}, h2d_ns{0}, reg_ns{0};
     std::atomic<bool> stop{false}, hb_paused{false};
     std::thread progress_thr, heartbeat_thr;
@@ -421,7 +424,45 @@ struct Agent::Impl {
     }
 
     // Retire one completed transfer (copy finished).
+    // Device status of a bulk launch (a bounded wait inside the kernel that
+    // ran out leaves the copy incomplete); the status buffer returns to the pool.
+    uint32_t take_device_status(Pending& p) {
+        if (!p.err.host) return 0;
+        const uint32_t e = *static_cast<volatile uint32_t*>(p.err.host);
+        pool.put(p.err);
+        p.err = PinnedPool::Buf{};
+        return e;
+    }
+
     void finish(Pending& p) {
+        if (const uint32_t derr = take_device_status(p)) {
+            LOG_ERR(TAG, "%s of tensor %llu v%llu incomplete: device status %u", p.d2h ? "evict" : "restore",
+                    (unsigned long long)p.tid, (unsigned long long)p.ver, derr);
+            ++xfer_errors;
+            if (p.d2h) {
+                // the pinned run holds partial bytes: give it back instead of publishing it
+                ReleaseLeaseRequest rl{opt.rank_id, epoch, p.lease, p.slot, "device copy incomplete"};
+                (void)call<Op::kReleaseLease>(rl);
+                pool.put(p.dig);
+                pool.put(p.zb);
+                p.zb = PinnedPool::Buf{};
+                {
+                    std::lock_guard<std::mutex> g(tab_mu);
+                    TensorRec& t = tensors[{p.tid, p.ver}];
+                    t.offloaded = true;  // waiters wake and see the failure
+                    t.failed = true;
+                }
+                inflight_d2h -= p.nbytes;
+                if (p.cb) p.cb();
+                if (p.batch_keep) p.batch_keep.reset();
+                else if (p.ev) cudaEventDestroy(p.ev);
+                p.ev = nullptr;
+                tab_cv.notify_all();
+                return;
+            }
+            std::lock_guard<std::mutex> g(tab_mu);
+            tensors[{p.tid, p.ver}].failed = true;
+        }
         if (p.d2h) {
             uint64_t lo = 0, hi = 0;
             std::vector<uint64_t> dig;
@@ -614,6 +655,11 @@ struct Agent::Impl {
         } else if (opt.engine == "copy_engine") {
             if (hash) CUDA_OK(kern::hash_device(reinterpret_cast<const void*>(src), p.nbytes, dig_dev, s, opt.hash_ctas));
             CUDA_OK(cudaMemcpyAsync(dst_host, reinterpret_cast<const void*>(src), p.nbytes, cudaMemcpyDeviceToHost, s));
+        } else if (opt.bulk && kern::bulk_ok(reinterpret_cast<const void*>(src), dst_dev, p.nbytes)) {
+            p.err = pool.get(16);
+            *static_cast<volatile uint32_t*>(p.err.host) = 0;
+            CUDA_OK(kern::evict_bulk(reinterpret_cast<const void*>(src), dst_dev, p.nbytes, dig_dev,
+                                     static_cast<uint32_t*>(p.err.dev), s, opt.evict_ctas));
         } else {
             CUDA_OK(kern::evict_hash(reinterpret_cast<const void*>(src), dst_dev, p.nbytes, dig_dev, s, opt.evict_ctas));
         }
@@ -737,6 +783,15 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
     t.message = "ok";
     t.lease_id = g.lease_id;
     t.slot_id = g.slot_id;
+    if (wait) {
+        std::lock_guard<std::mutex> lg(D.tab_mu);
+        auto it = D.tensors.find({tensor_id, version});
+        if (it != D.tensors.end() && it->second.failed) {
+            t.ok = false;
+            t.message = "evict: device copy incomplete (bounded wait expired)";
+            return t;
+        }
+    }
     if (wait) tensor_hash(tensor_id, version, &t.hash_lo, &t.hash_hi);
     return t;
 }
@@ -1019,6 +1074,11 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
                                 reinterpret_cast<float*>(ro.scales_ptr), exp_dev, mism_dev, s, D.opt.restore_ctas));
     } else if (D.opt.engine == "copy_engine" && ro.cast == 0 && !exp_dev) {
         CUDA_OK(cudaMemcpyAsync(reinterpret_cast<void*>(ptr), host, src_bytes, cudaMemcpyHostToDevice, s));
+    } else if (D.opt.bulk && ro.cast == 0 && !exp_dev && kern::bulk_ok(dev, reinterpret_cast<void*>(ptr), src_bytes)) {
+        p.err = D.pool.get(16);
+        *static_cast<volatile uint32_t*>(p.err.host) = 0;
+        CUDA_OK(kern::restore_bulk(dev, reinterpret_cast<void*>(ptr), src_bytes, static_cast<uint32_t*>(p.err.dev), s,
+                                   D.opt.restore_ctas));
     } else {
         CUDA_OK(kern::restore_cast(dev, reinterpret_cast<void*>(ptr), src_bytes, kern::Cast(ro.cast),
                                    reinterpret_cast<float*>(ro.scales_ptr), exp_dev, mism_dev, s, D.opt.restore_ctas));
@@ -1028,9 +1088,11 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
     if (wait) {
         CUDA_OK(cudaEventSynchronize(p.ev));
         if (mism_dev) out.mismatched_chunks = *static_cast<volatile uint32_t*>(p.mism.host);
+        const bool dev_err = p.err.host && *static_cast<volatile uint32_t*>(p.err.host) != 0;
         D.finish(p);
-        out.ok = out.mismatched_chunks == 0;
-        out.message = out.ok ? "ok" : "content digest mismatch";
+        out.ok = out.mismatched_chunks == 0 && !dev_err;
+        out.message = dev_err ? "restore: device copy incomplete (bounded wait expired)"
+                              : out.ok ? "ok" : "content digest mismatch";
         return out;
     }
     D.complete_or_queue(std::move(p), false);

@@ -37,6 +37,12 @@ struct AgentOptions {
     uint64_t progress_poll_us = 50;
     uint64_t prefetch_poll_us = 200;
     std::string engine = "kernel";  // "kernel" (SM copies) | "copy_engine" (cudaMemcpyAsync)
+    // In kernel mode, uncoded transfers whose pointers are 16-byte aligned and
+    // whose size is a multiple of 16 move as bulk copies (kern::evict_bulk /
+    // restore_bulk: one thread per CTA streams 32 KiB pieces between the
+    // host-mapped run and shared memory) instead of per-thread 16-byte
+    // accesses; restores that verify or cast keep the per-thread form.
+    bool bulk = true;
     int evict_ctas = 0, restore_ctas = 0, hash_ctas = 0;
     bool hash_on_evict = true;
     bool use_ring = true;

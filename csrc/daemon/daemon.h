@@ -376,6 +376,7 @@ class Daemon {
     void enqueue_drain(const Lease& L);
     bool force_drain_one(std::unique_lock<std::mutex>& lk);
     void pressure_drain();
+    void drain_settled(uint32_t base);  // a queued drain left the count (done, skipped or freed); mu_ held
     bool write_cold(const char* src, uint64_t nbytes, ColdEntry* out, bool allow_pageable, bool allow_nvme = true);
     // Cold tiers a drain of `tid` may use under its job's pageable / NVMe
     // quotas (both true for non-canonical tensors). mu_ held.
@@ -456,6 +457,7 @@ class Daemon {
     // reservation waits on for one of them to free its pinned run.
     uint32_t drains_pending_ = 0;
     uint64_t draining_slots_ = 0;  // slots of runs queued for or in a drain (still counted in used_slots_)
+    std::unordered_map<uint32_t, uint32_t> drain_queued_;  // run base -> slots counted in draining_slots_
     std::condition_variable_any drained_cv_;
 
     std::vector<std::thread> workers_;

@@ -433,6 +433,8 @@ RequestCanonicalRestoreResponse Daemon::on_canonical_restore(const RequestCanoni
         if (!allocate(r.gpu_id, r.numa_node, nbytes, OFLD_FLAG_ALLOW_OVERFLOW | OFLD_FLAG_ALLOW_REMOTE_NUMA, &base,
                       &count, lk)) {
             unpin_cold(cref);
+            // busy pinned runs free up as other transfers finish: the caller retries
+            resp.retriable = true;
             resp.message = "no pinned capacity to warm object";
             return resp;
         }

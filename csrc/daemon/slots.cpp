@@ -141,6 +141,7 @@ bool Daemon::alloc_in_window(Window& w, uint32_t count, uint32_t* base) {
 }
 
 void Daemon::free_run(uint32_t base, uint32_t count) {
+    drain_settled(base);
     for (uint32_t k = 0; k < count; ++k) {
         uint32_t id = base + k;
         ofld_slot_entry_t& e = slots_[id];
@@ -520,7 +521,22 @@ RequestPrefetchResponse Daemon::do_request_prefetch(const RequestPrefetchRequest
     uint32_t base = 0, count = 0;
     if (!allocate(r.gpu_id, r.numa_node, loc.nbytes, r.flags | OFLD_FLAG_ALLOW_REMOTE_NUMA, &base, &count, lk)) {
         Metrics::get().inc(M::kBlockedReservations);
-        resp.message = "no pinned capacity for readback";
+        uint32_t largest = 0;
+        for (const Window& w : windows_) largest = std::max(largest, w.nslots);
+        if (slots_for(loc.nbytes) > largest) {
+            resp.message = "no pinned window can hold this tensor for readback";
+            return resp;
+        }
+        // Every pinned run is busy (transfers in flight, prefetch leases not
+        // yet released, nothing left to drain): they free up as other
+        // restores finish, so this is backpressure, not a failure. The caller
+        // polls again, as it does while a readback is in flight.
+        resp.ok = true;
+        resp.ready = false;
+        resp.state = OFLD_SLOT_FREE;
+        resp.version = want;
+        resp.nbytes = loc.nbytes;
+        resp.message = "waiting for pinned capacity for readback";
         return resp;
     }
     // The lock may have been released by a forced drain; re-validate.

@@ -222,7 +222,9 @@ uint64_t Daemon::commit_cold(ColdEntry&& c) {
 void Daemon::enqueue_drain(const Lease& L) {
     set_run_state(L.base, L.count, OFLD_SLOT_DRAIN_IN_FLIGHT);
     ++drains_pending_;
+    drain_settled(L.base);  // a stale entry for this base (run freed and reused) leaves the count first
     draining_slots_ += L.count;
+    drain_queued_[L.base] = L.count;
     {
         std::lock_guard<std::mutex> q(q_mu_);
         drain_q_.push_back(DrainJob{L.base, L.count});
@@ -230,6 +232,18 @@ void Daemon::enqueue_drain(const Lease& L) {
     drain_cv_.notify_one();
     Metrics::get().inc(M::kDrainsEnqueued);
     Metrics::get().add(M::kDrainingBytes, L.nbytes);
+}
+
+// The slots of a queued drain stop counting as "about to be freed" once the
+// drain is done or skipped, or as soon as the run is freed by another path
+// (discard, recovery) while the job still waits in the queue: used_slots_
+// drops at that moment, so keeping them in draining_slots_ would subtract
+// them twice and make pressure drains stop short. mu_ held.
+void Daemon::drain_settled(uint32_t base) {
+    auto it = drain_queued_.find(base);
+    if (it == drain_queued_.end()) return;
+    draining_slots_ -= std::min<uint64_t>(draining_slots_, it->second);
+    drain_queued_.erase(it);
 }
 
 // Under the normal/priority/aggressive thresholds, queue background drains of
@@ -399,7 +413,7 @@ void Daemon::drain_loop() {
             if (state_of(job.base) != OFLD_SLOT_DRAIN_IN_FLIGHT) {
                 Metrics::get().sub(M::kDrainingBytes, slots_[job.base].nbytes);
                 if (drains_pending_) --drains_pending_;
-                draining_slots_ -= std::min<uint64_t>(draining_slots_, job.count);
+                drain_settled(job.base);
                 drained_cv_.notify_all();
                 continue;
             }
@@ -418,7 +432,7 @@ void Daemon::drain_loop() {
                 Metrics::get().inc(M::kQuotaRejections);
                 Metrics::get().sub(M::kDrainingBytes, nbytes);
                 if (drains_pending_) --drains_pending_;
-                draining_slots_ -= std::min<uint64_t>(draining_slots_, job.count);
+                drain_settled(job.base);
                 drained_cv_.notify_all();
                 continue;
             }
@@ -431,7 +445,7 @@ void Daemon::drain_loop() {
         if (!ref && ok) ref = commit_cold(std::move(cold));
         finish_drain(job.base, job.count, tid, ver, lid, owner, nbytes, ref);
         if (drains_pending_) --drains_pending_;
-        draining_slots_ -= std::min<uint64_t>(draining_slots_, job.count);
+        drain_settled(job.base);
         drained_cv_.notify_all();
     }
 }

@@ -132,8 +132,18 @@ inline uint64_t digest_count(uint64_t nbytes) { return (nbytes + 65535) / 65536;
 //                     writes every member's buffer
 // Without kPushMulticast, `dst` / `dst_scales` are typically peer-GPU
 // pointers (CUDA IPC or VMM mappings).
-enum : uint32_t { kPushRaw = 0, kPushFp8 = 1, kPushHash = 2 };
-enum : uint32_t { kPushDelta = 1u << 0, kPushMulticast = 1u << 1 };
+//        kPushBulk  copy each staged half-chunk to `dst` with one bulk store
+//                   (cp.async.bulk shared -> global, no multicast); `dst` is
+//                   this GPU's memory or host-mapped pinned memory, never a
+//                   peer. The evict / restore bulk forms (evict_bulk,
+//                   restore_bulk) are one-item launches of this mode.
+//   flags kPushNoHash  skip the ssh128 lane work and the digest write (a
+//                     plain copy; only with kPushBulk)
+enum : uint32_t { kPushRaw = 0, kPushFp8 = 1, kPushHash = 2, kPushBulk = 3 };
+enum : uint32_t { kPushDelta = 1u << 0, kPushMulticast = 1u << 1, kPushNoHash = 1u << 2 };
+// launch_flags only: four staged halves per CTA (128 KiB in flight, one CTA
+// per SM) instead of two; the bulk forms use it for host-mapped traffic.
+enum : uint32_t { kPushDeep = 1u << 8 };
 // `digest_base` is the index of the item's first chunk in the launch's digest
 // table (equal to chunk_begin for a full table; a subset launch keeps the
 // full table's indices so the record of what the destination holds stays put).
@@ -175,6 +185,23 @@ cudaError_t push(const PushItem* items_dev, int nitems, uint64_t total_chunks, P
 // shared memory, three CTAs per SM). src 16-byte aligned, nbytes % 16 == 0.
 cudaError_t hash_stream(const void* src_dev, uint64_t nbytes, uint64_t* digests, uint32_t* error, cudaStream_t s,
                         int ctas);
+
+// K1 / K2 bulk forms: the bytes cross PCIe as bulk copies issued by one
+// thread per CTA (host-mapped source or destination <-> shared memory), with
+// the ssh128 chunk digests of the evicted bytes computed from shared memory in
+// the same pass (`digests` null: no hash). src, dst 16-byte aligned,
+// nbytes % 16 == 0. `error` (device-accessible u32, may be null) receives a
+// non-zero code when a bounded wait inside the kernel ran out (the copy is
+// then incomplete). ctas = 0: the default for host-mapped traffic.
+cudaError_t evict_bulk(const void* src_dev, void* dst_mapped, uint64_t nbytes, uint64_t* digests, uint32_t* error,
+                       cudaStream_t s, int ctas);
+cudaError_t restore_bulk(const void* src_mapped, void* dst_dev, uint64_t nbytes, uint32_t* error, cudaStream_t s,
+                         int ctas);
+// Whether the bulk forms take these arguments (alignment and size rules).
+inline bool bulk_ok(const void* a, const void* b, uint64_t nbytes) {
+    return nbytes > 0 && (nbytes & 15) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(b) & 15) == 0;
+}
 
 // Dynamic shared memory of one delta-mode K4 CTA (three 32 KiB half-chunk
 // stages + barriers).

@@ -42,6 +42,8 @@ const char* kernel_name(uint32_t id) {
         case kIdZScanJobs: return "zbf16_scan_jobs";
         case kIdVerifyPeer: return "k3_verify_peer";
         case kIdPush: return "k4_push";
+        case kIdEvictBulk: return "k1_evict_bulk";
+        case kIdRestoreBulk: return "k2_restore_bulk";
         default: return "unknown";
     }
 }

@@ -39,6 +39,8 @@ enum KernelId : uint32_t {
     kIdZScanJobs = 9,   // zbf16 pre-pass over a batch
     kIdVerifyPeer = 10, // K3
     kIdPush = 11,       // K4
+    kIdEvictBulk = 12,  // K1, bulk-copy form
+    kIdRestoreBulk = 13,// K2, bulk-copy form
     kIdCount
 };
 const char* kernel_name(uint32_t id);

@@ -65,9 +65,12 @@ constexpr size_t smem_bytes() {
     return size_t(S) * kHalf + 2 * S * 8 + kGroupWarps * 8 + 16;
 }
 // S = 2 half-stages: three CTAs per SM (hash-only and non-delta pushes);
-// S = 3: two CTAs per SM, one half prefetched while a delta chunk is held.
+// S = 3: two CTAs per SM, one half prefetched while a delta chunk is held;
+// S = 4: one CTA per SM with 128 KiB in flight (host-mapped bulk transfers,
+// where a few dozen CTAs must cover PCIe latency).
 static_assert(3 * (smem_bytes<2>() + 1024) <= 233472, "three S=2 CTAs must fit one SM");
 static_assert(2 * (smem_bytes<3>() + 1024) <= 233472, "two S=3 CTAs must fit one SM");
+static_assert(smem_bytes<4>() + 1024 <= 233472, "an S=4 CTA must fit one SM");
 
 // Error codes written to PushState::error (first writer wins).
 constexpr uint32_t kErrFullTimeout = 1;
@@ -118,6 +121,22 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32
             smem_u32(dst_smem)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// Bulk store of a staged half: shared memory -> global (this GPU's memory or
+// host-mapped pinned memory), tracked by the issuing thread's bulk groups.
+__device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src_smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src_smem),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The stage may be refilled once every issued bulk store finished reading it.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Every issued bulk store complete (its writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ uint4 ld_smem(uint32_t addr) {
@@ -271,7 +290,7 @@ __device__ __forceinline__ void set_error(const PushState& st, uint32_t code) {
 }
 
 template <int S>
-__global__ void __launch_bounds__(kThreads, (S == 2 ? 3 : 2))
+__global__ void __launch_bounds__(kThreads, (S == 2 ? 3 : S == 3 ? 2 : 1))
     k_push(const PushItem* __restrict__ items, int nitems, uint64_t total_chunks, PushState st, PushItem one, KernelStamp* ks) {
     StampScope stamp_scope_(ks);
     // `items == nullptr`: a single item passed by value (no device table)
@@ -310,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, (S == 2 ? 3 : 2))
             // does not own chunk c, or a source that is not 16-byte aligned,
             // is recorded and ends the launch without issuing the copy.
             if (c < it.chunk_begin || off_in_item >= it.nbytes || (reinterpret_cast<uintptr_t>(src) & 15) ||
-                (it.nbytes & 15)) {
+                (it.nbytes & 15) || (it.mode == kPushBulk && (reinterpret_cast<uintptr_t>(it.dst) & 15))) {
                 set_error(st, kErrBadItem);
                 return;  // the consumers' bounded waits on the stages never filled end the launch
             }
@@ -337,16 +356,19 @@ __global__ void __launch_bounds__(kThreads, (S == 2 ? 3 : 2))
     const uint32_t lt = t;
     int idx = 0;
     uint32_t i = 0;
-    bool aborted = false, stored_any = false;
+    bool aborted = false, stored_any = false, bulk_any = false;
     for (uint64_t c = blockIdx.x; c < total_chunks; c += gridDim.x, ++i) {
         advance_item(items, nitems, c, idx);
         const PushItem it = items ? items[idx] : one;
         const uint64_t base = (c - it.chunk_begin) * kChunk;
         const uint32_t len = chunk_len(it, c);
         const uint32_t nvec = len / 16;  // the launcher guarantees nbytes % 16 == 0
-        const bool delta = (it.flags & kPushDelta) != 0;
-        const bool store_now = !delta && it.mode != kPushHash;  // stores need no digest: issue from the same registers
-        const bool hold = delta && it.mode != kPushHash;        // stages kept until the store decision
+        const bool bulk = it.mode == kPushBulk;
+        const bool nohash = bulk && (it.flags & kPushNoHash) != 0;
+        const bool delta = !bulk && (it.flags & kPushDelta) != 0;
+        // stores need no digest: issue from the same registers
+        const bool store_now = !delta && it.mode != kPushHash && !bulk;
+        const bool hold = delta && it.mode != kPushHash;  // stages kept until the store decision
         // the destination's digest of this chunk, loaded now and used after the hash
         const uint64_t dgi = it.digest_base + (c - it.chunk_begin);
         const uint64_t old_dg = (delta && lt == 0) ? st.digests[dgi] : 0;
@@ -364,7 +386,20 @@ __global__ void __launch_bounds__(kThreads, (S == 2 ? 3 : 2))
                 break;
             }
             const uint32_t sb = stage0 + uint32_t(s) * kHalf;
-            if (len == kChunk) {
+            if (bulk && lt == 0) {
+                // one thread hands the staged half to the bulk-copy unit; the
+                // group hashes the same shared memory meanwhile
+                const uint32_t lo = h * kHalf;
+                const uint32_t bytes = len > lo ? (len - lo < kHalf ? len - lo : kHalf) : 0;
+                if (bytes) {
+                    fence_proxy_async_smem();
+                    bulk_s2g(static_cast<uint8_t*>(it.dst) + base + lo, sb, bytes);
+                    bulk_commit();
+                    bulk_any = true;
+                }
+            }
+            if (nohash) {
+            } else if (len == kChunk) {
 #pragma unroll
                 for (int kk = 0; kk < kHalfVecs; ++kk) {
                     const uint4 v = ld_smem(sb + (uint32_t(kk) * kGroupThreads + lt) * 16);
@@ -383,17 +418,18 @@ __global__ void __launch_bounds__(kThreads, (S == 2 ? 3 : 2))
                 }
             }
             if (!hold) {
+                if (bulk && lt == 0) bulk_wait_read_all();  // the stage's bulk store has read it
                 __syncwarp();
                 if ((lt & 31) == 0) mbar_arrive(&empty[s]);
             }
         }
         if (aborted) break;
         stored_any |= store_now;
-        const uint64_t root = chunk_tree(ssh::lane_digest(L, lt), red, 0, lt);
+        const uint64_t root = nohash ? 0 : chunk_tree(ssh::lane_digest(L, lt), red, 0, lt);
         if (lt == 0) {
-            const uint64_t dg = ssh::chunk_finish(root, len);
+            const uint64_t dg = nohash ? 0 : ssh::chunk_finish(root, len);
             const bool same = delta && old_dg == dg;
-            st.digests[dgi] = dg;
+            if (!nohash) st.digests[dgi] = dg;
             const bool stored = it.mode != kPushHash && !same;
             flags[0] = hold && stored;
             if (stored && st.stats) {
@@ -427,6 +463,12 @@ __global__ void __launch_bounds__(kThreads, (S == 2 ? 3 : 2))
     // Peer stores are posted writes: make them visible system-wide before the
     // grid completes, so a host-side signal after the stream sync is safe.
     if (stored_any) __threadfence_system();
+    // Bulk stores read this CTA's shared memory and write asynchronously:
+    // wait for all of them before the CTA retires.
+    if (bulk_any) {
+        bulk_wait_all();
+        __threadfence_system();
+    }
     // Do not leave with bulk copies still writing this CTA's shared memory:
     // after an abort give the stages the producer may have filled a bounded
     // chance to complete.
@@ -459,7 +501,7 @@ size_t push_smem_bytes() { return smem_bytes<3>(); }
 namespace {
 template <int S>
 cudaError_t launch_stages(const PushItem* items_dev, int nitems, uint64_t total_chunks, const PushState& st,
-                          const PushItem& one, cudaStream_t s, int ctas) {
+                          const PushItem& one, cudaStream_t s, int ctas, uint32_t stamp_id = kIdPush) {
     static thread_local int configured_device = -1;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -471,9 +513,10 @@ cudaError_t launch_stages(const PushItem* items_dev, int nitems, uint64_t total_
     }
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int g = ctas > 0 ? ctas : sms * (S == 2 ? 3 : 2);  // persistent: every resident slot
+    int g = ctas > 0 ? ctas : sms * (S == 2 ? 3 : S == 3 ? 2 : 1);  // persistent: every resident slot
     if (uint64_t(g) > total_chunks) g = int(total_chunks);
-    KernelStamp* ks = timing_take(kIdPush, total_chunks * kChunk);  // source bytes read (chunk-rounded)
+    // bytes: one-item launches move exactly the item; tables are chunk-rounded
+    KernelStamp* ks = timing_take(stamp_id, items_dev ? total_chunks * kChunk : one.nbytes);
     k_push<S><<<g, kThreads, smem_bytes<S>(), s>>>(items_dev, nitems, total_chunks, st, one, ks);
     g_push_launches.fetch_add(1, std::memory_order_relaxed);
     e = cudaGetLastError();
@@ -503,6 +546,41 @@ cudaError_t hash_stream(const void* src_dev, uint64_t nbytes, uint64_t* digests,
     one.mode = kPushHash;
     PushState st{digests, nullptr, nullptr, error};
     return launch_stages<2>(nullptr, 1, ssh::num_chunks(nbytes), st, one, s, ctas);
+}
+
+// Default grid of the bulk forms: PCIe Gen5 x16 carries ~55 GB/s with about
+// 2 us of read latency, so ~110 KB must be in flight; 24 CTAs of 128 KiB keep
+// 3 MiB in flight and leave the other SMs to concurrent work.
+constexpr int kBulkCtas = 24;
+
+cudaError_t evict_bulk(const void* src_dev, void* dst_mapped, uint64_t nbytes, uint64_t* digests, uint32_t* error,
+                       cudaStream_t s, int ctas) {
+    if (nbytes == 0) return cudaSuccess;
+    if (!src_dev || !dst_mapped || !bulk_ok(src_dev, dst_mapped, nbytes)) return cudaErrorInvalidValue;
+    PushItem one{};
+    one.src = src_dev;
+    one.dst = dst_mapped;
+    one.nbytes = nbytes;
+    one.mode = kPushBulk;
+    one.flags = digests ? 0u : kPushNoHash;
+    PushState st{digests, nullptr, nullptr, error};
+    return launch_stages<4>(nullptr, 1, ssh::num_chunks(nbytes), st, one, s, ctas > 0 ? ctas : kBulkCtas,
+                            kIdEvictBulk);
+}
+
+cudaError_t restore_bulk(const void* src_mapped, void* dst_dev, uint64_t nbytes, uint32_t* error, cudaStream_t s,
+                         int ctas) {
+    if (nbytes == 0) return cudaSuccess;
+    if (!src_mapped || !dst_dev || !bulk_ok(src_mapped, dst_dev, nbytes)) return cudaErrorInvalidValue;
+    PushItem one{};
+    one.src = src_mapped;
+    one.dst = dst_dev;
+    one.nbytes = nbytes;
+    one.mode = kPushBulk;
+    one.flags = kPushNoHash;
+    PushState st{nullptr, nullptr, nullptr, error};
+    return launch_stages<4>(nullptr, 1, ssh::num_chunks(nbytes), st, one, s, ctas > 0 ? ctas : kBulkCtas,
+                            kIdRestoreBulk);
 }
 
 uint64_t push_launch_count() { return g_push_launches.load(std::memory_order_relaxed); }

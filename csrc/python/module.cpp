@@ -219,6 +219,7 @@ class PyAgent {
             else if (k == "progress_poll_us") o.progress_poll_us = v.cast<uint64_t>();
             else if (k == "prefetch_poll_us") o.prefetch_poll_us = v.cast<uint64_t>();
             else if (k == "engine") o.engine = v.cast<std::string>();
+            else if (k == "bulk") o.bulk = v.cast<bool>();
             else if (k == "evict_ctas") o.evict_ctas = v.cast<int>();
             else if (k == "restore_ctas") o.restore_ctas = v.cast<int>();
             else if (k == "hash_ctas") o.hash_ctas = v.cast<int>();
@@ -615,6 +616,18 @@ PYBIND11_MODULE(_C, m) {
                                  reinterpret_cast<float*>(scales), reinterpret_cast<const uint64_t*>(expect),
                                  reinterpret_cast<uint32_t*>(mismatch), reinterpret_cast<cudaStream_t>(stream), ctas),
               "restore_cast");
+    });
+    m.def("k_evict_bulk", [](uint64_t src, uint64_t dst, uint64_t n, uint64_t dig, uint64_t err, uint64_t stream,
+                             int ctas) {
+        check(kern::evict_bulk(reinterpret_cast<void*>(src), reinterpret_cast<void*>(dst), n,
+                               reinterpret_cast<uint64_t*>(dig), reinterpret_cast<uint32_t*>(err),
+                               reinterpret_cast<cudaStream_t>(stream), ctas),
+              "evict_bulk");
+    });
+    m.def("k_restore_bulk", [](uint64_t src, uint64_t dst, uint64_t n, uint64_t err, uint64_t stream, int ctas) {
+        check(kern::restore_bulk(reinterpret_cast<void*>(src), reinterpret_cast<void*>(dst), n,
+                                 reinterpret_cast<uint32_t*>(err), reinterpret_cast<cudaStream_t>(stream), ctas),
+              "restore_bulk");
     });
     m.def("k_hash_device", [](uint64_t src, uint64_t n, uint64_t dig, uint64_t stream, int ctas) {
         check(kern::hash_device(reinterpret_cast<void*>(src), n, reinterpret_cast<uint64_t*>(dig),

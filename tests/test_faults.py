@@ -302,6 +302,11 @@ nvme:
             atk.scribble_slot(slot, arena_id=999, arena_offset=1 << 50, nbytes=1 << 40)
             # fill the 8 MiB window: the oldest run (x) is drained under pressure
             hs = [off.copy(torch.randn(1 << 18), wait=True) for _ in range(10)]
+            # drains run in the background: x (least recently used) leaves the
+            # pinned tier once its queued drain finishes
+            deadline = time.time() + 30
+            while time.time() < deadline and h.location() == "pinned":
+                time.sleep(0.02)
             assert off.daemon_stats()["drains_completed"] >= 3 and h.location() != "pinned"
             assert torch.equal(h.restore(), x)
             assert atk.slot_fields(slot)[1:4] != (999, 1 << 50, 1 << 40)  # republished

@@ -170,3 +170,63 @@ def test_verify_peer_same_device_counts_mismatches():
     torch.cuda.synchronize()
     assert int(mism.item()) == 2
     assert [int(v) & 0xFFFFFFFFFFFFFFFF for v in dig.cpu().tolist()] == native().ssh_digests(a.cpu().numpy())
+
+
+BULK_SIZES = [16, 4096, 65536, 65536 + 16, 3 * 32768 + 48, (1 << 22) + 4080, 33 << 20]
+
+
+@pytest.mark.parametrize("n", BULK_SIZES)
+@pytest.mark.parametrize("ctas", [0, 3])
+def test_evict_bulk_bytes_and_digests(n, ctas):
+    """Bulk-copy K1: device -> host-mapped pinned memory through shared
+    memory, digests from the staged bytes; equal to the host oracle and to the
+    per-thread K1."""
+    C = native()
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+    dst = _pinned(n + 16)
+    dst.fill_(0xA5)
+    nd = (n + 65535) // 65536
+    dig = torch.zeros(nd, dtype=torch.int64, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    C.k_evict_bulk(src.data_ptr(), _dev_ptr_of_pinned(dst), n, dig.data_ptr(), err.data_ptr(), s, ctas)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    host = src.cpu()
+    assert torch.equal(dst[:n], host)
+    assert torch.all(dst[n:] == 0xA5)  # nothing written past the end
+    got = [int(v) & 0xFFFFFFFFFFFFFFFF for v in dig.cpu().tolist()]
+    assert got == _host_digests(host, n)
+    dig2 = torch.zeros_like(dig)
+    C.k_evict_hash(src.data_ptr(), _dev_ptr_of_pinned(dst), n, dig2.data_ptr(), s, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(dig, dig2)
+
+
+@pytest.mark.parametrize("n", BULK_SIZES)
+def test_evict_bulk_without_hash_and_restore_bulk(n):
+    C = native()
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+    host = _pinned(n)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    C.k_evict_bulk(src.data_ptr(), _dev_ptr_of_pinned(host), n, 0, err.data_ptr(), s, 0)
+    back = torch.full((n + 16,), 0x5A, dtype=torch.uint8, device="cuda")
+    C.k_restore_bulk(_dev_ptr_of_pinned(host), back.data_ptr(), n, err.data_ptr(), s, 0)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(host[:n], src.cpu())
+    assert torch.equal(back[:n], src)
+    assert torch.all(back[n:] == 0x5A)
+
+
+def test_bulk_forms_reject_unaligned_arguments():
+    C = native()
+    a = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    h = _pinned(1 << 16)
+    s = torch.cuda.current_stream().cuda_stream
+    for src, dst, n in ((a.data_ptr() + 1, h.data_ptr(), 4096), (a.data_ptr(), h.data_ptr(), 4095)):
+        with pytest.raises(RuntimeError):
+            C.k_evict_bulk(src, dst, n, 0, 0, s, 0)
+        with pytest.raises(RuntimeError):
+            C.k_restore_bulk(dst, src, n, 0, s, 0)

@@ -184,3 +184,50 @@ def test_pressure_drains_stop_at_the_normal_threshold_during_a_batch(sock_path):
             assert s["readbacks_completed"] <= 3 * 6
     finally:
         d.stop()
+
+
+def test_restore_waits_for_pinned_capacity_instead_of_failing(sock_path):
+    """A readback that finds every pinned run busy (D2H copies in flight, which
+    no drain can take) backs off and completes once capacity returns, rather
+    than failing the restore."""
+    import threading
+
+    from rawclient import RawRank
+    from statespectre_b200._wire import Op
+
+    d = in_process_daemon(socket=sock_path, arena_mb=16, slot_mb=1, drain_on_complete=True)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cpu") as off:
+            x = torch.randn(1 << 18)  # 1 MiB: one slot
+            h = off.copy(x, wait=True)
+            assert wait_for(lambda: h.location() == "pageable"), h.location()
+            r = RawRank(sock_path, 9)
+            held = []
+            for i in range(64):  # hold every free slot with a D2H that has not completed
+                g = r.reserve(1000 + i, 1, 1 << 20)
+                if not g["ok"]:
+                    break
+                assert r.mark(Op.MARK_D2H_SUBMITTED, g["lease_id"], 1000 + i, 1, g["slot_id"])["ok"]
+                held.append((1000 + i, g))
+            assert held, "no slot could be reserved"
+            out = {}
+
+            def restore():
+                try:
+                    out["y"] = h.restore()
+                except Exception as e:  # noqa: BLE001
+                    out["err"] = e
+
+            t = threading.Thread(target=restore, daemon=True)
+            t.start()
+            t.join(1.0)
+            assert t.is_alive() and not out, out  # waiting, not failed
+            assert off.daemon_stats()["blocked_reservation_count"] >= 1
+            for tid, g in held:  # the copies finish; their runs drain and free
+                assert r.mark(Op.MARK_D2H_COMPLETE, g["lease_id"], tid, 1, g["slot_id"])["ok"]
+            t.join(60)
+            assert not t.is_alive() and "err" not in out, out
+            assert torch.equal(out["y"], x)
+            r.close()
+    finally:
+        d.stop()
