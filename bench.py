@@ -62,7 +62,8 @@ def parse():
     p.add_argument("--size-mb", type=int, default=1024)
     p.add_argument("--matmul", type=int, default=1)
     p.add_argument("--engine", default="kernel", choices=["kernel", "copy_engine"])
-    p.add_argument("--bulk", type=int, default=1, help="uncoded transfers as bulk copies (kernel engine)")
+    p.add_argument("--uncoded", default="copy_engine", choices=["copy_engine", "bulk", "sm"],
+                   help="kernel engine: how bytes that are not zbf16-coded move")
     p.add_argument("--evict-ctas", type=int, default=0)
     p.add_argument("--restore-ctas", type=int, default=0)
     p.add_argument("--hash", type=int, default=1)
@@ -180,7 +181,7 @@ def main():
                            eager_register=True, engine=args.engine, evict_ctas=args.evict_ctas,
                            restore_ctas=args.restore_ctas, hash_on_evict=bool(args.hash), stream_priority=-1,
                            compress=bool(args.compress), kernel_timing=bool(args.kernel_timing),
-                           bulk=bool(args.bulk))
+                           uncoded=args.uncoded)
     off = sess.off
     g = torch.Generator(device=device)
     g.manual_seed(1234 + rank)
@@ -315,7 +316,7 @@ def main():
                 "tensor_bytes": nbytes, "global_batch": world, "seq_len": 0, "parallelism": f"dp{world}",
                 "concurrent_matmul": "8192x8192 bf16 loop" if args.matmul else "none",
                 "engine": args.engine, "hash": bool(args.hash), "slot_mb": 64,
-                "uncoded_form": "bulk copies" if args.bulk else "per-thread 16-byte accesses",
+                "uncoded_form": args.uncoded,
                 "transfer_coding": coding,
                 "l2": "inputs (1 GiB) larger than the 126 MB L2; no flush needed",
                 "baseline": f"StateSpectre H20 PCIe Gen5 1 GiB: D2H {BASELINE_D2H_GBS}, H2D {BASELINE_H2D_GBS} GB/s "

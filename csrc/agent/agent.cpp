@@ -133,6 +133,7 @@ struct Agent::Impl {
     std::mutex ring_mu;
 
     cudaStream_t stream = nullptr;
+    cudaStream_t side = nullptr;  // evict digests next to a copy-engine copy
     PinnedPool pool;
 
     struct Pending {
@@ -172,6 +173,8 @@ struct Agent::Impl {
 
     // ------------------------------------------------------------------
     explicit Impl(const AgentOptions& o) : opt(o) {
+        if (opt.uncoded != "copy_engine" && opt.uncoded != "bulk" && opt.uncoded != "sm")
+            throw std::invalid_argument("uncoded must be copy_engine, bulk or sm, not '" + opt.uncoded + "'");
         gpu = opt.device >= 0;
         if (gpu) {
             CUDA_OK(cudaSetDevice(opt.device));
@@ -241,7 +244,9 @@ struct Agent::Impl {
             cudaDeviceGetStreamPriorityRange(&lo, &hi);
             int prio = opt.stream_priority < 0 ? hi : 0;
             CUDA_OK(cudaStreamCreateWithPriority(&stream, cudaStreamNonBlocking, prio));
+            CUDA_OK(cudaStreamCreateWithPriority(&side, cudaStreamNonBlocking, prio));
         }
+
         // Heartbeats start before the eager pinning below: registering a
         // 100+ GB arena while other ranks pin theirs can outlast the daemon's
         // heartbeat timeout, which would expire this session.
@@ -263,6 +268,7 @@ struct Agent::Impl {
         } catch (...) {
         }
         if (stream) cudaStreamDestroy(stream);
+        if (side) cudaStreamDestroy(side);
         pool.clear();
         unmap_all();
     }
@@ -652,10 +658,27 @@ struct Agent::Impl {
         if (p.z) {
             CUDA_OK(kern::evict_z(reinterpret_cast<const void*>(src), dst_dev, p.nbytes,
                                   static_cast<const uint8_t*>(p.zb.dev), dig_dev, s, opt.evict_ctas));
-        } else if (opt.engine == "copy_engine") {
-            if (hash) CUDA_OK(kern::hash_device(reinterpret_cast<const void*>(src), p.nbytes, dig_dev, s, opt.hash_ctas));
-            CUDA_OK(cudaMemcpyAsync(dst_host, reinterpret_cast<const void*>(src), p.nbytes, cudaMemcpyDeviceToHost, s));
-        } else if (opt.bulk && kern::bulk_ok(reinterpret_cast<const void*>(src), dst_dev, p.nbytes)) {
+        } else if (opt.engine == "copy_engine" || opt.uncoded == "copy_engine") {
+            if (hash) {
+                // the digests read HBM on a side stream while the copy engine
+                // crosses PCIe; the caller's stream waits for both
+                cudaEvent_t fork = nullptr, join = nullptr;
+                CUDA_OK(cudaEventCreateWithFlags(&fork, cudaEventDisableTiming));
+                CUDA_OK(cudaEventCreateWithFlags(&join, cudaEventDisableTiming));
+                CUDA_OK(cudaEventRecord(fork, s));
+                CUDA_OK(cudaStreamWaitEvent(side, fork, 0));
+                CUDA_OK(kern::hash_device(reinterpret_cast<const void*>(src), p.nbytes, dig_dev, side, opt.hash_ctas));
+                CUDA_OK(cudaEventRecord(join, side));
+                CUDA_OK(cudaMemcpyAsync(dst_host, reinterpret_cast<const void*>(src), p.nbytes, cudaMemcpyDeviceToHost,
+                                        s));
+                CUDA_OK(cudaStreamWaitEvent(s, join, 0));
+                cudaEventDestroy(fork);
+                cudaEventDestroy(join);
+            } else {
+                CUDA_OK(cudaMemcpyAsync(dst_host, reinterpret_cast<const void*>(src), p.nbytes, cudaMemcpyDeviceToHost,
+                                        s));
+            }
+        } else if (opt.uncoded == "bulk" && kern::bulk_ok(reinterpret_cast<const void*>(src), dst_dev, p.nbytes)) {
             p.err = pool.get(16);
             *static_cast<volatile uint32_t*>(p.err.host) = 0;
             CUDA_OK(kern::evict_bulk(reinterpret_cast<const void*>(src), dst_dev, p.nbytes, dig_dev,
@@ -1072,9 +1095,10 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
     if (z) {
         CUDA_OK(kern::restore_z(dev, reinterpret_cast<void*>(ptr), src_bytes, kern::Cast(ro.cast),
                                 reinterpret_cast<float*>(ro.scales_ptr), exp_dev, mism_dev, s, D.opt.restore_ctas));
-    } else if (D.opt.engine == "copy_engine" && ro.cast == 0 && !exp_dev) {
+    } else if ((D.opt.engine == "copy_engine" || D.opt.uncoded == "copy_engine") && ro.cast == 0 && !exp_dev) {
         CUDA_OK(cudaMemcpyAsync(reinterpret_cast<void*>(ptr), host, src_bytes, cudaMemcpyHostToDevice, s));
-    } else if (D.opt.bulk && ro.cast == 0 && !exp_dev && kern::bulk_ok(dev, reinterpret_cast<void*>(ptr), src_bytes)) {
+    } else if (D.opt.uncoded == "bulk" && ro.cast == 0 && !exp_dev &&
+               kern::bulk_ok(dev, reinterpret_cast<void*>(ptr), src_bytes)) {
         p.err = D.pool.get(16);
         *static_cast<volatile uint32_t*>(p.err.host) = 0;
         CUDA_OK(kern::restore_bulk(dev, reinterpret_cast<void*>(ptr), src_bytes, static_cast<uint32_t*>(p.err.dev), s,

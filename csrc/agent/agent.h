@@ -37,12 +37,17 @@ struct AgentOptions {
     uint64_t progress_poll_us = 50;
     uint64_t prefetch_poll_us = 200;
     std::string engine = "kernel";  // "kernel" (SM copies) | "copy_engine" (cudaMemcpyAsync)
-    // In kernel mode, uncoded transfers whose pointers are 16-byte aligned and
-    // whose size is a multiple of 16 move as bulk copies (kern::evict_bulk /
-    // restore_bulk: one thread per CTA streams 32 KiB pieces between the
-    // host-mapped run and shared memory) instead of per-thread 16-byte
-    // accesses; restores that verify or cast keep the per-thread form.
-    bool bulk = true;
+    // How kernel mode moves the bytes it does not code (fp32, fp8, integer
+    // and small or unaligned tensors, bf16 data that does not code):
+    //   "copy_engine"  cudaMemcpyAsync, with the ssh128 chunk digests of an
+    //                  evict computed at HBM rate on a side stream meanwhile
+    //                  (default: SM-initiated PCIe traffic tops out ~7 % below
+    //                  the copy engine on B200, in every instruction form);
+    //   "bulk"         kern::evict_bulk / restore_bulk (bulk copies through
+    //                  shared memory; aligned, size % 16 == 0);
+    //   "sm"           per-thread K1 / K2.
+    // Restores that verify digests or cast always run K2.
+    std::string uncoded = "copy_engine";
     int evict_ctas = 0, restore_ctas = 0, hash_ctas = 0;
     bool hash_on_evict = true;
     bool use_ring = true;

@@ -6,7 +6,8 @@
 //                       re-verification and an optional cast (bf16 -> fp8 e4m3
 //                       with one fp32 scale per 128 elements, fp32 -> bf16,
 //                       bf16 -> fp32).
-//   hash_device         ssh128 chunk digests of a device buffer at HBM rate.
+//   hash_device         ssh128 chunk digests of a device buffer at HBM rate
+//                       (the K4 bulk-copy pipeline for aligned buffers).
 //   verify_peer     K3: digests of a local buffer plus an exact byte compare
 //                       against a peer GPU's replica read over NVLink.
 //   quant_fp8_block     standalone 1x128 block quantization (used by the
@@ -59,6 +60,9 @@ cudaError_t restore_cast(const void* src_mapped, void* dst_dev, uint64_t src_nby
                          cudaStream_t stream, int ctas);
 
 cudaError_t hash_device(const void* src_dev, uint64_t nbytes, uint64_t* digests, cudaStream_t stream, int ctas);
+// The one-pass hash kernel (per-thread loads, any alignment): hash_device's
+// form for unaligned buffers, and an independent second implementation.
+cudaError_t hash_onepass(const void* src_dev, uint64_t nbytes, uint64_t* digests, cudaStream_t stream, int ctas);
 
 // Fold chunk digests into the 128-bit object hash on the device (single CTA);
 // `out` receives {lo, hi}.
@@ -183,8 +187,10 @@ cudaError_t push(const PushItem* items_dev, int nitems, uint64_t total_chunks, P
 
 // Chunk digests of a device buffer through the K4 pipeline (bulk copies into
 // shared memory, three CTAs per SM). src 16-byte aligned, nbytes % 16 == 0.
+// `stages` picks the block shape: 2 (three CTAs per SM, 64 KiB staged each),
+// 3 (two per SM) or 4 (one per SM, 128 KiB); 0 = the measured default.
 cudaError_t hash_stream(const void* src_dev, uint64_t nbytes, uint64_t* digests, uint32_t* error, cudaStream_t s,
-                        int ctas);
+                        int ctas, int stages = 0);
 
 // K1 / K2 bulk forms: the bytes cross PCIe as bulk copies issued by one
 // thread per CTA (host-mapped source or destination <-> shared memory), with

@@ -820,7 +820,17 @@ cudaError_t evict_hash(const void* src, void* dst, uint64_t nbytes, uint64_t* di
     return cudaGetLastError();
 }
 
+// Aligned buffers go through the K4 bulk-copy pipeline (bulk copies into
+// shared memory keep more bytes in flight per SM than per-thread loads);
+// others take the one-pass kernel.
 cudaError_t hash_device(const void* src, uint64_t nbytes, uint64_t* digests, cudaStream_t s, int ctas) {
+    if (nbytes == 0) return cudaSuccess;
+    if (!src || !digests) return cudaErrorInvalidValue;
+    if (aligned16(src) && (nbytes & 15) == 0) return hash_stream(src, nbytes, digests, nullptr, s, ctas, 0);
+    return hash_onepass(src, nbytes, digests, s, ctas);
+}
+
+cudaError_t hash_onepass(const void* src, uint64_t nbytes, uint64_t* digests, cudaStream_t s, int ctas) {
     if (nbytes == 0) return cudaSuccess;
     if (!src || !digests) return cudaErrorInvalidValue;
     const int g = grid_for(nbytes, ctas, 148 * 4);

@@ -535,8 +535,11 @@ cudaError_t push(const PushItem* items_dev, int nitems, uint64_t total_chunks, P
     return launch_stages<2>(items_dev, nitems, total_chunks, st, PushItem{}, s, ctas);
 }
 
+// Block shape of the standalone hash (see hash_stream).
+constexpr int kHashStages = 3;
+
 cudaError_t hash_stream(const void* src_dev, uint64_t nbytes, uint64_t* digests, uint32_t* error, cudaStream_t s,
-                        int ctas) {
+                        int ctas, int stages) {
     if (nbytes == 0) return cudaSuccess;
     if (!src_dev || !digests || (reinterpret_cast<uintptr_t>(src_dev) & 15) || (nbytes & 15))
         return cudaErrorInvalidValue;
@@ -545,7 +548,12 @@ cudaError_t hash_stream(const void* src_dev, uint64_t nbytes, uint64_t* digests,
     one.nbytes = nbytes;
     one.mode = kPushHash;
     PushState st{digests, nullptr, nullptr, error};
-    return launch_stages<2>(nullptr, 1, ssh::num_chunks(nbytes), st, one, s, ctas);
+    const uint64_t nch = ssh::num_chunks(nbytes);
+    if (stages == 0) stages = kHashStages;
+    if (stages == 4) return launch_stages<4>(nullptr, 1, nch, st, one, s, ctas, kIdHash);
+    if (stages == 3) return launch_stages<3>(nullptr, 1, nch, st, one, s, ctas, kIdHash);
+    if (stages == 2) return launch_stages<2>(nullptr, 1, nch, st, one, s, ctas, kIdHash);
+    return cudaErrorInvalidValue;
 }
 
 // Default grid of the bulk forms: PCIe Gen5 x16 carries ~55 GB/s with about

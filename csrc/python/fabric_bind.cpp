@@ -87,11 +87,12 @@ void bind_fabric(py::module_& m) {
     m.def("push_smem_bytes", &kern::push_smem_bytes);
     m.def(
         "k_hash_stream",
-        [](uint64_t src, uint64_t n, uint64_t digests, uint64_t error, uint64_t stream, int ctas) {
+        [](uint64_t src, uint64_t n, uint64_t digests, uint64_t error, uint64_t stream, int ctas, int stages) {
             cudaError_t e = kern::hash_stream(reinterpret_cast<const void*>(src), n, reinterpret_cast<uint64_t*>(digests),
                                               reinterpret_cast<uint32_t*>(error), reinterpret_cast<cudaStream_t>(stream),
-                                              ctas);
+                                              ctas, stages);
             if (e != cudaSuccess) throw std::runtime_error(std::string("hash_stream: ") + cudaGetErrorString(e));
         },
-        py::arg("src"), py::arg("nbytes"), py::arg("digests"), py::arg("error"), py::arg("stream"), py::arg("ctas") = 0);
+        py::arg("src"), py::arg("nbytes"), py::arg("digests"), py::arg("error"), py::arg("stream"), py::arg("ctas") = 0,
+        py::arg("stages") = 0);
 }

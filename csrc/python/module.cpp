@@ -219,7 +219,7 @@ class PyAgent {
             else if (k == "progress_poll_us") o.progress_poll_us = v.cast<uint64_t>();
             else if (k == "prefetch_poll_us") o.prefetch_poll_us = v.cast<uint64_t>();
             else if (k == "engine") o.engine = v.cast<std::string>();
-            else if (k == "bulk") o.bulk = v.cast<bool>();
+            else if (k == "uncoded") o.uncoded = v.cast<std::string>();
             else if (k == "evict_ctas") o.evict_ctas = v.cast<int>();
             else if (k == "restore_ctas") o.restore_ctas = v.cast<int>();
             else if (k == "hash_ctas") o.hash_ctas = v.cast<int>();
@@ -628,6 +628,11 @@ PYBIND11_MODULE(_C, m) {
         check(kern::restore_bulk(reinterpret_cast<void*>(src), reinterpret_cast<void*>(dst), n,
                                  reinterpret_cast<uint32_t*>(err), reinterpret_cast<cudaStream_t>(stream), ctas),
               "restore_bulk");
+    });
+    m.def("k_hash_onepass", [](uint64_t src, uint64_t n, uint64_t dig, uint64_t stream, int ctas) {
+        check(kern::hash_onepass(reinterpret_cast<void*>(src), n, reinterpret_cast<uint64_t*>(dig),
+                                 reinterpret_cast<cudaStream_t>(stream), ctas),
+              "hash_onepass");
     });
     m.def("k_hash_device", [](uint64_t src, uint64_t n, uint64_t dig, uint64_t stream, int ctas) {
         check(kern::hash_device(reinterpret_cast<void*>(src), n, reinterpret_cast<uint64_t*>(dig),

@@ -884,7 +884,7 @@ _AGENT_OPTION_KEYS = {
     "kernels.restore_ctas": ("restore_ctas", int),
     "kernels.hash_ctas": ("hash_ctas", int),
     "kernels.engine": ("engine", str),
-    "kernels.bulk": ("bulk", _as_bool),
+    "kernels.uncoded": ("uncoded", str),
     "kernels.compress": ("compress", _as_bool),
     "kernels.compress_min_mb": ("compress_min_bytes", lambda v: int(float(v) * (1 << 20))),
     "kernels.batch_group_mb": ("batch_group_bytes", lambda v: int(float(v) * (1 << 20))),

@@ -3,8 +3,10 @@
     python -m statespectre_b200.ops.profile_case --kernel evict --mb 512 --iters 3
 
 Kernels: evict (K1, device -> pinned + ssh128), restore (K2, pinned ->
-device), restore_fp8 (K2 with the bf16 -> fp8 1x128 cast), hash (device
-ssh128), hash_stream (ssh128 through the K4 bulk-copy pipeline), verify (K3
+device), restore_fp8 (K2 with the bf16 -> fp8 1x128 cast), evict_bulk /
+restore_bulk (K1 / K2 as bulk copies through shared memory), hash (device
+ssh128, the library's choice of form), hash_onepass (the per-thread-load
+hash kernel), hash_stream (ssh128 through the K4 bulk-copy pipeline), verify (K3
 local vs second buffer), push / push_fp8 (K4 into a second buffer, raw or
 quantized; --peer 1 puts that buffer on cuda:1 so the stores cross NVLink).
 The case is larger than the 126 MB L2 so DRAM counters are meaningful; it
@@ -22,12 +24,13 @@ from .._native import native
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", required=True, choices=["evict", "restore", "restore_fp8", "hash", "hash_stream",
-                                                          "verify", "push", "push_fp8", "zscan", "evict_z",
-                                                          "restore_z"])
+    ap.add_argument("--kernel", required=True, choices=["evict", "restore", "restore_fp8", "hash", "hash_onepass",
+                                                          "hash_stream", "verify", "push", "push_fp8", "zscan",
+                                                          "evict_z", "restore_z", "evict_bulk", "restore_bulk"])
     ap.add_argument("--mb", type=int, default=512)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--ctas", type=int, default=0)
+    ap.add_argument("--stages", type=int, default=0, help="hash_stream: 2, 3 or 4 staged halves per CTA (0: default)")
     ap.add_argument("--peer", type=int, default=-1, help="device of the push destination (default: same GPU)")
     ap.add_argument("--items", type=int, default=64, help="push: split the buffer into this many tensors")
     ap.add_argument("--delta", type=int, default=0,
@@ -75,6 +78,12 @@ def main():
             C.k_restore_cast(host.data_ptr(), out.data_ptr(), n, 1, scales.data_ptr(), 0, 0, s, a.ctas)
         elif a.kernel == "hash":
             C.k_hash_device(x.data_ptr(), n, dig.data_ptr(), s, a.ctas)
+        elif a.kernel == "hash_onepass":
+            C.k_hash_onepass(x.data_ptr(), n, dig.data_ptr(), s, a.ctas)
+        elif a.kernel == "evict_bulk":
+            C.k_evict_bulk(x.data_ptr(), host.data_ptr(), n, dig.data_ptr(), err.data_ptr(), s, a.ctas)
+        elif a.kernel == "restore_bulk":
+            C.k_restore_bulk(host.data_ptr(), out.data_ptr(), n, err.data_ptr(), s, a.ctas)
         elif a.kernel == "zscan":
             C.k_zscan(x.data_ptr(), n, zeb.data_ptr(), err.data_ptr(), s, 0)
         elif a.kernel == "evict_z":
@@ -82,7 +91,7 @@ def main():
         elif a.kernel == "restore_z":
             C.k_restore_z(host.data_ptr(), out.data_ptr(), n, 0, 0, 0, 0, s, a.ctas)
         elif a.kernel == "hash_stream":
-            C.k_hash_stream(x.data_ptr(), n, dig.data_ptr(), err.data_ptr(), s, a.ctas)
+            C.k_hash_stream(x.data_ptr(), n, dig.data_ptr(), err.data_ptr(), s, a.ctas, a.stages)
         elif pusher is not None:
             if a.delta == 1:
                 pusher.invalidate()
@@ -95,12 +104,12 @@ def main():
     if int(err.item()) != 0 or (pusher is not None and pusher.result()["error"]):
         code = int(err.item()) if pusher is None else pusher.result()["error"]
         raise SystemExit(f"{a.kernel}: device status {code}")
-    if a.kernel == "hash_stream":  # the digests must equal the one-pass hash kernel's
+    if a.kernel in ("hash", "hash_stream", "evict_bulk"):  # the digests must equal the one-pass kernel's
         ref = torch.zeros_like(dig)
-        C.k_hash_device(x.data_ptr(), n, ref.data_ptr(), s, 0)
+        C.k_hash_onepass(x.data_ptr(), n, ref.data_ptr(), s, 0)
         torch.cuda.synchronize()
         if not torch.equal(ref, dig):
-            raise SystemExit("hash_stream: digests differ from hash_device")
+            raise SystemExit(f"{a.kernel}: digests differ from the one-pass hash")
     print(f"{a.kernel}: {n / (ms / 1e3) / 1e9:.2f} GB/s ({ms:.3f} ms per launch, {n} bytes)")
 
 

@@ -118,15 +118,17 @@ def test_kernel_timing_stamps_transfers(gpu_off):
     hf.restore_into(f, wait=True)
     torch.cuda.synchronize()
     recs, nxt = off.kernel_timings(start)
-    assert nxt >= start + 5
+    assert nxt >= start + 4  # zbf16 scan, coded K1, hash beside the fp32 copy, coded K2
     kinds = {r["kernel"] for r in recs}
-    assert {"zbf16_scan", "k1_evict_zbf16", "k1_evict", "k2_restore_zbf16", "k2_restore"} <= kinds, kinds
+    # bf16 moves coded through the SM kernels; fp32 moves on the copy engine
+    # with its digests computed by the hash kernel beside it
+    assert {"zbf16_scan", "k1_evict_zbf16", "k2_restore_zbf16", "k1_hash"} <= kinds, kinds
     for r in recs:
         assert r["ns"] > 0 and r["bytes"] > 0
         gbs = r["bytes"] / r["ns"]
         assert 1.0 < gbs < 20000.0, r  # PCIe kernels tens of GB/s, the scan HBM-rate
     prof = off.kernel_profile(start)
-    assert prof["k1_evict"]["bytes"] == 32 << 20
+    assert prof["k1_hash"]["bytes"] == 32 << 20
     # the session trace carries the stamped kernels as device-time events
     import json
     import os
@@ -140,3 +142,39 @@ def test_kernel_timing_stamps_transfers(gpu_off):
     assert {"zbf16_scan", "k1_evict_zbf16"} <= {e["name"] for e in kev} and all(e["dur"] > 0 for e in kev)
     hx.discard()
     hf.discard()
+
+
+@pytest.mark.parametrize("uncoded", ["copy_engine", "bulk", "sm"])
+@pytest.mark.parametrize("shape,dtype", [((12 << 20) // 4 + 7, torch.float32), ((1 << 20) + 8, torch.float8_e4m3fn),
+                                         ((3 << 20) + 5, torch.int16)])
+def test_uncoded_forms_roundtrip_with_host_oracle_hash(sock_path, uncoded, shape, dtype):
+    """Every way of moving uncoded bytes (copy engine with the hash beside
+    it, bulk copies, per-thread K1/K2) is byte-exact and yields the host
+    oracle's content hash; odd sizes take the per-thread form."""
+    d = in_process_daemon(socket=sock_path, arena_mb=256, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", uncoded=uncoded) as off:
+            if dtype == torch.float8_e4m3fn:
+                x = torch.randn(shape, device="cuda").to(dtype)
+            elif dtype == torch.int16:
+                x = torch.randint(-30000, 30000, (shape,), dtype=dtype, device="cuda")
+            else:
+                x = torch.randn(shape, dtype=dtype, device="cuda")
+            ref = x.clone()
+            for _ in range(2):
+                h = off.evict(x, wait=True)
+                assert h.content_hash == native().ssh_hash(ref.cpu().view(torch.uint8).numpy())
+                x = h.restore()
+                assert torch.equal(x.view(torch.uint8), ref.view(torch.uint8))
+                h.discard()
+    finally:
+        d.stop()
+
+
+def test_unknown_uncoded_form_is_rejected(sock_path):
+    d = in_process_daemon(socket=sock_path, arena_mb=64, drain_on_complete=False)
+    try:
+        with pytest.raises(Exception, match="uncoded"):
+            offload_context(daemon_addr=sock_path, device="cuda:0", uncoded="dma")
+    finally:
+        d.stop()

@@ -230,3 +230,24 @@ def test_bulk_forms_reject_unaligned_arguments():
             C.k_evict_bulk(src, dst, n, 0, 0, s, 0)
         with pytest.raises(RuntimeError):
             C.k_restore_bulk(dst, src, n, 0, s, 0)
+
+
+@pytest.mark.parametrize("n", [16, 65536 * 3 + 4096, (1 << 24) + 48, 200 << 20])
+@pytest.mark.parametrize("stages", [2, 3, 4])
+def test_hash_stream_shapes_match_one_pass_and_host(n, stages):
+    """The K4-pipeline hash in each block shape equals the one-pass kernel and
+    the host oracle; hash_device (which picks the form) agrees too."""
+    C = native()
+    x = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+    nd = (n + 65535) // 65536
+    a, b, c = (torch.zeros(nd, dtype=torch.int64, device="cuda") for _ in range(3))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    C.k_hash_stream(x.data_ptr(), n, a.data_ptr(), err.data_ptr(), s, 0, stages)
+    C.k_hash_onepass(x.data_ptr(), n, b.data_ptr(), s, 0)
+    C.k_hash_device(x.data_ptr(), n, c.data_ptr(), s, 0)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(a, b) and torch.equal(b, c)
+    if n <= (1 << 24) + 48:
+        assert [int(v) & 0xFFFFFFFFFFFFFFFF for v in b.cpu().tolist()] == _host_digests(x.cpu(), n)
