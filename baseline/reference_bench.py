@@ -267,11 +267,15 @@ def run(args, metric: str, baseline_roundtrip_gbs: float) -> dict | None:
         except subprocess.TimeoutExpired:
             daemon.kill()
         log.close()
+    ws = None
+    if world >= 2 and getattr(args, "weight_sync", 1) and world % 2 == 0:
+        ws = run_weight_sync(args, world, rank, local_rank, device, state_spectre,
+                             versions=getattr(args, "ref_ws_versions", 3), warmup=1)
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return None
-    return {
+    out = {
         "impl": "reference",
         "metric": metric,
         "value": round(value, 3),
@@ -302,6 +306,233 @@ def run(args, metric: str, baseline_roundtrip_gbs: float) -> dict | None:
         "matmul_iters": mm_count[0],
         "reference_build": os.path.relpath(REF, ROOT),
     }
+    if ws is not None:
+        out["weight_sync"] = ws
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Weight sync through the reference: the same Qwen2.5-32B-shaped TP shards and
+# per-version update as the main arm, moved the way StateSpectre moves a
+# sealed version (python_api/state_spectre/__init__.py:575-633,
+# _rollout.py:64-189, tests/python/trainer_seal.py): every trainer rank
+# canonical_evicts each tensor of its shard under the new model version
+# (D2H into the pinned arena), one rank promotes the version, and every
+# rollout rank reads the manifest of its TP shard and pulls the changed
+# objects over TCP from the daemon (RolloutWeightClient), then copies them
+# into its GPU tensors. The previous version is dropped once pulled.
+# ---------------------------------------------------------------------------
+
+QWEN2_5_32B = dict(layers=64, hidden=5120, ffn=27648, heads=40, kv_heads=8, head_dim=128, vocab=152064)
+
+
+def qwen_shard_shapes(tp_rank: int, tp: int, layers: int):
+    """(name, shape) of one TP shard in Hugging Face parameter order."""
+    c = QWEN2_5_32B
+    h, q, kv = c["hidden"], c["heads"] * c["head_dim"] // tp, c["kv_heads"] * c["head_dim"] // tp
+    f, v = c["ffn"] // tp, c["vocab"] // tp
+    out = [("model.embed_tokens.weight", (v, h))]
+    for i in range(layers):
+        p = f"model.layers.{i}."
+        out += [(p + "input_layernorm.weight", (h,)), (p + "self_attn.q_proj.weight", (q, h)),
+                (p + "self_attn.q_proj.bias", (q,)), (p + "self_attn.k_proj.weight", (kv, h)),
+                (p + "self_attn.k_proj.bias", (kv,)), (p + "self_attn.v_proj.weight", (kv, h)),
+                (p + "self_attn.v_proj.bias", (kv,)), (p + "self_attn.o_proj.weight", (h, q)),
+                (p + "post_attention_layernorm.weight", (h,)), (p + "mlp.gate_proj.weight", (f, h)),
+                (p + "mlp.up_proj.weight", (f, h)), (p + "mlp.down_proj.weight", (h, f))]
+    out += [("model.norm.weight", (h,)), ("lm_head.weight", (v, h))]
+    return out
+
+
+def _changed(names, fraction: float, seed: int):
+    import torch
+
+    gen = torch.Generator()
+    gen.manual_seed(seed)
+    k = max(1, int(round(fraction * len(names))))
+    return sorted(torch.randperm(len(names), generator=gen)[:k].tolist())
+
+
+def run_weight_sync(args, world: int, rank: int, local_rank: int, device, state_spectre, versions: int,
+                    warmup: int) -> dict | None:
+    import statistics
+
+    import torch
+    import torch.distributed as dist
+
+    tp = world // 2
+    trainer = rank < tp
+    tp_rank = rank % tp
+    layers = max(1, 64 * tp // 4)
+    shapes = qwen_shard_shapes(tp_rank, tp, layers)
+    names = [n for n, _ in shapes]
+    shard_bytes = sum(2 * _numel(s) for _, s in shapes)
+    trainer_group = dist.new_group(list(range(tp)))
+    port = 47311
+    run_dir = os.environ.get("OFLD_REF_BENCH_DIR", "/tmp/ssref_bench") + "_wsync"
+    os.makedirs(run_dir, exist_ok=True)
+    sock = os.path.join(run_dir, "offloadd.sock")
+    daemon = log = None
+    n_local = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    if local_rank == 0:
+        if os.path.exists(sock):
+            os.unlink(sock)
+        # trainer GPUs hold this version and the previous one until it is dropped
+        win = int(2 * shard_bytes / (1 << 30)) + 6
+        by_node = {}
+        for g in range(max(n_local, torch.cuda.device_count())):
+            by_node.setdefault(_gpu_numa_node(g), []).append(g)
+        lines = ["daemon:", f"  socket_path: {sock}", f"  control_shm_name: /ssref_ws_{os.getpid()}",
+                 "  heartbeat_timeout_ms: 60000", "arenas:", "  registration_policy: eager",
+                 "  allocation_granularity_mb: 2", "  per_numa:"]
+        for node, gpus in sorted(by_node.items()):
+            sizes = {g: (win if g < tp else 1) for g in gpus}
+            lines += [f"    - numa_node: {node}", f"      size_gb: {sum(sizes.values()) + 2}", "      overflow_gb: 2",
+                      "      gpu_windows:"]
+            for g in gpus:
+                lines += [f"        - gpu: {g}", f"          size_gb: {sizes[g]}"]
+        lines += ["drain_policy:", "  target_tier: pageable", "  drain_on_d2h_complete: false", "nvme:",
+                  "  enabled: false"]
+        cfg = os.path.join(run_dir, "offloadd.yaml")
+        with open(cfg, "w") as f:
+            f.write("\n".join(lines) + "\n")
+        log = open(os.path.join(run_dir, "offloadd.log"), "w")
+        daemon = subprocess.Popen([os.path.join(REF, "bin", "offloadd"), "--config", cfg, "--socket", sock,
+                                   "--tcp-port", str(port)], stdout=log, stderr=log)
+        deadline = time.time() + 300
+        while not os.path.exists(sock) and time.time() < deadline and daemon.poll() is None:
+            time.sleep(0.05)
+        if not os.path.exists(sock):
+            raise RuntimeError(f"reference offloadd did not come up (log {log.name})")
+    dist.barrier()
+    ident = torch.zeros(2, dtype=torch.int64, device=device)
+    sess = off = client = None
+    if trainer:
+        sess = state_spectre.offload_context(daemon_addr=sock, device=device, rank=rank, local_rank=local_rank,
+                                             world_rank=rank, eager_register=True, job_name="wsync-ref")
+        off = sess.__enter__()
+        g = torch.Generator(device=device)
+        g.manual_seed(1000 + tp_rank)
+        params = {}
+        for n, s in shapes:
+            t = torch.empty(s, dtype=torch.bfloat16, device=device)
+            t.normal_(1.0 if n.endswith("norm.weight") else 0.0, 0.02, generator=g)
+            params[n] = t
+        biggest = max(t.numel() for t in params.values())
+        scratch = torch.empty(biggest, dtype=torch.bfloat16, device=device)
+        scratch.normal_(0.0, float(args.delta_std), generator=torch.Generator(device=device).manual_seed(7 + tp_rank))
+        pool = torch.empty(biggest, dtype=torch.bfloat16, pin_memory=True)
+        pool.copy_(scratch)
+        if tp_rank == 0:
+            ident[0], ident[1] = int(off.job_id) & 0x7FFFFFFFFFFFFFFF, int(off.launch_epoch)
+            ident_hi = int(off.job_id) >> 63
+        dist.barrier(group=trainer_group)
+    dist.broadcast(ident, 0)
+    hi = torch.tensor([ident_hi if rank == 0 else 0], dtype=torch.int64, device=device)
+    dist.broadcast(hi, 0)
+    job_id = int(ident[0].item()) | (int(hi.item()) << 63)
+    epoch = int(ident[1].item())
+    if not trainer:
+        from state_spectre._rollout import RolloutWeightClient
+
+        client = RolloutWeightClient(f"tcp://127.0.0.1:{port}", job_id, epoch, recv_host="127.0.0.1")
+        bufs = {n: torch.empty(s, dtype=torch.bfloat16, device=device) for n, s in shapes}
+    peer = tp_rank + tp if trainer else tp_rank
+    go = torch.zeros(1, dtype=torch.int64, device=device)
+
+    def step(v: int, stats):
+        t0 = time.perf_counter()
+        h2d = 0
+        if trainer:
+            if v > 1:  # this version's update from pinned memory, applied on the device
+                off_e = 0
+                for i in _changed(names, args.change_fraction, seed=v * 7919 + tp_rank):
+                    t = params[names[i]]
+                    n = t.numel()
+                    if off_e + n > pool.numel():
+                        off_e = 0
+                    scratch[:n].copy_(pool[off_e:off_e + n], non_blocking=True)
+                    t.view(-1).add_(scratch[:n])
+                    off_e += n
+                    h2d += 2 * n
+            torch.cuda.synchronize(device)
+            for n in names:  # the reference records every tensor of the version
+                key = off.canonical_key(model_role="policy_rollout", model_version=v, param_name=n,
+                                        tensor=params[n], pp_rank=0, tp_rank=tp_rank, expert_id=-1)
+                off.canonical_evict(params[n], key, destructive=False, wait=True)
+            dist.barrier(group=trainer_group)
+            if tp_rank == 0:
+                off.promote_rollout_version(v)
+            dist.barrier(group=trainer_group)
+            go.fill_(v)
+            dist.send(go, peer)
+            dist.recv(go, peer)  # the rollout's answer
+            dist.barrier(group=trainer_group)
+            if tp_rank == 0 and v > 1:
+                off.drop_canonical_version("policy_rollout", v - 1)
+        else:
+            dist.recv(go, peer)
+            man = client.get_manifest(v, {"tp": tp_rank})
+            changed = {e["object_id"] for e in client.diff_local(man)}
+            pulled = 0
+            for e in man["tensors"]:
+                if e["object_id"] not in changed:
+                    continue
+                payload = client.pull_tensor(e, v)
+                dst = bufs[e["key"]["param_fqn_debug"]]
+                dst.view(-1).view(torch.uint8).copy_(torch.frombuffer(payload, dtype=torch.uint8))
+                pulled += len(payload)
+            torch.cuda.synchronize(device)
+            go.fill_(1 if pulled else 0)
+            dist.send(go, peer)
+        t1 = time.perf_counter()
+        if stats is not None:
+            vals = torch.tensor([(t1 - t0) * 1e3, float(h2d)], dtype=torch.float64, device=device)
+            dist.all_reduce(vals[:1], op=dist.ReduceOp.MAX)
+            stats["e2e_ms"].append(float(vals[0].item()))
+
+    for v in range(1, warmup + 1):
+        step(v, None)
+    stats = {"e2e_ms": []}
+    sampler = _clock_sampler_cls()([local_rank]).start().wait_first()
+    dist.barrier()
+    sampler.mark_start()
+    for v in range(warmup + 1, warmup + versions + 1):
+        step(v, stats)
+    sampler.mark_end()
+    clocks = sampler.stop()
+    if sess is not None:
+        sess.close()
+    dist.barrier()
+    if daemon is not None:
+        daemon.terminate()
+        try:
+            daemon.wait(timeout=60)
+        except subprocess.TimeoutExpired:
+            daemon.kill()
+        log.close()
+    dist.destroy_process_group(trainer_group)
+    if rank != 0:
+        return None
+    e2e = sorted(stats["e2e_ms"])
+    return {
+        "model": "Qwen2.5-32B-shaped" + (f" ({layers} of 64 layers)" if layers != 64 else ""),
+        "trainer": f"TP={tp} on GPUs 0-{tp - 1}", "rollout": f"TP={tp} on GPUs {tp}-{world - 1}",
+        "parallelism": f"tp{tp}->tp{tp}", "shard_bytes_per_trainer_gpu": shard_bytes,
+        "change_fraction": args.change_fraction, "persist": True,
+        "path": "canonical_evict of every tensor (wait=True) + promote_rollout_version; rollout "
+                "RolloutWeightClient get_manifest(tp filter) + pull_tensor over TCP + H2D",
+        "modes": {"bf16": {"e2e_ms": round(statistics.median(e2e), 3), "e2e_ms_max": round(e2e[-1], 3),
+                           "versions": versions, "clocks": clocks},
+                  "fp8": "not available: the reference has no fp8 weight path"},
+    }
+
+
+def _numel(shape) -> int:
+    n = 1
+    for d in shape:
+        n *= d
+    return n
 
 
 def main(args, metric: str, baseline_roundtrip_gbs: float) -> int:

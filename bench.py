@@ -8,6 +8,13 @@ streams from HBM) is evicted GPU -> pinned arena with the fused content hash
 concurrently on the same GPU. The arena lives on the GPU's NUMA node, slots
 are 64 MiB, data stays pinned between evict and restore.
 
+At N >= 2 (even) the line carries a ``weight_sync`` block, the second half
+of the metric: the sealed-version weight-sync latency of a Qwen2.5-32B-shaped
+model, trainer TP=N/2 on the first half of the GPUs -> rollout TP=N/2 on the
+second half (each trainer GPU holds a TP=4 shard: 64 layers at 8 GPUs, 32 at
+4, 16 at 2), 10 % of the tensors changed per version, bf16 and fp8 push
+modes, persistence on (statespectre_b200/parallel/weight_sync_bench.py).
+
 Timing: W warm-up steps, then K steps bracketed by barrier + synchronize;
 device time from CUDA events on the copy stream, max over ranks. ``value`` is
 the whole-job aggregate: N * K * 2 * nbytes / max_rank_time. ``e2e`` repeats
@@ -77,7 +84,14 @@ def parse():
                    choices=["evict_restore", "weight_sync", "sweep", "kv_cache", "dp_dedup", "sections"])
     p.add_argument("--model", default="", help="weight_sync: qwen2.5-32b (default); dp_dedup: llama-3-8b (default)")
     p.add_argument("--layers", type=int, default=0, help="weight_sync: layer count override (0 = the model's)")
-    p.add_argument("--push-mode", default="bf16", choices=["bf16", "fp8"])
+    p.add_argument("--push-mode", default="bf16", choices=["bf16", "fp8", "both"])
+    p.add_argument("--weight-sync", type=int, default=1,
+                   help="evict_restore at N >= 2: append the sealed-version weight-sync block "
+                        "(Qwen2.5-32B-shaped, TP=N/2 -> TP=N/2, bf16 and fp8)")
+    p.add_argument("--ws-versions", type=int, default=50, help="weight-sync block: timed versions per mode")
+    p.add_argument("--ws-warmup", type=int, default=3, help="weight-sync block: untimed versions per mode")
+    p.add_argument("--ref-ws-versions", type=int, default=3,
+                   help="reference arm's weight-sync block: timed versions (each moves every tensor over TCP)")
     p.add_argument("--rollout-replicas", type=int, default=1,
                    help="weight_sync: rollout engines fed by each trainer shard (GPUs split 1 + R ways)")
     p.add_argument("--transport", default="auto", choices=["auto", "p2p", "multicast"],
@@ -295,6 +309,15 @@ def main():
     barrier()
     if daemon is not None:
         daemon.stop()
+    ws = None
+    if world >= 2 and args.weight_sync and world % 2 == 0:
+        # second half of the metric: sealed-version weight sync, TP=N/2 -> TP=N/2, each trainer GPU
+        # holding a TP=4 shard of Qwen2.5-32B (all 64 layers at 8 GPUs, 32 at 4, 16 at 2)
+        from statespectre_b200.parallel.weight_sync_bench import layers_for, run_block
+
+        args.rollout_replicas = 1
+        ws = run_block(args, world, rank, local_rank, device, ["bf16", "fp8"], args.ws_versions, args.ws_warmup,
+                       layers=layers_for(world))
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
@@ -332,6 +355,8 @@ def main():
         }
         if kernels is not None:
             line["kernels"] = kernels  # device-stamped, timed region, rank 0
+        if ws is not None:
+            line["weight_sync"] = ws
         print(json.dumps(line), flush=True)
         if args.out:
             with open(args.out, "w") as f:

@@ -569,21 +569,31 @@ CarryForwardResponse Daemon::on_carry_forward(const CarryForwardRequest& r) {
         resp.message = "target version already sealed";
         return resp;
     }
-    std::unordered_map<uint64_t, uint64_t> by_param;  // param_id -> object id at from_version
+    // param_id -> objects at from_version, one per partition (TP/PP/EP
+    // shards of one parameter share its param_id)
+    std::unordered_map<uint64_t, std::vector<uint64_t>> by_param;
     for (uint64_t oid : objects_of_version(job->uid, r.model_role, r.from_version)) {
         const CanonicalObject& o = objects_[oid];
-        if (readable(o.state)) by_param[o.key.param_id] = oid;
+        if (!readable(o.state)) continue;
+        if (r.shard && (o.key.pp_rank != r.pp_rank || o.key.tp_rank != r.tp_rank || o.key.ep_rank != r.ep_rank ||
+                        o.key.etp_rank != r.etp_rank || o.key.expert_id != r.expert_id))
+            continue;
+        by_param[o.key.param_id].push_back(oid);
     }
     std::vector<uint64_t> want = r.param_ids;
     if (want.empty())
         for (auto& kv : by_param) want.push_back(kv.first);
+    std::vector<uint64_t> sources;
     for (uint64_t pid : want) {
         auto bit = by_param.find(pid);
         if (bit == by_param.end()) {
             resp.missing_count++;
             continue;
         }
-        const CanonicalObject src = objects_[bit->second];
+        sources.insert(sources.end(), bit->second.begin(), bit->second.end());
+    }
+    for (uint64_t src_oid : sources) {
+        const CanonicalObject src = objects_[src_oid];
         CanonicalTensorKeyWire key = src.key;
         key.model_version = r.to_version;
         const std::string ks = key_string(key, cfg_.v2_cross_job_dedup);

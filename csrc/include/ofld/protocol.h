@@ -667,6 +667,8 @@ template <class V> void fields(V& v, LookupPeerBufferResponse& m) {
 // (all objects when the list is empty), create the same key at `to_version`
 // sharing the old object's storage and content hash. No bytes move; the
 // storage is freed when the last object that shares it is released.
+// `shard`: only objects of this partition (pp, tp, ep, etp, expert) are
+// carried; without it every partition of each listed parameter is.
 struct CarryForwardRequest {
     uint32_t rank_id = 0;
     uint64_t rank_epoch = 0;
@@ -674,9 +676,13 @@ struct CarryForwardRequest {
     uint32_t model_role = 0;
     uint64_t from_version = 0, to_version = 0;
     std::vector<uint64_t> param_ids;
+    bool shard = false;
+    uint32_t pp_rank = 0, tp_rank = 0, ep_rank = 0, etp_rank = 0;
+    int32_t expert_id = -1;
 };
 template <class V> void fields(V& v, CarryForwardRequest& m) {
-    v(m.rank_id, m.rank_epoch, m.job, m.model_role, m.from_version, m.to_version, m.param_ids);
+    v(m.rank_id, m.rank_epoch, m.job, m.model_role, m.from_version, m.to_version, m.param_ids, m.shard, m.pp_rank,
+      m.tp_rank, m.ep_rank, m.etp_rank, m.expert_id);
 }
 
 struct CarryForwardResponse {

@@ -193,7 +193,9 @@ SCHEMA: Dict[str, List[Tuple[str, Any]]] = {
     "ExportManifestResponse": STATUS + [("bytes_written", "u64"), ("tensor_count", "u64")],
     "DiscardTensorRequest": [("rank_id", "u32"), ("rank_epoch", "u64"), ("tensor_id", "u64"), ("version", "u64")],
     "CarryForwardRequest": [("rank_id", "u32"), ("rank_epoch", "u64"), ("job", "JobKey"), ("model_role", "u32"),
-                            ("from_version", "u64"), ("to_version", "u64"), ("param_ids", ["u64"])],
+                            ("from_version", "u64"), ("to_version", "u64"), ("param_ids", ["u64"]),
+                            ("shard", "bool"), ("pp_rank", "u32"), ("tp_rank", "u32"), ("ep_rank", "u32"),
+                            ("etp_rank", "u32"), ("expert_id", "i32")],
     "CarryForwardResponse": STATUS + [("carried_count", "u32"), ("existing_count", "u32"), ("missing_count", "u32"),
                                       ("bytes_shared", "u64")],
     "OptionEntry": [("key", S), ("value", S)],

@@ -547,17 +547,25 @@ class Off:
                 "bytes_freed": r["bytes_freed"], "message": r["message"]}
 
     def carry_forward_version(self, model_role, from_version: int, to_version: int,
-                              param_ids: Optional[Sequence[int]] = None) -> dict:
+                              param_ids: Optional[Sequence[int]] = None, *, pp_rank: Optional[int] = None,
+                              tp_rank: Optional[int] = None, ep_rank: int = 0, etp_rank: int = 0,
+                              expert_id: int = -1) -> dict:
         """Make `to_version` objects for unchanged params that share the
         storage (and content hash) of `from_version`'s objects; nothing is
         copied. `param_ids=None` carries every object of `from_version`.
         Keys already present at `to_version` are left alone (`existing`).
+        With `tp_rank` / `pp_rank` only that partition's objects are carried
+        (a TP rank carrying its own shards); without, every partition of each
+        listed parameter is.
         (No reference counterpart: the reference re-evicts every object of
         each version, python_api/state_spectre/__init__.py:575.)"""
+        shard = tp_rank is not None or pp_rank is not None
         r = self._raw(_wire.Op.CARRY_FORWARD, {
             "rank_id": 0, "rank_epoch": 0, "job": self._job(), "model_role": ModelRole.parse(model_role),
             "from_version": int(from_version), "to_version": int(to_version),
-            "param_ids": [int(p) for p in (param_ids or [])]})
+            "param_ids": [int(p) for p in (param_ids or [])], "shard": shard, "pp_rank": int(pp_rank or 0),
+            "tp_rank": int(tp_rank or 0), "ep_rank": int(ep_rank), "etp_rank": int(etp_rank),
+            "expert_id": int(expert_id)})
         if not r["ok"]:
             raise RuntimeError(f"carry_forward failed: {r['message']}")
         return {"carried": r["carried_count"], "existing": r["existing_count"], "missing": r["missing_count"],

@@ -347,11 +347,16 @@ class TrainerWeightSync:
     multicast for two or more replicas when every buffer is VMM-shared on its
     own GPU and the GPUs support it, else p2p. Rollout ranks in other
     processes call ``RolloutWeights.connect`` to take part.
+
+    Several trainer ranks sharing one version (TP / PP shards of one model)
+    pass ``seal_barrier`` (a callable every one of them calls after recording
+    its shard) and ``sealer=True`` on exactly one of them.
     """
 
     def __init__(self, off, params: Dict[str, torch.Tensor], rollout_keys: Sequence[str], mode: str = "bf16",
                  model_role="policy_rollout", persist: bool = True, tp_rank: int = 0, pp_rank: int = 0,
-                 lookup_wait_ms: int = 60000, ctas: int = 0, transport: Optional[str] = None):
+                 lookup_wait_ms: int = 60000, ctas: int = 0, transport: Optional[str] = None,
+                 seal_barrier=None, sealer: bool = True):
         from ..api import ModelRole
         if transport is None:  # the daemon config's nvlink.weight_sync, else auto
             transport = getattr(off, "nvlink_options", {}).get("weight_sync", "auto")
@@ -395,6 +400,9 @@ class TrainerWeightSync:
         self.last_hash: Dict[str, Tuple[int, int]] = {}
         self.last_version: Optional[int] = None
         self._pids: Dict[str, int] = {}
+        self._pending = None  # (version, changed names, hashes) between push_version and seal_version
+        self.seal_barrier = seal_barrier
+        self.sealer = sealer
 
     def _choose(self, transport: str, descs) -> str:
         if transport == "p2p":
@@ -431,13 +439,25 @@ class TrainerWeightSync:
         return e0, e1
 
     def publish_version(self, version: int, changed: Optional[Sequence[str]] = None) -> dict:
-        """Push and (with ``persist``) seal version ``version``.
+        """Push and (with ``persist``) seal version ``version``: ``push_version``
+        followed by ``seal_version``.
 
         Without ``changed`` every parameter is hashed on the device and the
         changed set is found by comparing content hashes with the previous
         version (the manifest diff). With ``changed`` (names the caller
         updated) only those parameters are hashed and pushed; the others keep
         their previous hashes. The first version always covers everything."""
+        out = self.push_version(version, changed)
+        out.update(self.seal_version())
+        return out
+
+    def push_version(self, version: int, changed: Optional[Sequence[str]] = None) -> dict:
+        """The NVLink half of ``publish_version``: push the changed chunks into
+        every rollout buffer and find the changed parameters. When it returns
+        the rollout holds version ``version``; ``seal_version`` records it in
+        offloadd and may run while the rollout checks what it received."""
+        if self._pending is not None:
+            raise RuntimeError(f"version {self._pending[0]} was pushed but not sealed")
         t0 = time.perf_counter()
         hint = None if (changed is None or self.last_version is None) else list(changed)
         e0, e1 = self.push(hint)
@@ -447,28 +467,45 @@ class TrainerWeightSync:
         if res["error"]:
             raise RuntimeError(f"weight push failed with device status {res['error']}")
         hashes = self.pushers[0].hashes() if self.pushers else {}
-        changed = [n for n in self.params if self.last_hash.get(n) != hashes.get(n)]
-        t_push = time.perf_counter()
-        out = {"version": version, "changed": len(changed), "push_ms": push_ms,
-               "push_wall_ms": (t_push - t0) * 1e3}
+        names = [n for n in self.params if self.last_hash.get(n) != hashes.get(n)]
+        self._pending = (version, names, hashes)
+        return {"version": version, "changed": len(names), "push_ms": push_ms,
+                "push_wall_ms": (time.perf_counter() - t0) * 1e3}
+
+    def seal_version(self) -> dict:
+        """Record the pushed version in offloadd (``persist``): changed
+        parameters are copied to the host as new canonical objects, this
+        shard's unchanged ones are carried forward from the previous version,
+        and the version is sealed and promoted. With several trainer ranks per
+        version (``seal_barrier``), every rank records its shard first and the
+        ``sealer`` rank then seals."""
+        if self._pending is None:
+            raise RuntimeError("seal_version without a pushed version")
+        version, changed, hashes = self._pending
+        t0 = time.perf_counter()
+        out = {}
         if self.persist:
-            handles = []
             carry = self.last_version is not None
             for n in (changed if carry else self.params):
-                handles.append(self.off.canonical_evict(self.params[n], self._key(n, version), destructive=False,
-                                                        wait=False, stream=self.stream))
+                self.off.canonical_evict(self.params[n], self._key(n, version), destructive=False, wait=False,
+                                         stream=self.stream)
             if carry:
                 unchanged = [self._pids[n] if n in self._pids else self._key(n, version).param_id
                              for n in self.params if n not in changed]
                 if unchanged:
-                    self.off.carry_forward_version(self.role, self.last_version, version, unchanged)
+                    self.off.carry_forward_version(self.role, self.last_version, version, unchanged,
+                                                   tp_rank=self.tp_rank, pp_rank=self.pp_rank)
             self.stream.synchronize()
             self.off._agent.synchronize()
-            self.off.promote_rollout_version(version) if self.role == 2 else \
-                self.off.seal_model_version(self.role, version)
-            out["seal_wall_ms"] = (time.perf_counter() - t_push) * 1e3
+            if self.seal_barrier is not None:
+                self.seal_barrier()
+            if self.sealer:
+                self.off.promote_rollout_version(version) if self.role == 2 else \
+                    self.off.seal_model_version(self.role, version)
+            out["seal_wall_ms"] = (time.perf_counter() - t0) * 1e3
         self.last_hash = hashes
         self.last_version = version
+        self._pending = None
         return out
 
     def close(self) -> None:

@@ -408,3 +408,40 @@ quotas:
             assert js["inflight_d2h_bytes"] == 0  # settled at commit
     finally:
         d.stop()
+
+
+def test_carry_forward_of_one_tensor_parallel_shard(sock_path):
+    """Two TP ranks hold shards of the same parameters (same param_id): each
+    carries forward only its own partition, so a version where rank 0 changed
+    "w" and rank 1 did not has rank 0's new object and rank 1's old one."""
+    d = in_process_daemon(socket=sock_path, arena_mb=128, drain_on_complete=False)
+    try:
+        shards = {0: torch.randn(4096), 1: torch.randn(4096)}
+        with session(sock_path, 0) as off:
+            def key(v, r, t):
+                return off.canonical_key(model_role=ROLL, model_version=v, param_name="w", tensor=t, tp_rank=r)
+
+            for r, t in shards.items():
+                off.canonical_evict(t.clone(), key(1, r, t))
+            off.promote_rollout_version(1)
+            new0 = shards[0] + 1
+            off.canonical_evict(new0.clone(), key(2, 0, new0))            # rank 0 changed w
+            pid = key(2, 1, shards[1]).param_id
+            c1 = off.carry_forward_version(ROLL, 1, 2, [pid], tp_rank=1)  # rank 1 did not
+            assert c1["carried"] == 1 and c1["existing"] == 0
+            c0 = off.carry_forward_version(ROLL, 1, 2, [pid], tp_rank=0)  # rank 0 already has its v2 object
+            assert c0["carried"] == 0 and c0["existing"] == 1
+            off.promote_rollout_version(2)
+            c = RolloutWeightClient(sock_path, off.job_id, off.launch_epoch)
+            res = c.sync_latest()
+            man = c.get_manifest(2)
+            by_tp = {e["key"]["tp_rank"]: e["object_id"] for e in man["tensors"]}
+            assert sorted(by_tp) == [0, 1]
+            assert res["data"][by_tp[0]] == new0.numpy().tobytes()
+            assert res["data"][by_tp[1]] == shards[1].numpy().tobytes()
+            c.close()
+            # without a shard filter every partition of the parameter is carried
+            everything = off.carry_forward_version(ROLL, 2, 3, [pid])
+            assert everything["carried"] == 2
+    finally:
+        d.stop()
