@@ -467,11 +467,15 @@ def run_weight_sync(args, world: int, rank: int, local_rank: int, device, state_
             go.fill_(v)
             dist.send(go, peer)
             dist.recv(go, peer)  # the rollout's answer
+            if int(go.item()) != 1:  # .item(): an NCCL recv only orders the stream, the host waits here
+                raise RuntimeError(f"reference rollout pulled nothing for version {v}")
             dist.barrier(group=trainer_group)
             if tp_rank == 0 and v > 1:
                 off.drop_canonical_version("policy_rollout", v - 1)
         else:
             dist.recv(go, peer)
+            if int(go.item()) != v:  # wait on the host for the trainer's promote of version v
+                raise RuntimeError(f"rollout expected version {v}, trainer announced {int(go.item())}")
             man = client.get_manifest(v, {"tp": tp_rank})
             changed = {e["object_id"] for e in client.diff_local(man)}
             pulled = 0

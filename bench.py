@@ -110,6 +110,9 @@ def parse():
     p.add_argument("--pinned-gb", type=int, default=0, help="kv_cache: pinned window per GPU (0 = fits the set)")
     p.add_argument("--kv-group-mb", type=int, default=0, help="kv_cache: bytes per reservation group (0 = 256 MiB)")
     p.add_argument("--nvme-dir", default="", help="dp_dedup: NVMe spill directory")
+    p.add_argument("--dedup-mode", default="p2p_verified",
+                   choices=["p2p_verified", "device_hash_verified", "semantic_trusted", "hash_verified"],
+                   help="dp_dedup: how replicas confirm the owner's copy")
     p.add_argument("--spill-timeout", type=float, default=600.0, help="dp_dedup: seconds to wait for the spill")
     return p.parse_args()
 

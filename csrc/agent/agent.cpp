@@ -1411,10 +1411,11 @@ CanonicalOutcome Agent::canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHan
     if (!resp.ok) return out;
     cudaStream_t s = D.stream_of(stream);
 
-    if (resp.action == offload_v2::ATTACH_ACTION_ATTACHED_EXISTING ||
-        resp.action == offload_v2::ATTACH_ACTION_WAIT_FOR_CREATOR) {
+    const bool attached = resp.action == offload_v2::ATTACH_ACTION_ATTACHED_EXISTING ||
+                          resp.action == 7 /* attached after a peer byte compare */;
+    if (attached || resp.action == offload_v2::ATTACH_ACTION_WAIT_FOR_CREATOR) {
         out.ok = true;
-        if (resp.action == offload_v2::ATTACH_ACTION_ATTACHED_EXISTING && destructive && on_invalidate) {
+        if (attached && destructive && on_invalidate) {
             if (D.gpu) CUDA_OK(cudaStreamSynchronize(s));  // producer kernels done before the storage goes
             on_invalidate();
         }

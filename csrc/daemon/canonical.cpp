@@ -13,7 +13,10 @@
 // Additions of this runtime: dedup mode 4 ("device_hash_verified") answers an
 // existing object with action 6 (verify-hash-only): the replica hashes its own
 // GPU copy and commits the hash with lease 0, so no pinned slot is reserved and
-// no byte crosses PCIe for verification.
+// no byte crosses PCIe for verification. Mode 5 ("p2p_verified") is for a
+// replica that already compared its bytes with the owner's GPU copy over
+// NVLink (K3, statespectre_b200.parallel.dp_dedup): an existing object is
+// attached at once and answered with action 7.
 #include <cstring>
 
 #include "daemon.h"
@@ -228,6 +231,16 @@ RequestCanonicalEvictResponse Daemon::on_canonical_evict(const RequestCanonicalE
     if (existing && readable(existing->state)) {
         if (!r.attach_if_exists) {
             resp.message = "exists but attach disabled";
+            return resp;
+        }
+        if (mode == kDedupP2PVerified) {
+            attach(*existing);
+            Metrics::get().add(M::kCanonicalD2HBytesAvoided, r.key.nbytes);
+            Metrics::get().inc(M::kCanonicalP2PVerified);
+            resp.ok = true;
+            resp.action = kActionVerifiedByP2P;
+            resp.object_id = existing->object_id;
+            resp.message = "attached after peer byte compare";
             return resp;
         }
         if (mode == kDedupDeviceHashVerified) {

@@ -245,6 +245,7 @@ uint32_t dedup_mode_of(const std::string& s) {
     if (s == "hash_verified") return 2;
     if (s == "sampled_hash") return 3;
     if (s == "device_hash_verified") return 4;
+    if (s == "p2p_verified") return 5;
     return 1;
 }
 uint32_t transport_of(const std::string& s) {

@@ -55,6 +55,10 @@ inline bool is_candidate_tid(uint64_t t) { return (t & (kCanonicalTidBit | kCand
 // Extension values (outside the interoperable enum ranges).
 constexpr uint32_t kDedupDeviceHashVerified = 4;     // DedupMode extension
 constexpr uint32_t kActionVerifyHashOnly = 6;        // AttachCreateAction extension
+// Mode 5: the replica compared its bytes with the owner's GPU copy over NVLink
+// (K3) before asking; an existing object is attached and answered with 7.
+constexpr uint32_t kDedupP2PVerified = 5;            // DedupMode extension
+constexpr uint32_t kActionVerifiedByP2P = 7;         // AttachCreateAction extension
 
 struct JobUID {
     uint64_t tenant_id = 0, job_id = 0, launch_epoch = 0;

@@ -7,22 +7,37 @@
 // CPU computes the identical value (this header is the host oracle; the CUDA
 // kernels include the same functions).
 //
-// Definition (all integers little-endian):
+// Definition (all integers little-endian; arithmetic modulo 2^32 on u32 and
+// 2^64 on u64; rotl = rotate left):
+//   Constants (xxHash32 primes, Y. Collet, xxHash specification):
+//     P1 = 2654435761, P2 = 2246822519, P3 = 3266489917, P4 = 668265263,
+//     P5 = 374761393; G = 0x9E3779B97F4A7C15 (64-bit golden ratio).
+//   fmix64(k) (MurmurHash3 finalizer, A. Appleby): k ^= k >> 33;
+//     k *= 0xff51afd7ed558ccd; k ^= k >> 33; k *= 0xc4ceb9fe1a85ec53; k ^= k >> 33.
+//   fold(a, b) = fmix64(a ^ (b * G)).
+//   avalanche32(h) (xxHash32): h ^= h >> 15; h *= P2; h ^= h >> 13; h *= P3;
+//     h ^= h >> 16.
 //   * Bytes are split into chunks of 64 KiB; the last chunk may be short.
-//   * A chunk is a sequence of 16-byte vectors (the final vector zero-padded).
-//     Vector v belongs to lane (v mod 256); lane t sees vectors t, t+256, ...
-//   * Each lane keeps four 32-bit accumulators seeded from the lane index and
-//     applies the xxHash32 round (Y. Collet, xxHash specification):
-//     acc = rotl32(acc + word * P2, 13) * P1, one accumulator per 32-bit word.
-//   * A lane's 64-bit digest combines its accumulators (xxHash32 merge and
-//     avalanche for the low half, a rotate-xor for the high half).
-//   * The 256 lane digests are reduced by a binary tree: at distance s = 1, 2,
-//     ..., 128, entry i (bit s clear) becomes fold(x[i], x[i+s]) where fold is
-//     MurmurHash3's fmix64 (A. Appleby) applied to x[i] ^ (x[i+s] * golden).
-//     Chunk digest = fold(tree root, chunk length in bytes).
-//   * Object hash: lo = FNV-style multiply fold of the chunk digests finished
-//     with fmix64(.. ^ nbytes); hi = rotate-multiply fold with a different seed
-//     finished the same way. (0, 0) is reserved for "no hash" and maps to (1, 0).
+//   * A chunk is a sequence of 16-byte vectors of four u32 words w0..w3 (the
+//     final vector zero-padded to 16 bytes). Vector v belongs to lane
+//     (v mod 256); lane t sees vectors t, t+256, ..., at most 16 of them, in
+//     that order. Lanes past the chunk's last vector see none.
+//   * Lane t starts from seed = t * P5 + 0x9E3779B9 with accumulators
+//     (a0, a1, a2, a3) = (seed + P1 + P2, seed + P2, seed, seed - P1) and, per
+//     vector, applies the xxHash32 round to each word:
+//     ai = rotl32(ai + wi * P2, 13) * P1.
+//   * Lane digest (u64) = hi << 32 | lo, with
+//     lo = avalanche32((rotl32(a0,1) + rotl32(a1,7) + rotl32(a2,12) + rotl32(a3,18)) ^ (t * P3)),
+//     hi = avalanche32((rotl32(a0,3) ^ rotl32(a1,11) ^ rotl32(a2,17) ^ rotl32(a3,25)) + P4 + t).
+//   * The 256 lane digests x[0..255] are reduced by a binary tree: for
+//     s = 1, 2, 4, ..., 128, every i that is a multiple of 2s becomes
+//     fold(x[i], x[i + s]); the root is x[0].
+//     Chunk digest = fold(root, chunk length in bytes).
+//   * Object hash of n bytes with chunk digests d0, d1, ...: start from
+//     lo = 0xcbf29ce484222325, hi = 0x6a09e667f3bcc909; for each digest d in
+//     order: lo = (lo ^ d) * 0x100000001b3; hi = rotl64(hi ^ d, 29) * G +
+//     0x94d049bb133111eb. Result (fmix64(lo ^ n), fmix64(hi + n)); (0, 0) is
+//     reserved for "no hash" and maps to (1, 0).
 #pragma once
 
 #include <cstdint>

@@ -81,7 +81,8 @@ namespace ofld {
     X(kRingCompletionsApplied, "ring_completions_applied_total")                 \
     X(kVersionsPersisted, "versions_persisted_total")                          \
     X(kPersistedBytes, "persisted_bytes_total")                                \
-    X(kVersionsRecovered, "versions_recovered_total")
+    X(kVersionsRecovered, "versions_recovered_total")                          \
+    X(kCanonicalP2PVerified, "canonical_p2p_verified_total")
 
 enum class M : int {
 #define OFLD_ENUM(id, name) id,

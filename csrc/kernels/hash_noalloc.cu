@@ -23,7 +23,7 @@
 // Contract:
 //   int ofld_hash_noalloc(const void* src, uint64_t nbytes, uint64_t* out, cudaStream_t stream)
 //     src    device pointer to the bytes to hash (any alignment)
-//     nbytes at most OFLD_NOALLOC_MAX_BYTES (8 GiB)
+//     nbytes at most OFLD_NOALLOC_MAX_BYTES (8 GiB; ofld/hash_noalloc.h)
 //     out    device pointer receiving two uint64 values {lo, hi}
 //     stream the stream both kernels are enqueued on
 //   returns 0 on success (the hash is in `out` once the stream reaches it), or
@@ -34,18 +34,25 @@
 //
 // The scratch array. `g_digest_scratch` below is 1 MiB of device memory per
 // GPU that loads this library, held until the process exits: 131072 chunk
-// digests, hence the 8 GiB limit. Host code cannot pass the array's name to a
-// kernel (on the host the symbol is only a stand-in, not a device address), so
-// the first call on each device, with that device current, resolves the
-// address once with cudaGetSymbolAddress and caches it; make that first call
-// before any stream capture. Every call shares the array and it keeps the last
-// call's contents: calls that overlap on the GPU (different streams, or
-// different host threads on the same device) race on it and must be ordered by
-// the caller. Nothing in the array needs to start at zero: each call writes
+// digests, hence the OFLD_NOALLOC_MAX_BYTES limit of 8 GiB. Host code cannot
+// pass the array's name to a kernel (on the host the symbol is only a
+// stand-in, not a device address), so the first call in each CUDA context
+// (normally: on each device), with that device current, resolves the address
+// with cudaGetSymbolAddress, checks the result and keeps it for later calls in
+// the same context; make that first call before any stream capture. The
+// address is keyed by the context's unique id, so a new context on the same
+// device (after cudaDeviceReset, or a non-primary context) resolves it again
+// instead of reusing a stale one. Every call shares the array and it keeps the
+// last call's contents: calls that overlap on the GPU (different streams, or
+// different host threads on the same device) race on it and must be ordered
+// by the caller. Nothing in the array needs to start at zero: each call writes
 // every digest it reads.
 //
 // The two kernels are the library's own hash and fold kernels; their output
 // is identical to hash_device + fold_digests and to the host oracle.
+#include "ofld/hash_noalloc.h"
+
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -56,34 +63,77 @@
 namespace {
 
 constexpr uint64_t kMaxDigests = (1ull << 20) / sizeof(uint64_t);  // 1 MiB of digests
-constexpr uint64_t kMaxBytes = kMaxDigests * 65536ull;               // 8 GiB
-constexpr int kMaxDevices = 64;
+static_assert(kMaxDigests * 65536ull == OFLD_NOALLOC_MAX_BYTES, "limit matches the array");
 
 static __device__ __align__(256) uint64_t g_digest_scratch[kMaxDigests];
 
+// Driver entry points for the current context's id (no link-time libcuda).
+struct CtxApi {
+    decltype(&cuCtxGetCurrent) get_current = nullptr;
+    decltype(&cuCtxGetId) get_id = nullptr;
+};
+
+const CtxApi& ctx_api() {
+    static CtxApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            api.get_current = reinterpret_cast<decltype(api.get_current)>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            api.get_id = reinterpret_cast<decltype(api.get_id)>(p);
+    });
+    return api;
+}
+
+// Unique id of the current context (0 when it cannot be read: no caching then).
+unsigned long long current_ctx_id() {
+    const CtxApi& api = ctx_api();
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!api.get_current || !api.get_id || api.get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+    if (api.get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+constexpr int kCacheEntries = 16;
+struct CacheEntry {
+    unsigned long long ctx_id = 0;
+    uint64_t* addr = nullptr;
+};
 std::mutex g_mu;
-uint64_t* g_scratch_addr[kMaxDevices] = {nullptr};
+CacheEntry g_cache[kCacheEntries];
+int g_next = 0;
+
+uint64_t* scratch_address() {
+    const unsigned long long id = current_ctx_id();
+    std::lock_guard<std::mutex> g(g_mu);
+    if (id)
+        for (const CacheEntry& e : g_cache)
+            if (e.ctx_id == id) return e.addr;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_digest_scratch) != cudaSuccess || !p) return nullptr;
+    if (id) {
+        g_cache[g_next] = CacheEntry{id, static_cast<uint64_t*>(p)};
+        g_next = (g_next + 1) % kCacheEntries;
+    }
+    return static_cast<uint64_t*>(p);
+}
 
 }  // namespace
 
 extern "C" __attribute__((visibility("default"))) int ofld_hash_noalloc(const void* src, uint64_t nbytes,
                                                                         uint64_t* out, cudaStream_t stream) {
-    if (nbytes > kMaxBytes) return 1;
-    if (!out || (nbytes > 0 && !src)) return 2;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 3;
-    uint64_t* scratch = nullptr;
-    {
-        std::lock_guard<std::mutex> g(g_mu);
-        if (!g_scratch_addr[dev]) {
-            void* p = nullptr;
-            if (cudaGetSymbolAddress(&p, g_digest_scratch) != cudaSuccess || !p) return 3;
-            g_scratch_addr[dev] = static_cast<uint64_t*>(p);
-        }
-        scratch = g_scratch_addr[dev];
-    }
+    if (nbytes > OFLD_NOALLOC_MAX_BYTES) return OFLD_NOALLOC_TOO_LARGE;
+    if (!out || (nbytes > 0 && !src)) return OFLD_NOALLOC_NULL_ARG;
+    uint64_t* scratch = scratch_address();
+    if (!scratch) return OFLD_NOALLOC_NO_SCRATCH;
     const uint64_t nchunks = ofld::kern::digest_count(nbytes);
-    if (nbytes > 0 && ofld::kern::hash_device(src, nbytes, scratch, stream, 0) != cudaSuccess) return 4;
-    if (ofld::kern::fold_digests(scratch, nchunks, nbytes, out, stream) != cudaSuccess) return 4;
-    return 0;
+    if (nbytes > 0 && ofld::kern::hash_device(src, nbytes, scratch, stream, 0) != cudaSuccess)
+        return OFLD_NOALLOC_LAUNCH;
+    if (ofld::kern::fold_digests(scratch, nchunks, nbytes, out, stream) != cudaSuccess) return OFLD_NOALLOC_LAUNCH;
+    return OFLD_NOALLOC_OK;
 }

@@ -41,13 +41,6 @@ struct LaunchCfg {
 // gpu_launches). Monotonic per process.
 uint64_t launch_count();
 
-// Instruction forms used for host-mapped traffic (process-wide):
-//   load_form  0: ld.global.nc.L1::no_allocate   1: same + .L2::256B prefetch
-//              2: ld.global.L2::128B
-//   store_form 0: st.global.cs   1: st.global   2: st.global.wt
-void set_access_policy(int load_form, int store_form);
-int access_policy();
-
 // K1. `digests` (may be null) receives ceil(nbytes/64KiB) chunk digests and
 // must be device-accessible (device or host-mapped memory).
 cudaError_t evict_hash(const void* src_dev, void* dst_mapped, uint64_t nbytes, uint64_t* digests,

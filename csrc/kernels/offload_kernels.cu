@@ -50,43 +50,9 @@ __device__ __forceinline__ uint4 ld_once(const void* p) {
     return v;
 }
 
-// Memory-access policy (uniform kernel argument): low nibble selects the
-// load form, high nibble the store form. Host-mapped traffic crosses PCIe,
-// where request sizes matter more than cache behaviour.
-//   load 0: ld.global.nc.L1::no_allocate      load 1: ... + .L2::256B prefetch
-//   load 2: ld.global.L2::128B (coherent path)
-//   store 0: st.global.cs   store 1: st.global (write-back)   store 2: st.global.wt
-__device__ __forceinline__ uint4 ld_policy(const void* p, int pol) {
-    uint4 v;
-    if ((pol & 15) == 1) {
-        asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                     : "l"(p));
-    } else if ((pol & 15) == 2) {
-        asm volatile("ld.global.L2::128B.v4.u32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                     : "l"(p));
-    } else {
-        v = ld_once(p);
-    }
-    return v;
-}
-
 __device__ __forceinline__ void st_stream(void* p, uint4 v) {
     asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
-}
-
-__device__ __forceinline__ void st_policy(void* p, uint4 v, int pol) {
-    int s = (pol >> 4) & 15;
-    if (s == 1)
-        asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                     : "memory");
-    else if (s == 2)
-        asm volatile("st.global.wt.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                     : "memory");
-    else
-        st_stream(p, v);
 }
 
 __device__ __forceinline__ uint4 ld_bytes(const uint8_t* p, uint32_t n) {
@@ -101,15 +67,15 @@ __device__ __forceinline__ void st_bytes(uint8_t* p, uint4 v, uint32_t n) {
 }
 
 template <bool ALIGNED>
-__device__ __forceinline__ uint4 load_vec(const uint8_t* p, uint32_t n, int pol = 0) {
-    if (ALIGNED && n == 16) return ld_policy(p, pol);
+__device__ __forceinline__ uint4 load_vec(const uint8_t* p, uint32_t n) {
+    if (ALIGNED && n == 16) return ld_once(p);
     return ld_bytes(p, n);
 }
 
 template <bool ALIGNED>
-__device__ __forceinline__ void store_vec(uint8_t* p, uint4 v, uint32_t n, int pol = 0) {
+__device__ __forceinline__ void store_vec(uint8_t* p, uint4 v, uint32_t n) {
     if (ALIGNED && n == 16)
-        st_policy(p, v, pol);
+        st_stream(p, v);
     else
         st_bytes(p, v, n);
 }
@@ -144,7 +110,7 @@ __device__ __forceinline__ uint64_t tree_fold(uint64_t d, uint64_t* red) {
 template <bool ALIGNED, bool HASH, bool STORE>
 __global__ void __launch_bounds__(kThreads, 2)
     k_evict(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
-            uint64_t* __restrict__ digests, int pol, KernelStamp* ks) {
+            uint64_t* __restrict__ digests, KernelStamp* ks) {
     StampScope stamp_scope_(ks);
     __shared__ uint64_t red[kThreads / 32];
     const uint32_t t = threadIdx.x;
@@ -166,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint32_t vi = uint32_t(k) * kThreads + t;
             if (vi < nvec) {
                 if (HASH) ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
-                if (STORE) store_vec<ALIGNED>(dst + base + uint64_t(vi) * 16, v[k], min(16u, len - vi * 16), pol);
+                if (STORE) store_vec<ALIGNED>(dst + base + uint64_t(vi) * 16, v[k], min(16u, len - vi * 16));
             }
         }
         if (HASH) {
@@ -215,7 +181,7 @@ __device__ __forceinline__ uint2 quant8(uint4 v, bool valid, float* scale_out) {
 template <bool ALIGNED, bool VERIFY, int CAST>
 __global__ void __launch_bounds__(kThreads, 2)
     k_restore(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
-              float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, int pol, KernelStamp* ks) {
+              float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, KernelStamp* ks) {
     StampScope stamp_scope_(ks);
     __shared__ uint64_t red[kThreads / 32];
     const uint32_t t = threadIdx.x;
@@ -229,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int k = 0; k < kVecs; ++k) {
             const uint32_t vi = uint32_t(k) * kThreads + t;
             const uint32_t n = vi < nvec ? min(16u, len - vi * 16) : 0u;
-            v[k] = n ? load_vec<ALIGNED>(src + base + uint64_t(vi) * 16, n, pol) : make_uint4(0, 0, 0, 0);
+            v[k] = n ? load_vec<ALIGNED>(src + base + uint64_t(vi) * 16, n) : make_uint4(0, 0, 0, 0);
         }
         ssh::Lane L = ssh::lane_init(t);
 #pragma unroll
@@ -384,7 +350,7 @@ constexpr uint32_t kZStage = zbf16::kChunk;
 // 16-byte vector stores. `src`/`dst` point at the chunk; 16-byte aligned,
 // len % 16 == 0. Every thread of the block calls this.
 __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
-                                              uint32_t len, bool raw, uint32_t eb, uint64_t* digest_out, int pol,
+                                              uint32_t len, bool raw, uint32_t eb, uint64_t* digest_out,
                                               uint64_t* red, uint32_t* sc, uint8_t* zbuf) {
     const uint32_t t = threadIdx.x;
     const uint32_t nvec = len / 16;
@@ -392,7 +358,7 @@ __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, u
 #pragma unroll
     for (int k = 0; k < kVecs; ++k) {
         const uint32_t vi = uint32_t(k) * kThreads + t;
-        v[k] = vi < nvec ? ld_policy(src + uint64_t(vi) * 16, 0) : make_uint4(0, 0, 0, 0);
+        v[k] = vi < nvec ? ld_once(src + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
     }
     ssh::Lane L = ssh::lane_init(t);
     uint32_t cnt = 0;
@@ -402,7 +368,7 @@ __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, u
         if (vi < nvec) {
             ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
             if (raw) {
-                st_policy(dst + uint64_t(vi) * 16, v[k], pol);
+                st_stream(dst + uint64_t(vi) * 16, v[k]);
             } else {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
@@ -441,7 +407,7 @@ __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, u
         __syncthreads();
         const uint32_t nout = (comp + 15) / 16;  // <= len / 16: coded chunks fit their raw length
         for (uint32_t i = t; i < nout; i += kThreads)
-            st_policy(dst + uint64_t(i) * 16, *reinterpret_cast<const uint4*>(zbuf + i * 16), pol);
+            st_stream(dst + uint64_t(i) * 16, *reinterpret_cast<const uint4*>(zbuf + i * 16));
     }
     uint64_t root = tree_fold(ssh::lane_digest(L, t), red);  // also orders zbuf reuse
     if (t == 0 && digest_out) *digest_out = ssh::chunk_finish(root, len);
@@ -451,7 +417,7 @@ __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, u
 // nbytes % 16 == 0 (zbf16::eligible).
 __global__ void __launch_bounds__(kThreads, 2)
     k_evict_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
-              const uint8_t* __restrict__ ebase, uint64_t* __restrict__ digests, int pol, KernelStamp* ks) {
+              const uint8_t* __restrict__ ebase, uint64_t* __restrict__ digests, KernelStamp* ks) {
     StampScope stamp_scope_(ks);
     extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint64_t red[kThreads / 32];
@@ -462,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
         const bool raw = zbf16::raw_by_rule(c, nchunks, len);
         const uint32_t eb = raw ? 0u : uint32_t(ebase[c]);
-        evict_chunk_z(src + base, dst + base, len, raw, eb, digests ? digests + c : nullptr, pol, red, sc, zbuf);
+        evict_chunk_z(src + base, dst + base, len, raw, eb, digests ? digests + c : nullptr, red, sc, zbuf);
     }
 }
 
@@ -499,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 3)
 // K1 over a batch: one grid walks every chunk of every job (raw or coded per
 // job), so many small tensors (KV-cache blocks) cost one launch.
 __global__ void __launch_bounds__(kThreads, 2)
-    k_evict_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, int pol, KernelStamp* ks) {
+    k_evict_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, KernelStamp* ks) {
     StampScope stamp_scope_(ks);
     extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint64_t red[kThreads / 32];
@@ -514,13 +480,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         const bool raw = !j.ebase || zbf16::raw_by_rule(lc, nch, len);
         const uint32_t eb = raw ? 0u : uint32_t(j.ebase[lc]);
         evict_chunk_z(static_cast<const uint8_t*>(j.src) + base, static_cast<uint8_t*>(j.dst) + base, len, raw, eb,
-                      j.digests ? j.digests + lc : nullptr, pol, red, sc, zbuf);
+                      j.digests ? j.digests + lc : nullptr, red, sc, zbuf);
     }
 }
 
 // Loads [lo, hi) of a host-mapped chunk into the stage with 16-byte vectors,
 // up to 13 in flight per thread (one full coded chunk plus 1 KiB of escapes).
-__device__ __forceinline__ void stage_in(const uint8_t* in, uint8_t* zbuf, uint32_t lo, uint32_t hi, int pol) {
+__device__ __forceinline__ void stage_in(const uint8_t* in, uint8_t* zbuf, uint32_t lo, uint32_t hi) {
     constexpr int kPer = 13;
     const uint32_t t = threadIdx.x;
     const uint32_t v0 = lo / 16, v1 = (hi + 15) / 16;
@@ -529,7 +495,7 @@ __device__ __forceinline__ void stage_in(const uint8_t* in, uint8_t* zbuf, uint3
 #pragma unroll
         for (int k = 0; k < kPer; ++k) {
             const uint32_t i = b + uint32_t(k) * kThreads + t;
-            r[k] = i < v1 ? ld_policy(in + uint64_t(i) * 16, pol) : make_uint4(0, 0, 0, 0);
+            r[k] = i < v1 ? ld_once(in + uint64_t(i) * 16) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int k = 0; k < kPer; ++k) {
@@ -544,7 +510,7 @@ __device__ __forceinline__ void stage_in(const uint8_t* in, uint8_t* zbuf, uint3
 // 16-byte loads (header, planes and, speculatively, 1 KiB of escapes in one
 // round trip; the rest of the escapes in a second one when present); raw
 // chunks load straight into registers. Every thread of the block calls this.
-__device__ __forceinline__ void load_chunk_z(const uint8_t* __restrict__ in, uint32_t len, bool raw, int pol,
+__device__ __forceinline__ void load_chunk_z(const uint8_t* __restrict__ in, uint32_t len, bool raw,
                                              uint32_t* sc, uint8_t* zbuf, uint4 (&v)[kVecs]) {
     const uint32_t t = threadIdx.x;
     const uint32_t nvec = len / 16;
@@ -552,19 +518,19 @@ __device__ __forceinline__ void load_chunk_z(const uint8_t* __restrict__ in, uin
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) {
             const uint32_t vi = uint32_t(k) * kThreads + t;
-            v[k] = vi < nvec ? ld_policy(in + uint64_t(vi) * 16, pol) : make_uint4(0, 0, 0, 0);
+            v[k] = vi < nvec ? ld_once(in + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
         }
         return;
     }
     const uint32_t n = len / 2;
     const uint32_t fixed = zbf16::kHeader + n + n / 2;
     const uint32_t spec = min(len, fixed + 1024u);
-    stage_in(in, zbuf, 0, spec, pol);
+    stage_in(in, zbuf, 0, spec);
     __syncthreads();
     const uint4 hd = *reinterpret_cast<const uint4*>(zbuf);
     const uint32_t comp = min(hd.w, len);
     if (comp > spec) {  // uniform: every thread read the same header
-        stage_in(in, zbuf, spec / 16 * 16, comp, pol);
+        stage_in(in, zbuf, spec / 16 * 16, comp);
         __syncthreads();
     }
     const uint32_t eb = hd.x >> 24;
@@ -610,7 +576,7 @@ __device__ __forceinline__ void load_chunk_z(const uint8_t* __restrict__ in, uin
 template <bool VERIFY, int CAST>
 __global__ void __launch_bounds__(kThreads, 2)
     k_restore_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
-                float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, int pol, KernelStamp* ks) {
+                float* __restrict__ scales, const uint64_t* __restrict__ expect, uint32_t* mismatch, KernelStamp* ks) {
     StampScope stamp_scope_(ks);
     extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint64_t red[kThreads / 32];
@@ -622,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
         const uint32_t nvec = len / 16;
         uint4 v[kVecs];
-        load_chunk_z(src + base, len, zbf16::raw_by_rule(c, nchunks, len), pol, sc, zbuf, v);
+        load_chunk_z(src + base, len, zbf16::raw_by_rule(c, nchunks, len), sc, zbuf, v);
         ssh::Lane L = ssh::lane_init(t);
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) {
@@ -660,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // K2 over a batch (no cast, no verification): one grid for every chunk of
 // every job, raw or coded per job.
 __global__ void __launch_bounds__(kThreads, 2)
-    k_restore_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, int pol, KernelStamp* ks) {
+    k_restore_jobs(const XferJob* __restrict__ jobs, int njobs, uint64_t total_chunks, KernelStamp* ks) {
     StampScope stamp_scope_(ks);
     extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint32_t sc[kThreads / 32];
@@ -674,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t len = uint32_t(j.nbytes - base < kChunk ? j.nbytes - base : kChunk);
         const bool raw = !j.coded || zbf16::raw_by_rule(lc, nch, len);
         uint4 v[kVecs];
-        load_chunk_z(static_cast<const uint8_t*>(j.src) + base, len, raw, pol, sc, zbuf, v);
+        load_chunk_z(static_cast<const uint8_t*>(j.src) + base, len, raw, sc, zbuf, v);
         uint8_t* out = static_cast<uint8_t*>(j.dst) + base;
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) {
@@ -792,29 +758,20 @@ int grid_for(uint64_t nbytes, int ctas, int dflt) {
 
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed) + push_launch_count(); }
 
-namespace {
-// Process-wide access policy for host-mapped traffic (see ld_policy/st_policy).
-std::atomic<int> g_policy{0};
-}  // namespace
-
-void set_access_policy(int load_form, int store_form) { g_policy.store((load_form & 15) | ((store_form & 15) << 4)); }
-int access_policy() { return g_policy.load(); }
-
 cudaError_t evict_hash(const void* src, void* dst, uint64_t nbytes, uint64_t* digests, cudaStream_t s, int ctas) {
     if (nbytes == 0) return cudaSuccess;
     if (!src || !dst) return cudaErrorInvalidValue;
     const int g = grid_for(nbytes, ctas, 48);
     const bool al = aligned16(src) && aligned16(dst);
-    const int pol = g_policy.load(std::memory_order_relaxed);
     KernelStamp* ks = timing_take(kIdEvict, nbytes);
     auto S = static_cast<const uint8_t*>(src);
     auto D = static_cast<uint8_t*>(dst);
     if (digests) {
-        if (al) k_evict<true, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests, pol, ks);
-        else k_evict<false, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests, pol, ks);
+        if (al) k_evict<true, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests, ks);
+        else k_evict<false, true, true><<<g, kThreads, 0, s>>>(S, D, nbytes, digests, ks);
     } else {
-        if (al) k_evict<true, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, pol, ks);
-        else k_evict<false, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, pol, ks);
+        if (al) k_evict<true, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, ks);
+        else k_evict<false, false, true><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, ks);
     }
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
@@ -836,8 +793,8 @@ cudaError_t hash_onepass(const void* src, uint64_t nbytes, uint64_t* digests, cu
     const int g = grid_for(nbytes, ctas, 148 * 4);
     auto S = static_cast<const uint8_t*>(src);
     KernelStamp* ks = timing_take(kIdHash, nbytes);
-    if (aligned16(src)) k_evict<true, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests, 0, ks);
-    else k_evict<false, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests, 0, ks);
+    if (aligned16(src)) k_evict<true, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests, ks);
+    else k_evict<false, true, false><<<g, kThreads, 0, s>>>(S, nullptr, nbytes, digests, ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -848,31 +805,30 @@ cudaError_t restore_cast(const void* src, void* dst, uint64_t nbytes, Cast cast,
     if (!src || !dst) return cudaErrorInvalidValue;
     if (expect && !mismatch) return cudaErrorInvalidValue;
     const int g = grid_for(nbytes, ctas, 96);
-    const int p = g_policy.load(std::memory_order_relaxed);
     auto S = static_cast<const uint8_t*>(src);
     auto D = static_cast<uint8_t*>(dst);
     const bool verify = expect != nullptr;
     KernelStamp* ks = timing_take(kIdRestore, nbytes);
     if (cast == Cast::kNone) {
         const bool al = aligned16(src) && aligned16(dst);
-        if (al && verify) k_restore<true, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
-        else if (al) k_restore<true, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
-        else if (verify) k_restore<false, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
-        else k_restore<false, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
+        if (al && verify) k_restore<true, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, ks);
+        else if (al) k_restore<true, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, ks);
+        else if (verify) k_restore<false, true, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, ks);
+        else k_restore<false, false, 0><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, ks);
     } else {
         // Casts need element-aligned whole vectors.
         if (!aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7) || nbytes % 16) return cudaErrorInvalidValue;
         if (cast == Cast::kBf16ToFp8Block128) {
             if (!scales) return cudaErrorInvalidValue;
-            if (verify) k_restore<true, true, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, expect, mismatch, p, ks);
-            else k_restore<true, false, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, nullptr, nullptr, p, ks);
+            if (verify) k_restore<true, true, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, expect, mismatch, ks);
+            else k_restore<true, false, 1><<<g, kThreads, 0, s>>>(S, D, nbytes, scales, nullptr, nullptr, ks);
         } else if (cast == Cast::kFp32ToBf16) {
-            if (verify) k_restore<true, true, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
-            else k_restore<true, false, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
+            if (verify) k_restore<true, true, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, ks);
+            else k_restore<true, false, 2><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, ks);
         } else if (cast == Cast::kBf16ToFp32) {
             if (reinterpret_cast<uintptr_t>(dst) & 15) return cudaErrorInvalidValue;
-            if (verify) k_restore<true, true, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
-            else k_restore<true, false, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
+            if (verify) k_restore<true, true, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, expect, mismatch, ks);
+            else k_restore<true, false, 3><<<g, kThreads, 0, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, ks);
         } else {
             return cudaErrorInvalidValue;
         }
@@ -922,7 +878,7 @@ cudaError_t evict_z(const void* src, void* dst, uint64_t nbytes, const uint8_t* 
     const int g = grid_for(nbytes, ctas, 96);
     KernelStamp* ks = timing_take(kIdEvictZ, nbytes);
     k_evict_z<<<g, kThreads, kZStage, s>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nbytes,
-                                           ebase, digests, g_policy.load(std::memory_order_relaxed), ks);
+                                           ebase, digests, ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -932,7 +888,6 @@ cudaError_t restore_z(const void* src, void* dst, uint64_t nbytes, Cast cast, fl
     if (!zbf16::eligible(nbytes) || !aligned16(src) || !aligned16(dst)) return cudaErrorInvalidValue;
     if (expect && !mismatch) return cudaErrorInvalidValue;
     const int g = grid_for(nbytes, ctas, 96);
-    const int p = g_policy.load(std::memory_order_relaxed);
     auto S = static_cast<const uint8_t*>(src);
     auto D = static_cast<uint8_t*>(dst);
     const bool v = expect != nullptr;
@@ -953,16 +908,16 @@ cudaError_t restore_z(const void* src, void* dst, uint64_t nbytes, Cast cast, fl
     KernelStamp* ks = timing_take(kIdRestoreZ, nbytes);
     switch (cast) {
         case Cast::kNone:
-            if (v) k_restore_z<true, 0><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
-            else k_restore_z<false, 0><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
+            if (v) k_restore_z<true, 0><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, expect, mismatch, ks);
+            else k_restore_z<false, 0><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, ks);
             break;
         case Cast::kBf16ToFp8Block128:
-            if (v) k_restore_z<true, 1><<<g, kThreads, kZStage, s>>>(S, D, nbytes, scales, expect, mismatch, p, ks);
-            else k_restore_z<false, 1><<<g, kThreads, kZStage, s>>>(S, D, nbytes, scales, nullptr, nullptr, p, ks);
+            if (v) k_restore_z<true, 1><<<g, kThreads, kZStage, s>>>(S, D, nbytes, scales, expect, mismatch, ks);
+            else k_restore_z<false, 1><<<g, kThreads, kZStage, s>>>(S, D, nbytes, scales, nullptr, nullptr, ks);
             break;
         default:
-            if (v) k_restore_z<true, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, expect, mismatch, p, ks);
-            else k_restore_z<false, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, p, ks);
+            if (v) k_restore_z<true, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, expect, mismatch, ks);
+            else k_restore_z<false, 3><<<g, kThreads, kZStage, s>>>(S, D, nbytes, nullptr, nullptr, nullptr, ks);
             break;
     }
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -977,7 +932,7 @@ cudaError_t evict_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cu
     int g = ctas > 0 ? ctas : 96;  // as evict_z
     if (uint64_t(g) > total_chunks) g = int(total_chunks);
     KernelStamp* ks = timing_take(kIdEvictJobs, total_chunks * kChunk);
-    k_evict_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, g_policy.load(std::memory_order_relaxed), ks);
+    k_evict_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -990,7 +945,7 @@ cudaError_t restore_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, 
     int g = ctas > 0 ? ctas : 96;
     if (uint64_t(g) > total_chunks) g = int(total_chunks);
     KernelStamp* ks = timing_take(kIdRestoreJobs, total_chunks * kChunk);
-    k_restore_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, g_policy.load(std::memory_order_relaxed), ks);
+    k_restore_jobs<<<g, kThreads, kZStage, s>>>(jobs, njobs, total_chunks, ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }

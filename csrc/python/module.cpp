@@ -599,8 +599,6 @@ PYBIND11_MODULE(_C, m) {
             return py::make_tuple(out, next);
         },
         py::arg("device"), py::arg("since") = 0);
-    m.def("set_access_policy", &kern::set_access_policy, py::arg("load_form"), py::arg("store_form"));
-    m.def("access_policy", &kern::access_policy);
     m.def("cuda_available", [] {
         int n = 0;
         return cudaGetDeviceCount(&n) == cudaSuccess && n > 0;

@@ -67,10 +67,15 @@ class ModelRole:
         return cls._BY_NAME[r]
 
 
+# 4 and 5 are additions of this runtime: "device_hash_verified" replicas hash
+# their own GPU copy for the daemon to compare; "p2p_verified" replicas have
+# compared their bytes with the owner's GPU copy over NVLink
+# (parallel.dp_dedup) and attach.
 DEDUP_MODES = {"disabled": 0, "semantic_trusted": 1, "hash_verified": 2, "sampled_hash": 3,
-               "device_hash_verified": 4}
+               "device_hash_verified": 4, "p2p_verified": 5}
 ACTION_NAMES = {0: "ATTACHED_EXISTING", 1: "NEED_D2H_CREATE", 2: "WAIT_FOR_CREATOR", 3: "DUPLICATE_CANDIDATE",
-                4: "REJECTED_STALE_VERSION", 5: "QUOTA_EXCEEDED", 6: "VERIFIED_BY_DEVICE_HASH", 255: "ERROR"}
+                4: "REJECTED_STALE_VERSION", 5: "QUOTA_EXCEEDED", 6: "VERIFIED_BY_DEVICE_HASH",
+                7: "VERIFIED_BY_P2P", 255: "ERROR"}
 CASTS = {None: 0, "none": 0, "fp8_block128": 1, "bf16": 2, "fp32": 3}
 
 # c10::ScalarType numbering: the dtype field of a canonical key carries it so

@@ -1,10 +1,12 @@
 """Data-parallel canonical dedup with ZeRO-1 optimizer-state spill.
 
 Workload: every rank of a DP group holds the same Llama-3-8B-shaped bf16
-weights (random-init N(0, 0.02), identical seed). ``canonical_evict`` under
-``device_hash_verified`` has one owner per parameter (round robin) copy it to
-pinned memory (K1, fused hash) while every other rank confirms its replica by
-hashing its own HBM copy (no PCIe traffic); the daemon compares the hashes.
+weights (random-init N(0, 0.02), identical seed) in one flat parameter
+buffer. ``canonical_evict`` has one owner per parameter (round robin) copy it
+to pinned memory (K1, fused hash) while every other rank confirms its replica
+without PCIe traffic: ``--dedup-mode p2p_verified`` (default) compares its
+bytes with the owner's GPU copy over NVLink (K3), ``device_hash_verified``
+hashes its own HBM copy for the daemon to compare.
 Then each rank evicts its ZeRO-1 shard of fp32 Adam m and v (1/N of the
 parameters each), the daemon spills it to NVMe (``--nvme-dir``, O_DIRECT
 io_uring striped files), and the shard is restored back from NVMe.
@@ -24,7 +26,7 @@ import torch
 
 from .. import DedupPolicy, offload_context
 from .._native import native
-from ..models.shapes import LLAMA3_8B, MODELS, num_params, param_shapes, random_init
+from ..models.shapes import LLAMA3_8B, MODELS, num_params, param_shapes, random_init_flat
 from ..parallel.dp_dedup import dedup_evict_params
 from ..utils.clocks import ClockSampler
 from .common import node_daemon, setup
@@ -57,7 +59,8 @@ def run(args, metric: str) -> dict:
     sess = offload_context(daemon_addr=sock, device=env.device, rank=env.rank, local_rank=env.local_rank,
                            world_rank=env.rank, job_name="dp-dedup", eager_register=True)
     off = sess.off
-    params = random_init(shapes, env.device, seed=0)  # identical on every replica
+    _flat, params = random_init_flat(shapes, env.device, seed=0)  # identical on every replica
+    mode = getattr(args, "dedup_mode", "p2p_verified")
     ref = {n: off.hash_tensor(t) for n, t in list(params.items())[:4]}
     launches0 = native().kernel_launch_count()
     sampler = ClockSampler([env.local_rank]).start().wait_first()
@@ -66,7 +69,7 @@ def run(args, metric: str) -> dict:
     # ---- phase 1: canonical dedup of the replicated weights ----
     handles, dedup_ms = _sync_wall(env, lambda: dedup_evict_params(
         off, params, model_role="policy_trainable", model_version=1,
-        policy=DedupPolicy("device_hash_verified"), owner="round_robin", destructive=False))
+        policy=DedupPolicy(mode), owner="round_robin", destructive=False))
     actions = {}
     copied = 0
     for n, h in handles.items():
@@ -123,7 +126,7 @@ def run(args, metric: str) -> dict:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init N(0,0.02) weights (same seed on every replica); fp32 N(0,1) m/v shards",
         "config": {"model": f"{spec.name}-shaped" + (f" ({args.layers} layers)" if args.layers else ""),
-                   "model_bytes": model_bytes, "parallelism": f"dp{env.world}", "dedup": "device_hash_verified",
+                   "model_bytes": model_bytes, "parallelism": f"dp{env.world}", "dedup": mode,
                    "owner": "round_robin", "zero1_mv_bytes_per_rank": mv_bytes, "nvme_dir": nvme_dir,
                    "global_batch": env.world, "seq_len": 0, "slot_mb": 2,
                    "l2": "whole-model passes; no flush needed"},

@@ -106,6 +106,32 @@ def random_init(shapes, device, dtype=torch.bfloat16, std: float = 0.02, seed: i
     return out
 
 
+def random_init_flat(shapes, device, dtype=torch.bfloat16, std: float = 0.02, seed: int = 0, align: int = 256):
+    """Like ``random_init``, but every tensor is a view of one flat buffer
+    (each starting on an ``align``-byte boundary), the layout data-parallel
+    trainers keep their parameters in. Returns (flat uint8 buffer, name -> view)."""
+    esz = torch.tensor([], dtype=dtype).element_size()
+    offs, total = [], 0
+    for _, shape in shapes:
+        n = 1
+        for d in shape:
+            n *= d
+        offs.append(total)
+        total += (n * esz + align - 1) // align * align
+    flat = torch.empty(max(total, 1), dtype=torch.uint8, device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    out = {}
+    for (name, shape), off in zip(shapes, offs):
+        n = 1
+        for d in shape:
+            n *= d
+        t = flat[off:off + n * esz].view(dtype).view(shape)
+        t.normal_(1.0 if name.endswith("norm.weight") else 0.0, std, generator=g)
+        out[name] = t
+    return flat, out
+
+
 def pick_changed(names, fraction: float, seed: int) -> List[int]:
     """Indices of a seeded `fraction` of `names` (sorted)."""
     gen = torch.Generator()

@@ -445,3 +445,25 @@ def test_carry_forward_of_one_tensor_parallel_shard(sock_path):
             assert everything["carried"] == 2
     finally:
         d.stop()
+
+
+def test_p2p_verified_replica_attaches_with_its_own_action(cdaemon):
+    """Dedup mode 5: a replica that compared its bytes with the owner's GPU
+    copy (statespectre_b200.parallel.dp_dedup) attaches without any copy and
+    is counted separately from trusted attaches."""
+    w = torch.randn(300, 40)
+    pol = DedupPolicy("p2p_verified")
+    with session(cdaemon, 0) as r0, session(cdaemon, 1) as r1:
+        k = r0.canonical_key(model_role=ROLL, model_version=1, param_name="w", tensor=w)
+        h0 = r0.canonical_evict(w.clone(), k, dedup_policy=pol)
+        assert h0.action_name == "NEED_D2H_CREATE" and h0.did_d2h
+        before = r1.daemon_stats()
+        h1 = r1.canonical_evict(w.clone(), r1.canonical_key(model_role=ROLL, model_version=1, param_name="w",
+                                                            tensor=w), dedup_policy=pol)
+        assert h1.action_name == "VERIFIED_BY_P2P" and not h1.did_d2h and h1.object_id == h0.object_id
+        after = r1.daemon_stats()
+        assert after["canonical_p2p_verified_total"] == before["canonical_p2p_verified_total"] + 1
+        assert after["canonical_d2h_bytes_avoided"] - before["canonical_d2h_bytes_avoided"] == w.numel() * 4
+        out = torch.empty_like(w)
+        h1.restore_into(out)
+        assert torch.equal(out, w)

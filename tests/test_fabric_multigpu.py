@@ -178,3 +178,75 @@ def test_multicast_team_in_one_process(two_gpus, sock_path, mode):
                 rw.close()
     finally:
         d.stop()
+
+
+def _dedup_rank(rank, sock, pg_file, q_out):
+    import torch
+    import torch.distributed as dist
+
+    from statespectre_b200 import DedupPolicy, offload_context
+    from statespectre_b200.parallel.dp_dedup import dedup_evict_params
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"file://{pg_file}", rank=rank, world_size=2)
+    res = {}
+    try:
+        with offload_context(daemon_addr=sock, device=f"cuda:{rank}", rank=rank, job_name="dp2") as off:
+            g = torch.Generator(device=f"cuda:{rank}").manual_seed(0)  # same weights on both replicas
+            params = {f"w{i}": torch.randn(1000 + 333 * i, 96, device=f"cuda:{rank}", generator=g)
+                      .to(torch.bfloat16) for i in range(6)}
+            pol = DedupPolicy("p2p_verified")
+            hs = dedup_evict_params(off, params, model_role="policy_trainable", model_version=1, policy=pol,
+                                    destructive=False)
+            res["actions"] = {n: h.action_name for n, h in hs.items()}
+            res["restored_equal"] = all(
+                torch.equal(hs[n].restore_into(torch.empty_like(t)), t) for n, t in params.items())
+            res["p2p_verified"] = off.daemon_stats().get("canonical_p2p_verified_total")
+            if rank == 1:
+                params["w0"].view(-1)[12345] += 1  # w0 is owned by rank 0: rank 1's copy now differs
+            try:
+                dedup_evict_params(off, params, model_role="policy_trainable", model_version=2, policy=pol,
+                                   destructive=False)
+                res["mismatch"] = None
+            except RuntimeError as e:
+                res["mismatch"] = str(e)
+        q_out.put((rank, res))
+    except Exception as e:  # noqa: BLE001
+        q_out.put((rank, {"error": repr(e)}))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dp_dedup_verifies_replicas_by_peer_byte_compare(two_gpus, sock_path, tmp_path):
+    """p2p_verified: the owner of each parameter copies it to the host; the
+    other replica compares its bytes with the owner's GPU copy over NVLink
+    (K3) and attaches. A replica whose bytes differ is reported on both
+    ranks, by name."""
+    from statespectre_b200 import in_process_daemon
+
+    d = in_process_daemon(socket=sock_path, arena_mb=512, drain_on_complete=False)
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    procs = [ctx.Process(target=_dedup_rank, args=(r, sock_path, str(tmp_path / "pg"), q_out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        got = dict(q_out.get(timeout=TIMEOUT) for _ in range(2))
+        for p in procs:
+            p.join(TIMEOUT)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:  # point-to-point only (no multicast object): a stuck child may be killed
+            if p.is_alive():
+                p.kill()
+                p.join(10)
+        d.stop()
+    for r in (0, 1):
+        assert "error" not in got[r], got[r]
+        acts = got[r]["actions"]
+        for i in range(6):
+            want = "NEED_D2H_CREATE" if i % 2 == r else "VERIFIED_BY_P2P"
+            assert acts[f"w{i}"] == want, (r, acts)
+        assert got[r]["restored_equal"]
+        assert got[r]["mismatch"] is not None and "w0" in got[r]["mismatch"]
+    assert max(got[0]["p2p_verified"], got[1]["p2p_verified"]) == 6  # every parameter verified once

@@ -1,0 +1,103 @@
+"""Wire interoperability with the reference's own client code.
+
+StateSpectre's rollout wire module and RolloutWeightClient are pure Python
+(python_api/state_spectre/_wire.py, _rollout.py). This test loads those two
+files from the reference build in ``baseline/_ref`` (built by
+baseline/build_reference.py; skipped when absent) under a private package
+name, points them at this repository's offloadd over TCP, and pulls a sealed
+version: discovery, manifest, per-object PullTensor with the daemon
+connecting back, OFEX framing. Every pulled byte must equal the evicted
+tensor, and the next version's manifest, carried forward here for its
+unchanged objects, must show their content hashes unchanged when decoded by
+the reference's codec.
+"""
+
+import importlib.util
+import os
+import socket
+import sys
+import types
+
+import pytest
+import torch
+
+from statespectre_b200 import ModelRole, in_process_daemon, offload_context
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_PKG = os.environ.get("OFLD_REFERENCE_PY", os.path.join(ROOT, "baseline", "_ref", "state_spectre"))
+ROLL = ModelRole.POLICY_ROLLOUT
+
+
+def _load_reference_client():
+    wire_py, rollout_py = os.path.join(REF_PKG, "_wire.py"), os.path.join(REF_PKG, "_rollout.py")
+    if not (os.path.exists(wire_py) and os.path.exists(rollout_py)):
+        pytest.skip("reference build not present (python baseline/build_reference.py)")
+    name = "_ssref_pure"
+    pkg = types.ModuleType(name)
+    pkg.__path__ = [REF_PKG]
+    # the reference's ModelRole lives in its torch-extension __init__; the
+    # client only calls ModelRole.parse, whose values are the wire enum
+    pkg.ModelRole = ModelRole
+    sys.modules[name] = pkg
+    mods = {}
+    for sub, path in (("_wire", wire_py), ("_rollout", rollout_py)):
+        spec = importlib.util.spec_from_file_location(f"{name}.{sub}", path)
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[f"{name}.{sub}"] = mod
+        spec.loader.exec_module(mod)
+        setattr(pkg, sub, mod)
+        mods[sub] = mod
+    return mods["_rollout"].RolloutWeightClient, mods["_wire"]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_reference_rollout_client_pulls_from_this_daemon(sock_path):
+    RefClient, ref_wire = _load_reference_client()
+    port = _free_port()
+    d = in_process_daemon(socket=sock_path, arena_mb=128, drain_on_complete=False, tcp_port=port)
+    try:
+        tensors = {f"model.layers.{i}.mlp.w": torch.randn(257 + 31 * i, 65) for i in range(4)}
+        tensors["model.norm.weight"] = torch.randn(17)
+        with offload_context(daemon_addr=sock_path, device="cpu", rank=0, job_name="interop") as off:
+            for name, t in tensors.items():
+                off.canonical_evict(t.clone(), off.canonical_key(model_role=ROLL, model_version=1, param_name=name,
+                                                                 tensor=t))
+            off.promote_rollout_version(1)
+            c = RefClient(f"tcp://127.0.0.1:{port}", off.job_id, off.launch_epoch, recv_host="127.0.0.1")
+            assert c.get_latest_sealed_version() == 1
+            man = c.get_manifest(1)
+            assert len(man["tensors"]) == len(tensors)
+            for e in man["tensors"]:
+                payload = c.pull_tensor(e, 1)
+                assert payload == tensors[e["key"]["param_fqn_debug"]].numpy().tobytes()
+            # version 2: one tensor changes, the rest is carried forward with its content hash
+            changed = "model.layers.2.mlp.w"
+            tensors[changed] = tensors[changed] + 1
+            k = off.canonical_key(model_role=ROLL, model_version=2, param_name=changed, tensor=tensors[changed])
+            off.canonical_evict(tensors[changed].clone(), k)
+            off.carry_forward_version(ROLL, 1, 2, [off.canonical_key(model_role=ROLL, model_version=2,
+                                                                      param_name=n, tensor=t).param_id
+                                                   for n, t in tensors.items() if n != changed])
+            off.promote_rollout_version(2)
+            res = c.sync_latest()
+            assert res["version"] == 2
+            # the reference client caches by object id, and version 2's
+            # objects are new ids: it pulls all of them again
+            assert len(res["pulled"]) == len(tensors)
+            # the manifest, decoded by the reference's codec, carries the
+            # unchanged objects' content hashes unchanged
+            man2 = c.get_manifest(2, {"tp": 0})
+            assert man2["ok"] and man2["model_version"] == 2 and man2["state"] == 2
+            h1 = {e["key"]["param_fqn_debug"]: (e["content_hash_lo"], e["content_hash_hi"]) for e in man["tensors"]}
+            h2 = {e["key"]["param_fqn_debug"]: (e["content_hash_lo"], e["content_hash_hi"]) for e in man2["tensors"]}
+            assert {n for n in h1 if h1[n] != h2[n]} == {changed}
+            for e in man2["tensors"]:
+                assert c.pull_tensor(e, 2) == tensors[e["key"]["param_fqn_debug"]].numpy().tobytes()
+            assert ref_wire.EXPORT_HEADER_SIZE == 40
+    finally:
+        d.stop()

@@ -214,3 +214,38 @@ def test_vmm_buffer_tensor_view_and_p2p_push(sock_path):
             rw.close()
     finally:
         d.stop()
+
+
+def test_push_reports_a_bad_item_through_its_bounded_waits():
+    """The K4 error path, run on purpose and safely: an item whose source is
+    not 16-byte aligned is refused by the producer before any copy is issued
+    (status 3), the consumers' bounded waits on the stage it never fills run
+    out (about two seconds), and the kernel returns. The launch completes,
+    the status is read on the host, and the next push on the same context
+    works."""
+    import struct as _struct
+    import time
+
+    C = native()
+    s = torch.cuda.current_stream().cuda_stream
+    src = torch.randint(0, 256, (2 * 65536 + 64,), dtype=torch.uint8, device="cuda")
+    n = 65536
+    item = _struct.pack("<QQQQQIIQQ", src.data_ptr() + 8, 0, 0, n, 0, 2, 0, 0, 0)  # PUSH_HASH, misaligned src
+    items = torch.frombuffer(bytearray(item), dtype=torch.uint8).to("cuda")
+    dig = torch.zeros(1, dtype=torch.int64, device="cuda")
+    out = torch.zeros(2, dtype=torch.int64, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    t0 = time.time()
+    C.k_push(items.data_ptr(), 1, 1, dig.data_ptr(), out.data_ptr(), 0, err.data_ptr(), s, 1, 0)
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    assert int(err.item()) == 3  # bad item (first writer wins over the expired waits)
+    assert waited < 30
+    # the context is still usable: a well-formed launch succeeds
+    ok_item = _struct.pack("<QQQQQIIQQ", src.data_ptr(), 0, 0, n, 0, 2, 0, 0, 0)
+    items.copy_(torch.frombuffer(bytearray(ok_item), dtype=torch.uint8))
+    err.zero_()
+    C.k_push(items.data_ptr(), 1, 1, dig.data_ptr(), out.data_ptr(), 0, err.data_ptr(), s, 1, 0)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert [int(v) & M for v in dig.tolist()] == list(C.ssh_digests(src[:n].cpu().numpy()))

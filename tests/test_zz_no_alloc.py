@@ -54,7 +54,8 @@ def _regular_hash(x: torch.Tensor) -> tuple:
 
 def _noalloc_hash(fn, x: torch.Tensor) -> tuple:
     out = torch.zeros(2, dtype=torch.int64, device=x.device)
-    rc = fn(x.data_ptr(), x.numel() * x.element_size(), out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    n = x.numel() * x.element_size()
+    rc = fn(x.data_ptr() if n else None, n, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc == 0
     torch.cuda.synchronize()
     return tuple(int(v) & 0xFFFFFFFFFFFFFFFF for v in out.cpu().tolist())
@@ -69,6 +70,21 @@ def test_noalloc_hash_matches_regular_entry_point_twice():
     assert _noalloc_hash(fn, b) == _regular_hash(b)
     # the first call's digests left in the scratch array do not leak into a smaller call
     assert _noalloc_hash(fn, a[:1000]) == _regular_hash(a[:1000])
+
+
+def test_noalloc_hash_unaligned_and_empty_inputs():
+    """Any alignment and any size: a source one byte past an allocation
+    boundary with a ragged length takes the per-thread hash form through the
+    same scratch array; zero bytes runs only the fold."""
+    fn = _lib()
+    torch.manual_seed(5)
+    a = torch.randint(0, 256, ((3 << 20) + 64,), dtype=torch.uint8, device="cuda")
+    odd = a[1:1 + (1 << 20) + 5]
+    assert odd.data_ptr() % 16 == 1
+    assert _noalloc_hash(fn, odd) == _regular_hash(odd)
+    empty = a[:0]
+    assert _noalloc_hash(fn, empty) == _regular_hash(empty)
+    assert _noalloc_hash(fn, odd) == _regular_hash(odd)  # and once more after the empty call
 
 
 def test_noalloc_rejects_oversize_and_null_without_launching():
