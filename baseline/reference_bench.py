@@ -495,14 +495,24 @@ def run_weight_sync(args, world: int, rank: int, local_rank: int, device, state_
             dist.all_reduce(vals[:1], op=dist.ReduceOp.MAX)
             stats["e2e_ms"].append(float(vals[0].item()))
 
+    t_begin = time.time()
     for v in range(1, warmup + 1):
         step(v, None)
     stats = {"e2e_ms": []}
     sampler = _clock_sampler_cls()([local_rank]).start().wait_first()
     dist.barrier()
     sampler.mark_start()
-    for v in range(warmup + 1, warmup + versions + 1):
+    budget = float(getattr(args, "ref_ws_budget_s", 300.0))
+    v = warmup + 1
+    while v <= warmup + versions:
         step(v, stats)
+        v += 1
+        # every version moves the whole shard over TCP: stop early (same decision on every rank)
+        over = torch.tensor([1.0 if time.time() - t_begin > budget else 0.0], device=device)
+        dist.all_reduce(over, op=dist.ReduceOp.MAX)
+        if over.item():
+            break
+    versions = len(stats["e2e_ms"])
     sampler.mark_end()
     clocks = sampler.stop()
     if sess is not None:

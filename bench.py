@@ -92,6 +92,9 @@ def parse():
     p.add_argument("--ws-warmup", type=int, default=3, help="weight-sync block: untimed versions per mode")
     p.add_argument("--ref-ws-versions", type=int, default=3,
                    help="reference arm's weight-sync block: timed versions (each moves every tensor over TCP)")
+    p.add_argument("--ref-ws-budget-s", type=float, default=300.0,
+                   help="reference arm's weight-sync block: stop timing further versions after this many seconds "
+                        "(at least one timed version)")
     p.add_argument("--rollout-replicas", type=int, default=1,
                    help="weight_sync: rollout engines fed by each trainer shard (GPUs split 1 + R ways)")
     p.add_argument("--transport", default="auto", choices=["auto", "p2p", "multicast"],

@@ -502,7 +502,9 @@ class Off:
         mode = 0 if dedup == "disabled" else pol.mode_int
         unsafe = unsafe_autograd or self._unsafe_default
         src = tensor
-        if compact or allow_views:
+        if not destructive and tensor.is_contiguous():
+            pass  # a copy that leaves the tensor alone reads a contiguous view in place
+        elif compact or allow_views:
             src = tensor.clone(memory_format=torch.contiguous_format)
         else:
             _validate_destructive(tensor, unsafe)

@@ -467,3 +467,22 @@ def test_p2p_verified_replica_attaches_with_its_own_action(cdaemon):
         out = torch.empty_like(w)
         h1.restore_into(out)
         assert torch.equal(out, w)
+
+
+def test_non_destructive_canonical_evict_of_a_view_in_a_flat_buffer(cdaemon):
+    """Parameters that are views of one flat buffer (a data-parallel trainer's
+    layout) are copied in place by a non-destructive canonical evict; a
+    destructive one still refuses a view that does not own its storage."""
+    flat = torch.randn(10000)
+    a, b = flat[:4000].view(40, 100), flat[4000:]
+    with session(cdaemon, 0) as off:
+        ha = off.canonical_evict(a, off.canonical_key(model_role=ROLL, model_version=1, param_name="a", tensor=a),
+                                 destructive=False)
+        hb = off.canonical_evict(b, off.canonical_key(model_role=ROLL, model_version=1, param_name="b", tensor=b),
+                                 destructive=False)
+        assert ha.did_d2h and hb.did_d2h and flat.numel() == 10000
+        out = torch.empty(40, 100)
+        ha.restore_into(out)
+        assert torch.equal(out, a)
+        with pytest.raises(RuntimeError, match="does not own"):
+            off.canonical_evict(a, off.canonical_key(model_role=ROLL, model_version=2, param_name="a", tensor=a))
