@@ -139,8 +139,14 @@ def run(args, metric: str, baseline_roundtrip_gbs: float) -> dict | None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    nbytes = args.size_mb << 20
-    window_gb = max(4, (3 * nbytes >> 30) + 2)
+    sweep_sizes = []
+    if getattr(args, "workload", "evict_restore") == "sweep":
+        s_ = 4096
+        while s_ <= (args.max_size_mb << 20):
+            sweep_sizes.append(s_)
+            s_ <<= 1
+    nbytes = args.size_mb << 20 if not sweep_sizes else sweep_sizes[-1]
+    window_gb = max(4, (3 * nbytes >> 30) + 2, int(getattr(args, "arena_gb", 0) or 0))
     run_dir = os.environ.get("OFLD_REF_BENCH_DIR", "/tmp/ssref_bench")
     os.makedirs(run_dir, exist_ok=True)
     sock = os.path.join(run_dir, "offloadd.sock")
@@ -170,6 +176,9 @@ def run(args, metric: str, baseline_roundtrip_gbs: float) -> dict | None:
     sess = state_spectre.offload_context(daemon_addr=sock, device=device, rank=rank, local_rank=local_rank,
                                          world_rank=rank, eager_register=True)
     off = sess.__enter__()
+    if sweep_sizes:
+        return _sweep(args, metric, state_spectre, off, sess, sweep_sizes, world, rank, device, window_gb,
+                      max_over_ranks, barrier, daemon, log)
     g = torch.Generator(device=device)
     g.manual_seed(1234 + rank)
     x = torch.randn(nbytes // 2, dtype=torch.bfloat16, device=device, generator=g)
@@ -309,6 +318,94 @@ def run(args, metric: str, baseline_roundtrip_gbs: float) -> dict | None:
     if ws is not None:
         out["weight_sync"] = ws
     return out
+
+
+def _sweep(args, metric, state_spectre, off, sess, sizes, world, rank, device, window_gb, max_over_ranks,
+           barrier, daemon, log):
+    """The size sweep through the reference: bf16 N(0,1) tensors 4 KB .. max,
+    ``copy(wait=True)`` + ``restore_into(wait=True)`` per repeat, each
+    direction timed with CUDA events on the copy stream, max over ranks,
+    median over repeats, under the same GEMM loop."""
+    import statistics
+
+    import torch
+    import torch.distributed as dist
+
+    stream = torch.cuda.Stream(device=device, priority=-1)
+    stop_mm = threading.Event()
+    mm_thread = None
+    if args.matmul:
+        mm_stream = torch.cuda.Stream(device=device)
+        a = torch.randn(8192, 8192, dtype=torch.bfloat16, device=device)
+        b = torch.randn(8192, 8192, dtype=torch.bfloat16, device=device)
+        c = torch.empty(8192, 8192, dtype=torch.bfloat16, device=device)
+
+        def mm_loop():
+            torch.cuda.set_device(device)
+            with torch.cuda.stream(mm_stream):
+                while not stop_mm.is_set():
+                    for _ in range(8):
+                        torch.matmul(a, b, out=c)
+                    mm_stream.synchronize()
+
+        mm_thread = threading.Thread(target=mm_loop, daemon=True)
+        mm_thread.start()
+    g = torch.Generator(device=device).manual_seed(1234 + rank)
+    rows = []
+    sampler = _clock_sampler_cls()([int(device.index)]).start().wait_first()
+    sampler.mark_start()
+    for nbytes in sizes:
+        x = torch.randn(nbytes // 2, dtype=torch.bfloat16, device=device, generator=g)
+        ref = x.clone()
+        ev, rs = [], []
+        for i in range(args.warmup + args.steps):
+            barrier()
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(stream)
+            h = off.copy(x, stream=stream, wait=True)
+            e1.record(stream)
+            h.restore_into(x, stream=stream, wait=True)
+            e2.record(stream)
+            h.discard()
+            e2.synchronize()
+            if i >= args.warmup:
+                ev.append(max_over_ranks(e0.elapsed_time(e1)))
+                rs.append(max_over_ranks(e1.elapsed_time(e2)))
+        ok = bool(torch.equal(x, ref))
+        e_ms, r_ms = statistics.median(ev), statistics.median(rs)
+        rows.append({"bytes": nbytes, "evict_gbs": round(nbytes / (e_ms / 1e3) / 1e9, 3),
+                     "restore_gbs": round(nbytes / (r_ms / 1e3) / 1e9, 3), "evict_ms": round(e_ms, 4),
+                     "restore_ms": round(r_ms, 4), "byte_exact": ok})
+        del x, ref
+    sampler.mark_end()
+    clocks = sampler.stop()
+    stop_mm.set()
+    if mm_thread:
+        mm_thread.join(timeout=30)
+    sess.close()
+    barrier()
+    if daemon is not None:
+        daemon.terminate()
+        try:
+            daemon.wait(timeout=30)
+        except subprocess.TimeoutExpired:
+            daemon.kill()
+        log.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    head = next((r for r in rows if r["bytes"] == 1 << 30), rows[-1])
+    rt = 2 * head["bytes"] / ((head["evict_ms"] + head["restore_ms"]) / 1e3) / 1e9
+    return {"impl": "reference", "metric": metric, "workload": "sweep", "value": round(rt * world, 3),
+            "unit": "GB/s (aggregate round trip at the 1 GiB point; per-size rows below)",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(head["evict_ms"] + head["restore_ms"], 4), "higher_is_better": True,
+            "scaling": "weak", "dtype": "bf16", "data": "synthetic: bf16 N(0,1) per size, seeded per rank",
+            "config": {"model": "evict/restore size sweep through the reference (cudaMemcpyAsync)",
+                       "arena_gb_per_gpu": window_gb, "slot_mb": 64,
+                       "concurrent_matmul": "8192x8192 bf16 loop" if args.matmul else "none"},
+            "sweep": rows, "all_byte_exact": all(r["byte_exact"] for r in rows), "clocks": clocks}
 
 
 # ---------------------------------------------------------------------------

@@ -54,7 +54,7 @@ def _reference_arm(args) -> int:
     spec = importlib.util.spec_from_file_location("reference_bench", path)
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
-    if args.workload not in ("evict_restore",):
+    if args.workload not in ("evict_restore", "sweep"):
         print(json.dumps(mod.unavailable(f"no reference arm for workload {args.workload}")), flush=True)
         return 0
     return mod.main(args, METRIC, BASELINE_ROUNDTRIP_GBS)
@@ -106,6 +106,7 @@ def parse():
     p.add_argument("--hint", type=int, default=0,
                    help="weight_sync: pass the changed-tensor list instead of hashing every tensor")
     p.add_argument("--max-size-mb", type=int, default=8192, help="sweep: largest tensor")
+    p.add_argument("--arena-gb", type=int, default=0, help="sweep: pinned window per GPU (0: 3x the largest size)")
     p.add_argument("--kv-gb", type=float, default=40.0, help="kv_cache: KV cache bytes per GPU")
     p.add_argument("--evict-fraction", type=float, default=0.5, help="kv_cache: blocks moved per iteration")
     p.add_argument("--kv-batch", type=int, default=0,

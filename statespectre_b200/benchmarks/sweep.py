@@ -9,7 +9,8 @@ waits are inside the timed region); the reported rate per size is the median
 over repeats of the slowest rank. ``value`` is the round-trip rate at the
 1 GiB point (the headline size).
 
-    python bench.py --workload sweep --steps 20 --warmup 3
+    python bench.py --workload sweep --steps 20 --warmup 3 --arena-gb 64 [--compress 0]
+    python bench.py --impl reference --workload sweep ...   # the reference, same sizes and timing
 """
 
 from __future__ import annotations
@@ -35,7 +36,7 @@ def run(args, metric: str) -> dict:
     while s <= max_bytes:
         sizes.append(s)
         s <<= 1
-    window_gb = int(3 * max_bytes / GiB) + 2
+    window_gb = max(int(getattr(args, "arena_gb", 0) or 0), int(3 * max_bytes / GiB) + 2)
     sock, daemon = node_daemon(env, window_gb, "/tmp/ofld_sweep", slot_mb=64)
     sess = offload_context(daemon_addr=sock, device=env.device, rank=env.rank, local_rank=env.local_rank,
                            world_rank=env.rank, eager_register=True, compress=bool(args.compress),
@@ -92,6 +93,8 @@ def run(args, metric: str) -> dict:
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: bf16 N(0,1) per size, seeded per rank",
         "config": {"model": "evict/restore size sweep 4 KB - max size, bf16", "max_bytes": max_bytes,
+                   "arena_gb_per_gpu": window_gb, "transfer_coding": "zbf16 where it codes" if args.compress
+                   else "none (--compress 0)",
                    "concurrent_matmul": load.describe() if load else "none", "global_batch": env.world,
                    "seq_len": 0, "parallelism": f"dp{env.world}", "slot_mb": 64,
                    "l2": "sizes above 126 MB stream from HBM; smaller ones may hit L2 (reported as measured)"},
