@@ -183,6 +183,7 @@ def run(args, metric: str, baseline_roundtrip_gbs: float) -> dict | None:
     g.manual_seed(1234 + rank)
     x = torch.randn(nbytes // 2, dtype=torch.bfloat16, device=device, generator=g)
     ref_copy = x.clone()
+    torch.cuda.synchronize(device)  # the copy stream must not read x before it is written
     copy_stream = torch.cuda.Stream(device=device, priority=-1)
 
     stop_mm = threading.Event()
@@ -357,6 +358,7 @@ def _sweep(args, metric, state_spectre, off, sess, sizes, world, rank, device, w
     for nbytes in sizes:
         x = torch.randn(nbytes // 2, dtype=torch.bfloat16, device=device, generator=g)
         ref = x.clone()
+        torch.cuda.synchronize(device)  # the copy stream must not read x before it is written
         ev, rs = [], []
         for i in range(args.warmup + args.steps):
             barrier()
