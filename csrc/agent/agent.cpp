@@ -1249,6 +1249,14 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
         }
         pending.swap(again);
         if (!pending.empty()) {
+            // Items still waiting (readback in flight, or no pinned run free for
+            // one) may need the runs this batch holds: hand on the completions
+            // of what was launched first, so its prefetch leases return to the
+            // daemon before we ask again.
+            if (D.gpu && last_ev) CUDA_OK(cudaEventSynchronize(last_ev));
+            for (Impl::Pending& p : launched) D.finish(p);
+            launched.clear();
+            last_ev = nullptr;
             if (mono_ns() > deadline) {
                 for (size_t i : pending) out[i].message = "readback timed out";
                 break;

@@ -9,6 +9,11 @@ not the data copy, is what is measured:
   batch    evict_batch + restore_batch + discard_batch of 256 x 4 KiB
            tensors: items per second, per phase
   ranks    the single loop in 1, 4 and 16 rank processes at once: aggregate rate
+  kv       8 rank processes, each moving its own 64 blocks of 256 KiB per
+           iteration with evict_batch + restore_batch, against a pinned
+           window half the size of the blocks in flight, so background
+           pressure drains and readbacks run under the request load: items per
+           second in aggregate, per-iteration p50 / p99, drains and readbacks
 
 StateSpectre needs two RPCs per evict and one per restore on its one-mutex
 daemon; the paged KV-cache workload (about 10k block moves per GPU per
@@ -29,7 +34,7 @@ import time
 
 import torch
 
-from .. import in_process_daemon, offload_context
+from .. import DaemonClient, in_process_daemon, offload_context
 
 
 def _single(sock: str, rank: int, seconds: float, lat: list, barrier=None) -> int:
@@ -104,6 +109,65 @@ def run(seconds: float = 2.0, rank_counts=(1, 4, 16)) -> dict:
     return out
 
 
+def _kv_rank(sock: str, rank: int, seconds: float, nblocks: int, block: int, q, barrier) -> None:
+    try:
+        _kv_loop(sock, rank, seconds, nblocks, block, q, barrier)
+    except Exception as e:  # noqa: BLE001
+        q.put((0, [], repr(e)))
+
+
+def _kv_loop(sock: str, rank: int, seconds: float, nblocks: int, block: int, q, barrier) -> None:
+    lat = []
+    n = 0
+    with offload_context(daemon_addr=sock, device="cpu", rank=rank) as off:
+        g = torch.Generator().manual_seed(rank)
+        blocks = [torch.randn(block // 4, generator=g) for _ in range(nblocks)]
+        ref = [b.clone() for b in blocks]
+        barrier.wait(120)
+        deadline = time.perf_counter() + seconds
+        while time.perf_counter() < deadline:
+            t0 = time.perf_counter()
+            hs = off.evict_batch(blocks)
+            off.restore_batch(hs, blocks)
+            off.discard_batch(hs)
+            lat.append(time.perf_counter() - t0)
+            n += nblocks
+        ok = all(torch.equal(a, b) for a, b in zip(blocks, ref))
+    q.put((n, lat, ok))
+
+
+def run_kv(seconds: float = 3.0, ranks: int = 8, nblocks: int = 64, block: int = 256 << 10) -> dict:
+    tmp = tempfile.mkdtemp(prefix="ofld-control-kv-")
+    sock = os.path.join(tmp, "d.sock")
+    window_mb = max(4, ranks * nblocks * block // 2 >> 20)
+    d = in_process_daemon(socket=sock, arena_mb=window_mb, slot_mb=1, drain_on_complete=False)
+    try:
+        ctx = mp.get_context("spawn")
+        q = ctx.Queue()
+        bar = ctx.Barrier(ranks)
+        procs = [ctx.Process(target=_kv_rank, args=(sock, 200 + i, seconds, nblocks, block, q, bar))
+                 for i in range(ranks)]
+        for p in procs:
+            p.start()
+        res = [q.get(timeout=seconds + 180) for _ in procs]
+        for p in procs:
+            p.join(30)
+        c = DaemonClient(sock)
+        stats = c.stats()
+        c.close()
+    finally:
+        d.stop()
+    lat = sorted(x for _, ls, _ in res for x in ls)
+    items = sum(n for n, _, _ in res)
+    return {"ranks": ranks, "blocks_per_rank": nblocks, "block_bytes": block, "pinned_window_mb": window_mb,
+            "items_per_s": round(items / seconds, 1),
+            "iteration_p50_ms": round(lat[len(lat) // 2] * 1e3, 2) if lat else None,
+            "iteration_p99_ms": round(lat[min(len(lat) - 1, int(0.99 * len(lat)))] * 1e3, 2) if lat else None,
+            "drains": stats.get("drains_completed"), "readbacks": stats.get("readbacks_completed"),
+            "byte_exact": all(ok is True for _, _, ok in res),
+            "errors": [ok for _, _, ok in res if ok is not True and ok is not False]}
+
+
 def _rank_proc(sock: str, rank: int, seconds: float, q, barrier) -> None:
     lat: list = []
     n = _single(sock, rank, seconds, lat, barrier)
@@ -116,6 +180,7 @@ def main(argv=None) -> int:
     p.add_argument("--out", default="")
     a = p.parse_args(argv)
     res = run(a.seconds)
+    res["kv"] = run_kv(max(a.seconds, 3.0))
     line = json.dumps({"benchmark": "control_plane", **res})
     print(line)
     if a.out:

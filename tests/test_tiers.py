@@ -231,3 +231,15 @@ def test_restore_waits_for_pinned_capacity_instead_of_failing(sock_path):
             r.close()
     finally:
         d.stop()
+
+
+def test_batched_restores_under_pressure_from_several_ranks_make_progress():
+    """Ranks moving batches of blocks through a pinned window half the size
+    of what they hold: restore_batch hands on the completions of the blocks it
+    already restored before it waits for readback capacity, so a batch never
+    waits on runs it holds itself (or another rank's batch on those)."""
+    from statespectre_b200.benchmarks.control import run_kv
+
+    r = run_kv(1.5, ranks=2, nblocks=16)
+    assert r["errors"] == [] and r["byte_exact"]
+    assert r["items_per_s"] > 0 and r["drains"] > 0 and r["readbacks"] > 0
