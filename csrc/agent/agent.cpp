@@ -133,7 +133,49 @@ struct Agent::Impl {
     std::mutex ring_mu;
 
     cudaStream_t stream = nullptr;
-    cudaStream_t side = nullptr;  // evict digests next to a copy-engine copy
+    cudaStream_t side = nullptr;  // evict digests next to a copy-engine copy; coded restore copies
+
+    // Coded restore through the copy engine: two device staging buffers of
+    // kZPiece chunks each (allocated on first use, 2 x 32 MiB) and their events.
+    static constexpr uint64_t kZPiece = 512;
+    void* zstage[2] = {nullptr, nullptr};
+    cudaEvent_t zcopied[2] = {nullptr, nullptr}, zdecoded[2] = {nullptr, nullptr};
+    std::mutex zmu;  // restores on this session share the staging
+
+    // The copy engine moves each chunk's stored bytes (`zmax` per 64 KiB row,
+    // one strided copy per piece) into staging on the side stream; K2 decodes
+    // the piece from HBM on `s`, overlapping the next piece's copy.
+    void restore_z_ce(const char* host, uint8_t* dst, uint64_t nbytes, uint32_t zmax, cudaStream_t s) {
+        std::lock_guard<std::mutex> g(zmu);
+        constexpr uint64_t C = zbf16::kChunk;
+        if (!zstage[0]) {
+            for (int b = 0; b < 2; ++b) {
+                CUDA_OK(cudaMalloc(&zstage[b], kZPiece * C));
+                CUDA_OK(cudaEventCreateWithFlags(&zcopied[b], cudaEventDisableTiming));
+                CUDA_OK(cudaEventCreateWithFlags(&zdecoded[b], cudaEventDisableTiming));
+            }
+        }
+        const uint64_t nch = (nbytes + C - 1) / C;
+        const size_t width = std::min<size_t>((size_t(zmax) + 15) / 16 * 16, C);
+        const bool short_tail = nbytes - (nch - 1) * C < zbf16::kRawTail;
+        uint64_t c0 = 0;
+        for (int k = 0; c0 < nch; ++k) {
+            uint64_t c1 = std::min(nch, c0 + kZPiece);
+            // a short raw tail never sits alone in a piece (a piece must be a codable object):
+            // the piece before it gives up one chunk (pieces that leave one chunk are full, so > 1)
+            if (short_tail && nch - c1 == 1) c1 -= 1;
+            const int b = k & 1;
+            if (k >= 2) CUDA_OK(cudaStreamWaitEvent(side, zdecoded[b], 0));  // staging b decoded before reuse
+            CUDA_OK(cudaMemcpy2DAsync(zstage[b], C, host + c0 * C, C, width, c1 - c0, cudaMemcpyHostToDevice, side));
+            CUDA_OK(cudaEventRecord(zcopied[b], side));
+            CUDA_OK(cudaStreamWaitEvent(s, zcopied[b], 0));
+            const uint64_t piece = std::min(nbytes, c1 * C) - c0 * C;
+            CUDA_OK(kern::restore_z(zstage[b], dst + c0 * C, piece, kern::Cast::kNone, nullptr, nullptr, nullptr, s,
+                                    opt.restore_ctas));
+            CUDA_OK(cudaEventRecord(zdecoded[b], s));
+            c0 = c1;
+        }
+    }
     PinnedPool pool;
 
     struct Pending {
@@ -159,6 +201,7 @@ struct Agent::Impl {
         bool offloaded = false, restored = false;
         bool failed = false;  // the device reported an incomplete copy (bounded wait expired)
         uint64_t hash_lo = 0, hash_hi = 0, lease = 0;
+        uint32_t zmax = 0;    // zbf16 run: largest stored chunk length (0: unknown)
         std::vector<uint64_t> digests;
     };
     mutable std::mutex tab_mu;
@@ -175,6 +218,8 @@ struct Agent::Impl {
     explicit Impl(const AgentOptions& o) : opt(o) {
         if (opt.uncoded != "copy_engine" && opt.uncoded != "bulk" && opt.uncoded != "sm")
             throw std::invalid_argument("uncoded must be copy_engine, bulk or sm, not '" + opt.uncoded + "'");
+        if (opt.coded_restore != "copy_engine" && opt.coded_restore != "sm")
+            throw std::invalid_argument("coded_restore must be copy_engine or sm, not '" + opt.coded_restore + "'");
         gpu = opt.device >= 0;
         if (gpu) {
             CUDA_OK(cudaSetDevice(opt.device));
@@ -269,6 +314,11 @@ struct Agent::Impl {
         }
         if (stream) cudaStreamDestroy(stream);
         if (side) cudaStreamDestroy(side);
+        for (int b = 0; b < 2; ++b) {
+            if (zstage[b]) cudaFree(zstage[b]);
+            if (zcopied[b]) cudaEventDestroy(zcopied[b]);
+            if (zdecoded[b]) cudaEventDestroy(zdecoded[b]);
+        }
         pool.clear();
         unmap_all();
     }
@@ -610,8 +660,16 @@ struct Agent::Impl {
         const uint64_t flag_off = (nch + 15) / 16 * 16;
         *out = pool.get(flag_off + 16);
         *reinterpret_cast<volatile uint32_t*>(static_cast<char*>(out->host) + flag_off) = 0;
+        *reinterpret_cast<volatile uint32_t*>(static_cast<char*>(out->host) + flag_off + 4) = 0;
         CUDA_OK(kern::zscan(reinterpret_cast<const void*>(src), nbytes, static_cast<uint8_t*>(out->dev),
-                            reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off), s, 0));
+                            reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off), s, 0,
+                            reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off + 4)));
+    }
+    // Largest stored chunk length recorded by the pre-pass (valid after zscan_result).
+    uint32_t zscan_max(uint64_t nbytes, const PinnedPool::Buf& b) const {
+        if (!b.host) return 0;
+        const uint64_t flag_off = (kern::digest_count(nbytes) + 15) / 16 * 16;
+        return *reinterpret_cast<const volatile uint32_t*>(static_cast<const char*>(b.host) + flag_off + 4);
     }
     bool zscan_result(uint64_t nbytes, PinnedPool::Buf* out) {
         const uint64_t flag_off = (kern::digest_count(nbytes) + 15) / 16 * 16;
@@ -799,6 +857,7 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
         Impl::TensorRec& r = D.tensors[{tensor_id, version}];
         r.offloaded = false;
         r.lease = g.lease_id;
+        r.zmax = z ? D.zscan_max(nbytes, zb) : 0;
     }
     D.launch_d2h(p, ptr, host, dev, D.stream_of(stream), D.opt.hash_on_evict);
     D.complete_or_queue(std::move(p), wait);
@@ -992,12 +1051,14 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
     Impl& D = *d_;
     RestoreOutcome out;
     std::vector<uint64_t> expect;
+    uint32_t zmax = 0;
     {
         std::lock_guard<std::mutex> g(D.tab_mu);
         auto it = D.tensors.find({tensor_id, version});
         if (it != D.tensors.end()) {
             if (ro.verify) expect = it->second.digests;
             it->second.restored = false;
+            zmax = it->second.zmax;
         }
     }
     RequestPrefetchRequest pr;
@@ -1092,7 +1153,10 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
         std::memset(p.mism.host, 0, 4);
         mism_dev = static_cast<uint32_t*>(p.mism.dev);
     }
-    if (z) {
+    if (z && D.opt.coded_restore == "copy_engine" && ro.cast == 0 && !exp_dev && zmax > 0 &&
+        (reinterpret_cast<uintptr_t>(host) & 15) == 0 && (ptr & 15) == 0) {
+        D.restore_z_ce(host, reinterpret_cast<uint8_t*>(ptr), src_bytes, zmax, s);
+    } else if (z) {
         CUDA_OK(kern::restore_z(dev, reinterpret_cast<void*>(ptr), src_bytes, kern::Cast(ro.cast),
                                 reinterpret_cast<float*>(ro.scales_ptr), exp_dev, mism_dev, s, D.opt.restore_ctas));
     } else if ((D.opt.engine == "copy_engine" || D.opt.uncoded == "copy_engine") && ro.cast == 0 && !exp_dev) {

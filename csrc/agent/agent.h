@@ -48,6 +48,13 @@ struct AgentOptions {
     //   "sm"           per-thread K1 / K2.
     // Restores that verify digests or cast always run K2.
     std::string uncoded = "copy_engine";
+    // How a zbf16-coded run comes back: "copy_engine" (the copy engine moves
+    // each chunk's stored bytes as one strided copy into device staging, in
+    // pieces, while K2 decodes the previous piece from HBM; about 8 % more
+    // host-read bandwidth than SM loads) or "sm" (K2 decodes straight from
+    // host memory). The first needs the run's largest stored chunk, known to
+    // the session that evicted it; restores that verify or cast use K2.
+    std::string coded_restore = "copy_engine";
     int evict_ctas = 0, restore_ctas = 0, hash_ctas = 0;
     bool hash_on_evict = true;
     bool use_ring = true;

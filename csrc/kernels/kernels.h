@@ -76,8 +76,11 @@ cudaError_t quant_fp8_block(const void* bf16_src, void* fp8_dst, float* scales, 
 // object must move uncoded). evict_z / restore_z: K1 / K2 over a coded run;
 // all require zbf16::eligible(nbytes) and 16-byte aligned pointers. restore_z
 // supports Cast::kNone, kBf16ToFp8Block128 and kBf16ToFp32.
+// `max_coded` (device-accessible u32, may be null; the caller zeroes it)
+// receives the largest stored length of any chunk: what a strided copy of the
+// coded run must move per 64 KiB row.
 cudaError_t zscan(const void* src_dev, uint64_t nbytes, uint8_t* ebase, uint32_t* fail, cudaStream_t stream,
-                  int ctas);
+                  int ctas, uint32_t* max_coded = nullptr);
 cudaError_t evict_z(const void* src_dev, void* dst_mapped, uint64_t nbytes, const uint8_t* ebase,
                     uint64_t* digests, cudaStream_t stream, int ctas);
 cudaError_t restore_z(const void* src_mapped, void* dst_dev, uint64_t nbytes, Cast cast, float* scales_dev,

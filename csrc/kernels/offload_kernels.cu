@@ -277,7 +277,7 @@ __device__ __forceinline__ uint32_t half_of(const uint4& v, int j) {
 // per chunk, so the pass runs at HBM rate. Every thread of the block calls
 // this; `red` is reused on return.
 __device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uint32_t len, uint8_t* eb_out,
-                                            uint32_t* fail, uint32_t* red) {
+                                            uint32_t* fail, uint32_t* red, uint32_t* max_coded = nullptr) {
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const uint32_t nvec = len / 16;
     uint4 v[kVecs];
@@ -319,13 +319,16 @@ __device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uin
 #pragma unroll
         for (int w = 0; w < kThreads / 32; ++w) esc += red[w];
         *eb_out = uint8_t(eb);
-        if (zbf16::coded_len(len, esc) > len) atomicOr(fail, 1u);
+        const uint32_t clen = zbf16::coded_len(len, esc);
+        if (clen > len) atomicOr(fail, 1u);
+        if (max_coded) atomicMax(max_coded, clen);
     }
     __syncthreads();  // red[] is reused by the next chunk
 }
 
 __global__ void __launch_bounds__(kThreads, 3)
-    k_zscan(const uint8_t* __restrict__ src, uint64_t nbytes, uint8_t* __restrict__ ebase_out, uint32_t* fail, KernelStamp* ks) {
+    k_zscan(const uint8_t* __restrict__ src, uint64_t nbytes, uint8_t* __restrict__ ebase_out, uint32_t* fail,
+            uint32_t* max_coded, KernelStamp* ks) {
     StampScope stamp_scope_(ks);
     __shared__ uint32_t red[kThreads / 32];
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
@@ -333,10 +336,13 @@ __global__ void __launch_bounds__(kThreads, 3)
         const uint64_t base = c * kChunk;
         const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
         if (zbf16::raw_by_rule(c, nchunks, len)) {
-            if (threadIdx.x == 0) ebase_out[c] = 0;
+            if (threadIdx.x == 0) {
+                ebase_out[c] = 0;
+                if (max_coded) atomicMax(max_coded, len);  // stored raw
+            }
             continue;  // uniform per chunk
         }
-        zscan_chunk(src + base, len, ebase_out + c, fail, red);
+        zscan_chunk(src + base, len, ebase_out + c, fail, red, max_coded);
     }
 }
 
@@ -837,7 +843,8 @@ cudaError_t restore_cast(const void* src, void* dst, uint64_t nbytes, Cast cast,
     return cudaGetLastError();
 }
 
-cudaError_t zscan(const void* src, uint64_t nbytes, uint8_t* ebase, uint32_t* fail, cudaStream_t s, int ctas) {
+cudaError_t zscan(const void* src, uint64_t nbytes, uint8_t* ebase, uint32_t* fail, cudaStream_t s, int ctas,
+                  uint32_t* max_coded) {
     if (!zbf16::eligible(nbytes) || !aligned16(src) || !ebase || !fail) return cudaErrorInvalidValue;
     int sms = 148;
     int dev = 0;
@@ -847,7 +854,7 @@ cudaError_t zscan(const void* src, uint64_t nbytes, uint8_t* ebase, uint32_t* fa
     int g = ctas > 0 ? ctas : sms * 3;
     if (uint64_t(g) > nchunks) g = int(nchunks);
     KernelStamp* ks = timing_take(kIdZScan, nbytes);
-    k_zscan<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), nbytes, ebase, fail, ks);
+    k_zscan<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), nbytes, ebase, fail, max_coded, ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }

@@ -211,3 +211,31 @@ def test_batch_groups_mixed_items(sock_path):
                 h.discard()
     finally:
         d.stop()
+
+
+@pytest.mark.parametrize("coded_restore", ["copy_engine", "sm"])
+@pytest.mark.parametrize("n", [(8 << 20), (40 << 20) + 4096 + 16 * 37, 1024 * 65536 + 2048])
+def test_coded_restore_forms_are_byte_exact(sock_path, coded_restore, n):
+    """A zbf16-coded run comes back byte-exact both through the copy engine
+    (strided copies of each chunk's stored bytes into staging, decoded from
+    HBM piece by piece) and through K2 decoding from host memory; sizes cover
+    several pieces, a ragged last chunk and a short raw tail."""
+    from statespectre_b200 import in_process_daemon, offload_context
+
+    d = in_process_daemon(socket=sock_path, arena_mb=4096, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", coded_restore=coded_restore) as off:
+            x = torch.randn(n // 2, dtype=torch.bfloat16, device="cuda")
+            x.view(-1)[::997] = 1e-30  # a few escapes per chunk
+            ref = x.clone()
+            h = off.evict(x, wait=True)
+            assert h.coded
+            y = h.restore()
+            torch.cuda.synchronize()
+            assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+            z = torch.empty_like(ref)
+            h.restore_into(z)
+            assert torch.equal(z.view(torch.int16), ref.view(torch.int16))
+            h.discard()
+    finally:
+        d.stop()
