@@ -658,18 +658,22 @@ struct Agent::Impl {
     void zscan_launch(uint64_t src, uint64_t nbytes, cudaStream_t s, PinnedPool::Buf* out) {
         const uint64_t nch = kern::digest_count(nbytes);
         const uint64_t flag_off = (nch + 15) / 16 * 16;
-        *out = pool.get(flag_off + 16);
-        *reinterpret_cast<volatile uint32_t*>(static_cast<char*>(out->host) + flag_off) = 0;
-        *reinterpret_cast<volatile uint32_t*>(static_cast<char*>(out->host) + flag_off + 4) = 0;
+        // [window bases][pad][fail word + 12 pad][kZScanSlots per-CTA stored-length maxima]
+        *out = pool.get(flag_off + 16 + 4 * kern::kZScanSlots);
+        std::memset(static_cast<char*>(out->host) + flag_off, 0, 16 + 4 * kern::kZScanSlots);
         CUDA_OK(kern::zscan(reinterpret_cast<const void*>(src), nbytes, static_cast<uint8_t*>(out->dev),
                             reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off), s, 0,
-                            reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off + 4)));
+                            reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off + 16)));
     }
     // Largest stored chunk length recorded by the pre-pass (valid after zscan_result).
     uint32_t zscan_max(uint64_t nbytes, const PinnedPool::Buf& b) const {
         if (!b.host) return 0;
         const uint64_t flag_off = (kern::digest_count(nbytes) + 15) / 16 * 16;
-        return *reinterpret_cast<const volatile uint32_t*>(static_cast<const char*>(b.host) + flag_off + 4);
+        const volatile uint32_t* m =
+            reinterpret_cast<const volatile uint32_t*>(static_cast<const char*>(b.host) + flag_off + 16);
+        uint32_t w = 0;
+        for (int i = 0; i < kern::kZScanSlots; ++i) w = std::max<uint32_t>(w, uint32_t(m[i]));
+        return w;
     }
     bool zscan_result(uint64_t nbytes, PinnedPool::Buf* out) {
         const uint64_t flag_off = (kern::digest_count(nbytes) + 15) / 16 * 16;

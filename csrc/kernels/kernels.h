@@ -76,9 +76,12 @@ cudaError_t quant_fp8_block(const void* bf16_src, void* fp8_dst, float* scales, 
 // object must move uncoded). evict_z / restore_z: K1 / K2 over a coded run;
 // all require zbf16::eligible(nbytes) and 16-byte aligned pointers. restore_z
 // supports Cast::kNone, kBf16ToFp8Block128 and kBf16ToFp32.
-// `max_coded` (device-accessible u32, may be null; the caller zeroes it)
-// receives the largest stored length of any chunk: what a strided copy of the
-// coded run must move per 64 KiB row.
+// `max_coded` (device-accessible, kZScanSlots u32 slots, may be null; the
+// caller zeroes it): each CTA stores the largest stored length of the chunks
+// it scanned in its own slot (the grid is at most kZScanSlots CTAs then); the
+// maximum over the slots is what a strided copy of the coded run must move
+// per 64 KiB row.
+constexpr int kZScanSlots = 512;
 cudaError_t zscan(const void* src_dev, uint64_t nbytes, uint8_t* ebase, uint32_t* fail, cudaStream_t stream,
                   int ctas, uint32_t* max_coded = nullptr);
 cudaError_t evict_z(const void* src_dev, void* dst_mapped, uint64_t nbytes, const uint8_t* ebase,

@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <set>
@@ -276,8 +277,9 @@ __device__ __forceinline__ uint32_t half_of(const uint4& v, int j) {
 // fit sets *fail and the object is then moved uncoded. Two register passes
 // per chunk, so the pass runs at HBM rate. Every thread of the block calls
 // this; `red` is reused on return.
+// `stored` (may be null; thread 0's value counts) receives the chunk's stored length.
 __device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uint32_t len, uint8_t* eb_out,
-                                            uint32_t* fail, uint32_t* red, uint32_t* max_coded = nullptr) {
+                                            uint32_t* fail, uint32_t* red, uint32_t* stored = nullptr) {
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const uint32_t nvec = len / 16;
     uint4 v[kVecs];
@@ -321,7 +323,7 @@ __device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uin
         *eb_out = uint8_t(eb);
         const uint32_t clen = zbf16::coded_len(len, esc);
         if (clen > len) atomicOr(fail, 1u);
-        if (max_coded) atomicMax(max_coded, clen);
+        if (stored) *stored = clen;
     }
     __syncthreads();  // red[] is reused by the next chunk
 }
@@ -332,18 +334,24 @@ __global__ void __launch_bounds__(kThreads, 3)
     StampScope stamp_scope_(ks);
     __shared__ uint32_t red[kThreads / 32];
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    uint32_t cta_max = 0;  // thread 0: largest stored length of this CTA's chunks
     for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
         const uint64_t base = c * kChunk;
         const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
         if (zbf16::raw_by_rule(c, nchunks, len)) {
             if (threadIdx.x == 0) {
                 ebase_out[c] = 0;
-                if (max_coded) atomicMax(max_coded, len);  // stored raw
+                cta_max = max(cta_max, len);  // stored raw
             }
             continue;  // uniform per chunk
         }
-        zscan_chunk(src + base, len, ebase_out + c, fail, red, max_coded);
+        uint32_t clen = 0;
+        zscan_chunk(src + base, len, ebase_out + c, fail, red, &clen);
+        cta_max = max(cta_max, clen);
     }
+    // One plain store per CTA into its own slot (the slots may be host-mapped
+    // memory: per-chunk atomics there would each cross PCIe); the host reduces.
+    if (max_coded && threadIdx.x == 0) max_coded[blockIdx.x] = cta_max;
 }
 
 // Shared-memory stage of one coded chunk: PCIe moves it with full 16-byte
@@ -845,6 +853,7 @@ cudaError_t restore_cast(const void* src, void* dst, uint64_t nbytes, Cast cast,
 
 cudaError_t zscan(const void* src, uint64_t nbytes, uint8_t* ebase, uint32_t* fail, cudaStream_t s, int ctas,
                   uint32_t* max_coded) {
+    if (max_coded) ctas = ctas > 0 ? std::min(ctas, kZScanSlots) : kZScanSlots;
     if (!zbf16::eligible(nbytes) || !aligned16(src) || !ebase || !fail) return cudaErrorInvalidValue;
     int sms = 148;
     int dev = 0;
