@@ -140,6 +140,11 @@ struct Agent::Impl {
     static constexpr uint64_t kZPiece = 512;
     void* zstage[2] = {nullptr, nullptr};
     cudaEvent_t zcopied[2] = {nullptr, nullptr}, zdecoded[2] = {nullptr, nullptr};
+    cudaEvent_t zstart = nullptr, zdone = nullptr;
+    // Decodes run on their own stream at the device's highest priority: a
+    // restore issues one short decode per piece, and at equal priority each
+    // would queue behind the kernels of a concurrent training step.
+    cudaStream_t zdec = nullptr;
     std::mutex zmu;  // restores on this session share the staging
 
     // The copy engine moves each chunk's stored bytes (`zmax` per 64 KiB row,
@@ -154,7 +159,15 @@ struct Agent::Impl {
                 CUDA_OK(cudaEventCreateWithFlags(&zcopied[b], cudaEventDisableTiming));
                 CUDA_OK(cudaEventCreateWithFlags(&zdecoded[b], cudaEventDisableTiming));
             }
+            CUDA_OK(cudaEventCreateWithFlags(&zstart, cudaEventDisableTiming));
+            CUDA_OK(cudaEventCreateWithFlags(&zdone, cudaEventDisableTiming));
+            int lo = 0, hi = 0;
+            cudaDeviceGetStreamPriorityRange(&lo, &hi);
+            CUDA_OK(cudaStreamCreateWithPriority(&zdec, cudaStreamNonBlocking, hi));
         }
+        // the decodes write dst after the work already queued on the caller's stream
+        CUDA_OK(cudaEventRecord(zstart, s));
+        CUDA_OK(cudaStreamWaitEvent(zdec, zstart, 0));
         const uint64_t nch = (nbytes + C - 1) / C;
         const size_t width = std::min<size_t>((size_t(zmax) + 15) / 16 * 16, C);
         const bool short_tail = nbytes - (nch - 1) * C < zbf16::kRawTail;
@@ -168,13 +181,15 @@ struct Agent::Impl {
             if (k >= 2) CUDA_OK(cudaStreamWaitEvent(side, zdecoded[b], 0));  // staging b decoded before reuse
             CUDA_OK(cudaMemcpy2DAsync(zstage[b], C, host + c0 * C, C, width, c1 - c0, cudaMemcpyHostToDevice, side));
             CUDA_OK(cudaEventRecord(zcopied[b], side));
-            CUDA_OK(cudaStreamWaitEvent(s, zcopied[b], 0));
+            CUDA_OK(cudaStreamWaitEvent(zdec, zcopied[b], 0));
             const uint64_t piece = std::min(nbytes, c1 * C) - c0 * C;
-            CUDA_OK(kern::restore_z(zstage[b], dst + c0 * C, piece, kern::Cast::kNone, nullptr, nullptr, nullptr, s,
+            CUDA_OK(kern::restore_z(zstage[b], dst + c0 * C, piece, kern::Cast::kNone, nullptr, nullptr, nullptr, zdec,
                                     opt.restore_ctas));
-            CUDA_OK(cudaEventRecord(zdecoded[b], s));
+            CUDA_OK(cudaEventRecord(zdecoded[b], zdec));
             c0 = c1;
         }
+        CUDA_OK(cudaEventRecord(zdone, zdec));
+        CUDA_OK(cudaStreamWaitEvent(s, zdone, 0));  // the caller's stream continues after the last decode
     }
     PinnedPool pool;
 
@@ -319,6 +334,9 @@ struct Agent::Impl {
             if (zcopied[b]) cudaEventDestroy(zcopied[b]);
             if (zdecoded[b]) cudaEventDestroy(zdecoded[b]);
         }
+        if (zstart) cudaEventDestroy(zstart);
+        if (zdone) cudaEventDestroy(zdone);
+        if (zdec) cudaStreamDestroy(zdec);
         pool.clear();
         unmap_all();
     }
