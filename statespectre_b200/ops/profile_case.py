@@ -31,7 +31,8 @@ def main():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--ctas", type=int, default=0)
     ap.add_argument("--stages", type=int, default=0, help="hash_stream: 2, 3 or 4 staged halves per CTA (0: default)")
-    ap.add_argument("--peer", type=int, default=-1, help="device of the push destination (default: same GPU)")
+    ap.add_argument("--peer", type=int, default=-1,
+                    help="device of the push destination or of the copy verify compares against (default: same GPU)")
     ap.add_argument("--items", type=int, default=64, help="push: split the buffer into this many tensors")
     ap.add_argument("--delta", type=int, default=0,
                     help="push: 1 = delta mode with the destination table cleared before each launch "
@@ -53,6 +54,14 @@ def main():
     if a.kernel in ("zscan", "evict_z", "restore_z"):  # zbf16: window bases, then the coded host copy
         C.k_zscan(x.data_ptr(), n, zeb.data_ptr(), err.data_ptr(), s, 0)
         C.k_evict_z(x.data_ptr(), host.data_ptr(), n, zeb.data_ptr(), dig.data_ptr(), s, a.ctas)
+    if a.kernel == "verify":
+        # K3 compares x with a second copy: on this GPU, or with --peer on that
+        # GPU (plain peer loads over NVLink); the copy goes through host memory
+        if a.peer >= 0:
+            C.enable_peer(a.peer)
+            out = torch.empty(n, dtype=torch.uint8, device=torch.device("cuda", a.peer))
+        out.copy_(x.view(torch.uint8).cpu())
+        torch.cuda.synchronize()
     pusher = None
     if a.kernel.startswith("push"):
         from ..parallel.weight_sync import WeightLayout, WeightPusher
@@ -101,6 +110,8 @@ def main():
     ev1.record()
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / a.iters
+    if a.kernel == "verify" and int(mism.item()) != 0:
+        raise SystemExit(f"verify: {int(mism.item())} vectors differ")
     if int(err.item()) != 0 or (pusher is not None and pusher.result()["error"]):
         code = int(err.item()) if pusher is None else pusher.result()["error"]
         raise SystemExit(f"{a.kernel}: device status {code}")
