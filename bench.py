@@ -71,6 +71,8 @@ def parse():
     p.add_argument("--engine", default="kernel", choices=["kernel", "copy_engine"])
     p.add_argument("--uncoded", default="copy_engine", choices=["copy_engine", "bulk", "sm"],
                    help="kernel engine: how bytes that are not zbf16-coded move")
+    p.add_argument("--coded-evict", default="sm", choices=["copy_engine", "sm"],
+                   help="how zbf16-coded evicts leave the GPU (K1 into host memory, or via staging + copy engine)")
     p.add_argument("--coded-restore", default="copy_engine", choices=["copy_engine", "sm"],
                    help="how zbf16-coded runs come back (strided copy-engine copies + HBM decode, or K2 from host)")
     p.add_argument("--evict-ctas", type=int, default=0)
@@ -204,7 +206,7 @@ def main():
                            eager_register=True, engine=args.engine, evict_ctas=args.evict_ctas,
                            restore_ctas=args.restore_ctas, hash_on_evict=bool(args.hash), stream_priority=-1,
                            compress=bool(args.compress), kernel_timing=bool(args.kernel_timing),
-                           uncoded=args.uncoded, coded_restore=args.coded_restore)
+                           uncoded=args.uncoded, coded_restore=args.coded_restore, coded_evict=args.coded_evict)
     off = sess.off
     g = torch.Generator(device=device)
     g.manual_seed(1234 + rank)
@@ -348,7 +350,7 @@ def main():
                 "tensor_bytes": nbytes, "global_batch": world, "seq_len": 0, "parallelism": f"dp{world}",
                 "concurrent_matmul": "8192x8192 bf16 loop" if args.matmul else "none",
                 "engine": args.engine, "hash": bool(args.hash), "slot_mb": 64,
-                "uncoded_form": args.uncoded, "coded_restore": args.coded_restore,
+                "uncoded_form": args.uncoded, "coded_evict": args.coded_evict, "coded_restore": args.coded_restore,
                 "transfer_coding": coding,
                 "l2": "inputs (1 GiB) larger than the 126 MB L2; no flush needed",
                 "baseline": f"StateSpectre H20 PCIe Gen5 1 GiB: D2H {BASELINE_D2H_GBS}, H2D {BASELINE_H2D_GBS} GB/s "

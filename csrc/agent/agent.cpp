@@ -139,25 +139,64 @@ struct Agent::Impl {
     // kZPiece chunks each (allocated on first use, 2 x 32 MiB) and their events.
     static constexpr uint64_t kZPiece = 512;
     void* zstage[2] = {nullptr, nullptr};
-    cudaEvent_t zcopied[2] = {nullptr, nullptr}, zdecoded[2] = {nullptr, nullptr};
+    // zfull[b]: staging b holds a piece (recorded by its producer); zfree[b]:
+    // nothing reads staging b any more (recorded by its consumer). Every
+    // writer of b waits zfree[b], whichever operation used it last.
+    cudaEvent_t zfull[2] = {nullptr, nullptr}, zfree[2] = {nullptr, nullptr};
     cudaEvent_t zstart = nullptr, zdone = nullptr;
     // Decodes run on their own stream at the device's highest priority: a
     // restore issues one short decode per piece, and at equal priority each
     // would queue behind the kernels of a concurrent training step.
     cudaStream_t zdec = nullptr;
-    std::mutex zmu;  // restores on this session share the staging
+    std::mutex zmu;  // coded evicts and restores of this session share the staging
 
-    // The copy engine moves each chunk's stored bytes (`zmax` per 64 KiB row,
-    // one strided copy per piece) into staging on the side stream; K2 decodes
-    // the piece from HBM on `s`, overlapping the next piece's copy.
-    void restore_z_ce(const char* host, uint8_t* dst, uint64_t nbytes, uint32_t zmax, cudaStream_t s) {
+    // Piece boundaries of a coded run: kZPiece chunks each, except that a
+    // short raw tail never sits alone (a piece must itself be a codable
+    // object): the piece before it gives up one chunk.
+    static uint64_t zpiece_end(uint64_t c0, uint64_t nch, bool short_tail) {
+        uint64_t c1 = std::min(nch, c0 + kZPiece);
+        if (short_tail && nch - c1 == 1) c1 -= 1;  // pieces that leave one chunk are full, so > 1
+        return c1;
+    }
+
+    // Coded evict through the copy engine: K1 codes a piece into staging (HBM,
+    // digests from the same pass) on the top-priority stream while the copy
+    // engine moves the previous piece's stored bytes (`zmax` per 64 KiB row)
+    // into the host run on the side stream.
+    void evict_z_ce(const uint8_t* src, char* host, uint64_t nbytes, const uint8_t* ebase, uint64_t* dig,
+                    uint32_t zmax, cudaStream_t s) {
         std::lock_guard<std::mutex> g(zmu);
         constexpr uint64_t C = zbf16::kChunk;
+        zstage_init();
+        const uint64_t nch = (nbytes + C - 1) / C;
+        const size_t width = std::min<size_t>((size_t(zmax) + 15) / 16 * 16, C);
+        const bool short_tail = nbytes - (nch - 1) * C < zbf16::kRawTail;
+        CUDA_OK(cudaEventRecord(zstart, s));  // the source is complete on the caller's stream
+        CUDA_OK(cudaStreamWaitEvent(zdec, zstart, 0));
+        uint64_t c0 = 0;
+        for (int k = 0; c0 < nch; ++k) {
+            const uint64_t c1 = zpiece_end(c0, nch, short_tail);
+            const int b = k & 1;
+            CUDA_OK(cudaStreamWaitEvent(zdec, zfree[b], 0));  // the last reader of staging b is done
+            const uint64_t piece = std::min(nbytes, c1 * C) - c0 * C;
+            CUDA_OK(kern::evict_z(src + c0 * C, zstage[b], piece, ebase + c0, dig ? dig + c0 : nullptr, zdec,
+                                  opt.evict_ctas));
+            CUDA_OK(cudaEventRecord(zfull[b], zdec));
+            CUDA_OK(cudaStreamWaitEvent(side, zfull[b], 0));
+            CUDA_OK(cudaMemcpy2DAsync(host + c0 * C, C, zstage[b], C, width, c1 - c0, cudaMemcpyDeviceToHost, side));
+            CUDA_OK(cudaEventRecord(zfree[b], side));
+            c0 = c1;
+        }
+        CUDA_OK(cudaEventRecord(zdone, side));
+        CUDA_OK(cudaStreamWaitEvent(s, zdone, 0));  // the evict completes on the caller's stream
+    }
+
+    void zstage_init() {
         if (!zstage[0]) {
             for (int b = 0; b < 2; ++b) {
-                CUDA_OK(cudaMalloc(&zstage[b], kZPiece * C));
-                CUDA_OK(cudaEventCreateWithFlags(&zcopied[b], cudaEventDisableTiming));
-                CUDA_OK(cudaEventCreateWithFlags(&zdecoded[b], cudaEventDisableTiming));
+                CUDA_OK(cudaMalloc(&zstage[b], kZPiece * zbf16::kChunk));
+                CUDA_OK(cudaEventCreateWithFlags(&zfull[b], cudaEventDisableTiming));
+                CUDA_OK(cudaEventCreateWithFlags(&zfree[b], cudaEventDisableTiming));
             }
             CUDA_OK(cudaEventCreateWithFlags(&zstart, cudaEventDisableTiming));
             CUDA_OK(cudaEventCreateWithFlags(&zdone, cudaEventDisableTiming));
@@ -165,6 +204,16 @@ struct Agent::Impl {
             cudaDeviceGetStreamPriorityRange(&lo, &hi);
             CUDA_OK(cudaStreamCreateWithPriority(&zdec, cudaStreamNonBlocking, hi));
         }
+    }
+
+    // Coded restore through the copy engine: each chunk's stored bytes (`zmax`
+    // per 64 KiB row, one strided copy per piece) go into staging on the side
+    // stream; K2 decodes the piece from HBM on the top-priority stream,
+    // overlapping the next piece's copy, and the caller's stream joins at the end.
+    void restore_z_ce(const char* host, uint8_t* dst, uint64_t nbytes, uint32_t zmax, cudaStream_t s) {
+        std::lock_guard<std::mutex> g(zmu);
+        constexpr uint64_t C = zbf16::kChunk;
+        zstage_init();
         // the decodes write dst after the work already queued on the caller's stream
         CUDA_OK(cudaEventRecord(zstart, s));
         CUDA_OK(cudaStreamWaitEvent(zdec, zstart, 0));
@@ -173,19 +222,16 @@ struct Agent::Impl {
         const bool short_tail = nbytes - (nch - 1) * C < zbf16::kRawTail;
         uint64_t c0 = 0;
         for (int k = 0; c0 < nch; ++k) {
-            uint64_t c1 = std::min(nch, c0 + kZPiece);
-            // a short raw tail never sits alone in a piece (a piece must be a codable object):
-            // the piece before it gives up one chunk (pieces that leave one chunk are full, so > 1)
-            if (short_tail && nch - c1 == 1) c1 -= 1;
+            const uint64_t c1 = zpiece_end(c0, nch, short_tail);
             const int b = k & 1;
-            if (k >= 2) CUDA_OK(cudaStreamWaitEvent(side, zdecoded[b], 0));  // staging b decoded before reuse
+            CUDA_OK(cudaStreamWaitEvent(side, zfree[b], 0));  // the last reader of staging b is done
             CUDA_OK(cudaMemcpy2DAsync(zstage[b], C, host + c0 * C, C, width, c1 - c0, cudaMemcpyHostToDevice, side));
-            CUDA_OK(cudaEventRecord(zcopied[b], side));
-            CUDA_OK(cudaStreamWaitEvent(zdec, zcopied[b], 0));
+            CUDA_OK(cudaEventRecord(zfull[b], side));
+            CUDA_OK(cudaStreamWaitEvent(zdec, zfull[b], 0));
             const uint64_t piece = std::min(nbytes, c1 * C) - c0 * C;
             CUDA_OK(kern::restore_z(zstage[b], dst + c0 * C, piece, kern::Cast::kNone, nullptr, nullptr, nullptr, zdec,
                                     opt.restore_ctas));
-            CUDA_OK(cudaEventRecord(zdecoded[b], zdec));
+            CUDA_OK(cudaEventRecord(zfree[b], zdec));
             c0 = c1;
         }
         CUDA_OK(cudaEventRecord(zdone, zdec));
@@ -235,6 +281,8 @@ struct Agent::Impl {
             throw std::invalid_argument("uncoded must be copy_engine, bulk or sm, not '" + opt.uncoded + "'");
         if (opt.coded_restore != "copy_engine" && opt.coded_restore != "sm")
             throw std::invalid_argument("coded_restore must be copy_engine or sm, not '" + opt.coded_restore + "'");
+        if (opt.coded_evict != "copy_engine" && opt.coded_evict != "sm")
+            throw std::invalid_argument("coded_evict must be copy_engine or sm, not '" + opt.coded_evict + "'");
         gpu = opt.device >= 0;
         if (gpu) {
             CUDA_OK(cudaSetDevice(opt.device));
@@ -331,8 +379,8 @@ struct Agent::Impl {
         if (side) cudaStreamDestroy(side);
         for (int b = 0; b < 2; ++b) {
             if (zstage[b]) cudaFree(zstage[b]);
-            if (zcopied[b]) cudaEventDestroy(zcopied[b]);
-            if (zdecoded[b]) cudaEventDestroy(zdecoded[b]);
+            if (zfull[b]) cudaEventDestroy(zfull[b]);
+            if (zfree[b]) cudaEventDestroy(zfree[b]);
         }
         if (zstart) cudaEventDestroy(zstart);
         if (zdone) cudaEventDestroy(zdone);
@@ -735,7 +783,12 @@ struct Agent::Impl {
             p.dig = pool.get(std::max<uint64_t>(p.ndig, 1) * 8);
             dig_dev = static_cast<uint64_t*>(p.dig.dev);
         }
-        if (p.z) {
+        const uint32_t zmax = p.z ? zscan_max(p.nbytes, p.zb) : 0;
+        if (p.z && opt.coded_evict == "copy_engine" && zmax > 0 && (src & 15) == 0 &&
+            (reinterpret_cast<uintptr_t>(dst_host) & 15) == 0) {
+            evict_z_ce(reinterpret_cast<const uint8_t*>(src), dst_host, p.nbytes, static_cast<const uint8_t*>(p.zb.dev),
+                       dig_dev, zmax, s);
+        } else if (p.z) {
             CUDA_OK(kern::evict_z(reinterpret_cast<const void*>(src), dst_dev, p.nbytes,
                                   static_cast<const uint8_t*>(p.zb.dev), dig_dev, s, opt.evict_ctas));
         } else if (opt.engine == "copy_engine" || opt.uncoded == "copy_engine") {

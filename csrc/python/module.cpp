@@ -221,6 +221,7 @@ class PyAgent {
             else if (k == "engine") o.engine = v.cast<std::string>();
             else if (k == "uncoded") o.uncoded = v.cast<std::string>();
             else if (k == "coded_restore") o.coded_restore = v.cast<std::string>();
+            else if (k == "coded_evict") o.coded_evict = v.cast<std::string>();
             else if (k == "evict_ctas") o.evict_ctas = v.cast<int>();
             else if (k == "restore_ctas") o.restore_ctas = v.cast<int>();
             else if (k == "hash_ctas") o.hash_ctas = v.cast<int>();

@@ -213,23 +213,27 @@ def test_batch_groups_mixed_items(sock_path):
         d.stop()
 
 
-@pytest.mark.parametrize("coded_restore", ["copy_engine", "sm"])
+@pytest.mark.parametrize("coded_evict,coded_restore", [("sm", "copy_engine"), ("sm", "sm"),
+                                                         ("copy_engine", "copy_engine"), ("copy_engine", "sm")])
 @pytest.mark.parametrize("n", [(8 << 20), (40 << 20) + 4096 + 16 * 37, 1024 * 65536 + 2048])
-def test_coded_restore_forms_are_byte_exact(sock_path, coded_restore, n):
-    """A zbf16-coded run comes back byte-exact both through the copy engine
-    (strided copies of each chunk's stored bytes into staging, decoded from
-    HBM piece by piece) and through K2 decoding from host memory; sizes cover
-    several pieces, a ragged last chunk and a short raw tail."""
+def test_coded_transfer_forms_are_byte_exact(sock_path, coded_evict, coded_restore, n):
+    """A zbf16-coded run is byte-exact through every combination of the
+    transfer forms: K1 coding into the host run or into device staging moved
+    by the copy engine, and K2 decoding from host memory or from staging
+    filled by the copy engine; the content hash equals the host oracle's.
+    Sizes cover several pieces, a ragged last chunk and a short raw tail."""
     from statespectre_b200 import in_process_daemon, offload_context
 
     d = in_process_daemon(socket=sock_path, arena_mb=4096, drain_on_complete=False)
     try:
-        with offload_context(daemon_addr=sock_path, device="cuda:0", coded_restore=coded_restore) as off:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", coded_restore=coded_restore,
+                             coded_evict=coded_evict) as off:
             x = torch.randn(n // 2, dtype=torch.bfloat16, device="cuda")
             x.view(-1)[::997] = 1e-30  # a few escapes per chunk
             ref = x.clone()
             h = off.evict(x, wait=True)
             assert h.coded
+            assert h.content_hash == native().ssh_hash(ref.cpu().view(torch.uint8).numpy())
             y = h.restore()
             torch.cuda.synchronize()
             assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
@@ -237,5 +241,34 @@ def test_coded_restore_forms_are_byte_exact(sock_path, coded_restore, n):
             h.restore_into(z)
             assert torch.equal(z.view(torch.int16), ref.view(torch.int16))
             h.discard()
+    finally:
+        d.stop()
+
+
+def test_copy_engine_evicts_and_restores_back_to_back_share_staging(sock_path):
+    """Asynchronous coded evicts and restores issued back to back on one
+    session share the device staging: each waits for the last reader of a
+    staging buffer before writing it, so every tensor comes back intact."""
+    from statespectre_b200 import in_process_daemon, offload_context
+
+    d = in_process_daemon(socket=sock_path, arena_mb=2048, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", coded_restore="copy_engine",
+                             coded_evict="copy_engine") as off:
+            xs = [torch.randn((48 << 20) // 2 + 4096 * i, dtype=torch.bfloat16, device="cuda") for i in range(4)]
+            refs = [x.clone() for x in xs]
+            hs = [off.copy(x) for x in xs]  # asynchronous
+            outs = [torch.empty_like(r) for r in refs]
+            for h, o in zip(hs, outs):
+                h.wait_offloaded()
+                h.restore_into(o, wait=False)
+            h2 = off.copy(xs[0])  # an evict queued behind the restores
+            torch.cuda.synchronize()
+            h2.wait_offloaded()
+            for o, r in zip(outs, refs):
+                assert torch.equal(o.view(torch.int16), r.view(torch.int16))
+            back = torch.empty_like(refs[0])
+            h2.restore_into(back)
+            assert torch.equal(back.view(torch.int16), refs[0].view(torch.int16))
     finally:
         d.stop()
