@@ -71,7 +71,7 @@ def parse():
     p.add_argument("--engine", default="kernel", choices=["kernel", "copy_engine"])
     p.add_argument("--uncoded", default="copy_engine", choices=["copy_engine", "bulk", "sm"],
                    help="kernel engine: how bytes that are not zbf16-coded move")
-    p.add_argument("--coded-evict", default="sm", choices=["copy_engine", "sm"],
+    p.add_argument("--coded-evict", default="copy_engine", choices=["copy_engine", "sm"],
                    help="how zbf16-coded evicts leave the GPU (K1 into host memory, or via staging + copy engine)")
     p.add_argument("--coded-restore", default="copy_engine", choices=["copy_engine", "sm"],
                    help="how zbf16-coded runs come back (strided copy-engine copies + HBM decode, or K2 from host)")

@@ -55,11 +55,11 @@ struct AgentOptions {
     // host memory). The first needs the run's largest stored chunk, known to
     // the session that evicted it; restores that verify or cast use K2.
     std::string coded_restore = "copy_engine";
-    // How a zbf16 evict leaves the GPU: "sm" (K1 codes straight into the
-    // host-mapped run) or "copy_engine" (K1 codes into device staging at HBM
-    // rate and the copy engine moves each chunk's stored bytes, piece by
-    // piece, as strided copies).
-    std::string coded_evict = "sm";
+    // How a zbf16 evict leaves the GPU: "copy_engine" (K1 codes into device
+    // staging at HBM rate, digests from the same pass, and the copy engine
+    // moves each chunk's stored bytes, piece by piece, as strided copies) or
+    // "sm" (K1 codes straight into the host-mapped run).
+    std::string coded_evict = "copy_engine";
     int evict_ctas = 0, restore_ctas = 0, hash_ctas = 0;
     bool hash_on_evict = true;
     bool use_ring = true;
