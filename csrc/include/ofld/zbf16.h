@@ -19,7 +19,23 @@
 // with n = len / 2 elements. The window is anchored at the top: ebase =
 // max(emax - 14, 0) for the chunk's largest exponent emax, so only values
 // more than 14 binades below the chunk's largest escape (for N(0, s) data a
-// few per chunk). A coded chunk must fit in its own raw length (so every byte of an object stays inside [0, nbytes)
+// few per chunk). That is mode 1 (header mode byte 1, 12 bits per value).
+//
+// Mode 2 (header mode byte 2, 11 bits per value): the code plane holds 3-bit
+// codes, 3 bytes per 16-byte source vector (the vector's 8 codes as one
+// little-endian 24-bit value, element j in bits 3j..3j+2), and the window is
+// the top 7 binades: base = ebase + 8 (mode 1's base plus 8, stored in the
+// header), code = exponent - base when that is 0..6, else 7 (escape):
+//
+//   16                 low plane (n bytes, as in mode 1)
+//   16 + n             code plane (3 * n / 8 bytes)
+//   16 + n + 3n/8      escape bytes, in the same lane order as mode 1
+//
+// A chunk is stored in mode 2 when mode 1's base is above 0 and mode 2 is
+// strictly shorter (it is for Gaussian-like data: the eighth binade below the
+// top holds fewer than 1/8 of the values); ties and base 0 stay mode 1. The
+// GPU pre-pass, the GPU coder and this reference apply the same rule, so the
+// coded bytes are identical. A coded chunk must fit in its own raw length (so every byte of an object stays inside [0, nbytes)
 // of its pinned run and tiers that copy nbytes keep it intact). A final
 // chunk shorter than kRawTail bytes is stored raw (decided from nbytes
 // alone). An object is coded only when every other chunk fits; the format is
@@ -69,6 +85,35 @@ SSH_HD uint32_t coded_len(uint32_t len, uint32_t n_esc) {
     const uint32_t n = len / 2;
     return kHeader + n + n / 2 + n_esc;
 }
+// ---- mode 2: 3-bit codes over the top 7 binades -----------------------------
+constexpr uint32_t kWindow3 = 7;
+constexpr uint32_t kEscape3 = 7;
+constexpr uint32_t kBase3Offset = 8;  // mode 2 base = mode 1 base + 8
+SSH_HD uint32_t code3_of(uint32_t e, uint32_t base3) {
+    const uint32_t d = e - base3;  // wraps below base3
+    return d < kWindow3 ? d : kEscape3;
+}
+SSH_HD uint32_t coded_len3(uint32_t len, uint32_t n_esc3) {
+    const uint32_t n = len / 2;
+    return kHeader + n + (n / 8) * 3 + n_esc3;
+}
+// Mode 2 escapes from the mode-1 statistics of a chunk: the mode-1 escapes
+// (below base or above base + 14, never above for a top-anchored base) plus
+// the values in the lowest 8 binades of the mode-1 window.
+SSH_HD uint32_t escapes3(uint32_t esc1, uint32_t low8) { return esc1 + low8; }
+// Whether an element falls in the lowest 8 binades of the mode-1 window.
+SSH_HD bool in_low8(uint32_t e, uint32_t ebase) { return e - ebase < kBase3Offset; }
+// The stored mode and length of a chunk (the shared selection rule).
+SSH_HD uint32_t choose_mode(uint32_t len, uint32_t ebase, uint32_t esc1, uint32_t low8, uint32_t* stored) {
+    const uint32_t l1 = coded_len(len, esc1);
+    const uint32_t l2 = coded_len3(len, escapes3(esc1, low8));
+    if (ebase > 0 && l2 < l1) {
+        *stored = l2;
+        return 2;
+    }
+    *stored = l1;
+    return 1;
+}
 // Whether chunk c (of `nchunks`, raw length len) is stored raw by rule.
 SSH_HD bool raw_by_rule(uint64_t c, uint64_t nchunks, uint32_t len) { return c + 1 == nchunks && len < kRawTail; }
 // Objects that can be coded at all: 16-byte multiple, at least one chunk.
@@ -99,23 +144,38 @@ inline uint32_t encode_chunk(const uint8_t* src, uint32_t len, uint8_t* out) {
     uint32_t emax = 0;
     for (uint32_t i = 0; i < n; ++i) emax = exponent(h[i]) > emax ? exponent(h[i]) : emax;
     const uint32_t ebase = window_base(emax);
-    uint32_t n_esc = 0;
-    for (uint32_t i = 0; i < n; ++i) n_esc += code_of(exponent(h[i]), ebase) == kEscape;
-    const uint32_t total = coded_len(len, n_esc);
+    uint32_t esc1 = 0, low8 = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        esc1 += code_of(exponent(h[i]), ebase) == kEscape;
+        low8 += in_low8(exponent(h[i]), ebase);
+    }
+    uint32_t total = 0;
+    const uint32_t mode = choose_mode(len, ebase, esc1, low8, &total);
     if (total > len) return 0;
-    Header hd{kTag, 1, uint8_t(ebase), n_esc, len, total};
+    const uint32_t base = mode == 2 ? ebase + kBase3Offset : ebase;
+    auto code = [&](uint32_t e) { return mode == 2 ? code3_of(e, base) : code_of(e, base); };
+    const uint32_t escape = mode == 2 ? kEscape3 : kEscape;
+    const uint32_t plane = mode == 2 ? (n / 8) * 3 : n / 2;
+    Header hd{kTag, uint8_t(mode), uint8_t(base), total - (kHeader + n + plane), len, total};
     std::memcpy(out, &hd, kHeader);
     uint8_t* low = out + kHeader;
     uint8_t* codes = low + n;
-    uint8_t* esc = codes + n / 2;
-    std::memset(codes, 0, n / 2);
+    uint8_t* esc = codes + plane;
+    std::memset(codes, 0, plane);
     for (uint32_t i = 0; i < n; ++i) {
         low[i] = low_byte(h[i]);
-        codes[i / 2] |= uint8_t(code_of(exponent(h[i]), ebase) << (4 * (i & 1)));
+        const uint32_t cd = code(exponent(h[i]));
+        if (mode == 2) {
+            const uint32_t bit = (i / 8) * 24 + (i % 8) * 3;  // vector i/8, element i%8
+            for (uint32_t b = 0; b < 3; ++b)
+                codes[(bit + b) / 8] |= uint8_t(((cd >> b) & 1u) << ((bit + b) % 8));
+        } else {
+            codes[i / 2] |= uint8_t(cd << (4 * (i & 1)));
+        }
     }
     uint32_t k = 0;
     for_each_in_lane_order(len, [&](uint32_t i) {
-        if (code_of(exponent(h[i]), ebase) == kEscape) esc[k++] = uint8_t(exponent(h[i]));
+        if (code(exponent(h[i])) == escape) esc[k++] = uint8_t(exponent(h[i]));
     });
     return total;
 }
@@ -124,23 +184,29 @@ inline uint32_t encode_chunk(const uint8_t* src, uint32_t len, uint8_t* out) {
 inline bool decode_chunk(const uint8_t* in, uint32_t len, uint8_t* out) {
     Header hd;
     std::memcpy(&hd, in, kHeader);
-    if (hd.tag != kTag || hd.mode != 1 || hd.src_len != len || hd.comp_len != coded_len(len, hd.n_esc) ||
-        hd.comp_len > len)
+    if (hd.tag != kTag || (hd.mode != 1 && hd.mode != 2) || hd.src_len != len || hd.comp_len > len ||
+        hd.comp_len != (hd.mode == 2 ? coded_len3(len, hd.n_esc) : coded_len(len, hd.n_esc)))
         return false;
     const uint32_t n = len / 2;
+    const bool m2 = hd.mode == 2;
     const uint8_t* low = in + kHeader;
     const uint8_t* codes = low + n;
-    const uint8_t* esc = codes + n / 2;
+    const uint8_t* esc = codes + (m2 ? (n / 8) * 3 : n / 2);
+    const uint32_t escape = m2 ? kEscape3 : kEscape;
+    auto code_at = [&](uint32_t i) -> uint32_t {
+        if (!m2) return (codes[i / 2] >> (4 * (i & 1))) & 15u;
+        const uint32_t bit = (i / 8) * 24 + (i % 8) * 3;
+        uint32_t c = 0;
+        for (uint32_t b = 0; b < 3; ++b) c |= ((codes[(bit + b) / 8] >> ((bit + b) % 8)) & 1u) << b;
+        return c;
+    };
     std::vector<uint16_t> h(n);
-    for (uint32_t i = 0; i < n; ++i) {
-        const uint32_t c = (codes[i / 2] >> (4 * (i & 1))) & 15u;
-        h[i] = rebuild(low[i], hd.ebase + c);  // escapes patched below
-    }
+    for (uint32_t i = 0; i < n; ++i) h[i] = rebuild(low[i], hd.ebase + code_at(i));  // escapes patched below
     uint32_t k = 0;
     bool ok = true;
     for_each_in_lane_order(len, [&](uint32_t i) {
-        const uint32_t c = (codes[i / 2] >> (4 * (i & 1))) & 15u;
-        if (c == kEscape) {
+        const uint32_t c = code_at(i);
+        if (c == escape) {
             if (k >= hd.n_esc) {
                 ok = false;
                 return;

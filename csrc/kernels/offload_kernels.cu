@@ -302,14 +302,18 @@ __device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uin
 #pragma unroll
     for (int w = 0; w < kThreads / 32; ++w) mm = max(mm, red[w]);
     const uint32_t eb = zbf16::window_base(zbf16::exponent(uint16_t(mm)));
+    // mode-1 escapes in the low half, values in the window's lowest 8 binades
+    // in the high half (each at most 32768 per chunk: no carry between halves)
     uint32_t cnt = 0;
 #pragma unroll
     for (int k = 0; k < kVecs; ++k) {
         const uint32_t vi = uint32_t(k) * kThreads + t;
         if (vi < nvec)
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                cnt += zbf16::code_of(zbf16::exponent(uint16_t(half_of(v[k], j))), eb) == zbf16::kEscape;
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t e = zbf16::exponent(uint16_t(half_of(v[k], j)));
+                cnt += (zbf16::code_of(e, eb) == zbf16::kEscape ? 1u : 0u) + (zbf16::in_low8(e, eb) ? 0x10000u : 0u);
+            }
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
@@ -317,11 +321,12 @@ __device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uin
     if (lane == 0) red[warp] = cnt;
     __syncthreads();
     if (t == 0) {
-        uint32_t esc = 0;
+        uint32_t tot = 0;
 #pragma unroll
-        for (int w = 0; w < kThreads / 32; ++w) esc += red[w];
+        for (int w = 0; w < kThreads / 32; ++w) tot += red[w];
         *eb_out = uint8_t(eb);
-        const uint32_t clen = zbf16::coded_len(len, esc);
+        uint32_t clen = 0;
+        zbf16::choose_mode(len, eb, tot & 0xFFFFu, tot >> 16, &clen);
         if (clen > len) atomicOr(fail, 1u);
         if (stored) *stored = clen;
     }
@@ -375,6 +380,8 @@ __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, u
         v[k] = vi < nvec ? ld_once(src + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
     }
     ssh::Lane L = ssh::lane_init(t);
+    // mode-1 escapes (low half) and values in the lowest 8 binades of the
+    // mode-1 window (high half); one scan of the pair gives both modes' offsets
     uint32_t cnt = 0;
 #pragma unroll
     for (int k = 0; k < kVecs; ++k) {
@@ -385,20 +392,26 @@ __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, u
                 st_stream(dst + uint64_t(vi) * 16, v[k]);
             } else {
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    cnt += zbf16::code_of(zbf16::exponent(uint16_t(half_of(v[k], j))), eb) == zbf16::kEscape;
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t e = zbf16::exponent(uint16_t(half_of(v[k], j)));
+                    cnt += (zbf16::code_of(e, eb) == zbf16::kEscape ? 1u : 0u) + (zbf16::in_low8(e, eb) ? 0x10000u : 0u);
+                }
             }
         }
     }
     if (!raw) {  // uniform per chunk
-        uint32_t total;
-        uint32_t off = block_excl_scan(cnt, sc, &total);
+        uint32_t tot;
+        const uint32_t offp = block_excl_scan(cnt, sc, &tot);
         const uint32_t n = len / 2;
-        const uint32_t comp = zbf16::coded_len(len, total);
+        uint32_t comp = 0;
+        const bool m2 = zbf16::choose_mode(len, eb, tot & 0xFFFFu, tot >> 16, &comp) == 2;
+        const uint32_t base = m2 ? eb + zbf16::kBase3Offset : eb;
+        const uint32_t plane = m2 ? (n / 8) * 3 : n / 2;
+        uint32_t off = m2 ? (offp & 0xFFFFu) + (offp >> 16) : (offp & 0xFFFFu);
         if (t == 0)
-            *reinterpret_cast<uint4*>(zbuf) =
-                make_uint4(uint32_t(zbf16::kTag) | (1u << 16) | (eb << 24), total, len, comp);
-        uint8_t* esc = zbuf + zbf16::kHeader + n + n / 2;
+            *reinterpret_cast<uint4*>(zbuf) = make_uint4(uint32_t(zbf16::kTag) | ((m2 ? 2u : 1u) << 16) | (base << 24),
+                                                         comp - (zbf16::kHeader + n + plane), len, comp);
+        uint8_t* esc = zbuf + zbf16::kHeader + n + plane;
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) {
             const uint32_t vi = uint32_t(k) * kThreads + t;
@@ -408,15 +421,28 @@ __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, u
             for (int j = 0; j < 8; ++j) {
                 const uint16_t h = uint16_t(half_of(v[k], j));
                 const uint32_t e = zbf16::exponent(h);
-                const uint32_t cd = zbf16::code_of(e, eb);
                 const uint32_t lb = zbf16::low_byte(h);
                 if (j < 4) lo0 |= lb << (8 * j);
                 else lo1 |= lb << (8 * (j - 4));
-                codes |= cd << (4 * j);
-                if (cd == zbf16::kEscape) esc[off++] = uint8_t(e);
+                if (m2) {
+                    const uint32_t cd = zbf16::code3_of(e, base);
+                    codes |= cd << (3 * j);
+                    if (cd == zbf16::kEscape3) esc[off++] = uint8_t(e);
+                } else {
+                    const uint32_t cd = zbf16::code_of(e, base);
+                    codes |= cd << (4 * j);
+                    if (cd == zbf16::kEscape) esc[off++] = uint8_t(e);
+                }
             }
             *reinterpret_cast<uint2*>(zbuf + zbf16::kHeader + vi * 8) = make_uint2(lo0, lo1);
-            *reinterpret_cast<uint32_t*>(zbuf + zbf16::kHeader + n + vi * 4) = codes;
+            if (m2) {
+                uint8_t* c3 = zbuf + zbf16::kHeader + n + vi * 3;
+                c3[0] = uint8_t(codes);
+                c3[1] = uint8_t(codes >> 8);
+                c3[2] = uint8_t(codes >> 16);
+            } else {
+                *reinterpret_cast<uint32_t*>(zbuf + zbf16::kHeader + n + vi * 4) = codes;
+            }
         }
         __syncthreads();
         const uint32_t nout = (comp + 15) / 16;  // <= len / 16: coded chunks fit their raw length
@@ -537,8 +563,10 @@ __device__ __forceinline__ void load_chunk_z(const uint8_t* __restrict__ in, uin
         return;
     }
     const uint32_t n = len / 2;
-    const uint32_t fixed = zbf16::kHeader + n + n / 2;
-    const uint32_t spec = min(len, fixed + 1024u);
+    // stage the header, both planes and 1 KiB of escapes in one round trip
+    // (sized for mode 1, whose code plane is the larger)
+    const uint32_t fixed1 = zbf16::kHeader + n + n / 2;
+    const uint32_t spec = min(len, fixed1 + 1024u);
     stage_in(in, zbuf, 0, spec);
     __syncthreads();
     const uint4 hd = *reinterpret_cast<const uint4*>(zbuf);
@@ -547,7 +575,9 @@ __device__ __forceinline__ void load_chunk_z(const uint8_t* __restrict__ in, uin
         stage_in(in, zbuf, spec / 16 * 16, comp);
         __syncthreads();
     }
-    const uint32_t eb = hd.x >> 24;
+    const bool m2 = ((hd.x >> 16) & 0xFFu) == 2u;
+    const uint32_t fixed = m2 ? zbf16::kHeader + n + (n / 8) * 3 : fixed1;
+    const uint32_t eb = hd.x >> 24;  // the stored mode's base
     uint2 lo[kVecs];
     uint32_t cd[kVecs];
     uint32_t cnt = 0;
@@ -556,7 +586,19 @@ __device__ __forceinline__ void load_chunk_z(const uint8_t* __restrict__ in, uin
         const uint32_t vi = uint32_t(k) * kThreads + t;
         if (vi < nvec) {
             lo[k] = *reinterpret_cast<const uint2*>(zbuf + zbf16::kHeader + vi * 8);
-            cd[k] = *reinterpret_cast<const uint32_t*>(zbuf + zbf16::kHeader + n + vi * 4);
+            if (m2) {  // widen the 3-bit codes to mode 1's nibbles (escape 7 -> 15)
+                const uint8_t* c3 = zbuf + zbf16::kHeader + n + vi * 3;
+                const uint32_t w = uint32_t(c3[0]) | (uint32_t(c3[1]) << 8) | (uint32_t(c3[2]) << 16);
+                uint32_t c4 = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t c = (w >> (3 * j)) & 7u;
+                    c4 |= (c == zbf16::kEscape3 ? zbf16::kEscape : c) << (4 * j);
+                }
+                cd[k] = c4;
+            } else {
+                cd[k] = *reinterpret_cast<const uint32_t*>(zbuf + zbf16::kHeader + n + vi * 4);
+            }
         } else {
             lo[k] = make_uint2(0, 0);
             cd[k] = 0;

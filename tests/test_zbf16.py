@@ -29,7 +29,7 @@ def test_gaussian_round_trip_and_ratio(std, nbytes):
     ratio = C.zbf16_coded_bytes(coded) / nbytes
     tail = nbytes % CHUNK
     if tail == 0 or tail >= 4096:
-        assert ratio < 0.77, ratio  # 12 bits per value + a few escapes
+        assert ratio < 0.73, ratio  # 11 bits per value (3-bit codes) + the escapes below 7 binades
 
 
 def test_zeros_and_constants_code():
@@ -58,7 +58,44 @@ def test_wide_range_values_escape_and_still_round_trip():
     coded = C.zbf16_encode(raw)
     assert coded is not None
     assert C.zbf16_decode(coded) == raw.tobytes()
-    assert C.zbf16_coded_bytes(coded) > 0.75 * len(raw)
+    plain = C.zbf16_encode(_bf16_bytes(torch.randn(1 << 16, generator=torch.Generator().manual_seed(3))))
+    assert C.zbf16_coded_bytes(coded) > C.zbf16_coded_bytes(plain)  # the escapes cost bytes
+
+
+def _modes(coded: bytes, nbytes: int):
+    return [coded[c * CHUNK + 2] for c in range(nbytes // CHUNK)]
+
+
+def test_each_chunk_takes_the_shorter_code_width():
+    """Gaussian-like chunks store 3-bit codes over the top 7 binades (mode
+    2); values spread evenly over 14 binades keep 4-bit codes (mode 1), and
+    so do chunks whose largest exponent is too small for a mode-2 window."""
+    C = native()
+    g = torch.Generator().manual_seed(11)
+    gauss = _bf16_bytes(torch.randn(4 * CHUNK // 2, generator=g))
+    wide = _bf16_bytes(torch.exp2(torch.rand(4 * CHUNK // 2, generator=g) * 14 - 7)
+                       * torch.sign(torch.randn(4 * CHUNK // 2, generator=g)))
+    tiny = _bf16_bytes(torch.randn(4 * CHUNK // 2, generator=g) * 1e-36)
+    for raw, mode in ((gauss, 2), (wide, 1), (tiny, 1)):
+        coded = C.zbf16_encode(raw)
+        assert coded is not None and set(_modes(coded, len(raw))) == {mode}
+        assert C.zbf16_decode(coded) == raw.tobytes()
+
+
+def test_three_bit_code_layout():
+    """Mode 2 byte layout of a chunk of 1.0s (exponent 127): base = 127 - 6,
+    every code 6, a vector's eight codes as one little-endian 24-bit value
+    (0b110 repeated: bytes B6 6D DB), no escapes."""
+    C = native()
+    raw = _bf16_bytes(torch.ones(CHUNK // 2))
+    coded = C.zbf16_encode(raw)
+    n = CHUNK // 2
+    assert coded[2] == 2 and coded[3] == 121  # mode, base
+    assert int.from_bytes(coded[4:8], "little") == 0  # escapes
+    assert int.from_bytes(coded[12:16], "little") == 16 + n + 3 * n // 8
+    assert coded[16:16 + n] == bytes(n)  # sign + mantissa of 1.0 are all zero
+    assert coded[16 + n:16 + n + 6] == bytes([0xB6, 0x6D, 0xDB] * 2)
+    assert C.zbf16_decode(coded) == raw.tobytes()
 
 
 def test_ineligible_sizes():
