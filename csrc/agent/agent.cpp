@@ -180,7 +180,7 @@ struct Agent::Impl {
             CUDA_OK(cudaStreamWaitEvent(zdec, zfree[b], 0));  // the last reader of staging b is done
             const uint64_t piece = std::min(nbytes, c1 * C) - c0 * C;
             CUDA_OK(kern::evict_z(src + c0 * C, zstage[b], piece, ebase + c0, dig ? dig + c0 : nullptr, zdec,
-                                  opt.evict_ctas));
+                                  zstage_ctas));
             CUDA_OK(cudaEventRecord(zfull[b], zdec));
             CUDA_OK(cudaStreamWaitEvent(side, zfull[b], 0));
             CUDA_OK(cudaMemcpy2DAsync(host + c0 * C, C, zstage[b], C, width, c1 - c0, cudaMemcpyDeviceToHost, side));
@@ -203,8 +203,14 @@ struct Agent::Impl {
             int lo = 0, hi = 0;
             cudaDeviceGetStreamPriorityRange(&lo, &hi);
             CUDA_OK(cudaStreamCreateWithPriority(&zdec, cudaStreamNonBlocking, hi));
+            // coding into / decoding from staging is HBM to HBM: two CTAs per
+            // SM (the kernels' occupancy), not the few dozen a PCIe pass needs
+            int sms = 148;
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, opt.device);
+            zstage_ctas = 2 * sms;
         }
     }
+    int zstage_ctas = 0;
 
     // Coded restore through the copy engine: each chunk's stored bytes (`zmax`
     // per 64 KiB row, one strided copy per piece) go into staging on the side
@@ -230,7 +236,7 @@ struct Agent::Impl {
             CUDA_OK(cudaStreamWaitEvent(zdec, zfull[b], 0));
             const uint64_t piece = std::min(nbytes, c1 * C) - c0 * C;
             CUDA_OK(kern::restore_z(zstage[b], dst + c0 * C, piece, kern::Cast::kNone, nullptr, nullptr, nullptr, zdec,
-                                    opt.restore_ctas));
+                                    zstage_ctas));
             CUDA_OK(cudaEventRecord(zfree[b], zdec));
             c0 = c1;
         }
