@@ -3,7 +3,10 @@
     python -m statespectre_b200.ops.profile_case --kernel evict --mb 512 --iters 3
 
 Kernels: evict (K1, device -> pinned + ssh128), restore (K2, pinned ->
-device), restore_fp8 (K2 with the bf16 -> fp8 1x128 cast), evict_bulk /
+device), restore_fp8 (K2 with the bf16 -> fp8 1x128 cast), evict_z /
+restore_z (coded K1 / K2 to and from host memory), evict_z_stage /
+restore_z_stage (the same coding into and decoding from device memory, the
+passes of the copy-engine coded paths), evict_bulk /
 restore_bulk (K1 / K2 as bulk copies through shared memory), hash (device
 ssh128, the library's choice of form), hash_onepass (the per-thread-load
 hash kernel), hash_stream (ssh128 through the K4 bulk-copy pipeline), verify (K3
@@ -26,7 +29,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True, choices=["evict", "restore", "restore_fp8", "hash", "hash_onepass",
                                                           "hash_stream", "verify", "push", "push_fp8", "zscan",
-                                                          "evict_z", "restore_z", "evict_bulk", "restore_bulk"])
+                                                          "evict_z", "restore_z", "evict_bulk", "restore_bulk",
+                                                          "evict_z_stage", "restore_z_stage"])
     ap.add_argument("--mb", type=int, default=512)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--ctas", type=int, default=0)
@@ -51,9 +55,14 @@ def main():
     C.k_evict_hash(x.data_ptr(), host.data_ptr(), n, dig.data_ptr(), s, a.ctas)  # fill the host copy
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     zeb = torch.zeros((n + 65535) // 65536, dtype=torch.uint8, device=dev)
-    if a.kernel in ("zscan", "evict_z", "restore_z"):  # zbf16: window bases, then the coded host copy
+    stage = None
+    if a.kernel in ("zscan", "evict_z", "restore_z", "evict_z_stage", "restore_z_stage"):
+        # zbf16: window bases, then the coded host copy (and a device copy of it)
         C.k_zscan(x.data_ptr(), n, zeb.data_ptr(), err.data_ptr(), s, 0)
         C.k_evict_z(x.data_ptr(), host.data_ptr(), n, zeb.data_ptr(), dig.data_ptr(), s, a.ctas)
+        if a.kernel == "restore_z_stage":
+            stage = torch.empty(n, dtype=torch.uint8, device=dev)
+            stage.copy_(host)
     if a.kernel == "verify":
         # K3 compares x with a second copy: on this GPU, or with --peer on that
         # GPU (plain peer loads over NVLink); the copy goes through host memory
@@ -99,6 +108,10 @@ def main():
             C.k_evict_z(x.data_ptr(), host.data_ptr(), n, zeb.data_ptr(), dig.data_ptr(), s, a.ctas)
         elif a.kernel == "restore_z":
             C.k_restore_z(host.data_ptr(), out.data_ptr(), n, 0, 0, 0, 0, s, a.ctas)
+        elif a.kernel == "evict_z_stage":  # coding into device memory (the copy-engine evict's staging pass)
+            C.k_evict_z(x.data_ptr(), out.data_ptr(), n, zeb.data_ptr(), dig.data_ptr(), s, a.ctas)
+        elif a.kernel == "restore_z_stage":  # decoding from device memory (the copy-engine restore's pass)
+            C.k_restore_z(stage.data_ptr(), out.data_ptr(), n, 0, 0, 0, 0, s, a.ctas)
         elif a.kernel == "hash_stream":
             C.k_hash_stream(x.data_ptr(), n, dig.data_ptr(), err.data_ptr(), s, a.ctas, a.stages)
         elif pusher is not None:
