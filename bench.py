@@ -75,6 +75,10 @@ def parse():
                    help="how zbf16-coded evicts leave the GPU (K1 into host memory, or via staging + copy engine)")
     p.add_argument("--coded-restore", default="copy_engine", choices=["copy_engine", "sm"],
                    help="how zbf16-coded runs come back (strided copy-engine copies + HBM decode, or K2 from host)")
+    p.add_argument("--stage-ctas", type=int, default=0,
+                   help="CTAs of the staged zbf16 coding/decoding passes (0 = auto)")
+    p.add_argument("--stage-depth", type=int, default=0, help="staging buffers of the coded paths (0 = auto)")
+    p.add_argument("--stage-piece-chunks", type=int, default=0, help="64 KiB chunks per staging buffer (0 = auto)")
     p.add_argument("--evict-ctas", type=int, default=0)
     p.add_argument("--restore-ctas", type=int, default=0)
     p.add_argument("--hash", type=int, default=1)
@@ -206,7 +210,9 @@ def main():
                            eager_register=True, engine=args.engine, evict_ctas=args.evict_ctas,
                            restore_ctas=args.restore_ctas, hash_on_evict=bool(args.hash), stream_priority=-1,
                            compress=bool(args.compress), kernel_timing=bool(args.kernel_timing),
-                           uncoded=args.uncoded, coded_restore=args.coded_restore, coded_evict=args.coded_evict)
+                           uncoded=args.uncoded, coded_restore=args.coded_restore, coded_evict=args.coded_evict,
+                           stage_ctas=args.stage_ctas, stage_depth=args.stage_depth,
+                           stage_piece_chunks=args.stage_piece_chunks)
     off = sess.off
     g = torch.Generator(device=device)
     g.manual_seed(1234 + rank)
@@ -351,6 +357,8 @@ def main():
                 "concurrent_matmul": "8192x8192 bf16 loop" if args.matmul else "none",
                 "engine": args.engine, "hash": bool(args.hash), "slot_mb": 64,
                 "uncoded_form": args.uncoded, "coded_evict": args.coded_evict, "coded_restore": args.coded_restore,
+                "stage_ctas": args.stage_ctas or "auto", "stage_depth": args.stage_depth or "auto",
+                "stage_piece_chunks": args.stage_piece_chunks or "auto",
                 "transfer_coding": coding,
                 "l2": "inputs (1 GiB) larger than the 126 MB L2; no flush needed",
                 "baseline": f"StateSpectre H20 PCIe Gen5 1 GiB: D2H {BASELINE_D2H_GBS}, H2D {BASELINE_H2D_GBS} GB/s "

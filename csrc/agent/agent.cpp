@@ -135,14 +135,18 @@ struct Agent::Impl {
     cudaStream_t stream = nullptr;
     cudaStream_t side = nullptr;  // evict digests next to a copy-engine copy; coded restore copies
 
-    // Coded restore through the copy engine: two device staging buffers of
-    // kZPiece chunks each (allocated on first use, 2 x 32 MiB) and their events.
-    static constexpr uint64_t kZPiece = 512;
-    void* zstage[2] = {nullptr, nullptr};
+    // Coded paths through the copy engine: a ring of device staging buffers
+    // of zpiece chunks each (allocated on first use; default 2 x 32 MiB) and
+    // their events.
+    static constexpr int kZDepthMax = 8;
+    uint64_t zpiece = 512;
+    int zdepth = 2;
+    void* zstage[kZDepthMax] = {};
     // zfull[b]: staging b holds a piece (recorded by its producer); zfree[b]:
     // nothing reads staging b any more (recorded by its consumer). Every
     // writer of b waits zfree[b], whichever operation used it last.
-    cudaEvent_t zfull[2] = {nullptr, nullptr}, zfree[2] = {nullptr, nullptr};
+    cudaEvent_t zfull[kZDepthMax] = {}, zfree[kZDepthMax] = {};
+    uint64_t zturn = 0;  // next staging buffer of the ring
     cudaEvent_t zstart = nullptr, zdone = nullptr;
     // Decodes run on their own stream at the device's highest priority: a
     // restore issues one short decode per piece, and at equal priority each
@@ -150,11 +154,11 @@ struct Agent::Impl {
     cudaStream_t zdec = nullptr;
     std::mutex zmu;  // coded evicts and restores of this session share the staging
 
-    // Piece boundaries of a coded run: kZPiece chunks each, except that a
+    // Piece boundaries of a coded run: zpiece chunks each, except that a
     // short raw tail never sits alone (a piece must itself be a codable
     // object): the piece before it gives up one chunk.
-    static uint64_t zpiece_end(uint64_t c0, uint64_t nch, bool short_tail) {
-        uint64_t c1 = std::min(nch, c0 + kZPiece);
+    static uint64_t zpiece_end(uint64_t c0, uint64_t nch, bool short_tail, uint64_t zpiece) {
+        uint64_t c1 = std::min(nch, c0 + zpiece);
         if (short_tail && nch - c1 == 1) c1 -= 1;  // pieces that leave one chunk are full, so > 1
         return c1;
     }
@@ -174,9 +178,9 @@ struct Agent::Impl {
         CUDA_OK(cudaEventRecord(zstart, s));  // the source is complete on the caller's stream
         CUDA_OK(cudaStreamWaitEvent(zdec, zstart, 0));
         uint64_t c0 = 0;
-        for (int k = 0; c0 < nch; ++k) {
-            const uint64_t c1 = zpiece_end(c0, nch, short_tail);
-            const int b = k & 1;
+        while (c0 < nch) {
+            const uint64_t c1 = zpiece_end(c0, nch, short_tail, zpiece);
+            const int b = int(zturn++ % uint64_t(zdepth));
             CUDA_OK(cudaStreamWaitEvent(zdec, zfree[b], 0));  // the last reader of staging b is done
             const uint64_t piece = std::min(nbytes, c1 * C) - c0 * C;
             CUDA_OK(kern::evict_z(src + c0 * C, zstage[b], piece, ebase + c0, dig ? dig + c0 : nullptr, zdec,
@@ -193,8 +197,10 @@ struct Agent::Impl {
 
     void zstage_init() {
         if (!zstage[0]) {
-            for (int b = 0; b < 2; ++b) {
-                CUDA_OK(cudaMalloc(&zstage[b], kZPiece * zbf16::kChunk));
+            if (opt.stage_piece_chunks > 0) zpiece = std::max<uint64_t>(opt.stage_piece_chunks, 2);
+            if (opt.stage_depth > 0) zdepth = std::min(std::max(opt.stage_depth, 2), kZDepthMax);
+            for (int b = 0; b < zdepth; ++b) {
+                CUDA_OK(cudaMalloc(&zstage[b], zpiece * zbf16::kChunk));
                 CUDA_OK(cudaEventCreateWithFlags(&zfull[b], cudaEventDisableTiming));
                 CUDA_OK(cudaEventCreateWithFlags(&zfree[b], cudaEventDisableTiming));
             }
@@ -207,7 +213,7 @@ struct Agent::Impl {
             // SM (the kernels' occupancy), not the few dozen a PCIe pass needs
             int sms = 148;
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, opt.device);
-            zstage_ctas = 2 * sms;
+            zstage_ctas = opt.stage_ctas > 0 ? opt.stage_ctas : 2 * sms;
         }
     }
     int zstage_ctas = 0;
@@ -227,9 +233,9 @@ struct Agent::Impl {
         const size_t width = std::min<size_t>((size_t(zmax) + 15) / 16 * 16, C);
         const bool short_tail = nbytes - (nch - 1) * C < zbf16::kRawTail;
         uint64_t c0 = 0;
-        for (int k = 0; c0 < nch; ++k) {
-            const uint64_t c1 = zpiece_end(c0, nch, short_tail);
-            const int b = k & 1;
+        while (c0 < nch) {
+            const uint64_t c1 = zpiece_end(c0, nch, short_tail, zpiece);
+            const int b = int(zturn++ % uint64_t(zdepth));
             CUDA_OK(cudaStreamWaitEvent(side, zfree[b], 0));  // the last reader of staging b is done
             CUDA_OK(cudaMemcpy2DAsync(zstage[b], C, host + c0 * C, C, width, c1 - c0, cudaMemcpyHostToDevice, side));
             CUDA_OK(cudaEventRecord(zfull[b], side));
@@ -383,7 +389,7 @@ struct Agent::Impl {
         }
         if (stream) cudaStreamDestroy(stream);
         if (side) cudaStreamDestroy(side);
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kZDepthMax; ++b) {
             if (zstage[b]) cudaFree(zstage[b]);
             if (zfull[b]) cudaEventDestroy(zfull[b]);
             if (zfree[b]) cudaEventDestroy(zfree[b]);

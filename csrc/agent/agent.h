@@ -61,6 +61,13 @@ struct AgentOptions {
     // "sm" (K1 codes straight into the host-mapped run).
     std::string coded_evict = "copy_engine";
     int evict_ctas = 0, restore_ctas = 0, hash_ctas = 0;
+    // CTAs of the staged (HBM to HBM) coding and decoding passes of the
+    // copy-engine coded paths; 0 = auto.
+    int stage_ctas = 0;
+    // Staging ring of those paths: buffers (2..8) and 64 KiB chunks per
+    // buffer; 0 = auto (2 x 512 chunks, 64 MiB of HBM).
+    int stage_depth = 0;
+    int stage_piece_chunks = 0;
     bool hash_on_evict = true;
     bool use_ring = true;
     bool fast_submit = true;     // reserve+submit and ready+submit in one round trip

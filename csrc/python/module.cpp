@@ -225,6 +225,9 @@ class PyAgent {
             else if (k == "evict_ctas") o.evict_ctas = v.cast<int>();
             else if (k == "restore_ctas") o.restore_ctas = v.cast<int>();
             else if (k == "hash_ctas") o.hash_ctas = v.cast<int>();
+            else if (k == "stage_ctas") o.stage_ctas = v.cast<int>();
+            else if (k == "stage_depth") o.stage_depth = v.cast<int>();
+            else if (k == "stage_piece_chunks") o.stage_piece_chunks = v.cast<int>();
             else if (k == "hash_on_evict") o.hash_on_evict = v.cast<bool>();
             else if (k == "use_ring") o.use_ring = v.cast<bool>();
             else if (k == "fast_submit") o.fast_submit = v.cast<bool>();

@@ -898,6 +898,9 @@ _AGENT_OPTION_KEYS = {
     "kernels.evict_ctas": ("evict_ctas", int),
     "kernels.restore_ctas": ("restore_ctas", int),
     "kernels.hash_ctas": ("hash_ctas", int),
+    "kernels.stage_ctas": ("stage_ctas", int),
+    "kernels.stage_depth": ("stage_depth", int),
+    "kernels.stage_piece_chunks": ("stage_piece_chunks", int),
     "kernels.engine": ("engine", str),
     "kernels.uncoded": ("uncoded", str),
     "kernels.coded_restore": ("coded_restore", str),

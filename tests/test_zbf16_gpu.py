@@ -245,16 +245,19 @@ def test_coded_transfer_forms_are_byte_exact(sock_path, coded_evict, coded_resto
         d.stop()
 
 
-def test_copy_engine_evicts_and_restores_back_to_back_share_staging(sock_path):
+@pytest.mark.parametrize("ring", [{}, {"stage_depth": 3, "stage_piece_chunks": 48, "stage_ctas": 37}])
+def test_copy_engine_evicts_and_restores_back_to_back_share_staging(sock_path, ring):
     """Asynchronous coded evicts and restores issued back to back on one
     session share the device staging: each waits for the last reader of a
-    staging buffer before writing it, so every tensor comes back intact."""
+    staging buffer before writing it, so every tensor comes back intact
+    (default ring, and an odd-sized ring of small pieces whose turns wrap
+    across operations)."""
     from statespectre_b200 import in_process_daemon, offload_context
 
     d = in_process_daemon(socket=sock_path, arena_mb=2048, drain_on_complete=False)
     try:
         with offload_context(daemon_addr=sock_path, device="cuda:0", coded_restore="copy_engine",
-                             coded_evict="copy_engine") as off:
+                             coded_evict="copy_engine", **ring) as off:
             xs = [torch.randn((48 << 20) // 2 + 4096 * i, dtype=torch.bfloat16, device="cuda") for i in range(4)]
             refs = [x.clone() for x in xs]
             hs = [off.copy(x) for x in xs]  # asynchronous
