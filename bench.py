@@ -309,7 +309,8 @@ def main():
     for i in range(e2e_steps):
         h = off.evict(x, wait=True, tensor_id=tid, version=20000 + i)   # D2H, VRAM released
         x = h.restore()                                                   # H2D from pinned host memory
-        hashes_ok &= h.content_hash == ref_hash                           # 16 B result read back
+        if args.hash:
+            hashes_ok &= h.content_hash == ref_hash                       # 16 B result read back
         h.discard()
     torch.cuda.synchronize(device)
     e2e_s = time.perf_counter() - t0
@@ -321,6 +322,8 @@ def main():
         mm_thread.join(timeout=30)
     mm_tflops = None
     assert hashes_ok, "content hash changed across the e2e round trips"
+    if not args.hash:  # no digests on evict: the tensor itself is the check
+        assert off.hash_tensor(x) == ref_hash, "e2e round trips corrupted the tensor"
 
     sess.close()
     barrier()
@@ -367,7 +370,7 @@ def main():
             "evict_gbs_per_gpu": round(nbytes / (ev / 1e3) / 1e9, 3),
             "restore_gbs_per_gpu": round(nbytes / (rs / 1e3) / 1e9, 3),
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s (aggregate, public API, host-timed)",
-                    "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes + 16},
+                    "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes + (16 if args.hash else 0)},
             "gpu_launches": int(launches),
             "clocks": clocks,
             "matmul_iters": mm_count[0],

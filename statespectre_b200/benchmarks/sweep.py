@@ -40,6 +40,7 @@ def run(args, metric: str) -> dict:
     sock, daemon = node_daemon(env, window_gb, "/tmp/ofld_sweep", slot_mb=64)
     sess = offload_context(daemon_addr=sock, device=env.device, rank=env.rank, local_rank=env.local_rank,
                            world_rank=env.rank, eager_register=True, compress=bool(args.compress),
+                           hash_on_evict=bool(getattr(args, "hash", 1)),
                            stream_priority=-1, stage_ctas=int(getattr(args, "stage_ctas", 0) or 0),
                            stage_depth=int(getattr(args, "stage_depth", 0) or 0),
                            stage_piece_chunks=int(getattr(args, "stage_piece_chunks", 0) or 0))
