@@ -75,6 +75,8 @@ def parse():
                    help="how zbf16-coded evicts leave the GPU (K1 into host memory, or via staging + copy engine)")
     p.add_argument("--coded-restore", default="copy_engine", choices=["copy_engine", "sm"],
                    help="how zbf16-coded runs come back (strided copy-engine copies + HBM decode, or K2 from host)")
+    p.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"],
+                   help="payload dtype (fp32: N(0, 0.02) values, like master weights; zf32-coded)")
     p.add_argument("--stage-ctas", type=int, default=0,
                    help="CTAs of the staged zbf16 coding/decoding passes (0 = auto)")
     p.add_argument("--stage-depth", type=int, default=0, help="staging buffers of the coded paths (0 = auto)")
@@ -216,15 +218,20 @@ def main():
     off = sess.off
     g = torch.Generator(device=device)
     g.manual_seed(1234 + rank)
-    x = torch.randn(nbytes // 2, dtype=torch.bfloat16, device=device, generator=g)
+    if args.dtype == "fp32":
+        x = torch.randn(nbytes // 4, dtype=torch.float32, device=device, generator=g) * 0.02
+    else:
+        x = torch.randn(nbytes // 2, dtype=torch.bfloat16, device=device, generator=g)
     ref_hash = off.hash_tensor(x)
-    # what crosses PCIe: zbf16 coding of the bf16 payload (host codec on a 64 MiB sample)
+    # what crosses PCIe: zbf16 / zf32 coding of the payload (host codec on a 64 MiB sample)
     coding = "none"
     if args.compress and args.engine == "kernel":
         sample = x.view(torch.uint8)[: min(nbytes, 64 << 20)].cpu().numpy()
-        coded = native().zbf16_encode(sample)
+        codec = "zf32" if args.dtype == "fp32" else "zbf16"
+        coded = getattr(native(), f"{codec}_encode")(sample)
         if coded is not None:
-            coding = f"zbf16 lossless, {native().zbf16_coded_bytes(coded) / len(sample):.4f} of the bytes"
+            frac = getattr(native(), f"{codec}_coded_bytes")(coded) / len(sample)
+            coding = f"{codec} lossless, {frac:.4f} of the bytes"
     copy_stream = torch.cuda.Stream(device=device, priority=-1)
 
     # ---- concurrent 8192^2 bf16 matmul loop on its own stream ----
@@ -352,10 +359,12 @@ def main():
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": round(value / (world * BASELINE_ROUNDTRIP_GBS), 4),
-            "dtype": "bf16",
-            "data": "synthetic: bf16 N(0,1) random tensor, seeded per rank",
+            "dtype": args.dtype,
+            "data": "synthetic: fp32 N(0, 0.02) random tensor, seeded per rank" if args.dtype == "fp32"
+                    else "synthetic: bf16 N(0,1) random tensor, seeded per rank",
             "config": {
-                "model": "single-B200 eviction sweep point: bf16 tensor evict (K1, fused ssh128 hash) + restore (K2)",
+                "model": f"single-B200 eviction sweep point: {args.dtype} tensor evict (K1, fused ssh128 hash) + "
+                         "restore (K2)",
                 "tensor_bytes": nbytes, "global_batch": world, "seq_len": 0, "parallelism": f"dp{world}",
                 "concurrent_matmul": "8192x8192 bf16 loop" if args.matmul else "none",
                 "engine": args.engine, "hash": bool(args.hash), "slot_mb": 64,

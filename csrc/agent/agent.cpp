@@ -134,6 +134,7 @@ struct Agent::Impl {
 
     cudaStream_t stream = nullptr;
     cudaStream_t side = nullptr;  // evict digests next to a copy-engine copy; coded restore copies
+    cudaStream_t aux = nullptr;   // zf32: digests of the fp32 bytes next to the coding and its copies
 
     // Coded paths through the copy engine: a ring of device staging buffers
     // of zpiece chunks each (allocated on first use; default 2 x 32 MiB) and
@@ -249,6 +250,57 @@ struct Agent::Impl {
         CUDA_OK(cudaEventRecord(zdone, zdec));
         CUDA_OK(cudaStreamWaitEvent(s, zdone, 0));  // the caller's stream continues after the last decode
     }
+
+    // zf32 through the copy engine: the same ring over 128 KiB rows (half as
+    // many rows per piece as chunks, so a piece fills the same staging). A
+    // row crosses PCIe as its 64 KiB low plane plus the stored bytes of its
+    // coded top halves (`zmax`): one strided copy per piece.
+    void evict_zf32_ce(const uint8_t* src, char* host, uint64_t nbytes, const uint8_t* ebase, uint32_t zmax,
+                       cudaStream_t s) {
+        std::lock_guard<std::mutex> g(zmu);
+        constexpr uint64_t R = zf32::kRow;
+        zstage_init();
+        const uint64_t nrows = zf32::rows(nbytes), per = std::max<uint64_t>(zpiece / 2, 1);
+        const size_t width = zf32::kLowPlane + std::min<size_t>((size_t(zmax) + 15) / 16 * 16, zbf16::kChunk);
+        CUDA_OK(cudaEventRecord(zstart, s));
+        CUDA_OK(cudaStreamWaitEvent(zdec, zstart, 0));
+        for (uint64_t r0 = 0; r0 < nrows;) {
+            const uint64_t r1 = std::min(nrows, r0 + per);
+            const int b = int(zturn++ % uint64_t(zdepth));
+            CUDA_OK(cudaStreamWaitEvent(zdec, zfree[b], 0));
+            CUDA_OK(kern::evict_zf32(src + r0 * R, zstage[b], (r1 - r0) * R, ebase + r0, zdec, zstage_ctas));
+            CUDA_OK(cudaEventRecord(zfull[b], zdec));
+            CUDA_OK(cudaStreamWaitEvent(side, zfull[b], 0));
+            CUDA_OK(cudaMemcpy2DAsync(host + r0 * R, R, zstage[b], R, width, r1 - r0, cudaMemcpyDeviceToHost, side));
+            CUDA_OK(cudaEventRecord(zfree[b], side));
+            r0 = r1;
+        }
+        CUDA_OK(cudaEventRecord(zdone, side));
+        CUDA_OK(cudaStreamWaitEvent(s, zdone, 0));
+    }
+
+    void restore_zf32_ce(const char* host, uint8_t* dst, uint64_t nbytes, uint32_t zmax, cudaStream_t s) {
+        std::lock_guard<std::mutex> g(zmu);
+        constexpr uint64_t R = zf32::kRow;
+        zstage_init();
+        CUDA_OK(cudaEventRecord(zstart, s));
+        CUDA_OK(cudaStreamWaitEvent(zdec, zstart, 0));
+        const uint64_t nrows = zf32::rows(nbytes), per = std::max<uint64_t>(zpiece / 2, 1);
+        const size_t width = zf32::kLowPlane + std::min<size_t>((size_t(zmax) + 15) / 16 * 16, zbf16::kChunk);
+        for (uint64_t r0 = 0; r0 < nrows;) {
+            const uint64_t r1 = std::min(nrows, r0 + per);
+            const int b = int(zturn++ % uint64_t(zdepth));
+            CUDA_OK(cudaStreamWaitEvent(side, zfree[b], 0));
+            CUDA_OK(cudaMemcpy2DAsync(zstage[b], R, host + r0 * R, R, width, r1 - r0, cudaMemcpyHostToDevice, side));
+            CUDA_OK(cudaEventRecord(zfull[b], side));
+            CUDA_OK(cudaStreamWaitEvent(zdec, zfull[b], 0));
+            CUDA_OK(kern::restore_zf32(zstage[b], dst + r0 * R, (r1 - r0) * R, zdec, zstage_ctas));
+            CUDA_OK(cudaEventRecord(zfree[b], zdec));
+            r0 = r1;
+        }
+        CUDA_OK(cudaEventRecord(zdone, zdec));
+        CUDA_OK(cudaStreamWaitEvent(s, zdone, 0));
+    }
     PinnedPool pool;
 
     struct Pending {
@@ -263,6 +315,7 @@ struct Agent::Impl {
         PinnedPool::Buf zb;              // zbf16 window bases (one byte per chunk) + pre-pass flag
         PinnedPool::Buf err;             // bulk forms: device status word (0 = the copy completed)
         bool z = false;
+        bool f32 = false;                // with z: the run is zf32-coded fp32 (else zbf16)
         // Batched launches: every item of the batch shares one event and the
         // job table; the last item to finish releases both.
         std::shared_ptr<void> batch_keep;
@@ -365,6 +418,7 @@ struct Agent::Impl {
             int prio = opt.stream_priority < 0 ? hi : 0;
             CUDA_OK(cudaStreamCreateWithPriority(&stream, cudaStreamNonBlocking, prio));
             CUDA_OK(cudaStreamCreateWithPriority(&side, cudaStreamNonBlocking, prio));
+            CUDA_OK(cudaStreamCreateWithPriority(&aux, cudaStreamNonBlocking, prio));
         }
 
         // Heartbeats start before the eager pinning below: registering a
@@ -389,6 +443,7 @@ struct Agent::Impl {
         }
         if (stream) cudaStreamDestroy(stream);
         if (side) cudaStreamDestroy(side);
+        if (aux) cudaStreamDestroy(aux);
         for (int b = 0; b < kZDepthMax; ++b) {
             if (zstage[b]) cudaFree(zstage[b]);
             if (zfull[b]) cudaEventDestroy(zfull[b]);
@@ -636,6 +691,7 @@ struct Agent::Impl {
             h2d_bytes += p.nbytes;
             pool.put(p.mism);
             pool.put(p.exp);
+            pool.put(p.dig);  // zf32 verification: digests of the restored bytes
             if (p.cb) p.cb();
         }
         if (p.batch_keep) p.batch_keep.reset();  // shared event: the keep owns it
@@ -726,22 +782,28 @@ struct Agent::Impl {
     // zbf16 pre-pass: per-chunk window bases into a mapped buffer; true when
     // every chunk fits coded. Waits for the stream (the decision precedes the
     // reservation, whose flags record the format).
-    bool zscan(uint64_t src, uint64_t nbytes, cudaStream_t s, PinnedPool::Buf* out) {
-        zscan_launch(src, nbytes, s, out);
+    bool zscan(uint64_t src, uint64_t nbytes, cudaStream_t s, PinnedPool::Buf* out, bool f32 = false) {
+        zscan_launch(src, nbytes, s, out, f32);
         stream_wait(s);
         return zscan_result(nbytes, out);
     }
     // The pre-pass in two halves, so a batch launches every item's scan and
-    // waits once.
-    void zscan_launch(uint64_t src, uint64_t nbytes, cudaStream_t s, PinnedPool::Buf* out) {
+    // waits once. f32: the zf32 pre-pass (one window base per 128 KiB row;
+    // the layout below is sized by 64 KiB chunks either way).
+    void zscan_launch(uint64_t src, uint64_t nbytes, cudaStream_t s, PinnedPool::Buf* out, bool f32 = false) {
         const uint64_t nch = kern::digest_count(nbytes);
         const uint64_t flag_off = (nch + 15) / 16 * 16;
         // [window bases][pad][fail word + 12 pad][kZScanSlots per-CTA stored-length maxima]
         *out = pool.get(flag_off + 16 + 4 * kern::kZScanSlots);
         std::memset(static_cast<char*>(out->host) + flag_off, 0, 16 + 4 * kern::kZScanSlots);
-        CUDA_OK(kern::zscan(reinterpret_cast<const void*>(src), nbytes, static_cast<uint8_t*>(out->dev),
-                            reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off), s, 0,
-                            reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off + 16)));
+        auto* fail = reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off);
+        auto* maxc = reinterpret_cast<uint32_t*>(static_cast<char*>(out->dev) + flag_off + 16);
+        if (f32)
+            CUDA_OK(kern::zscan_f32(reinterpret_cast<const void*>(src), nbytes, static_cast<uint8_t*>(out->dev), fail,
+                                    s, 0, maxc));
+        else
+            CUDA_OK(kern::zscan(reinterpret_cast<const void*>(src), nbytes, static_cast<uint8_t*>(out->dev), fail, s, 0,
+                                maxc));
     }
     // Largest stored chunk length recorded by the pre-pass (valid after zscan_result).
     uint32_t zscan_max(uint64_t nbytes, const PinnedPool::Buf& b) const {
@@ -772,12 +834,19 @@ struct Agent::Impl {
         return gpu && fmt_hint == kFmtBf16 && opt.compress && opt.engine != "copy_engine" &&
                nbytes >= opt.compress_min_bytes && zbf16::eligible(nbytes) && (ptr & 15) == 0;
     }
+    bool want_zf32(uint64_t ptr, uint64_t nbytes, uint32_t fmt_hint) const {
+        return gpu && fmt_hint == kFmtF32 && opt.compress && opt.engine != "copy_engine" &&
+               nbytes >= opt.compress_min_bytes && zf32::eligible(nbytes) && (ptr & 15) == 0;
+    }
 
     // Format of the bytes in a granted run (slot entries of the shared table).
-    bool run_is_z(uint32_t slot) const {
-        return slots && slot < num_slots &&
-               (reinterpret_cast<const volatile uint64_t&>(slots[slot].flags) & OFLD_FLAG_FORMAT_ZBF16) != 0;
+    uint64_t run_format(uint32_t slot) const {
+        return slots && slot < num_slots
+                   ? reinterpret_cast<const volatile uint64_t&>(slots[slot].flags) & OFLD_FLAG_FORMAT_MASK
+                   : 0;
     }
+    bool run_is_z(uint32_t slot) const { return (run_format(slot) & OFLD_FLAG_FORMAT_ZBF16) != 0; }
+    bool run_is_zf32(uint32_t slot) const { return (run_format(slot) & OFLD_FLAG_FORMAT_ZF32) != 0; }
 
     void launch_d2h(Pending& p, uint64_t src, char* dst_host, char* dst_dev, cudaStream_t s, bool hash) {
         if (!gpu) {
@@ -796,7 +865,31 @@ struct Agent::Impl {
             dig_dev = static_cast<uint64_t*>(p.dig.dev);
         }
         const uint32_t zmax = p.z ? zscan_max(p.nbytes, p.zb) : 0;
-        if (p.z && opt.coded_evict == "copy_engine" && zmax > 0 && (src & 15) == 0 &&
+        if (p.z && p.f32) {
+            // zf32: the coder computes no digests; they come from the fp32
+            // bytes on the aux stream, next to the coding and the copies
+            cudaEvent_t fork = nullptr, join = nullptr;
+            if (hash) {
+                CUDA_OK(cudaEventCreateWithFlags(&fork, cudaEventDisableTiming));
+                CUDA_OK(cudaEventCreateWithFlags(&join, cudaEventDisableTiming));
+                CUDA_OK(cudaEventRecord(fork, s));
+                CUDA_OK(cudaStreamWaitEvent(aux, fork, 0));
+                CUDA_OK(kern::hash_device(reinterpret_cast<const void*>(src), p.nbytes, dig_dev, aux, opt.hash_ctas));
+                CUDA_OK(cudaEventRecord(join, aux));
+            }
+            if (opt.coded_evict == "copy_engine" && zmax > 0 && (src & 15) == 0 &&
+                (reinterpret_cast<uintptr_t>(dst_host) & 15) == 0)
+                evict_zf32_ce(reinterpret_cast<const uint8_t*>(src), dst_host, p.nbytes,
+                              static_cast<const uint8_t*>(p.zb.dev), zmax, s);
+            else
+                CUDA_OK(kern::evict_zf32(reinterpret_cast<const void*>(src), dst_dev, p.nbytes,
+                                         static_cast<const uint8_t*>(p.zb.dev), s, opt.evict_ctas));
+            if (hash) {
+                CUDA_OK(cudaStreamWaitEvent(s, join, 0));
+                cudaEventDestroy(fork);
+                cudaEventDestroy(join);
+            }
+        } else if (p.z && opt.coded_evict == "copy_engine" && zmax > 0 && (src & 15) == 0 &&
             (reinterpret_cast<uintptr_t>(dst_host) & 15) == 0) {
             evict_z_ce(reinterpret_cast<const uint8_t*>(src), dst_host, p.nbytes, static_cast<const uint8_t*>(p.zb.dev),
                        dig_dev, zmax, s);
@@ -901,8 +994,12 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
                (D.opt.fast_submit ? OFLD_FLAG_SUBMIT_ON_GRANT : 0);
     rq.debug_name = name;
     PinnedPool::Buf zb;
-    const bool z = D.want_z(ptr, nbytes, fmt_hint) && D.zscan(ptr, nbytes, D.stream_of(stream), &zb);
-    if (z) rq.flags |= OFLD_FLAG_FORMAT_ZBF16;
+    bool z = false, f32 = false;
+    if (D.want_z(ptr, nbytes, fmt_hint))
+        z = D.zscan(ptr, nbytes, D.stream_of(stream), &zb);
+    else if (D.want_zf32(ptr, nbytes, fmt_hint))
+        z = f32 = D.zscan(ptr, nbytes, D.stream_of(stream), &zb, true);
+    if (z) rq.flags |= f32 ? OFLD_FLAG_FORMAT_ZF32 : OFLD_FLAG_FORMAT_ZBF16;
     RequestOffloadResponse g = D.call<Op::kRequestOffload>(rq);
     // Backpressure: every pinned run can be briefly held by transfers in
     // flight (readbacks, restores) with nothing drainable; they release runs
@@ -936,6 +1033,7 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
     p.nbytes = nbytes;
     p.cb = std::move(on_done);
     p.z = z;
+    p.f32 = f32;
     p.zb = zb;
     t.coded = z;
     D.inflight_d2h += nbytes;
@@ -1205,18 +1303,32 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
     D.inflight_h2d += src_bytes;
     uint32_t* mism_dev = nullptr;
     const bool z = D.run_is_z(r.slot_id);
+    const bool zf = D.run_is_zf32(r.slot_id);
     if (!D.gpu) {
         if (ro.cast != 0) {
             out.message = "casts need a GPU";
             return out;
         }
-        if (z) {
-            if (!zbf16::decode_object(reinterpret_cast<const uint8_t*>(host), src_bytes,
-                                      reinterpret_cast<uint8_t*>(ptr))) {
-                out.message = "malformed zbf16 object";
+        if (z || zf) {
+            const bool okd = z ? zbf16::decode_object(reinterpret_cast<const uint8_t*>(host), src_bytes,
+                                                      reinterpret_cast<uint8_t*>(ptr))
+                               : zf32::decode_object(reinterpret_cast<const uint8_t*>(host), src_bytes,
+                                                     reinterpret_cast<uint8_t*>(ptr));
+            if (!okd) {
+                out.message = z ? "malformed zbf16 object" : "malformed zf32 object";
                 D.finish(p);
                 return out;
             }
+            if (ro.verify && !expect.empty()) {  // digests are of the decoded bytes
+                std::vector<uint64_t> got(kern::digest_count(src_bytes));
+                ssh::host_chunk_digests(reinterpret_cast<const char*>(ptr), src_bytes, got.data());
+                for (size_t i = 0; i < got.size() && i < expect.size(); ++i)
+                    out.mismatched_chunks += got[i] != expect[i];
+            }
+            D.finish(p);
+            out.ok = out.mismatched_chunks == 0;
+            out.message = out.ok ? "ok" : "content digest mismatch";
+            return out;
         } else {
             std::memcpy(reinterpret_cast<void*>(ptr), host, src_bytes);
         }
@@ -1240,7 +1352,40 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
         std::memset(p.mism.host, 0, 4);
         mism_dev = static_cast<uint32_t*>(p.mism.dev);
     }
-    if (z && D.opt.coded_restore == "copy_engine" && ro.cast == 0 && !exp_dev && zmax > 0 &&
+    if (zf) {
+        // zf32: decode into the destination (through the staging ring when
+        // the run's largest coded row is known) or, for a cast, into a
+        // temporary fp32 copy that K2 then casts (and verifies)
+        const bool ce = D.opt.coded_restore == "copy_engine" && zmax > 0 &&
+                        (reinterpret_cast<uintptr_t>(host) & 15) == 0;
+        void* tmp = nullptr;
+        uint8_t* into = reinterpret_cast<uint8_t*>(ptr);
+        if (ro.cast != 0 || (ptr & 15) != 0) {  // the decoders write 16-byte aligned vectors
+            CUDA_OK(cudaMallocAsync(&tmp, src_bytes, s));
+            into = static_cast<uint8_t*>(tmp);
+        }
+        if (ce)
+            D.restore_zf32_ce(host, into, src_bytes, zmax, s);
+        else
+            CUDA_OK(kern::restore_zf32(dev, into, src_bytes, s, D.opt.restore_ctas));
+        if (tmp && ro.cast != 0) {
+            CUDA_OK(kern::restore_cast(tmp, reinterpret_cast<void*>(ptr), src_bytes, kern::Cast(ro.cast),
+                                       reinterpret_cast<float*>(ro.scales_ptr), exp_dev, mism_dev, s,
+                                       D.opt.restore_ctas));
+            CUDA_OK(cudaFreeAsync(tmp, s));
+            exp_dev = nullptr;  // verified by the cast's pass
+        } else if (tmp) {
+            CUDA_OK(cudaMemcpyAsync(reinterpret_cast<void*>(ptr), tmp, src_bytes, cudaMemcpyDeviceToDevice, s));
+            CUDA_OK(cudaFreeAsync(tmp, s));
+        }
+        if (exp_dev) {
+            const uint64_t nd = kern::digest_count(src_bytes);
+            p.dig = D.pool.get(nd * 8);
+            CUDA_OK(kern::hash_device(reinterpret_cast<const void*>(ptr), src_bytes, static_cast<uint64_t*>(p.dig.dev),
+                                      s, D.opt.hash_ctas));
+            CUDA_OK(kern::compare_digests(static_cast<const uint64_t*>(p.dig.dev), exp_dev, nd, mism_dev, s));
+        }
+    } else if (z && D.opt.coded_restore == "copy_engine" && ro.cast == 0 && !exp_dev && zmax > 0 &&
         (reinterpret_cast<uintptr_t>(host) & 15) == 0 && (ptr & 15) == 0) {
         D.restore_z_ce(host, reinterpret_cast<uint8_t*>(ptr), src_bytes, zmax, s);
     } else if (z) {
@@ -1343,7 +1488,21 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
                 D.inflight_h2d += p.nbytes;
                 ++D.restores;
                 const bool z = D.run_is_z(r.slot_id);
-                if (D.batch_kernel_ok(items[i].ptr, r.nbytes)) {
+                const bool zf = D.run_is_zf32(r.slot_id);
+                if (zf) {  // a zf32 run (evicted singly): its own decode
+                    if (D.gpu) {
+                        CUDA_OK(kern::restore_zf32(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes, s,
+                                                   D.opt.restore_ctas));
+                        CUDA_OK(cudaEventCreateWithFlags(&p.ev, cudaEventDisableTiming));
+                        CUDA_OK(cudaEventRecord(p.ev, s));
+                        last_ev = p.ev;
+                    } else if (!zf32::decode_object(reinterpret_cast<const uint8_t*>(host), r.nbytes,
+                                                    reinterpret_cast<uint8_t*>(items[i].ptr))) {
+                        out[i].message = "malformed zf32 object";
+                        D.finish(p);
+                        continue;
+                    }
+                } else if (D.batch_kernel_ok(items[i].ptr, r.nbytes)) {
                     kern::XferJob j{};
                     j.src = dev;
                     j.dst = reinterpret_cast<void*>(items[i].ptr);

@@ -100,6 +100,7 @@ struct AgentOptions {
 // evict() data hints.
 constexpr uint32_t kFmtUnknown = 0;
 constexpr uint32_t kFmtBf16 = 1;
+constexpr uint32_t kFmtF32 = 2;  // fp32 payload: zf32 coding when it pays
 
 struct EvictTicket {
     bool ok = false;

@@ -95,7 +95,10 @@ typedef enum ofld_arena_kind_e {
  * Set by the rank at reservation, stamped on the run's slot entries, kept
  * across drains and readbacks; readers decode. */
 #define OFLD_FLAG_FORMAT_ZBF16 (1ull << 18)
-#define OFLD_FLAG_FORMAT_MASK (OFLD_FLAG_FORMAT_ZBF16)
+/* Extension: the run holds an fp32 object in zf32 coding (ofld/zbf16.h),
+ * carried like OFLD_FLAG_FORMAT_ZBF16. */
+#define OFLD_FLAG_FORMAT_ZF32 (1ull << 19)
+#define OFLD_FLAG_FORMAT_MASK (OFLD_FLAG_FORMAT_ZBF16 | OFLD_FLAG_FORMAT_ZF32)
 
 typedef struct ofld_arena_desc_s {
     ofld_arena_id_t arena_id;

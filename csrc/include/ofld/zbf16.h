@@ -270,4 +270,90 @@ inline uint64_t coded_bytes(const uint8_t* in, uint64_t nbytes) {
 }
 
 }  // namespace zbf16
+
+// zf32: lossless coding of fp32 tensors for host transfers, built on zbf16.
+//
+// An fp32 value is the bf16 value of its top 16 bits (sign, exponent,
+// 7 mantissa bits) followed by 16 low mantissa bits. The top halves carry
+// the exponents and code like bf16 data; the low halves are near-random and
+// travel as they are. Per 128 KiB row of the object (32768 values):
+//
+//   row + 0            low plane: the low 16 bits of every value, in order
+//                      (64 KiB)
+//   row + 65536        the zbf16 coded chunk (mode 1 or 2, header first) of
+//                      the row's top halves, a 64 KiB bf16 chunk whose
+//                      element i is the top half of value i
+//
+// A row occupies its own 128 KiB of the run, so every byte of an object stays
+// inside [0, nbytes). Objects must be a whole number of rows (nbytes %
+// 131072 == 0); an object is coded only when every row's top-half chunk
+// codes (fits in 64 KiB). Typical ratio for N(0, s) fp32 data: 0.5 + 0.5 x
+// the zbf16 ratio of the top halves (about 0.85). The format is a property
+// of the pinned run (OFLD_FLAG_FORMAT_ZF32 on its slot entries).
+namespace zf32 {
+
+constexpr uint32_t kRow = 2 * zbf16::kChunk;
+constexpr uint32_t kLowPlane = zbf16::kChunk;  // offset of the coded chunk in a row
+
+SSH_HD bool eligible(uint64_t nbytes) { return nbytes >= kRow && nbytes % kRow == 0; }
+SSH_HD uint64_t rows(uint64_t nbytes) { return nbytes / kRow; }
+
+// Split one row of fp32 values into its top halves (`hi`, kChunk bytes) and
+// low halves (`lo`, kChunk bytes).
+inline void split_row(const uint8_t* src, uint8_t* hi, uint8_t* lo) {
+    for (uint32_t i = 0; i < kRow / 4; ++i) {
+        uint32_t w;
+        std::memcpy(&w, src + 4 * i, 4);
+        const uint16_t h = uint16_t(w >> 16), l = uint16_t(w & 0xFFFFu);
+        std::memcpy(hi + 2 * i, &h, 2);
+        std::memcpy(lo + 2 * i, &l, 2);
+    }
+}
+
+inline void join_row(const uint8_t* hi, const uint8_t* lo, uint8_t* out) {
+    for (uint32_t i = 0; i < kRow / 4; ++i) {
+        uint16_t h, l;
+        std::memcpy(&h, hi + 2 * i, 2);
+        std::memcpy(&l, lo + 2 * i, 2);
+        const uint32_t w = (uint32_t(h) << 16) | l;
+        std::memcpy(out + 4 * i, &w, 4);
+    }
+}
+
+// Whole objects. encode_object returns false (and leaves `out` unspecified)
+// when the object is not codable.
+inline bool encode_object(const uint8_t* src, uint64_t nbytes, uint8_t* out) {
+    if (!eligible(nbytes)) return false;
+    std::vector<uint8_t> hi(zbf16::kChunk);
+    for (uint64_t r = 0; r < rows(nbytes); ++r) {
+        const uint64_t base = r * kRow;
+        split_row(src + base, hi.data(), out + base);
+        if (!zbf16::encode_chunk(hi.data(), zbf16::kChunk, out + base + kLowPlane)) return false;
+    }
+    return true;
+}
+
+inline bool decode_object(const uint8_t* in, uint64_t nbytes, uint8_t* out) {
+    if (!eligible(nbytes)) return false;
+    std::vector<uint8_t> hi(zbf16::kChunk);
+    for (uint64_t r = 0; r < rows(nbytes); ++r) {
+        const uint64_t base = r * kRow;
+        if (!zbf16::decode_chunk(in + base + kLowPlane, zbf16::kChunk, hi.data())) return false;
+        join_row(hi.data(), in + base, out + base);
+    }
+    return true;
+}
+
+// Bytes that actually carry data (what crosses PCIe), for statistics.
+inline uint64_t coded_bytes(const uint8_t* in, uint64_t nbytes) {
+    uint64_t total = 0;
+    for (uint64_t r = 0; r < rows(nbytes); ++r) {
+        zbf16::Header hd;
+        std::memcpy(&hd, in + r * kRow + kLowPlane, zbf16::kHeader);
+        total += kLowPlane + hd.comp_len;
+    }
+    return total;
+}
+
+}  // namespace zf32
 }  // namespace ofld

@@ -89,6 +89,23 @@ cudaError_t evict_z(const void* src_dev, void* dst_mapped, uint64_t nbytes, cons
 cudaError_t restore_z(const void* src_mapped, void* dst_dev, uint64_t nbytes, Cast cast, float* scales_dev,
                       const uint64_t* expect, uint32_t* mismatch_dev, cudaStream_t stream, int ctas);
 
+// zf32 coding of fp32 objects (format: ofld/zbf16.h, namespace zf32): the
+// same three passes over whole 128 KiB rows (zf32::eligible(nbytes), 16-byte
+// aligned pointers). zscan_f32 writes one window base per row and, like
+// zscan, the per-CTA largest stored length of the rows' coded top halves
+// (what a strided copy moves per row beyond the 64 KiB low plane).
+// evict_zf32 computes no digests (hash the fp32 bytes with hash_device);
+// restore_zf32 has no cast or verification (compare_digests after a
+// hash_device of the result verifies).
+cudaError_t zscan_f32(const void* src_dev, uint64_t nbytes, uint8_t* ebase, uint32_t* fail, cudaStream_t stream,
+                      int ctas, uint32_t* max_coded = nullptr);
+cudaError_t evict_zf32(const void* src_dev, void* dst, uint64_t nbytes, const uint8_t* ebase, cudaStream_t stream,
+                       int ctas);
+cudaError_t restore_zf32(const void* src, void* dst_dev, uint64_t nbytes, cudaStream_t stream, int ctas);
+// *mismatch (device-accessible) += the number of i < n with got[i] != expect[i].
+cudaError_t compare_digests(const uint64_t* got, const uint64_t* expect, uint64_t n, uint32_t* mismatch,
+                            cudaStream_t stream);
+
 // Batched K1/K2: one launch moves every item of a batch (KV-cache blocks).
 // Jobs are 64-byte records sorted by chunk_begin (the global index of the
 // job's first 64 KiB chunk; total_chunks covers them all), in

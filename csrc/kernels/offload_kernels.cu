@@ -272,12 +272,27 @@ __device__ __forceinline__ uint32_t half_of(const uint4& v, int j) {
     return (j & 1) ? (w >> 16) : (w & 0xFFFFu);
 }
 
+// Vector vi of a coded chunk's bf16 elements. bf16 objects: the 16 bytes at
+// src + 16 vi. zf32 rows: the top halves of the eight fp32 values at
+// src + 32 vi, in element order, with their low halves in *lo.
+template <bool F32>
+__device__ __forceinline__ uint4 ld_zvec(const uint8_t* __restrict__ src, uint32_t vi, uint4* lo) {
+    if (!F32) return ld_once(src + uint64_t(vi) * 16);
+    const uint4 a = ld_once(src + uint64_t(vi) * 32), b = ld_once(src + uint64_t(vi) * 32 + 16);
+    *lo = make_uint4(__byte_perm(a.x, a.y, 0x5410), __byte_perm(a.z, a.w, 0x5410), __byte_perm(b.x, b.y, 0x5410),
+                     __byte_perm(b.z, b.w, 0x5410));
+    return make_uint4(__byte_perm(a.x, a.y, 0x7632), __byte_perm(a.z, a.w, 0x7632), __byte_perm(b.x, b.y, 0x7632),
+                      __byte_perm(b.z, b.w, 0x7632));
+}
+
 // Pre-pass over one chunk: the largest exponent (window base = emax - 14)
 // and whether the coded chunk fits in its raw length; a chunk that does not
 // fit sets *fail and the object is then moved uncoded. Two register passes
 // per chunk, so the pass runs at HBM rate. Every thread of the block calls
 // this; `red` is reused on return.
 // `stored` (may be null; thread 0's value counts) receives the chunk's stored length.
+// F32: `src` is a zf32 row and the chunk is its top halves (len = kChunk).
+template <bool F32 = false>
 __device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uint32_t len, uint8_t* eb_out,
                                             uint32_t* fail, uint32_t* red, uint32_t* stored = nullptr) {
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -286,7 +301,8 @@ __device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uin
 #pragma unroll
     for (int k = 0; k < kVecs; ++k) {
         const uint32_t vi = uint32_t(k) * kThreads + t;
-        v[k] = vi < nvec ? ld_once(src + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
+        uint4 lo;
+        v[k] = vi < nvec ? ld_zvec<F32>(src, vi, &lo) : make_uint4(0, 0, 0, 0);
     }
     // bf16 bit patterns with the sign cleared order like their magnitudes
     uint32_t m = 0;
@@ -333,17 +349,20 @@ __device__ __forceinline__ void zscan_chunk(const uint8_t* __restrict__ src, uin
     __syncthreads();  // red[] is reused by the next chunk
 }
 
-__global__ void __launch_bounds__(kThreads, 3)
+// F32: `nbytes` is the fp32 object's size (whole zf32 rows); chunk c is the
+// top halves of row c.
+template <bool F32>
+__global__ void __launch_bounds__(kThreads, F32 ? 2 : 3)
     k_zscan(const uint8_t* __restrict__ src, uint64_t nbytes, uint8_t* __restrict__ ebase_out, uint32_t* fail,
             uint32_t* max_coded, KernelStamp* ks) {
     StampScope stamp_scope_(ks);
     __shared__ uint32_t red[kThreads / 32];
-    const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+    const uint64_t nchunks = F32 ? nbytes / zf32::kRow : (nbytes + kChunk - 1) / kChunk;
     uint32_t cta_max = 0;  // thread 0: largest stored length of this CTA's chunks
     for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
         const uint64_t base = c * kChunk;
-        const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
-        if (zbf16::raw_by_rule(c, nchunks, len)) {
+        const uint32_t len = F32 ? kChunk : uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+        if (!F32 && zbf16::raw_by_rule(c, nchunks, len)) {
             if (threadIdx.x == 0) {
                 ebase_out[c] = 0;
                 cta_max = max(cta_max, len);  // stored raw
@@ -351,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 3)
             continue;  // uniform per chunk
         }
         uint32_t clen = 0;
-        zscan_chunk(src + base, len, ebase_out + c, fail, red, &clen);
+        zscan_chunk<F32>(src + (F32 ? c * zf32::kRow : base), len, ebase_out + c, fail, red, &clen);
         cta_max = max(cta_max, clen);
     }
     // One plain store per CTA into its own slot (the slots may be host-mapped
@@ -368,16 +387,45 @@ constexpr uint32_t kZStage = zbf16::kChunk;
 // memory (or keep it raw) and stream it to the host-mapped destination with
 // 16-byte vector stores. `src`/`dst` point at the chunk; 16-byte aligned,
 // len % 16 == 0. Every thread of the block calls this.
+// F32: `src`/`dst` are a zf32 row: the low halves go to dst, the coded top
+// halves to dst + kChunk; no digests (the caller hashes the fp32 bytes).
+template <bool F32 = false>
 __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                               uint32_t len, bool raw, uint32_t eb, uint64_t* digest_out,
                                               uint64_t* red, uint32_t* sc, uint8_t* zbuf) {
     const uint32_t t = threadIdx.x;
     const uint32_t nvec = len / 16;
     uint4 v[kVecs];
+    if (F32) {
+        // groups of four vectors: eight 16-byte loads in flight, then the
+        // four low-half vectors leave (bounded registers: the top halves of
+        // all sixteen stay for the coding below)
 #pragma unroll
-    for (int k = 0; k < kVecs; ++k) {
-        const uint32_t vi = uint32_t(k) * kThreads + t;
-        v[k] = vi < nvec ? ld_once(src + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
+        for (int k0 = 0; k0 < kVecs; k0 += 4) {
+            uint4 a[4], b[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint64_t off = uint64_t(uint32_t(k0 + q) * kThreads + t) * 32;
+                a[q] = ld_once(src + off);
+                b[q] = ld_once(src + off + 16);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t vi = uint32_t(k0 + q) * kThreads + t;
+                v[k0 + q] = make_uint4(__byte_perm(a[q].x, a[q].y, 0x7632), __byte_perm(a[q].z, a[q].w, 0x7632),
+                                       __byte_perm(b[q].x, b[q].y, 0x7632), __byte_perm(b[q].z, b[q].w, 0x7632));
+                st_stream(dst + uint64_t(vi) * 16,
+                          make_uint4(__byte_perm(a[q].x, a[q].y, 0x5410), __byte_perm(a[q].z, a[q].w, 0x5410),
+                                     __byte_perm(b[q].x, b[q].y, 0x5410), __byte_perm(b[q].z, b[q].w, 0x5410)));
+            }
+        }
+        dst += kChunk;
+    } else {
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;
+            v[k] = vi < nvec ? ld_once(src + uint64_t(vi) * 16) : make_uint4(0, 0, 0, 0);
+        }
     }
     ssh::Lane L = ssh::lane_init(t);
     // mode-1 escapes (low half) and values in the lowest 8 binades of the
@@ -387,7 +435,7 @@ __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, u
     for (int k = 0; k < kVecs; ++k) {
         const uint32_t vi = uint32_t(k) * kThreads + t;
         if (vi < nvec) {
-            ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
+            if (!F32) ssh::lane_update(L, v[k].x, v[k].y, v[k].z, v[k].w);
             if (raw) {
                 st_stream(dst + uint64_t(vi) * 16, v[k]);
             } else {
@@ -449,12 +497,18 @@ __device__ __forceinline__ void evict_chunk_z(const uint8_t* __restrict__ src, u
         for (uint32_t i = t; i < nout; i += kThreads)
             st_stream(dst + uint64_t(i) * 16, *reinterpret_cast<const uint4*>(zbuf + i * 16));
     }
+    if (F32) {
+        __syncthreads();  // orders zbuf reuse
+        return;
+    }
     uint64_t root = tree_fold(ssh::lane_digest(L, t), red);  // also orders zbuf reuse
     if (t == 0 && digest_out) *digest_out = ssh::chunk_finish(root, len);
 }
 
 // K1 with coding over one object. Requires 16-byte aligned src/dst and
 // nbytes % 16 == 0 (zbf16::eligible).
+// F32: a zf32 object (nbytes a whole number of rows), no digests.
+template <bool F32>
 __global__ void __launch_bounds__(kThreads, 2)
     k_evict_z(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes,
               const uint8_t* __restrict__ ebase, uint64_t* __restrict__ digests, KernelStamp* ks) {
@@ -462,6 +516,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     extern __shared__ __align__(16) uint8_t zbuf[];
     __shared__ uint64_t red[kThreads / 32];
     __shared__ uint32_t sc[kThreads / 32];
+    if (F32) {
+        const uint64_t nrows = nbytes / zf32::kRow;
+        // == kChunk, but computed: with the length a compile-time constant the
+        // coder's specialised form needs far more than its 128 registers
+        const uint32_t len = nrows ? uint32_t(nbytes / nrows / 2) : kChunk;
+        for (uint64_t c = blockIdx.x; c < nrows; c += gridDim.x)
+            evict_chunk_z<true>(src + c * zf32::kRow, dst + c * zf32::kRow, len, false, uint32_t(ebase[c]), nullptr,
+                                red, sc, zbuf);
+        return;
+    }
     const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
     for (uint64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
         const uint64_t base = c * kChunk;
@@ -625,6 +689,40 @@ __device__ __forceinline__ void load_chunk_z(const uint8_t* __restrict__ in, uin
         v[k] = make_uint4(w[0], w[1], w[2], w[3]);
     }
     __syncthreads();  // the stage is refilled by the next chunk
+}
+
+// zf32 decode (K2 over a zf32 object, no cast or verification): the top
+// halves decode into registers, the low halves load from the row's low
+// plane, and each vector leaves as eight interleaved fp32 values.
+__global__ void __launch_bounds__(kThreads, 2)
+    k_restore_zf32(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t nbytes, KernelStamp* ks) {
+    StampScope stamp_scope_(ks);
+    extern __shared__ __align__(16) uint8_t zbuf[];
+    __shared__ uint32_t sc[kThreads / 32];
+    const uint32_t t = threadIdx.x;
+    const uint64_t nrows = nbytes / zf32::kRow;
+    const uint32_t len = nrows ? uint32_t(nbytes / nrows / 2) : kChunk;  // == kChunk, computed (registers)
+    for (uint64_t c = blockIdx.x; c < nrows; c += gridDim.x) {
+        const uint8_t* row = src + c * zf32::kRow;
+        uint8_t* out = dst + c * zf32::kRow;
+        uint4 v[kVecs];
+        load_chunk_z(row + zf32::kLowPlane, len, false, sc, zbuf, v);
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+            const uint32_t vi = uint32_t(k) * kThreads + t;  // < kChunk / 16: rows are full
+            const uint4 lo = ld_once(row + uint64_t(vi) * 16);
+            const uint4 a = make_uint4(__byte_perm(lo.x, v[k].x, 0x5410), __byte_perm(lo.x, v[k].x, 0x7632),
+                                       __byte_perm(lo.y, v[k].y, 0x5410), __byte_perm(lo.y, v[k].y, 0x7632));
+            const uint4 b = make_uint4(__byte_perm(lo.z, v[k].z, 0x5410), __byte_perm(lo.z, v[k].z, 0x7632),
+                                       __byte_perm(lo.w, v[k].w, 0x5410), __byte_perm(lo.w, v[k].w, 0x7632));
+            // write-back stores: a warp instruction covers every other 16 bytes
+            // of its 1 KiB, and L2 must hold the line until the second
+            // instruction fills the gaps (an evict-first store made the HBM
+            // writes partial-sector read-modify-writes)
+            *reinterpret_cast<uint4*>(out + uint64_t(vi) * 32) = a;
+            *reinterpret_cast<uint4*>(out + uint64_t(vi) * 32 + 16) = b;
+        }
+    }
 }
 
 // K2 with decoding over one object: decode into registers, then continue as
@@ -905,7 +1003,24 @@ cudaError_t zscan(const void* src, uint64_t nbytes, uint8_t* ebase, uint32_t* fa
     int g = ctas > 0 ? ctas : sms * 3;
     if (uint64_t(g) > nchunks) g = int(nchunks);
     KernelStamp* ks = timing_take(kIdZScan, nbytes);
-    k_zscan<<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), nbytes, ebase, fail, max_coded, ks);
+    k_zscan<false><<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), nbytes, ebase, fail, max_coded, ks);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t zscan_f32(const void* src, uint64_t nbytes, uint8_t* ebase, uint32_t* fail, cudaStream_t s, int ctas,
+                      uint32_t* max_coded) {
+    if (max_coded) ctas = ctas > 0 ? std::min(ctas, kZScanSlots) : kZScanSlots;
+    if (!zf32::eligible(nbytes) || !aligned16(src) || !ebase || !fail) return cudaErrorInvalidValue;
+    int sms = 148;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint64_t nrows = zf32::rows(nbytes);
+    int g = ctas > 0 ? ctas : sms * 3;
+    if (uint64_t(g) > nrows) g = int(nrows);
+    KernelStamp* ks = timing_take(kIdZScanF32, nbytes);
+    k_zscan<true><<<g, kThreads, 0, s>>>(static_cast<const uint8_t*>(src), nbytes, ebase, fail, max_coded, ks);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }
@@ -928,15 +1043,57 @@ cudaError_t zscan_jobs(const XferJob* jobs, int njobs, uint64_t total_chunks, cu
 cudaError_t evict_z(const void* src, void* dst, uint64_t nbytes, const uint8_t* ebase, uint64_t* digests,
                     cudaStream_t s, int ctas) {
     if (!zbf16::eligible(nbytes) || !aligned16(src) || !aligned16(dst) || !ebase) return cudaErrorInvalidValue;
-    cudaError_t e = allow_stage(reinterpret_cast<const void*>(&k_evict_z), 0);
+    cudaError_t e = allow_stage(reinterpret_cast<const void*>(&k_evict_z<false>), 0);
     if (e != cudaSuccess) return e;
     // 96 CTAs: PCIe saturates with 48 at full clock, but a training step at
     // the power cap lowers SM clocks and these latency-bound CTAs need the
     // margin (KV blocks under an 8192^2 GEMM loop: 58.8 -> 66.1 GB/s).
     const int g = grid_for(nbytes, ctas, 96);
     KernelStamp* ks = timing_take(kIdEvictZ, nbytes);
-    k_evict_z<<<g, kThreads, kZStage, s>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nbytes,
+    k_evict_z<false><<<g, kThreads, kZStage, s>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nbytes,
                                            ebase, digests, ks);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t evict_zf32(const void* src, void* dst, uint64_t nbytes, const uint8_t* ebase, cudaStream_t s, int ctas) {
+    if (!zf32::eligible(nbytes) || !aligned16(src) || !aligned16(dst) || !ebase) return cudaErrorInvalidValue;
+    cudaError_t e = allow_stage(reinterpret_cast<const void*>(&k_evict_z<true>), 12);
+    if (e != cudaSuccess) return e;
+    const int g = grid_for(nbytes / 2, ctas, 96);  // one CTA iteration per row
+    KernelStamp* ks = timing_take(kIdEvictZF32, nbytes);
+    k_evict_z<true><<<g, kThreads, kZStage, s>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nbytes,
+                                                 ebase, nullptr, ks);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+cudaError_t restore_zf32(const void* src, void* dst, uint64_t nbytes, cudaStream_t s, int ctas) {
+    if (!zf32::eligible(nbytes) || !aligned16(src) || !aligned16(dst)) return cudaErrorInvalidValue;
+    cudaError_t e = allow_stage(reinterpret_cast<const void*>(&k_restore_zf32), 13);
+    if (e != cudaSuccess) return e;
+    const int g = grid_for(nbytes / 2, ctas, 96);
+    KernelStamp* ks = timing_take(kIdRestoreZF32, nbytes);
+    k_restore_zf32<<<g, kThreads, kZStage, s>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nbytes,
+                                                ks);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
+
+__global__ void k_compare_digests(const uint64_t* __restrict__ got, const uint64_t* __restrict__ expect, uint64_t n,
+                                  uint32_t* mismatch) {
+    uint32_t bad = 0;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x)
+        bad += got[i] != expect[i];
+    if (bad) atomicAdd(mismatch, bad);
+}
+
+cudaError_t compare_digests(const uint64_t* got, const uint64_t* expect, uint64_t n, uint32_t* mismatch,
+                            cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    if (!got || !expect || !mismatch) return cudaErrorInvalidValue;
+    const int g = int(std::min<uint64_t>((n + 255) / 256, 148));
+    k_compare_digests<<<g, 256, 0, s>>>(got, expect, n, mismatch);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError();
 }

@@ -44,6 +44,9 @@ const char* kernel_name(uint32_t id) {
         case kIdPush: return "k4_push";
         case kIdEvictBulk: return "k1_evict_bulk";
         case kIdRestoreBulk: return "k2_restore_bulk";
+        case kIdEvictZF32: return "k1_evict_zf32";
+        case kIdRestoreZF32: return "k2_restore_zf32";
+        case kIdZScanF32: return "zf32_scan";
         default: return "unknown";
     }
 }

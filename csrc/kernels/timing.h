@@ -41,6 +41,9 @@ enum KernelId : uint32_t {
     kIdPush = 11,       // K4
     kIdEvictBulk = 12,  // K1, bulk-copy form
     kIdRestoreBulk = 13,// K2, bulk-copy form
+    kIdEvictZF32 = 14,  // K1 with zf32 coding
+    kIdRestoreZF32 = 15,// K2 with zf32 decoding
+    kIdZScanF32 = 16,   // zf32 pre-pass
     kIdCount
 };
 const char* kernel_name(uint32_t id);

@@ -711,6 +711,54 @@ PYBIND11_MODULE(_C, m) {
                               reinterpret_cast<uint32_t*>(mismatch), reinterpret_cast<cudaStream_t>(stream), ctas),
               "restore_z");
     });
+    // zf32 host reference codec (tests, tools)
+    m.def("zf32_encode", [](py::buffer b) -> py::object {
+        py::buffer_info i = b.request();
+        const uint64_t n = uint64_t(i.size) * uint64_t(i.itemsize);
+        std::string out(n, '\0');
+        bool ok;
+        {
+            py::gil_scoped_release nogil;
+            ok = zf32::encode_object(static_cast<const uint8_t*>(i.ptr), n, reinterpret_cast<uint8_t*>(&out[0]));
+        }
+        if (!ok) return py::none();
+        return py::bytes(out);
+    });
+    m.def("zf32_decode", [](py::bytes coded) {
+        std::string in = coded;
+        std::string out(in.size(), '\0');
+        if (!zf32::decode_object(reinterpret_cast<const uint8_t*>(in.data()), in.size(),
+                                 reinterpret_cast<uint8_t*>(&out[0])))
+            throw std::runtime_error("malformed zf32 object");
+        return py::bytes(out);
+    });
+    m.def("zf32_coded_bytes", [](py::bytes coded) {
+        std::string in = coded;
+        return zf32::coded_bytes(reinterpret_cast<const uint8_t*>(in.data()), in.size());
+    });
+    m.def("k_zscan_f32", [](uint64_t src, uint64_t n, uint64_t ebase, uint64_t fail, uint64_t stream, int ctas,
+                            uint64_t max_coded) {
+        check(kern::zscan_f32(reinterpret_cast<const void*>(src), n, reinterpret_cast<uint8_t*>(ebase),
+                              reinterpret_cast<uint32_t*>(fail), reinterpret_cast<cudaStream_t>(stream), ctas,
+                              reinterpret_cast<uint32_t*>(max_coded)),
+              "zscan_f32");
+    }, py::arg("src"), py::arg("n"), py::arg("ebase"), py::arg("fail"), py::arg("stream"), py::arg("ctas"),
+       py::arg("max_coded") = 0);
+    m.def("k_evict_zf32", [](uint64_t src, uint64_t dst, uint64_t n, uint64_t ebase, uint64_t stream, int ctas) {
+        check(kern::evict_zf32(reinterpret_cast<const void*>(src), reinterpret_cast<void*>(dst), n,
+                               reinterpret_cast<const uint8_t*>(ebase), reinterpret_cast<cudaStream_t>(stream), ctas),
+              "evict_zf32");
+    });
+    m.def("k_restore_zf32", [](uint64_t src, uint64_t dst, uint64_t n, uint64_t stream, int ctas) {
+        check(kern::restore_zf32(reinterpret_cast<const void*>(src), reinterpret_cast<void*>(dst), n,
+                                 reinterpret_cast<cudaStream_t>(stream), ctas),
+              "restore_zf32");
+    });
+    m.def("k_compare_digests", [](uint64_t got, uint64_t expect, uint64_t n, uint64_t mismatch, uint64_t stream) {
+        check(kern::compare_digests(reinterpret_cast<const uint64_t*>(got), reinterpret_cast<const uint64_t*>(expect),
+                                    n, reinterpret_cast<uint32_t*>(mismatch), reinterpret_cast<cudaStream_t>(stream)),
+              "compare_digests");
+    });
     m.def("host_unregister", [](uint64_t ptr) { check(cudaHostUnregister(reinterpret_cast<void*>(ptr)), "cudaHostUnregister"); });
     bind_fabric(m);
 }

@@ -77,6 +77,8 @@ ACTION_NAMES = {0: "ATTACHED_EXISTING", 1: "NEED_D2H_CREATE", 2: "WAIT_FOR_CREAT
                 4: "REJECTED_STALE_VERSION", 5: "QUOTA_EXCEEDED", 6: "VERIFIED_BY_DEVICE_HASH",
                 7: "VERIFIED_BY_P2P", 255: "ERROR"}
 CASTS = {None: 0, "none": 0, "fp8_block128": 1, "bf16": 2, "fp32": 3}
+# evict data hints: payloads the agent may code for transfer (zbf16 / zf32)
+_FMT_HINTS = {torch.bfloat16: 1, torch.float32: 2}
 
 # c10::ScalarType numbering: the dtype field of a canonical key carries it so
 # keys match ranks that report tensor.scalar_type() from C++.
@@ -692,8 +694,9 @@ class Off:
         nbytes = src.numel() * src.element_size()
         tid = int(tensor_id) or self._next_tensor_id()
         ver = int(version) or 1
-        # bf16 payloads may travel zbf16-coded (lossless; the agent decides per object)
-        hint = 1 if src.dtype == torch.bfloat16 else 0
+        # bf16 and fp32 payloads may travel coded (zbf16 / zf32, lossless; the
+        # agent decides per object)
+        hint = _FMT_HINTS.get(src.dtype, 0)
         ok, msg, _lease, _slot, _lo, _hi, coded = self._agent.evict(
             src.data_ptr(), nbytes, _stream_handle(stream, src.device), bool(destructive), tid, ver, name or "",
             cb, bool(wait), hint)
@@ -753,7 +756,7 @@ class Off:
                 raise RuntimeError("evict_batch: tensors must be contiguous")
         ids = [self._next_tensor_id() for _ in tensors]
         vers = list(versions) if versions is not None else [1] * len(tensors)
-        items = [(t.data_ptr(), t.numel() * t.element_size(), i, v, 1 if t.dtype == torch.bfloat16 else 0)
+        items = [(t.data_ptr(), t.numel() * t.element_size(), i, v, _FMT_HINTS.get(t.dtype, 0))
                  for t, i, v in zip(tensors, ids, vers)]
         res = self._agent.evict_batch(items, _stream_handle(stream, tensors[0].device), bool(wait))
         out = []

@@ -1,6 +1,7 @@
 """Evict/restore size sweep on every GPU of the job.
 
-Workload: bf16 tensors with N(0,1) values, sizes powers of two from 4 KB to
+Workload: bf16 tensors with N(0,1) values (``--dtype fp32``: fp32 with
+N(0, 0.02) values, zf32-coded), sizes powers of two from 4 KB to
 8 GB (``--max-size-mb``), evicted into the GPU's pinned window (fused content
 hash; bf16 payloads zbf16-coded) and restored, ``--steps`` repeats per size,
 while an 8192x8192 bf16 GEMM loop runs on the same GPU. Each direction is
@@ -49,11 +50,15 @@ def run(args, metric: str) -> dict:
     load = GemmLoad(env.device).start() if args.matmul else None
     g = torch.Generator(device=env.device).manual_seed(1234 + env.rank)
     rows = []
+    fp32 = getattr(args, "dtype", "bf16") == "fp32"
     launches0 = native().kernel_launch_count()
     sampler = ClockSampler([env.local_rank]).start().wait_first()
     sampler.mark_start()
     for nbytes in sizes:
-        x = torch.randn(nbytes // 2, dtype=torch.bfloat16, device=env.device, generator=g)
+        if fp32:
+            x = torch.randn(nbytes // 4, dtype=torch.float32, device=env.device, generator=g) * 0.02
+        else:
+            x = torch.randn(nbytes // 2, dtype=torch.bfloat16, device=env.device, generator=g)
         ref = off.hash_tensor(x)
         ev, rs = [], []
         coded = False
@@ -93,10 +98,11 @@ def run(args, metric: str) -> dict:
         "unit": "GB/s (aggregate round trip at the 1 GiB point; per-size rows below)",
         "n_gpus": env.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(head["evict_ms"] + head["restore_ms"], 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: bf16 N(0,1) per size, seeded per rank",
-        "config": {"model": "evict/restore size sweep 4 KB - max size, bf16", "max_bytes": max_bytes,
-                   "arena_gb_per_gpu": window_gb, "transfer_coding": "zbf16 where it codes" if args.compress
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32" if fp32 else "bf16",
+        "data": "synthetic: fp32 N(0, 0.02) per size, seeded per rank" if fp32
+                else "synthetic: bf16 N(0,1) per size, seeded per rank",
+        "config": {"model": f"evict/restore size sweep 4 KB - max size, {'fp32' if fp32 else 'bf16'}", "max_bytes": max_bytes,
+                   "arena_gb_per_gpu": window_gb, "transfer_coding": ("zf32" if fp32 else "zbf16") + " where it codes" if args.compress
                    else "none (--compress 0)",
                    "concurrent_matmul": load.describe() if load else "none", "global_batch": env.world,
                    "seq_len": 0, "parallelism": f"dp{env.world}", "slot_mb": 64,

@@ -6,7 +6,8 @@ Kernels: evict (K1, device -> pinned + ssh128), restore (K2, pinned ->
 device), restore_fp8 (K2 with the bf16 -> fp8 1x128 cast), evict_z /
 restore_z (coded K1 / K2 to and from host memory), evict_z_stage /
 restore_z_stage (the same coding into and decoding from device memory, the
-passes of the copy-engine coded paths), evict_bulk /
+passes of the copy-engine coded paths), zscan_f32 / evict_zf32 / restore_zf32
+and their _stage forms (zf32 coding of an fp32 tensor), evict_bulk /
 restore_bulk (K1 / K2 as bulk copies through shared memory), hash (device
 ssh128, the library's choice of form), hash_onepass (the per-thread-load
 hash kernel), hash_stream (ssh128 through the K4 bulk-copy pipeline), verify (K3
@@ -30,7 +31,9 @@ def main():
     ap.add_argument("--kernel", required=True, choices=["evict", "restore", "restore_fp8", "hash", "hash_onepass",
                                                           "hash_stream", "verify", "push", "push_fp8", "zscan",
                                                           "evict_z", "restore_z", "evict_bulk", "restore_bulk",
-                                                          "evict_z_stage", "restore_z_stage"])
+                                                          "evict_z_stage", "restore_z_stage", "zscan_f32",
+                                                          "evict_zf32", "restore_zf32", "evict_zf32_stage",
+                                                          "restore_zf32_stage"])
     ap.add_argument("--mb", type=int, default=512)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--ctas", type=int, default=0)
@@ -61,6 +64,16 @@ def main():
         C.k_zscan(x.data_ptr(), n, zeb.data_ptr(), err.data_ptr(), s, 0)
         C.k_evict_z(x.data_ptr(), host.data_ptr(), n, zeb.data_ptr(), dig.data_ptr(), s, a.ctas)
         if a.kernel == "restore_z_stage":
+            stage = torch.empty(n, dtype=torch.uint8, device=dev)
+            stage.copy_(host)
+    xf = None
+    if "f32" in a.kernel:
+        # zf32: an fp32 tensor of the same byte size (N(0, 0.02): master
+        # weights), its row window bases and coded host copy (and a device copy)
+        xf = torch.randn(n // 4, device=dev) * 0.02
+        C.k_zscan_f32(xf.data_ptr(), n, zeb.data_ptr(), err.data_ptr(), s, 0)
+        C.k_evict_zf32(xf.data_ptr(), host.data_ptr(), n, zeb.data_ptr(), s, a.ctas)
+        if a.kernel == "restore_zf32_stage":
             stage = torch.empty(n, dtype=torch.uint8, device=dev)
             stage.copy_(host)
     if a.kernel == "verify":
@@ -112,6 +125,16 @@ def main():
             C.k_evict_z(x.data_ptr(), out.data_ptr(), n, zeb.data_ptr(), dig.data_ptr(), s, a.ctas)
         elif a.kernel == "restore_z_stage":  # decoding from device memory (the copy-engine restore's pass)
             C.k_restore_z(stage.data_ptr(), out.data_ptr(), n, 0, 0, 0, 0, s, a.ctas)
+        elif a.kernel == "zscan_f32":
+            C.k_zscan_f32(xf.data_ptr(), n, zeb.data_ptr(), err.data_ptr(), s, 0)
+        elif a.kernel == "evict_zf32":
+            C.k_evict_zf32(xf.data_ptr(), host.data_ptr(), n, zeb.data_ptr(), s, a.ctas)
+        elif a.kernel == "restore_zf32":
+            C.k_restore_zf32(host.data_ptr(), out.data_ptr(), n, s, a.ctas)
+        elif a.kernel == "evict_zf32_stage":
+            C.k_evict_zf32(xf.data_ptr(), out.data_ptr(), n, zeb.data_ptr(), s, a.ctas)
+        elif a.kernel == "restore_zf32_stage":
+            C.k_restore_zf32(stage.data_ptr(), out.data_ptr(), n, s, a.ctas)
         elif a.kernel == "hash_stream":
             C.k_hash_stream(x.data_ptr(), n, dig.data_ptr(), err.data_ptr(), s, a.ctas, a.stages)
         elif pusher is not None:
@@ -128,6 +151,8 @@ def main():
     if int(err.item()) != 0 or (pusher is not None and pusher.result()["error"]):
         code = int(err.item()) if pusher is None else pusher.result()["error"]
         raise SystemExit(f"{a.kernel}: device status {code}")
+    if a.kernel in ("restore_zf32", "restore_zf32_stage") and not torch.equal(out.view(torch.float32), xf):
+        raise SystemExit(f"{a.kernel}: decoded values differ")
     if a.kernel in ("hash", "hash_stream", "evict_bulk"):  # the digests must equal the one-pass kernel's
         ref = torch.zeros_like(dig)
         C.k_hash_onepass(x.data_ptr(), n, ref.data_ptr(), s, 0)

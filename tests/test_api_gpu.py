@@ -112,15 +112,15 @@ def test_kernel_timing_stamps_transfers(gpu_off):
     off.enable_kernel_timing()
     _, start = off.kernel_timings()
     x = torch.randn(32 << 20, dtype=torch.bfloat16, device="cuda")  # 64 MiB: zbf16-coded
-    f = torch.randn(8 << 20, device="cuda")                         # 32 MiB fp32: uncoded
+    f = torch.randint(-2**31, 2**31 - 1, (8 << 20,), dtype=torch.int32, device="cuda")  # 32 MiB int32: uncoded
     hx, hf = off.copy(x, wait=True), off.copy(f, wait=True)
     hx.restore_into(x, wait=True)
     hf.restore_into(f, wait=True)
     torch.cuda.synchronize()
     recs, nxt = off.kernel_timings(start)
-    assert nxt >= start + 4  # zbf16 scan, coded K1, hash beside the fp32 copy, coded K2
+    assert nxt >= start + 4  # zbf16 scan, coded K1, hash beside the int32 copy, coded K2
     kinds = {r["kernel"] for r in recs}
-    # bf16 moves coded through the SM kernels; fp32 moves on the copy engine
+    # bf16 moves coded through the SM kernels; int32 moves on the copy engine
     # with its digests computed by the hash kernel beside it
     assert {"zbf16_scan", "k1_evict_zbf16", "k2_restore_zbf16", "k1_hash"} <= kinds, kinds
     for r in recs:

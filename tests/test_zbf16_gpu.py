@@ -133,10 +133,17 @@ def test_api_codes_bf16_and_round_trips(zsession):
     q, sc = h.restore(cast="fp8_block128")
     assert q.dtype == torch.float8_e4m3fn and sc.numel() == ref.numel() // 128
     h.discard()
-    # fp32 and small tensors move uncoded
+    # fp32 in whole 128 KiB rows moves zf32-coded; other fp32 sizes, integer
+    # and small tensors move uncoded
     f = torch.randn(8 << 20, device="cuda")
     hf = off.copy(f, wait=True)
-    assert not hf.coded and torch.equal(hf.restore(), f)
+    assert hf.coded and torch.equal(hf.restore(), f)
+    f2 = torch.randn((8 << 20) + 4, device="cuda")
+    hf2 = off.copy(f2, wait=True)
+    assert not hf2.coded and torch.equal(hf2.restore(), f2)
+    i32 = torch.randint(0, 1000, (8 << 20,), dtype=torch.int32, device="cuda")
+    hi = off.copy(i32, wait=True)
+    assert not hi.coded and torch.equal(hi.restore(), i32)
     small = _case(1 << 20, "weights")
     hs = off.copy(small, wait=True)
     assert not hs.coded and torch.equal(hs.restore(), small)
