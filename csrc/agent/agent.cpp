@@ -1709,11 +1709,27 @@ void Agent::synchronize() {
 // ---------------------------------------------------------------------------
 RegisterJobResponse Agent::register_job(const RegisterJobRequest& r) { return d_->call<Op::kRegisterJob>(r); }
 
-CanonicalOutcome Agent::canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
-                                        const RequestCanonicalEvictRequest& in, DoneCallback on_invalidate, bool wait) {
-    NvtxRange nvtx_("ofld.canonical_evict");
-    Impl& D = *d_;
+// A canonical evict in two halves. begin: the attach-or-create round trip
+// and, for a create or a candidate, the submitted mark and the copy's launch
+// (copy engine or K1, hash in the same pass). end: wait for that copy, fold
+// the digests, mark the copy complete and commit the object. canonical_evict
+// runs both; canonical_evict_batch begins every item before it ends the
+// first, so each item's round trips overlap the copies launched before it.
+struct Agent::CanonPending {
     CanonicalOutcome out;
+    bool copying = false;
+    bool trusted = false;
+    uint64_t nbytes = 0;
+    TransferMark mark{};
+    RequestCanonicalEvictResponse resp;
+    DoneCallback cb;
+    bool destructive = false;
+    std::unique_ptr<Impl::Pending> p;
+};
+
+void Agent::canonical_begin(CanonPending& c, uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
+                            const RequestCanonicalEvictRequest& in, DoneCallback on_invalidate) {
+    Impl& D = *d_;
     RequestCanonicalEvictRequest req = in;
     req.rank_id = D.opt.rank_id;
     req.rank_epoch = D.epoch;
@@ -1722,22 +1738,28 @@ CanonicalOutcome Agent::canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHan
     req.destructive = destructive;
     req.key.nbytes = nbytes;
     if (req.key.shard_nbytes == 0) req.key.shard_nbytes = nbytes;
-    RequestCanonicalEvictResponse resp = D.call<Op::kRequestCanonicalEvict>(req);
+    c.nbytes = nbytes;
+    c.destructive = destructive;
+    c.cb = std::move(on_invalidate);
+    c.trusted = req.dedup_mode == offload_v2::DEDUP_SEMANTIC_TRUSTED || req.dedup_mode == offload_v2::DEDUP_DISABLED;
+    c.resp = D.call<Op::kRequestCanonicalEvict>(req);
+    const RequestCanonicalEvictResponse& resp = c.resp;
+    CanonicalOutcome& out = c.out;
     out.action = resp.action;
     out.object_id = resp.object_id;
     out.message = resp.message;
-    if (!resp.ok) return out;
+    if (!resp.ok) return;
     cudaStream_t s = D.stream_of(stream);
 
     const bool attached = resp.action == offload_v2::ATTACH_ACTION_ATTACHED_EXISTING ||
                           resp.action == 7 /* attached after a peer byte compare */;
     if (attached || resp.action == offload_v2::ATTACH_ACTION_WAIT_FOR_CREATOR) {
         out.ok = true;
-        if (attached && destructive && on_invalidate) {
+        if (attached && destructive && c.cb) {
             if (D.gpu) CUDA_OK(cudaStreamSynchronize(s));  // producer kernels done before the storage goes
-            on_invalidate();
+            c.cb();
         }
-        return out;
+        return;
     }
     if (resp.action == 6 /* verify-hash-only */) {
         // Replica verification without a copy: hash the local GPU bytes.
@@ -1752,48 +1774,58 @@ CanonicalOutcome Agent::canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHan
         CommitCanonicalObjectResponse cr = D.call<Op::kCommitCanonicalObject>(cm);
         out.ok = cr.ok;
         out.message = cr.message;
-        if (cr.ok && destructive && on_invalidate) on_invalidate();
-        return out;
+        if (cr.ok && destructive && c.cb) c.cb();
+        return;
     }
     if (resp.action != offload_v2::ATTACH_ACTION_NEED_D2H_CREATE &&
         resp.action != offload_v2::ATTACH_ACTION_DUPLICATE_CANDIDATE)
-        return out;
+        return;
 
     // Create or candidate: copy into the reserved run with the fused hash.
     char *host = nullptr, *dev = nullptr;
     D.resolve(resp.arena_id, resp.arena_offset, nbytes, &host, &dev);
-    TransferMark m{D.opt.rank_id, D.epoch, resp.lease_id, resp.synthetic_tid, 1, resp.slot_id, 0, real_ns()};
-    StatusResponse sr = D.call<Op::kMarkD2HSubmitted>(m);
+    c.mark = TransferMark{D.opt.rank_id, D.epoch, resp.lease_id, resp.synthetic_tid, 1, resp.slot_id, 0, real_ns()};
+    StatusResponse sr = D.call<Op::kMarkD2HSubmitted>(c.mark);
     if (!sr.ok) LOG_WARN(TAG, "canonical MarkD2HSubmitted: %s", sr.message.c_str());
     ++D.evicts;
-    Impl::Pending p;
-    p.nbytes = nbytes;
-    D.launch_d2h(p, ptr, host, dev, s, true);
+    c.p.reset(new Impl::Pending());
+    c.p->nbytes = nbytes;
+    D.launch_d2h(*c.p, ptr, host, dev, s, true);
+    c.copying = true;
+}
+
+void Agent::canonical_end(CanonPending& c) {
+    Impl& D = *d_;
+    if (!c.copying) return;
+    c.copying = false;
+    Impl::Pending& p = *c.p;
+    CanonicalOutcome& out = c.out;
     if (p.ev) CUDA_OK(cudaEventSynchronize(p.ev));
     if (p.ev) cudaEventDestroy(p.ev);
+    p.ev = nullptr;
     ssh::Object h{0, 0};
     if (p.dig.host) {
-        h = ssh::fold_digests(static_cast<const uint64_t*>(p.dig.host), p.ndig, nbytes);
+        h = ssh::fold_digests(static_cast<const uint64_t*>(p.dig.host), p.ndig, c.nbytes);
         if (D.gpu)
             D.pool.put(p.dig);
         else
             std::free(p.dig.host);
+        p.dig = {};
     }
-    D.d2h_bytes += nbytes;
+    D.d2h_bytes += c.nbytes;
     ++D.d2h_done;
-    MarkD2HCompleteResponse dr = D.call<Op::kMarkD2HComplete>(m);
+    MarkD2HCompleteResponse dr = D.call<Op::kMarkD2HComplete>(c.mark);
     if (!dr.ok) {
         out.message = "canonical MarkD2HComplete rejected";
-        return out;
+        return;
     }
-    const bool trusted = req.dedup_mode == offload_v2::DEDUP_SEMANTIC_TRUSTED || req.dedup_mode == offload_v2::DEDUP_DISABLED;
     CommitCanonicalObjectRequest cm;
     cm.rank_id = D.opt.rank_id;
     cm.rank_epoch = D.epoch;
-    cm.object_id = resp.object_id;
-    cm.lease_id = resp.lease_id;
-    cm.slot_id = resp.slot_id;
-    if (!(trusted && D.opt.zero_canonical_hash)) {
+    cm.object_id = c.resp.object_id;
+    cm.lease_id = c.resp.lease_id;
+    cm.slot_id = c.resp.slot_id;
+    if (!(c.trusted && D.opt.zero_canonical_hash)) {
         cm.content_hash_lo = h.lo;
         cm.content_hash_hi = h.hi;
     }
@@ -1803,7 +1835,43 @@ CanonicalOutcome Agent::canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHan
     out.message = cr.message;
     out.hash_lo = h.lo;
     out.hash_hi = h.hi;
-    if (cr.ok && destructive && on_invalidate) on_invalidate();
+    if (cr.ok && c.destructive && c.cb) c.cb();
+}
+
+CanonicalOutcome Agent::canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
+                                        const RequestCanonicalEvictRequest& in, DoneCallback on_invalidate, bool) {
+    NvtxRange nvtx_("ofld.canonical_evict");
+    CanonPending c;
+    canonical_begin(c, ptr, nbytes, stream, destructive, in, std::move(on_invalidate));
+    canonical_end(c);
+    return c.out;
+}
+
+// Many canonical evicts on one stream: every item's attach-or-create round
+// trip and copy launch first, then the completions in order. The copies run
+// back to back on the stream while the later items' round trips and the
+// earlier items' commits proceed on the host. At most `max_inflight_bytes`
+// of copies are outstanding (0: no limit); beyond it the oldest item is
+// finished before the next begins.
+std::vector<CanonicalOutcome> Agent::canonical_evict_batch(const std::vector<CanonicalItem>& items,
+                                                           StreamHandle stream, bool destructive,
+                                                           uint64_t max_inflight_bytes) {
+    NvtxRange nvtx_("ofld.canonical_evict_batch");
+    std::vector<CanonPending> cs(items.size());
+    size_t done = 0;
+    uint64_t inflight = 0;
+    for (size_t i = 0; i < items.size(); ++i) {
+        while (max_inflight_bytes && inflight > 0 && inflight + items[i].nbytes > max_inflight_bytes && done < i) {
+            if (cs[done].copying) inflight -= cs[done].nbytes;
+            canonical_end(cs[done++]);
+        }
+        canonical_begin(cs[i], items[i].ptr, items[i].nbytes, stream, destructive, items[i].req, items[i].on_invalidate);
+        if (cs[i].copying) inflight += cs[i].nbytes;
+    }
+    for (; done < items.size(); ++done) canonical_end(cs[done]);
+    std::vector<CanonicalOutcome> out;
+    out.reserve(items.size());
+    for (CanonPending& c : cs) out.push_back(std::move(c.out));
     return out;
 }
 

@@ -133,6 +133,13 @@ struct CanonicalOutcome {
     uint64_t hash_lo = 0, hash_hi = 0;
 };
 
+// One item of canonical_evict_batch.
+struct CanonicalItem {
+    uint64_t ptr = 0, nbytes = 0;
+    RequestCanonicalEvictRequest req;
+    DoneCallback on_invalidate;
+};
+
 struct AgentStats {
     uint32_t rank_id = 0;
     int gpu_id = -1, numa_node = 0;
@@ -187,6 +194,10 @@ class Agent {
     RegisterJobResponse register_job(const RegisterJobRequest& r);
     CanonicalOutcome canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
                                      const RequestCanonicalEvictRequest& req, DoneCallback on_invalidate, bool wait);
+    // Many canonical evicts: all round trips and copies are issued before the
+    // first completion is awaited (bounded by max_inflight_bytes, 0 = none).
+    std::vector<CanonicalOutcome> canonical_evict_batch(const std::vector<CanonicalItem>& items, StreamHandle stream,
+                                                        bool destructive, uint64_t max_inflight_bytes = 0);
     RestoreOutcome canonical_restore(uint64_t object_id, uint64_t ptr, uint64_t nbytes, StreamHandle stream,
                                      bool wait, const RestoreOptions& ro);
     SealModelVersionResponse seal(const SealModelVersionRequest& r);
@@ -222,6 +233,10 @@ class Agent {
     struct Impl;
 
  private:
+    struct CanonPending;
+    void canonical_begin(CanonPending& c, uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
+                         const RequestCanonicalEvictRequest& req, DoneCallback on_invalidate);
+    void canonical_end(CanonPending& c);
     std::unique_ptr<Impl> d_;
 };
 

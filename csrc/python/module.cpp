@@ -383,6 +383,33 @@ PYBIND11_MODULE(_C, m) {
                 return py::make_tuple(r.ok, r.action, r.object_id, r.did_d2h, r.message, r.hash_lo, r.hash_hi);
             })
         .def(
+            "canonical_evict_batch",
+            [](PyAgent& self, py::list items, uint64_t stream, bool destructive, uint64_t max_inflight_bytes) {
+                // items: (ptr, nbytes, request body, invalidate callback or None)
+                std::vector<CanonicalItem> v;
+                v.reserve(items.size());
+                for (py::handle it : items) {
+                    py::tuple t = py::reinterpret_borrow<py::tuple>(it);
+                    CanonicalItem ci;
+                    ci.ptr = t[0].cast<uint64_t>();
+                    ci.nbytes = t[1].cast<uint64_t>();
+                    std::string b = t[2].cast<py::bytes>();
+                    ci.req = decode<RequestCanonicalEvictRequest>(reinterpret_cast<const uint8_t*>(b.data()), b.size());
+                    ci.on_invalidate = wrap_cb(py::reinterpret_borrow<py::object>(t[3]));
+                    v.push_back(std::move(ci));
+                }
+                std::vector<CanonicalOutcome> rs;
+                {
+                    py::gil_scoped_release nogil;
+                    rs = self.ag().canonical_evict_batch(v, stream, destructive, max_inflight_bytes);
+                }
+                py::list out;
+                for (const CanonicalOutcome& r : rs)
+                    out.append(py::make_tuple(r.ok, r.action, r.object_id, r.did_d2h, r.message, r.hash_lo, r.hash_hi));
+                return out;
+            },
+            py::arg("items"), py::arg("stream"), py::arg("destructive"), py::arg("max_inflight_bytes") = 0)
+        .def(
             "canonical_restore",
             [](PyAgent& self, uint64_t oid, uint64_t ptr, uint64_t nbytes, uint64_t stream, bool wait, int cast,
                uint64_t scales_ptr) {

@@ -31,7 +31,7 @@ import json
 import os
 import threading
 import time
-from typing import Iterable, List, Optional, Sequence, Union
+from typing import Iterable, List, Optional, Sequence, Tuple, Union
 
 import torch
 
@@ -499,26 +499,9 @@ class Off:
         for ``device_hash_verified`` replicas (hash of the local GPU copy
         compared by the daemon; nothing crosses PCIe).
         """
-        job = self._job()
-        pol = dedup_policy or self._dedup_policy
-        mode = 0 if dedup == "disabled" else pol.mode_int
-        unsafe = unsafe_autograd or self._unsafe_default
-        src = tensor
-        if not destructive and tensor.is_contiguous():
-            pass  # a copy that leaves the tensor alone reads a contiguous view in place
-        elif compact or allow_views:
-            src = tensor.clone(memory_format=torch.contiguous_format)
-        else:
-            _validate_destructive(tensor, unsafe)
-        nbytes = src.numel() * src.element_size()
-        key = canonical_key
-        if key.dtype == 0:
-            key.dtype = _SCALAR_TYPE.get(src.dtype, 0)
-        body = _wire.encode("RequestCanonicalEvictRequest", {
-            "key": key.to_wire(job, nbytes), "local_tensor_id": local_tensor_id, "local_version": local_version,
-            "destructive": destructive, "attach_if_exists": True, "create_if_missing": True, "dedup_mode": mode,
-            "allow_duplicate_candidate": pol.allow_duplicate_candidate, "alignment": 256})
-        cb = _invalidate_callback(tensor) if destructive and not (compact or allow_views) else None
+        src, nbytes, body, cb = self._canonical_request(tensor, canonical_key, dedup, destructive, allow_views,
+                                                        unsafe_autograd, compact, local_tensor_id, local_version,
+                                                        dedup_policy)
         stream_h = _stream_handle(stream, src.device)
         deadline = time.monotonic() + timeout_s
         while True:
@@ -532,6 +515,75 @@ class Off:
             raise RuntimeError(f"canonical_evict failed (action={ACTION_NAMES.get(action, action)}): {msg}")
         return CanonicalHandle(oid, action, did_d2h, canonical_key, msg, off=self,
                                content_hash=(hlo, hhi) if (hlo or hhi) else None)
+
+    def _canonical_request(self, tensor, key, dedup, destructive, allow_views, unsafe_autograd, compact,
+                           local_tensor_id, local_version, dedup_policy):
+        """Source tensor, byte count, encoded RequestCanonicalEvict body and
+        invalidate callback of one canonical evict."""
+        job = self._job()
+        pol = dedup_policy or self._dedup_policy
+        mode = 0 if dedup == "disabled" else pol.mode_int
+        unsafe = unsafe_autograd or self._unsafe_default
+        src = tensor
+        if not destructive and tensor.is_contiguous():
+            pass  # a copy that leaves the tensor alone reads a contiguous view in place
+        elif compact or allow_views:
+            src = tensor.clone(memory_format=torch.contiguous_format)
+        else:
+            _validate_destructive(tensor, unsafe)
+        nbytes = src.numel() * src.element_size()
+        if key.dtype == 0:
+            key.dtype = _SCALAR_TYPE.get(src.dtype, 0)
+        body = _wire.encode("RequestCanonicalEvictRequest", {
+            "key": key.to_wire(job, nbytes), "local_tensor_id": local_tensor_id, "local_version": local_version,
+            "destructive": destructive, "attach_if_exists": True, "create_if_missing": True, "dedup_mode": mode,
+            "allow_duplicate_candidate": pol.allow_duplicate_candidate, "alignment": 256})
+        cb = _invalidate_callback(tensor) if destructive and not (compact or allow_views) else None
+        return src, nbytes, body, cb
+
+    def canonical_evict_batch(self, items: Sequence[Tuple[torch.Tensor, CanonicalKey]],
+                              dedup: str = "attach_or_create", destructive: bool = True, stream=None,
+                              allow_views: bool = False, unsafe_autograd: bool = False, compact: bool = False,
+                              dedup_policy: Optional[DedupPolicy] = None, max_inflight_bytes: int = 0,
+                              wait_for_creator: bool = False, timeout_s: float = 600.0) -> List[CanonicalHandle]:
+        """``canonical_evict`` of many ``(tensor, key)`` pairs on one stream.
+
+        Every item's attach-or-create round trip and copy are issued before
+        the first copy is awaited, so the round trips of later items and the
+        commits of earlier ones overlap the copies in flight (at most
+        ``max_inflight_bytes`` of copies outstanding; 0 = no limit). The
+        outcome of each item is that of ``canonical_evict``; items answered
+        WAIT_FOR_CREATOR are retried one by one when ``wait_for_creator``.
+        Additive to StateSpectre's API (its sealed versions record one tensor
+        per call: python_api/state_spectre/__init__.py canonical_evict).
+        """
+        if not items:
+            return []
+        reqs = []
+        keep = []
+        dev = None
+        for tensor, key in items:
+            src, nbytes, body, cb = self._canonical_request(tensor, key, dedup, destructive, allow_views,
+                                                            unsafe_autograd, compact, 0, 1, dedup_policy)
+            dev = dev or src.device
+            keep.append(src)
+            reqs.append((src.data_ptr(), nbytes, body, cb))
+        stream_h = _stream_handle(stream, dev)
+        outs = self._agent.canonical_evict_batch(reqs, stream_h, bool(destructive), int(max_inflight_bytes))
+        handles = []
+        for (tensor, key), (ok, action, oid, did_d2h, msg, hlo, hhi) in zip(items, outs):
+            if ok and action == 2 and wait_for_creator:
+                handles.append(self.canonical_evict(tensor, key, dedup=dedup, destructive=destructive, stream=stream,
+                                                    allow_views=allow_views, unsafe_autograd=unsafe_autograd,
+                                                    compact=compact, dedup_policy=dedup_policy,
+                                                    wait_for_creator=True, timeout_s=timeout_s))
+                continue
+            if not ok:
+                raise RuntimeError(f"canonical_evict failed (action={ACTION_NAMES.get(action, action)}): {msg}")
+            handles.append(CanonicalHandle(oid, action, did_d2h, key, msg, off=self,
+                                           content_hash=(hlo, hhi) if (hlo or hhi) else None))
+        del keep
+        return handles
 
     def seal_model_version(self, model_role, model_version: int, fail_if_missing: bool = True,
                            promote: bool = False, expected_param_ids: Sequence[int] = ()) -> dict:

@@ -67,18 +67,20 @@ def dedup_evict_params(off: Off, params: Dict[str, torch.Tensor], *, model_role,
     out: Dict[str, CanonicalHandle] = {}
     keys = {n: off.canonical_key(model_role=model_role, model_version=model_version, param_name=n,
                                  tensor=params[n], tp_rank=tp_rank, pp_rank=pp_rank) for n in names}
-    for i, n in enumerate(names):  # phase 1: owners create (and keep their GPU copy for peers in p2p mode)
-        if owner_of(i) == rank:
-            out[n] = off.canonical_evict(params[n], keys[n], dedup_policy=policy,
-                                         destructive=destructive and not p2p)
+    # phase 1: owners create (and keep their GPU copy for peers in p2p mode);
+    # one batch, so the round trips of later parameters overlap earlier copies
+    mine = [n for i, n in enumerate(names) if owner_of(i) == rank]
+    for n, h in zip(mine, off.canonical_evict_batch([(params[n], keys[n]) for n in mine], dedup_policy=policy,
+                                                    destructive=destructive and not p2p)):
+        out[n] = h
     if p2p:
         _verify_replicas_p2p(params, names, owner_of, rank, world, group)
     elif world > 1:
         dist.barrier(group)
-    for i, n in enumerate(names):  # phase 2: replicas verify or attach
-        if owner_of(i) != rank:
-            out[n] = off.canonical_evict(params[n], keys[n], dedup_policy=policy, destructive=destructive,
-                                         wait_for_creator=True)
+    theirs = [n for i, n in enumerate(names) if owner_of(i) != rank]  # phase 2: replicas verify or attach
+    for n, h in zip(theirs, off.canonical_evict_batch([(params[n], keys[n]) for n in theirs], dedup_policy=policy,
+                                                      destructive=destructive, wait_for_creator=True)):
+        out[n] = h
     if world > 1:
         dist.barrier(group)  # in p2p mode: no replica reads an owner's copy any more
     if p2p and destructive:

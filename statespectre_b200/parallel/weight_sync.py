@@ -486,9 +486,10 @@ class TrainerWeightSync:
         out = {}
         if self.persist:
             carry = self.last_version is not None
-            for n in (changed if carry else self.params):
-                self.off.canonical_evict(self.params[n], self._key(n, version), destructive=False, wait=False,
-                                         stream=self.stream)
+            # one batch: every round trip and copy issued before the first is awaited
+            self.off.canonical_evict_batch([(self.params[n], self._key(n, version))
+                                            for n in (changed if carry else self.params)],
+                                           destructive=False, stream=self.stream)
             if carry:
                 unchanged = [self._pids[n] if n in self._pids else self._key(n, version).param_id
                              for n in self.params if n not in changed]

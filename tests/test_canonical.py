@@ -486,3 +486,60 @@ def test_non_destructive_canonical_evict_of_a_view_in_a_flat_buffer(cdaemon):
         assert torch.equal(out, a)
         with pytest.raises(RuntimeError, match="does not own"):
             off.canonical_evict(a, off.canonical_key(model_role=ROLL, model_version=2, param_name="a", tensor=a))
+
+
+@pytest.mark.parametrize("max_inflight", [0, 5000])
+def test_canonical_evict_batch_matches_one_by_one(cdaemon, max_inflight):
+    """canonical_evict_batch records the same objects, hashes and manifest as
+    one canonical_evict per tensor; a DP replica's batch attaches; the
+    in-flight bound only changes when copies are awaited."""
+    torch.manual_seed(3)
+    tensors = {f"l{i}.w": torch.randn(40 + 7 * i, 31) for i in range(6)}
+    with session(cdaemon, 0) as a, session(cdaemon, 1) as b:
+        one = {}
+        for name, t in tensors.items():
+            k = a.canonical_key(model_role=ROLL, model_version=1, param_name=name, tensor=t)
+            one[name] = a.canonical_evict(t.clone(), k, destructive=False)
+        man1 = a.promote_rollout_version(1)
+        items = [(t.clone(), a.canonical_key(model_role=ROLL, model_version=2, param_name=n, tensor=t))
+                 for n, t in tensors.items()]
+        hs = a.canonical_evict_batch(items, destructive=False, max_inflight_bytes=max_inflight)
+        assert [h.action_name for h in hs] == ["NEED_D2H_CREATE"] * len(tensors)
+        assert all(h.did_d2h for h in hs)
+        assert [h.content_hash for h in hs] == [one[n].content_hash for n in tensors]
+        man2 = a.promote_rollout_version(2)
+        assert man2["tensor_count"] == man1["tensor_count"] == len(tensors)
+        def entries(v):
+            man = a.get_manifest(ROLL, v)
+            return sorted((e["key"]["param_fqn_debug"], e["content_hash_lo"], e["content_hash_hi"], e["nbytes"])
+                          for e in man["tensors"])
+
+        assert entries(2) == entries(1)
+        # a DP replica (another rank, same identity) attaches without copying
+        rep = [(t.clone(), b.canonical_key(model_role=ROLL, model_version=3, param_name=n, tensor=t))
+               for n, t in tensors.items()]
+        own = [(t.clone(), a.canonical_key(model_role=ROLL, model_version=3, param_name=n, tensor=t))
+               for n, t in tensors.items()]
+        a.canonical_evict_batch(own, destructive=False)
+        hb = b.canonical_evict_batch(rep, destructive=False)
+        assert all(h.action_name == "ATTACHED_EXISTING" and not h.did_d2h for h in hb)
+        # bytes come back exactly
+        for (name, t), h in zip(tensors.items(), hs):
+            out = torch.empty_like(t)
+            h.restore_into(out)
+            assert torch.equal(out, t)
+        assert a.canonical_evict_batch([]) == []
+
+
+def test_canonical_evict_batch_destructive_releases_storage(cdaemon):
+    with session(cdaemon, 0) as off:
+        ts = [torch.randn(64, 16) for _ in range(3)]
+        refs = [t.clone() for t in ts]
+        items = [(t, off.canonical_key(model_role=ROLL, model_version=1, param_name=f"p{i}", tensor=t))
+                 for i, t in enumerate(ts)]
+        hs = off.canonical_evict_batch(items)
+        assert all(t.numel() == 0 for t in ts)
+        for h, r in zip(hs, refs):
+            out = torch.empty_like(r)
+            h.restore_into(out)
+            assert torch.equal(out, r)
