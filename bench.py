@@ -122,6 +122,8 @@ def parse():
     p.add_argument("--kv-batch", type=int, default=0,
                    help="kv_cache: blocks per evict_batch/restore_batch call (0: the whole iteration in one call)")
     p.add_argument("--pinned-gb", type=int, default=0, help="kv_cache: pinned window per GPU (0 = fits the set)")
+    p.add_argument("--tier-threads", default="",
+                   help="kv_cache: offloadd drain workers, readback workers and copy threads, e.g. 4,4,8")
     p.add_argument("--kv-group-mb", type=int, default=0, help="kv_cache: bytes per reservation group (0 = 256 MiB)")
     p.add_argument("--nvme-dir", default="", help="dp_dedup: NVMe spill directory")
     p.add_argument("--dedup-mode", default="p2p_verified",

@@ -61,7 +61,8 @@ struct DaemonConfig {
     // Freed pageable buffers kept for reuse (bytes), so tensors that cycle
     // through the pageable tier copy into memory that is already faulted in.
     uint64_t pageable_pool_bytes = 4ull << 30;
-    // Threads that share one large pinned <-> pageable copy (64 MiB pieces).
+    // Pool threads that share pinned <-> pageable copies (1 MiB pieces) with
+    // the drain and readback workers.
     uint32_t copy_threads = 4;
 
     // nvme

@@ -255,6 +255,7 @@ void Daemon::run() {
     if (cfg_.v2_control_tcp_port) tcp_fd_ = tcp_listen(uint16_t(cfg_.v2_control_tcp_port));
     running_.store(true);
     workers_on_.store(true);
+    copy_pool_.start(cfg_.copy_threads);
     for (uint32_t i = 0; i < std::max<uint32_t>(1, cfg_.drain_workers); ++i)
         workers_.emplace_back([this] { drain_loop(); });
     for (uint32_t i = 0; i < std::max<uint32_t>(1, cfg_.readback_workers); ++i)
@@ -278,6 +279,7 @@ void Daemon::run() {
     for (auto& t : workers_)
         if (t.joinable()) t.join();
     workers_.clear();
+    copy_pool_.stop();
     close_fd(listen_fd_);
     close_fd(tcp_fd_);
     listen_fd_ = tcp_fd_ = -1;

@@ -343,7 +343,33 @@ class Daemon {
         std::atomic<uint64_t> pooled_{0};
     };
     PageablePool pageable_pool_;
-    void copy_bytes(char* dst, const char* src, uint64_t n) const;  // threaded for large copies
+    // Persistent memcpy threads shared by every drain and readback worker. A
+    // copy of at least two pieces (1 MiB each) is split: the calling worker
+    // copies one piece and pool threads take the rest, so a few concurrent
+    // 4 MiB KV-block copies keep drain_policy.copy_threads + workers cores
+    // busy without a thread start per copy.
+    class CopyPool {
+     public:
+        void start(uint32_t threads);
+        void stop();
+        void copy(char* dst, const char* src, uint64_t n);
+        ~CopyPool() { stop(); }
+     private:
+        struct Piece {
+            char* dst;
+            const char* src;
+            uint64_t n;
+            std::atomic<uint32_t>* left;
+        };
+        void run_piece(const Piece& p);
+        std::mutex mu_;
+        std::condition_variable cv_, done_cv_;
+        std::deque<Piece> q_;
+        std::vector<std::thread> ts_;
+        bool on_ = false;
+    };
+    mutable CopyPool copy_pool_;
+    void copy_bytes(char* dst, const char* src, uint64_t n) const;  // split over the copy pool
 
     // ---------------- read holds and durable versions (persist.cpp) ----------------
     bool begin_read(CanonicalObject& o, ReadSrc* src, std::string* why);  // mu_ held

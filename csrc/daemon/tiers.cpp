@@ -15,6 +15,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
 #include <thread>
 #include <vector>
 
@@ -73,23 +74,84 @@ Daemon::PageablePool::~PageablePool() {
     for (auto& kv : free_) ::munmap(kv.second, kv.first);
 }
 
-void Daemon::copy_bytes(char* dst, const char* src, uint64_t n) const {
-    const uint64_t piece = 64ull << 20;
-    const uint64_t parts = std::min<uint64_t>(std::max<uint32_t>(cfg_.copy_threads, 1), n / piece);
+void Daemon::CopyPool::start(uint32_t threads) {
+    std::lock_guard<std::mutex> g(mu_);
+    if (on_) return;
+    on_ = true;
+    for (uint32_t i = 0; i < threads; ++i)
+        ts_.emplace_back([this] {
+            for (;;) {
+                Piece p;
+                {
+                    std::unique_lock<std::mutex> l(mu_);
+                    cv_.wait(l, [&] { return !q_.empty() || !on_; });
+                    if (q_.empty()) return;
+                    p = q_.front();
+                    q_.pop_front();
+                }
+                run_piece(p);
+            }
+        });
+}
+
+void Daemon::CopyPool::stop() {
+    {
+        std::lock_guard<std::mutex> g(mu_);
+        on_ = false;
+    }
+    cv_.notify_all();
+    for (auto& t : ts_) t.join();
+    ts_.clear();
+}
+
+void Daemon::CopyPool::run_piece(const Piece& p) {
+    std::memcpy(p.dst, p.src, p.n);
+    if (p.left->fetch_sub(1, std::memory_order_acq_rel) == 1) {
+        std::lock_guard<std::mutex> g(mu_);  // the waiter checks `left` under mu_
+        done_cv_.notify_all();
+    }
+}
+
+void Daemon::CopyPool::copy(char* dst, const char* src, uint64_t n) {
+    constexpr uint64_t kPiece = 1ull << 20;
+    uint64_t parts = 0;
+    {
+        std::lock_guard<std::mutex> g(mu_);
+        if (on_) parts = std::min<uint64_t>(ts_.size() + 1, n / kPiece);
+    }
     if (parts <= 1) {
         std::memcpy(dst, src, n);
         return;
     }
     const uint64_t step = (n / parts + 4095) & ~uint64_t(4095);
-    std::vector<std::thread> ts;
-    for (uint64_t k = 1; k < parts; ++k) {
-        const uint64_t off = k * step;
-        if (off >= n) break;
-        ts.emplace_back([=] { std::memcpy(dst + off, src + off, std::min(step, n - off)); });
+    std::atomic<uint32_t> left{0};
+    std::vector<Piece> mine;
+    for (uint64_t off = step; off < n; off += step) mine.push_back(Piece{dst + off, src + off, std::min(step, n - off), &left});
+    left.store(uint32_t(mine.size()) + 1);
+    {
+        std::lock_guard<std::mutex> g(mu_);
+        for (const Piece& p : mine) q_.push_back(p);
     }
-    std::memcpy(dst, src, std::min(step, n));
-    for (auto& t : ts) t.join();
+    cv_.notify_all();
+    run_piece(Piece{dst, src, std::min(step, n), &left});
+    // Help with queued pieces (this copy's or another's) until ours are done.
+    for (;;) {
+        Piece p;
+        {
+            std::unique_lock<std::mutex> l(mu_);
+            if (left.load(std::memory_order_acquire) == 0) return;
+            if (q_.empty()) {
+                done_cv_.wait(l, [&] { return left.load(std::memory_order_acquire) == 0 || !q_.empty(); });
+                continue;
+            }
+            p = q_.front();
+            q_.pop_front();
+        }
+        run_piece(p);
+    }
 }
+
+void Daemon::copy_bytes(char* dst, const char* src, uint64_t n) const { copy_pool_.copy(dst, src, n); }
 
 void Daemon::cold_quota(uint64_t tid, uint64_t nbytes, bool* allow_pageable, bool* allow_nvme) {
     *allow_pageable = *allow_nvme = true;

@@ -172,6 +172,7 @@ DaemonConfig config_from(py::dict kw) {
     }
     if (kw.contains("quota_max_pinned_bytes")) c.v2_quota_max_pinned_bytes = kw["quota_max_pinned_bytes"].cast<uint64_t>();
     if (kw.contains("creating_policy")) c.v2_creating_policy = kw["creating_policy"].cast<uint32_t>();
+    if (kw.contains("copy_threads")) c.copy_threads = kw["copy_threads"].cast<uint32_t>();
     validate(c);
     return c;
 }

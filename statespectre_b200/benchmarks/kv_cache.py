@@ -38,7 +38,8 @@ def run(args, metric: str) -> dict:
     per_iter = max(1, int(round(args.evict_fraction * nblocks)))
     batch = args.kv_batch if args.kv_batch > 0 else per_iter
     pinned_gb = args.pinned_gb or int(per_iter * spec.block_bytes * 1.2 / GiB) + 2
-    sock, daemon = node_daemon(env, pinned_gb, "/tmp/ofld_kv", slot_mb=4)
+    sock, daemon = node_daemon(env, pinned_gb, "/tmp/ofld_kv", slot_mb=4,
+                               tier_threads=getattr(args, "tier_threads", ""))
     sess = offload_context(daemon_addr=sock, device=env.device, rank=env.rank, local_rank=env.local_rank,
                            world_rank=env.rank, eager_register=True, stream_priority=-1,
                            kernel_timing=bool(getattr(args, "kernel_timing", 0)),

@@ -113,7 +113,7 @@ def in_process_daemon(**kw):
     Keywords: socket, arena_mb, slot_mb, numa, gpu, yaml, drain_on_complete,
     heartbeat_timeout_ms, tcp_port, nvme_dir, direct_io, drain_target,
     pageable_limit_mb, io_engine, retain_sealed_versions, thresholds,
-    quota_max_pinned_bytes, creating_policy.
+    quota_max_pinned_bytes, creating_policy, copy_threads.
     """
     if "socket" not in kw:
         kw["socket"] = os.path.join(tempfile.mkdtemp(prefix="offloadd-"), "offloadd.sock")

@@ -32,11 +32,13 @@ def gpu_numa_nodes(num_gpus: int) -> List[int]:
 
 def daemon_yaml(socket_path: str, gpu_nodes: List[int], window_gb_per_gpu, slot_mb: int = 64,
                 overflow_gb: int = 1, drain_on_complete: bool = False, extra: str = "",
-                drain_target: str = "pageable", nvme_dir: str = "") -> str:
+                drain_target: str = "pageable", nvme_dir: str = "", tier_threads: str = "") -> str:
     """A daemon config with one arena per NUMA node holding a window per GPU.
 
     ``window_gb_per_gpu`` is one size for every GPU or a list (one per GPU;
-    GPUs with 0 get no window and allocate from the overflow pool)."""
+    GPUs with 0 get no window and allocate from the overflow pool).
+    ``tier_threads`` "drain,readback,copy" sets drain_policy's drain and
+    readback worker counts and its copy-pool size (empty: the defaults)."""
     sizes = list(window_gb_per_gpu) if isinstance(window_gb_per_gpu, (list, tuple)) else \
         [window_gb_per_gpu] * len(gpu_nodes)
     sizes += [0] * (len(gpu_nodes) - len(sizes))
@@ -53,7 +55,11 @@ def daemon_yaml(socket_path: str, gpu_nodes: List[int], window_gb_per_gpu, slot_
         for g in gpus:
             lines += [f"        - gpu: {g}", f"          size_gb: {sizes[g]}"]
     lines += ["drain_policy:", f"  target_tier: {drain_target}",
-              f"  drain_on_d2h_complete: {str(drain_on_complete).lower()}", "nvme:"]
+              f"  drain_on_d2h_complete: {str(drain_on_complete).lower()}"]
+    if tier_threads:
+        dw, rw, ct = (int(x) for x in tier_threads.split(","))
+        lines += [f"  drain_workers: {dw}", f"  readback_workers: {rw}", f"  copy_threads: {ct}"]
+    lines += ["nvme:"]
     if nvme_dir:
         lines += ["  enabled: true", f"  path: {nvme_dir}", "  io_engine: io_uring", "  direct_io: true"]
     else:

@@ -243,3 +243,24 @@ def test_batched_restores_under_pressure_from_several_ranks_make_progress():
     r = run_kv(1.5, ranks=2, nblocks=16)
     assert r["errors"] == [] and r["byte_exact"]
     assert r["items_per_s"] > 0 and r["drains"] > 0 and r["readbacks"] > 0
+
+
+@pytest.mark.parametrize("copy_threads", [0, 8])
+def test_tier_copies_split_over_the_copy_pool_are_exact(sock_path, copy_threads):
+    """Drains and readbacks of sizes that split into uneven 1 MiB pieces (and
+    a size below two pieces) come back byte-exact with and without pool
+    threads."""
+    d = in_process_daemon(socket=sock_path, arena_mb=64, drain_on_complete=True, copy_threads=copy_threads)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cpu") as off:
+            g = torch.Generator().manual_seed(copy_threads)
+            xs = [torch.randint(0, 255, (n,), dtype=torch.uint8, generator=g)
+                  for n in (3 * MB + 4097, 1 * MB + 17, 9 * MB + 123, 2 * MB)]
+            hs = [off.copy(x, wait=True) for x in xs]
+            for h in hs:
+                assert wait_for(lambda: h.location() == "pageable"), h.location()
+            for h, x in zip(hs, xs):
+                assert torch.equal(h.restore(), x)
+                h.discard()
+    finally:
+        d.stop()
