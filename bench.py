@@ -177,6 +177,8 @@ def main():
     if world > 1:
         import datetime
 
+        # the weight-sync block's trainer/rollout pairs exchange hashes with plain send/recv
+        os.environ.setdefault("TORCH_NCCL_SHOW_EAGER_INIT_P2P_SERIALIZATION_WARNING", "false")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
 
     def barrier():
