@@ -84,6 +84,8 @@ def parse():
     p.add_argument("--evict-ctas", type=int, default=0)
     p.add_argument("--restore-ctas", type=int, default=0)
     p.add_argument("--hash", type=int, default=1)
+    p.add_argument("--host-hash-kb", type=int, default=-1,
+                   help="uncoded evicts up to this size hash their pinned copy on the host (-1: the agent's default)")
     p.add_argument("--compress", type=int, default=1, help="zbf16 lossless coding of the bf16 payload over PCIe")
     p.add_argument("--e2e-steps", type=int, default=0, help="default: same as --steps")
     p.add_argument("--kernel-timing", type=int, default=0,

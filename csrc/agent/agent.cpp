@@ -316,6 +316,7 @@ struct Agent::Impl {
         PinnedPool::Buf err;             // bulk forms: device status word (0 = the copy completed)
         bool z = false;
         bool f32 = false;                // with z: the run is zf32-coded fp32 (else zbf16)
+        const char* host_hash_src = nullptr;  // digests still to compute on the host from this pinned copy
         // Batched launches: every item of the batch shares one event and the
         // job table; the last item to finish releases both.
         std::shared_ptr<void> batch_keep;
@@ -655,6 +656,7 @@ struct Agent::Impl {
         if (p.d2h) {
             uint64_t lo = 0, hi = 0;
             std::vector<uint64_t> dig;
+            host_digests(p);
             if (p.dig.host) {
                 const uint64_t* d = static_cast<const uint64_t*>(p.dig.host);
                 ssh::Object o = ssh::fold_digests(d, p.ndig, p.nbytes);
@@ -848,6 +850,14 @@ struct Agent::Impl {
     bool run_is_z(uint32_t slot) const { return (run_format(slot) & OFLD_FLAG_FORMAT_ZBF16) != 0; }
     bool run_is_zf32(uint32_t slot) const { return (run_format(slot) & OFLD_FLAG_FORMAT_ZF32) != 0; }
 
+    // Digests of a small evict hashed on the host (host_hash_max_bytes), from
+    // its pinned copy, once that copy has completed.
+    static void host_digests(Pending& p) {
+        if (!p.host_hash_src || !p.dig.host) return;
+        ssh::host_chunk_digests(p.host_hash_src, p.nbytes, static_cast<uint64_t*>(p.dig.host));
+        p.host_hash_src = nullptr;
+    }
+
     void launch_d2h(Pending& p, uint64_t src, char* dst_host, char* dst_dev, cudaStream_t s, bool hash) {
         if (!gpu) {
             std::memcpy(dst_host, reinterpret_cast<const void*>(src), p.nbytes);
@@ -897,7 +907,11 @@ struct Agent::Impl {
             CUDA_OK(kern::evict_z(reinterpret_cast<const void*>(src), dst_dev, p.nbytes,
                                   static_cast<const uint8_t*>(p.zb.dev), dig_dev, s, opt.evict_ctas));
         } else if (opt.engine == "copy_engine" || opt.uncoded == "copy_engine") {
-            if (hash) {
+            if (hash && p.nbytes <= opt.host_hash_max_bytes) {
+                CUDA_OK(cudaMemcpyAsync(dst_host, reinterpret_cast<const void*>(src), p.nbytes, cudaMemcpyDeviceToHost,
+                                        s));
+                p.host_hash_src = dst_host;  // digests once the copy is done (host_digests)
+            } else if (hash) {
                 // the digests read HBM on a side stream while the copy engine
                 // crosses PCIe; the caller's stream waits for both
                 cudaEvent_t fork = nullptr, join = nullptr;
@@ -1803,6 +1817,7 @@ void Agent::canonical_end(CanonPending& c) {
     if (p.ev) CUDA_OK(cudaEventSynchronize(p.ev));
     if (p.ev) cudaEventDestroy(p.ev);
     p.ev = nullptr;
+    Impl::host_digests(p);
     ssh::Object h{0, 0};
     if (p.dig.host) {
         h = ssh::fold_digests(static_cast<const uint64_t*>(p.dig.host), p.ndig, c.nbytes);

@@ -69,6 +69,11 @@ struct AgentOptions {
     int stage_depth = 0;
     int stage_piece_chunks = 0;
     bool hash_on_evict = true;
+    // Uncoded copy-engine evicts of at most this many bytes hash their pinned
+    // copy on the host once the copy is done, instead of launching the digest
+    // kernel on a side stream: beside a training step a tiny kernel waits for
+    // SM room longer than the host takes to hash a few KB. 0 = always on the GPU.
+    uint64_t host_hash_max_bytes = 16384;
     bool use_ring = true;
     bool fast_submit = true;     // reserve+submit and ready+submit in one round trip
     bool keep_digests = true;    // remember chunk digests for verify-on-restore

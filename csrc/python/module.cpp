@@ -230,6 +230,7 @@ class PyAgent {
             else if (k == "stage_depth") o.stage_depth = v.cast<int>();
             else if (k == "stage_piece_chunks") o.stage_piece_chunks = v.cast<int>();
             else if (k == "hash_on_evict") o.hash_on_evict = v.cast<bool>();
+            else if (k == "host_hash_max_bytes") o.host_hash_max_bytes = v.cast<uint64_t>();
             else if (k == "use_ring") o.use_ring = v.cast<bool>();
             else if (k == "fast_submit") o.fast_submit = v.cast<bool>();
             else if (k == "keep_digests") o.keep_digests = v.cast<bool>();

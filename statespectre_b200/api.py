@@ -965,6 +965,7 @@ _AGENT_OPTION_KEYS = {
     "kernels.batch_group_mb": ("batch_group_bytes", lambda v: int(float(v) * (1 << 20))),
     "kernels.timing": ("kernel_timing", _as_bool),
     "kernels.stream_priority": ("stream_priority", int),
+    "kernels.host_hash_max_kb": ("host_hash_max_bytes", lambda v: int(float(v) * 1024)),
 }
 
 

@@ -44,7 +44,9 @@ def run(args, metric: str) -> dict:
                            hash_on_evict=bool(getattr(args, "hash", 1)),
                            stream_priority=-1, stage_ctas=int(getattr(args, "stage_ctas", 0) or 0),
                            stage_depth=int(getattr(args, "stage_depth", 0) or 0),
-                           stage_piece_chunks=int(getattr(args, "stage_piece_chunks", 0) or 0))
+                           stage_piece_chunks=int(getattr(args, "stage_piece_chunks", 0) or 0),
+                           **({"host_hash_max_bytes": int(args.host_hash_kb) << 10}
+                              if getattr(args, "host_hash_kb", -1) >= 0 else {}))
     off = sess.off
     stream = torch.cuda.Stream(device=env.device, priority=-1)
     load = GemmLoad(env.device).start() if args.matmul else None

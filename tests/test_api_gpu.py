@@ -178,3 +178,29 @@ def test_unknown_uncoded_form_is_rejected(sock_path):
             offload_context(daemon_addr=sock_path, device="cuda:0", uncoded="dma")
     finally:
         d.stop()
+
+
+@pytest.mark.parametrize("host_hash_max", [0, 16384])
+def test_small_evicts_hash_on_host_or_device_alike(sock_path, host_hash_max):
+    """Small uncoded evicts hash their pinned copy on the host (up to
+    host_hash_max_bytes) or on the device beside the copy; both give the host
+    oracle's content hash, verify on restore, and the same bytes back."""
+    d = in_process_daemon(socket=sock_path, arena_mb=256, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", host_hash_max_bytes=host_hash_max) as off:
+            for n in (1, 4096, 4097, 16384, 16400, 65536 + 48):
+                x = torch.randint(0, 255, (n,), dtype=torch.uint8, device="cuda")
+                ref = x.clone()
+                h = off.copy(x, wait=True)
+                assert h.content_hash == native().ssh_hash(ref.cpu().numpy()), n
+                z = torch.empty_like(ref)
+                h.restore_into(z, verify=True)
+                assert torch.equal(z, ref), n
+                h.discard()
+            # canonical objects take the same path
+            w = torch.randn(2048, dtype=torch.bfloat16, device="cuda")
+            k = off.canonical_key(model_role=ModelRole.POLICY_ROLLOUT, model_version=1, param_name="w", tensor=w)
+            c = off.canonical_evict(w, k, destructive=False)
+            assert c.content_hash == native().ssh_hash(w.cpu().view(torch.uint8).numpy())
+    finally:
+        d.stop()
