@@ -187,7 +187,8 @@ def test_small_evicts_hash_on_host_or_device_alike(sock_path, host_hash_max):
     oracle's content hash, verify on restore, and the same bytes back."""
     d = in_process_daemon(socket=sock_path, arena_mb=256, drain_on_complete=False)
     try:
-        with offload_context(daemon_addr=sock_path, device="cuda:0", host_hash_max_bytes=host_hash_max) as off:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", job_name="small-hash",
+                             host_hash_max_bytes=host_hash_max) as off:
             for n in (1, 4096, 4097, 16384, 16400, 65536 + 48):
                 x = torch.randint(0, 255, (n,), dtype=torch.uint8, device="cuda")
                 ref = x.clone()
