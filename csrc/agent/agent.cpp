@@ -336,6 +336,7 @@ struct Agent::Impl {
     std::map<TvKey, TensorRec> tensors;
 
     std::atomic<uint64_t> inflight_d2h{0}, inflight_h2d{0}, evicts{0}, restores{0}, d2h_done{0}, h2d_done{0};
+    std::atomic<uint64_t> coded_canonical{0};  // canonical objects that crossed PCIe zbf16-coded
     std::atomic<uint64_t> xfer_errors{0};  // copies a kernel reported incomplete
     std::atomic<uint64_t> d2h_bytes{0}, h2d_bytes{0}, registered_bytes{0}, d2h_ns{0}, h2d_ns{0}, reg_ns{0};
     std::atomic<bool> stop{false}, hb_paused{false};
@@ -848,6 +849,20 @@ struct Agent::Impl {
                    : 0;
     }
     bool run_is_z(uint32_t slot) const { return (run_format(slot) & OFLD_FLAG_FORMAT_ZBF16) != 0; }
+    // First slot of the run that starts at (arena, offset): the slot table's
+    // placement never changes, so the index is built once (canonical restores
+    // learn a run by its arena position only).
+    std::mutex slot_index_mu;
+    std::unordered_map<uint64_t, uint32_t> slot_index;  // (arena << 48) | offset -> slot
+    int64_t slot_at(uint64_t arena_id, uint64_t offset) {
+        if (!slots) return -1;
+        std::lock_guard<std::mutex> g(slot_index_mu);
+        if (slot_index.empty())
+            for (uint32_t i = 0; i < num_slots; ++i)
+                slot_index[(uint64_t(slots[i].arena_id) << 48) | slots[i].arena_offset] = i;
+        auto it = slot_index.find((arena_id << 48) | offset);
+        return it == slot_index.end() ? -1 : int64_t(it->second);
+    }
     bool run_is_zf32(uint32_t slot) const { return (run_format(slot) & OFLD_FLAG_FORMAT_ZF32) != 0; }
 
     // Digests of a small evict hashed on the host (host_hash_max_bytes), from
@@ -1723,26 +1738,35 @@ void Agent::synchronize() {
 // ---------------------------------------------------------------------------
 RegisterJobResponse Agent::register_job(const RegisterJobRequest& r) { return d_->call<Op::kRegisterJob>(r); }
 
-// A canonical evict in two halves. begin: the attach-or-create round trip
-// and, for a create or a candidate, the submitted mark and the copy's launch
-// (copy engine or K1, hash in the same pass). end: wait for that copy, fold
-// the digests, mark the copy complete and commit the object. canonical_evict
-// runs both; canonical_evict_batch begins every item before it ends the
-// first, so each item's round trips overlap the copies launched before it.
+// A canonical evict in phases. request: the attach-or-create round trip
+// (attach, wait and verify-only answers finish there). scan: for a create of
+// a bf16 object, the zbf16 pre-pass decides whether the bytes cross PCIe
+// coded. launch: the run's coding (SetRunFormat), the submitted mark and the
+// copy (copy engine or K1, chunk digests of the raw bytes from the same
+// pass). end: wait for the copy, fold the digests, mark it complete and
+// commit. canonical_evict runs the phases in turn; canonical_evict_batch
+// requests every item, scans every candidate with one stream wait, then
+// launches and ends them, so each item's round trips overlap earlier copies.
 struct Agent::CanonPending {
     CanonicalOutcome out;
-    bool copying = false;
+    bool create = false;    // the daemon asked this rank to copy the object
+    bool copying = false;   // launched, not yet ended
+    bool zcand = false;     // a bf16 object that may cross PCIe coded
+    bool z = false;         // the pre-pass found every chunk codable
     bool trusted = false;
-    uint64_t nbytes = 0;
+    uint64_t ptr = 0, nbytes = 0;
+    cudaStream_t s = nullptr;
+    char *host = nullptr, *dev = nullptr;
     TransferMark mark{};
     RequestCanonicalEvictResponse resp;
     DoneCallback cb;
     bool destructive = false;
+    PinnedPool::Buf zb;
     std::unique_ptr<Impl::Pending> p;
 };
 
-void Agent::canonical_begin(CanonPending& c, uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
-                            const RequestCanonicalEvictRequest& in, DoneCallback on_invalidate) {
+void Agent::canonical_request(CanonPending& c, uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
+                              const RequestCanonicalEvictRequest& in, DoneCallback on_invalidate) {
     Impl& D = *d_;
     RequestCanonicalEvictRequest req = in;
     req.rank_id = D.opt.rank_id;
@@ -1752,6 +1776,7 @@ void Agent::canonical_begin(CanonPending& c, uint64_t ptr, uint64_t nbytes, Stre
     req.destructive = destructive;
     req.key.nbytes = nbytes;
     if (req.key.shard_nbytes == 0) req.key.shard_nbytes = nbytes;
+    c.ptr = ptr;
     c.nbytes = nbytes;
     c.destructive = destructive;
     c.cb = std::move(on_invalidate);
@@ -1763,14 +1788,14 @@ void Agent::canonical_begin(CanonPending& c, uint64_t ptr, uint64_t nbytes, Stre
     out.object_id = resp.object_id;
     out.message = resp.message;
     if (!resp.ok) return;
-    cudaStream_t s = D.stream_of(stream);
+    c.s = D.stream_of(stream);
 
     const bool attached = resp.action == offload_v2::ATTACH_ACTION_ATTACHED_EXISTING ||
                           resp.action == 7 /* attached after a peer byte compare */;
     if (attached || resp.action == offload_v2::ATTACH_ACTION_WAIT_FOR_CREATOR) {
         out.ok = true;
         if (attached && destructive && c.cb) {
-            if (D.gpu) CUDA_OK(cudaStreamSynchronize(s));  // producer kernels done before the storage goes
+            if (D.gpu) CUDA_OK(cudaStreamSynchronize(c.s));  // producer kernels done before the storage goes
             c.cb();
         }
         return;
@@ -1794,17 +1819,36 @@ void Agent::canonical_begin(CanonPending& c, uint64_t ptr, uint64_t nbytes, Stre
     if (resp.action != offload_v2::ATTACH_ACTION_NEED_D2H_CREATE &&
         resp.action != offload_v2::ATTACH_ACTION_DUPLICATE_CANDIDATE)
         return;
+    c.create = true;
+    D.resolve(resp.arena_id, resp.arena_offset, nbytes, &c.host, &c.dev);
+    c.zcand = D.opt.compress_canonical && req.key.dtype == kScalarBf16 && D.want_z(ptr, nbytes, kFmtBf16) &&
+              (reinterpret_cast<uintptr_t>(c.host) & 15) == 0;
+}
 
-    // Create or candidate: copy into the reserved run with the fused hash.
-    char *host = nullptr, *dev = nullptr;
-    D.resolve(resp.arena_id, resp.arena_offset, nbytes, &host, &dev);
+void Agent::canonical_launch(CanonPending& c) {
+    Impl& D = *d_;
+    if (!c.create) return;
+    const RequestCanonicalEvictResponse& resp = c.resp;
     c.mark = TransferMark{D.opt.rank_id, D.epoch, resp.lease_id, resp.synthetic_tid, 1, resp.slot_id, 0, real_ns()};
+    if (c.z) {
+        SetRunFormatRequest f{D.opt.rank_id, D.epoch, resp.lease_id, resp.slot_id, OFLD_FLAG_FORMAT_ZBF16};
+        StatusResponse fr = D.call<Op::kSetRunFormat>(f);
+        if (!fr.ok) {  // a daemon that cannot record the coding gets the raw bytes
+            LOG_WARN(TAG, "SetRunFormat: %s (object moves uncoded)", fr.message.c_str());
+            D.pool.put(c.zb);
+            c.zb = PinnedPool::Buf{};
+            c.z = false;
+        }
+    }
     StatusResponse sr = D.call<Op::kMarkD2HSubmitted>(c.mark);
     if (!sr.ok) LOG_WARN(TAG, "canonical MarkD2HSubmitted: %s", sr.message.c_str());
     ++D.evicts;
     c.p.reset(new Impl::Pending());
-    c.p->nbytes = nbytes;
-    D.launch_d2h(*c.p, ptr, host, dev, s, true);
+    c.p->nbytes = c.nbytes;
+    c.p->z = c.z;
+    c.p->zb = c.zb;
+    c.zb = PinnedPool::Buf{};
+    D.launch_d2h(*c.p, c.ptr, c.host, c.dev, c.s, true);
     c.copying = true;
 }
 
@@ -1827,8 +1871,11 @@ void Agent::canonical_end(CanonPending& c) {
             std::free(p.dig.host);
         p.dig = {};
     }
+    D.pool.put(p.zb);
+    p.zb = PinnedPool::Buf{};
     D.d2h_bytes += c.nbytes;
     ++D.d2h_done;
+    if (c.z) ++D.coded_canonical;
     MarkD2HCompleteResponse dr = D.call<Op::kMarkD2HComplete>(c.mark);
     if (!dr.ok) {
         out.message = "canonical MarkD2HComplete rejected";
@@ -1853,39 +1900,63 @@ void Agent::canonical_end(CanonPending& c) {
     if (cr.ok && c.destructive && c.cb) c.cb();
 }
 
+// The pre-pass of every coding candidate among `cs`: all launched on their
+// streams, then one wait per distinct stream (a stream's wait also covers the
+// producers of its objects, as the copies that follow must).
+void Agent::canonical_scan(std::vector<CanonPending*>& cs) {
+    Impl& D = *d_;
+    std::vector<cudaStream_t> streams;
+    for (CanonPending* c : cs) {
+        if (!c->zcand) continue;
+        D.zscan_launch(c->ptr, c->nbytes, c->s, &c->zb);
+        if (std::find(streams.begin(), streams.end(), c->s) == streams.end()) streams.push_back(c->s);
+    }
+    for (cudaStream_t s : streams) D.stream_wait(s);
+    for (CanonPending* c : cs)
+        if (c->zcand) c->z = D.zscan_result(c->nbytes, &c->zb);
+}
+
 CanonicalOutcome Agent::canonical_evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
                                         const RequestCanonicalEvictRequest& in, DoneCallback on_invalidate, bool) {
     NvtxRange nvtx_("ofld.canonical_evict");
     CanonPending c;
-    canonical_begin(c, ptr, nbytes, stream, destructive, in, std::move(on_invalidate));
+    canonical_request(c, ptr, nbytes, stream, destructive, in, std::move(on_invalidate));
+    std::vector<CanonPending*> one{&c};
+    canonical_scan(one);
+    canonical_launch(c);
     canonical_end(c);
     return c.out;
 }
 
 // Many canonical evicts on one stream: every item's attach-or-create round
-// trip and copy launch first, then the completions in order. The copies run
-// back to back on the stream while the later items' round trips and the
-// earlier items' commits proceed on the host. At most `max_inflight_bytes`
-// of copies are outstanding (0: no limit); beyond it the oldest item is
-// finished before the next begins.
+// trip, then one pre-pass wait for the coding candidates, then the copies
+// back to back while the host marks and commits the earlier items. At most
+// `max_inflight_bytes` of copies are outstanding (0: no limit); beyond it the
+// oldest item is ended before the next is launched.
 std::vector<CanonicalOutcome> Agent::canonical_evict_batch(const std::vector<CanonicalItem>& items,
                                                            StreamHandle stream, bool destructive,
                                                            uint64_t max_inflight_bytes) {
     NvtxRange nvtx_("ofld.canonical_evict_batch");
     std::vector<CanonPending> cs(items.size());
+    for (size_t i = 0; i < items.size(); ++i)
+        canonical_request(cs[i], items[i].ptr, items[i].nbytes, stream, destructive, items[i].req,
+                          items[i].on_invalidate);
+    std::vector<CanonPending*> all;
+    for (CanonPending& c : cs) all.push_back(&c);
+    canonical_scan(all);
     size_t done = 0;
     uint64_t inflight = 0;
-    for (size_t i = 0; i < items.size(); ++i) {
-        while (max_inflight_bytes && inflight > 0 && inflight + items[i].nbytes > max_inflight_bytes && done < i) {
+    for (size_t i = 0; i < cs.size(); ++i) {
+        while (max_inflight_bytes && inflight > 0 && inflight + cs[i].nbytes > max_inflight_bytes && done < i) {
             if (cs[done].copying) inflight -= cs[done].nbytes;
             canonical_end(cs[done++]);
         }
-        canonical_begin(cs[i], items[i].ptr, items[i].nbytes, stream, destructive, items[i].req, items[i].on_invalidate);
+        canonical_launch(cs[i]);
         if (cs[i].copying) inflight += cs[i].nbytes;
     }
-    for (; done < items.size(); ++done) canonical_end(cs[done]);
+    for (; done < cs.size(); ++done) canonical_end(cs[done]);
     std::vector<CanonicalOutcome> out;
-    out.reserve(items.size());
+    out.reserve(cs.size());
     for (CanonPending& c : cs) out.push_back(std::move(c.out));
     return out;
 }
@@ -1927,8 +1998,20 @@ RestoreOutcome Agent::canonical_restore(uint64_t object_id, uint64_t ptr, uint64
         D.resolve(rr.arena_id, rr.arena_offset, rr.nbytes, &host, &dev);
         ++D.restores;
         uint64_t n = ro.cast == 0 ? nbytes : rr.nbytes;
+        const int64_t slot = D.gpu ? D.slot_at(rr.arena_id, rr.arena_offset) : -1;
+        const bool coded = slot >= 0 && D.run_is_z(uint32_t(slot));
         if (!D.gpu) {
             std::memcpy(reinterpret_cast<void*>(ptr), host, n);
+        } else if (coded) {
+            // zbf16 run: K2 decodes from host memory. A prefix of the object
+            // decodes on its own only at a chunk boundary.
+            if (n != rr.nbytes && n % zbf16::kChunk)
+                throw std::runtime_error("partial restore of a coded object must be a multiple of 64 KiB");
+            if ((ptr & 15) || !zbf16::eligible(n)) throw std::runtime_error("coded object: destination not 16-byte aligned");
+            cudaStream_t s = D.stream_of(stream);
+            CUDA_OK(kern::restore_z(dev, reinterpret_cast<void*>(ptr), n, kern::Cast(ro.cast),
+                                    reinterpret_cast<float*>(ro.scales_ptr), nullptr, nullptr, s, D.opt.restore_ctas));
+            CUDA_OK(cudaStreamSynchronize(s));
         } else {
             cudaStream_t s = D.stream_of(stream);
             CUDA_OK(kern::restore_cast(dev, reinterpret_cast<void*>(ptr), n, kern::Cast(ro.cast),
@@ -2044,6 +2127,7 @@ AgentStats Agent::stats() const {
     s.d2h_ns = D.d2h_ns;
     s.h2d_ns = D.h2d_ns;
     s.registration_ns = D.reg_ns;
+    s.coded_canonical = D.coded_canonical;
     return s;
 }
 

@@ -83,6 +83,10 @@ struct AgentOptions {
     // and host memory. Applies to evict() calls that pass fmt_hint = kFmtBf16,
     // on objects of at least compress_min_bytes, in kernel-engine mode.
     bool compress = true;
+    // The same coding for canonical objects of bf16 tensors (sealed versions,
+    // DP dedup owners): offloadd records the run's coding and decodes it when
+    // it exports the object, so TCP / FILE receivers get the raw bytes.
+    bool compress_canonical = true;
     uint64_t compress_min_bytes = 4ull << 20;
     // evict_batch/restore_batch reserve and launch in groups of about this
     // many bytes: one daemon round trip and one kernel launch per group, the
@@ -106,6 +110,8 @@ struct AgentOptions {
 constexpr uint32_t kFmtUnknown = 0;
 constexpr uint32_t kFmtBf16 = 1;
 constexpr uint32_t kFmtF32 = 2;  // fp32 payload: zf32 coding when it pays
+// torch's ScalarType code of bfloat16, as canonical keys carry it
+constexpr uint32_t kScalarBf16 = 15;
 
 struct EvictTicket {
     bool ok = false;
@@ -154,6 +160,7 @@ struct AgentStats {
     uint64_t d2h_bytes = 0, h2d_bytes = 0, kernel_launches = 0, rpc_count = 0;
     uint64_t d2h_ns = 0, h2d_ns = 0;  // summed device time of completed copies (wait paths)
     uint64_t registration_ns = 0;     // host time spent registering arenas with CUDA
+    uint64_t coded_canonical = 0;     // canonical objects that crossed PCIe zbf16-coded
 };
 
 struct BatchItem {
@@ -239,8 +246,10 @@ class Agent {
 
  private:
     struct CanonPending;
-    void canonical_begin(CanonPending& c, uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
-                         const RequestCanonicalEvictRequest& req, DoneCallback on_invalidate);
+    void canonical_request(CanonPending& c, uint64_t ptr, uint64_t nbytes, StreamHandle stream, bool destructive,
+                           const RequestCanonicalEvictRequest& req, DoneCallback on_invalidate);
+    void canonical_scan(std::vector<CanonPending*>& cs);
+    void canonical_launch(CanonPending& c);
     void canonical_end(CanonPending& c);
     std::unique_ptr<Impl> d_;
 };

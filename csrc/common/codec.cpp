@@ -43,6 +43,7 @@ const char* op_name(Op op) {
         case Op::kCarryForward: return "CarryForward";
         case Op::kGetAgentOptions: return "GetAgentOptions";
         case Op::kBatchDiscardTensor: return "BatchDiscardTensor";
+        case Op::kSetRunFormat: return "SetRunFormat";
     }
     return "Unknown";
 }
@@ -93,6 +94,7 @@ std::vector<uint8_t> reencode_body(Op op, bool response, const std::vector<uint8
         CASE(kCarryForward)
         CASE(kGetAgentOptions)
         CASE(kBatchDiscardTensor)
+        CASE(kSetRunFormat)
 #undef CASE
         default: break;
     }

@@ -423,6 +423,7 @@ void Daemon::dispatch(int fd, Op op, const std::vector<uint8_t>& b, std::vector<
         ROUTE(kCarryForward, on_carry_forward(req))
         ROUTE(kGetAgentOptions, on_get_agent_options(req))
         ROUTE(kBatchDiscardTensor, on_batch_discard(req))
+        ROUTE(kSetRunFormat, on_set_run_format(req))
         default:
             LOG_WARN(TAG, "unknown opcode %u", unsigned(op));
             throw std::runtime_error("unknown opcode");

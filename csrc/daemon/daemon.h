@@ -23,6 +23,7 @@
 #include <condition_variable>
 #include <cstdint>
 #include <deque>
+#include <functional>
 #include <list>
 #include <map>
 #include <memory>
@@ -211,6 +212,7 @@ class Daemon {
         ColdEntry cold;
         uint64_t cold_ref = 0, nbytes = 0;
         ofld_location_kind_t kind = OFLD_LOC_NONE;
+        uint64_t fmt = 0;  // OFLD_FLAG_FORMAT_* of the stored bytes (exports decode them)
     };
     struct PeerBuffer {
         PeerBufferDesc desc;
@@ -278,6 +280,7 @@ class Daemon {
     GetAgentOptionsResponse on_get_agent_options(const GetAgentOptionsRequest& r);
     StatusResponse on_discard_tensor(const DiscardTensorRequest& r);
     BatchDiscardTensorResponse on_batch_discard(const BatchDiscardTensorRequest& r);
+    StatusResponse on_set_run_format(const SetRunFormatRequest& r);
     StatusResponse do_discard(uint32_t rank, uint64_t tid, uint64_t ver);  // mu_ held, epoch checked
 
     // canonical.cpp
@@ -353,12 +356,18 @@ class Daemon {
         void start(uint32_t threads);
         void stop();
         void copy(char* dst, const char* src, uint64_t n);
+        // fn(0) .. fn(tasks - 1) over the pool threads and the caller; returns
+        // when all have run (coded-object decoding on export uses it too).
+        void run(uint32_t tasks, const std::function<void(uint32_t)>& fn);
+        uint32_t threads() {
+            std::lock_guard<std::mutex> g(mu_);
+            return on_ ? uint32_t(ts_.size()) : 0;
+        }
         ~CopyPool() { stop(); }
      private:
         struct Piece {
-            char* dst;
-            const char* src;
-            uint64_t n;
+            const std::function<void(uint32_t)>* fn;
+            uint32_t index;
             std::atomic<uint32_t>* left;
         };
         void run_piece(const Piece& p);
@@ -374,7 +383,10 @@ class Daemon {
     // ---------------- read holds and durable versions (persist.cpp) ----------------
     bool begin_read(CanonicalObject& o, ReadSrc* src, std::string* why);  // mu_ held
     void end_read(uint64_t oid, const ReadSrc& src);                      // mu_ held
-    bool copy_out(const ReadSrc& src, char* dst, uint64_t off, uint64_t n);  // no lock
+    bool copy_out(const ReadSrc& src, char* dst, uint64_t off, uint64_t n);  // no lock; stored bytes
+    // Raw bytes [off, off + n) of a coded object from its stored bytes at the
+    // same offsets, decoded in 1 MiB tasks over the copy pool (no lock).
+    bool decode_out(const ReadSrc& src, const char* stored, uint64_t off, uint64_t n, char* out);
     // Sealed versions are written under manifest.persist_dir by a worker and
     // reloaded when a daemon starts on the same directory.
     static constexpr uint32_t kPersistHolder = 0xFFFFFFFEu;  // holder id that keeps persisted objects

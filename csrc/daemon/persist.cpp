@@ -28,6 +28,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <map>
 #include <cerrno>
 #include <cstdio>
 #include <cstring>
@@ -35,6 +36,7 @@
 #include "daemon.h"
 #include "ofld/log.h"
 #include "ofld/metrics.h"
+#include "ofld/zbf16.h"
 
 namespace ofld {
 
@@ -162,6 +164,7 @@ bool Daemon::begin_read(CanonicalObject& o, ReadSrc* src, std::string* why) {
     *src = ReadSrc{};
     src->kind = lit->second.kind;
     src->nbytes = o.nbytes;
+    src->fmt = lit->second.fmt;
     if (src->kind == OFLD_LOC_PINNED) {
         uint32_t st = state_of(lit->second.slot);
         if (st != OFLD_SLOT_PINNED_VALID && st != OFLD_SLOT_DRAIN_IN_FLIGHT) {
@@ -195,6 +198,21 @@ void Daemon::end_read(uint64_t oid, const ReadSrc& src) {
         if (o->export_refs == 0) o->state = o->state_before_export;
         maybe_free_object(*o);
     }
+}
+
+bool Daemon::decode_out(const ReadSrc& src, const char* stored, uint64_t off, uint64_t n, char* out) {
+    const zbf16::Coding c = (src.fmt & OFLD_FLAG_FORMAT_ZF32) ? zbf16::Coding::kZf32 : zbf16::Coding::kZbf16;
+    constexpr uint64_t kTask = 1ull << 20;  // a multiple of both block sizes
+    const uint32_t tasks = uint32_t((n + kTask - 1) / kTask);
+    std::atomic<bool> ok{true};
+    copy_pool_.run(tasks, [&](uint32_t i) {
+        thread_local std::vector<uint32_t> keys;
+        const uint64_t o = uint64_t(i) * kTask, len = std::min(kTask, n - o);
+        if (!zbf16::decode_range(c, reinterpret_cast<const uint8_t*>(stored) + o, src.nbytes, off + o, len,
+                                 reinterpret_cast<uint8_t*>(out) + o, keys))
+            ok.store(false);
+    });
+    return ok.load();
 }
 
 bool Daemon::copy_out(const ReadSrc& src, char* dst, uint64_t off, uint64_t n) {
@@ -325,7 +343,8 @@ int Daemon::persist_version(const VersionKey& vk) {
         int fd = ::open(tmp.c_str(), O_WRONLY | O_CREAT | O_TRUNC | O_CLOEXEC, 0644);
         if (fd >= 0) {
             std::vector<uint8_t> head(kDataOffset, 0);
-            StorageHeader h{kStorageMagic, kFormat, tid, nbytes, hlo, hhi, {0, 0, 0}};
+            // reserved[0]: the coding of the stored bytes (OFLD_FLAG_FORMAT_*), written as stored
+            StorageHeader h{kStorageMagic, kFormat, tid, nbytes, hlo, hhi, {src.fmt, 0, 0}};
             std::memcpy(head.data(), &h, sizeof(h));
             ok = write_fully(fd, head.data(), head.size());
             const uint64_t chunk = 8ull << 20;
@@ -437,6 +456,7 @@ void Daemon::recover_persisted() {
             if (pv.format != kFormat) continue;
             // every storage file must be present and match before anything is loaded
             bool complete = true;
+            std::map<uint64_t, uint64_t> coding;  // storage id -> OFLD_FLAG_FORMAT_* of its bytes
             for (const PersistedObject& po : pv.objects) {
                 if (persisted_files_.count(po.storage_id)) continue;
                 StorageHeader h{};
@@ -444,7 +464,9 @@ void Daemon::recover_persisted() {
                 struct stat st;
                 complete = fd >= 0 && ::pread(fd, &h, sizeof(h), 0) == ssize_t(sizeof(h)) && ::fstat(fd, &st) == 0 &&
                            h.magic == kStorageMagic && h.storage_id == po.storage_id && h.nbytes == po.nbytes &&
-                           uint64_t(st.st_size) >= kDataOffset + po.nbytes;
+                           uint64_t(st.st_size) >= kDataOffset + po.nbytes &&
+                           (h.reserved[0] & ~OFLD_FLAG_FORMAT_MASK) == 0 && h.reserved[0] != OFLD_FLAG_FORMAT_MASK;
+                if (complete) coding[po.storage_id] = h.reserved[0];
                 if (fd >= 0) ::close(fd);
                 if (!complete) break;
             }
@@ -477,6 +499,7 @@ void Daemon::recover_persisted() {
                     loc.kind = OFLD_LOC_NVME;
                     loc.cold_ref = commit_cold(std::move(c));
                     loc.nbytes = po.nbytes;
+                    loc.fmt = coding[po.storage_id];
                     locations_[po.storage_id] = loc;
                     persisted_files_[po.storage_id] = path;
                 }

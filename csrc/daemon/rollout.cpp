@@ -331,7 +331,9 @@ PullTensorResponse Daemon::on_pull_tensor(const PullTensorRequest& r) {
                        : src.kind == OFLD_LOC_PAGEABLE ? M::kExportFromPageable
                                                        : M::kExportFromNvme);
     const uint64_t hlo = o->hash_lo, hhi = o->hash_hi;
-    const uint64_t chunk = std::max<uint64_t>(cfg_.v2_export_chunk_bytes, 1 << 20);
+    // whole 128 KiB blocks, so a coded object's pieces decode on their own
+    const uint64_t chunk = (std::max<uint64_t>(cfg_.v2_export_chunk_bytes, 1 << 20) + (128u << 10) - 1) &
+                           ~uint64_t((128u << 10) - 1);
     uint32_t transport = r.transport;
     if (transport == TRANSPORT_LIBFABRIC_SEND || transport == TRANSPORT_RDMA_READ ||
         transport == TRANSPORT_RDMA_WRITE) {
@@ -349,18 +351,35 @@ PullTensorResponse Daemon::on_pull_tensor(const PullTensorRequest& r) {
         uint8_t hdr[40];
         export_header(hdr, r.object_id, nbytes, hlo, hhi);
         ok = sink->write(hdr, sizeof(hdr));
-        std::vector<char> bounce;
+        std::vector<char> bounce, plain;
         for (uint64_t off = 0; ok && off < nbytes; off += chunk) {
             uint64_t n = std::min(chunk, nbytes - off);
+            const char* stored = nullptr;  // the stored bytes of [off, off + n)
             if (src.pinned) {
-                ok = sink->write(src.pinned + off, n);
+                stored = src.pinned + off;
             } else if (src.kind == OFLD_LOC_PAGEABLE) {
-                ok = sink->write(src.cold.pageable + off, n);
+                stored = src.cold.pageable + off;
             } else {
                 bounce.resize(n);
-                ok = read_cold(src.cold, bounce.data(), off, n) && sink->write(bounce.data(), n);
-                if (!ok) err = "cold read or transport write failed";
+                if (!read_cold(src.cold, bounce.data(), off, n)) {
+                    ok = false;
+                    err = "cold read failed";
+                    break;
+                }
+                stored = bounce.data();
             }
+            if (src.fmt) {
+                // a coded run (zbf16 / zf32 canonical object): receivers get the raw bytes
+                plain.resize(n);
+                if (!decode_out(src, stored, off, n, plain.data())) {
+                    ok = false;
+                    err = "coded object failed to decode";
+                    break;
+                }
+                stored = plain.data();
+                Metrics::get().add(M::kExportDecodedBytes, n);
+            }
+            ok = sink->write(stored, n);
             if (!ok && err.empty()) err = "transport write failed";
         }
         Metrics::get().add(M::kExportStagingBytes, 0);

@@ -376,6 +376,34 @@ StatusResponse Daemon::on_d2h_submitted(const TransferMark& r) {
     return {true, "ok"};
 }
 
+// The coding of a run's bytes, recorded by the rank that copies into it
+// (canonical evicts decide it after their reservation). The slot entries carry
+// it like the format bits of a v1 reservation, so drains, readbacks,
+// restores and exports see it.
+StatusResponse Daemon::on_set_run_format(const SetRunFormatRequest& r) {
+    std::lock_guard<std::mutex> g(mu_);
+    if (!epoch_ok(r.rank_id, r.rank_epoch)) {
+        Metrics::get().inc(M::kEpochMismatchRejected);
+        return {false, "epoch invalid"};
+    }
+    if ((r.format & ~OFLD_FLAG_FORMAT_MASK) || r.format == OFLD_FLAG_FORMAT_MASK) return {false, "bad format bits"};
+    Lease* L = lease(r.lease_id);
+    if (!L || L->owner_rank != r.rank_id || L->base != r.slot_id) {
+        Metrics::get().inc(M::kLeaseOwnerMismatchRejected);
+        return {false, "lease/owner/slot mismatch"};
+    }
+    const uint32_t st = state_of(L->base);
+    if (st != OFLD_SLOT_RESERVED_D2H && st != OFLD_SLOT_D2H_IN_FLIGHT) {
+        Metrics::get().inc(M::kInvalidTransitionRejected);
+        return {false, "run not being written"};
+    }
+    for (uint32_t k = 0; k < L->count; ++k) {
+        slots_[L->base + k].flags = (slots_[L->base + k].flags & ~OFLD_FLAG_FORMAT_MASK) | r.format;
+        publish_slot(L->base + k);
+    }
+    return {true, "ok"};
+}
+
 bool Daemon::apply_d2h_complete(uint32_t rank, uint64_t epoch, uint64_t lease_id, uint64_t tid,
                                 uint64_t ver, uint32_t slot, uint64_t seq, bool* latest, bool* drained) {
     *latest = *drained = false;

@@ -105,36 +105,27 @@ void Daemon::CopyPool::stop() {
 }
 
 void Daemon::CopyPool::run_piece(const Piece& p) {
-    std::memcpy(p.dst, p.src, p.n);
+    (*p.fn)(p.index);
     if (p.left->fetch_sub(1, std::memory_order_acq_rel) == 1) {
         std::lock_guard<std::mutex> g(mu_);  // the waiter checks `left` under mu_
         done_cv_.notify_all();
     }
 }
 
-void Daemon::CopyPool::copy(char* dst, const char* src, uint64_t n) {
-    constexpr uint64_t kPiece = 1ull << 20;
-    uint64_t parts = 0;
-    {
-        std::lock_guard<std::mutex> g(mu_);
-        if (on_) parts = std::min<uint64_t>(ts_.size() + 1, n / kPiece);
-    }
-    if (parts <= 1) {
-        std::memcpy(dst, src, n);
+void Daemon::CopyPool::run(uint32_t tasks, const std::function<void(uint32_t)>& fn) {
+    if (tasks == 0) return;
+    if (tasks == 1 || threads() == 0) {
+        for (uint32_t i = 0; i < tasks; ++i) fn(i);
         return;
     }
-    const uint64_t step = (n / parts + 4095) & ~uint64_t(4095);
-    std::atomic<uint32_t> left{0};
-    std::vector<Piece> mine;
-    for (uint64_t off = step; off < n; off += step) mine.push_back(Piece{dst + off, src + off, std::min(step, n - off), &left});
-    left.store(uint32_t(mine.size()) + 1);
+    std::atomic<uint32_t> left{tasks};
     {
         std::lock_guard<std::mutex> g(mu_);
-        for (const Piece& p : mine) q_.push_back(p);
+        for (uint32_t i = 1; i < tasks; ++i) q_.push_back(Piece{&fn, i, &left});
     }
     cv_.notify_all();
-    run_piece(Piece{dst, src, std::min(step, n), &left});
-    // Help with queued pieces (this copy's or another's) until ours are done.
+    run_piece(Piece{&fn, 0, &left});
+    // Help with queued pieces (this call's or another's) until ours are done.
     for (;;) {
         Piece p;
         {
@@ -149,6 +140,21 @@ void Daemon::CopyPool::copy(char* dst, const char* src, uint64_t n) {
         }
         run_piece(p);
     }
+}
+
+void Daemon::CopyPool::copy(char* dst, const char* src, uint64_t n) {
+    constexpr uint64_t kPiece = 1ull << 20;
+    const uint64_t parts = std::min<uint64_t>(threads() + 1, n / kPiece);
+    if (parts <= 1) {
+        std::memcpy(dst, src, n);
+        return;
+    }
+    const uint64_t step = (n / parts + 4095) & ~uint64_t(4095);
+    const uint32_t tasks = uint32_t((n + step - 1) / step);
+    run(tasks, [&](uint32_t i) {
+        const uint64_t off = uint64_t(i) * step;
+        std::memcpy(dst + off, src + off, std::min(step, n - off));
+    });
 }
 
 void Daemon::copy_bytes(char* dst, const char* src, uint64_t n) const { copy_pool_.copy(dst, src, n); }

@@ -201,6 +201,7 @@ OFLD_OP(kDiscardTensor, DiscardTensorRequest, StatusResponse)
 OFLD_OP(kCarryForward, CarryForwardRequest, CarryForwardResponse)
 OFLD_OP(kGetAgentOptions, GetAgentOptionsRequest, GetAgentOptionsResponse)
 OFLD_OP(kBatchDiscardTensor, BatchDiscardTensorRequest, BatchDiscardTensorResponse)
+OFLD_OP(kSetRunFormat, SetRunFormatRequest, StatusResponse)
 #undef OFLD_OP
 
 // Re-encode a body through the C++ schema (decode then encode). Used by the

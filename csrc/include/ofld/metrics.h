@@ -82,7 +82,8 @@ namespace ofld {
     X(kVersionsPersisted, "versions_persisted_total")                          \
     X(kPersistedBytes, "persisted_bytes_total")                                \
     X(kVersionsRecovered, "versions_recovered_total")                          \
-    X(kCanonicalP2PVerified, "canonical_p2p_verified_total")
+    X(kCanonicalP2PVerified, "canonical_p2p_verified_total")                   \
+    X(kExportDecodedBytes, "export_decoded_bytes_total")
 
 enum class M : int {
 #define OFLD_ENUM(id, name) id,

@@ -59,6 +59,7 @@ enum class Op : uint16_t {
     kCarryForward = 47,          // new-version objects that share an older version's storage
     kGetAgentOptions = 48,       // tuning the daemon config forwards to rank agents (kernels:, nvlink:)
     kBatchDiscardTensor = 49,    // DiscardTensor for many (tensor, version) pairs in one round trip
+    kSetRunFormat = 50,          // record the coding (OFLD_FLAG_FORMAT_*) of a reserved run's bytes
 };
 
 const char* op_name(Op op);
@@ -772,6 +773,19 @@ struct BatchDiscardTensorResponse {
     std::vector<StatusResponse> results;
 };
 template <class V> void fields(V& v, BatchDiscardTensorResponse& m) { v(m.ok, m.message, m.results); }
+
+// The rank that holds a reservation records how the bytes it copies into the
+// run are coded (canonical evicts: their request has no flags field). Only
+// before the copy is marked complete.
+struct SetRunFormatRequest {
+    uint32_t rank_id = 0;
+    uint64_t rank_epoch = 0, lease_id = 0;
+    uint32_t slot_id = 0;
+    uint64_t format = 0;  // OFLD_FLAG_FORMAT_* bits (0 = raw)
+};
+template <class V> void fields(V& v, SetRunFormatRequest& m) {
+    v(m.rank_id, m.rank_epoch, m.lease_id, m.slot_id, m.format);
+}
 
 struct ExportManifestResponse {
     bool ok = false;

@@ -44,7 +44,9 @@
 // Typical ratio for N(0, s) bf16 data: 0.75 + escapes (a few per chunk).
 #pragma once
 
+#include <algorithm>
 #include <cstdint>
+#include <type_traits>
 #include <cstring>
 #include <vector>
 
@@ -216,6 +218,117 @@ inline bool decode_chunk(const uint8_t* in, uint32_t len, uint8_t* out) {
     });
     if (!ok || k != hd.n_esc) return false;
     std::memcpy(out, h.data(), len);
+    return true;
+}
+
+// The same decoding without the lane-order walk over every element and
+// without allocation (the daemon decodes coded canonical objects on export):
+// one pass in element order rebuilds every value from its window code and
+// notes the escaped elements; a counting pass over the 256 lanes then maps
+// each to its escape byte. `keys` is caller scratch reused across calls.
+inline bool decode_chunk_fast(const uint8_t* in, uint32_t len, uint8_t* out, std::vector<uint32_t>& keys) {
+    Header hd;
+    std::memcpy(&hd, in, kHeader);
+    if (hd.tag != kTag || (hd.mode != 1 && hd.mode != 2) || hd.src_len != len || hd.comp_len > len || len % 16 ||
+        hd.comp_len != (hd.mode == 2 ? coded_len3(len, hd.n_esc) : coded_len(len, hd.n_esc)))
+        return false;
+    const uint32_t n = len / 2;
+    const bool m2 = hd.mode == 2;
+    const uint8_t* low = in + kHeader;
+    const uint8_t* codes = low + n;
+    const uint8_t* esc = codes + (m2 ? (n / 8) * 3 : n / 2);
+    const uint32_t ebase = hd.ebase;
+    keys.clear();
+    uint16_t* dst = reinterpret_cast<uint16_t*>(out);  // out is 2-byte aligned in every caller
+    // One pass per code width (constant shifts let the compiler unroll and
+    // vectorize the rebuild); an escape is a field of all ones, found from
+    // bit 0 of every field after ANDing the field's bits together.
+    auto scan = [&](auto width) -> bool {
+        constexpr uint32_t B = decltype(width)::value;
+        constexpr uint32_t M = (1u << B) - 1;
+        constexpr uint32_t lsb = B == 3 ? 0x249249u : 0x11111111u;
+        for (uint32_t v = 0; v < n / 8; ++v) {
+            uint32_t cw;  // the vector's 8 codes
+            if (B == 3) {
+                cw = uint32_t(codes[3 * v]) | (uint32_t(codes[3 * v + 1]) << 8) | (uint32_t(codes[3 * v + 2]) << 16);
+            } else {
+                std::memcpy(&cw, codes + 4 * v, 4);
+            }
+            const uint8_t* lo = low + 8 * v;
+            uint16_t* d = dst + 8 * v;
+            for (uint32_t j = 0; j < 8; ++j) {
+                const uint32_t ex = ebase + ((cw >> (B * j)) & M);
+                d[j] = uint16_t((uint32_t(lo[j] & 0x80u) << 8) | ((ex & 0xFFu) << 7) | (lo[j] & 0x7Fu));
+            }
+            const uint32_t ones = B == 3 ? (cw & (cw >> 1) & (cw >> 2)) : (cw & (cw >> 1) & (cw >> 2) & (cw >> 3));
+            if (ones & lsb) {
+                for (uint32_t j = 0; j < 8; ++j) {
+                    if (((cw >> (B * j)) & M) != M) continue;
+                    if (keys.size() >= hd.n_esc) return false;
+                    keys.push_back(8 * v + j);
+                }
+            }
+        }
+        return true;
+    };
+    if (!(m2 ? scan(std::integral_constant<uint32_t, 3>{}) : scan(std::integral_constant<uint32_t, 4>{})))
+        return false;
+    if (keys.size() != hd.n_esc) return false;
+    // Escape order is lane-major (lane t = vector index mod 256, then the
+    // lane's vectors, then elements); the scan above found them vector-major,
+    // which within one lane is already that order. A counting pass over the
+    // lanes gives each lane's first escape byte.
+    uint32_t start[kLanes] = {};
+    for (uint32_t i : keys) ++start[(i >> 3) & (kLanes - 1)];
+    uint32_t acc = 0;
+    for (uint32_t l = 0; l < kLanes; ++l) {
+        const uint32_t c = start[l];
+        start[l] = acc;
+        acc += c;
+    }
+    for (uint32_t i : keys) {
+        const uint32_t k = start[(i >> 3) & (kLanes - 1)]++;
+        dst[i] = rebuild(low[i], esc[k]);
+    }
+    return true;
+}
+
+// Decode bytes [off, off + n) of a coded object of `nbytes` (format bits of
+// OFLD_FLAG_FORMAT_*: 1 = zbf16, 2 = zf32) whose coded run is `in` (the run's
+// bytes at the same offsets). `off` must be a multiple of the format's block
+// (64 KiB zbf16 chunks, 128 KiB zf32 rows); n may end mid-object only at a
+// block boundary or at nbytes. False on a malformed block.
+enum class Coding : uint32_t { kZbf16 = 1, kZf32 = 2 };
+inline bool decode_range(Coding fmt, const uint8_t* in, uint64_t nbytes, uint64_t off, uint64_t n, uint8_t* out,
+                         std::vector<uint32_t>& keys) {
+    const uint64_t block = fmt == Coding::kZf32 ? 2ull * kChunk : kChunk;
+    if (off % block || off + n > nbytes || ((off + n) % block && off + n != nbytes)) return false;
+    if (fmt == Coding::kZbf16) {
+        const uint64_t nchunks = (nbytes + kChunk - 1) / kChunk;
+        for (uint64_t base = off; base < off + n; base += kChunk) {
+            const uint64_t c = base / kChunk;
+            const uint32_t len = uint32_t(nbytes - base < kChunk ? nbytes - base : kChunk);
+            if (raw_by_rule(c, nchunks, len)) {
+                std::memcpy(out + (base - off), in + (base - off), len);
+            } else if (!decode_chunk_fast(in + (base - off), len, out + (base - off), keys)) {
+                return false;
+            }
+        }
+        return true;
+    }
+    std::vector<uint8_t> hi(kChunk);
+    for (uint64_t base = off; base < off + n; base += block) {
+        const uint8_t* row = in + (base - off);
+        uint8_t* dst = out + (base - off);
+        if (!decode_chunk_fast(row + kChunk, kChunk, hi.data(), keys)) return false;
+        for (uint32_t i = 0; i < kChunk / 2; ++i) {  // value i = top half i << 16 | low half i
+            uint16_t h, l;
+            std::memcpy(&h, hi.data() + 2 * i, 2);
+            std::memcpy(&l, row + 2 * i, 2);
+            const uint32_t w = (uint32_t(h) << 16) | l;
+            std::memcpy(dst + 4 * i, &w, 4);
+        }
+    }
     return true;
 }
 

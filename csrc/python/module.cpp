@@ -198,6 +198,7 @@ py::dict stats_dict(const AgentStats& s) {
     d["d2h_ns"] = s.d2h_ns;
     d["h2d_ns"] = s.h2d_ns;
     d["registration_ns"] = s.registration_ns;
+    d["coded_canonical"] = s.coded_canonical;
     return d;
 }
 
@@ -237,6 +238,7 @@ class PyAgent {
             else if (k == "zero_canonical_hash") o.zero_canonical_hash = v.cast<bool>();
             else if (k == "stream_priority") o.stream_priority = v.cast<int>();
             else if (k == "compress") o.compress = v.cast<bool>();
+            else if (k == "compress_canonical") o.compress_canonical = v.cast<bool>();
             else if (k == "compress_min_bytes") o.compress_min_bytes = v.cast<uint64_t>();
             else if (k == "batch_group_bytes") o.batch_group_bytes = v.cast<uint64_t>();
             else if (k == "kernel_timing") o.kernel_timing = v.cast<bool>();
@@ -715,6 +717,18 @@ PYBIND11_MODULE(_C, m) {
         if (!zbf16::decode_object(reinterpret_cast<const uint8_t*>(in.data()), in.size(),
                                   reinterpret_cast<uint8_t*>(&out[0])))
             throw std::runtime_error("malformed zbf16 object");
+        return py::bytes(out);
+    });
+    // The daemon's export decoder (allocation-free chunk decoding) over bytes
+    // [off, off + n) of a coded object: fmt 1 = zbf16, 2 = zf32.
+    m.def("zcoded_decode_range", [](int fmt, py::bytes coded, uint64_t off, uint64_t n) {
+        std::string in = coded;
+        if (off > in.size()) throw std::runtime_error("offset beyond the object");
+        std::string out(n, '\0');
+        std::vector<uint32_t> keys;
+        if (!zbf16::decode_range(zbf16::Coding(fmt), reinterpret_cast<const uint8_t*>(in.data()) + off, in.size(), off,
+                                 n, reinterpret_cast<uint8_t*>(&out[0]), keys))
+            throw std::runtime_error("malformed coded range");
         return py::bytes(out);
     });
     m.def("zbf16_coded_bytes", [](py::bytes coded) {

@@ -61,6 +61,7 @@ class Op:
     CARRY_FORWARD = 47
     GET_AGENT_OPTIONS = 48
     BATCH_DISCARD_TENSOR = 49
+    SET_RUN_FORMAT = 50
 
 
 # Backward-compatible names used by rollout engines.
@@ -204,6 +205,8 @@ SCHEMA: Dict[str, List[Tuple[str, Any]]] = {
     "TensorVersion": [("tensor_id", "u64"), ("version", "u64")],
     "BatchDiscardTensorRequest": [("rank_id", "u32"), ("rank_epoch", "u64"), ("items", ["TensorVersion"])],
     "BatchDiscardTensorResponse": STATUS + [("results", ["Status"])],
+    "SetRunFormatRequest": [("rank_id", "u32"), ("rank_epoch", "u64"), ("lease_id", "u64"), ("slot_id", "u32"),
+                            ("format", "u64")],
 }
 
 # opcode -> (request message, response message)
@@ -242,6 +245,7 @@ OPS: Dict[int, Tuple[str, str]] = {
     Op.CARRY_FORWARD: ("CarryForwardRequest", "CarryForwardResponse"),
     Op.GET_AGENT_OPTIONS: ("GetAgentOptionsRequest", "GetAgentOptionsResponse"),
     Op.BATCH_DISCARD_TENSOR: ("BatchDiscardTensorRequest", "BatchDiscardTensorResponse"),
+    Op.SET_RUN_FORMAT: ("SetRunFormatRequest", "Status"),
 }
 
 _PRIM = {"u8": struct.Struct("<B"), "u16": struct.Struct("<H"), "u32": struct.Struct("<I"),

@@ -961,6 +961,7 @@ _AGENT_OPTION_KEYS = {
     "kernels.coded_restore": ("coded_restore", str),
     "kernels.coded_evict": ("coded_evict", str),
     "kernels.compress": ("compress", _as_bool),
+    "kernels.compress_canonical": ("compress_canonical", _as_bool),
     "kernels.compress_min_mb": ("compress_min_bytes", lambda v: int(float(v) * (1 << 20))),
     "kernels.batch_group_mb": ("batch_group_bytes", lambda v: int(float(v) * (1 << 20))),
     "kernels.timing": ("kernel_timing", _as_bool),

@@ -36,6 +36,7 @@ class RawRank:
         req = dict(rank_id=rank_id, local_rank=rank_id, world_rank=rank_id, gpu_id=gpu, numa_node=numa,
                    pid=pid if pid is not None else os.getpid() * 1000 + rank_id)
         self.control = None
+        self.arenas = {}
         if map_control:
             r = self._register_with_fds(req)
         else:
@@ -58,6 +59,8 @@ class RawRank:
         try:
             if r["ok"]:
                 self.control = mmap.mmap(fds[r["control_fd_index"]], r["control_size"])
+                for a in r["arenas"]:
+                    self.arenas[a["arena_id"]] = mmap.mmap(fds[a["fd_index"]], a["size"])
         finally:
             for fd in fds:
                 os.close(fd)
@@ -99,6 +102,10 @@ class RawRank:
         arena_id, off = struct.unpack_from("<QQ", self.control, at + 16)
         return state, arena_id, off, struct.unpack_from("<Q", self.control, at + 40)[0], \
             struct.unpack_from("<Q", self.control, at + 48)[0]
+
+    def write_arena(self, arena_id: int, offset: int, data: bytes) -> None:
+        """Store bytes in a reserved run, as an agent's copy would (needs map_control)."""
+        self.arenas[arena_id][offset:offset + len(data)] = data
 
     def set_ring_tail(self, tail: int) -> None:
         struct.pack_into("<Q", self.control, self._ring() + 128, tail)
@@ -148,6 +155,8 @@ class RawRank:
         return {e["key"]: e["value"] for e in r["stats"]}
 
     def close(self):
+        for m in self.arenas.values():
+            m.close()
         if self.control is not None:
             self.control.close()
         self.conn.close()

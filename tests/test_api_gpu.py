@@ -205,3 +205,55 @@ def test_small_evicts_hash_on_host_or_device_alike(sock_path, host_hash_max):
             assert c.content_hash == native().ssh_hash(w.cpu().view(torch.uint8).numpy())
     finally:
         d.stop()
+
+
+@pytest.mark.parametrize("compress_canonical", [True, False])
+def test_coded_canonical_objects_round_trip_and_export_raw(sock_path, compress_canonical):
+    """bf16 canonical objects of 4 MiB and more cross PCIe zbf16-coded (one
+    batch and one single evict); their content hash is the raw bytes' (host
+    oracle), canonical restore decodes them (also with the fp32 cast), and
+    TCP / FILE pulls from offloadd get the raw bytes. Small and fp32 objects
+    stay raw; with compress_canonical off nothing is coded."""
+    from statespectre_b200 import RolloutWeightClient
+
+    d = in_process_daemon(socket=sock_path, arena_mb=512, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", job_name="coded-canon",
+                             compress_canonical=compress_canonical) as off:
+            g = torch.Generator(device="cuda").manual_seed(3)
+            ts = {"big": torch.randn(6 << 20, device="cuda", generator=g).to(torch.bfloat16) * 0.02,
+                  "odd": torch.randn((5 << 20) + 8 * 333, device="cuda", generator=g).to(torch.bfloat16),
+                  "small": torch.randn(4096, device="cuda", generator=g).to(torch.bfloat16),
+                  "f32": torch.randn(3 << 20, device="cuda", generator=g)}
+            refs = {n: t.clone() for n, t in ts.items()}
+            keys = {n: off.canonical_key(model_role=ModelRole.POLICY_ROLLOUT, model_version=1, param_name=n, tensor=t)
+                    for n, t in ts.items()}
+            before = off.summary_dict()["coded_canonical"]
+            hs = dict(zip(["big", "small", "f32"],
+                          off.canonical_evict_batch([(ts[n], keys[n]) for n in ("big", "small", "f32")],
+                                                    destructive=False)))
+            hs["odd"] = off.canonical_evict(ts["odd"], keys["odd"], destructive=False)
+            coded = off.summary_dict()["coded_canonical"] - before
+            assert coded == (2 if compress_canonical else 0)
+            for n, h in hs.items():
+                assert h.content_hash == native().ssh_hash(refs[n].cpu().view(torch.uint8).numpy()), n
+                out = torch.empty_like(refs[n])
+                h.restore_into(out)
+                torch.cuda.synchronize()
+                assert torch.equal(out, refs[n]), n
+            # the fp32 cast decodes too
+            f32 = torch.empty(refs["big"].numel(), dtype=torch.float32, device="cuda")
+            ok, msg = off._agent.canonical_restore(hs["big"].object_id, f32.data_ptr(), f32.numel() * 4,
+                                                   torch.cuda.current_stream().cuda_stream, True, 3, 0)
+            torch.cuda.synchronize()
+            assert ok, msg
+            assert torch.equal(f32, refs["big"].float())
+            off.promote_rollout_version(1)
+            for transport in ("tcp", "file"):
+                cl = RolloutWeightClient(sock_path, off.job_id, off.launch_epoch, job_name=off.job_name)
+                res = cl.sync_latest(transport=transport)
+                for n, h in hs.items():
+                    assert res["data"][h.object_id] == refs[n].cpu().view(torch.uint8).numpy().tobytes(), (n, transport)
+                cl.close()
+    finally:
+        d.stop()

@@ -8,6 +8,7 @@ an unsealed version, quota; reference: tests/cpp/test_canonical.cpp:226-727).
 
 import os
 import struct
+import time
 
 import pytest
 import torch
@@ -543,3 +544,115 @@ def test_canonical_evict_batch_destructive_releases_storage(cdaemon):
             out = torch.empty_like(r)
             h.restore_into(out)
             assert torch.equal(out, r)
+
+
+def _coded_canonical_object(sock, raw: bytes, job_name: str, version: int = 1, fmt: str = "zbf16"):
+    """Create a canonical object whose pinned run holds `raw` coded (zbf16 or
+    zf32, the host codec's bytes, as a GPU agent's coded evict stores them),
+    record its coding with SetRunFormat, commit it with the raw bytes' hash
+    and promote the version. Returns (rank, job, object id)."""
+    import numpy as np
+
+    from statespectre_b200._native import native
+
+    C = native()
+    arr = np.frombuffer(raw, dtype=np.uint8)
+    coded = C.zbf16_encode(arr) if fmt == "zbf16" else C.zf32_encode(arr)
+    assert coded is not None and len(coded) == len(raw) and coded != raw
+    r = RawRank(sock, 0, map_control=True)
+    job = r.call(Op.REGISTER_JOB, tenant_id=0, job_name=job_name)["job"]
+    key = {"job": job, "model_role": ROLL, "model_version": version, "param_id": 77, "param_fqn_debug": "coded.w",
+           "nbytes": len(raw), "shard_nbytes": len(raw), "expert_id": -1, "dtype": 15 if fmt == "zbf16" else 6}
+    c = r.call(Op.REQUEST_CANONICAL_EVICT, rank_id=0, rank_epoch=r.epoch, key=key, destructive=False,
+               attach_if_exists=True, create_if_missing=True, dedup_mode=1, alignment=256)
+    assert c["ok"] and c["action"] == 1, c
+    r.write_arena(c["arena_id"], c["arena_offset"], coded)
+    bit = (1 << 18) if fmt == "zbf16" else (1 << 19)
+    bad = r.call(Op.SET_RUN_FORMAT, rank_id=0, rank_epoch=r.epoch, lease_id=c["lease_id"] + 99, slot_id=c["slot_id"],
+                 format=bit)
+    assert not bad["ok"]  # only the lease holder records a coding
+    assert not r.call(Op.SET_RUN_FORMAT, rank_id=0, rank_epoch=r.epoch, lease_id=c["lease_id"], slot_id=c["slot_id"],
+                      format=3 << 18)["ok"]  # both codings at once is no coding
+    assert r.call(Op.SET_RUN_FORMAT, rank_id=0, rank_epoch=r.epoch, lease_id=c["lease_id"], slot_id=c["slot_id"],
+                  format=bit)["ok"]
+    assert r.mark(Op.MARK_D2H_SUBMITTED, c["lease_id"], c["synthetic_tid"], 1, c["slot_id"])["ok"]
+    assert r.mark(Op.MARK_D2H_COMPLETE, c["lease_id"], c["synthetic_tid"], 1, c["slot_id"])["ok"]
+    lo, hi = C.ssh_hash(arr)
+    cm = r.call(Op.COMMIT_CANONICAL_OBJECT, rank_id=0, rank_epoch=r.epoch, object_id=c["object_id"],
+                lease_id=c["lease_id"], slot_id=c["slot_id"], content_hash_lo=lo, content_hash_hi=hi)
+    assert cm["ok"], cm
+    s = r.call(Op.SEAL_MODEL_VERSION, job=job, model_role=ROLL, model_version=version, fail_if_missing=True,
+               expected_param_ids=[], promote=True)
+    assert s["ok"], s
+    # once complete, the coding of the run is fixed
+    assert not r.call(Op.SET_RUN_FORMAT, rank_id=0, rank_epoch=r.epoch, lease_id=c["lease_id"],
+                      slot_id=c["slot_id"], format=0)["ok"]
+    return r, job, c["object_id"]
+
+
+def _pull_all(sock, job, transports=("tcp", "file")):
+    out = {}
+    for transport in transports:
+        cl = RolloutWeightClient(sock, job["job_id"], job["launch_epoch"], job_name=job["job_name"])
+        res = cl.sync_latest(transport=transport)
+        out[transport] = res["data"]
+        cl.close()
+    return out
+
+
+@pytest.mark.parametrize("fmt", ["zbf16", "zf32"])
+def test_coded_canonical_object_is_served_raw_from_pinned(sock_path, fmt):
+    """A canonical object whose run is coded is exported decoded: TCP and
+    FILE pulls (and the reference-format receiver's hash check) see the raw
+    bytes; the export counts the decoded bytes."""
+    d = in_process_daemon(socket=sock_path, arena_mb=128, drain_on_complete=False)
+    try:
+        g = torch.Generator().manual_seed(5)
+        if fmt == "zbf16":
+            raw = (torch.randn((3 << 20) // 2 + 8 * 1000, generator=g) * 0.02).to(torch.bfloat16)
+        else:
+            raw = torch.randn(5 * 32768, generator=g) * 0.02
+        raw = raw.view(torch.uint8).numpy().tobytes()
+        r, job, oid = _coded_canonical_object(sock_path, raw, f"coded-{fmt}", fmt=fmt)
+        before = r.stats().get("export_decoded_bytes_total", 0)
+        for transport, data in _pull_all(sock_path, job).items():
+            assert data[oid] == raw, transport
+        assert r.stats()["export_decoded_bytes_total"] - before == 2 * len(raw)
+        r.close()
+    finally:
+        d.stop()
+
+
+def test_coded_canonical_object_drained_and_persisted_stays_exact(tmp_path):
+    """The coding follows the bytes: drained to pageable memory, written to
+    the persist directory verbatim and reloaded by a restarted daemon, the
+    object still pulls as its raw bytes."""
+    sock = str(tmp_path / "d.sock")
+    pdir = str(tmp_path / "persist")
+    raw = (torch.randn(1 << 20, generator=torch.Generator().manual_seed(9))).to(torch.bfloat16)
+    raw = raw.view(torch.uint8).numpy().tobytes()
+    d = in_process_daemon(socket=sock, arena_mb=128, drain_on_complete=True, persist_dir=pdir)
+    try:
+        r, job, oid = _coded_canonical_object(sock, raw, "coded-tiers")
+        man = RolloutWeightClient(sock, job["job_id"], job["launch_epoch"], job_name=job["job_name"])
+        for _ in range(500):
+            if man.get_manifest(1)["tensors"][0]["location_hint"] != "pinned":
+                break
+            time.sleep(0.01)
+        assert man.get_manifest(1)["tensors"][0]["location_hint"] in ("pageable", "nvme")
+        man.close()
+        assert _pull_all(sock, job)["tcp"][oid] == raw
+        for _ in range(500):
+            if r.stats().get("versions_persisted_total", 0) >= 1:
+                break
+            time.sleep(0.01)
+        assert r.stats()["versions_persisted_total"] >= 1
+        r.close()
+    finally:
+        d.stop()
+    d = in_process_daemon(socket=sock, arena_mb=128, drain_on_complete=False, persist_dir=pdir)
+    try:
+        data = _pull_all(sock, job)
+        assert data["tcp"][oid] == raw and data["file"][oid] == raw
+    finally:
+        d.stop()

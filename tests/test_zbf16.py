@@ -121,3 +121,46 @@ def test_decoder_rejects_corruption():
     coded[0] ^= 0xFF  # header tag
     with pytest.raises(RuntimeError):
         C.zbf16_decode(bytes(coded))
+
+
+@pytest.mark.parametrize("nbytes", [4096, 65536, 3 * 65536 + 4096, 7 * 65536 + 2048, 9 * 65536 + 16 * 1000])
+def test_export_decoder_matches_the_reference_decoder(nbytes):
+    """The daemon's allocation-free decoder (element-order pass, sorted escape
+    patch) gives the reference decoder's bytes, for whole objects and for
+    chunk-aligned sub-ranges, in both code widths and with many escapes."""
+    C = native()
+    g = torch.Generator().manual_seed(nbytes + 1)
+    x = torch.randn(nbytes // 2, generator=g)
+    x[::97] *= 1e-6  # deep escapes (mode 1)
+    x[::13] *= 300.0  # widen the window so some chunks pick mode 2 and some mode 1
+    raw = _bf16_bytes(x)
+    coded = C.zbf16_encode(raw)
+    assert coded is not None
+    assert C.zcoded_decode_range(1, coded, 0, nbytes) == raw.tobytes()
+    for off in range(0, nbytes, 2 * CHUNK):
+        n = min(2 * CHUNK, nbytes - off)
+        assert C.zcoded_decode_range(1, coded, off, n) == raw[off:off + n].tobytes()
+    if nbytes > CHUNK:
+        with pytest.raises(RuntimeError):
+            C.zcoded_decode_range(1, coded, 16, CHUNK)  # not chunk-aligned
+
+
+@pytest.mark.parametrize("rows", [1, 3])
+def test_export_decoder_handles_zf32_rows(rows):
+    C = native()
+    g = torch.Generator().manual_seed(rows)
+    x = torch.randn(rows * 32768, generator=g) * 0.02
+    raw = x.contiguous().view(torch.uint8).numpy()
+    coded = C.zf32_encode(raw)
+    assert coded is not None
+    assert C.zcoded_decode_range(2, coded, 0, len(raw)) == raw.tobytes()
+    assert C.zcoded_decode_range(2, coded, 131072 * (rows - 1), 131072) == raw[131072 * (rows - 1):].tobytes()
+
+
+def test_export_decoder_rejects_corruption():
+    C = native()
+    x = torch.randn(65536)
+    coded = bytearray(C.zbf16_encode(_bf16_bytes(x)))
+    coded[8] ^= 0xFF  # escape count no longer matches the codes
+    with pytest.raises(RuntimeError):
+        C.zcoded_decode_range(1, bytes(coded), 0, len(coded))
