@@ -1203,7 +1203,9 @@ std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items,
                     std::lock_guard<std::mutex> lg(D.tab_mu);
                     D.tensors[{p.tid, p.ver}].offloaded = false;
                 }
-                if (D.batch_kernel_ok(items[i].ptr, p.nbytes)) {
+                // coded items share the group's job kernel; uncoded ones go to the
+                // copy engine (digests beside it) unless the session asks for SM copies
+                if (D.batch_kernel_ok(items[i].ptr, p.nbytes) && (p.z || D.opt.uncoded != "copy_engine")) {
                     kern::XferJob j{};
                     j.src = reinterpret_cast<const void*>(items[i].ptr);
                     j.dst = dev;
@@ -1531,7 +1533,7 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
                         D.finish(p);
                         continue;
                     }
-                } else if (D.batch_kernel_ok(items[i].ptr, r.nbytes)) {
+                } else if (D.batch_kernel_ok(items[i].ptr, r.nbytes) && (z || D.opt.uncoded != "copy_engine")) {
                     kern::XferJob j{};
                     j.src = dev;
                     j.dst = reinterpret_cast<void*>(items[i].ptr);
@@ -1544,7 +1546,7 @@ std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& i
                     if (z)
                         CUDA_OK(kern::restore_z(dev, reinterpret_cast<void*>(items[i].ptr), r.nbytes,
                                                 kern::Cast::kNone, nullptr, nullptr, nullptr, s, D.opt.restore_ctas));
-                    else if (D.opt.engine == "copy_engine")
+                    else if (D.opt.engine == "copy_engine" || D.opt.uncoded == "copy_engine")
                         CUDA_OK(cudaMemcpyAsync(reinterpret_cast<void*>(items[i].ptr), host, r.nbytes,
                                                 cudaMemcpyHostToDevice, s));
                     else

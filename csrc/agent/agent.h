@@ -46,7 +46,10 @@ struct AgentOptions {
     //   "bulk"         kern::evict_bulk / restore_bulk (bulk copies through
     //                  shared memory; aligned, size % 16 == 0);
     //   "sm"           per-thread K1 / K2.
-    // Restores that verify digests or cast always run K2.
+    // Restores that verify digests or cast always run K2. In evict_batch /
+    // restore_batch, "copy_engine" moves each uncoded item with its own copy
+    // (digests beside it); the other forms put uncoded items into the group's
+    // job kernel with the coded ones.
     std::string uncoded = "copy_engine";
     // How a zbf16-coded run comes back: "copy_engine" (the copy engine moves
     // each chunk's stored bytes as one strided copy into device staging, in

@@ -45,6 +45,8 @@ def run(args, metric: str) -> dict:
                            kernel_timing=bool(getattr(args, "kernel_timing", 0)),
                            evict_ctas=int(getattr(args, "evict_ctas", 0)),
                            restore_ctas=int(getattr(args, "restore_ctas", 0)),
+                           compress=bool(getattr(args, "compress", 1)),
+                           uncoded=getattr(args, "uncoded", "copy_engine"),
                            **({"batch_group_bytes": int(args.kv_group_mb) << 20}
                               if getattr(args, "kv_group_mb", 0) else {}))
     off = sess.off

@@ -257,3 +257,31 @@ def test_coded_canonical_objects_round_trip_and_export_raw(sock_path, compress_c
                 cl.close()
     finally:
         d.stop()
+
+
+@pytest.mark.parametrize("uncoded", ["copy_engine", "sm"])
+def test_batch_uncoded_items_on_either_form(sock_path, uncoded):
+    """A batch that mixes coded bf16 blocks with uncoded ones (fp32, fp8,
+    int, an odd-sized block and bf16 with coding off) round-trips byte for
+    byte, with the host oracle's content hashes, whether uncoded items take
+    the copy engine or the group's job kernel."""
+    d = in_process_daemon(socket=sock_path, arena_mb=512, drain_on_complete=False)
+    try:
+        with offload_context(daemon_addr=sock_path, device="cuda:0", uncoded=uncoded) as off:
+            g = torch.Generator(device="cuda").manual_seed(11)
+            blocks = [torch.randn(2 << 20, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3)]
+            blocks += [torch.randn(1 << 20, device="cuda", generator=g) for _ in range(3)]
+            blocks += [torch.randn(3 << 20, device="cuda", generator=g).to(torch.float8_e4m3fn),
+                       torch.randint(-9, 9, ((1 << 20) + 3,), dtype=torch.int32, device="cuda"),
+                       torch.randint(0, 255, (4 * 1024 + 7,), dtype=torch.uint8, device="cuda")]
+            refs = [b.clone() for b in blocks]
+            hs = off.evict_batch(blocks)
+            assert [h.coded for h in hs[:3]] == [True] * 3 and not any(h.coded for h in hs[3:])
+            for h, r in zip(hs, refs):
+                assert h.content_hash == native().ssh_hash(r.cpu().view(torch.uint8).numpy())
+            outs = off.restore_batch(hs)
+            torch.cuda.synchronize()
+            for o, r in zip(outs, refs):
+                assert torch.equal(o.view(torch.uint8), r.view(torch.uint8))
+    finally:
+        d.stop()
