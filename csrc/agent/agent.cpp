@@ -2000,9 +2000,18 @@ RestoreOutcome Agent::canonical_restore(uint64_t object_id, uint64_t ptr, uint64
         D.resolve(rr.arena_id, rr.arena_offset, rr.nbytes, &host, &dev);
         ++D.restores;
         uint64_t n = ro.cast == 0 ? nbytes : rr.nbytes;
-        const int64_t slot = D.gpu ? D.slot_at(rr.arena_id, rr.arena_offset) : -1;
+        const int64_t slot = D.slot_at(rr.arena_id, rr.arena_offset);
         const bool coded = slot >= 0 && D.run_is_z(uint32_t(slot));
-        if (!D.gpu) {
+        if (!D.gpu && coded) {
+            // a host-mode consumer of an object a GPU rank stored coded
+            if (ro.cast != 0) throw std::runtime_error("host-mode restore of a coded object cannot cast");
+            if (n != rr.nbytes && n % zbf16::kChunk)
+                throw std::runtime_error("partial restore of a coded object must be a multiple of 64 KiB");
+            std::vector<uint32_t> keys;
+            if (!zbf16::decode_range(zbf16::Coding::kZbf16, reinterpret_cast<const uint8_t*>(host), rr.nbytes, 0, n,
+                                     reinterpret_cast<uint8_t*>(ptr), keys))
+                throw std::runtime_error("malformed coded object");
+        } else if (!D.gpu) {
             std::memcpy(reinterpret_cast<void*>(ptr), host, n);
         } else if (coded) {
             // zbf16 run: K2 decodes from host memory. A prefix of the object

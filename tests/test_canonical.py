@@ -656,3 +656,24 @@ def test_coded_canonical_object_drained_and_persisted_stays_exact(tmp_path):
         assert data["tcp"][oid] == raw and data["file"][oid] == raw
     finally:
         d.stop()
+
+
+def test_host_mode_consumer_decodes_a_coded_object(cdaemon):
+    """A CPU (host-mode) session restoring an object that a GPU rank stored
+    coded gets the raw bytes, whole or as a 64 KiB-multiple prefix."""
+    raw_t = (torch.randn(3 << 19, generator=torch.Generator().manual_seed(4)) * 0.02).to(torch.bfloat16)
+    raw = raw_t.view(torch.uint8).numpy().tobytes()
+    r, job, oid = _coded_canonical_object(cdaemon, raw, "coded-host")
+    with session(cdaemon, 5, job="coded-host") as off:
+        out = torch.empty_like(raw_t)
+        ok, msg = off._agent.canonical_restore(oid, out.data_ptr(), len(raw), 0, True)
+        assert ok, msg
+        assert out.view(torch.uint8).numpy().tobytes() == raw
+        part = torch.empty(65536, dtype=torch.uint8)
+        ok, msg = off._agent.canonical_restore(oid, part.data_ptr(), 65536, 0, True)
+        assert ok, msg
+        assert part.numpy().tobytes() == raw[:65536]
+        odd = torch.empty(1000, dtype=torch.uint8)
+        ok, msg = off._agent.canonical_restore(oid, odd.data_ptr(), 1000, 0, True)
+        assert not ok and "64 KiB" in msg
+    r.close()
