@@ -262,9 +262,9 @@ def test_coded_canonical_objects_round_trip_and_export_raw(sock_path, compress_c
 @pytest.mark.parametrize("uncoded", ["copy_engine", "sm"])
 def test_batch_uncoded_items_on_either_form(sock_path, uncoded):
     """A batch that mixes coded bf16 blocks with uncoded ones (fp32, fp8,
-    int, an odd-sized block and bf16 with coding off) round-trips byte for
-    byte, with the host oracle's content hashes, whether uncoded items take
-    the copy engine or the group's job kernel."""
+    int and an odd-sized block) round-trips byte for byte, with the host
+    oracle's content hashes, whether uncoded items are restored by the copy
+    engine or by the group's job kernel."""
     d = in_process_daemon(socket=sock_path, arena_mb=512, drain_on_complete=False)
     try:
         with offload_context(daemon_addr=sock_path, device="cuda:0", uncoded=uncoded) as off:
