@@ -167,6 +167,7 @@ def main():
     from statespectre_b200 import launch_daemon, offload_context
     from statespectre_b200._native import native
     from statespectre_b200.utils.clocks import ClockSampler
+    from statespectre_b200.utils.launch import host_mem_available_bytes
     from statespectre_b200.utils.topology import daemon_yaml, gpu_numa_nodes
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -195,7 +196,12 @@ def main():
         return float(t.item())
 
     nbytes = args.size_mb << 20
-    window_gb = max(4, (3 * nbytes >> 30) + 2)
+    # three tensors' room per GPU window, unless the host cannot pin that for
+    # every window of the node (GPU hosts here have about 196 GB): then one
+    # tensor plus 2 GB, which the evict/restore loop needs at any time
+    n_windows = max(int(os.environ.get("LOCAL_WORLD_SIZE", str(world))), torch.cuda.device_count(), 1)
+    room_gb = int(0.6 * host_mem_available_bytes() / (1 << 30) / n_windows)
+    window_gb = max(4, min((3 * nbytes >> 30) + 2, max((nbytes >> 30) + 2, room_gb)))
     run_dir = os.environ.get("OFLD_BENCH_DIR", "/tmp/ofld_bench")
     os.makedirs(run_dir, exist_ok=True)
     sock = os.path.join(run_dir, "offloadd.sock")
