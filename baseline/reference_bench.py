@@ -476,8 +476,10 @@ def run_weight_sync(args, world: int, rank: int, local_rank: int, device, state_
     if local_rank == 0:
         if os.path.exists(sock):
             os.unlink(sock)
-        # trainer GPUs hold this version and the previous one until it is dropped
-        win = int(2 * shard_bytes / (1 << 30)) + 6
+        # trainer GPUs hold one version: the previous one is dropped before the
+        # next is recorded (its rollout pull finished in the previous step), so
+        # 8 GPUs fit the GPU hosts' ~196 GB of memory (two versions would pin 150 GB)
+        win = int(shard_bytes / (1 << 30)) + 6
         by_node = {}
         for g in range(max(n_local, torch.cuda.device_count())):
             by_node.setdefault(_gpu_numa_node(g), []).append(g)
@@ -555,6 +557,10 @@ def run_weight_sync(args, world: int, rank: int, local_rank: int, device, state_
                     off_e += n
                     h2d += 2 * n
             torch.cuda.synchronize(device)
+            if v > 1:  # the rollout finished pulling v - 1 in the previous step
+                if tp_rank == 0:
+                    off.drop_canonical_version("policy_rollout", v - 1)
+                dist.barrier(group=trainer_group)  # every trainer's window is free again
             for n in names:  # the reference records every tensor of the version
                 key = off.canonical_key(model_role="policy_rollout", model_version=v, param_name=n,
                                         tensor=params[n], pp_rank=0, tp_rank=tp_rank, expert_id=-1)
@@ -569,8 +575,6 @@ def run_weight_sync(args, world: int, rank: int, local_rank: int, device, state_
             if int(go.item()) != 1:  # .item(): an NCCL recv only orders the stream, the host waits here
                 raise RuntimeError(f"reference rollout pulled nothing for version {v}")
             dist.barrier(group=trainer_group)
-            if tp_rank == 0 and v > 1:
-                off.drop_canonical_version("policy_rollout", v - 1)
         else:
             dist.recv(go, peer)
             if int(go.item()) != v:  # wait on the host for the trainer's promote of version v
