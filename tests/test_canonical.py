@@ -677,3 +677,30 @@ def test_host_mode_consumer_decodes_a_coded_object(cdaemon):
         ok, msg = off._agent.canonical_restore(oid, odd.data_ptr(), 1000, 0, True)
         assert not ok and "64 KiB" in msg
     r.close()
+
+
+def test_corrupt_coded_object_fails_its_export_and_the_daemon_survives(cdaemon):
+    """Coded bytes that no longer decode (a rank scribbled over its run after
+    the commit) make that pull fail with a message; other objects and later
+    pulls are unaffected."""
+    raw = (torch.randn(1 << 20, generator=torch.Generator().manual_seed(2))).to(torch.bfloat16)
+    raw = raw.view(torch.uint8).numpy().tobytes()
+    r, job, oid = _coded_canonical_object(cdaemon, raw, "coded-corrupt")
+    cl = RolloutWeightClient(cdaemon, job["job_id"], job["launch_epoch"], job_name=job["job_name"])
+    man = cl.get_manifest(1)
+    entry = man["tensors"][0]
+    assert cl.pull_tensor(entry, 1) == raw
+    # find the run and overwrite the escape count of its third chunk header
+    arena_id, off = None, None
+    for s in range(r.num_slots):
+        state, a, o, n, tid = r.slot_fields(s)
+        if n == len(raw) and tid >> 63:
+            arena_id, off = a, o
+            break
+    assert arena_id is not None
+    r.write_arena(arena_id, off + 2 * 65536 + 4, b"\xff\xff\x00\x00")
+    with pytest.raises(Exception, match="decode|transport|export|failed"):
+        cl.pull_tensor(entry, 1)
+    cl.close()
+    assert r.stats()["export_transport_errors_total"] >= 1
+    r.close()
