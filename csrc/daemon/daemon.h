@@ -147,6 +147,9 @@ class Daemon {
         fail_writes_.store(writes);
         fail_reads_.store(reads);
     }
+    // Test hook: report this many bytes of available host memory instead of
+    // /proc/meminfo's MemAvailable (0 = the real figure).
+    void fake_host_memory(uint64_t available) { fake_mem_available_.store(available); }
     // Test hook: stop (and resume) consuming the ranks' completion rings, so
     // a test can fill a ring and watch the agents fall back to RPCs.
     void pause_rings(bool paused) { rings_paused_.store(paused); }
@@ -518,6 +521,14 @@ class Daemon {
     std::vector<std::atomic<uint64_t>> stripe_cursor_;
     uint32_t stripes_ = 1;
     std::atomic<int> fail_writes_{0}, fail_reads_{0};
+    std::atomic<uint64_t> fake_mem_available_{0};
+    // Whether the pageable tier can take `nbytes` more: within
+    // drain_policy.pageable_limit_gb when set, else within the host memory
+    // the kernel reports available (plus reusable pooled buffers), less a
+    // reserve of max(4 GiB, 5 % of the host): anonymous memory is committed
+    // only as the copy touches it, so an unchecked drain of tens of GB runs
+    // the host out of memory and the kernel kills the daemon.
+    bool pageable_room(uint64_t nbytes) const;
 };
 
 }  // namespace ofld

@@ -13,6 +13,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <deque>
@@ -169,6 +170,36 @@ void Daemon::cold_quota(uint64_t tid, uint64_t nbytes, bool* allow_pageable, boo
     *allow_nvme = !j->max_nvme || j->nvme_bytes + nbytes <= j->max_nvme;
 }
 
+namespace {
+// A /proc/meminfo field in bytes (0 when unreadable).
+uint64_t meminfo_bytes(const char* field) {
+    FILE* f = std::fopen("/proc/meminfo", "r");
+    if (!f) return 0;
+    char line[256];
+    uint64_t v = 0;
+    const size_t n = std::strlen(field);
+    while (std::fgets(line, sizeof(line), f)) {
+        if (std::strncmp(line, field, n) == 0 && line[n] == ':') {
+            v = std::strtoull(line + n + 1, nullptr, 10) * 1024;  // kB
+            break;
+        }
+    }
+    std::fclose(f);
+    return v;
+}
+}  // namespace
+
+bool Daemon::pageable_room(uint64_t nbytes) const {
+    const uint64_t resident = Metrics::get().value(M::kPageableResidentBytes);
+    if (cfg_.pageable_limit_bytes) return resident + nbytes <= cfg_.pageable_limit_bytes;
+    const uint64_t fake = fake_mem_available_.load();
+    const uint64_t avail = fake ? fake : meminfo_bytes("MemAvailable");
+    if (!avail) return true;  // no /proc/meminfo: nothing to go by
+    static const uint64_t total = meminfo_bytes("MemTotal");
+    const uint64_t reserve = std::max<uint64_t>(4ull << 30, total / 20);
+    return nbytes + reserve <= avail + pageable_pool_.pooled();
+}
+
 bool Daemon::write_cold(const char* src, uint64_t nbytes, ColdEntry* out, bool allow_pageable, bool allow_nvme) {
     out->nbytes = nbytes;
     if (fail_writes_.load() > 0 && fail_writes_.fetch_sub(1) > 0) {
@@ -179,12 +210,13 @@ bool Daemon::write_cold(const char* src, uint64_t nbytes, ColdEntry* out, bool a
     switch (cfg_.drain_target) {
         case DrainTarget::kPageableOnly: pageable = true; break;
         case DrainTarget::kNvmeOnly: pageable = !cfg_.nvme_enabled; break;
-        case DrainTarget::kPageableThenNvme: {
-            uint64_t resident = Metrics::get().value(M::kPageableResidentBytes);
-            bool fits = cfg_.pageable_limit_bytes == 0 || resident + nbytes <= cfg_.pageable_limit_bytes;
-            pageable = fits || !cfg_.nvme_enabled;
-            break;
-        }
+        case DrainTarget::kPageableThenNvme: pageable = true; break;
+    }
+    if (pageable && allow_pageable && !pageable_room(nbytes)) {
+        // over the pageable budget or out of host memory: NVMe when it may
+        // take the bytes, else the drain fails and the run stays pinned
+        pageable = false;
+        Metrics::get().inc(M::kPageableRoomRejected);
     }
     pageable = pageable && allow_pageable;
     uint64_t t0 = mono_ns();

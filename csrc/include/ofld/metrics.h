@@ -83,7 +83,8 @@ namespace ofld {
     X(kPersistedBytes, "persisted_bytes_total")                                \
     X(kVersionsRecovered, "versions_recovered_total")                          \
     X(kCanonicalP2PVerified, "canonical_p2p_verified_total")                   \
-    X(kExportDecodedBytes, "export_decoded_bytes_total")
+    X(kExportDecodedBytes, "export_decoded_bytes_total")                       \
+    X(kPageableRoomRejected, "pageable_room_rejected_total")
 
 enum class M : int {
 #define OFLD_ENUM(id, name) id,

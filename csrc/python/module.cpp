@@ -121,6 +121,9 @@ class DaemonThread {
         }
         d_.reset();
     }
+    void fake_host_memory(uint64_t avail) {
+        if (d_) d_->fake_host_memory(avail);
+    }
     void inject_io_failures(int w, int r) {
         if (d_) d_->inject_io_failures(w, r);
     }
@@ -501,6 +504,7 @@ PYBIND11_MODULE(_C, m) {
         .def(py::init([](py::kwargs kw) { return new DaemonThread(config_from(kw)); }))
         .def("stop", &DaemonThread::stop)
         .def("inject_io_failures", &DaemonThread::inject_io_failures)
+        .def("fake_host_memory", &DaemonThread::fake_host_memory)
         .def("pause_rings", &DaemonThread::pause_rings)
         .def_property_readonly("socket", &DaemonThread::socket);
 

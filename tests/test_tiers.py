@@ -264,3 +264,30 @@ def test_tier_copies_split_over_the_copy_pool_are_exact(sock_path, copy_threads)
                 h.discard()
     finally:
         d.stop()
+
+
+def test_drains_stay_pinned_when_the_host_is_out_of_memory(sock_path):
+    """Without a pageable budget the pageable tier takes only what the host
+    has to spare: with (fake) available memory under the reserve, drains fail
+    and the tensors stay pinned and restorable; once memory is back, drains
+    go through."""
+    d = in_process_daemon(socket=sock_path, arena_mb=64, drain_on_complete=True)
+    try:
+        d.fake_host_memory(1 << 30)  # 1 GiB available: below the 4 GiB reserve
+        with offload_context(daemon_addr=sock_path, device="cpu") as off:
+            xs = [torch.randn(1 << 20) for _ in range(3)]
+            hs = [off.copy(x, wait=True) for x in xs]
+            assert wait_for(lambda: off.daemon_stats()["pageable_room_rejected_total"] >= 3)
+            assert all(h.location() == "pinned" for h in hs)
+            assert off.daemon_stats()["pageable_resident_bytes"] == 0
+            for h, x in zip(hs, xs):
+                assert torch.equal(h.restore(), x)
+            d.fake_host_memory(1 << 50)
+            more = [torch.randn(1 << 20) for _ in range(2)]
+            hm = [off.copy(x, wait=True) for x in more]
+            for h in hm:
+                assert wait_for(lambda: h.location() == "pageable"), h.location()
+            for h, x in zip(hm, more):
+                assert torch.equal(h.restore(), x)
+    finally:
+        d.stop()
