@@ -65,6 +65,17 @@ Daemon::~Daemon() {
 }
 
 void Daemon::build_arenas() {
+    // Arenas are shared memory faulted in here: more than the host has would
+    // get the daemon killed in the middle of the first touch. Refuse instead,
+    // with the numbers (skipped when /proc/meminfo is unreadable).
+    if (cfg_.numa_first_touch) {
+        uint64_t want = 0;
+        for (const NumaArena& ac : cfg_.per_numa) want += round_up(ac.size_bytes, cfg_.allocation_granularity_bytes);
+        const uint64_t avail = host_memory_available();
+        if (avail && want > avail)
+            throw std::runtime_error("arenas need " + std::to_string(want >> 20) + " MiB but the host has " +
+                                     std::to_string(avail >> 20) + " MiB available");
+    }
     for (size_t i = 0; i < cfg_.per_numa.size(); ++i) {
         const NumaArena& ac = cfg_.per_numa[i];
         Arena a;

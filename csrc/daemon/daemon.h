@@ -529,6 +529,9 @@ class Daemon {
     // only as the copy touches it, so an unchecked drain of tens of GB runs
     // the host out of memory and the kernel kills the daemon.
     bool pageable_room(uint64_t nbytes) const;
+    // MemAvailable of /proc/meminfo in bytes (the test hook's figure when set;
+    // 0 when unreadable).
+    uint64_t host_memory_available() const;
 };
 
 }  // namespace ofld

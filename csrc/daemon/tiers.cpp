@@ -189,11 +189,15 @@ uint64_t meminfo_bytes(const char* field) {
 }
 }  // namespace
 
+uint64_t Daemon::host_memory_available() const {
+    const uint64_t fake = fake_mem_available_.load();
+    return fake ? fake : meminfo_bytes("MemAvailable");
+}
+
 bool Daemon::pageable_room(uint64_t nbytes) const {
     const uint64_t resident = Metrics::get().value(M::kPageableResidentBytes);
     if (cfg_.pageable_limit_bytes) return resident + nbytes <= cfg_.pageable_limit_bytes;
-    const uint64_t fake = fake_mem_available_.load();
-    const uint64_t avail = fake ? fake : meminfo_bytes("MemAvailable");
+    const uint64_t avail = host_memory_available();
     if (!avail) return true;  // no /proc/meminfo: nothing to go by
     static const uint64_t total = meminfo_bytes("MemTotal");
     const uint64_t reserve = std::max<uint64_t>(4ull << 30, total / 20);

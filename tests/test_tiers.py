@@ -291,3 +291,11 @@ def test_drains_stay_pinned_when_the_host_is_out_of_memory(sock_path):
                 assert torch.equal(h.restore(), x)
     finally:
         d.stop()
+
+
+def test_daemon_refuses_arenas_larger_than_host_memory(sock_path):
+    """Arenas are faulted in at start: a config asking for more than the host
+    has is refused with the numbers instead of the daemon being killed
+    half-way through the first touch."""
+    with pytest.raises(Exception, match="arenas need .* MiB but the host has .* MiB available"):
+        in_process_daemon(socket=sock_path, arena_mb=1 << 26)  # 64 TiB
