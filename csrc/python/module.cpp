@@ -5,6 +5,9 @@
 // (statespectre_b200/_wire.py) encodes and decodes, so the binding has no
 // per-message code; data-moving calls have typed bindings.
 #include <cuda_runtime.h>
+#include <sys/socket.h>
+#include <sys/time.h>
+
 #include <pybind11/functional.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
@@ -61,7 +64,9 @@ void check(cudaError_t e, const char* what) {
 // fallbacks and tests that drive the wire directly).
 class RawConn {
  public:
-    RawConn(const std::string& addr, int timeout_ms) {
+    // reply_timeout_ms > 0: a call whose reply does not arrive in time fails
+    // (a daemon that does not know an opcode may leave it unanswered)
+    RawConn(const std::string& addr, int timeout_ms, int reply_timeout_ms) {
         if (addr.rfind("tcp://", 0) == 0) {
             std::string host;
             uint16_t port = 0;
@@ -69,6 +74,10 @@ class RawConn {
             fd_ = tcp_connect(host, port, timeout_ms);
         } else {
             fd_ = uds_connect(addr.rfind("unix://", 0) == 0 ? addr.substr(7) : addr, timeout_ms);
+        }
+        if (reply_timeout_ms > 0) {
+            timeval tv{reply_timeout_ms / 1000, (reply_timeout_ms % 1000) * 1000};
+            ::setsockopt(fd_, SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof(tv));
         }
     }
     ~RawConn() { close_fd(fd_); }
@@ -509,7 +518,8 @@ PYBIND11_MODULE(_C, m) {
         .def_property_readonly("socket", &DaemonThread::socket);
 
     py::class_<RawConn>(m, "RawConn")
-        .def(py::init<std::string, int>(), py::arg("addr"), py::arg("timeout_ms") = 10000)
+        .def(py::init<std::string, int, int>(), py::arg("addr"), py::arg("timeout_ms") = 10000,
+             py::arg("reply_timeout_ms") = 0)
         .def("call", &RawConn::call, py::arg("op"), py::arg("body"), py::arg("fds") = std::vector<int>{})
         .def("send_bytes", &RawConn::send_bytes)
         .def("close", &RawConn::close);

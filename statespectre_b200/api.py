@@ -976,7 +976,8 @@ def _daemon_agent_options(path: str, rank: int, gpu: int) -> dict:
     if not path.startswith("tcp://") and not os.path.exists(path):
         return {}  # no daemon there; the session's own connect reports it
     try:
-        conn = native().RawConn(path, 5000)
+        # StateSpectre's own offloadd logs an unknown opcode and sends nothing back
+        conn = native().RawConn(path, 5000, 2000)
     except Exception:  # noqa: BLE001 - the agent reports connection errors itself
         return {}
     try:

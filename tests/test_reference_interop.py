@@ -101,3 +101,59 @@ def test_reference_rollout_client_pulls_from_this_daemon(sock_path):
             assert ref_wire.EXPORT_HEADER_SIZE == 40
     finally:
         d.stop()
+
+
+def test_this_agent_records_and_pulls_through_the_reference_daemon(tmp_path):
+    """The other direction: a host-mode session of this repository against
+    StateSpectre's own offloadd (baseline/_ref/bin/offloadd; skipped when not
+    built). The session's start-up probe for forwarded agent options
+    (opcode 48, which that daemon logs as unknown and leaves unanswered) gives
+    up after its reply timeout; registration, the control region, canonical
+    evicts, the seal and a TCP pull then work byte for byte."""
+    import subprocess
+    import time
+
+    from statespectre_b200 import RolloutWeightClient
+
+    binary = os.path.join(ROOT, "baseline", "_ref", "bin", "offloadd")
+    if not os.path.exists(binary):
+        pytest.skip("reference build not present (python baseline/build_reference.py)")
+    sock = str(tmp_path / "d.sock")
+    port = _free_port()
+    cfg = tmp_path / "offloadd.yaml"
+    cfg.write_text("\n".join([
+        "daemon:", f"  socket_path: {sock}", f"  control_shm_name: /ofld_interop_{os.getpid()}",
+        "  heartbeat_timeout_ms: 60000", "arenas:", "  allocation_granularity_mb: 2", "  per_numa:",
+        "    - numa_node: 0", "      size_gb: 2", "      overflow_gb: 1", "      gpu_windows:",
+        "        - gpu: 0", "          size_gb: 1",
+        "drain_policy:", "  target_tier: pageable", "  drain_on_d2h_complete: false", "nvme:", "  enabled: false"])
+        + "\n")
+    log = open(tmp_path / "ref.log", "w")
+    proc = subprocess.Popen([binary, "--config", str(cfg), "--socket", sock, "--tcp-port", str(port)],
+                            stdout=log, stderr=log)
+    try:
+        deadline = time.time() + 30
+        while not os.path.exists(sock) and time.time() < deadline and proc.poll() is None:
+            time.sleep(0.05)
+        assert os.path.exists(sock), (tmp_path / "ref.log").read_text()
+        tensors = {f"layers.{i}.w": torch.randn(1000 + 77 * i, 33) for i in range(3)}
+        t0 = time.time()
+        with offload_context(daemon_addr=sock, device="cpu", rank=0, job_name="interop-rev") as off:
+            assert time.time() - t0 < 20  # the options probe did not hang the session
+            for n, t in tensors.items():
+                h = off.canonical_evict(t.clone(), off.canonical_key(model_role=ROLL, model_version=1, param_name=n,
+                                                                     tensor=t))
+                assert h.action_name == "NEED_D2H_CREATE"
+            assert off.promote_rollout_version(1)["tensor_count"] == len(tensors)
+            cl = RolloutWeightClient(f"tcp://127.0.0.1:{port}", off.job_id, off.launch_epoch, recv_host="127.0.0.1")
+            man = cl.get_manifest(1)
+            for e in man["tensors"]:
+                assert cl.pull_tensor(e, 1) == tensors[e["key"]["param_fqn_debug"]].numpy().tobytes()
+            cl.close()
+    finally:
+        proc.terminate()
+        try:
+            proc.wait(timeout=30)
+        except subprocess.TimeoutExpired:
+            proc.kill()
+        log.close()
