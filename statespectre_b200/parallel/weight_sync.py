@@ -16,8 +16,9 @@ bytes take one hop instead:
   differs from what the rollout already holds cross NVLink, quantized on the
   fly in fp8 mode; the same pass yields every parameter's 128-bit content hash;
 * the version is then made durable in offloadd without re-copying unchanged
-  parameters: changed ones go through ``canonical_evict`` (K1, D2H + hash),
-  unchanged ones are carried forward (objects that share the previous
+  parameters: changed ones go through one ``canonical_evict_batch`` (K1, D2H
+  + hash, zbf16-coded over PCIe; every round trip and copy issued before the
+  first copy is awaited), unchanged ones are carried forward (objects that share the previous
   version's storage), then the version is sealed and promoted. Manifests are
   the same as StateSpectre's, so cross-node rollouts pull as before.
 """
