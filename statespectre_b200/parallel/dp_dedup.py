@@ -7,7 +7,9 @@ compares host-side hashes (reference: src/daemon/canonical.cpp:298-341,
 324-341 and 488-495 for the candidate path).
 
 Here, for each parameter one owner rank creates the object (K1 copies the
-bytes to pinned memory and computes the ssh128 hash in the same pass).
+bytes to pinned memory, zbf16-coded for bf16 parameters, and computes the
+ssh128 hash of the raw bytes in the same pass; each rank's parameters go in
+one ``canonical_evict_batch``).
 Ownership is round-robin over parameters by default, which spreads the copies
 over all the replicas' PCIe links instead of funnelling the whole model
 through one. The other replicas then verify without copying, by one of:
