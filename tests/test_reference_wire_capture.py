@@ -1,0 +1,200 @@
+"""Wire golden vectors captured from StateSpectre's own daemon.
+
+``capture()`` starts the reference's ``offloadd`` (built offline in
+``baseline/_ref`` by baseline/build_reference.py), walks it through a session
+over a raw socket (register, heartbeat, the v1 evict / restore state machine,
+location, stats, a job, a canonical object, seal, manifest, FILE pull,
+canonical restore, release, drop, batch completion) and records every request
+body this repository encoded and every response body the reference's codec
+encoded. The capture is committed as ``tests/golden/reference_wire.json``:
+
+  * the reference answered every captured request with ok, so it decoded what
+    this repository's codec wrote;
+  * this repository's C++ codec and its Python mirror both decode every
+    reference response and re-encode it to the same bytes.
+
+The round trips over the committed file run everywhere; with the reference
+build present, a fresh capture is checked the same way. Regenerate the file
+with ``python tests/test_reference_wire_capture.py --write``.
+"""
+
+import json
+import os
+import socket
+import subprocess
+import sys
+import tempfile
+import time
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from statespectre_b200 import _wire  # noqa: E402
+from statespectre_b200._native import native  # noqa: E402
+from statespectre_b200._wire import Op  # noqa: E402
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "reference_wire.json")
+REF_DAEMON = os.path.join(ROOT, "baseline", "_ref", "bin", "offloadd")
+ROLL = 2  # policy_rollout
+
+
+class _Raw:
+    """One control connection that keeps every request and response body."""
+
+    def __init__(self, path: str):
+        self.sock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        self.sock.settimeout(20)
+        self.sock.connect(path)
+        self.records = []
+
+    def call(self, op: int, fds: bool = False, **kw) -> dict:
+        req_name, resp_name = _wire.OPS[op]
+        body = _wire.encode(req_name, kw)
+        self.sock.sendall(_wire.make_frame(op, body))
+        if fds:  # RegisterRank: descriptors ride on the reply's frame header
+            head, got_fds, _, _ = socket.recv_fds(self.sock, _wire.FRAME_HEADER.size, 64)
+            for fd in got_fds:
+                os.close(fd)
+            if len(head) < _wire.FRAME_HEADER.size:
+                head += _wire.recv_exact(self.sock, _wire.FRAME_HEADER.size - len(head))
+            rop, _flags, n = _wire.parse_frame_header(head)
+            payload = _wire.recv_exact(self.sock, n)
+        else:
+            rop, payload = _wire.recv_frame(self.sock)
+        assert rop == op, (op, rop)
+        resp = _wire.decode(resp_name, payload)
+        self.records.append({"op": int(op), "request": req_name, "response": resp_name, "request_hex": body.hex(),
+                             "response_hex": payload.hex(), "ok": bool(resp.get("ok", True))})
+        return resp
+
+
+def _session(raw: _Raw, run_dir: str) -> None:
+    """A session through every opcode the reference serves (1-30)."""
+    reg = raw.call(Op.REGISTER_RANK, fds=True, rank_id=0, local_rank=0, world_rank=0, gpu_id=0, numa_node=0,
+                   pid=os.getpid() * 1000, capabilities=0)
+    ep = reg["rank_epoch"]
+    raw.call(Op.HEARTBEAT, rank_id=0, rank_epoch=ep, timestamp_ns=1)
+    g = raw.call(Op.REQUEST_OFFLOAD, rank_id=0, rank_epoch=ep, tensor_id=100, version=1, nbytes=4096, gpu_id=0,
+                 numa_node=0, alignment=256, priority=0, flags=0, debug_name="layers.0.w")
+    mark = dict(rank_id=0, rank_epoch=ep, lease_id=g["lease_id"], tensor_id=100, version=1, slot_id=g["slot_id"],
+                seq=1, timestamp_ns=1)
+    raw.call(Op.MARK_D2H_SUBMITTED, **mark)
+    raw.call(Op.MARK_D2H_COMPLETE, **mark)
+    raw.call(Op.QUERY_LOCATION, tensor_id=100, version=1)
+    p = raw.call(Op.REQUEST_PREFETCH, rank_id=0, rank_epoch=ep, tensor_id=100, version=1, nbytes=4096, gpu_id=0,
+                 numa_node=0, priority=0, flags=0)
+    hmark = dict(mark, lease_id=p["lease_id"], slot_id=p["slot_id"], seq=2)
+    raw.call(Op.MARK_H2D_SUBMITTED, **hmark)
+    raw.call(Op.MARK_H2D_COMPLETE, **hmark, keep_pinned=True)
+    raw.call(Op.RELEASE_LEASE, rank_id=0, rank_epoch=ep, lease_id=g["lease_id"], slot_id=g["slot_id"],
+             reason="golden capture")
+    g2 = raw.call(Op.REQUEST_OFFLOAD, rank_id=0, rank_epoch=ep, tensor_id=101, version=3, nbytes=1 << 20, gpu_id=0,
+                  numa_node=0, alignment=256, priority=0, flags=0, debug_name="")
+    raw.call(Op.MARK_D2H_SUBMITTED, **dict(mark, lease_id=g2["lease_id"], tensor_id=101, version=3,
+                                          slot_id=g2["slot_id"]))
+    raw.call(Op.BATCH_COMPLETE, rank_id=0, rank_epoch=ep,
+             completions=[{"event_type": 1, "lease_id": g2["lease_id"], "tensor_id": 101, "version": 3,
+                           "slot_id": g2["slot_id"], "seq": 3, "timestamp_ns": 5, "keep_pinned": False}])
+    raw.call(Op.GET_STATS, rank_id=0xFFFFFFFF)
+    job = raw.call(Op.REGISTER_JOB, tenant_id=0, job_name="golden", scheduler_job_id=0, label_keys=[],
+                   label_values=[])["job"]
+    key = _wire.defaults("CanonicalKey")
+    key.update(job=job, model_role=ROLL, model_version=1, param_id=7, param_fqn_hash=8, param_fqn_debug="layers.0.w",
+               dtype=15, nbytes=8192, shard_nbytes=8192, tp_rank=1, expert_id=-1)
+    c = raw.call(Op.REQUEST_CANONICAL_EVICT, rank_id=0, rank_epoch=ep, key=key, destructive=False,
+                 attach_if_exists=True, create_if_missing=True, dedup_mode=1, alignment=256)
+    cmark = dict(mark, lease_id=c["lease_id"], tensor_id=c["synthetic_tid"], version=1, slot_id=c["slot_id"], seq=4)
+    raw.call(Op.MARK_D2H_SUBMITTED, **cmark)
+    raw.call(Op.MARK_D2H_COMPLETE, **cmark)
+    raw.call(Op.COMMIT_CANONICAL_OBJECT, rank_id=0, rank_epoch=ep, object_id=c["object_id"], lease_id=c["lease_id"],
+             slot_id=c["slot_id"], content_hash_lo=0x1122334455667788, content_hash_hi=0x99AABBCCDDEEFF00)
+    raw.call(Op.SEAL_MODEL_VERSION, job=job, model_role=ROLL, model_version=1, fail_if_missing=True,
+             expected_param_ids=[7], promote=True)
+    raw.call(Op.GET_LATEST_SEALED_VERSION, job=job, model_role=ROLL)
+    raw.call(Op.GET_MANIFEST, job=job, model_role=ROLL, model_version=1, filter={"tp_present": True, "tp_rank": 1})
+    raw.call(Op.PULL_TENSOR, job=job, model_role=ROLL, model_version=1, object_id=c["object_id"], transport=2,
+             target_descriptor=os.path.join(run_dir, "pull.bin"))
+    raw.call(Op.REQUEST_CANONICAL_RESTORE, rank_id=0, rank_epoch=ep, object_id=c["object_id"], gpu_id=0,
+             numa_node=0)
+    raw.call(Op.RELEASE_CANONICAL_RESTORE, rank_id=0, rank_epoch=ep, object_id=c["object_id"])
+    raw.call(Op.RELEASE_CANONICAL, rank_id=0, rank_epoch=ep, job=job, model_role=ROLL, model_version=1,
+             object_id=c["object_id"])
+    raw.call(Op.DROP_CANONICAL_VERSION, job=job, model_role=ROLL, model_version=1)
+
+
+def capture(binary: str = REF_DAEMON) -> list:
+    """Records of one session against the reference daemon at `binary`."""
+    run_dir = tempfile.mkdtemp(prefix="ssref-golden-")
+    sock = os.path.join(run_dir, "d.sock")
+    cfg = os.path.join(run_dir, "offloadd.yaml")
+    with open(cfg, "w") as f:
+        f.write("\n".join([
+            "daemon:", f"  socket_path: {sock}", f"  control_shm_name: /ssref_golden_{os.getpid()}",
+            "  heartbeat_timeout_ms: 60000", "arenas:", "  allocation_granularity_mb: 2", "  per_numa:",
+            "    - numa_node: 0", "      size_gb: 1", "      overflow_gb: 0", "      gpu_windows:",
+            "        - gpu: 0", "          size_gb: 1",
+            "drain_policy:", "  target_tier: pageable", "  drain_on_d2h_complete: false", "nvme:",
+            "  enabled: false"]) + "\n")
+    log = open(os.path.join(run_dir, "offloadd.log"), "w")
+    proc = subprocess.Popen([binary, "--config", cfg, "--socket", sock], stdout=log, stderr=log)
+    raw = None
+    try:
+        deadline = time.time() + 30
+        while not os.path.exists(sock) and time.time() < deadline and proc.poll() is None:
+            time.sleep(0.05)
+        if not os.path.exists(sock):
+            raise RuntimeError(f"reference offloadd did not start (log {log.name})")
+        raw = _Raw(sock)
+        _session(raw, run_dir)
+        return raw.records
+    finally:
+        if raw is not None:
+            raw.sock.close()
+        proc.terminate()
+        try:
+            proc.wait(timeout=30)
+        except subprocess.TimeoutExpired:
+            proc.kill()
+        log.close()
+
+
+def _check(records: list) -> None:
+    C = native()
+    assert records, "empty capture"
+    for r in records:
+        req, resp = bytes.fromhex(r["request_hex"]), bytes.fromhex(r["response_hex"])
+        what = f"{r['request']} -> {r['response']}"
+        assert r["ok"], f"the reference refused {what}"
+        # the reference's response bytes, through this repository's C++ codec and its Python mirror
+        assert C.reencode(r["op"], True, resp) == resp, what
+        assert _wire.encode(r["response"], _wire.decode(r["response"], resp)) == resp, what
+        # this repository's request bytes, which the reference accepted, are stable in both codecs
+        assert C.reencode(r["op"], False, req) == req, what
+        assert _wire.encode(r["request"], _wire.decode(r["request"], req)) == req, what
+
+
+def test_golden_capture_from_the_reference_round_trips():
+    with open(GOLDEN) as f:
+        records = json.load(f)["records"]
+    ops = {r["op"] for r in records}
+    assert set(range(1, 12)) | {13} | set(range(20, 31)) <= ops  # every opcode but Shutdown
+    _check(records)
+
+
+def test_live_capture_from_the_reference_round_trips():
+    if not os.path.exists(REF_DAEMON):
+        pytest.skip("reference build not present (python baseline/build_reference.py)")
+    _check(capture())
+
+
+if __name__ == "__main__":
+    if "--write" in sys.argv:
+        recs = capture()
+        os.makedirs(os.path.dirname(GOLDEN), exist_ok=True)
+        with open(GOLDEN, "w") as f:
+            json.dump({"source": "StateSpectre offloadd built from the reference sources (baseline/_ref/bin)",
+                       "records": recs}, f, indent=1)
+        print(f"wrote {len(recs)} records to {GOLDEN}")
