@@ -506,7 +506,7 @@ RequestPrefetchResponse Daemon::do_request_prefetch(const RequestPrefetchRequest
         }
         resp.ready = true;
         resp.state = submit ? OFLD_SLOT_H2D_IN_FLIGHT : OFLD_SLOT_PINNED_VALID;
-        resp.message = "ready";
+        resp.message = "ok";  // StateSpectre's text for a pinned-ready prefetch
         Trace::get().event("PINNED_READY", r.rank_id, gpu, r.tensor_id, want, L.id, L.base, L.nbytes);
     };
 

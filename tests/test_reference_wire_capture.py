@@ -198,3 +198,26 @@ if __name__ == "__main__":
             json.dump({"source": "StateSpectre offloadd built from the reference sources (baseline/_ref/bin)",
                        "records": recs}, f, indent=1)
         print(f"wrote {len(recs)} records to {GOLDEN}")
+
+
+def test_this_daemon_answers_the_session_as_the_reference_did():
+    """The same session against this repository's offloadd: every response
+    decodes to the reference's values field by field (epochs, slot and lease
+    numbers, arena offsets, job id, object ids, actions, manifest hash,
+    counts), apart from the FILE pull's path; GetStats carries every counter
+    name the reference reports."""
+    from statespectre_b200._native import bin_path
+
+    ours = capture(bin_path("offloadd"))
+    with open(GOLDEN) as f:
+        ref = json.load(f)["records"]
+    assert [r["op"] for r in ours] == [r["op"] for r in ref]
+    for a, b in zip(ref, ours):
+        da = _wire.decode(a["response"], bytes.fromhex(a["response_hex"]))
+        db = _wire.decode(b["response"], bytes.fromhex(b["response_hex"]))
+        if a["response"] == "GetStatsResponse":
+            assert {e["key"] for e in da["stats"]} <= {e["key"] for e in db["stats"]}
+            continue
+        da.pop("transport_metadata", None)
+        db.pop("transport_metadata", None)
+        assert da == db, (a["request"], {k: (da[k], db.get(k)) for k in da if da[k] != db.get(k)})
