@@ -44,11 +44,11 @@ ROLL = 2  # policy_rollout
 class _Raw:
     """One control connection that keeps every request and response body."""
 
-    def __init__(self, path: str):
+    def __init__(self, path: str, records=None):
         self.sock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
         self.sock.settimeout(20)
         self.sock.connect(path)
-        self.records = []
+        self.records = records if records is not None else []
 
     def call(self, op: int, fds: bool = False, **kw) -> dict:
         req_name, resp_name = _wire.OPS[op]
@@ -71,7 +71,7 @@ class _Raw:
         return resp
 
 
-def _session(raw: _Raw, run_dir: str) -> None:
+def _session(raw: _Raw, run_dir: str, sock: str) -> None:
     """A session through every opcode the reference serves (1-30)."""
     reg = raw.call(Op.REGISTER_RANK, fds=True, rank_id=0, local_rank=0, world_rank=0, gpu_id=0, numa_node=0,
                    pid=os.getpid() * 1000, capabilities=0)
@@ -125,8 +125,86 @@ def _session(raw: _Raw, run_dir: str) -> None:
     raw.call(Op.DROP_CANONICAL_VERSION, job=job, model_role=ROLL, model_version=1)
 
 
-def capture(binary: str = REF_DAEMON) -> list:
-    """Records of one session against the reference daemon at `binary`."""
+def _faults(raw: _Raw, run_dir: str, sock: str) -> None:
+    """Refusals and dedup decisions: a stale epoch after re-registration, an
+    invalid transition, an older version that must not win the location, DP
+    attach / TP distinct / wait-for-creator / duplicate candidates with a
+    mismatching hash, a seal missing a parameter, a pull of an unsealed
+    version, a restore of an unknown object."""
+    r1 = _Raw(sock, raw.records)  # a second rank on its own connection
+    reg = raw.call(Op.REGISTER_RANK, fds=True, rank_id=0, local_rank=0, world_rank=0, gpu_id=0, numa_node=0,
+                   pid=4242000, capabilities=0)
+    old = reg["rank_epoch"]
+    ep = raw.call(Op.REGISTER_RANK, fds=True, rank_id=0, local_rank=0, world_rank=0, gpu_id=0, numa_node=0,
+                  pid=4242001, capabilities=0)["rank_epoch"]
+    raw.call(Op.HEARTBEAT, rank_id=0, rank_epoch=old, timestamp_ns=1)  # the invalidated epoch
+    offload = dict(rank_id=0, gpu_id=0, numa_node=0, alignment=256, priority=0, flags=0, debug_name="")
+    raw.call(Op.REQUEST_OFFLOAD, rank_epoch=old, tensor_id=200, version=1, nbytes=4096, **offload)
+    g = raw.call(Op.REQUEST_OFFLOAD, rank_epoch=ep, tensor_id=200, version=2, nbytes=4096, **offload)
+    mark = dict(rank_id=0, rank_epoch=ep, lease_id=g["lease_id"], tensor_id=200, version=2, slot_id=g["slot_id"],
+                seq=1, timestamp_ns=1)
+    raw.call(Op.MARK_D2H_COMPLETE, **mark)  # complete before submitted
+    raw.call(Op.MARK_D2H_SUBMITTED, **mark)
+    raw.call(Op.MARK_D2H_COMPLETE, **mark)
+    g1 = raw.call(Op.REQUEST_OFFLOAD, rank_epoch=ep, tensor_id=200, version=1, nbytes=4096, **offload)
+    m1 = dict(mark, lease_id=g1["lease_id"], version=1, slot_id=g1["slot_id"])
+    raw.call(Op.MARK_D2H_SUBMITTED, **m1)
+    raw.call(Op.MARK_D2H_COMPLETE, **m1)  # an older version: not the latest
+    raw.call(Op.QUERY_LOCATION, tensor_id=200, version=0)
+    raw.call(Op.RELEASE_LEASE, rank_id=0, rank_epoch=ep, lease_id=g1["lease_id"], slot_id=g1["slot_id"],
+             reason="stale")
+    raw.call(Op.RELEASE_LEASE, rank_id=0, rank_epoch=ep, lease_id=g1["lease_id"], slot_id=g1["slot_id"],
+             reason="again")  # idempotent
+    e1 = r1.call(Op.REGISTER_RANK, fds=True, rank_id=1, local_rank=1, world_rank=1, gpu_id=0, numa_node=0,
+                 pid=4242002, capabilities=0)["rank_epoch"]
+    job = raw.call(Op.REGISTER_JOB, tenant_id=0, job_name="golden-dedup", scheduler_job_id=0, label_keys=[],
+                   label_values=[])["job"]
+    r1.call(Op.REGISTER_JOB, tenant_id=0, job_name="golden-dedup", scheduler_job_id=0, label_keys=[],
+            label_values=[])  # joins the live job
+
+    def key(pid, tp=0, nbytes=8192, version=1):
+        k = _wire.defaults("CanonicalKey")
+        k.update(job=job, model_role=ROLL, model_version=version, param_id=pid, param_fqn_hash=pid,
+                 param_fqn_debug=f"p{pid}", dtype=15, nbytes=nbytes, shard_nbytes=nbytes, tp_rank=tp, expert_id=-1)
+        return k
+
+    def evict(conn, rank, epoch, k, mode=1, dup=False):
+        return conn.call(Op.REQUEST_CANONICAL_EVICT, rank_id=rank, rank_epoch=epoch, key=k, destructive=False,
+                         attach_if_exists=True, create_if_missing=True, dedup_mode=mode,
+                         allow_duplicate_candidate=dup, alignment=256)
+
+    def finish(conn, rank, epoch, c, lo, hi, seq):
+        m = dict(rank_id=rank, rank_epoch=epoch, lease_id=c["lease_id"], tensor_id=c["synthetic_tid"], version=1,
+                 slot_id=c["slot_id"], seq=seq, timestamp_ns=1)
+        conn.call(Op.MARK_D2H_SUBMITTED, **m)
+        conn.call(Op.MARK_D2H_COMPLETE, **m)
+        return conn.call(Op.COMMIT_CANONICAL_OBJECT, rank_id=rank, rank_epoch=epoch, object_id=c["object_id"],
+                         lease_id=c["lease_id"], slot_id=c["slot_id"], content_hash_lo=lo, content_hash_hi=hi)
+
+    c = evict(raw, 0, ep, key(1))  # create
+    evict(r1, 1, e1, key(1))  # same identity while creating: wait for the creator
+    finish(raw, 0, ep, c, 11, 12, 2)
+    evict(r1, 1, e1, key(1))  # DP replica: attach
+    evict(r1, 1, e1, key(1, tp=1))  # another TP shard: a new object
+    h = evict(raw, 0, ep, key(2), mode=2)  # hash-verified create
+    finish(raw, 0, ep, h, 21, 22, 3)
+    d = evict(r1, 1, e1, key(2), mode=2, dup=True)  # candidate copy
+    finish(r1, 1, e1, d, 99, 98, 4)  # a different hash: refused
+    evict(raw, 0, ep, key(3, nbytes=4096, version=1))
+    raw.call(Op.SEAL_MODEL_VERSION, job=job, model_role=ROLL, model_version=1, fail_if_missing=True,
+             expected_param_ids=[1, 2, 3, 4], promote=False)  # parameter 4 was never recorded
+    raw.call(Op.GET_MANIFEST, job=job, model_role=ROLL, model_version=1, filter={})  # not sealed
+    raw.call(Op.PULL_TENSOR, job=job, model_role=ROLL, model_version=1, object_id=c["object_id"], transport=2,
+             target_descriptor=os.path.join(run_dir, "unsealed.bin"))
+    raw.call(Op.GET_LATEST_SEALED_VERSION, job=job, model_role=ROLL)
+    raw.call(Op.REQUEST_CANONICAL_RESTORE, rank_id=0, rank_epoch=ep, object_id=987654, gpu_id=0, numa_node=0)
+    raw.call(Op.DROP_CANONICAL_VERSION, job=job, model_role=ROLL, model_version=1)
+    r1.sock.close()
+
+
+def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
+    """Records of one scenario (`session` or `faults`) against the daemon at
+    `binary` (the reference's by default)."""
     run_dir = tempfile.mkdtemp(prefix="ssref-golden-")
     sock = os.path.join(run_dir, "d.sock")
     cfg = os.path.join(run_dir, "offloadd.yaml")
@@ -148,7 +226,7 @@ def capture(binary: str = REF_DAEMON) -> list:
         if not os.path.exists(sock):
             raise RuntimeError(f"reference offloadd did not start (log {log.name})")
         raw = _Raw(sock)
-        _session(raw, run_dir)
+        (_session if scenario == "session" else _faults)(raw, run_dir, sock)
         return raw.records
     finally:
         if raw is not None:
@@ -161,13 +239,13 @@ def capture(binary: str = REF_DAEMON) -> list:
         log.close()
 
 
-def _check(records: list) -> None:
+def _check(records: list, all_ok: bool = True) -> None:
     C = native()
     assert records, "empty capture"
     for r in records:
         req, resp = bytes.fromhex(r["request_hex"]), bytes.fromhex(r["response_hex"])
         what = f"{r['request']} -> {r['response']}"
-        assert r["ok"], f"the reference refused {what}"
+        assert r["ok"] or not all_ok, f"the reference refused {what}"
         # the reference's response bytes, through this repository's C++ codec and its Python mirror
         assert C.reencode(r["op"], True, resp) == resp, what
         assert _wire.encode(r["response"], _wire.decode(r["response"], resp)) == resp, what
@@ -178,39 +256,43 @@ def _check(records: list) -> None:
 
 def test_golden_capture_from_the_reference_round_trips():
     with open(GOLDEN) as f:
-        records = json.load(f)["records"]
-    ops = {r["op"] for r in records}
+        g = json.load(f)
+    ops = {r["op"] for r in g["records"]}
     assert set(range(1, 12)) | {13} | set(range(20, 31)) <= ops  # every opcode but Shutdown
-    _check(records)
+    _check(g["records"])
+    assert sum(not r["ok"] for r in g["faults"]) >= 8  # the refusals are in the capture
+    _check(g["faults"], all_ok=False)
 
 
 def test_live_capture_from_the_reference_round_trips():
     if not os.path.exists(REF_DAEMON):
         pytest.skip("reference build not present (python baseline/build_reference.py)")
     _check(capture())
+    _check(capture(scenario="faults"), all_ok=False)
 
 
 if __name__ == "__main__":
     if "--write" in sys.argv:
-        recs = capture()
+        recs, faults = capture(), capture(scenario="faults")
         os.makedirs(os.path.dirname(GOLDEN), exist_ok=True)
         with open(GOLDEN, "w") as f:
             json.dump({"source": "StateSpectre offloadd built from the reference sources (baseline/_ref/bin)",
-                       "records": recs}, f, indent=1)
-        print(f"wrote {len(recs)} records to {GOLDEN}")
+                       "records": recs, "faults": faults}, f, indent=1)
+        print(f"wrote {len(recs)} + {len(faults)} records to {GOLDEN}")
 
 
-def test_this_daemon_answers_the_session_as_the_reference_did():
-    """The same session against this repository's offloadd: every response
+@pytest.mark.parametrize("scenario", ["session", "faults"])
+def test_this_daemon_answers_as_the_reference_did(scenario):
+    """The same scenarios against this repository's offloadd: every response
     decodes to the reference's values field by field (epochs, slot and lease
-    numbers, arena offsets, job id, object ids, actions, manifest hash,
-    counts), apart from the FILE pull's path; GetStats carries every counter
-    name the reference reports."""
+    numbers, arena offsets, job id, object ids, actions, refusals and their
+    messages, manifest hash, counts), apart from the FILE pull's path;
+    GetStats carries every counter name the reference reports."""
     from statespectre_b200._native import bin_path
 
-    ours = capture(bin_path("offloadd"))
+    ours = capture(bin_path("offloadd"), scenario=scenario)
     with open(GOLDEN) as f:
-        ref = json.load(f)["records"]
+        ref = json.load(f)["records" if scenario == "session" else "faults"]
     assert [r["op"] for r in ours] == [r["op"] for r in ref]
     for a, b in zip(ref, ours):
         da = _wire.decode(a["response"], bytes.fromhex(a["response_hex"]))
