@@ -518,10 +518,12 @@ RequestPrefetchResponse Daemon::do_request_prefetch(const RequestPrefetchRequest
             uint32_t st = state_of(EL->base);
             if (st == OFLD_SLOT_READBACK_IN_FLIGHT || st == OFLD_SLOT_PINNED_VALID) {
                 fill(EL->id, EL->base, st);
-                if (st == OFLD_SLOT_PINNED_VALID)
+                if (st == OFLD_SLOT_PINNED_VALID) {
                     mark_ready(*EL);
-                else
+                    resp.message = "ready";  // StateSpectre's text for a landed readback
+                } else {
                     resp.message = "readback in flight";
+                }
                 return resp;
             }
         }

@@ -1,12 +1,15 @@
 """Wire golden vectors captured from StateSpectre's own daemon.
 
 ``capture()`` starts the reference's ``offloadd`` (built offline in
-``baseline/_ref`` by baseline/build_reference.py), walks it through a session
-over a raw socket (register, heartbeat, the v1 evict / restore state machine,
+``baseline/_ref`` by baseline/build_reference.py), walks it through one of
+four scenarios over raw sockets and records every request body this
+repository encoded and every response body the reference's codec encoded:
+``session`` (register, heartbeat, the v1 evict / restore state machine,
 location, stats, a job, a canonical object, seal, manifest, FILE pull,
-canonical restore, release, drop, batch completion) and records every request
-body this repository encoded and every response body the reference's codec
-encoded. The capture is committed as ``tests/golden/reference_wire.json``:
+canonical restore, release, drop, batch completion), ``faults`` (refusals and
+dedup decisions), ``pageable`` and ``nvme`` (drain on completion, readback,
+restore from the cold tier). The capture is committed as
+``tests/golden/reference_wire.json``:
 
   * the reference answered every captured request with ok, so it decoded what
     this repository's codec wrote;
@@ -14,7 +17,8 @@ encoded. The capture is committed as ``tests/golden/reference_wire.json``:
     reference response and re-encode it to the same bytes.
 
 The round trips over the committed file run everywhere; with the reference
-build present, a fresh capture is checked the same way. Regenerate the file
+build present, a fresh capture is checked the same way. The same scenarios
+run against this repository's offloadd must answer as the reference did. Regenerate the file
 with ``python tests/test_reference_wire_capture.py --write``.
 """
 
@@ -202,20 +206,88 @@ def _faults(raw: _Raw, run_dir: str, sock: str) -> None:
     r1.sock.close()
 
 
+SCENARIOS = ("session", "faults", "pageable", "nvme")
+
+
+def _tiers(raw: _Raw, run_dir: str, sock: str) -> None:
+    """A tensor drained to the cold tier on completion (pageable memory, or
+    NVMe files), read back by a prefetch and restored without keeping the
+    pinned copy; a canonical object created beside it (not drained: it was
+    still being created when its copy completed) is sealed, listed and pulled.
+    Polls run on a
+    connection whose records are dropped (their count depends on timing)."""
+    poll = _Raw(sock)
+
+    def wait(op, pred, **kw):
+        deadline = time.time() + 20
+        while time.time() < deadline:
+            r = poll.call(op, **kw)
+            if pred(r):
+                return
+            time.sleep(0.01)
+        raise TimeoutError(f"{op} never reached the wanted state")
+
+    ep = raw.call(Op.REGISTER_RANK, fds=True, rank_id=0, local_rank=0, world_rank=0, gpu_id=0, numa_node=0,
+                  pid=5151000, capabilities=0)["rank_epoch"]
+    g = raw.call(Op.REQUEST_OFFLOAD, rank_id=0, rank_epoch=ep, tensor_id=300, version=1, nbytes=3 << 20, gpu_id=0,
+                 numa_node=0, alignment=256, priority=0, flags=0, debug_name="kv.0")
+    mark = dict(rank_id=0, rank_epoch=ep, lease_id=g["lease_id"], tensor_id=300, version=1, slot_id=g["slot_id"],
+                seq=1, timestamp_ns=1)
+    raw.call(Op.MARK_D2H_SUBMITTED, **mark)
+    raw.call(Op.MARK_D2H_COMPLETE, **mark)
+    wait(Op.QUERY_LOCATION, lambda r: r["location_kind"] in (2, 3), tensor_id=300, version=1)
+    time.sleep(0.3)  # the drain's bookkeeping settles after the location flips
+    raw.call(Op.QUERY_LOCATION, tensor_id=300, version=1)
+    pre = dict(rank_id=0, rank_epoch=ep, tensor_id=300, version=1, nbytes=3 << 20, gpu_id=0, numa_node=0,
+               priority=0, flags=0)
+    wait(Op.REQUEST_PREFETCH, lambda r: r["ready"], **pre)
+    p = raw.call(Op.REQUEST_PREFETCH, **pre)  # the readback's lease, handed back again
+    hmark = dict(mark, lease_id=p["lease_id"], slot_id=p["slot_id"], seq=2)
+    raw.call(Op.MARK_H2D_SUBMITTED, **hmark)
+    raw.call(Op.MARK_H2D_COMPLETE, **hmark, keep_pinned=False)
+    raw.call(Op.QUERY_LOCATION, tensor_id=300, version=1)
+    job = raw.call(Op.REGISTER_JOB, tenant_id=0, job_name="golden-tiers", scheduler_job_id=0, label_keys=[],
+                   label_values=[])["job"]
+    key = _wire.defaults("CanonicalKey")
+    key.update(job=job, model_role=ROLL, model_version=1, param_id=9, param_fqn_hash=9, param_fqn_debug="w9",
+               dtype=15, nbytes=1 << 20, shard_nbytes=1 << 20, expert_id=-1)
+    c = raw.call(Op.REQUEST_CANONICAL_EVICT, rank_id=0, rank_epoch=ep, key=key, destructive=False,
+                 attach_if_exists=True, create_if_missing=True, dedup_mode=1, alignment=256)
+    cm = dict(mark, lease_id=c["lease_id"], tensor_id=c["synthetic_tid"], slot_id=c["slot_id"], seq=3)
+    raw.call(Op.MARK_D2H_SUBMITTED, **cm)
+    raw.call(Op.MARK_D2H_COMPLETE, **cm)
+    raw.call(Op.COMMIT_CANONICAL_OBJECT, rank_id=0, rank_epoch=ep, object_id=c["object_id"], lease_id=c["lease_id"],
+             slot_id=c["slot_id"], content_hash_lo=5, content_hash_hi=6)
+    raw.call(Op.SEAL_MODEL_VERSION, job=job, model_role=ROLL, model_version=1, fail_if_missing=True,
+             expected_param_ids=[], promote=True)
+    raw.call(Op.GET_MANIFEST, job=job, model_role=ROLL, model_version=1, filter={})
+    raw.call(Op.PULL_TENSOR, job=job, model_role=ROLL, model_version=1, object_id=c["object_id"], transport=2,
+             target_descriptor=os.path.join(run_dir, "cold.bin"))
+    raw.call(Op.DROP_CANONICAL_VERSION, job=job, model_role=ROLL, model_version=1)
+    raw.call(Op.RELEASE_LEASE, rank_id=0, rank_epoch=ep, lease_id=p["lease_id"], slot_id=p["slot_id"],
+             reason="done")
+    poll.sock.close()
+
+
 def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
-    """Records of one scenario (`session` or `faults`) against the daemon at
+    """Records of one scenario (one of SCENARIOS) against the daemon at
     `binary` (the reference's by default)."""
     run_dir = tempfile.mkdtemp(prefix="ssref-golden-")
     sock = os.path.join(run_dir, "d.sock")
     cfg = os.path.join(run_dir, "offloadd.yaml")
+    tiers = scenario in ("pageable", "nvme")
+    nvme = ["  enabled: false"] if scenario != "nvme" else [
+        "  enabled: true", f"  path: {os.path.join(run_dir, 'nvme')}", "  io_engine: pwrite", "  direct_io: false"]
+    if scenario == "nvme":
+        os.makedirs(os.path.join(run_dir, "nvme"))
     with open(cfg, "w") as f:
         f.write("\n".join([
             "daemon:", f"  socket_path: {sock}", f"  control_shm_name: /ssref_golden_{os.getpid()}",
             "  heartbeat_timeout_ms: 60000", "arenas:", "  allocation_granularity_mb: 2", "  per_numa:",
             "    - numa_node: 0", "      size_gb: 1", "      overflow_gb: 0", "      gpu_windows:",
             "        - gpu: 0", "          size_gb: 1",
-            "drain_policy:", "  target_tier: pageable", "  drain_on_d2h_complete: false", "nvme:",
-            "  enabled: false"]) + "\n")
+            "drain_policy:", f"  target_tier: {'nvme' if scenario == 'nvme' else 'pageable'}",
+            f"  drain_on_d2h_complete: {'true' if tiers else 'false'}", "nvme:"] + nvme) + "\n")
     log = open(os.path.join(run_dir, "offloadd.log"), "w")
     proc = subprocess.Popen([binary, "--config", cfg, "--socket", sock], stdout=log, stderr=log)
     raw = None
@@ -226,7 +298,7 @@ def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
         if not os.path.exists(sock):
             raise RuntimeError(f"reference offloadd did not start (log {log.name})")
         raw = _Raw(sock)
-        (_session if scenario == "session" else _faults)(raw, run_dir, sock)
+        {"session": _session, "faults": _faults}.get(scenario, _tiers)(raw, run_dir, sock)
         return raw.records
     finally:
         if raw is not None:
@@ -262,26 +334,29 @@ def test_golden_capture_from_the_reference_round_trips():
     _check(g["records"])
     assert sum(not r["ok"] for r in g["faults"]) >= 8  # the refusals are in the capture
     _check(g["faults"], all_ok=False)
+    _check(g["pageable"])
+    _check(g["nvme"])
 
 
 def test_live_capture_from_the_reference_round_trips():
     if not os.path.exists(REF_DAEMON):
         pytest.skip("reference build not present (python baseline/build_reference.py)")
-    _check(capture())
-    _check(capture(scenario="faults"), all_ok=False)
+    for sc in SCENARIOS:
+        _check(capture(scenario=sc), all_ok=sc != "faults")
 
 
 if __name__ == "__main__":
     if "--write" in sys.argv:
-        recs, faults = capture(), capture(scenario="faults")
+        out = {"source": "StateSpectre offloadd built from the reference sources (baseline/_ref/bin)"}
+        for sc in SCENARIOS:
+            out["records" if sc == "session" else sc] = capture(scenario=sc)
         os.makedirs(os.path.dirname(GOLDEN), exist_ok=True)
         with open(GOLDEN, "w") as f:
-            json.dump({"source": "StateSpectre offloadd built from the reference sources (baseline/_ref/bin)",
-                       "records": recs, "faults": faults}, f, indent=1)
-        print(f"wrote {len(recs)} + {len(faults)} records to {GOLDEN}")
+            json.dump(out, f, indent=1)
+        print(f"wrote {', '.join(f'{k}: {len(v)}' for k, v in out.items() if k != 'source')} records to {GOLDEN}")
 
 
-@pytest.mark.parametrize("scenario", ["session", "faults"])
+@pytest.mark.parametrize("scenario", SCENARIOS)
 def test_this_daemon_answers_as_the_reference_did(scenario):
     """The same scenarios against this repository's offloadd: every response
     decodes to the reference's values field by field (epochs, slot and lease
@@ -292,7 +367,7 @@ def test_this_daemon_answers_as_the_reference_did(scenario):
 
     ours = capture(bin_path("offloadd"), scenario=scenario)
     with open(GOLDEN) as f:
-        ref = json.load(f)["records" if scenario == "session" else "faults"]
+        ref = json.load(f)["records" if scenario == "session" else scenario]
     assert [r["op"] for r in ours] == [r["op"] for r in ref]
     for a, b in zip(ref, ours):
         da = _wire.decode(a["response"], bytes.fromhex(a["response_hex"]))
