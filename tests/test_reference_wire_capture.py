@@ -206,7 +206,7 @@ def _faults(raw: _Raw, run_dir: str, sock: str) -> None:
     r1.sock.close()
 
 
-SCENARIOS = ("session", "faults", "pageable", "nvme")
+SCENARIOS = ("session", "faults", "pageable", "nvme", "crash")
 
 
 def _tiers(raw: _Raw, run_dir: str, sock: str) -> None:
@@ -269,6 +269,40 @@ def _tiers(raw: _Raw, run_dir: str, sock: str) -> None:
     poll.sock.close()
 
 
+def _crash(raw: _Raw, run_dir: str, sock: str) -> None:
+    """A rank that stops heartbeating with one tensor offloaded and another
+    still in flight, and closes its connection: after the heartbeat timeout
+    (300 ms here) its epoch is refused, the completed tensor survives in
+    pinned memory, the in-flight reservation is gone and its slots are
+    reused, and the restarted rank restores the survivor."""
+    first = _Raw(sock, raw.records)
+    ep = first.call(Op.REGISTER_RANK, fds=True, rank_id=0, local_rank=0, world_rank=0, gpu_id=0, numa_node=0,
+                    pid=6161000, capabilities=0)["rank_epoch"]
+    off = dict(rank_id=0, gpu_id=0, numa_node=0, alignment=256, priority=0, flags=0, debug_name="")
+    a = first.call(Op.REQUEST_OFFLOAD, rank_epoch=ep, tensor_id=400, version=1, nbytes=1 << 20, **off)
+    ma = dict(rank_id=0, rank_epoch=ep, lease_id=a["lease_id"], tensor_id=400, version=1, slot_id=a["slot_id"],
+              seq=1, timestamp_ns=1)
+    first.call(Op.MARK_D2H_SUBMITTED, **ma)
+    first.call(Op.MARK_D2H_COMPLETE, **ma)
+    b = first.call(Op.REQUEST_OFFLOAD, rank_epoch=ep, tensor_id=401, version=1, nbytes=1 << 20, **off)
+    first.call(Op.MARK_D2H_SUBMITTED, **dict(ma, lease_id=b["lease_id"], tensor_id=401, slot_id=b["slot_id"]))
+    first.sock.close()  # the rank dies: no more heartbeats
+    time.sleep(1.5)
+    raw.call(Op.HEARTBEAT, rank_id=0, rank_epoch=ep, timestamp_ns=2)
+    raw.call(Op.QUERY_LOCATION, tensor_id=400, version=1)
+    raw.call(Op.QUERY_LOCATION, tensor_id=401, version=1)
+    ep2 = raw.call(Op.REGISTER_RANK, fds=True, rank_id=0, local_rank=0, world_rank=0, gpu_id=0, numa_node=0,
+                   pid=6161001, capabilities=0)["rank_epoch"]
+    raw.call(Op.REQUEST_OFFLOAD, rank_epoch=ep2, tensor_id=402, version=1, nbytes=1 << 20, **off)
+    p = raw.call(Op.REQUEST_PREFETCH, rank_id=0, rank_epoch=ep2, tensor_id=400, version=1, nbytes=1 << 20,
+                 gpu_id=0, numa_node=0, priority=0, flags=0)
+    hm = dict(rank_id=0, rank_epoch=ep2, lease_id=p["lease_id"], tensor_id=400, version=1, slot_id=p["slot_id"],
+              seq=2, timestamp_ns=3)
+    raw.call(Op.MARK_H2D_SUBMITTED, **hm)
+    raw.call(Op.MARK_H2D_COMPLETE, **hm, keep_pinned=True)
+    raw.call(Op.MARK_D2H_COMPLETE, **dict(ma, lease_id=b["lease_id"], tensor_id=401, slot_id=b["slot_id"]))
+
+
 def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
     """Records of one scenario (one of SCENARIOS) against the daemon at
     `binary` (the reference's by default)."""
@@ -283,7 +317,8 @@ def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
     with open(cfg, "w") as f:
         f.write("\n".join([
             "daemon:", f"  socket_path: {sock}", f"  control_shm_name: /ssref_golden_{os.getpid()}",
-            "  heartbeat_timeout_ms: 60000", "arenas:", "  allocation_granularity_mb: 2", "  per_numa:",
+            f"  heartbeat_timeout_ms: {300 if scenario == 'crash' else 60000}", "arenas:",
+            "  allocation_granularity_mb: 2", "  per_numa:",
             "    - numa_node: 0", "      size_gb: 1", "      overflow_gb: 0", "      gpu_windows:",
             "        - gpu: 0", "          size_gb: 1",
             "drain_policy:", f"  target_tier: {'nvme' if scenario == 'nvme' else 'pageable'}",
@@ -298,7 +333,7 @@ def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
         if not os.path.exists(sock):
             raise RuntimeError(f"reference offloadd did not start (log {log.name})")
         raw = _Raw(sock)
-        {"session": _session, "faults": _faults}.get(scenario, _tiers)(raw, run_dir, sock)
+        {"session": _session, "faults": _faults, "crash": _crash}.get(scenario, _tiers)(raw, run_dir, sock)
         return raw.records
     finally:
         if raw is not None:
@@ -336,13 +371,14 @@ def test_golden_capture_from_the_reference_round_trips():
     _check(g["faults"], all_ok=False)
     _check(g["pageable"])
     _check(g["nvme"])
+    _check(g["crash"], all_ok=False)
 
 
 def test_live_capture_from_the_reference_round_trips():
     if not os.path.exists(REF_DAEMON):
         pytest.skip("reference build not present (python baseline/build_reference.py)")
     for sc in SCENARIOS:
-        _check(capture(scenario=sc), all_ok=sc != "faults")
+        _check(capture(scenario=sc), all_ok=sc not in ("faults", "crash"))
 
 
 if __name__ == "__main__":
@@ -354,6 +390,14 @@ if __name__ == "__main__":
         with open(GOLDEN, "w") as f:
             json.dump(out, f, indent=1)
         print(f"wrote {', '.join(f'{k}: {len(v)}' for k, v in out.items() if k != 'source')} records to {GOLDEN}")
+
+
+# Deliberate departures, per scenario: (response, field). After a heartbeat
+# timeout StateSpectre never frees the dead session's completion ring (its
+# re-registration path returns early for a session already marked dead:
+# src/daemon/daemon.cpp:725), so the restarted rank gets the next ring and the
+# old one is lost for good; this daemon frees it and hands it out again.
+DEPARTURES = {"crash": {("RegisterRankResponse", "ring_index")}}
 
 
 @pytest.mark.parametrize("scenario", SCENARIOS)
@@ -377,4 +421,8 @@ def test_this_daemon_answers_as_the_reference_did(scenario):
             continue
         da.pop("transport_metadata", None)
         db.pop("transport_metadata", None)
+        for resp, field in DEPARTURES.get(scenario, ()):
+            if a["response"] == resp:
+                da.pop(field, None)
+                db.pop(field, None)
         assert da == db, (a["request"], {k: (da[k], db.get(k)) for k in da if da[k] != db.get(k)})
