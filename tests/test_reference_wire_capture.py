@@ -8,7 +8,9 @@ repository encoded and every response body the reference's codec encoded:
 location, stats, a job, a canonical object, seal, manifest, FILE pull,
 canonical restore, release, drop, batch completion), ``faults`` (refusals and
 dedup decisions), ``pageable`` and ``nvme`` (drain on completion, readback,
-restore from the cold tier). The capture is committed as
+restore from the cold tier), ``crash`` (heartbeat timeout and restart) and
+``versions`` (retention, shared objects released holder by holder, the
+pinned quota). The capture is committed as
 ``tests/golden/reference_wire.json``:
 
   * the reference answered every captured request with ok, so it decoded what
@@ -206,7 +208,7 @@ def _faults(raw: _Raw, run_dir: str, sock: str) -> None:
     r1.sock.close()
 
 
-SCENARIOS = ("session", "faults", "pageable", "nvme", "crash")
+SCENARIOS = ("session", "faults", "pageable", "nvme", "crash", "versions")
 
 
 def _tiers(raw: _Raw, run_dir: str, sock: str) -> None:
@@ -303,6 +305,54 @@ def _crash(raw: _Raw, run_dir: str, sock: str) -> None:
     raw.call(Op.MARK_D2H_COMPLETE, **dict(ma, lease_id=b["lease_id"], tensor_id=401, slot_id=b["slot_id"]))
 
 
+def _versions(raw: _Raw, run_dir: str, sock: str) -> None:
+    """Sealed-version retention (2 kept), objects shared by two ranks and
+    released one holder at a time, and the per-job pinned quota (3 MiB)."""
+    r1 = _Raw(sock, raw.records)
+    reg = dict(local_rank=0, world_rank=0, gpu_id=0, numa_node=0, capabilities=0)
+    ep = raw.call(Op.REGISTER_RANK, fds=True, rank_id=0, pid=7171000, **reg)["rank_epoch"]
+    e1 = r1.call(Op.REGISTER_RANK, fds=True, rank_id=1, pid=7171001, **reg)["rank_epoch"]
+    jobreq = dict(tenant_id=0, job_name="golden-versions", scheduler_job_id=0, label_keys=[], label_values=[])
+    job = raw.call(Op.REGISTER_JOB, **jobreq)["job"]
+    r1.call(Op.REGISTER_JOB, **jobreq)
+
+    def key(version, pid=1, nbytes=1 << 20):
+        k = _wire.defaults("CanonicalKey")
+        k.update(job=job, model_role=ROLL, model_version=version, param_id=pid, param_fqn_hash=pid,
+                 param_fqn_debug=f"w{pid}", dtype=15, nbytes=nbytes, shard_nbytes=nbytes, expert_id=-1)
+        return k
+
+    def evict(conn, rank, epoch, k):
+        return conn.call(Op.REQUEST_CANONICAL_EVICT, rank_id=rank, rank_epoch=epoch, key=k, destructive=False,
+                         attach_if_exists=True, create_if_missing=True, dedup_mode=1, alignment=256)
+
+    objs = {}
+    for v in (1, 2, 3):
+        c = evict(raw, 0, ep, key(v))
+        m = dict(rank_id=0, rank_epoch=ep, lease_id=c["lease_id"], tensor_id=c["synthetic_tid"], version=1,
+                 slot_id=c["slot_id"], seq=v, timestamp_ns=1)
+        raw.call(Op.MARK_D2H_SUBMITTED, **m)
+        raw.call(Op.MARK_D2H_COMPLETE, **m)
+        raw.call(Op.COMMIT_CANONICAL_OBJECT, rank_id=0, rank_epoch=ep, object_id=c["object_id"],
+                 lease_id=c["lease_id"], slot_id=c["slot_id"], content_hash_lo=v, content_hash_hi=v)
+        if v == 3:
+            evict(r1, 1, e1, key(v))  # a second holder of the newest object
+        raw.call(Op.SEAL_MODEL_VERSION, job=job, model_role=ROLL, model_version=v, fail_if_missing=True,
+                 expected_param_ids=[], promote=True)
+        objs[v] = c["object_id"]
+    for v in (1, 2, 3):  # the oldest was retired by retention
+        raw.call(Op.GET_MANIFEST, job=job, model_role=ROLL, model_version=v, filter={})
+    raw.call(Op.GET_LATEST_SEALED_VERSION, job=job, model_role=ROLL)
+    evict(raw, 0, ep, key(4, pid=2, nbytes=4 << 20))  # over the job's pinned quota
+    rel = dict(job=job, model_role=ROLL, model_version=3, object_id=objs[3])
+    raw.call(Op.RELEASE_CANONICAL, rank_id=0, rank_epoch=ep, **rel)
+    r1.call(Op.RELEASE_CANONICAL, rank_id=1, rank_epoch=e1, **rel)
+    raw.call(Op.RELEASE_CANONICAL, rank_id=0, rank_epoch=ep, **rel)  # nothing left to release
+    raw.call(Op.DROP_CANONICAL_VERSION, job=job, model_role=ROLL, model_version=2)
+    raw.call(Op.DROP_CANONICAL_VERSION, job=job, model_role=ROLL, model_version=3)
+    r1.sock.close()
+
+
 def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
     """Records of one scenario (one of SCENARIOS) against the daemon at
     `binary` (the reference's by default)."""
@@ -322,7 +372,9 @@ def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
             "    - numa_node: 0", "      size_gb: 1", "      overflow_gb: 0", "      gpu_windows:",
             "        - gpu: 0", "          size_gb: 1",
             "drain_policy:", f"  target_tier: {'nvme' if scenario == 'nvme' else 'pageable'}",
-            f"  drain_on_d2h_complete: {'true' if tiers else 'false'}", "nvme:"] + nvme) + "\n")
+            f"  drain_on_d2h_complete: {'true' if tiers else 'false'}", "nvme:"] + nvme +
+            (["manifest:", "  retain_sealed_versions: 2", "quotas:", "  default:", "    max_pinned_bytes: 3MiB"]
+             if scenario == "versions" else [])) + "\n")
     log = open(os.path.join(run_dir, "offloadd.log"), "w")
     proc = subprocess.Popen([binary, "--config", cfg, "--socket", sock], stdout=log, stderr=log)
     raw = None
@@ -333,7 +385,8 @@ def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
         if not os.path.exists(sock):
             raise RuntimeError(f"reference offloadd did not start (log {log.name})")
         raw = _Raw(sock)
-        {"session": _session, "faults": _faults, "crash": _crash}.get(scenario, _tiers)(raw, run_dir, sock)
+        {"session": _session, "faults": _faults, "crash": _crash, "versions": _versions}.get(
+            scenario, _tiers)(raw, run_dir, sock)
         return raw.records
     finally:
         if raw is not None:
@@ -372,13 +425,14 @@ def test_golden_capture_from_the_reference_round_trips():
     _check(g["pageable"])
     _check(g["nvme"])
     _check(g["crash"], all_ok=False)
+    _check(g["versions"], all_ok=False)
 
 
 def test_live_capture_from_the_reference_round_trips():
     if not os.path.exists(REF_DAEMON):
         pytest.skip("reference build not present (python baseline/build_reference.py)")
     for sc in SCENARIOS:
-        _check(capture(scenario=sc), all_ok=sc not in ("faults", "crash"))
+        _check(capture(scenario=sc), all_ok=sc not in ("faults", "crash", "versions"))
 
 
 if __name__ == "__main__":
