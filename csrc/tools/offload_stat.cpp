@@ -6,6 +6,9 @@
 // --jobs prints the per-job accounting table (an addition of this runtime).
 #include <unistd.h>
 
+#include <sys/socket.h>
+#include <sys/time.h>
+
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -69,13 +72,23 @@ std::pair<std::string, std::string> split_scope(const std::string& key) {
     return {name, labels};
 }
 
-// One TYPE line per metric family; scoped keys become labelled samples.
+// Exposition of StateSpectre's offload-stat, so its dashboards keep working:
+// `offload_<key>`, a HELP line "offload daemon metric <key>", and gauges for
+// levels (names with "bytes", used_ / inflight_ / draining_ prefixes, the
+// bandwidth percentiles), counters for everything else.
+bool prom_gauge(const std::string& key) {
+    auto has = [&](const char* s) { return key.find(s) != std::string::npos; };
+    auto starts = [&](const char* s) { return key.rfind(s, 0) == 0; };
+    return has("bytes") || starts("used_") || starts("inflight_") || starts("draining_") || has("bandwidth_mbps");
+}
+
+// One HELP and TYPE line per metric family; scoped keys become labelled samples.
 void print_prometheus(const GetStatsResponse& r, const GetJobStatsResponse* jobs) {
     std::map<std::string, std::vector<std::pair<std::string, uint64_t>>> fams;
     std::vector<std::string> order;
     for (const StatEntry& e : r.stats) {
         auto nl = split_scope(e.key);
-        const std::string name = "offloadd_" + nl.first;
+        const std::string name = "offload_" + nl.first;
         if (!fams.count(name)) order.push_back(name);
         fams[name].push_back({nl.second, e.value});
     }
@@ -84,13 +97,13 @@ void print_prometheus(const GetStatsResponse& r, const GetJobStatsResponse* jobs
             const std::string l = "job=\"" + j.job.job_name + "\",job_id=\"" + std::to_string(j.job.job_id) +
                                   "\",tenant=\"" + std::to_string(j.job.tenant_id) + "\"";
             const std::pair<const char*, uint64_t> vals[] = {
-                {"offloadd_job_pinned_bytes", j.pinned_bytes},
-                {"offloadd_job_pageable_bytes", j.pageable_bytes},
-                {"offloadd_job_nvme_bytes", j.nvme_bytes},
-                {"offloadd_job_inflight_d2h_bytes", j.inflight_d2h_bytes},
-                {"offloadd_job_inflight_export_bytes", j.inflight_export_bytes},
-                {"offloadd_job_canonical_objects", j.canonical_object_count},
-                {"offloadd_job_dedup_bytes_saved", j.dedup_bytes_saved}};
+                {"offload_job_pinned_bytes", j.pinned_bytes},
+                {"offload_job_pageable_bytes", j.pageable_bytes},
+                {"offload_job_nvme_bytes", j.nvme_bytes},
+                {"offload_job_inflight_d2h_bytes", j.inflight_d2h_bytes},
+                {"offload_job_inflight_export_bytes", j.inflight_export_bytes},
+                {"offload_job_canonical_objects", j.canonical_object_count},
+                {"offload_job_dedup_bytes_saved", j.dedup_bytes_saved}};
             for (const auto& v : vals) {
                 if (!fams.count(v.first)) order.push_back(v.first);
                 fams[v.first].push_back({l, v.second});
@@ -98,8 +111,9 @@ void print_prometheus(const GetStatsResponse& r, const GetJobStatsResponse* jobs
         }
     }
     for (const std::string& name : order) {
-        const bool counter = name.size() > 6 && name.compare(name.size() - 6, 6, "_total") == 0;
-        std::printf("# TYPE %s %s\n", name.c_str(), counter ? "counter" : "gauge");
+        const std::string key = name.substr(8);  // after "offload_"
+        std::printf("# HELP %s offload daemon metric %s\n", name.c_str(), key.c_str());
+        std::printf("# TYPE %s %s\n", name.c_str(), prom_gauge(key) ? "gauge" : "counter");
         for (const auto& sample : fams[name]) {
             if (sample.first.empty())
                 std::printf("%s %llu\n", name.c_str(), (unsigned long long)sample.second);
@@ -156,14 +170,35 @@ int main(int argc, char** argv) {
             std::printf("%s\n", r.message.c_str());
             return r.ok ? 0 : 1;
         }
+        // Per-job labels for the Prometheus output come from an additive
+        // opcode: StateSpectre's own daemon logs it as unknown and never
+        // answers, so ask on a second connection that gives up after 2 s and
+        // print the daemon-wide counters alone then.
+        auto job_stats = [&](GetJobStatsResponse* out) -> bool {
+            try {
+                int fd2 = !tcp.empty() ? tcp_connect(tcp.substr(0, tcp.rfind(':')),
+                                                     uint16_t(std::stoi(tcp.substr(tcp.rfind(':') + 1))), 3000)
+                                       : uds_connect(sock, 3000);
+                timeval tv{2, 0};
+                ::setsockopt(fd2, SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof(tv));
+                RpcClient c2(fd2);
+                *out = c2.call<Op::kGetJobStats>(GetJobStatsRequest{});
+                return out->ok;
+            } catch (const std::exception&) {
+                return false;
+            }
+        };
         do {
             if (jobs) {
-                print_jobs(c.call<Op::kGetJobStats>(GetJobStatsRequest{}));
+                GetJobStatsResponse js;
+                if (!job_stats(&js)) throw std::runtime_error("the daemon does not answer GetJobStats (opcode 44)");
+                print_jobs(js);
             } else {
                 GetStatsResponse r = c.call<Op::kGetStats>(GetStatsRequest{});
                 if (prom) {
-                    GetJobStatsResponse js = c.call<Op::kGetJobStats>(GetJobStatsRequest{});
-                    print_prometheus(r, js.ok ? &js : nullptr);
+                    GetJobStatsResponse js;
+                    const bool have_jobs = job_stats(&js);
+                    print_prometheus(r, have_jobs ? &js : nullptr);
                 } else {
                     print_table(r);
                 }

@@ -171,8 +171,8 @@ def test_offload_stat_cli(tmp_path):
         assert "d2h_bytes" in out and "canonical_objects_created_total" in out
         prom = subprocess.run([bin_path("offload-stat"), "--socket", sock, "--prometheus"], capture_output=True,
                               text=True, check=True).stdout
-        assert "# TYPE offloadd_jobs_registered_total counter" in prom
-        assert "offloadd_used_pinned_bytes 0" in prom
+        assert "# TYPE offload_jobs_registered_total counter" in prom
+        assert "offload_used_pinned_bytes 0" in prom
         # labelled series: one family per metric, a sample per GPU window and per job
         import torch
 
@@ -182,10 +182,10 @@ def test_offload_stat_cli(tmp_path):
             off.copy(torch.randn(300000), wait=True)
             prom = subprocess.run([bin_path("offload-stat"), "--socket", sock, "--prometheus"],
                                   capture_output=True, text=True, check=True).stdout
-        assert prom.count("# TYPE offloadd_window_used_bytes gauge") == 1
-        assert 'offloadd_window_used_bytes{gpu="0"}' in prom
-        assert 'offloadd_gpu_live_sessions' not in prom
-        assert 'job="prom-job"' in prom and "# TYPE offloadd_job_pinned_bytes gauge" in prom
+        assert prom.count("# TYPE offload_window_used_bytes gauge") == 1
+        assert 'offload_window_used_bytes{gpu="0"}' in prom
+        assert 'offload_gpu_live_sessions' not in prom
+        assert 'job="prom-job"' in prom and "# TYPE offload_job_pinned_bytes gauge" in prom
         jobs = subprocess.run([bin_path("offload-stat"), "--socket", sock, "--jobs"], capture_output=True, text=True,
                               check=True).stdout
         assert "job_id" in jobs

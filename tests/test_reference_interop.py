@@ -157,3 +157,48 @@ def test_this_agent_records_and_pulls_through_the_reference_daemon(tmp_path):
         except subprocess.TimeoutExpired:
             proc.kill()
         log.close()
+
+
+def test_offload_stat_prometheus_matches_the_reference_tool(tmp_path):
+    """Dashboards built on StateSpectre's `offload-stat --prometheus` keep
+    working: against StateSpectre's own daemon, every HELP and TYPE line and
+    every sample the reference's tool prints, this repository's tool prints
+    too (its per-job series, which need an opcode that daemon lacks, are left
+    out within 2 s instead of hanging)."""
+    import subprocess
+    import time
+
+    from statespectre_b200._native import bin_path
+
+    ref_bin = os.path.join(ROOT, "baseline", "_ref", "bin")
+    if not os.path.exists(os.path.join(ref_bin, "offload-stat")):
+        pytest.skip("reference build not present (python baseline/build_reference.py)")
+    sock = str(tmp_path / "d.sock")
+    cfg = tmp_path / "offloadd.yaml"
+    cfg.write_text("\n".join([
+        "daemon:", f"  socket_path: {sock}", f"  control_shm_name: /ofld_stat_{os.getpid()}",
+        "arenas:", "  allocation_granularity_mb: 2", "  per_numa:", "    - numa_node: 0", "      size_gb: 1",
+        "      overflow_gb: 0", "      gpu_windows:", "        - gpu: 0", "          size_gb: 1",
+        "nvme:", "  enabled: false"]) + "\n")
+    log = open(tmp_path / "ref.log", "w")
+    proc = subprocess.Popen([os.path.join(ref_bin, "offloadd"), "--config", str(cfg), "--socket", sock],
+                            stdout=log, stderr=log)
+    try:
+        deadline = time.time() + 30
+        while not os.path.exists(sock) and time.time() < deadline and proc.poll() is None:
+            time.sleep(0.05)
+        ref = subprocess.run([os.path.join(ref_bin, "offload-stat"), "--socket", sock, "--prometheus"],
+                             capture_output=True, text=True, timeout=30, check=True).stdout.splitlines()
+        ours = subprocess.run([bin_path("offload-stat"), "--socket", sock, "--prometheus"],
+                              capture_output=True, text=True, timeout=30, check=True).stdout.splitlines()
+        assert len(ref) > 100
+        mine = set(ours)
+        missing = [line for line in ref if line not in mine]
+        assert not missing, missing[:10]
+    finally:
+        proc.terminate()
+        try:
+            proc.wait(timeout=30)
+        except subprocess.TimeoutExpired:
+            proc.kill()
+        log.close()
