@@ -386,8 +386,8 @@ def recv_frame(sock: socket.socket) -> Tuple[int, bytes]:
     return op, recv_exact(sock, n) if n else b""
 
 
-def parse_export_header(data: bytes) -> dict:
-    magic, ver, oid, nbytes, hlo, hhi = EXPORT_HEADER.unpack(data[:EXPORT_HEADER_SIZE])
+def parse_export_header(hdr: bytes) -> dict:
+    magic, ver, oid, nbytes, hlo, hhi = EXPORT_HEADER.unpack(hdr[:EXPORT_HEADER_SIZE])
     if magic != EXPORT_MAGIC:
         raise WireError("bad export header magic")
     return {"version": ver, "object_id": oid, "nbytes": nbytes, "content_hash_lo": hlo, "content_hash_hi": hhi}

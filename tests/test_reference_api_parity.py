@@ -1,0 +1,111 @@
+"""Public Python API parity with StateSpectre's own package.
+
+Reads StateSpectre's ``state_spectre/__init__.py`` from the reference build in
+``baseline/_ref`` (skipped when absent) as text, with ``ast``, and checks that
+``import state_spectre`` here offers every public class, method, property and
+function it defines (constructors of the objects the library hands out
+excepted), with every parameter it names, positional parameters in
+the same order, and a default wherever the reference has one, so code written
+against the reference calls this package unchanged.
+"""
+
+import ast
+import inspect
+import os
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_PKG = os.path.join(ROOT, "baseline", "_ref", "state_spectre")
+
+
+# Objects the library hands out (sessions, handles, records): user code gets
+# them from calls and never builds them, so their constructors are internal.
+LIBRARY_MADE = {"Off", "OffloadHandle", "PrefetchHandle", "ManagedRecord", "CanonicalHandle"}
+
+
+def _reference_api(filename: str):
+    path = os.path.join(REF_PKG, filename)
+    if not os.path.exists(path):
+        pytest.skip("reference build not present (python baseline/build_reference.py)")
+    with open(path) as f:
+        tree = ast.parse(f.read())
+    classes, funcs = {}, {}
+    for node in tree.body:
+        if isinstance(node, ast.ClassDef) and not node.name.startswith("_"):
+            classes[node.name] = [n for n in node.body if isinstance(n, ast.FunctionDef)
+                                  and (not n.name.startswith("_") or n.name == "__init__")]
+        elif isinstance(node, ast.FunctionDef) and not node.name.startswith("_"):
+            funcs[node.name] = node
+    return classes, funcs
+
+
+def _params(fn: ast.FunctionDef):
+    a = fn.args
+    pos = [x.arg for x in a.posonlyargs + a.args]
+    with_default = set(pos[len(pos) - len(a.defaults):]) if a.defaults else set()
+    kw = [x.arg for x in a.kwonlyargs]
+    with_default |= {x.arg for x, d in zip(a.kwonlyargs, a.kw_defaults) if d is not None}
+    return pos, kw, with_default
+
+
+def _check_callable(qual: str, ref_fn: ast.FunctionDef, ours) -> list:
+    problems = []
+    try:
+        sig = inspect.signature(ours)
+    except (TypeError, ValueError):
+        return problems  # a builtin or C callable: presence is what can be checked
+    params = sig.parameters
+    has_var_kw = any(p.kind == p.VAR_KEYWORD for p in params.values())
+    pos, kw, with_default = _params(ref_fn)
+    if pos and pos[0] in ("self", "cls"):
+        pos = pos[1:]
+    our_pos = [n for n, p in params.items() if p.kind in (p.POSITIONAL_ONLY, p.POSITIONAL_OR_KEYWORD)]
+    if our_pos and our_pos[0] in ("self", "cls"):
+        our_pos = our_pos[1:]
+    for i, name in enumerate(pos):
+        if name not in params and not has_var_kw:
+            problems.append(f"{qual}: parameter {name!r} missing")
+        elif name in params and name not in with_default and (i >= len(our_pos) or our_pos[i] != name):
+            problems.append(f"{qual}: positional parameter {name!r} not at position {i}")
+    for name in kw:
+        if name not in params and not has_var_kw:
+            problems.append(f"{qual}: keyword parameter {name!r} missing")
+    for name in with_default:
+        if name in params and params[name].default is inspect.Parameter.empty:
+            problems.append(f"{qual}: parameter {name!r} has no default here")
+    return problems
+
+
+@pytest.mark.parametrize("filename,module", [("__init__.py", "state_spectre"),
+                                             ("_rollout.py", "state_spectre._rollout"),
+                                             ("_wire.py", "state_spectre._wire")])
+def test_state_spectre_offers_the_reference_api(filename, module):
+    import importlib
+
+    ns = importlib.import_module(module)
+    classes, funcs = _reference_api(filename)
+    problems = []
+    for cname, methods in classes.items():
+        ours = getattr(ns, cname, None)
+        if ours is None:
+            problems.append(f"class {cname} missing")
+            continue
+        for m in methods:
+            if m.name == "__init__" and cname in LIBRARY_MADE:
+                continue
+            attr = inspect.getattr_static(ours, m.name, None)
+            if attr is None:
+                problems.append(f"{cname}.{m.name} missing")
+                continue
+            is_prop = any(isinstance(d, ast.Name) and d.id == "property" for d in m.decorator_list)
+            if is_prop or isinstance(attr, property):
+                continue
+            problems += _check_callable(f"{cname}.{m.name}", m, getattr(ours, m.name))
+    for fname, node in funcs.items():
+        ours = getattr(ns, fname, None)
+        if ours is None:
+            problems.append(f"function {fname} missing")
+            continue
+        problems += _check_callable(fname, node, ours)
+    assert not problems, problems
