@@ -109,3 +109,47 @@ def test_state_spectre_offers_the_reference_api(filename, module):
             continue
         problems += _check_callable(fname, node, ours)
     assert not problems, problems
+
+
+def _load_reference_wire():
+    import importlib.util
+
+    path = os.path.join(REF_PKG, "_wire.py")
+    if not os.path.exists(path):
+        pytest.skip("reference build not present (python baseline/build_reference.py)")
+    spec = importlib.util.spec_from_file_location("_ssref_wire_only", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_wire_helpers_produce_and_read_what_the_reference_helpers_do():
+    """StateSpectre's pure-Python wire helpers and this package's, side by
+    side: the same request bytes for the same arguments (filters included),
+    the same dicts from the reference daemon's captured responses, the same
+    frames and export headers."""
+    import json
+    import struct
+
+    from state_spectre import _wire as ours
+
+    ref = _load_reference_wire()
+    job = (0, 12345678901234567890, 3, "job/a")
+    assert ours.encode_get_latest(*job, 2) == ref.encode_get_latest(*job, 2)
+    for flt in (None, {}, {"tp": 3}, {"pp": 1, "tp": 2, "ep": 3, "etp": 4, "expert": -7}):
+        assert ours.encode_get_manifest(*job, 2, 9, flt) == ref.encode_get_manifest(*job, 2, 9, flt), flt
+    for transport, target in ((1, "127.0.0.1:5555"), (2, "/tmp/x.bin"), (3, "nic0|abcd")):
+        assert ours.encode_pull(*job, 2, 9, 77, transport, target) == ref.encode_pull(*job, 2, 9, 77, transport, target)
+    assert ours.make_frame(25, b"abc", 1) == ref.make_frame(25, b"abc", 1)
+    hdr = struct.pack("<IIQQQQ", ref.EXPORT_MAGIC, 1, 5, 100, 7, 8)
+    assert ours.parse_export_header(hdr) == ref.parse_export_header(hdr)
+    with open(os.path.join(ROOT, "tests", "golden", "reference_wire.json")) as f:
+        records = json.load(f)["records"]
+    seen = set()
+    for r in records:
+        payload = bytes.fromhex(r["response_hex"])
+        for op, fn in ((24, "decode_get_latest_resp"), (25, "decode_get_manifest_resp"), (26, "decode_pull_resp")):
+            if r["op"] == op:
+                assert getattr(ours, fn)(payload) == getattr(ref, fn)(payload), fn
+                seen.add(fn)
+    assert len(seen) == 3
