@@ -409,9 +409,10 @@ def _dedup(raw: _Raw, run_dir: str, sock: str) -> None:
     r1.sock.close()
 
 
-def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
+def capture(binary: str = REF_DAEMON, scenario: str = "session", trace: str = "") -> list:
     """Records of one scenario (one of SCENARIOS) against the daemon at
-    `binary` (the reference's by default)."""
+    `binary` (the reference's by default); `trace`: the daemon's JSONL trace
+    file."""
     run_dir = tempfile.mkdtemp(prefix="ssref-golden-")
     sock = os.path.join(run_dir, "d.sock")
     cfg = os.path.join(run_dir, "offloadd.yaml")
@@ -432,7 +433,8 @@ def capture(binary: str = REF_DAEMON, scenario: str = "session") -> list:
             (["manifest:", "  retain_sealed_versions: 2", "quotas:", "  default:", "    max_pinned_bytes: 3MiB"]
              if scenario == "versions" else [])) + "\n")
     log = open(os.path.join(run_dir, "offloadd.log"), "w")
-    proc = subprocess.Popen([binary, "--config", cfg, "--socket", sock], stdout=log, stderr=log)
+    proc = subprocess.Popen([binary, "--config", cfg, "--socket", sock] + (["--trace", trace] if trace else []),
+                            stdout=log, stderr=log)
     raw = None
     try:
         deadline = time.time() + 30
@@ -490,6 +492,29 @@ def test_live_capture_from_the_reference_round_trips():
         pytest.skip("reference build not present (python baseline/build_reference.py)")
     for sc in SCENARIOS:
         _check(capture(scenario=sc), all_ok=sc in ("session", "pageable", "nvme"))
+
+
+@pytest.mark.parametrize("scenario", ["session", "faults", "versions", "dedup", "crash"])
+def test_this_daemon_traces_the_scenario_as_the_reference_does(scenario, tmp_path):
+    """The JSONL trace (one event per state change, StateSpectre's schema):
+    run on both daemons, the same scenario gives the same events in the same
+    order with the same fields and values, timestamps aside."""
+    if not os.path.exists(REF_DAEMON):
+        pytest.skip("reference build not present (python baseline/build_reference.py)")
+    from statespectre_b200._native import bin_path
+
+    traces = []
+    for binary in (REF_DAEMON, bin_path("offloadd")):
+        path = str(tmp_path / f"trace_{len(traces)}.jsonl")
+        capture(binary, scenario=scenario, trace=path)
+        with open(path) as f:
+            events = [json.loads(line) for line in f if line.strip()]
+        for e in events:
+            e.pop("ts_ns", None)
+        traces.append(events)
+    ref, ours = traces
+    assert len(ref) > 5
+    assert ours == ref
 
 
 if __name__ == "__main__":
