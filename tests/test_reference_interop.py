@@ -202,3 +202,54 @@ def test_offload_stat_prometheus_matches_the_reference_tool(tmp_path):
         except subprocess.TimeoutExpired:
             proc.kill()
         log.close()
+
+
+BASE_CFG = """daemon:
+  socket_path: SOCK
+arenas:
+  allocation_granularity_mb: 2
+  per_numa:
+    - numa_node: 0
+      size_gb: 1
+      overflow_gb: 0
+      gpu_windows:
+        - gpu: 0
+          size_gb: 1
+nvme:
+  enabled: false
+"""
+
+
+@pytest.mark.parametrize("case,edit", [
+    ("valid", lambda c: c),
+    ("tab indentation", lambda c: c.replace("  socket_path", "\tsocket_path")),
+    ("windows beyond the arena", lambda c: c.replace("          size_gb: 1", "          size_gb: 5")),
+    ("unknown drain tier", lambda c: c + "drain_policy:\n  target_tier: floppy\n"),
+    ("size that is not a number", lambda c: c.replace("      size_gb: 1\n      overflow", "      size_gb: lots\n"
+                                                                                         "      overflow")),
+    ("unknown section", lambda c: c + "bogus_section:\n  x: 1\n"),
+    ("v2 sections", lambda c: c + "canonical_store:\n  dedup_default_mode: hash_verified\nmanifest:\n"
+                                  "  retain_sealed_versions: 3\nquotas:\n  default:\n    max_pinned_bytes: 1GiB\n"),
+])
+def test_config_files_are_accepted_and_refused_alike(tmp_path, case, edit):
+    """A config file StateSpectre's offloadd starts with, this offloadd starts
+    with; one it refuses at start-up, this one refuses too."""
+    import subprocess
+
+    from statespectre_b200._native import bin_path
+
+    ref = os.path.join(ROOT, "baseline", "_ref", "bin", "offloadd")
+    if not os.path.exists(ref):
+        pytest.skip("reference build not present (python baseline/build_reference.py)")
+    outcome = []
+    for i, binary in enumerate((ref, bin_path("offloadd"))):
+        sock = str(tmp_path / f"d{i}.sock")
+        cfg = tmp_path / f"c{i}.yaml"
+        cfg.write_text(edit(BASE_CFG).replace("SOCK", sock))
+        try:
+            r = subprocess.run([binary, "--config", str(cfg), "--socket", sock], capture_output=True, text=True,
+                               timeout=3)
+            outcome.append(("exited", r.returncode))
+        except subprocess.TimeoutExpired:
+            outcome.append(("serving", None))
+    assert outcome[0] == outcome[1], (case, outcome)
