@@ -46,7 +46,6 @@
 
 #include <algorithm>
 #include <cstdint>
-#include <type_traits>
 #include <cstring>
 #include <vector>
 
@@ -223,9 +222,9 @@ inline bool decode_chunk(const uint8_t* in, uint32_t len, uint8_t* out) {
 
 // The same decoding without the lane-order walk over every element and
 // without allocation (the daemon decodes coded canonical objects on export):
-// one pass in element order rebuilds every value from its window code and
-// notes the escaped elements; a counting pass over the 256 lanes then maps
-// each to its escape byte. `keys` is caller scratch reused across calls.
+// passes in element order rebuild every value from its window code and find
+// the escaped elements; a counting pass over the 256 lanes then maps each to
+// its escape byte. `keys` is caller scratch reused across calls.
 inline bool decode_chunk_fast(const uint8_t* in, uint32_t len, uint8_t* out, std::vector<uint32_t>& keys) {
     Header hd;
     std::memcpy(&hd, in, kHeader);
@@ -240,39 +239,32 @@ inline bool decode_chunk_fast(const uint8_t* in, uint32_t len, uint8_t* out, std
     const uint32_t ebase = hd.ebase;
     keys.clear();
     uint16_t* dst = reinterpret_cast<uint16_t*>(out);  // out is 2-byte aligned in every caller
-    // One pass per code width (constant shifts let the compiler unroll and
-    // vectorize the rebuild); an escape is a field of all ones, found from
-    // bit 0 of every field after ANDing the field's bits together.
-    auto scan = [&](auto width) -> bool {
-        constexpr uint32_t B = decltype(width)::value;
-        constexpr uint32_t M = (1u << B) - 1;
-        constexpr uint32_t lsb = B == 3 ? 0x249249u : 0x11111111u;
-        for (uint32_t v = 0; v < n / 8; ++v) {
-            uint32_t cw;  // the vector's 8 codes
-            if (B == 3) {
-                cw = uint32_t(codes[3 * v]) | (uint32_t(codes[3 * v + 1]) << 8) | (uint32_t(codes[3 * v + 2]) << 16);
-            } else {
-                std::memcpy(&cw, codes + 4 * v, 4);
-            }
-            const uint8_t* lo = low + 8 * v;
-            uint16_t* d = dst + 8 * v;
-            for (uint32_t j = 0; j < 8; ++j) {
-                const uint32_t ex = ebase + ((cw >> (B * j)) & M);
-                d[j] = uint16_t((uint32_t(lo[j] & 0x80u) << 8) | ((ex & 0xFFu) << 7) | (lo[j] & 0x7Fu));
-            }
-            const uint32_t ones = B == 3 ? (cw & (cw >> 1) & (cw >> 2)) : (cw & (cw >> 1) & (cw >> 2) & (cw >> 3));
-            if (ones & lsb) {
-                for (uint32_t j = 0; j < 8; ++j) {
-                    if (((cw >> (B * j)) & M) != M) continue;
-                    if (keys.size() >= hd.n_esc) return false;
-                    keys.push_back(8 * v + j);
-                }
-            }
+    // Three simple passes the compiler vectorizes: every value's exponent
+    // (window base + code) into a byte array, the rebuild of every value from
+    // its low byte and exponent, and a memchr scan for the escape marker
+    // (base + the all-ones code; its byte value cannot be a window exponent).
+    uint8_t e8[kChunk / 2];
+    const uint8_t eb = uint8_t(hd.ebase);
+    if (!m2) {
+        for (uint32_t j = 0; j < n / 2; ++j) {
+            e8[2 * j] = uint8_t(eb + (codes[j] & 15u));
+            e8[2 * j + 1] = uint8_t(eb + (codes[j] >> 4));
         }
-        return true;
-    };
-    if (!(m2 ? scan(std::integral_constant<uint32_t, 3>{}) : scan(std::integral_constant<uint32_t, 4>{})))
-        return false;
+    } else {
+        for (uint32_t v = 0; v < n / 8; ++v) {
+            const uint32_t w =
+                uint32_t(codes[3 * v]) | (uint32_t(codes[3 * v + 1]) << 8) | (uint32_t(codes[3 * v + 2]) << 16);
+            for (uint32_t j = 0; j < 8; ++j) e8[8 * v + j] = uint8_t(eb + ((w >> (3 * j)) & 7u));
+        }
+    }
+    for (uint32_t i = 0; i < n; ++i)
+        dst[i] = uint16_t((uint32_t(low[i] & 0x80u) << 8) | (uint32_t(e8[i]) << 7) | (low[i] & 0x7Fu));
+    const uint8_t mark = uint8_t(eb + (m2 ? kEscape3 : kEscape));
+    for (const uint8_t* q = e8; (q = static_cast<const uint8_t*>(std::memchr(q, mark, size_t(e8 + n - q)))) != nullptr;
+         ++q) {
+        if (keys.size() >= hd.n_esc) return false;
+        keys.push_back(uint32_t(q - e8));
+    }
     if (keys.size() != hd.n_esc) return false;
     // Escape order is lane-major (lane t = vector index mod 256, then the
     // lane's vectors, then elements); the scan above found them vector-major,
