@@ -200,7 +200,8 @@ def main():
     # every window of the node (GPU hosts here have about 196 GB): then one
     # tensor plus 2 GB, which the evict/restore loop needs at any time
     n_windows = max(int(os.environ.get("LOCAL_WORLD_SIZE", str(world))), torch.cuda.device_count(), 1)
-    room_gb = int(0.6 * host_mem_available_bytes() / (1 << 30) / n_windows)
+    avail = host_mem_available_bytes()
+    room_gb = int(0.6 * avail / (1 << 30) / n_windows) if avail else 1 << 20
     window_gb = max(4, min((3 * nbytes >> 30) + 2, max((nbytes >> 30) + 2, room_gb)))
     run_dir = os.environ.get("OFLD_BENCH_DIR", "/tmp/ofld_bench")
     os.makedirs(run_dir, exist_ok=True)
