@@ -116,6 +116,21 @@ nvme:
         while time.time() < deadline and d.stats()["versions_persisted_total"] < 3:
             time.sleep(0.05)
         assert d.stats()["versions_persisted_total"] == 3
+        # a zbf16-coded canonical object pulled by three receivers at once: the
+        # export decodes it over the copy pool from several connection threads
+        from test_canonical import _coded_canonical_object, _pull_all
+
+        raw = (torch.randn(3 << 19, generator=torch.Generator().manual_seed(1)) * 0.02).to(torch.bfloat16)
+        raw = raw.view(torch.uint8).numpy().tobytes()
+        rr, job, oid = _coded_canonical_object(sock, raw, "sanitized-coded")
+        got = []
+        pulls = [threading.Thread(target=lambda: got.append(_pull_all(sock, job))) for _ in range(3)]
+        for t in pulls:
+            t.start()
+        for t in pulls:
+            t.join(120)
+        assert len(got) == 3 and all(g[k][oid] == raw for g in got for k in g)
+        rr.close()
         # a session that stops heartbeating: the daemon reclaims it by timeout
         s = offload_context(daemon_addr=sock, device="cpu", rank=9)
         s.off.copy(torch.randn(5000), wait=True)
