@@ -328,6 +328,7 @@ struct Agent::Impl {
         bool offloaded = false, restored = false;
         bool failed = false;  // the device reported an incomplete copy (bounded wait expired)
         uint64_t hash_lo = 0, hash_hi = 0, lease = 0;
+        uint32_t slot = 0;    // first slot of the run (a v1-only discard releases lease and slot)
         uint32_t zmax = 0;    // zbf16 run: largest stored chunk length (0: unknown)
         std::vector<uint64_t> digests;
     };
@@ -350,6 +351,14 @@ struct Agent::Impl {
             throw std::invalid_argument("coded_restore must be copy_engine or sm, not '" + opt.coded_restore + "'");
         if (opt.coded_evict != "copy_engine" && opt.coded_evict != "sm")
             throw std::invalid_argument("coded_evict must be copy_engine or sm, not '" + opt.coded_evict + "'");
+        if (opt.v1_only) {  // StateSpectre's daemon keeps no run formats and knows no submit flags
+            // and applies ring entries only on its poller's schedule, so a
+            // restore could overtake its own evict's completion: report by RPC
+            opt.use_ring = false;
+            opt.fast_submit = false;
+            opt.compress = false;
+            opt.compress_canonical = false;
+        }
         gpu = opt.device >= 0;
         if (gpu) {
             CUDA_OK(cudaSetDevice(opt.device));
@@ -677,6 +686,7 @@ struct Agent::Impl {
                 t.hash_lo = lo;
                 t.hash_hi = hi;
                 t.lease = p.lease;
+                t.slot = p.slot;
                 t.digests = std::move(dig);
             }
             inflight_d2h -= p.nbytes;
@@ -833,6 +843,13 @@ struct Agent::Impl {
         cudaEventDestroy(ev);
     }
 
+    // Calls on opcodes StateSpectre's daemon does not have: refuse in v1-only
+    // mode (that daemon would leave them unanswered).
+    void need_ext(const char* what) const {
+        if (opt.v1_only)
+            throw std::runtime_error(std::string(what) + " needs this repository's offloadd (the session is v1-only)");
+    }
+
     bool want_z(uint64_t ptr, uint64_t nbytes, uint32_t fmt_hint) const {
         return gpu && fmt_hint == kFmtBf16 && opt.compress && opt.engine != "copy_engine" &&
                nbytes >= opt.compress_min_bytes && zbf16::eligible(nbytes) && (ptr & 15) == 0;
@@ -976,6 +993,7 @@ struct Agent::Impl {
                     t.hash_lo = o.lo;
                     t.hash_hi = o.hi;
                     t.lease = p.lease;
+                    t.slot = p.slot;
                     if (opt.keep_digests) t.digests = std::move(keep);
                 }
                 inflight_d2h -= p.nbytes;
@@ -1071,6 +1089,7 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
         Impl::TensorRec& r = D.tensors[{tensor_id, version}];
         r.offloaded = false;
         r.lease = g.lease_id;
+        r.slot = g.slot_id;
         r.zmax = z ? D.zscan_max(nbytes, zb) : 0;
     }
     D.launch_d2h(p, ptr, host, dev, D.stream_of(stream), D.opt.hash_on_evict);
@@ -1103,6 +1122,13 @@ EvictTicket Agent::evict(uint64_t ptr, uint64_t nbytes, StreamHandle stream, boo
 std::vector<EvictTicket> Agent::evict_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait) {
     NvtxRange nvtx_("ofld.evict_batch");
     Impl& D = *d_;
+    if (D.opt.v1_only) {  // no batch opcodes: one evict per item
+        std::vector<EvictTicket> out;
+        out.reserve(items.size());
+        for (const BatchItem& it : items)
+            out.push_back(evict(it.ptr, it.nbytes, stream, false, it.tensor_id, it.version, "", {}, wait, it.fmt_hint));
+        return out;
+    }
     std::vector<EvictTicket> out(items.size());
     cudaStream_t s = D.stream_of(stream);
     std::vector<PinnedPool::Buf> zb(items.size());
@@ -1459,6 +1485,13 @@ RestoreOutcome Agent::restore(uint64_t tensor_id, uint64_t version, uint64_t ptr
 // group's round trip overlapping this group's copy). Items the daemon still
 // has to read back from a cold tier are asked for again after the rest.
 std::vector<RestoreOutcome> Agent::restore_batch(const std::vector<BatchItem>& items, StreamHandle stream, bool wait) {
+    if (d_->opt.v1_only) {  // no batch opcodes: one restore per item
+        std::vector<RestoreOutcome> out;
+        out.reserve(items.size());
+        for (const BatchItem& it : items)
+            out.push_back(restore(it.tensor_id, it.version, it.ptr, it.nbytes, stream, wait, RestoreOptions{}));
+        return out;
+    }
     NvtxRange nvtx_("ofld.restore_batch");
     Impl& D = *d_;
     std::vector<RestoreOutcome> out(items.size());
@@ -1674,6 +1707,29 @@ std::string Agent::location(uint64_t tid, uint64_t ver) {
 // settle, so a discard never leaves the tensor's pinned or cold copy behind.
 void Agent::discard(uint64_t tid, uint64_t ver) {
     Impl& D = *d_;
+    if (D.opt.v1_only) {
+        // StateSpectre's discard: release the lease the evict was granted
+        uint64_t lease = 0;
+        uint32_t slot = 0;
+        {
+            std::lock_guard<std::mutex> g(D.tab_mu);
+            auto it = D.tensors.find({tid, ver});
+            if (it != D.tensors.end()) {
+                lease = it->second.lease;
+                slot = it->second.slot;
+            }
+        }
+        if (lease) {
+            StatusResponse s = D.call<Op::kReleaseLease>(ReleaseLeaseRequest{D.opt.rank_id, D.epoch, lease, slot,
+                                                                              "discard"});
+            if (!s.ok) LOG_WARN(TAG, "discard(%llu:%llu): %s", (unsigned long long)tid, (unsigned long long)ver,
+                                s.message.c_str());
+        }
+        std::lock_guard<std::mutex> g(D.tab_mu);
+        D.tensors.erase({tid, ver});
+        D.tab_cv.notify_all();
+        return;
+    }
     DiscardTensorRequest r{D.opt.rank_id, D.epoch, tid, ver};
     StatusResponse s = D.call<Op::kDiscardTensor>(r);
     const uint64_t deadline = mono_ns() + 30ull * 1000000000ull;
@@ -1691,6 +1747,10 @@ void Agent::discard(uint64_t tid, uint64_t ver) {
 
 void Agent::discard_batch(const std::vector<std::pair<uint64_t, uint64_t>>& items) {
     Impl& D = *d_;
+    if (D.opt.v1_only) {
+        for (const auto& tv : items) discard(tv.first, tv.second);
+        return;
+    }
     std::vector<std::pair<uint64_t, uint64_t>> todo = items;
     const uint64_t deadline = mono_ns() + 30ull * 1000000000ull;
     uint64_t backoff_us = 100;
@@ -2064,18 +2124,24 @@ ReleaseCanonicalResponse Agent::release(const ReleaseCanonicalRequest& in) {
     return d_->call<Op::kReleaseCanonical>(r);
 }
 CarryForwardResponse Agent::carry_forward(const CarryForwardRequest& in) {
+    d_->need_ext("carry_forward");
     CarryForwardRequest r = in;
     r.rank_id = d_->opt.rank_id;
     r.rank_epoch = d_->epoch;
     return d_->call<Op::kCarryForward>(r);
 }
 ExportManifestResponse Agent::export_manifest(const ExportManifestRequest& r) {
+    d_->need_ext("export_manifest");
     return d_->call<Op::kExportManifest>(r);
 }
-GetJobStatsResponse Agent::job_stats(const GetJobStatsRequest& r) { return d_->call<Op::kGetJobStats>(r); }
+GetJobStatsResponse Agent::job_stats(const GetJobStatsRequest& r) {
+    d_->need_ext("job_stats");
+    return d_->call<Op::kGetJobStats>(r);
+}
 GetStatsResponse Agent::daemon_stats() { return d_->call<Op::kGetStats>(GetStatsRequest{}); }
 
 StatusResponse Agent::publish_peer_buffer(const PeerBufferDesc& desc, int fd) {
+    d_->need_ext("publish_peer_buffer");
     PublishPeerBufferRequest r;
     r.rank_id = d_->opt.rank_id;
     r.rank_epoch = d_->epoch;
@@ -2087,6 +2153,7 @@ StatusResponse Agent::publish_peer_buffer(const PeerBufferDesc& desc, int fd) {
 }
 
 LookupPeerBufferResponse Agent::lookup_peer_buffer(const std::string& key, uint32_t wait_ms, int* fd_out) {
+    d_->need_ext("lookup_peer_buffer");
     ++d_->rpc_count;
     std::vector<int> fds;
     LookupPeerBufferResponse r = d_->rpc->call<Op::kLookupPeerBuffer>(LookupPeerBufferRequest{key, wait_ms}, &fds);

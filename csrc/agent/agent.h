@@ -92,6 +92,13 @@ struct AgentOptions {
     // DP dedup owners): offloadd records the run's coding and decodes it when
     // it exports the object, so TCP / FILE receivers get the raw bytes.
     bool compress_canonical = true;
+    // Talk to StateSpectre's own offloadd: only its opcodes 1-30. Batches run
+    // as one call per item, discard releases the tensor's lease, runs are not
+    // coded (it keeps no run formats), reservations carry no submit flags and
+    // completions go by RPC (it applies ring entries on its own schedule).
+    // Calls that need this repository's daemon (carry-forward, job stats,
+    // peer buffers) raise instead of waiting for an answer that never comes.
+    bool v1_only = false;
     uint64_t compress_min_bytes = 4ull << 20;
     // evict_batch/restore_batch reserve and launch in groups of about this
     // many bytes: one daemon round trip and one kernel launch per group, the

@@ -251,6 +251,7 @@ class PyAgent {
             else if (k == "stream_priority") o.stream_priority = v.cast<int>();
             else if (k == "compress") o.compress = v.cast<bool>();
             else if (k == "compress_canonical") o.compress_canonical = v.cast<bool>();
+            else if (k == "v1_only") o.v1_only = v.cast<bool>();
             else if (k == "compress_min_bytes") o.compress_min_bytes = v.cast<uint64_t>();
             else if (k == "batch_group_bytes") o.batch_group_bytes = v.cast<uint64_t>();
             else if (k == "kernel_timing") o.kernel_timing = v.cast<bool>();

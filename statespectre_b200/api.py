@@ -970,9 +970,10 @@ _AGENT_OPTION_KEYS = {
 }
 
 
-def _daemon_agent_options(path: str, rank: int, gpu: int) -> dict:
+def _daemon_agent_options(path: str, rank: int, gpu: int) -> Optional[dict]:
     """The daemon's forwarded ``kernels:`` / ``nvlink:`` settings (empty when
-    the daemon does not offer them)."""
+    the daemon does not offer them; None when it left the request unanswered,
+    as StateSpectre's own offloadd does with every opcode it does not know)."""
     if not path.startswith("tcp://") and not os.path.exists(path):
         return {}  # no daemon there; the session's own connect reports it
     try:
@@ -985,8 +986,8 @@ def _daemon_agent_options(path: str, rank: int, gpu: int) -> dict:
                                _wire.encode("GetAgentOptionsRequest", {"rank_id": rank, "gpu_id": gpu}))
         r = _wire.decode("GetAgentOptionsResponse", body)
         return {e["key"]: e["value"] for e in r["options"]} if r["ok"] else {}
-    except Exception:  # noqa: BLE001
-        return {}
+    except Exception:  # noqa: BLE001 - no answer within the reply timeout
+        return None
     finally:
         conn.close()
 
@@ -1007,6 +1008,10 @@ class _OffloadSession:
                 "local_rank": int(local_rank), "world_rank": int(world_rank), "numa_node": int(numa_node),
                 "eager_register": bool(eager_register or register_policy in ("eager", "eager_all"))}
         daemon_opts = _daemon_agent_options(path, int(rank), dev.index if dev.type == "cuda" else 0)
+        if daemon_opts is None:
+            # StateSpectre's own offloadd: speak its opcodes 1-30 only
+            opts["v1_only"] = True
+            daemon_opts = {}
         for k, v in daemon_opts.items():
             if k in _AGENT_OPTION_KEYS and _AGENT_OPTION_KEYS[k][0] not in agent_opts:
                 name, conv = _AGENT_OPTION_KEYS[k]

@@ -150,6 +150,21 @@ def test_this_agent_records_and_pulls_through_the_reference_daemon(tmp_path):
             for e in man["tensors"]:
                 assert cl.pull_tensor(e, 1) == tensors[e["key"]["param_fqn_debug"]].numpy().tobytes()
             cl.close()
+            # v1 tensors: the session speaks only StateSpectre's opcodes (batches
+            # one call per item, discard by lease release)
+            xs = [torch.randn(5000 + 17 * i) for i in range(4)]
+            for x in xs:
+                h = off.copy(x, wait=True)
+                assert torch.equal(h.restore(), x)
+                h.discard()
+            hs = off.evict_batch(xs)
+            outs = off.restore_batch(hs)
+            assert all(torch.equal(o, x) for o, x in zip(outs, xs))
+            off.discard_batch(hs)
+            t1 = time.time()
+            with pytest.raises(RuntimeError, match="v1-only"):
+                off.carry_forward_version(ROLL, 1, 2, [1])
+            assert time.time() - t1 < 5
     finally:
         proc.terminate()
         try:
