@@ -358,6 +358,7 @@ struct Agent::Impl {
             opt.fast_submit = false;
             opt.compress = false;
             opt.compress_canonical = false;
+            LOG_WARN(TAG, "v1-only session: StateSpectre opcodes 1-30, no coding, batches per item");
         }
         gpu = opt.device >= 0;
         if (gpu) {

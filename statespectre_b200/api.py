@@ -978,7 +978,7 @@ def _daemon_agent_options(path: str, rank: int, gpu: int) -> Optional[dict]:
         return {}  # no daemon there; the session's own connect reports it
     try:
         # StateSpectre's own offloadd logs an unknown opcode and sends nothing back
-        conn = native().RawConn(path, 5000, 2000)
+        conn = native().RawConn(path, 5000, 5000)
     except Exception:  # noqa: BLE001 - the agent reports connection errors itself
         return {}
     try:
