@@ -111,3 +111,35 @@ def test_schema_covers_every_opcode():
         assert native().op_name(op) != "Unknown", op
     with pytest.raises(RuntimeError, match="unknown opcode"):
         native().reencode(999, False, b"")
+
+
+@SETTINGS
+@given(mode=st.sampled_from([1, 2]), ebase=st.integers(0, 255), n_esc=st.integers(0, 3000),
+       len_kib=st.sampled_from([4, 16, 64]), seed=st.integers(0, 2**32 - 1), flip=st.integers(0, 65535))
+def test_export_decoder_survives_arbitrary_chunks(mode, ebase, n_esc, len_kib, seed, flip):
+    """The daemon's export decoder on chunks with a self-consistent header and
+    arbitrary contents (random planes, any escape count, one flipped byte):
+    it returns bytes or refuses, and it never reads or writes outside the
+    chunk, whatever the codes say."""
+    import struct
+
+    import numpy as np
+
+    from statespectre_b200._native import native
+
+    length = len_kib * 1024
+    n = length // 2
+    plane = (n // 8) * 3 if mode == 2 else n // 2
+    comp = 16 + n + plane + n_esc
+    if comp > length:
+        comp, n_esc = length, max(0, length - 16 - n - plane)
+    rng = np.random.default_rng(seed)
+    body = bytearray(rng.integers(0, 256, length, dtype=np.uint8).tobytes())
+    body[:16] = struct.pack("<HBBIII", 0x425A, mode, ebase, n_esc, length, 16 + n + plane + n_esc)
+    if flip >= 16 and flip < length:
+        body[flip] ^= 0x5A
+    try:
+        out = native().zcoded_decode_range(1, bytes(body), 0, length)
+        assert len(out) == length
+    except RuntimeError:
+        pass
