@@ -185,6 +185,45 @@ void zbf16_codec() {
     CHECK(!zbf16::encode_object(reinterpret_cast<uint8_t*>(h.data()), n * 2, coded.data()));
 }
 
+// The export decoder agrees with the reference decoder on coded objects
+// (whole and in 64 KiB-aligned ranges) and, on chunks with a consistent
+// header but arbitrary planes, decodes or refuses without touching memory
+// outside the chunk (this runs under AddressSanitizer too).
+void zbf16_export_decoder() {
+    std::mt19937 rng(11);
+    std::normal_distribution<float> nd(0.f, 1.f);
+    const uint64_t n = 7 * 65536 / 2 + 2048;
+    std::vector<uint16_t> h(n);
+    for (size_t i = 0; i < n; ++i) {
+        float f = nd(rng) * (i % 13 == 0 ? 300.f : 1.f) * (i % 97 == 0 ? 1e-6f : 1.f);
+        uint32_t u;
+        std::memcpy(&u, &f, 4);
+        h[i] = uint16_t((u + 0x8000u) >> 16);
+    }
+    std::vector<uint8_t> coded(n * 2), a(n * 2), b(n * 2);
+    CHECK(zbf16::encode_object(reinterpret_cast<uint8_t*>(h.data()), n * 2, coded.data()));
+    CHECK(zbf16::decode_object(coded.data(), n * 2, a.data()));
+    std::vector<uint32_t> keys;
+    CHECK(zbf16::decode_range(zbf16::Coding::kZbf16, coded.data(), n * 2, 0, n * 2, b.data(), keys));
+    CHECK(a == b);
+    std::fill(b.begin(), b.end(), 0);
+    CHECK(zbf16::decode_range(zbf16::Coding::kZbf16, coded.data() + 2 * 65536, n * 2, 2 * 65536, 3 * 65536,
+                              b.data(), keys));
+    CHECK(std::memcmp(b.data(), a.data() + 2 * 65536, 3 * 65536) == 0);
+    for (int trial = 0; trial < 400; ++trial) {
+        const uint32_t len = (trial % 3 == 0) ? 4096 : (trial % 3 == 1) ? 16384 : 65536;
+        const uint32_t mode = 1 + trial % 2, ne = len / 2;
+        const uint32_t plane = mode == 2 ? (ne / 8) * 3 : ne / 2;
+        const uint32_t room = len - 16 - ne - plane;
+        const uint32_t n_esc = uint32_t(rng() % (room + 1));
+        std::vector<uint8_t> chunk(len), out(len);
+        for (auto& c : chunk) c = uint8_t(rng());
+        zbf16::Header hd{zbf16::kTag, uint8_t(mode), uint8_t(rng()), n_esc, len, 16 + ne + plane + n_esc};
+        std::memcpy(chunk.data(), &hd, sizeof(hd));
+        (void)zbf16::decode_chunk_fast(chunk.data(), len, out.data(), keys);
+    }
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -192,7 +231,7 @@ int main(int argc, char** argv) {
         {"codec_round_trips", codec_round_trips}, {"codec_rejects_truncation", codec_rejects_truncation},
         {"framing", framing},                     {"config_parse", config_parse},
         {"layout_and_ring", layout_and_ring},     {"hash_properties", hash_properties},
-        {"zbf16_codec", zbf16_codec},
+        {"zbf16_codec", zbf16_codec},             {"zbf16_export_decoder", zbf16_export_decoder},
     };
     const char* filter = argc > 1 ? argv[1] : nullptr;
     for (const Case& c : cases) {
