@@ -82,6 +82,10 @@ def build(src: str = DEFAULT_SRC, jobs: int = 0) -> dict:
         os.makedirs(bindir, exist_ok=True)
         for exe in ("offloadd", "offload-stat", "offload_bench"):
             shutil.copy2(os.path.join(bdir, exe), os.path.join(bindir, exe))
+        # the reference's C++ agent interface, read as text by the API parity test
+        incdir = os.path.join(OUT, "include", "agent")
+        os.makedirs(incdir, exist_ok=True)
+        shutil.copy2(os.path.join(tree, "src", "agent", "agent.h"), os.path.join(incdir, "agent.h"))
         env = dict(os.environ)
         env["CFLAGS"] = (env.get("CFLAGS", "") + f" -I{inc}").strip()
         env["CPPFLAGS"] = (env.get("CPPFLAGS", "") + f" -I{inc}").strip()

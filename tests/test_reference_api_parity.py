@@ -153,3 +153,32 @@ def test_wire_helpers_produce_and_read_what_the_reference_helpers_do():
                 assert getattr(ours, fn)(payload) == getattr(ref, fn)(payload), fn
                 seen.add(fn)
     assert len(seen) == 3
+
+
+def test_cpp_agent_interface_offers_the_reference_methods_and_types():
+    """StateSpectre's C++ `offload::OffloadAgent` (its header, read as text
+    from the reference build): every public method name and every struct the
+    header declares is in this repository's `ofld/offload_agent.h`, whose
+    OffloadAgent forwards to this agent (`csrc/tests/compat_agent.cpp` is a
+    program written against it)."""
+    import re
+
+    ref_h = os.path.join(ROOT, "baseline", "_ref", "include", "agent", "agent.h")
+    if not os.path.exists(ref_h):
+        pytest.skip("reference build not present (python baseline/build_reference.py)")
+    with open(ref_h) as f:
+        ref = f.read()
+    with open(os.path.join(ROOT, "csrc", "include", "ofld", "offload_agent.h")) as f:
+        ours = f.read()
+    body = ref[ref.index("class OffloadAgent"):]
+    body = body[:body.index("\n};")]
+    public = body.split("private:")[0]
+    methods = set(re.findall(r"^\s+(?:[\w:<>,]+\s+)+?[&*]?(\w+)\s*\(", public, flags=re.M))
+    methods -= {"OffloadAgent", "operator"}
+    assert {"evict", "restore", "canonical_evict", "canonical_restore", "discard"} <= methods
+    missing = sorted(m for m in methods if not re.search(rf"\b{m}\s*\(", ours))
+    assert not missing, missing
+    structs = set(re.findall(r"^struct\s+(\w+)", ref, flags=re.M))
+    assert structs
+    missing = sorted(s for s in structs if not re.search(rf"\b{s}\b", ours))
+    assert not missing, missing
