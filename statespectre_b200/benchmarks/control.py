@@ -9,6 +9,9 @@ not the data copy, is what is measured:
   batch    evict_batch + restore_batch + discard_batch of 256 x 4 KiB
            tensors: items per second, per phase
   ranks    the single loop in 1, 4 and 16 rank processes at once: aggregate rate
+  vs_reference  the single loop against StateSpectre's own daemon (built in
+           baseline/_ref) and this one, both as separate processes, with
+           the same client (held to StateSpectre's opcodes for the first two)
   kv       8 rank processes, each moving its own 64 blocks of 256 KiB per
            iteration with evict_batch + restore_batch, against a pinned
            window half the size of the blocks in flight, so background
@@ -168,6 +171,65 @@ def run_kv(seconds: float = 3.0, ranks: int = 8, nblocks: int = 64, block: int =
             "errors": [ok for _, _, ok in res if ok is not True and ok is not False]}
 
 
+REF_DAEMON = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                          "baseline", "_ref", "bin", "offloadd")
+
+
+def _external_daemon(binary: str, tag: str):
+    """`binary` as its own process on a 1 GiB window, no drain on completion."""
+    import subprocess
+
+    d = tempfile.mkdtemp(prefix=f"ofld-control-{tag}-")
+    sock, cfg = os.path.join(d, "d.sock"), os.path.join(d, "offloadd.yaml")
+    with open(cfg, "w") as f:
+        f.write("\n".join(["daemon:", f"  socket_path: {sock}", f"  control_shm_name: /ofld_cp_{os.getpid()}_{tag}",
+                           "arenas:", "  allocation_granularity_mb: 1", "  per_numa:", "    - numa_node: 0",
+                           "      size_gb: 1", "      overflow_gb: 0", "      gpu_windows:", "        - gpu: 0",
+                           "          size_gb: 1", "drain_policy:", "  drain_on_d2h_complete: false", "nvme:",
+                           "  enabled: false"]) + "\n")
+    p = subprocess.Popen([binary, "--config", cfg, "--socket", sock], stdout=subprocess.DEVNULL,
+                         stderr=subprocess.DEVNULL)
+    deadline = time.time() + 30
+    while not os.path.exists(sock) and time.time() < deadline and p.poll() is None:
+        time.sleep(0.05)
+    return p, sock
+
+
+def run_vs_reference(seconds: float = 2.0) -> dict:
+    """The single-tensor cycle (copy, restore_into, discard of 4 KiB) with the
+    same client against StateSpectre's own daemon (the session speaks its
+    opcodes only), against this daemon with the session held to the same
+    opcodes, and against this daemon with everything on (reservation and
+    submit in one round trip, completions through the shared ring)."""
+    from .._native import bin_path
+
+    if not os.path.exists(REF_DAEMON):
+        return {"unavailable": "reference build not present (python baseline/build_reference.py)"}
+    out = {}
+    for name, binary, v1 in (("reference_daemon", REF_DAEMON, True), ("this_daemon_v1_only", bin_path("offloadd"), True),
+                             ("this_daemon", bin_path("offloadd"), False)):
+        p, sock = _external_daemon(binary, name)
+        try:
+            with offload_context(daemon_addr=sock, device="cpu", rank=0, v1_only=v1) as off:
+                t = torch.randn(1024)
+                dst = torch.empty_like(t)
+                lat = []
+                deadline = time.perf_counter() + seconds
+                while time.perf_counter() < deadline:
+                    t0 = time.perf_counter()
+                    h = off.copy(t, wait=True)
+                    h.restore_into(dst)
+                    h.discard()
+                    lat.append(time.perf_counter() - t0)
+            lat.sort()
+            out[name] = {"cycles_per_s": round(len(lat) / seconds, 1), "p50_us": round(lat[len(lat) // 2] * 1e6, 1),
+                         "p99_us": round(lat[min(len(lat) - 1, int(0.99 * len(lat)))] * 1e6, 1)}
+        finally:
+            p.terminate()
+            p.wait(30)
+    return out
+
+
 def _rank_proc(sock: str, rank: int, seconds: float, q, barrier) -> None:
     lat: list = []
     n = _single(sock, rank, seconds, lat, barrier)
@@ -181,6 +243,7 @@ def main(argv=None) -> int:
     a = p.parse_args(argv)
     res = run(a.seconds)
     res["kv"] = run_kv(max(a.seconds, 3.0))
+    res["vs_reference"] = run_vs_reference(a.seconds)
     line = json.dumps({"benchmark": "control_plane", **res})
     print(line)
     if a.out:
