@@ -221,9 +221,23 @@ def run_vs_reference(seconds: float = 2.0) -> dict:
                     h.restore_into(dst)
                     h.discard()
                     lat.append(time.perf_counter() - t0)
+                # 256 blocks of 4 KiB per batch call (KV-cache style); against
+                # StateSpectre's daemon each batch call is one call per block
+                blocks = [torch.randn(1024) for _ in range(256)]
+                outs = [torch.empty_like(b) for b in blocks]
+                items, t_total = 0, 0.0
+                deadline = time.perf_counter() + seconds
+                while time.perf_counter() < deadline:
+                    t0 = time.perf_counter()
+                    hs = off.evict_batch(blocks)
+                    off.restore_batch(hs, outs)
+                    off.discard_batch(hs)
+                    t_total += time.perf_counter() - t0
+                    items += len(blocks)
             lat.sort()
             out[name] = {"cycles_per_s": round(len(lat) / seconds, 1), "p50_us": round(lat[len(lat) // 2] * 1e6, 1),
-                         "p99_us": round(lat[min(len(lat) - 1, int(0.99 * len(lat)))] * 1e6, 1)}
+                         "p99_us": round(lat[min(len(lat) - 1, int(0.99 * len(lat)))] * 1e6, 1),
+                         "batch_items_per_s": round(items / t_total, 1)}
         finally:
             p.terminate()
             p.wait(30)
